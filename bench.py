@@ -1,0 +1,382 @@
+#!/usr/bin/env python
+"""Prefill-stage benchmark on B200: one NVFP4 MoE layer over an 8,192-token microbatch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--tokens T]
+
+One JSON line on rank 0. A step is one forward of the layer (quantize -> router GEMM -> top-8 routing -> permutation
+-> grouped NVFP4 gate_up GEMM + SwiGLU + requant -> grouped down GEMM -> weighted combine + shared expert) over T
+tokens with the inputs resident in HBM; `e2e` is the same metric through the public API (`MoELayer.forward`) with the
+step's input copied from pinned host memory and its output read back inside the timed region. At N > 1 every rank
+runs its own replica on its own microbatch (weak scaling, no collective on the data path); the time is the max over
+ranks. `--impl reference` times the CPU restatement of the path (the reference has no CPU implementation of its
+own; its GPU path needs a vLLM fork and FlashInfer builds absent here) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+H, F, E, K_TOP = 4096, 1024, 128, 8
+SEED = 20261201
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=8192)
+    ap.add_argument("--cpu-tokens", type=int, default=1024, help="CPU baseline sample (tokens)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+def workload(T: int) -> str:
+    return (f"BASELINE config 2: one NVFP4 MoE layer, {T} tokens, hidden {H}, {E} experts top-{K_TOP} + 1 shared, "
+            f"expert FFN {H}->2x{F} SwiGLU->{H}")
+
+
+def layer_flops(T: int) -> float:
+    rows = T * K_TOP + T
+    return 2.0 * T * H * E + rows * (2.0 * H * 2 * F + 2.0 * F * H)
+
+
+# ---------------------------------------------------------------------------------------------- clocks
+class Clocks:
+    """nvidia-smi sampler over a time window (every 100 ms)."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.count(",") >= 7]
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            try:
+                sm.append(float(r[0]))
+                mx.append(float(r[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[4:8]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------- CPU side
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def dense_on_host(layer) -> tuple[dict, dict]:
+    """The layer's logical NVFP4 parameters and their fp32 dequantization (done on the device: exact products and
+    one IEEE division, the same values as the checker's numpy dequantization), copied to host memory."""
+    import numpy as np
+    import torch
+
+    from ssengine_b200 import layout
+
+    dev = layer.device
+    e2m1 = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6], device=dev)
+    e4m3 = torch.tensor([float(v) for v in _e4m3_table()], device=dev)
+
+    def deq(codes, sf, gs):
+        v = e2m1[codes.long()].view(codes.shape[0], -1, 16) * e4m3[sf.long()][:, :, None]
+        return (v / torch.tensor(gs, dtype=torch.float32, device=dev)).reshape(codes.shape[0], -1)
+
+    Hh, Ff, Ee = layer.H, layer.F, layer.E
+    rc = layout.unpack_codes(layer.router_codes)[:Ee]
+    rs = layout.atoms_to_sf(layer.router_sf, layer.router_rows, Hh)[:Ee]
+    g_r = float(1.0 / (layer.router_alpha * layer.gs_x))
+    experts, logical = [], []
+    a1 = layer.w1_alpha.cpu().numpy().astype(np.float64)
+    a2 = layer.w2_alpha.cpu().numpy().astype(np.float64)
+    s1n, s2n = layer.w1_sf.numel() // (Ee + 1), layer.w2_sf.numel() // (Ee + 1)
+    c1a = layer.w1_codes.view(Ee + 1, 2 * Ff, Hh // 2)
+    c2a = layer.w2_codes.view(Ee + 1, Hh, Ff // 2)
+    for e in range(Ee + 1):
+        c1 = layout.gate_up_deinterleave(layout.unpack_codes(c1a[e]))
+        s1 = layout.gate_up_deinterleave(layout.atoms_to_sf(layer.w1_sf[e * s1n:(e + 1) * s1n], 2 * Ff, Hh))
+        c2 = layout.unpack_codes(c2a[e])
+        s2 = layout.atoms_to_sf(layer.w2_sf[e * s2n:(e + 1) * s2n], Hh, Ff)
+        g1, g2 = float(1.0 / (a1[e] * layer.gs_x)), float(1.0 / (a2[e] * layer.gs_h))
+        experts.append((deq(c1, s1, g1).cpu().numpy(), deq(c2, s2, g2).cpu().numpy()))
+        logical.append((None, None, g1, None, None, g2))
+        del c1, s1, c2, s2
+    dense = {"router": deq(rc, rs, g_r).cpu().numpy(), "experts": experts}
+    p = {"H": Hh, "F": Ff, "E": Ee, "gs_x": layer.gs_x, "gs_h": layer.gs_h, "router": (None, None, g_r),
+         "experts": [(np.empty((2 * Ff, 0), dtype=np.uint8),) + tuple(l[1:]) for l in logical]}
+    return p, dense
+
+
+def _e4m3_table():
+    out = []
+    for c in range(256):
+        s, e, m = c >> 7, (c >> 3) & 0xF, c & 7
+        v = float("nan") if (e == 15 and m == 7) else (m * 2.0 ** -9 if e == 0 else (1 + m / 8) * 2.0 ** (e - 7))
+        out.append(-v if s else v)
+    return out
+
+
+def time_oracle(p: dict, dense: dict, x_np, reps: int = 1) -> float:
+    """Seconds per forward of the CPU restatement over x_np (weights already fp32)."""
+    from oracle import moe as omoe
+
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        omoe.moe_forward(x_np, p, K_TOP, dense=dense)
+    return (time.perf_counter() - t0) / reps
+
+
+# ---------------------------------------------------------------------------------------------- runs
+def build_layer(device, T: int, rank: int):
+    import __graft_entry__
+
+    __graft_entry__.import_package()
+    from ssengine_b200 import moe, weights
+
+    p = weights.moe_logical(SEED, H, F, E, device=device)
+    layer = moe.MoELayer.from_logical(p, K_TOP, device)
+    del p
+    x = weights.hidden_states(SEED + 1 + rank, T, H, device=device)
+    return layer, x
+
+
+def run_reference(args, rank: int) -> None:
+    """CPU restatement of the path on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+
+    torch.set_num_threads(cpu_threads())
+    device = "cuda:0" if torch.cuda.is_available() else "cpu"
+    layer_T = args.tokens
+    sample = min(args.cpu_tokens, layer_T)
+    from ssengine_b200 import weights
+
+    if device == "cpu":
+        raise SystemExit(json.dumps({"impl": "reference", "unavailable": "needs the GPU box to build the weights"}))
+    layer, x = build_layer(device, layer_T, 0)
+    p, dense = dense_on_host(layer)
+    x_np = x[:sample].float().cpu().numpy()
+    del layer
+    torch.cuda.empty_cache()
+    for _ in range(args.warmup):
+        time_oracle(p, dense, x_np)
+    t = [time_oracle(p, dense, x_np) for _ in range(args.steps)]
+    sec = sum(t) / len(t)
+    v = sample / sec
+    line = {"impl": "reference", "metric": "prefill tok/s", "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (dequantized NVFP4 weights)",
+            "data": "synthetic: hidden N(0,1) bf16, seeded random-init NVFP4 weights",
+            "config": {"workload": workload(layer_T), "sample_tokens": sample},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
+                             "sample": f"{sample} of the {layer_T} tokens per step through oracle.moe.moe_forward "
+                                       f"(numpy fp32, weights dequantized before timing)"},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    del np
+
+
+def main() -> None:
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+
+    import __graft_entry__
+
+    __graft_entry__.import_package()
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    from ssengine_b200 import lib
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    T = args.tokens
+    layer, x = build_layer(device, T, rank)
+    out = torch.empty_like(x)
+    steps, warm = args.steps, max(3, args.warmup)
+    for _ in range(warm):
+        layer.forward(x, out)
+    torch.cuda.synchronize()
+    layer.check_status()
+
+    # clocks: sample through ~1 s of the same work right before the timed region and through the timed region
+    props = torch.cuda.get_device_properties(device)
+    gpu_id = str(getattr(props, "uuid", local))
+    gpu_id = gpu_id if gpu_id.startswith("GPU-") or not gpu_id.count("-") else "GPU-" + gpu_id
+    clocks = Clocks(gpu_id)
+    clocks.start()
+    t_end = time.time() + 1.0
+    while time.time() < t_end:
+        layer.forward(x, out)
+        torch.cuda.synchronize()
+
+    nst = len(lib.MOE_STEPS)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nst + 1)] for _ in range(steps)]
+    for row in evs:
+        for e in row:
+            e.record()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(steps):
+        layer.forward_profiled(x, out, evs[i])
+    end.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if dist is not None:
+        dist.barrier()
+    layer.check_status()
+    elapsed_ms = start.elapsed_time(end)
+    per_kernel = {name: statistics.mean(evs[i][s].elapsed_time(evs[i][s + 1]) for i in range(steps))
+                  for s, name in enumerate(lib.MOE_STEPS)}
+
+    # e2e through the public API, host buffers: pinned input -> device -> forward -> pinned output
+    e2e_ms = None
+    if not args.no_e2e:
+        xh = x.cpu().pin_memory()
+        oh = torch.empty_like(xh).pin_memory()
+        xd = torch.empty_like(x)
+        for _ in range(warm):
+            xd.copy_(xh, non_blocking=True)
+            oh.copy_(layer.forward(xd), non_blocking=True)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            xd.copy_(xh, non_blocking=True)
+            oh.copy_(layer.forward(xd), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1)
+        layer.check_status()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    elapsed_ms = max_over_ranks(elapsed_ms)
+    e2e_ms = max_over_ranks(e2e_ms) if e2e_ms is not None else None
+    gate_ms = max_over_ranks(per_kernel["gate_up_gemm"])
+
+    if rank == 0:
+        pk, src = peaks()
+        ms_step = elapsed_ms / steps
+        value = world * T * steps / (elapsed_ms / 1e3)
+        gate_flops = 2.0 * (T * K_TOP + T) * (2 * F) * H
+        fp4_peak = 4.0 * pk["bf16_tflops"]
+        achieved = gate_flops / (gate_ms / 1e3) / 1e12
+        line = {
+            "metric": "prefill tok/s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": warm, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e2m1, ue4m3 per-16 scales, fp32 accumulate)",
+            "data": "synthetic: hidden N(0,1) bf16, seeded random-init NVFP4 weights",
+            "config": {"workload": workload(T), "global_batch": world * T, "seq_len": T,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single stage slice",
+                       "l2": "inputs larger than L2 (0.9 GB of expert weights + 1 GB workspace per step)"},
+            "roofline": {"kernel": "gate_up grouped NVFP4 GEMM (SwiGLU + requant epilogue)", "bound": "tensor",
+                         "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
+                         "traffic": None,
+                         "peak_source": f"4 x {src} dense bf16 {pk['bf16_tflops']} TFLOP/s (B200 dense NVFP4 rate "
+                                        f"is 4x bf16)",
+                         "algorithmic": f"2 * {T * K_TOP + T} rows * {2 * F} * {H} = {gate_flops:.4e} FLOP/launch",
+                         "layer_frac": layer_flops(T) / (ms_step / 1e3) / 1e12 / fp4_peak},
+            "kernels_ms": {k: round(v, 5) for k, v in per_kernel.items()},
+            "gpu_launches": steps * nst,
+            "clocks": clk,
+        }
+        if e2e_ms is not None:
+            line["e2e"] = {"value": world * T * steps / (e2e_ms / 1e3), "unit": "tok/s",
+                           "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2}
+        if world == 1 and not args.no_cpu_baseline:
+            import numpy as np
+
+            torch.set_num_threads(cpu_threads())
+            p, dense = dense_on_host(layer)
+            sample = min(args.cpu_tokens, T)
+            x_np = x[:sample].float().cpu().numpy()
+            time_oracle(p, dense, x_np[: min(64, sample)])
+            sec = time_oracle(p, dense, x_np)
+            line["cpu_baseline"] = {"value": sample / sec, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
+                                    "sample": f"{sample} of the {T} tokens through oracle.moe.moe_forward (numpy "
+                                              f"fp32, weights dequantized before timing), {sec:.2f} s"}
+            del np
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,124 @@
+/* C ABI of the B200 prefill-stage library (libssengine_b200.so, sm_100a).
+ *
+ * Conventions (the style of the reference's only native ABI, ssengine/native/kda_split_heads.cpp:17-19: plain
+ * pointers and sizes, an int return code, out-parameters):
+ * - every pointer argument named *_codes, *_sf, x, out, ws, logits, ids, weights, status is DEVICE memory owned by
+ *   the caller; the library never allocates device memory;
+ * - `stream` is a cudaStream_t passed as void*; every entry point only enqueues work on it (no host sync);
+ * - return 0 on success, else an ssb status code (1 bad arguments, 2 CUDA launch error, 3 workspace too small,
+ *   5 driver entry point missing); device-side failures (4 a bounded wait expired, 6 a table overflowed) are written
+ *   to the caller's int32 device `status` word (first error wins), read by the caller after the stream's work ends;
+ * - NVFP4 operands: e2m1 codes packed two per byte (even element in the low nibble), rows K/2 bytes apart; scales
+ *   are e4m3 bytes in the 128x4-atom layout: rows padded to 128, K padded to 256, atom (row block rb, atom column
+ *   cb) at ((rb * ssb_sf_atom_cols(K)) + cb) * 512, scale (r, c) at byte (r % 32) * 16 + ((r / 32) % 4) * 4 + c % 4.
+ */
+#ifndef SSENGINE_B200_H_
+#define SSENGINE_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Library version string. */
+const char* ssb_version(void);
+
+/* Scale atom columns per 128-row block for a reduction length K (K padded to 256, 4 atoms per 256). */
+int64_t ssb_sf_atom_cols(int64_t K);
+
+/* NVFP4 quantization of bf16 rows with a static global scale `gs`:
+ *   sf = e4m3((amax16 / 6) * gs), code = e2m1(x * (gs / sf)), each step one IEEE fp32 operation.
+ * x [rows, K] bf16 (row pitch ldx elements), codes [rows, ldc bytes], sf atoms (rows padded to 128).
+ * Replaces the reference's activation quantizers, vLLM `scaled_fp4_quant` at ssengine/kernels.py:109-111 (config 8),
+ * :116-118 (config 10) and :179-181 (config 29). */
+int ssb_nvfp4_quantize(const void* x, int64_t rows, int64_t K, int64_t ldx, float gs, uint8_t* codes, int64_t ldc,
+                       uint8_t* sf, void* stream);
+
+/* Output stage selectors of ssb_nvfp4_gemm. */
+#define SSB_EPI_F32 0    /* out fp32 [M, ldo] = alpha * A x B^T, columns < N */
+#define SSB_EPI_BF16 1   /* out bf16 [M, ldo] = alpha * A x B^T (N % 256 == 0) */
+#define SSB_EPI_SWIGLU 2 /* B rows in 256-row tiles of 128 gate + 128 up rows; h = silu(alpha g) * (alpha u),
+                            quantized to NVFP4 with global scale out_gs: out = codes [M, ldo bytes], out_sf atoms */
+
+/* Dense NVFP4 GEMM D = alpha * A x B^T on tcgen05 tensor cores (e2m1 x e2m1, ue4m3 scales per 16 elements applied
+ * in the MMA, fp32 accumulation in TMEM). A [M, K] codes + scales, B [N, K] codes + scales (rows padded to 128 in the
+ * scale layout), K % 64 == 0. Replaces the reference's NVFP4 dense projections, FlashInfer `mm_fp4` at
+ * ssengine/kernels.py:112-121 (configs 9, 11), and (with BASELINE's NVFP4 projections) the BF16 router / shared
+ * expert / projection GEMMs at :174-178, :188-193. */
+int ssb_nvfp4_gemm(int32_t epilogue, const uint8_t* a_codes, const uint8_t* a_sf, int64_t M, int64_t K,
+                   const uint8_t* b_codes, const uint8_t* b_sf, int64_t N, float alpha, void* out, int64_t ldo,
+                   uint8_t* out_sf, float out_gs, int32_t* status, void* stream);
+
+/* MoE routing: softmax over the top-k logits of each token; selection by value descending, ties to the lower expert
+ * index; slots in rank order. logits fp32 [T, E] (E <= 512), ids int32 [T, k], weights fp32 [T, k].
+ * Replaces the routing stage of FlashInfer `trtllm_fp4_block_scale_moe` (ssengine/kernels.py:182-187, config 30). */
+int ssb_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* ids, float* weights, void* stream);
+
+/* One NVFP4 MoE layer's device parameters (all pointers device memory, owned by the caller).
+ * Experts 0..E-1 are routed, expert E is the shared expert (every token, weight 1). */
+typedef struct ssb_moe_layer {
+  int32_t hidden;              /* H, % 256 == 0 */
+  int32_t inter;               /* F (expert intermediate), % 128 == 0 */
+  int32_t num_experts;         /* E routed experts, <= 512 */
+  int32_t top_k;               /* k, < 32 */
+  float gs_x;                  /* global scale of the layer input's NVFP4 quantization */
+  float gs_h;                  /* global scale of the SwiGLU output's NVFP4 quantization */
+  const uint8_t* router_codes; /* [router_rows, H/2], rows >= E zero */
+  const uint8_t* router_sf;    /* atoms of [router_rows, H] */
+  int64_t router_rows;         /* E padded to a multiple of 128 */
+  float router_alpha;          /* 1 / (gs_x * gs_router) */
+  const uint8_t* w1_codes;     /* [(E+1) * 2F, H/2]; per expert 256-row tiles of 128 gate + 128 up rows */
+  const uint8_t* w1_sf;        /* atoms of [(E+1) * 2F, H] */
+  const float* w1_alpha;       /* [E+1]: 1 / (gs_x * gs_w1[e]) */
+  const uint8_t* w2_codes;     /* [(E+1) * H, F/2] */
+  const uint8_t* w2_sf;        /* atoms of [(E+1) * H, F] */
+  const float* w2_alpha;       /* [E+1]: 1 / (gs_h * gs_w2[e]) */
+} ssb_moe_layer;
+
+/* Workspace of ssb_moe_forward for T tokens, in bytes (one caller-owned device buffer, 256-byte aligned). */
+int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T);
+
+/* Byte offsets of the workspace's buffers (SSB_WS_* below) for T tokens; n = entries to fill. Lets a caller read the
+ * intermediate routing / permutation / activation buffers of the last forward. */
+#define SSB_WS_XQ 0          /* uint8 [Tpad, H/2] input codes (token order) */
+#define SSB_WS_XSF 1         /* input scale atoms */
+#define SSB_WS_LOGITS 2      /* fp32 [T, E] router logits */
+#define SSB_WS_IDS 3         /* int32 [T, k] routed experts */
+#define SSB_WS_WEIGHTS 4     /* fp32 [T, k] routing weights */
+#define SSB_WS_ROWS 5        /* int32 [T, k] permuted row of each (token, slot) */
+#define SSB_WS_COUNTS 6      /* int32 [E+1] tokens per expert (shared last) */
+#define SSB_WS_OFFSETS 7     /* int32 [E+2] first permuted row per expert (128-aligned), total rows last */
+#define SSB_WS_MASKS 8
+#define SSB_WS_BLOCKS 9
+#define SSB_WS_MTILES 10     /* int32 [cap, 4] GEMM row tiles {expert, first row, rows, 0} */
+#define SSB_WS_NUM_MTILES 11 /* int32 [1] */
+#define SSB_WS_XQ_PERM 12    /* uint8 [cap*128, H/2] permuted input codes */
+#define SSB_WS_XSF_PERM 13
+#define SSB_WS_ACT 14        /* uint8 [cap*128, F/2] SwiGLU output codes */
+#define SSB_WS_ACT_SF 15
+#define SSB_WS_Y 16          /* bf16 [cap*128, H] expert outputs per permuted row */
+#define SSB_WS_END 17
+int ssb_moe_workspace_offsets(const ssb_moe_layer* layer, int64_t T, int64_t* offsets, int32_t n);
+
+/* Whole MoE layer on `stream`: quantize x -> router GEMM -> top-k routing -> permutation + gather -> grouped NVFP4
+ * gate_up GEMM with SwiGLU + NVFP4 requant epilogue -> grouped down GEMM -> weighted combine (+ shared expert).
+ * x bf16 [T, H] (contiguous), out bf16 [T, H]. Replaces the MoE block of a reference MoE layer
+ * (ssengine/kernels.py:174-193: configs 28-32, the router GEMM, the input quant, FlashInfer
+ * `trtllm_fp4_block_scale_moe` and the shared expert's two GEMMs). */
+int ssb_moe_forward(const ssb_moe_layer* layer, const void* x, int64_t T, void* out, void* ws, int64_t ws_bytes,
+                    int32_t* status, void* stream);
+
+/* ssb_moe_forward with a cudaEvent_t recorded on `stream` before each of its SSB_MOE_STEPS launch steps and one after
+ * the last (events: SSB_MOE_STEPS + 1 created events; steps: input quant, router GEMM, route, count, offsets,
+ * scatter, gate_up GEMM, down GEMM, combine). For per-kernel device timing; the same work as ssb_moe_forward.
+ * No counterpart in the reference (its per-kernel timing comes from nsys traces, benchmarks/nsys_trace.py:121-160). */
+#define SSB_MOE_STEPS 9
+int ssb_moe_forward_profiled(const ssb_moe_layer* layer, const void* x, int64_t T, void* out, void* ws,
+                             int64_t ws_bytes, int32_t* status, void* stream, void* const* events);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SSENGINE_B200_H_ */

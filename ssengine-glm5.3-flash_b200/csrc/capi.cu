@@ -1,0 +1,296 @@
+// extern "C" entry points of libssengine_b200.so (declared in include/ssengine_b200.h).
+// Host-side argument checks, the MoE workspace layout and the launch sequence of one MoE layer.
+
+#include <cstring>
+
+#include "../../include/ssengine_b200.h"
+#include "common.cuh"
+#include "ops.h"
+
+namespace {
+
+using ssb::kErrArgs;
+using ssb::kErrWorkspace;
+using ssb::kOk;
+
+int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+struct MoeDims {
+  int64_t T, H, F, E, k, Tpad, rcap, mtile_cap, nblocks, ncbH, ncbF;
+};
+
+bool dims_of(const ssb_moe_layer* L, int64_t T, MoeDims& d) {
+  if (L == nullptr || T < 0) return false;
+  d.T = T;
+  d.H = L->hidden;
+  d.F = L->inter;
+  d.E = L->num_experts;
+  d.k = L->top_k;
+  if (d.H <= 0 || d.H % 256 != 0 || d.F <= 0 || d.F % 128 != 0 || d.E <= 0 || d.E > 512 || d.k <= 0 || d.k >= 32 ||
+      d.k > d.E)
+    return false;
+  d.Tpad = ceil_div(T > 0 ? T : 1, 128) * 128;
+  d.rcap = ceil_div(T * (d.k + 1) + (d.E + 1) * 127, 128) * 128;
+  if (d.rcap < 128) d.rcap = 128;
+  d.mtile_cap = d.rcap / 128;
+  d.nblocks = ceil_div(T > 0 ? T : 1, 256);
+  d.ncbH = ssb::sf_atom_cols(d.H);
+  d.ncbF = ssb::sf_atom_cols(d.F);
+  return true;
+}
+
+void layout(const MoeDims& d, int64_t* off) {
+  int64_t sz[SSB_WS_END];
+  sz[SSB_WS_XQ] = d.Tpad * d.H / 2;
+  sz[SSB_WS_XSF] = (d.Tpad / 128) * d.ncbH * 512;
+  sz[SSB_WS_LOGITS] = d.T * d.E * 4;
+  sz[SSB_WS_IDS] = d.T * d.k * 4;
+  sz[SSB_WS_WEIGHTS] = d.T * d.k * 4;
+  sz[SSB_WS_ROWS] = d.T * d.k * 4;
+  sz[SSB_WS_COUNTS] = (d.E + 1) * 4;
+  sz[SSB_WS_OFFSETS] = (d.E + 2) * 4;
+  sz[SSB_WS_MASKS] = d.nblocks * d.E * 8 * 4;
+  sz[SSB_WS_BLOCKS] = d.nblocks * d.E * 4;
+  sz[SSB_WS_MTILES] = d.mtile_cap * 16;
+  sz[SSB_WS_NUM_MTILES] = 16;
+  sz[SSB_WS_XQ_PERM] = d.rcap * d.H / 2;
+  sz[SSB_WS_XSF_PERM] = (d.rcap / 128) * d.ncbH * 512;
+  sz[SSB_WS_ACT] = d.rcap * d.F / 2;
+  sz[SSB_WS_ACT_SF] = (d.rcap / 128) * d.ncbF * 512;
+  sz[SSB_WS_Y] = d.rcap * d.H * 2;
+  int64_t o = 0;
+  for (int i = 0; i < SSB_WS_END; ++i) {
+    off[i] = o;
+    o += align256(sz[i] > 0 ? sz[i] : 16);
+  }
+  off[SSB_WS_END] = o;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+const char* ssb_version(void) { return "ssengine_b200 0.1 (sm_100a)"; }
+
+int64_t ssb_sf_atom_cols(int64_t K) { return ssb::sf_atom_cols(K); }
+
+int ssb_nvfp4_quantize(const void* x, int64_t rows, int64_t K, int64_t ldx, float gs, uint8_t* codes, int64_t ldc,
+                       uint8_t* sf, void* stream) {
+  if (x == nullptr || codes == nullptr || sf == nullptr || rows < 0) return kErrArgs;
+  return ssb::launch_nvfp4_quantize(x, rows, K, ldx, gs, codes, ldc, sf, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_nvfp4_gemm(int32_t epilogue, const uint8_t* a_codes, const uint8_t* a_sf, int64_t M, int64_t K,
+                   const uint8_t* b_codes, const uint8_t* b_sf, int64_t N, float alpha, void* out, int64_t ldo,
+                   uint8_t* out_sf, float out_gs, int32_t* status, void* stream) {
+  if (a_codes == nullptr || a_sf == nullptr || b_codes == nullptr || b_sf == nullptr || out == nullptr || M < 0 ||
+      K <= 0 || N <= 0 || M > (1ll << 30) || N > (1ll << 30))
+    return kErrArgs;
+  if (!aligned16(a_codes) || !aligned16(b_codes) || !aligned16(out) || (K / 2) % 16 != 0) return kErrArgs;
+  if (epilogue == SSB_EPI_F32 && (ldo % 4 != 0 || ldo < N)) return kErrArgs;
+  if (epilogue == SSB_EPI_BF16 && ldo < N) return kErrArgs;
+  if (epilogue == SSB_EPI_SWIGLU && (out_sf == nullptr || ldo < N / 4)) return kErrArgs;
+  if (M == 0) return kOk;
+  ssb::GemmArgs g;
+  g.sfa = a_sf;
+  g.sfb = b_sf;
+  g.M = static_cast<int32_t>(M);
+  g.K = static_cast<int32_t>(K);
+  g.N = static_cast<int32_t>(N);
+  g.ncb_k = static_cast<int32_t>(ssb::sf_atom_cols(K));
+  g.alpha_scalar = alpha;
+  g.out = out;
+  g.ldo = ldo;
+  g.out_sf = out_sf;
+  g.out_ncb = static_cast<int32_t>(ssb::sf_atom_cols(N / 2));
+  g.out_gs = out_gs;
+  g.status = status;
+  const int64_t b_rows = epilogue == SSB_EPI_F32 ? ceil_div(N, 128) * 128 : N;
+  return ssb::launch_gemm_nvfp4(epilogue, a_codes, M, K / 2, b_codes, b_rows, K / 2, g, ssb::device_sm_count(),
+                                static_cast<cudaStream_t>(stream));
+}
+
+int ssb_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* ids, float* weights, void* stream) {
+  if (logits == nullptr || ids == nullptr || weights == nullptr || T < 0) return kErrArgs;
+  return ssb::launch_moe_route(logits, T, E, k, ids, weights, static_cast<cudaStream_t>(stream));
+}
+
+int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T) {
+  MoeDims d;
+  if (!dims_of(layer, T, d)) return -1;
+  int64_t off[SSB_WS_END + 1];
+  layout(d, off);
+  return off[SSB_WS_END];
+}
+
+int ssb_moe_workspace_offsets(const ssb_moe_layer* layer, int64_t T, int64_t* offsets, int32_t n) {
+  MoeDims d;
+  if (!dims_of(layer, T, d) || offsets == nullptr || n < 0) return kErrArgs;
+  int64_t off[SSB_WS_END + 1];
+  layout(d, off);
+  for (int i = 0; i < n && i <= SSB_WS_END; ++i) offsets[i] = off[i];
+  return kOk;
+}
+
+}  // extern "C"
+
+namespace {
+
+// The layer's launch sequence; when `events` is not null, events[i] is recorded before step i and events[9] after the
+// last (steps: quantize, router GEMM, route, count, offsets, scatter, gate_up GEMM, down GEMM, combine).
+int moe_forward(const ssb_moe_layer* L, const void* x, int64_t T, void* out, void* ws, int64_t ws_bytes,
+                int32_t* status, void* stream_, void* const* events) {
+  MoeDims d;
+  if (!dims_of(L, T, d)) return kErrArgs;
+  if (T == 0) return kOk;
+  if (x == nullptr || out == nullptr || ws == nullptr) return kErrArgs;
+  if (L->router_codes == nullptr || L->router_sf == nullptr || L->w1_codes == nullptr || L->w1_sf == nullptr ||
+      L->w1_alpha == nullptr || L->w2_codes == nullptr || L->w2_sf == nullptr || L->w2_alpha == nullptr ||
+      L->router_rows < d.E || L->router_rows % 128 != 0)
+    return kErrArgs;
+  if (!aligned16(x) || !aligned16(out) || (reinterpret_cast<uintptr_t>(ws) & 255)) return kErrArgs;
+  int64_t off[SSB_WS_END + 1];
+  layout(d, off);
+  if (ws_bytes < off[SSB_WS_END]) return kErrWorkspace;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  auto at = [&](int i) { return w + off[i]; };
+  uint8_t* xq = at(SSB_WS_XQ);
+  uint8_t* xsf = at(SSB_WS_XSF);
+  float* logits = reinterpret_cast<float*>(at(SSB_WS_LOGITS));
+  int32_t* ids = reinterpret_cast<int32_t*>(at(SSB_WS_IDS));
+  float* wts = reinterpret_cast<float*>(at(SSB_WS_WEIGHTS));
+  int32_t* rows = reinterpret_cast<int32_t*>(at(SSB_WS_ROWS));
+  int32_t* counts = reinterpret_cast<int32_t*>(at(SSB_WS_COUNTS));
+  int32_t* offsets = reinterpret_cast<int32_t*>(at(SSB_WS_OFFSETS));
+  uint32_t* masks = reinterpret_cast<uint32_t*>(at(SSB_WS_MASKS));
+  int32_t* bcounts = reinterpret_cast<int32_t*>(at(SSB_WS_BLOCKS));
+  int32_t* mtiles = reinterpret_cast<int32_t*>(at(SSB_WS_MTILES));
+  int32_t* num_mtiles = reinterpret_cast<int32_t*>(at(SSB_WS_NUM_MTILES));
+  uint8_t* xqp = at(SSB_WS_XQ_PERM);
+  uint8_t* xsfp = at(SSB_WS_XSF_PERM);
+  uint8_t* act = at(SSB_WS_ACT);
+  uint8_t* asf = at(SSB_WS_ACT_SF);
+  void* y = at(SSB_WS_Y);
+  const int sms = ssb::device_sm_count();
+  int rc;
+  auto mark = [&](int i) {
+    if (events != nullptr) cudaEventRecord(static_cast<cudaEvent_t>(events[i]), stream);
+  };
+
+  // 1. input quantization (token order)
+  mark(0);
+  rc = ssb::launch_nvfp4_quantize(x, T, d.H, d.H, L->gs_x, xq, d.H / 2, xsf, stream);
+  if (rc != kOk) return rc;
+  // 2. router logits
+  mark(1);
+  {
+    ssb::GemmArgs g;
+    g.sfa = xsf;
+    g.sfb = L->router_sf;
+    g.M = static_cast<int32_t>(T);
+    g.K = static_cast<int32_t>(d.H);
+    g.N = static_cast<int32_t>(d.E);
+    g.ncb_k = static_cast<int32_t>(d.ncbH);
+    g.alpha_scalar = L->router_alpha;
+    g.out = logits;
+    g.ldo = d.E;
+    g.status = status;
+    if (d.E % 4 != 0) return kErrArgs;   // fp32 rows of the logits are stored as 16-byte vectors
+    rc = ssb::launch_gemm_nvfp4(ssb::kEpiF32, xq, d.Tpad, d.H / 2, L->router_codes, L->router_rows, d.H / 2, g, sms,
+                                stream);
+    if (rc != kOk) return rc;
+  }
+  // 3. routing, 4. permutation
+  mark(2);
+  rc = ssb::launch_moe_route(logits, T, static_cast<int32_t>(d.E), static_cast<int32_t>(d.k), ids, wts, stream);
+  if (rc != kOk) return rc;
+  mark(3);
+  rc = ssb::launch_moe_count(ids, T, static_cast<int32_t>(d.E), static_cast<int32_t>(d.k), masks, bcounts, stream);
+  if (rc != kOk) return rc;
+  mark(4);
+  rc = ssb::launch_moe_offsets(T, static_cast<int32_t>(d.E), bcounts, counts, offsets, mtiles, num_mtiles,
+                               static_cast<int32_t>(d.mtile_cap), status, stream);
+  if (rc != kOk) return rc;
+  mark(5);
+  rc = ssb::launch_moe_scatter(ids, T, static_cast<int32_t>(d.E), static_cast<int32_t>(d.k), masks, bcounts, offsets,
+                               rows, xq, xsf, d.H, xqp, xsfp, stream);
+  if (rc != kOk) return rc;
+  // 5. grouped gate_up GEMM, SwiGLU + NVFP4 requant epilogue. When F is not a multiple of 256 the down GEMM's last
+  //    k-block reads scale atoms past F that the epilogue never writes: they must hold zeros (finite scales times the
+  //    zero-filled codes), not stale bytes.
+  mark(6);
+  if (d.F % 256 != 0 &&
+      cudaMemsetAsync(asf, 0, static_cast<size_t>((d.rcap / 128) * d.ncbF * 512), stream) != cudaSuccess)
+    return ssb::kErrCuda;
+  {
+    ssb::GemmArgs g;
+    g.sfa = xsfp;
+    g.sfb = L->w1_sf;
+    g.mtiles = mtiles;
+    g.num_mtiles = num_mtiles;
+    g.mtile_cap = static_cast<int32_t>(d.mtile_cap);
+    g.K = static_cast<int32_t>(d.H);
+    g.N = static_cast<int32_t>(2 * d.F);
+    g.ncb_k = static_cast<int32_t>(d.ncbH);
+    g.alpha = L->w1_alpha;
+    g.out = act;
+    g.ldo = d.F / 2;
+    g.out_sf = asf;
+    g.out_ncb = static_cast<int32_t>(d.ncbF);
+    g.out_gs = L->gs_h;
+    g.status = status;
+    rc = ssb::launch_gemm_nvfp4(ssb::kEpiSwiGLU, xqp, d.rcap, d.H / 2, L->w1_codes, (d.E + 1) * 2 * d.F, d.H / 2, g,
+                                sms, stream);
+    if (rc != kOk) return rc;
+  }
+  // 6. grouped down GEMM -> bf16 rows
+  mark(7);
+  {
+    ssb::GemmArgs g;
+    g.sfa = asf;
+    g.sfb = L->w2_sf;
+    g.mtiles = mtiles;
+    g.num_mtiles = num_mtiles;
+    g.mtile_cap = static_cast<int32_t>(d.mtile_cap);
+    g.K = static_cast<int32_t>(d.F);
+    g.N = static_cast<int32_t>(d.H);
+    g.ncb_k = static_cast<int32_t>(d.ncbF);
+    g.alpha = L->w2_alpha;
+    g.out = y;
+    g.ldo = d.H;
+    g.status = status;
+    rc = ssb::launch_gemm_nvfp4(ssb::kEpiBF16, act, d.rcap, d.F / 2, L->w2_codes, (d.E + 1) * d.H, d.F / 2, g, sms,
+                                stream);
+    if (rc != kOk) return rc;
+  }
+  // 7. weighted combine + shared expert
+  mark(8);
+  rc = ssb::launch_moe_combine(y, d.H, rows, wts, offsets, T, static_cast<int32_t>(d.E), static_cast<int32_t>(d.k),
+                               out, stream);
+  if (rc != kOk) return rc;
+  mark(9);
+  return kOk;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ssb_moe_forward(const ssb_moe_layer* L, const void* x, int64_t T, void* out, void* ws, int64_t ws_bytes,
+                    int32_t* status, void* stream) {
+  return moe_forward(L, x, T, out, ws, ws_bytes, status, stream, nullptr);
+}
+
+int ssb_moe_forward_profiled(const ssb_moe_layer* L, const void* x, int64_t T, void* out, void* ws, int64_t ws_bytes,
+                             int32_t* status, void* stream, void* const* events) {
+  if (events == nullptr) return kErrArgs;
+  for (int i = 0; i <= SSB_MOE_STEPS; ++i)
+    if (events[i] == nullptr) return kErrArgs;
+  return moe_forward(L, x, T, out, ws, ws_bytes, status, stream, events);
+}
+
+}  // extern "C"

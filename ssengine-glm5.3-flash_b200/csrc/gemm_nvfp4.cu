@@ -1,0 +1,428 @@
+// Persistent grouped NVFP4 GEMM for sm_100a: TMA-fed shared-memory pipeline, tcgen05 block-scaled MMA
+// (kind::mxf4nvf4, ue4m3 scale per 16 elements applied inside the MMA), fp32 accumulator in TMEM, fused epilogues.
+//
+//   D[m, n] = alpha[g] * sum_k (a[m, k] * sfa[m, k/16]) * (b[g*N + n, k] * sfb[g*N + n, k/16])
+//
+// Roles (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: A tile 128 x 256 (e2m1, 128-byte swizzle), B tile BN x 256, and their scale atoms by
+//               plain bulk copies; STAGES-deep ring of shared-memory stages guarded by full/empty mbarriers.
+//   warp 1      TMEM owner and MMA issuer (one thread): per k-block copies the scale atoms into TMEM
+//               (tcgen05.cp 32x128b.warpx4) and issues 4 MMAs of K = 64; tcgen05.commit frees the stage and, after the
+//               tile's last k-block, signals the accumulator full.
+//   warps 2-5   epilogue: each warp reads its TMEM lane quadrant (32 rows) with tcgen05.ld and runs the output stage.
+// Tiles are M-major over N tiles (consecutive CTAs share the A row block and walk one expert's weights), so an
+// expert's weights stay in L2 while its row blocks are in flight.
+// Every wait is bounded (common.cuh); on expiry all roles leave, in-flight copies and MMAs are drained with bounded
+// waits, TMEM is freed and the status word holds kErrTimeout.
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace ssb {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBKBytes = 128;   // one k-block: 256 e2m1 elements = 128 bytes = one 128-byte swizzle row
+constexpr int kThreads = 192;
+
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = kBM * kBKBytes;               // 16 KB
+  static constexpr int B_BYTES = BN * kBKBytes;
+  static constexpr int SFA_BYTES = 2048;                        // 4 atoms (128 rows x 64 K each)
+  static constexpr int SFB_BYTES = (BN / 128) * 2048;
+  static constexpr int TX_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_SFA = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_SFB = OFF_SFA + STAGES * SFA_BYTES;
+  static constexpr int OFF_BAR = OFF_SFB + STAGES * SFB_BYTES;  // full[S], empty[S], acc_full, acc_empty, drain
+  static constexpr int OFF_MISC = OFF_BAR + (2 * STAGES + 3) * 8;
+  static constexpr int SMEM = OFF_MISC + 16 + 1024;             // + alignment slack
+  // TMEM columns: accumulator [0, BN), A scales 16 columns, B scales 4 * BN / 32 columns
+  static constexpr int SFA_COL = BN;
+  static constexpr int SFB_COL = BN + 16;
+  static constexpr int TMEM_COLS = (BN + 16 + BN / 8) <= 256 ? 256 : 512;
+};
+
+struct TileInfo {
+  int group, row0, rows, nt;
+};
+
+SSB_DEVICE bool tile_info(const GemmArgs& a, int t, int n_tiles, TileInfo& ti) {
+  const int mt = t / n_tiles;
+  ti.nt = t - mt * n_tiles;
+  if (a.mtiles == nullptr) {
+    ti.group = 0;
+    ti.row0 = mt * kBM;
+    ti.rows = min(kBM, a.M - ti.row0);
+  } else {
+    const int4 e = reinterpret_cast<const int4*>(a.mtiles)[mt];
+    ti.group = e.x;
+    ti.row0 = e.y;
+    ti.rows = e.z;
+  }
+  return ti.rows > 0;
+}
+
+SSB_DEVICE int total_tiles(const GemmArgs& a, int n_tiles) {
+  int num_m;
+  if (a.mtiles == nullptr) {
+    num_m = (a.M + kBM - 1) / kBM;
+  } else {
+    num_m = min(*a.num_mtiles, a.mtile_cap);
+  }
+  return num_m * n_tiles;
+}
+
+// Bounded wait that ignores the abort flag: used only to drain copies / MMAs already in flight before exit.
+SSB_DEVICE void drain_wait(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitNs) break;
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const GemmArgs args) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar_full = sbase + C::OFF_BAR;
+  const uint32_t bar_empty = bar_full + C::STAGES * 8;
+  const uint32_t bar_acc_full = bar_empty + C::STAGES * 8;
+  const uint32_t bar_acc_empty = bar_acc_full + 8;
+  const uint32_t bar_drain = bar_acc_empty + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + C::OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_acc_full, 1);
+    mbar_init(bar_acc_empty, 4);
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int n_tiles = EPI == kEpiF32 ? (args.N + BN - 1) / BN : args.N / BN;
+  const int num_kb = (args.K + 255) / 256;
+  const int total = total_tiles(args, n_tiles);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        TileInfo ti;
+        if (!tile_info(args, t, n_tiles, ti)) continue;
+        const int brow0 = ti.group * args.N + ti.nt * BN;
+        const uint8_t* sfa = args.sfa + (int64_t)(ti.row0 / kBM) * args.ncb_k * 512;
+        const uint8_t* sfb = args.sfb + (int64_t)(brow0 / kBM) * args.ncb_k * 512;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = bar_full + 8 * stage;
+          mbar_arrive_expect_tx(fb, C::TX_BYTES);
+          tma_load_2d(sbase + C::OFF_A + stage * C::A_BYTES, &tmA, kb * kBKBytes, ti.row0, fb);
+          tma_load_2d(sbase + C::OFF_B + stage * C::B_BYTES, &tmB, kb * kBKBytes, brow0, fb);
+          bulk_load(sbase + C::OFF_SFA + stage * C::SFA_BYTES, sfa + (int64_t)kb * 2048, 2048, fb);
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j)
+            bulk_load(sbase + C::OFF_SFB + stage * C::SFB_BYTES + j * 2048,
+                      sfb + ((int64_t)j * args.ncb_k + kb * 4) * 512, 2048, fb);
+          ++issued;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // drain: the last min(issued, STAGES) loads may still be landing in shared memory
+        int s = stage;
+        uint32_t p = phase;
+        for (int i = 0; i < min(issued, C::STAGES); ++i) {
+          if (--s < 0) {
+            s = C::STAGES - 1;
+            p ^= 1;
+          }
+          drain_wait(bar_full + 8 * s, p);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = idesc_nvf4(kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t iter = 0;
+      bool ok = true;
+      bool any_mma = false;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        TileInfo ti;
+        if (!tile_info(args, t, n_tiles, ti)) continue;
+        if (!mbar_wait(bar_acc_empty, (iter & 1) ^ 1, abort_flag, args.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = sbase + C::OFF_A + stage * C::A_BYTES;
+          const uint32_t sb = sbase + C::OFF_B + stage * C::B_BYTES;
+          const uint32_t ssfa = sbase + C::OFF_SFA + stage * C::SFA_BYTES;
+          const uint32_t ssfb = sbase + C::OFF_SFB + stage * C::SFB_BYTES;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            tc_cp_sf(tmem + C::SFA_COL + 4 * i, smem_desc(ssfa + i * 512, 0, 128, 0));
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              tc_cp_sf(tmem + C::SFB_COL + (BN / 32) * i + 4 * j, smem_desc(ssfb + j * 2048 + i * 512, 0, 128, 0));
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint64_t ad = smem_desc(sa + i * 32, 0, 1024, 2);
+            const uint64_t bd = smem_desc(sb + i * 32, 0, 1024, 2);
+            tc_mma_nvf4(tmem, ad, bd, idesc, (kb | i) != 0 ? 1u : 0u, tmem + C::SFA_COL + 4 * i,
+                        tmem + C::SFB_COL + (BN / 32) * i);
+          }
+          any_mma = true;
+          tc_commit(bar_empty + 8 * stage);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(bar_acc_full);
+        ++iter;
+      }
+      if (!ok && any_mma) {
+        tc_commit(bar_drain);
+        drain_wait(bar_drain, 0);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quad = warp & 3;
+    const int rl = quad * 32 + lane;                       // row inside the tile = TMEM lane
+    const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    uint32_t iter = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      TileInfo ti;
+      if (!tile_info(args, t, n_tiles, ti)) continue;
+      if (!mbar_wait(bar_acc_full, iter & 1, abort_flag, args.status)) break;
+      tc_fence_after();
+      const float alpha = args.alpha != nullptr ? args.alpha[ti.group] : args.alpha_scalar;
+      const bool valid = rl < ti.rows;
+      const int64_t row = (int64_t)ti.row0 + rl;
+      if constexpr (EPI == kEpiSwiGLU) {
+        uint8_t* codes = reinterpret_cast<uint8_t*>(args.out);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float g[32], u[32];
+          tmem_ld_32x32b_x32(tq + 32 * c, g);
+          tmem_ld_32x32b_x32(tq + 128 + 32 * c, u);
+          tmem_ld_wait();
+          float h[2][16];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float gv = g[i] * alpha;
+            const float uv = u[i] * alpha;
+            h[i >> 4][i & 15] = gv / (1.0f + expf(-gv)) * uv;
+          }
+          uint32_t p0[2], p1[2];
+          const uint32_t s0 = nvfp4_quant16(h[0], args.out_gs, p0);
+          const uint32_t s1 = nvfp4_quant16(h[1], args.out_gs, p1);
+          if (valid) {
+            const int col = ti.nt * 128 + 32 * c;   // first h column of this chunk
+            uint4 v = make_uint4(p0[0], p0[1], p1[0], p1[1]);
+            *reinterpret_cast<uint4*>(codes + row * args.ldo + col / 2) = v;
+            const int64_t so = sf_atom_offset(row, col / 16, args.out_ncb);
+            *reinterpret_cast<uint16_t*>(args.out_sf + so) = static_cast<uint16_t>(s0 | (s1 << 8));
+          }
+        }
+      } else if constexpr (EPI == kEpiBF16) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld_32x32b_x32(tq + 32 * c, v);
+          tmem_ld_wait();
+          if (valid) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i] * alpha, v[2 * i + 1] * alpha);
+              w[i] = *reinterpret_cast<uint32_t*>(&b2);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(out + row * args.ldo + ti.nt * BN + 32 * c);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
+        }
+      } else {
+        float* out = reinterpret_cast<float*>(args.out);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld_32x32b_x32(tq + 32 * c, v);
+          tmem_ld_wait();
+          const int col0 = ti.nt * BN + 32 * c;
+          if (valid) {
+            if (col0 + 32 <= args.N) {
+              float4* dst = reinterpret_cast<float4*>(out + row * args.ldo + col0);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                dst[i] = make_float4(v[4 * i] * alpha, v[4 * i + 1] * alpha, v[4 * i + 2] * alpha,
+                                     v[4 * i + 3] * alpha);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < args.N) out[row * args.ldo + col0 + i] = v[i] * alpha;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_acc_empty);
+      ++iter;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// ---- host side ------------------------------------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2D uint8 map over [rows, width bytes] with row pitch `ld` bytes; box = 128 bytes x box_rows, 128-byte swizzle.
+int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t width, int64_t ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return kErrNoDriver;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld & 15) || width <= 0 || rows <= 0) return kErrArgs;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBKBytes), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrArgs;
+}
+
+template <int BN, int EPI>
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int grid, cudaStream_t stream) {
+  using Cf = Cfg<BN>;
+  auto kern = gemm_nvfp4_kernel<BN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM) != cudaSuccess)
+      return kErrCuda;
+    attr_set = true;
+  }
+  kern<<<grid, kThreads, Cf::SMEM, stream>>>(ma, mb, args);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+}  // namespace
+
+int device_sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+int launch_gemm_nvfp4(int epilogue, const uint8_t* a, int64_t a_rows, int64_t lda, const uint8_t* b, int64_t b_rows,
+                      int64_t ldb, const GemmArgs& args, int num_sms, cudaStream_t stream) {
+  if (args.K <= 0 || args.K % 64 != 0 || args.N <= 0) return kErrArgs;
+  if (args.ncb_k != sf_atom_cols(args.K)) return kErrArgs;
+  if ((reinterpret_cast<uintptr_t>(args.sfa) & 15) || (reinterpret_cast<uintptr_t>(args.sfb) & 15)) return kErrArgs;
+  const int BN = epilogue == kEpiF32 ? 128 : 256;
+  if (epilogue != kEpiF32 && args.N % BN != 0) return kErrArgs;
+  if (epilogue == kEpiSwiGLU && (args.ldo % 16 != 0 || args.out_ncb != sf_atom_cols(args.N / 2))) return kErrArgs;
+  if (epilogue == kEpiBF16 && args.ldo % 8 != 0) return kErrArgs;
+  if (args.mtiles == nullptr && args.M <= 0) return kOk;
+  CUtensorMap ma, mb;
+  int rc = make_map(&ma, a, a_rows, args.K / 2, lda, kBM);
+  if (rc != kOk) return rc;
+  rc = make_map(&mb, b, b_rows, args.K / 2, ldb, BN);
+  if (rc != kOk) return rc;
+  int grid = num_sms;
+  if (args.mtiles == nullptr) {
+    const int n_tiles = (args.N + BN - 1) / BN;
+    const int tiles = ((args.M + kBM - 1) / kBM) * n_tiles;
+    grid = tiles < num_sms ? tiles : num_sms;
+  }
+  switch (epilogue) {
+    case kEpiF32:
+      return launch<128, kEpiF32>(ma, mb, args, grid, stream);
+    case kEpiBF16:
+      return launch<256, kEpiBF16>(ma, mb, args, grid, stream);
+    case kEpiSwiGLU:
+      return launch<256, kEpiSwiGLU>(ma, mb, args, grid, stream);
+    default:
+      return kErrArgs;
+  }
+}
+
+}  // namespace ssb

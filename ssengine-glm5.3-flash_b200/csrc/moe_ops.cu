@@ -1,0 +1,336 @@
+// MoE routing / permutation / combine and the NVFP4 activation quantizer (sm_100a, HBM-bound integer and byte
+// work: coalesced vector loads and stores, grids sized in multiples of the SM count where the work allows).
+//
+// Permutation contract (bit-exact): expert-major, tokens ascending inside an expert, the shared expert (index E)
+// last with every token; expert e's rows start at offsets[e] = sum over e' < e of ceil(n_e' / 128) * 128, so every
+// 128-row GEMM tile belongs to one expert. The rank of token t inside expert e is the number of tokens before t that
+// route to e: per 256-token block a bit mask per expert (built with shared-memory atomicOr, order independent),
+// block bases by an exclusive scan over blocks, and popcounts inside the block -- deterministic, no global atomics.
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace ssb {
+
+namespace {
+
+constexpr int kBlockTokens = 256;
+constexpr int kMaskWords = kBlockTokens / 32;
+
+// ---- NVFP4 activation quantizer: one thread per (row, atom column) = 64 elements, 4 scale bytes ----------------
+__global__ void nvfp4_quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t K, int64_t ldx,
+                                      float gs, uint8_t* __restrict__ codes, int64_t ldc, uint8_t* __restrict__ sf,
+                                      int64_t ncb) {
+  const int64_t total = rows * ncb;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = idx / ncb;
+    const int64_t a = idx - r * ncb;
+    uint32_t word = 0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int64_t k0 = a * 64 + g * 16;
+      if (k0 >= K) break;
+      const uint4* src = reinterpret_cast<const uint4*>(x + r * ldx + k0);
+      const uint4 v0 = src[0], v1 = src[1];
+      const __nv_bfloat16* b0 = reinterpret_cast<const __nv_bfloat16*>(&v0);
+      const __nv_bfloat16* b1 = reinterpret_cast<const __nv_bfloat16*>(&v1);
+      float f[16];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        f[i] = __bfloat162float(b0[i]);
+        f[8 + i] = __bfloat162float(b1[i]);
+      }
+      uint32_t p[2];
+      const uint32_t s = nvfp4_quant16(f, gs, p);
+      *reinterpret_cast<uint2*>(codes + r * ldc + k0 / 2) = make_uint2(p[0], p[1]);
+      word |= s << (8 * g);
+    }
+    *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(r, a * 4, ncb)) = word;
+  }
+}
+
+// ---- routing: softmax top-k, one warp per token -------------------------------------------------------------------
+// Selection: k rounds of a warp arg-max with (value desc, expert index asc); weights softmax over the selected.
+template <int EPL>
+__global__ void moe_route_kernel(const float* __restrict__ logits, int64_t T, int E, int k, int32_t* __restrict__ ids,
+                                 float* __restrict__ weights) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  float v[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = lane + 32 * j;
+    float x = e < E ? logits[t * E + e] : -INFINITY;
+    if (x != x) x = -INFINITY;   // NaN never outranks a number
+    v[j] = e < E ? x : -INFINITY;
+  }
+  uint32_t taken = 0;
+  int my_id = -1;
+  float my_val = 0.0f, top = 0.0f;
+  for (int r = 0; r < k; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7FFFFFFF;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && !((taken >> j) & 1u) && (v[j] > bv || (v[j] == bv && e < bi))) {
+        bv = v[j];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+      const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (lane == r) {
+      my_id = bi;
+      my_val = bv;
+    }
+    if (r == 0) top = bv;
+  }
+  const float p = lane < k ? expf(my_val - top) : 0.0f;
+  // sum in rank order (lane 0 .. k-1), the same order on every call
+  float s = 0.0f;
+  for (int r = 0; r < k; ++r) s += __shfl_sync(0xFFFFFFFFu, p, r);
+  if (lane < k) {
+    ids[t * k + lane] = my_id;
+    weights[t * k + lane] = p / s;
+  }
+}
+
+// ---- per-block expert masks and counts ------------------------------------------------------------------------------
+__global__ void moe_count_kernel(const int32_t* __restrict__ ids, int64_t T, int E, int k, uint32_t* __restrict__ masks,
+                                 int32_t* __restrict__ block_counts) {
+  extern __shared__ uint32_t sm[];   // [E][kMaskWords]
+  const int b = blockIdx.x;
+  for (int i = threadIdx.x; i < E * kMaskWords; i += blockDim.x) sm[i] = 0u;
+  __syncthreads();
+  const int64_t t = (int64_t)b * kBlockTokens + threadIdx.x;
+  if (t < T) {
+    for (int j = 0; j < k; ++j) {
+      const int e = ids[t * k + j];
+      if (e >= 0 && e < E) atomicOr(&sm[e * kMaskWords + (threadIdx.x >> 5)], 1u << (threadIdx.x & 31));
+    }
+  }
+  __syncthreads();
+  uint32_t* gm = masks + (int64_t)b * E * kMaskWords;
+  for (int i = threadIdx.x; i < E * kMaskWords; i += blockDim.x) gm[i] = sm[i];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int c = 0;
+#pragma unroll
+    for (int w = 0; w < kMaskWords; ++w) c += __popc(sm[e * kMaskWords + w]);
+    block_counts[(int64_t)b * E + e] = c;
+  }
+}
+
+// ---- expert offsets, block bases, GEMM tile table (one block) ------------------------------------------------------
+__global__ void moe_offsets_kernel(int64_t T, int E, int nblocks, int32_t* __restrict__ block_counts,
+                                   int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
+                                   int32_t* __restrict__ mtiles, int32_t* __restrict__ num_mtiles, int cap,
+                                   int32_t* status) {
+  extern __shared__ int32_t sh[];     // [E + 1] padded sizes
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) {
+    int run = 0;
+    if (e < E) {
+      for (int b = 0; b < nblocks; ++b) {
+        const int c = block_counts[(int64_t)b * E + e];
+        block_counts[(int64_t)b * E + e] = run;   // exclusive base of block b inside expert e
+        run += c;
+      }
+    } else {
+      run = static_cast<int>(T);                  // the shared expert takes every token
+    }
+    counts[e] = run;
+    sh[e] = (run + 127) / 128 * 128;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e <= E; ++e) {
+      const int p = sh[e];
+      sh[e] = acc;
+      offsets[e] = acc;
+      acc += p;
+    }
+    offsets[E + 1] = acc;
+    const int n = acc / 128;
+    *num_mtiles = n;
+    if (n > cap) raise_status(status, kErrCapacity);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) {
+    const int c = counts[e];
+    const int base = sh[e];
+    for (int i = 0; i * 128 < c; ++i) {
+      const int tile = base / 128 + i;
+      if (tile < cap) {
+        int4 v = make_int4(e, base + 128 * i, min(128, c - 128 * i), 0);
+        reinterpret_cast<int4*>(mtiles)[tile] = v;
+      }
+    }
+  }
+}
+
+// ---- permuted rows + gather of the token's NVFP4 codes and scales into its k + 1 rows -------------------------------
+__global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int64_t T, int E, int k,
+                                   const uint32_t* __restrict__ masks, const int32_t* __restrict__ block_base,
+                                   const int32_t* __restrict__ offsets, int32_t* __restrict__ rows,
+                                   const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsf, int64_t H,
+                                   uint8_t* __restrict__ xq_perm, uint8_t* __restrict__ xsf_perm) {
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  const int b = blockIdx.x;
+  const int64_t ncb = sf_atom_cols(H);
+  const int64_t row_bytes = H / 2;
+  for (int i = threadIdx.x >> 5; i < kBlockTokens; i += warps) {
+    const int64_t t = (int64_t)b * kBlockTokens + i;
+    if (t >= T) break;
+    int my_row = -1;
+    if (lane < k) {
+      const int e = ids[t * k + lane];
+      const uint32_t* m = masks + ((int64_t)b * E + e) * kMaskWords;
+      const int w = i >> 5;
+      int rank = block_base[(int64_t)b * E + e];
+      for (int q = 0; q < w; ++q) rank += __popc(m[q]);
+      rank += __popc(m[w] & ((1u << (i & 31)) - 1u));
+      my_row = offsets[e] + rank;
+      rows[t * k + lane] = my_row;
+    }
+    if (lane == k) my_row = offsets[E] + static_cast<int>(t);   // shared expert
+    // gather: codes (16-byte vectors) and scale words of row t into the k + 1 destination rows
+    const uint4* src = reinterpret_cast<const uint4*>(xq + t * row_bytes);
+    const int nvec = static_cast<int>(row_bytes / 16);
+    for (int d = 0; d <= k; ++d) {
+      const int64_t dst_row = __shfl_sync(0xFFFFFFFFu, my_row, d);
+      uint4* dst = reinterpret_cast<uint4*>(xq_perm + dst_row * row_bytes);
+      for (int v = lane; v < nvec; v += 32) dst[v] = src[v];
+      for (int a = lane; a < ncb; a += 32) {
+        const uint32_t wv = *reinterpret_cast<const uint32_t*>(xsf + sf_atom_offset(t, a * 4, ncb));
+        *reinterpret_cast<uint32_t*>(xsf_perm + sf_atom_offset(dst_row, a * 4, ncb)) = wv;
+      }
+    }
+  }
+}
+
+// ---- weighted combine: out[t] = sum_j w[t, j] y[rows[t, j]] + y[shared row of t], fp32 accumulate, bf16 out -------
+__global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int64_t H, const int32_t* __restrict__ rows,
+                                   const float* __restrict__ weights, const int32_t* __restrict__ offsets, int64_t T,
+                                   int E, int k, __nv_bfloat16* __restrict__ out) {
+  const int64_t t = blockIdx.x;
+  if (t >= T) return;
+  const int64_t srow = offsets[E] + t;
+  const int nvec = static_cast<int>(H / 8);
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    for (int j = 0; j < k; ++j) {
+      const int64_t r = rows[t * k + j];
+      const float w = weights[t * k + j];
+      const uint4 q = reinterpret_cast<const uint4*>(y + r * H)[v];
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&q);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(w, __bfloat162float(b[i]), acc[i]);
+    }
+    const uint4 q = reinterpret_cast<const uint4*>(y + srow * H)[v];
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&q);
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 p = __floats2bfloat162_rn(acc[2 * i] + __bfloat162float(b[2 * i]),
+                                               acc[2 * i + 1] + __bfloat162float(b[2 * i + 1]));
+      o[i] = *reinterpret_cast<uint32_t*>(&p);
+    }
+    reinterpret_cast<uint4*>(out + t * H)[v] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+int grid_for(int64_t work, int threads) {
+  const int64_t sms = device_sm_count();
+  int64_t blocks = (work + threads - 1) / threads;
+  const int64_t cap = sms * 16;
+  if (blocks > cap) blocks = cap;
+  return static_cast<int>(blocks < 1 ? 1 : blocks);
+}
+
+int last_error() { return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda; }
+
+}  // namespace
+
+int launch_nvfp4_quantize(const void* x, int64_t rows, int64_t K, int64_t ldx, float gs, uint8_t* codes, int64_t ldc,
+                          uint8_t* sf, cudaStream_t stream) {
+  if (K <= 0 || K % 16 != 0 || ldx % 8 != 0 || ldc % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(codes) & 7) || (reinterpret_cast<uintptr_t>(sf) & 3))
+    return kErrArgs;
+  if (rows == 0) return kOk;
+  const int64_t ncb = sf_atom_cols(K);
+  const int threads = 256;
+  nvfp4_quantize_kernel<<<grid_for(rows * ncb, threads), threads, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), rows, K, ldx, gs, codes, ldc, sf, ncb);
+  return last_error();
+}
+
+int launch_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* ids, float* weights,
+                     cudaStream_t stream) {
+  if (E <= 0 || E > 512 || k <= 0 || k > 32 || k > E) return kErrArgs;
+  if (T == 0) return kOk;
+  const int threads = 256;
+  const int64_t blocks = (T + 7) / 8;
+  const int epl = (E + 31) / 32;
+  if (epl <= 4)
+    moe_route_kernel<4><<<blocks, threads, 0, stream>>>(logits, T, E, k, ids, weights);
+  else if (epl <= 8)
+    moe_route_kernel<8><<<blocks, threads, 0, stream>>>(logits, T, E, k, ids, weights);
+  else
+    moe_route_kernel<16><<<blocks, threads, 0, stream>>>(logits, T, E, k, ids, weights);
+  return last_error();
+}
+
+int launch_moe_count(const int32_t* ids, int64_t T, int32_t E, int32_t k, uint32_t* masks, int32_t* block_counts,
+                     cudaStream_t stream) {
+  if (T == 0) return kOk;
+  const int nblocks = static_cast<int>((T + kBlockTokens - 1) / kBlockTokens);
+  const size_t sm = static_cast<size_t>(E) * kMaskWords * 4;
+  moe_count_kernel<<<nblocks, kBlockTokens, sm, stream>>>(ids, T, E, k, masks, block_counts);
+  return last_error();
+}
+
+int launch_moe_offsets(int64_t T, int32_t E, int32_t* block_counts, int32_t* counts, int32_t* offsets,
+                       int32_t* mtiles, int32_t* num_mtiles, int32_t mtile_cap, int32_t* status, cudaStream_t stream) {
+  const int nblocks = static_cast<int>((T + kBlockTokens - 1) / kBlockTokens);
+  moe_offsets_kernel<<<1, 512, (E + 1) * 4, stream>>>(T, E, nblocks, block_counts, counts, offsets, mtiles,
+                                                      num_mtiles, mtile_cap, status);
+  return last_error();
+}
+
+int launch_moe_scatter(const int32_t* ids, int64_t T, int32_t E, int32_t k, const uint32_t* masks,
+                       const int32_t* block_base, const int32_t* offsets, int32_t* rows, const uint8_t* xq,
+                       const uint8_t* xsf, int64_t H, uint8_t* xq_perm, uint8_t* xsf_perm, cudaStream_t stream) {
+  if (k >= 32 || H % 32 != 0) return kErrArgs;
+  if (T == 0) return kOk;
+  const int nblocks = static_cast<int>((T + kBlockTokens - 1) / kBlockTokens);
+  moe_scatter_kernel<<<nblocks, 512, 0, stream>>>(ids, T, E, k, masks, block_base, offsets, rows, xq, xsf, H, xq_perm,
+                                                  xsf_perm);
+  return last_error();
+}
+
+int launch_moe_combine(const void* y, int64_t H, const int32_t* rows, const float* weights, const int32_t* offsets,
+                       int64_t T, int32_t E, int32_t k, void* out, cudaStream_t stream) {
+  if (H % 8 != 0) return kErrArgs;
+  if (T == 0) return kOk;
+  const int threads = H / 8 >= 512 ? 512 : static_cast<int>((H / 8 + 31) / 32 * 32);
+  moe_combine_kernel<<<static_cast<unsigned>(T), threads, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(y), H, rows, weights, offsets, T, E, k,
+      reinterpret_cast<__nv_bfloat16*>(out));
+  return last_error();
+}
+
+}  // namespace ssb

@@ -1,0 +1,64 @@
+// Internal host-side launchers of the sm_100a kernels (not part of the C ABI; see include/ssengine_b200.h).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ssb {
+
+// Output stage of the NVFP4 GEMM.
+enum Epilogue : int {
+  kEpiF32 = 0,     // fp32 [rows, ldo] = alpha * acc, columns < N stored (router logits)
+  kEpiBF16 = 1,    // bf16 [rows, ldo] = alpha[g] * acc (expert down projection)
+  kEpiSwiGLU = 2,  // a 256-wide tile holds 128 gate + 128 up columns; h = silu(alpha g) * (alpha u) quantized to
+                   // NVFP4 (codes [rows, ldo bytes] + 128x4-atom scales) with global scale out_gs
+};
+
+struct GemmArgs {
+  const uint8_t* sfa = nullptr;        // A scales, 128x4 atoms, sf_atom_cols(K) atom columns per row block
+  const uint8_t* sfb = nullptr;        // B scales (all groups, group g's rows start at g * N)
+  const int32_t* mtiles = nullptr;     // grouped: [cap][4] = {group, first A row, valid rows, 0}; nullptr = dense
+  const int32_t* num_mtiles = nullptr; // grouped: device count of valid entries
+  int32_t mtile_cap = 0;
+  int32_t M = 0;                       // dense: rows of A
+  int32_t K = 0;                       // reduction length (elements)
+  int32_t N = 0;                       // B rows per group
+  int32_t ncb_k = 0;                   // sf_atom_cols(K)
+  const float* alpha = nullptr;        // per-group output scale (device), or nullptr -> alpha_scalar
+  float alpha_scalar = 1.0f;
+  void* out = nullptr;
+  int64_t ldo = 0;                     // elements (F32 / BF16) or bytes (SwiGLU codes)
+  uint8_t* out_sf = nullptr;           // SwiGLU: output scales
+  int32_t out_ncb = 0;                 // SwiGLU: sf_atom_cols(N / 2)
+  float out_gs = 1.0f;                 // SwiGLU: output global scale
+  int32_t* status = nullptr;           // device status word
+};
+
+// Builds the TMA maps for A ([a_rows, K/2] bytes, row pitch lda bytes) and B ([b_rows, K/2], pitch ldb) and launches
+// the persistent GEMM on `stream`. Returns a Status.
+int launch_gemm_nvfp4(int epilogue, const uint8_t* a, int64_t a_rows, int64_t lda, const uint8_t* b, int64_t b_rows,
+                      int64_t ldb, const GemmArgs& args, int num_sms, cudaStream_t stream);
+
+int launch_nvfp4_quantize(const void* x, int64_t rows, int64_t K, int64_t ldx, float gs, uint8_t* codes, int64_t ldc,
+                          uint8_t* sf, cudaStream_t stream);
+
+int launch_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* ids, float* weights,
+                     cudaStream_t stream);
+
+int launch_moe_count(const int32_t* ids, int64_t T, int32_t E, int32_t k, uint32_t* masks, int32_t* block_counts,
+                     cudaStream_t stream);
+
+int launch_moe_offsets(int64_t T, int32_t E, int32_t* block_counts, int32_t* counts, int32_t* offsets,
+                       int32_t* mtiles, int32_t* num_mtiles, int32_t mtile_cap, int32_t* status, cudaStream_t stream);
+
+int launch_moe_scatter(const int32_t* ids, int64_t T, int32_t E, int32_t k, const uint32_t* masks,
+                       const int32_t* block_base, const int32_t* offsets, int32_t* rows, const uint8_t* xq,
+                       const uint8_t* xsf, int64_t H, uint8_t* xq_perm, uint8_t* xsf_perm, cudaStream_t stream);
+
+int launch_moe_combine(const void* y, int64_t H, const int32_t* rows, const float* weights, const int32_t* offsets,
+                       int64_t T, int32_t E, int32_t k, void* out, cudaStream_t stream);
+
+int device_sm_count();
+
+}  // namespace ssb

@@ -1,0 +1,94 @@
+"""ctypes bindings of libssengine_b200.so (the C ABI of include/ssengine_b200.h).
+
+The library is the only compute path: there is no CPU or PyTorch fallback. `load()` raises if the shared object is
+missing or was built without an entry point the header declares, and every call raises `SsbError` on a non-zero
+return code.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libssengine_b200.so"
+
+# every symbol include/ssengine_b200.h declares
+EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_gemm", "ssb_moe_route",
+           "ssb_moe_workspace_bytes", "ssb_moe_workspace_offsets", "ssb_moe_forward", "ssb_moe_forward_profiled")
+
+EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
+
+WS = dict(XQ=0, XSF=1, LOGITS=2, IDS=3, WEIGHTS=4, ROWS=5, COUNTS=6, OFFSETS=7, MASKS=8, BLOCKS=9, MTILES=10,
+          NUM_MTILES=11, XQ_PERM=12, XSF_PERM=13, ACT=14, ACT_SF=15, Y=16, END=17)
+
+STATUS = {0: "ok", 1: "bad arguments", 2: "CUDA launch error", 3: "workspace too small",
+          4: "a bounded device wait expired", 5: "cuTensorMapEncodeTiled unavailable", 6: "device table overflow"}
+
+
+class SsbError(RuntimeError):
+    def __init__(self, fn: str, code: int):
+        super().__init__(f"{fn} failed: {code} ({STATUS.get(code, 'unknown')})")
+        self.code = code
+
+
+class MoeLayerC(ctypes.Structure):
+    """Mirror of `ssb_moe_layer`."""
+    _fields_ = [("hidden", ctypes.c_int32), ("inter", ctypes.c_int32), ("num_experts", ctypes.c_int32),
+                ("top_k", ctypes.c_int32), ("gs_x", ctypes.c_float), ("gs_h", ctypes.c_float),
+                ("router_codes", ctypes.c_void_p), ("router_sf", ctypes.c_void_p), ("router_rows", ctypes.c_int64),
+                ("router_alpha", ctypes.c_float), ("w1_codes", ctypes.c_void_p), ("w1_sf", ctypes.c_void_p),
+                ("w1_alpha", ctypes.c_void_p), ("w2_codes", ctypes.c_void_p), ("w2_sf", ctypes.c_void_p),
+                ("w2_alpha", ctypes.c_void_p)]
+
+
+_LIB = None
+
+_P, _I32, _I64, _F = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
+_SIGS = {
+    "ssb_version": ([], ctypes.c_char_p),
+    "ssb_sf_atom_cols": ([_I64], _I64),
+    "ssb_nvfp4_quantize": ([_P, _I64, _I64, _I64, _F, _P, _I64, _P, _P], ctypes.c_int),
+    "ssb_nvfp4_gemm": ([_I32, _P, _P, _I64, _I64, _P, _P, _I64, _F, _P, _I64, _P, _F, _P, _P], ctypes.c_int),
+    "ssb_moe_route": ([_P, _I64, _I32, _I32, _P, _P, _P], ctypes.c_int),
+    "ssb_moe_workspace_bytes": ([ctypes.POINTER(MoeLayerC), _I64], _I64),
+    "ssb_moe_workspace_offsets": ([ctypes.POINTER(MoeLayerC), _I64, ctypes.POINTER(ctypes.c_int64), _I32],
+                                  ctypes.c_int),
+    "ssb_moe_forward": ([ctypes.POINTER(MoeLayerC), _P, _I64, _P, _P, _I64, _P, _P], ctypes.c_int),
+    "ssb_moe_forward_profiled": ([ctypes.POINTER(MoeLayerC), _P, _I64, _P, _P, _I64, _P, _P,
+                                  ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+}
+
+MOE_STEPS = ("quantize", "router_gemm", "route", "count", "offsets", "scatter", "gate_up_gemm", "down_gemm",
+             "combine")
+
+
+def load(path: Path | None = None):
+    """Load the library (once). Raises FileNotFoundError / AttributeError when it is missing or incomplete."""
+    global _LIB
+    if _LIB is not None and path is None:
+        return _LIB
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise FileNotFoundError(f"{p} is not built: run `python -c 'import __graft_entry__ as g; g.build()'`")
+    lib = ctypes.CDLL(str(p))
+    for name in EXPORTS:
+        fn = getattr(lib, name)        # AttributeError when the symbol is missing
+        args, res = _SIGS[name]
+        fn.argtypes = args
+        fn.restype = res
+    if path is None:
+        _LIB = lib
+    return lib
+
+
+def check(name: str, rc: int) -> None:
+    if rc != 0:
+        raise SsbError(name, rc)
+
+
+def stream_ptr(stream=None) -> int:
+    import torch
+
+    s = torch.cuda.current_stream() if stream is None else stream
+    return int(s.cuda_stream)

@@ -1,0 +1,143 @@
+"""GPU parity of the single kernels through the C ABI against the CPU oracle: the NVFP4 quantizer (bit-exact), the
+tcgen05 NVFP4 GEMM in its three epilogues, and the MoE routing (indices bit-exact on identical logits)."""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe as omoe
+from oracle import nvfp4
+
+pytestmark = pytest.mark.gpu
+
+
+def _lib():
+    from ssengine_b200 import lib
+
+    return lib, lib.load()
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _rand_operand(rng, rows, K):
+    from ssengine_b200 import weights
+
+    codes = rng.integers(0, 16, size=(rows, K), dtype=np.uint8)
+    sf = np.asarray(weights.SCALE_CODES, dtype=np.uint8)[rng.integers(0, len(weights.SCALE_CODES), size=(rows, K // 16))]
+    return codes, sf
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("rows,K", [(300, 320), (128, 4096), (1, 64)])
+def test_quantize_bit_exact(cuda, rows, K):
+    lib, so = _lib()
+    rng = np.random.default_rng(rows + K)
+    x = (rng.standard_normal((rows, K)) * 2).astype(np.float32)
+    x[0, :16] = 0.0
+    x[0, 16:32] = [0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, -0.25, -0.75, -5.0, 6.0, 7.0, 1e-3, -1e-3, 40.0, -40.0]
+    if rows > 1:
+        x[1, :16] = 1e4
+    xb = torch.from_numpy(x).to(torch.bfloat16)
+    gs = 448.0 * 6 / 8
+    ncb = so.ssb_sf_atom_cols(K)
+    codes = torch.zeros(rows, K // 2, dtype=torch.uint8, device=cuda)
+    sf = torch.zeros(-(-rows // 128) * ncb * 512, dtype=torch.uint8, device=cuda)
+    rc = so.ssb_nvfp4_quantize(xb.cuda().data_ptr(), rows, K, K, gs, codes.data_ptr(), K // 2, sf.data_ptr(),
+                               _stream())
+    lib.check("ssb_nvfp4_quantize", rc)
+    torch.cuda.synchronize()
+    oc, osf = nvfp4.quantize(xb.float().numpy(), gs)
+    np.testing.assert_array_equal(codes.cpu().numpy(), nvfp4.pack(oc))
+    np.testing.assert_array_equal(sf.cpu().numpy(), nvfp4.sf_to_atoms(osf))
+
+
+def _gemm(epi, a, asf, M, K, b, bsf, N, alpha, out, ldo, out_sf=None, out_gs=1.0):
+    lib, so = _lib()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = so.ssb_nvfp4_gemm(epi, a.data_ptr(), asf.data_ptr(), M, K, b.data_ptr(), bsf.data_ptr(), N, alpha,
+                           out.data_ptr(), ldo, 0 if out_sf is None else out_sf.data_ptr(), out_gs,
+                           status.data_ptr(), _stream())
+    lib.check("ssb_nvfp4_gemm", rc)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+
+
+@pytest.mark.parametrize("M,K,N", [(300, 512, 128), (129, 4096, 8), (1000, 1024, 256)])
+def test_gemm_f32_epilogue(cuda, M, K, N):
+    rng = np.random.default_rng(M * 7 + N)
+    ac, asf = _rand_operand(rng, M, K)
+    bc, bsf = _rand_operand(rng, N, K)
+    nb = -(-N // 128) * 128
+    bcp = np.zeros((nb, K), dtype=np.uint8)
+    bcp[:N] = bc
+    bsfp = np.zeros((nb, K // 16), dtype=np.uint8)
+    bsfp[:N] = bsf
+    out = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+    _gemm(0, _dev(nvfp4.pack(ac)), _dev(nvfp4.sf_to_atoms(asf)), M, K, _dev(nvfp4.pack(bcp)),
+          _dev(nvfp4.sf_to_atoms(bsfp)), N, 0.5, out, N)
+    ref = 0.5 * (nvfp4.dequantize(ac, asf, 1.0).astype(np.float64) @ nvfp4.dequantize(bc, bsf, 1.0).T)
+    got = out.cpu().numpy()
+    scale = np.abs(ref).max()
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-5 * scale)
+
+
+def test_gemm_bf16_epilogue(cuda):
+    M, K, N = 300, 4096, 512
+    rng = np.random.default_rng(11)
+    ac, asf = _rand_operand(rng, M, K)
+    bc, bsf = _rand_operand(rng, N, K)
+    out = torch.zeros((M, N), dtype=torch.bfloat16, device=cuda)
+    _gemm(1, _dev(nvfp4.pack(ac)), _dev(nvfp4.sf_to_atoms(asf)), M, K, _dev(nvfp4.pack(bc)),
+          _dev(nvfp4.sf_to_atoms(bsf)), N, 1e-2, out, N)
+    ref = 1e-2 * (nvfp4.dequantize(ac, asf, 1.0).astype(np.float64) @ nvfp4.dequantize(bc, bsf, 1.0).T)
+    got = out.float().cpu().numpy()
+    np.testing.assert_allclose(got, ref, rtol=8e-3, atol=1e-3 * np.abs(ref).max())
+
+
+def test_gemm_swiglu_requant_epilogue(cuda):
+    from ssengine_b200 import layout
+
+    M, K, F = 300, 512, 256
+    rng = np.random.default_rng(12)
+    ac, asf = _rand_operand(rng, M, K)
+    bc, bsf = _rand_operand(rng, 2 * F, K)          # logical: gate rows [0, F), up rows [F, 2F)
+    bci = layout.gate_up_interleave(torch.from_numpy(bc)).numpy()
+    bsfi = layout.gate_up_interleave(torch.from_numpy(bsf)).numpy()
+    alpha, gs_h = 1.0 / 60.0, 448.0 * 6 / 32
+    codes = torch.zeros((M, F // 2), dtype=torch.uint8, device=cuda)
+    osf = torch.zeros(-(-M // 128) * nvfp4.atom_cols(F) * 512, dtype=torch.uint8, device=cuda)
+    _gemm(2, _dev(nvfp4.pack(ac)), _dev(nvfp4.sf_to_atoms(asf)), M, K, _dev(nvfp4.pack(bci)),
+          _dev(nvfp4.sf_to_atoms(bsfi)), 2 * F, alpha, codes, F // 2, osf, gs_h)
+    gu = alpha * (nvfp4.dequantize(ac, asf, 1.0) @ nvfp4.dequantize(bc, bsf, 1.0).T)
+    h = omoe.silu(gu[:, :F].astype(np.float32)) * gu[:, F:].astype(np.float32)
+    rc_, rs_ = nvfp4.quantize(h, gs_h)
+    got_c = nvfp4.unpack(codes.cpu().numpy())
+    got_s = nvfp4.atoms_to_sf(osf.cpu().numpy(), M, F // 16)
+    # codes and scales agree except where h sits on a rounding boundary (fp32 summation order)
+    assert (got_c == rc_).mean() > 0.99 and (got_s == rs_).mean() > 0.99
+    d_gpu = nvfp4.dequantize(got_c, got_s, gs_h)
+    d_ref = nvfp4.dequantize(rc_, rs_, gs_h)
+    assert np.linalg.norm(d_gpu - d_ref) / np.linalg.norm(d_ref) < 1e-2
+
+
+@pytest.mark.parametrize("T,E,k", [(1000, 128, 8), (257, 8, 2), (64, 288, 8), (33, 512, 31)])
+def test_route_indices_bit_exact(cuda, T, E, k):
+    lib, so = _lib()
+    rng = np.random.default_rng(T + E)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    logits[: T // 2] = np.round(logits[: T // 2] * 2) / 2        # many exact ties
+    lg = _dev(logits)
+    ids = torch.zeros((T, k), dtype=torch.int32, device=cuda)
+    w = torch.zeros((T, k), dtype=torch.float32, device=cuda)
+    lib.check("ssb_moe_route", so.ssb_moe_route(lg.data_ptr(), T, E, k, ids.data_ptr(), w.data_ptr(), _stream()))
+    torch.cuda.synchronize()
+    rid, rw = omoe.route_softmax_topk(logits, k)
+    np.testing.assert_array_equal(ids.cpu().numpy(), rid)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
