@@ -6,7 +6,7 @@
  *   the caller; the library never allocates device memory;
  * - `stream` is a cudaStream_t passed as void*; every entry point only enqueues work on it (no host sync);
  * - return 0 on success, else an ssb status code (1 bad arguments, 2 CUDA launch error, 3 workspace too small,
- *   5 driver entry point missing); device-side failures (4 a bounded wait expired, 6 a table overflowed) are written
+ *   5 driver entry point missing, 7 size beyond ssb_moe_route_permute_noalloc's limits); device-side failures (4 a bounded wait expired, 6 a table overflowed) are written
  *   to the caller's int32 device `status` word (first error wins), read by the caller after the stream's work ends;
  * - NVFP4 operands: e2m1 codes packed two per byte (even element in the low nibble), rows K/2 bytes apart; scales
  *   are e4m3 bytes in the 128x4-atom layout: rows padded to 128, K padded to 256, atom (row block rb, atom column
@@ -116,6 +116,19 @@ int ssb_moe_forward(const ssb_moe_layer* layer, const void* x, int64_t T, void* 
 #define SSB_MOE_STEPS 9
 int ssb_moe_forward_profiled(const ssb_moe_layer* layer, const void* x, int64_t T, void* out, void* ws,
                              int64_t ws_bytes, int32_t* status, void* stream, void* const* events);
+
+/* MoE routing + permutation that allocates nothing: the same routing as ssb_moe_route and the same permutation as
+ * ssb_moe_forward (expert-major, tokens ascending, shared expert last, experts at 128-aligned offsets), for callers
+ * that cannot allocate device memory -- a stage whose KV pool already took the free HBM at start-up, code that must
+ * not stall the GPU with a cudaMalloc mid-microbatch, a host holding only buffers mapped from another process.
+ * Inputs: logits fp32 [T, E]. Outputs: ids int32 [T, k], weights fp32 [T, k], rows int32 [T, k] (permuted row of each
+ * (token, slot)), counts int32 [E+1], offsets int32 [E+2]. Its scratch is one static device array of about 1.25 MiB
+ * that every GPU loading the library holds until exit; limits T <= 16384, E <= 512, k <= 31, beyond which it returns
+ * 7 before any launch. Calls share that array: calls whose work overlaps on the GPU race. The first call on a device
+ * looks up the array's address and should come before any stream capture.
+ * No counterpart in the reference. */
+int ssb_moe_route_permute_noalloc(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* ids, float* weights,
+                                  int32_t* rows, int32_t* counts, int32_t* offsets, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

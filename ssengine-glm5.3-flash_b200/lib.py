@@ -15,7 +15,8 @@ LIB_PATH = PKG / "libssengine_b200.so"
 
 # every symbol include/ssengine_b200.h declares
 EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_gemm", "ssb_moe_route",
-           "ssb_moe_workspace_bytes", "ssb_moe_workspace_offsets", "ssb_moe_forward", "ssb_moe_forward_profiled")
+           "ssb_moe_workspace_bytes", "ssb_moe_workspace_offsets", "ssb_moe_forward", "ssb_moe_forward_profiled",
+           "ssb_moe_route_permute_noalloc")
 
 EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
 
@@ -23,7 +24,8 @@ WS = dict(XQ=0, XSF=1, LOGITS=2, IDS=3, WEIGHTS=4, ROWS=5, COUNTS=6, OFFSETS=7, 
           NUM_MTILES=11, XQ_PERM=12, XSF_PERM=13, ACT=14, ACT_SF=15, Y=16, END=17)
 
 STATUS = {0: "ok", 1: "bad arguments", 2: "CUDA launch error", 3: "workspace too small",
-          4: "a bounded device wait expired", 5: "cuTensorMapEncodeTiled unavailable", 6: "device table overflow"}
+          4: "a bounded device wait expired", 5: "cuTensorMapEncodeTiled unavailable", 6: "device table overflow",
+          7: "size beyond the no-alloc entry point's static scratch"}
 
 
 class SsbError(RuntimeError):
@@ -57,6 +59,7 @@ _SIGS = {
     "ssb_moe_forward": ([ctypes.POINTER(MoeLayerC), _P, _I64, _P, _P, _I64, _P, _P], ctypes.c_int),
     "ssb_moe_forward_profiled": ([ctypes.POINTER(MoeLayerC), _P, _I64, _P, _P, _I64, _P, _P,
                                   ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "ssb_moe_route_permute_noalloc": ([_P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int),
 }
 
 MOE_STEPS = ("quantize", "router_gemm", "route", "count", "offsets", "scatter", "gate_up_gemm", "down_gemm",
