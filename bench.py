@@ -41,6 +41,7 @@ def parse():
     ap.add_argument("--cpu-tokens", type=int, default=1024, help="CPU baseline sample (tokens)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true", help="skip the nvidia-smi window (profiling runs)")
     return ap.parse_args()
 
 
@@ -268,11 +269,12 @@ def main() -> None:
     gpu_id = str(getattr(props, "uuid", local))
     gpu_id = gpu_id if gpu_id.startswith("GPU-") or not gpu_id.count("-") else "GPU-" + gpu_id
     clocks = Clocks(gpu_id)
-    clocks.start()
-    t_end = time.time() + 1.0
-    while time.time() < t_end:
-        layer.forward(x, out)
-        torch.cuda.synchronize()
+    if not args.no_clocks:
+        clocks.start()
+        t_end = time.time() + 1.0
+        while time.time() < t_end:
+            layer.forward(x, out)
+            torch.cuda.synchronize()
 
     nst = len(lib.MOE_STEPS)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nst + 1)] for _ in range(steps)]
