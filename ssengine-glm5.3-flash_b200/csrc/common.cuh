@@ -10,6 +10,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp4.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -185,6 +186,19 @@ SSB_DEVICE float e4m3_value(uint32_t code) {
   return __half2float(__half(h));
 }
 
+// Eight e2m1 codes (a 32-bit word, element i in nibble i) of a[0..7], round to nearest even, saturating at 6, by the
+// hardware conversion (cvt.rn.satfinite.e2m1x2.f32); then a code of magnitude 0 loses its sign, as in e2m1_encode.
+SSB_DEVICE uint32_t e2m1x8(const float* a) {
+  uint32_t w = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w |= static_cast<uint32_t>(__nv_cvt_float2_to_fp4x2(make_float2(a[2 * i], a[2 * i + 1]), __NV_E2M1,
+                                                        cudaRoundNearest)) << (8 * i);
+  const uint32_t m = w & 0x77777777u;
+  const uint32_t nz = (m | (m >> 1) | (m >> 2)) & 0x11111111u;
+  return m | (w & (nz << 3));
+}
+
 // Quantize 16 values with global scale gs: returns the scale byte, writes 8 bytes of packed codes (element 2i in the
 // low nibble of byte i).
 SSB_DEVICE uint32_t nvfp4_quant16(const float (&x)[16], float gs, uint32_t (&packed)[2]) {
@@ -195,12 +209,11 @@ SSB_DEVICE uint32_t nvfp4_quant16(const float (&x)[16], float gs, uint32_t (&pac
   const uint32_t sf = e4m3_encode(sf_f);
   const float sfv = e4m3_value(sf);
   const float r = sfv > 0.0f ? __fdiv_rn(gs, sfv) : 0.0f;
-  packed[0] = packed[1] = 0u;
+  float y[16];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint32_t c = sfv > 0.0f ? e2m1_encode(__fmul_rn(x[i], r)) : 0u;
-    packed[i >> 3] |= c << (4 * (i & 7));
-  }
+  for (int i = 0; i < 16; ++i) y[i] = __fmul_rn(x[i], r);
+  packed[0] = e2m1x8(y);
+  packed[1] = e2m1x8(y + 8);
   return sf;
 }
 

@@ -3,13 +3,15 @@
 //
 //   D[m, n] = alpha[g] * sum_k (a[m, k] * sfa[m, k/16]) * (b[g*N + n, k] * sfb[g*N + n, k/16])
 //
-// Roles (192 threads, one CTA per SM, persistent over output tiles):
+// Roles (320 threads, one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: A tile 128 x 256 (e2m1, 128-byte swizzle), B tile BN x 256, and their scale atoms by
 //               plain bulk copies; STAGES-deep ring of shared-memory stages guarded by full/empty mbarriers.
 //   warp 1      TMEM owner and MMA issuer (one thread): per k-block copies the scale atoms into TMEM
 //               (tcgen05.cp 32x128b.warpx4) and issues 4 MMAs of K = 64; tcgen05.commit frees the stage and, after the
 //               tile's last k-block, signals the accumulator full.
-//   warps 2-5   epilogue: each warp reads its TMEM lane quadrant (32 rows) with tcgen05.ld and runs the output stage.
+//   warps 2-9   epilogue: two warps per TMEM lane quadrant (32 rows), each owning half of the tile's columns; a warp
+//               copies its accumulator share to registers (tcgen05.ld), releases the accumulator at once so the MMAs
+//               of the next tile start, then runs the output stage from registers, overlapping the next mainloop.
 // Tiles are M-major over N tiles (consecutive CTAs share the A row block and walk one expert's weights), so an
 // expert's weights stay in L2 while its row blocks are in flight.
 // Every wait is bounded (common.cuh); on expiry all roles leave, in-flight copies and MMAs are drained with bounded
@@ -24,7 +26,7 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBKBytes = 128;   // one k-block: 256 e2m1 elements = 128 bytes = one 128-byte swizzle row
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 
 template <int BN>
 struct Cfg {
@@ -110,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_empty + 8 * s, 1);
     }
     mbar_init(bar_acc_full, 1);
-    mbar_init(bar_acc_empty, 4);
+    mbar_init(bar_acc_empty, 8);
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -236,8 +238,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2..9) ----------------
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;                      // which half of the tile's columns this warp owns
     const int rl = quad * 32 + lane;                       // row inside the tile = TMEM lane
     const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     uint32_t iter = 0;
@@ -250,76 +253,87 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = rl < ti.rows;
       const int64_t row = (int64_t)ti.row0 + rl;
       if constexpr (EPI == kEpiSwiGLU) {
+        // columns [64 half, +64) of the gate block and the same of the up block (tile columns 128 + ...)
+        float g[64], u[64];
+        tmem_ld_32x32b_x32(tq + 64 * half, *reinterpret_cast<float(*)[32]>(g));
+        tmem_ld_32x32b_x32(tq + 64 * half + 32, *reinterpret_cast<float(*)[32]>(g + 32));
+        tmem_ld_32x32b_x32(tq + 128 + 64 * half, *reinterpret_cast<float(*)[32]>(u));
+        tmem_ld_32x32b_x32(tq + 128 + 64 * half + 32, *reinterpret_cast<float(*)[32]>(u + 32));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_acc_empty);
         uint8_t* codes = reinterpret_cast<uint8_t*>(args.out);
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float g[32], u[32];
-          tmem_ld_32x32b_x32(tq + 32 * c, g);
-          tmem_ld_32x32b_x32(tq + 128 + 32 * c, u);
-          tmem_ld_wait();
-          float h[2][16];
+        uint32_t pk[8], sfw = 0;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float gv = g[i] * alpha;
-            const float uv = u[i] * alpha;
-            h[i >> 4][i & 15] = gv / (1.0f + expf(-gv)) * uv;
+        for (int q = 0; q < 4; ++q) {
+          float h[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float gv = g[16 * q + i] * alpha;
+            const float uv = u[16 * q + i] * alpha;
+            h[i] = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
           }
-          uint32_t p0[2], p1[2];
-          const uint32_t s0 = nvfp4_quant16(h[0], args.out_gs, p0);
-          const uint32_t s1 = nvfp4_quant16(h[1], args.out_gs, p1);
-          if (valid) {
-            const int col = ti.nt * 128 + 32 * c;   // first h column of this chunk
-            uint4 v = make_uint4(p0[0], p0[1], p1[0], p1[1]);
-            *reinterpret_cast<uint4*>(codes + row * args.ldo + col / 2) = v;
-            const int64_t so = sf_atom_offset(row, col / 16, args.out_ncb);
-            *reinterpret_cast<uint16_t*>(args.out_sf + so) = static_cast<uint16_t>(s0 | (s1 << 8));
-          }
+          uint32_t p2[2];
+          sfw |= nvfp4_quant16(h, args.out_gs, p2) << (8 * q);
+          pk[2 * q] = p2[0];
+          pk[2 * q + 1] = p2[1];
+        }
+        if (valid) {
+          const int col = ti.nt * 128 + 64 * half;          // first h column of this warp's share
+          uint4* dst = reinterpret_cast<uint4*>(codes + row * args.ldo + col / 2);
+          dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          *reinterpret_cast<uint32_t*>(args.out_sf + sf_atom_offset(row, col / 16, args.out_ncb)) = sfw;
         }
       } else if constexpr (EPI == kEpiBF16) {
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld_32x32b_x32(tq + 32 * c, v);
-          tmem_ld_wait();
-          if (valid) {
-            uint32_t w[16];
+        // columns [128 half, +128)
+        float v[128];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i] * alpha, v[2 * i + 1] * alpha);
-              w[i] = *reinterpret_cast<uint32_t*>(&b2);
+        for (int c = 0; c < 4; ++c)
+          tmem_ld_32x32b_x32(tq + 128 * half + 32 * c, *reinterpret_cast<float(*)[32]>(v + 32 * c));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_acc_empty);
+        if (valid) {
+          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+          uint4* dst = reinterpret_cast<uint4*>(out + row * args.ldo + ti.nt * BN + 128 * half);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * i + 2 * j] * alpha, v[8 * i + 2 * j + 1] * alpha);
+              w[j] = *reinterpret_cast<uint32_t*>(&b2);
             }
-            uint4* dst = reinterpret_cast<uint4*>(out + row * args.ldo + ti.nt * BN + 32 * c);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       } else {
-        float* out = reinterpret_cast<float*>(args.out);
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld_32x32b_x32(tq + 32 * c, v);
-          tmem_ld_wait();
-          const int col0 = ti.nt * BN + 32 * c;
-          if (valid) {
-            if (col0 + 32 <= args.N) {
-              float4* dst = reinterpret_cast<float4*>(out + row * args.ldo + col0);
+        // columns [64 half, +64) of a 128-wide tile
+        float v[64];
+        tmem_ld_32x32b_x32(tq + 64 * half, *reinterpret_cast<float(*)[32]>(v));
+        tmem_ld_32x32b_x32(tq + 64 * half + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_acc_empty);
+        if (valid) {
+          float* out = reinterpret_cast<float*>(args.out);
+          const int col0 = ti.nt * BN + 64 * half;
+          if (col0 + 64 <= args.N) {
+            float4* dst = reinterpret_cast<float4*>(out + row * args.ldo + col0);
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
-                dst[i] = make_float4(v[4 * i] * alpha, v[4 * i + 1] * alpha, v[4 * i + 2] * alpha,
-                                     v[4 * i + 3] * alpha);
-            } else {
+            for (int i = 0; i < 16; ++i)
+              dst[i] = make_float4(v[4 * i] * alpha, v[4 * i + 1] * alpha, v[4 * i + 2] * alpha, v[4 * i + 3] * alpha);
+          } else {
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < args.N) out[row * args.ldo + col0 + i] = v[i] * alpha;
-            }
+            for (int i = 0; i < 64; ++i)
+              if (col0 + i < args.N) out[row * args.ldo + col0 + i] = v[i] * alpha;
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_acc_empty);
       ++iter;
     }
   }

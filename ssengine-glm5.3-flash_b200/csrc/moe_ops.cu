@@ -18,6 +18,7 @@ constexpr int kBlockTokens = 256;
 constexpr int kMaskWords = kBlockTokens / 32;
 
 // ---- NVFP4 activation quantizer: one thread per (row, atom column) = 64 elements, 4 scale bytes ----------------
+// The 128 input bytes are loaded before any arithmetic (8 independent 16-byte loads in flight per thread).
 __global__ void nvfp4_quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t K, int64_t ldx,
                                       float gs, uint8_t* __restrict__ codes, int64_t ldc, uint8_t* __restrict__ sf,
                                       int64_t ncb) {
@@ -26,25 +27,33 @@ __global__ void nvfp4_quantize_kernel(const __nv_bfloat16* __restrict__ x, int64
        idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = idx / ncb;
     const int64_t a = idx - r * ncb;
+    const int64_t k0 = a * 64;
+    const int64_t left = K - k0;
+    const int ng = left <= 0 ? 0 : (left >= 64 ? 4 : static_cast<int>(left / 16));
+    uint4 v[8];
+    const uint4* src = reinterpret_cast<const uint4*>(x + r * ldx + k0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (i >> 1) < ng ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
     uint32_t word = 0;
+    uint32_t pk[8];
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const int64_t k0 = a * 64 + g * 16;
-      if (k0 >= K) break;
-      const uint4* src = reinterpret_cast<const uint4*>(x + r * ldx + k0);
-      const uint4 v0 = src[0], v1 = src[1];
-      const __nv_bfloat16* b0 = reinterpret_cast<const __nv_bfloat16*>(&v0);
-      const __nv_bfloat16* b1 = reinterpret_cast<const __nv_bfloat16*>(&v1);
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v[2 * g]);
       float f[16];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        f[i] = __bfloat162float(b0[i]);
-        f[8 + i] = __bfloat162float(b1[i]);
-      }
+      for (int i = 0; i < 16; ++i) f[i] = __bfloat162float(b[i]);
       uint32_t p[2];
       const uint32_t s = nvfp4_quant16(f, gs, p);
-      *reinterpret_cast<uint2*>(codes + r * ldc + k0 / 2) = make_uint2(p[0], p[1]);
-      word |= s << (8 * g);
+      pk[2 * g] = p[0];
+      pk[2 * g + 1] = p[1];
+      if (g < ng) word |= s << (8 * g);
+    }
+    uint8_t* dst = codes + r * ldc + k0 / 2;
+    if (ng == 4) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<uint4*>(dst + 16) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    } else {
+      for (int g = 0; g < ng; ++g) *reinterpret_cast<uint2*>(dst + 8 * g) = make_uint2(pk[2 * g], pk[2 * g + 1]);
     }
     *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(r, a * 4, ncb)) = word;
   }
@@ -180,43 +189,57 @@ __global__ void moe_offsets_kernel(int64_t T, int E, int nblocks, int32_t* __res
 }
 
 // ---- permuted rows + gather of the token's NVFP4 codes and scales into its k + 1 rows -------------------------------
+// One warp per token: lanes 0..k-1 rank the token's routed slots, lane k takes the shared expert row; then the warp
+// copies the token's code row (16-byte vectors) and scale words into each destination row.
 __global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int64_t T, int E, int k,
                                    const uint32_t* __restrict__ masks, const int32_t* __restrict__ block_base,
                                    const int32_t* __restrict__ offsets, int32_t* __restrict__ rows,
                                    const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsf, int64_t H,
                                    uint8_t* __restrict__ xq_perm, uint8_t* __restrict__ xsf_perm) {
   const int lane = threadIdx.x & 31;
-  const int warps = blockDim.x >> 5;
-  const int b = blockIdx.x;
+  const int64_t t = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
   const int64_t ncb = sf_atom_cols(H);
   const int64_t row_bytes = H / 2;
-  for (int i = threadIdx.x >> 5; i < kBlockTokens; i += warps) {
-    const int64_t t = (int64_t)b * kBlockTokens + i;
-    if (t >= T) break;
-    int my_row = -1;
-    if (lane < k) {
-      const int e = ids[t * k + lane];
-      const uint32_t* m = masks + ((int64_t)b * E + e) * kMaskWords;
-      const int w = i >> 5;
-      int rank = block_base[(int64_t)b * E + e];
-      for (int q = 0; q < w; ++q) rank += __popc(m[q]);
-      rank += __popc(m[w] & ((1u << (i & 31)) - 1u));
-      my_row = offsets[e] + rank;
-      rows[t * k + lane] = my_row;
-    }
-    if (lane == k) my_row = offsets[E] + static_cast<int>(t);   // shared expert
-    // gather: codes (16-byte vectors) and scale words of row t into the k + 1 destination rows
-    const uint4* src = reinterpret_cast<const uint4*>(xq + t * row_bytes);
-    const int nvec = static_cast<int>(row_bytes / 16);
-    for (int d = 0; d <= k; ++d) {
-      const int64_t dst_row = __shfl_sync(0xFFFFFFFFu, my_row, d);
-      uint4* dst = reinterpret_cast<uint4*>(xq_perm + dst_row * row_bytes);
-      for (int v = lane; v < nvec; v += 32) dst[v] = src[v];
-      for (int a = lane; a < ncb; a += 32) {
-        const uint32_t wv = *reinterpret_cast<const uint32_t*>(xsf + sf_atom_offset(t, a * 4, ncb));
-        *reinterpret_cast<uint32_t*>(xsf_perm + sf_atom_offset(dst_row, a * 4, ncb)) = wv;
-      }
-    }
+  const int64_t b = t / kBlockTokens;
+  const int i = static_cast<int>(t - b * kBlockTokens);
+  int my_row = -1;
+  if (lane < k) {
+    const int e = ids[t * k + lane];
+    const uint32_t* m = masks + (b * E + e) * kMaskWords;
+    const int w = i >> 5;
+    int rank = block_base[b * E + e];
+    for (int q = 0; q < w; ++q) rank += __popc(m[q]);
+    rank += __popc(m[w] & ((1u << (i & 31)) - 1u));
+    my_row = offsets[e] + rank;
+    rows[t * k + lane] = my_row;
+  }
+  if (lane == k) my_row = offsets[E] + static_cast<int>(t);   // shared expert
+  const uint4* src = reinterpret_cast<const uint4*>(xq + t * row_bytes);
+  const int nvec = static_cast<int>(row_bytes / 16);
+  constexpr int kVecPerLane = 8;                               // up to H = 8192 in registers
+  uint4 reg[kVecPerLane];
+#pragma unroll
+  for (int j = 0; j < kVecPerLane; ++j)
+    if (lane + 32 * j < nvec) reg[j] = __ldg(src + lane + 32 * j);
+  uint32_t sw[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (lane + 32 * j < ncb) sw[j] = *reinterpret_cast<const uint32_t*>(xsf + sf_atom_offset(t, (lane + 32 * j) * 4, ncb));
+  for (int d = 0; d <= k; ++d) {
+    const int64_t dst_row = __shfl_sync(0xFFFFFFFFu, my_row, d);
+    uint4* dst = reinterpret_cast<uint4*>(xq_perm + dst_row * row_bytes);
+#pragma unroll
+    for (int j = 0; j < kVecPerLane; ++j)
+      if (lane + 32 * j < nvec) dst[lane + 32 * j] = reg[j];
+    for (int v = lane + 32 * kVecPerLane; v < nvec; v += 32) dst[v] = src[v];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (lane + 32 * j < ncb)
+        *reinterpret_cast<uint32_t*>(xsf_perm + sf_atom_offset(dst_row, (lane + 32 * j) * 4, ncb)) = sw[j];
+    for (int a = lane + 128; a < ncb; a += 32)
+      *reinterpret_cast<uint32_t*>(xsf_perm + sf_atom_offset(dst_row, a * 4, ncb)) =
+          *reinterpret_cast<const uint32_t*>(xsf + sf_atom_offset(t, a * 4, ncb));
   }
 }
 
@@ -316,9 +339,9 @@ int launch_moe_scatter(const int32_t* ids, int64_t T, int32_t E, int32_t k, cons
                        const uint8_t* xsf, int64_t H, uint8_t* xq_perm, uint8_t* xsf_perm, cudaStream_t stream) {
   if (k >= 32 || H % 32 != 0) return kErrArgs;
   if (T == 0) return kOk;
-  const int nblocks = static_cast<int>((T + kBlockTokens - 1) / kBlockTokens);
-  moe_scatter_kernel<<<nblocks, 512, 0, stream>>>(ids, T, E, k, masks, block_base, offsets, rows, xq, xsf, H, xq_perm,
-                                                  xsf_perm);
+  const int64_t blocks = (T + 7) / 8;   // 8 warps per block, one token per warp
+  moe_scatter_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ids, T, E, k, masks, block_base, offsets, rows,
+                                                                        xq, xsf, H, xq_perm, xsf_perm);
   return last_error();
 }
 
