@@ -355,7 +355,7 @@ def main() -> None:
                          "algorithmic": f"2 * {T * K_TOP + T} rows * {2 * F} * {H} = {gate_flops:.4e} FLOP/launch",
                          "layer_frac": layer_flops(T) / (ms_step / 1e3) / 1e12 / fp4_peak},
             "kernels_ms": {k: round(v, 5) for k, v in per_kernel.items()},
-            "gpu_launches": steps * nst,
+            "gpu_launches": steps * lib.MOE_KERNELS,
             "clocks": clk,
         }
         if e2e_ms is not None:
