@@ -29,6 +29,9 @@ sys.path.insert(0, str(ROOT))
 H, F, E, K_TOP = 4096, 1024, 128, 8
 SEED = 20261201
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch at T = 8192, from the ncu capture summarised in
+# profiles/gemm_nvfp4_moe_T8192_full.md (796.9 MB + 39.6 MB); None for other token counts
+GATE_UP_TRAFFIC_T8192 = 836.5e6
 
 
 def parse():
@@ -349,7 +352,8 @@ def main() -> None:
                        "l2": "inputs larger than L2 (0.9 GB of expert weights + 1 GB workspace per step)"},
             "roofline": {"kernel": "gate_up grouped NVFP4 GEMM (SwiGLU + requant epilogue)", "bound": "tensor",
                          "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
-                         "traffic": None,
+                         "traffic": GATE_UP_TRAFFIC_T8192 if T == 8192 else None,
+                         "traffic_unit": "bytes per launch (ncu capture)",
                          "peak_source": f"4 x {src} dense bf16 {pk['bf16_tflops']} TFLOP/s (B200 dense NVFP4 rate "
                                         f"is 4x bf16)",
                          "algorithmic": f"2 * {T * K_TOP + T} rows * {2 * F} * {H} = {gate_flops:.4e} FLOP/launch",
