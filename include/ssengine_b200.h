@@ -55,6 +55,16 @@ int ssb_nvfp4_gemm(int32_t epilogue, const uint8_t* a_codes, const uint8_t* a_sf
  * Replaces the routing stage of FlashInfer `trtllm_fp4_block_scale_moe` (ssengine/kernels.py:182-187, config 30). */
 int ssb_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* ids, float* weights, void* stream);
 
+/* Canonical top-k of the DSA indexer, per row: over columns [ks[r], ke[r]) of logits (fp32, row pitch ld elements),
+ * every key above the k-th largest value plus the lowest-column keys equal to it, as columns relative to ks[r] in
+ * ascending order, -1 past the number selected; rows of at most k keys select all their keys. out int32 [rows, k].
+ * max_keys: an upper bound of ke - ks (rows up to min(max_keys, 4096) keys are cached in shared memory, longer rows
+ * are re-read from L2 per pass). NaN sorts below every number. Replaces the reference's per-row top-k kernels (DeepSelect /
+ * vLLM top_k_per_row_prefill, ssengine/kernels.py:147-154, configs 20/21) followed by `topk_canon.canonicalize`
+ * (ssengine/model/topk_canon.py:130-147): the canonical set is selected directly. */
+int ssb_topk_canonical(const float* logits, int64_t rows, int64_t ld, const int32_t* ks, const int32_t* ke, int32_t k,
+                       int32_t* out, int32_t max_keys, void* stream);
+
 /* One NVFP4 MoE layer's device parameters (all pointers device memory, owned by the caller).
  * Experts 0..E-1 are routed, expert E is the shared expert (every token, weight 1). */
 typedef struct ssb_moe_layer {

@@ -118,6 +118,14 @@ int ssb_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32_t*
   return ssb::launch_moe_route(logits, T, E, k, ids, weights, static_cast<cudaStream_t>(stream));
 }
 
+int ssb_topk_canonical(const float* logits, int64_t rows, int64_t ld, const int32_t* ks, const int32_t* ke, int32_t k,
+                       int32_t* out, int32_t max_keys, void* stream) {
+  if (logits == nullptr || ks == nullptr || ke == nullptr || out == nullptr || rows < 0 || k <= 0 || ld <= 0 ||
+      max_keys < 0)
+    return kErrArgs;
+  return ssb::launch_topk_canonical(logits, rows, ld, ks, ke, k, out, max_keys, static_cast<cudaStream_t>(stream));
+}
+
 int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T) {
   MoeDims d;
   if (!dims_of(layer, T, d)) return -1;

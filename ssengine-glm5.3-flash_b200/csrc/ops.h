@@ -59,6 +59,10 @@ int launch_moe_scatter(const int32_t* ids, int64_t T, int32_t E, int32_t k, cons
 int launch_moe_combine(const void* y, int64_t H, const int32_t* rows, const float* weights, const int32_t* offsets,
                        int64_t T, int32_t E, int32_t k, void* out, cudaStream_t stream);
 
+// Canonical per-row top-k of the indexer (csrc/topk.cu); max_keys bounds ke - ks (sizes the shared-memory row cache).
+int launch_topk_canonical(const float* logits, int64_t rows, int64_t ld, const int32_t* ks, const int32_t* ke,
+                          int32_t k, int32_t* out, int32_t max_keys, cudaStream_t stream);
+
 int device_sm_count();
 
 }  // namespace ssb

@@ -16,7 +16,7 @@ LIB_PATH = PKG / "libssengine_b200.so"
 # every symbol include/ssengine_b200.h declares
 EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_gemm", "ssb_moe_route",
            "ssb_moe_workspace_bytes", "ssb_moe_workspace_offsets", "ssb_moe_forward", "ssb_moe_forward_profiled",
-           "ssb_moe_route_permute_noalloc")
+           "ssb_moe_route_permute_noalloc", "ssb_topk_canonical")
 
 EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
 
@@ -60,6 +60,7 @@ _SIGS = {
     "ssb_moe_forward_profiled": ([ctypes.POINTER(MoeLayerC), _P, _I64, _P, _P, _I64, _P, _P,
                                   ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "ssb_moe_route_permute_noalloc": ([_P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int),
+    "ssb_topk_canonical": ([_P, _I64, _I64, _P, _P, _I32, _P, _I32, _P], ctypes.c_int),
 }
 
 MOE_KERNELS = 9       # kernels ssb_moe_forward launches (+ a memset when F % 256 != 0)
