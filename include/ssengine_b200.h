@@ -65,6 +65,31 @@ int ssb_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32_t*
 int ssb_topk_canonical(const float* logits, int64_t rows, int64_t ld, const int32_t* ks, const int32_t* ke, int32_t k,
                        int32_t* out, int32_t max_keys, void* stream);
 
+/* Device-side metadata of a microbatch (the reference builds it with numpy on the host: ssengine/model/metadata.py
+ * `g0_table` :79-96 and `graph_rows` :65-76, inside `StageMetadata.build` :210-313). Inputs, device, the plan's
+ * requests in row order: qsl int32 [R+1] (first row of each request, qsl[R] = T), starts int32 [R] (tokens already in
+ * KV), page_ptr int32 [R+1] and pages int32 (each request's KV pages of page_tokens tokens, page p = kernel blocks
+ * p * kpp .. p * kpp + kpp - 1, kpp = page_tokens / 64). Outputs: positions int64 [bucket] and slots int64 [bucket]
+ * (rows >= T of a CUDA-graph bucket: position 0, slot -1), table int32 [R, width] (kernel-block table, zero past a
+ * request's pages; may be null). Bit-exact with the reference's functions. */
+int ssb_stage_metadata(const int32_t* qsl, const int32_t* starts, const int32_t* page_ptr, const int32_t* pages,
+                       int32_t R, int64_t T, int64_t bucket, int32_t page_tokens, int32_t width, int64_t* positions,
+                       int64_t* slots, int32_t* table, void* stream);
+
+/* Stage-0 embedding: out bf16 [T, H] = table bf16 [vocab, H] rows ids int64 [T] (ids outside [0, vocab): zeros).
+ * Replaces the fork's embedding lookup on stage 0 (ssengine/model/stage.py:725-734, `hidden_in is None`). */
+int ssb_embed_rows(const void* table, int64_t vocab, int64_t H, const int64_t* ids, int64_t T, void* out,
+                   void* stream);
+
+/* y bf16 [n, H] = RMSNorm(x[rows[i]]) * w (rows int64 [n] or null for rows 0..n-1), fp32 statistics.
+ * Replaces vLLM `rms_norm` of the final norm (ssengine/kernels.py:200-202, config 34). */
+int ssb_rmsnorm(const void* x, int64_t H, const int64_t* rows, int64_t n, const void* w, float eps, void* y,
+                void* stream);
+
+/* out int64 [n] = the lowest column of the maximum of logits fp32 [n, N] (row pitch ld; NaN never wins): the last
+ * stage's greedy token (ssengine/model/stage.py:746-762 `head_logits` + argmax). */
+int ssb_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, void* stream);
+
 /* One NVFP4 MoE layer's device parameters (all pointers device memory, owned by the caller).
  * Experts 0..E-1 are routed, expert E is the shared expert (every token, weight 1). */
 typedef struct ssb_moe_layer {
@@ -84,6 +109,7 @@ typedef struct ssb_moe_layer {
   const uint8_t* w2_codes;     /* [(E+1) * H, F/2] */
   const uint8_t* w2_sf;        /* atoms of [(E+1) * H, F] */
   const float* w2_alpha;       /* [E+1]: 1 / (gs_h * gs_w2[e]) */
+  int32_t add_input;           /* nonzero: out = x + MoE(x) (the residual add fused into the combine) */
 } ssb_moe_layer;
 
 /* Workspace of ssb_moe_forward for T tokens, in bytes (one caller-owned device buffer, 256-byte aligned). */

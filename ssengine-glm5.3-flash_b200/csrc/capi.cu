@@ -126,6 +126,33 @@ int ssb_topk_canonical(const float* logits, int64_t rows, int64_t ld, const int3
   return ssb::launch_topk_canonical(logits, rows, ld, ks, ke, k, out, max_keys, static_cast<cudaStream_t>(stream));
 }
 
+int ssb_stage_metadata(const int32_t* qsl, const int32_t* starts, const int32_t* page_ptr, const int32_t* pages,
+                       int32_t R, int64_t T, int64_t bucket, int32_t page_tokens, int32_t width, int64_t* positions,
+                       int64_t* slots, int32_t* table, void* stream) {
+  if (positions == nullptr || slots == nullptr || (R > 0 && (qsl == nullptr || starts == nullptr ||
+                                                              page_ptr == nullptr || pages == nullptr)))
+    return kErrArgs;
+  return ssb::launch_stage_metadata(qsl, starts, page_ptr, pages, R, T, bucket, page_tokens, width, positions, slots,
+                                    table, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_embed_rows(const void* table, int64_t vocab, int64_t H, const int64_t* ids, int64_t T, void* out,
+                   void* stream) {
+  if (table == nullptr || ids == nullptr || out == nullptr) return kErrArgs;
+  return ssb::launch_embed_rows(table, vocab, H, ids, T, out, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_rmsnorm(const void* x, int64_t H, const int64_t* rows, int64_t n, const void* w, float eps, void* y,
+                void* stream) {
+  if (x == nullptr || w == nullptr || y == nullptr) return kErrArgs;
+  return ssb::launch_rmsnorm(x, H, rows, n, w, eps, y, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, void* stream) {
+  if (logits == nullptr || out == nullptr) return kErrArgs;
+  return ssb::launch_argmax_rows(logits, ld, N, n, out, static_cast<cudaStream_t>(stream));
+}
+
 int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T) {
   MoeDims d;
   if (!dims_of(layer, T, d)) return -1;
@@ -278,7 +305,7 @@ int moe_forward(const ssb_moe_layer* L, const void* x, int64_t T, void* out, voi
   // 7. weighted combine + shared expert
   mark(8);
   rc = ssb::launch_moe_combine(y, d.H, rows, wts, offsets, T, static_cast<int32_t>(d.E), static_cast<int32_t>(d.k),
-                               out, stream);
+                               L->add_input ? x : nullptr, out, stream);
   if (rc != kOk) return rc;
   mark(9);
   return kOk;

@@ -243,18 +243,26 @@ __global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int64_t T, i
   }
 }
 
-// ---- weighted combine: out[t] = sum_j w[t, j] y[rows[t, j]] + y[shared row of t], fp32 accumulate, bf16 out -------
+// ---- weighted combine: out[t] = (x[t]) + sum_j w[t, j] y[rows[t, j]] + y[shared row of t], fp32 accumulate -----
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int64_t H, const int32_t* __restrict__ rows,
                                    const float* __restrict__ weights, const int32_t* __restrict__ offsets, int64_t T,
-                                   int E, int k, __nv_bfloat16* __restrict__ out) {
+                                   int E, int k, const __nv_bfloat16* __restrict__ residual,
+                                   __nv_bfloat16* __restrict__ out) {
   const int64_t t = blockIdx.x;
   if (t >= T) return;
   const int64_t srow = offsets[E] + t;
   const int nvec = static_cast<int>(H / 8);
   for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
     float acc[8];
+    if (residual != nullptr) {
+      const uint4 q = reinterpret_cast<const uint4*>(residual + t * H)[v];
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&q);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+      for (int i = 0; i < 8; ++i) acc[i] = __bfloat162float(b[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    }
     for (int j = 0; j < k; ++j) {
       const int64_t r = rows[t * k + j];
       const float w = weights[t * k + j];
@@ -346,13 +354,13 @@ int launch_moe_scatter(const int32_t* ids, int64_t T, int32_t E, int32_t k, cons
 }
 
 int launch_moe_combine(const void* y, int64_t H, const int32_t* rows, const float* weights, const int32_t* offsets,
-                       int64_t T, int32_t E, int32_t k, void* out, cudaStream_t stream) {
+                       int64_t T, int32_t E, int32_t k, const void* residual, void* out, cudaStream_t stream) {
   if (H % 8 != 0) return kErrArgs;
   if (T == 0) return kOk;
   const int threads = H / 8 >= 512 ? 512 : static_cast<int>((H / 8 + 31) / 32 * 32);
   moe_combine_kernel<<<static_cast<unsigned>(T), threads, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(y), H, rows, weights, offsets, T, E, k,
-      reinterpret_cast<__nv_bfloat16*>(out));
+      reinterpret_cast<const __nv_bfloat16*>(residual), reinterpret_cast<__nv_bfloat16*>(out));
   return last_error();
 }
 

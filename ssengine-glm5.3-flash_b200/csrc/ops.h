@@ -56,12 +56,23 @@ int launch_moe_scatter(const int32_t* ids, int64_t T, int32_t E, int32_t k, cons
                        const int32_t* block_base, const int32_t* offsets, int32_t* rows, const uint8_t* xq,
                        const uint8_t* xsf, int64_t H, uint8_t* xq_perm, uint8_t* xsf_perm, cudaStream_t stream);
 
+// out = (residual if not null) + sum_j w[t, j] y[rows[t, j]] + y[shared row of t]
 int launch_moe_combine(const void* y, int64_t H, const int32_t* rows, const float* weights, const int32_t* offsets,
-                       int64_t T, int32_t E, int32_t k, void* out, cudaStream_t stream);
+                       int64_t T, int32_t E, int32_t k, const void* residual, void* out, cudaStream_t stream);
 
 // Canonical per-row top-k of the indexer (csrc/topk.cu); max_keys bounds ke - ks (sizes the shared-memory row cache).
 int launch_topk_canonical(const float* logits, int64_t rows, int64_t ld, const int32_t* ks, const int32_t* ke,
                           int32_t k, int32_t* out, int32_t max_keys, cudaStream_t stream);
+
+// Stage kernels (csrc/stage.cu).
+int launch_stage_metadata(const int32_t* qsl, const int32_t* starts, const int32_t* page_ptr, const int32_t* pages,
+                          int32_t R, int64_t T, int64_t bucket, int32_t page_tokens, int32_t width,
+                          int64_t* positions, int64_t* slots, int32_t* table, cudaStream_t stream);
+int launch_embed_rows(const void* table, int64_t vocab, int64_t H, const int64_t* ids, int64_t T, void* out,
+                      cudaStream_t stream);
+int launch_rmsnorm(const void* x, int64_t H, const int64_t* rows, int64_t n, const void* w, float eps, void* y,
+                   cudaStream_t stream);
+int launch_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, cudaStream_t stream);
 
 int device_sm_count();
 

@@ -1,0 +1,196 @@
+// Stage-level kernels around the layers (sm_100a): device-side microbatch metadata, the stage-0 embedding gather,
+// RMSNorm and the last stage's greedy argmax.
+//
+// Metadata (the reference builds it on the host with numpy and copies one packed buffer, ssengine/model/metadata.py:
+// 79-96, 210-313): from the compact per-request arrays of a plan in row order -- qsl [R+1] (first row of each
+// request), starts [R] (tokens already in KV), page_ptr [R+1] and pages (each request's 128-token KV pages) --
+// this builds on the device, bit-exact with the reference's `g0_table` / `graph_rows`:
+//   positions[t] = starts[r] + t - qsl[r]                         (pad rows of a graph bucket: 0)
+//   slots[t]     = pages[r][pos / P] * P + pos % P                (pad rows: -1, they write no KV)
+//   table[r, c]  = pages[r][c / kpp] * kpp + c % kpp  for c < ceil(seq_len / P) * kpp, else 0   (kpp = P / 64)
+// so only the plan's page ids cross PCIe, not the expanded tables.
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace ssb {
+
+namespace {
+
+__global__ void stage_rows_kernel(const int32_t* __restrict__ qsl, const int32_t* __restrict__ starts,
+                                  const int32_t* __restrict__ page_ptr, const int32_t* __restrict__ pages, int R,
+                                  int64_t T, int64_t bucket, int page_tokens, int64_t* __restrict__ positions,
+                                  int64_t* __restrict__ slots) {
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < bucket; t += (int64_t)gridDim.x * blockDim.x) {
+    if (t >= T) {
+      positions[t] = 0;
+      slots[t] = -1;
+      continue;
+    }
+    int lo = 0, hi = R;                          // last r with qsl[r] <= t
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (qsl[mid] <= t) lo = mid; else hi = mid;
+    }
+    const int64_t pos = starts[lo] + (t - qsl[lo]);
+    positions[t] = pos;
+    slots[t] = static_cast<int64_t>(pages[page_ptr[lo] + pos / page_tokens]) * page_tokens + pos % page_tokens;
+  }
+}
+
+__global__ void stage_table_kernel(const int32_t* __restrict__ qsl, const int32_t* __restrict__ starts,
+                                   const int32_t* __restrict__ page_ptr, const int32_t* __restrict__ pages, int R,
+                                   int width, int page_tokens, int kpp, int32_t* __restrict__ table) {
+  const int64_t total = static_cast<int64_t>(R) * width;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int r = static_cast<int>(idx / width);
+    const int c = static_cast<int>(idx - static_cast<int64_t>(r) * width);
+    const int64_t seq = starts[r] + (qsl[r + 1] - qsl[r]);
+    const int64_t n = (seq + page_tokens - 1) / page_tokens;
+    table[idx] = c < n * kpp ? pages[page_ptr[r] + c / kpp] * kpp + c % kpp : 0;
+  }
+}
+
+// out[t, :] = table[ids[t], :] (bf16 rows, 16-byte vectors); ids outside [0, vocab) give a zero row.
+__global__ void embed_rows_kernel(const __nv_bfloat16* __restrict__ table, int64_t vocab, int64_t H,
+                                  const int64_t* __restrict__ ids, int64_t T, __nv_bfloat16* __restrict__ out) {
+  const int64_t nvec = H / 8;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < T * nvec;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = idx / nvec, v = idx - t * nvec;
+    const int64_t id = ids[t];
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (id >= 0 && id < vocab) val = reinterpret_cast<const uint4*>(table + id * H)[v];
+    reinterpret_cast<uint4*>(out + t * H)[v] = val;
+  }
+}
+
+// y[r] = x[rows[r]] * rsqrt(mean(x^2) + eps) * w, one block per output row (rows == nullptr: row r).
+__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int64_t H, const int64_t* __restrict__ rows,
+                               int64_t n, const __nv_bfloat16* __restrict__ w, float eps,
+                               __nv_bfloat16* __restrict__ y) {
+  __shared__ float red[32];
+  const int64_t r = blockIdx.x;
+  if (r >= n) return;
+  const int64_t src = rows != nullptr ? rows[r] : r;
+  const __nv_bfloat16* xr = x + src * H;
+  float ss = 0.0f;
+  for (int64_t i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = __bfloat162float(xr[i]);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / static_cast<float>(H) + eps);
+  for (int64_t i = threadIdx.x; i < H; i += blockDim.x)
+    y[r * H + i] = __float2bfloat16(__bfloat162float(xr[i]) * inv * __bfloat162float(w[i]));
+}
+
+// out[r] = the lowest column holding the maximum of logits[r, :N] (NaN never wins), one block per row.
+__global__ void argmax_kernel(const float* __restrict__ logits, int64_t ld, int64_t N, int64_t n,
+                              int64_t* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int64_t si[32];
+  const int64_t r = blockIdx.x;
+  if (r >= n) return;
+  const float* row = logits + r * ld;
+  float bv = -INFINITY;
+  int64_t bi = N;
+  for (int64_t i = threadIdx.x; i < N; i += blockDim.x) {
+    const float v = row[i];
+    if (v > bv || (v == bv && i < bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+    const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = bv;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    bv = threadIdx.x < nw ? sv[threadIdx.x] : -INFINITY;
+    bi = threadIdx.x < nw ? si[threadIdx.x] : N;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+      const int64_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (threadIdx.x == 0) out[r] = bi < N ? bi : 0;
+  }
+}
+
+int grid_of(int64_t work, int threads) {
+  int64_t b = (work + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+  if (b > cap) b = cap;
+  return static_cast<int>(b < 1 ? 1 : b);
+}
+
+}  // namespace
+
+int launch_stage_metadata(const int32_t* qsl, const int32_t* starts, const int32_t* page_ptr, const int32_t* pages,
+                          int32_t R, int64_t T, int64_t bucket, int32_t page_tokens, int32_t width,
+                          int64_t* positions, int64_t* slots, int32_t* table, cudaStream_t stream) {
+  if (R < 0 || T < 0 || bucket < T || page_tokens <= 0 || page_tokens % 64 != 0 || width < 0) return kErrArgs;
+  if (R == 0 && T > 0) return kErrArgs;
+  if (bucket > 0)
+    stage_rows_kernel<<<grid_of(bucket, 256), 256, 0, stream>>>(qsl, starts, page_ptr, pages, R, T, bucket,
+                                                                 page_tokens, positions, slots);
+  if (R > 0 && width > 0 && table != nullptr)
+    stage_table_kernel<<<grid_of(static_cast<int64_t>(R) * width, 256), 256, 0, stream>>>(
+        qsl, starts, page_ptr, pages, R, width, page_tokens, page_tokens / 64, table);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int launch_embed_rows(const void* table, int64_t vocab, int64_t H, const int64_t* ids, int64_t T, void* out,
+                      cudaStream_t stream) {
+  if (H % 8 != 0 || T < 0) return kErrArgs;
+  if (T == 0) return kOk;
+  embed_rows_kernel<<<grid_of(T * (H / 8), 256), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(table), vocab, H, ids, T, reinterpret_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int launch_rmsnorm(const void* x, int64_t H, const int64_t* rows, int64_t n, const void* w, float eps, void* y,
+                   cudaStream_t stream) {
+  if (H <= 0 || n < 0) return kErrArgs;
+  if (n == 0) return kOk;
+  rmsnorm_kernel<<<static_cast<unsigned>(n), 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), H, rows, n,
+                                                                reinterpret_cast<const __nv_bfloat16*>(w), eps,
+                                                                reinterpret_cast<__nv_bfloat16*>(y));
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int launch_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, cudaStream_t stream) {
+  if (N <= 0 || n < 0 || ld < N) return kErrArgs;
+  if (n == 0) return kOk;
+  argmax_kernel<<<static_cast<unsigned>(n), 256, 0, stream>>>(logits, ld, N, n, out);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+}  // namespace ssb

@@ -16,7 +16,8 @@ LIB_PATH = PKG / "libssengine_b200.so"
 # every symbol include/ssengine_b200.h declares
 EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_gemm", "ssb_moe_route",
            "ssb_moe_workspace_bytes", "ssb_moe_workspace_offsets", "ssb_moe_forward", "ssb_moe_forward_profiled",
-           "ssb_moe_route_permute_noalloc", "ssb_topk_canonical")
+           "ssb_moe_route_permute_noalloc", "ssb_topk_canonical", "ssb_stage_metadata", "ssb_embed_rows",
+           "ssb_rmsnorm", "ssb_argmax_rows")
 
 EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
 
@@ -41,7 +42,7 @@ class MoeLayerC(ctypes.Structure):
                 ("router_codes", ctypes.c_void_p), ("router_sf", ctypes.c_void_p), ("router_rows", ctypes.c_int64),
                 ("router_alpha", ctypes.c_float), ("w1_codes", ctypes.c_void_p), ("w1_sf", ctypes.c_void_p),
                 ("w1_alpha", ctypes.c_void_p), ("w2_codes", ctypes.c_void_p), ("w2_sf", ctypes.c_void_p),
-                ("w2_alpha", ctypes.c_void_p)]
+                ("w2_alpha", ctypes.c_void_p), ("add_input", ctypes.c_int32)]
 
 
 _LIB = None
@@ -61,6 +62,10 @@ _SIGS = {
                                   ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "ssb_moe_route_permute_noalloc": ([_P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int),
     "ssb_topk_canonical": ([_P, _I64, _I64, _P, _P, _I32, _P, _I32, _P], ctypes.c_int),
+    "ssb_stage_metadata": ([_P, _P, _P, _P, _I32, _I64, _I64, _I32, _I32, _P, _P, _P, _P], ctypes.c_int),
+    "ssb_embed_rows": ([_P, _I64, _I64, _P, _I64, _P, _P], ctypes.c_int),
+    "ssb_rmsnorm": ([_P, _I64, _P, _I64, _P, _F, _P, _P], ctypes.c_int),
+    "ssb_argmax_rows": ([_P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
 }
 
 MOE_KERNELS = 9       # kernels ssb_moe_forward launches (+ a memset when F % 256 != 0)

@@ -16,7 +16,7 @@ from . import layout, lib
 
 class MoELayer:
     def __init__(self, H: int, F: int, E: int, k: int, gs_x: float, gs_h: float, router: tuple, w1: tuple,
-                 w2: tuple, device):
+                 w2: tuple, device, add_input: bool = False):
         self.H, self.F, self.E, self.k = H, F, E, k
         self.gs_x, self.gs_h = float(gs_x), float(gs_h)
         self.device = torch.device(device)
@@ -27,14 +27,16 @@ class MoELayer:
         self._c = lib.MoeLayerC(H, F, E, k, self.gs_x, self.gs_h, self.router_codes.data_ptr(),
                                 self.router_sf.data_ptr(), self.router_rows, self.router_alpha,
                                 self.w1_codes.data_ptr(), self.w1_sf.data_ptr(), self.w1_alpha.data_ptr(),
-                                self.w2_codes.data_ptr(), self.w2_sf.data_ptr(), self.w2_alpha.data_ptr())
+                                self.w2_codes.data_ptr(), self.w2_sf.data_ptr(), self.w2_alpha.data_ptr(),
+                                1 if add_input else 0)
+        self.add_input = add_input
         self._ws = None
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     # ---------------------------------------------------------------- construction
     @classmethod
-    def from_logical(cls, p: dict, k: int, device) -> "MoELayer":
-        """From `weights.moe_logical` parameters (torch tensors on any device)."""
+    def from_logical(cls, p: dict, k: int, device, add_input: bool = False) -> "MoELayer":
+        """From `weights.moe_logical` parameters (torch tensors on any device); `add_input`: out = x + MoE(x)."""
         dev = torch.device(device)
         H, F, E = p["H"], p["F"], p["E"]
         rc, rs, rg = (t.to(dev) if isinstance(t, torch.Tensor) else t for t in p["router"])
@@ -58,7 +60,7 @@ class MoELayer:
               torch.tensor(a1, dtype=torch.float32, device=dev))
         w2 = (torch.cat(w2c).contiguous(), torch.cat(w2s).contiguous(),
               torch.tensor(a2, dtype=torch.float32, device=dev))
-        return cls(H, F, E, k, p["gs_x"], p["gs_h"], router, w1, w2, dev)
+        return cls(H, F, E, k, p["gs_x"], p["gs_h"], router, w1, w2, dev, add_input)
 
     # ---------------------------------------------------------------- forward
     def workspace_bytes(self, T: int) -> int:

@@ -1,0 +1,270 @@
+"""`StageModel`: the reference's stage interface over the CUDA library (the drop-in boundary).
+
+Mirrors ssengine/model/stage.py:216-762 of the reference and its contract in ssengine/runtime/README.md:72-100:
+- construction `StageModel(cfg, stage, device, *, num_blocks=None, warmup=True, cuda_graphs=None, ipc_kv=False,
+  extra_blocks=0)`; attributes `num_blocks` (counts the null block), `hidden_width`, `first`, `last`, `layer_range`;
+- `prepare(plan) -> Batch`: host work only (no wait on queued GPU work): row order with decode-class chunks
+  (<= 256 tokens) first, stably (ssengine/model/metadata.py:43,214), query start offsets, each request's KV pages,
+  stage-0 token ids and the last stage's rows, packed into ONE pinned buffer and copied in stream order; the
+  expanded metadata (positions, g0 slot mapping, kernel-block table) is then built on the device by
+  `ssb_stage_metadata` (the reference expands it with numpy on the host, metadata.py:79-96);
+- `run(batch, hidden_in)`: stage 0 embeds the token ids; the stage's layers run in order; stages 0..n-2 return
+  [T, hidden_width] bf16 on the device, the last stage returns int64 greedy tokens, one per `is_last` chunk in plan
+  chunk order; enqueues GPU work only, a fresh output per call;
+- `forward(plan, hidden_in) = run(prepare(plan), hidden_in)`; `tier_ranges()`.
+
+Layers built so far: NVFP4 MoE layers with a residual (x + MoE(x)); the hybrid model's mHC, KDA and DSA layers are
+not built yet, so `hidden_width` is the plain hidden size and the stage owns no KV tensors (`tier_ranges()` is empty).
+The last stage's head: RMSNorm of each request's last row, NVFP4 lm_head GEMM (fp32 logits), argmax (lowest index on
+ties).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import layout, lib, moe, weights
+
+DECODE_THRESHOLD = 256
+PAGE_TOKENS = 128
+BLOCK_TOKENS = 8576
+KERNEL_BLOCK = 64
+GRAPH_BUCKETS = (128,) + tuple(range(256, 8192 + 1, 256))
+PACK_ALIGN = 256
+
+
+def row_order(num_tokens: list[int]) -> list[int]:
+    """Chunk indices in row order: decode-class chunks (<= 256 tokens) first, stable (metadata.py:214)."""
+    return sorted(range(len(num_tokens)), key=lambda i: num_tokens[i] > DECODE_THRESHOLD)
+
+
+def graph_bucket(num_tokens: int, buckets=GRAPH_BUCKETS):
+    """The smallest bucket that holds the microbatch, or None (stage.py:67-69)."""
+    return next((b for b in sorted(buckets) if b >= num_tokens), None)
+
+
+def table_width(blocks: int, page_tokens: int = PAGE_TOKENS, block_tokens: int = BLOCK_TOKENS) -> int:
+    """Kernel-block columns of the g0 table: the longest request's blocks rounded up to a power of two
+    (metadata.py:181-189, without vLLM's full-width cap)."""
+    per_block = block_tokens // KERNEL_BLOCK
+    return (1 << max(blocks - 1, 0).bit_length()) * per_block
+
+
+@dataclass
+class StageConfig:
+    """What a stage reads of the run config (the reference's RunConfig fields `layer_split`, `scheduler.mb_tokens`,
+    `cuda_graphs`, plus the model dimensions the random-init weights need)."""
+    layer_split: tuple = (2,)
+    hidden: int = 4096
+    inter: int = 1024
+    experts: int = 128
+    top_k: int = 8
+    vocab: int = 151_552
+    mb_tokens: int = 8192
+    cuda_graphs: bool = False
+    num_blocks: int = 64
+    seed: int = 0
+    norm_eps: float = 1e-5
+
+
+@dataclass
+class Batch:
+    num_tokens: int
+    order: list[int]                   # plan chunk indices in row order
+    positions: torch.Tensor            # int64 [bucket or T], device
+    slots: torch.Tensor                # int64 [bucket or T], device (pad rows -1)
+    table: torch.Tensor                # int32 [R, width], device (g0 kernel-block table)
+    token_ids: torch.Tensor | None     # int64 [T], device (stage 0)
+    last_rows: torch.Tensor            # int64 [#is_last], rows whose token the last stage returns, plan chunk order
+    bucket: int | None = None
+    keep: list = field(default_factory=list)   # host / device buffers that must outlive the queued work
+
+
+class _Pack:
+    """Arrays of one microbatch in one pinned host buffer, copied to the device with one stream-ordered copy."""
+
+    def __init__(self):
+        self.items, self.size = [], 0
+
+    def add(self, a: np.ndarray) -> int:
+        a = np.ascontiguousarray(a)
+        off = -(-self.size // PACK_ALIGN) * PACK_ALIGN
+        self.items.append((off, a))
+        self.size = off + a.nbytes
+        return len(self.items) - 1
+
+    def copy(self, device) -> tuple[torch.Tensor, torch.Tensor]:
+        host = torch.empty(max(self.size, 8), dtype=torch.uint8, pin_memory=True)
+        hv = host.numpy()
+        for off, a in self.items:
+            hv[off:off + a.nbytes] = a.reshape(-1).view(np.uint8)
+        return host, host.to(device, non_blocking=True)
+
+    def view(self, dev: torch.Tensor, h: int, dtype: torch.dtype) -> torch.Tensor:
+        off, a = self.items[h]
+        return dev[off:off + a.nbytes].view(dtype).view(a.shape)
+
+
+class StageModel:
+    def __init__(self, cfg: StageConfig, stage: int, device, *, num_blocks: int | None = None, warmup: bool = True,
+                 cuda_graphs: bool | None = None, ipc_kv: bool = False, extra_blocks: int = 0):
+        self.cfg, self.stage = cfg, stage
+        self.device = torch.device(device)
+        split = list(cfg.layer_split)
+        if not 0 <= stage < len(split):
+            raise ValueError(f"stage {stage} outside the split {split}")
+        self.first, self.last = stage == 0, stage == len(split) - 1
+        start = sum(split[:stage])
+        self.layer_range = range(start, start + split[stage])
+        self.hidden_width = cfg.hidden
+        self.num_blocks = (num_blocks if num_blocks is not None else cfg.num_blocks) + extra_blocks
+        self.cuda_graphs = cfg.cuda_graphs if cuda_graphs is None else cuda_graphs
+        self.ipc_kv = ipc_kv
+        self._lib = lib.load()
+        H, F, E = cfg.hidden, cfg.inter, cfg.experts
+        self.layers = [moe.MoELayer.from_logical(weights.moe_logical(cfg.seed * 1000 + i, H, F, E, device=self.device),
+                                                 cfg.top_k, self.device, add_input=True) for i in self.layer_range]
+        if self.first:
+            g = torch.Generator(device=self.device)
+            g.manual_seed(cfg.seed * 1000 + 999)
+            self.embed = torch.randn(cfg.vocab, H, generator=g, device=self.device).to(torch.bfloat16)
+        if self.last:
+            self._init_head()
+        if warmup:
+            self._warm()
+
+    # ---------------------------------------------------------------- construction helpers
+    def _init_head(self) -> None:
+        cfg, H, V = self.cfg, self.cfg.hidden, self.cfg.vocab
+        g = torch.Generator(device=self.device)
+        g.manual_seed(cfg.seed * 1000 + 998)
+        rows = -(-V // 128) * 128
+        codes = torch.zeros(rows, H, dtype=torch.uint8, device=self.device)
+        codes[:V] = torch.randint(0, 16, (V, H), generator=g, device=self.device, dtype=torch.uint8)
+        table = torch.tensor(weights.SCALE_CODES, dtype=torch.uint8, device=self.device)
+        sf = torch.zeros(rows, H // 16, dtype=torch.uint8, device=self.device)
+        sf[:V] = table[torch.randint(0, len(weights.SCALE_CODES), (V, H // 16), generator=g, device=self.device)]
+        self.head_gs = weights.unit_gs(H)
+        self.head_codes = layout.pack_codes(codes).contiguous()
+        self.head_sf = layout.sf_to_atoms(sf, H)
+        self.head_alpha = float(1.0 / (weights.GS_X * self.head_gs))
+        self.norm_weight = torch.ones(H, dtype=torch.bfloat16, device=self.device)
+
+    def _warm(self) -> None:
+        """One forward of a small dummy plan: loads every kernel and sizes the shared workspace."""
+        from .messages import Chunk, Plan
+
+        n = min(256, self.cfg.mb_tokens)
+        pages = list(range(1, -(-n // PAGE_TOKENS) + 1))
+        plan = Plan(-1, [Chunk("warmup", 0, n, pages, [0] * 6, True, [0] * n if self.first else None)])
+        hidden = None if self.first else torch.zeros(n, self.hidden_width, dtype=torch.bfloat16, device=self.device)
+        self.forward(plan, hidden)
+        ws = max(layer.workspace_bytes(self.cfg.mb_tokens) for layer in self.layers) if self.layers else 0
+        shared = torch.empty(ws, dtype=torch.uint8, device=self.device) if ws else None
+        for layer in self.layers:
+            layer._ws = shared
+        torch.cuda.synchronize(self.device)
+
+    # ---------------------------------------------------------------- the interface
+    def prepare(self, plan) -> Batch:
+        chunks = plan.chunks
+        order = row_order([c.num_tokens for c in chunks])
+        R = len(order)
+        q_lens = np.array([chunks[i].num_tokens for i in order], dtype=np.int64)
+        starts = np.array([chunks[i].start for i in order], dtype=np.int64)
+        qsl = np.zeros(R + 1, dtype=np.int64)
+        np.cumsum(q_lens, out=qsl[1:])
+        T = int(qsl[-1])
+        seq = starts + q_lens
+        need = -(-seq // PAGE_TOKENS)
+        page_lists = []
+        for r, i in enumerate(order):
+            pg = chunks[i].kv_pages
+            if len(pg) < need[r]:
+                raise ValueError(f"chunk {chunks[i].req_id}: {len(pg)} KV pages for {int(seq[r])} tokens")
+            page_lists.append(np.asarray(pg[: need[r]], dtype=np.int64))
+        page_ptr = np.zeros(R + 1, dtype=np.int64)
+        np.cumsum([len(p) for p in page_lists], out=page_ptr[1:])
+        pages = np.concatenate(page_lists) if page_lists else np.zeros(0, dtype=np.int64)
+        if pages.size and (pages.max() >= 2 ** 31 or pages.min() < 0):
+            raise ValueError("page id outside int32")
+        row_end = {i: int(qsl[r + 1]) - 1 for r, i in enumerate(order)}
+        last = np.array([row_end[i] for i, c in enumerate(chunks) if c.is_last], dtype=np.int64)
+        bucket = graph_bucket(T) if self.cuda_graphs else None
+        width = table_width(int(max((-(-int(s) // BLOCK_TOKENS) for s in seq), default=1)))
+
+        pk = _Pack()
+        h = {"qsl": pk.add(qsl.astype(np.int32)), "starts": pk.add(starts.astype(np.int32)),
+             "page_ptr": pk.add(page_ptr.astype(np.int32)), "pages": pk.add(np.maximum(pages, 0).astype(np.int32)),
+             "last": pk.add(last)}
+        if self.first:
+            tok = np.concatenate([np.asarray(chunks[i].token_ids, dtype=np.int64) for i in order]) if R else \
+                np.zeros(0, dtype=np.int64)
+            if tok.shape[0] != T:
+                raise ValueError(f"stage 0 needs every chunk's token ids ({tok.shape[0]} for {T} rows)")
+            h["tok"] = pk.add(tok)
+        host, dev = pk.copy(self.device)
+        rows_out = bucket if bucket is not None else T
+        positions = torch.empty(max(rows_out, 1), dtype=torch.int64, device=self.device)
+        slots = torch.empty(max(rows_out, 1), dtype=torch.int64, device=self.device)
+        table = torch.empty(max(R * width, 1), dtype=torch.int32, device=self.device)
+        v = {k: pk.view(dev, i, torch.int64 if k in ("last", "tok") else torch.int32) for k, i in h.items()}
+        rc = self._lib.ssb_stage_metadata(v["qsl"].data_ptr(), v["starts"].data_ptr(), v["page_ptr"].data_ptr(),
+                                          v["pages"].data_ptr(), R, T, rows_out, PAGE_TOKENS, width,
+                                          positions.data_ptr(), slots.data_ptr(), table.data_ptr(), lib.stream_ptr())
+        lib.check("ssb_stage_metadata", rc)
+        return Batch(T, order, positions[:rows_out], slots[:rows_out], table[: R * width].view(R, width),
+                     v.get("tok"), v["last"], bucket, keep=[host, dev])
+
+    def run(self, batch: Batch, hidden_in: torch.Tensor | None) -> torch.Tensor:
+        T, H = batch.num_tokens, self.hidden_width
+        s = lib.stream_ptr()
+        if self.first:
+            x = torch.empty(T, H, dtype=torch.bfloat16, device=self.device)
+            lib.check("ssb_embed_rows", self._lib.ssb_embed_rows(self.embed.data_ptr(), self.cfg.vocab, H,
+                                                                 batch.token_ids.data_ptr(), T, x.data_ptr(), s))
+        else:
+            if hidden_in is None or tuple(hidden_in.shape) != (T, H) or hidden_in.dtype != torch.bfloat16:
+                raise ValueError(f"stage {self.stage} needs hidden_in bf16 [{T}, {H}]")
+            x = hidden_in
+        for layer in self.layers:
+            x = layer.forward(x, out=torch.empty(T, H, dtype=torch.bfloat16, device=self.device))
+        if not self.last:
+            return x
+        return self._head(x, batch.last_rows)
+
+    def forward(self, plan, hidden_in: torch.Tensor | None = None) -> torch.Tensor:
+        return self.run(self.prepare(plan), hidden_in)
+
+    def tier_ranges(self) -> list:
+        """Byte ranges of the stage's KV tensors for the capacity tiers: none yet (no KDA / DSA layers)."""
+        return []
+
+    # ---------------------------------------------------------------- last stage
+    def _head(self, x: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
+        n, H, V = rows.shape[0], self.hidden_width, self.cfg.vocab
+        tokens = torch.empty(n, dtype=torch.int64, device=self.device)
+        if n == 0:
+            return tokens
+        s = lib.stream_ptr()
+        y = torch.empty(n, H, dtype=torch.bfloat16, device=self.device)
+        lib.check("ssb_rmsnorm", self._lib.ssb_rmsnorm(x.data_ptr(), H, rows.data_ptr(), n, self.norm_weight.data_ptr(),
+                                                       self.cfg.norm_eps, y.data_ptr(), s))
+        npad = -(-n // 128) * 128
+        codes = torch.empty(npad, H // 2, dtype=torch.uint8, device=self.device)
+        sf = torch.zeros(npad // 128 * layout.sf_atom_cols(H) * 512, dtype=torch.uint8, device=self.device)
+        lib.check("ssb_nvfp4_quantize", self._lib.ssb_nvfp4_quantize(y.data_ptr(), n, H, H, weights.GS_X,
+                                                                     codes.data_ptr(), H // 2, sf.data_ptr(), s))
+        logits = torch.empty(n, V, dtype=torch.float32, device=self.device)
+        status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        lib.check("ssb_nvfp4_gemm", self._lib.ssb_nvfp4_gemm(lib.EPI_F32, codes.data_ptr(), sf.data_ptr(), n, H,
+                                                             self.head_codes.data_ptr(), self.head_sf.data_ptr(), V,
+                                                             self.head_alpha, logits.data_ptr(), V, None, 1.0,
+                                                             status.data_ptr(), s))
+        lib.check("ssb_argmax_rows", self._lib.ssb_argmax_rows(logits.data_ptr(), V, V, n, tokens.data_ptr(), s))
+        self.last_logits, self.last_normed, self.last_status = logits, y, status
+        return tokens

@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
 def layer_c(H=4096, F=1024, E=128, k=8):
     from ssengine_b200 import lib
 
-    return lib.MoeLayerC(H, F, E, k, 336.0, 84.0, 0, 0, 128, 1.0, 0, 0, 0, 0, 0, 0)
+    return lib.MoeLayerC(H, F, E, k, 336.0, 84.0, 0, 0, 128, 1.0, 0, 0, 0, 0, 0, 0, 0)
 
 
 def test_workspace_layout_on_the_host():
