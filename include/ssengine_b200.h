@@ -90,6 +90,27 @@ int ssb_rmsnorm(const void* x, int64_t H, const int64_t* rows, int64_t n, const 
  * stage's greedy token (ssengine/model/stage.py:746-762 `head_logits` + argmax). */
 int ssb_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, void* stream);
 
+/* mHC (4-stream hyper-connection) parameters of one layer boundary (device pointers except the scalars). */
+typedef struct ssb_mhc_params {
+  int32_t hidden;              /* H, % 64 == 0 */
+  int32_t hc_mult;             /* streams: 4 */
+  const float* fn;             /* [24, 4H] fp32: mixes = z @ fn^T */
+  const float* scale;          /* [3] fp32 */
+  const float* base;           /* [24] fp32 */
+  const void* norm_weight;     /* [H] bf16, the next layer's input RMSNorm */
+  float rms_eps, pre_eps, sinkhorn_eps, post_mult, norm_eps;
+  int32_t sinkhorn_repeat;
+} ssb_mhc_params;
+
+/* mHC at a layer boundary, one kernel. With x != NULL (post): new_res bf16 [T, 4, H] = post_in[j] * x + sum_i
+ * comb_in[i][j] * res[i] (x bf16 [T, H], post_in fp32 [T, 4], comb_in fp32 [T, 4, 4]). With y != NULL (pre, on new_res
+ * or, without post, on res): post_out fp32 [T, 4], comb_out fp32 [T, 4, 4] (Sinkhorn) and y bf16 [T, H] = the next
+ * layer's RMS-normed input. Both: the reference's fused boundary `MegaMhcPostPre` (ssengine/model/pp_patch.py:125-153,
+ * DeepGEMM mega_mhc, configs 1 and 7 at ssengine/kernels.py:76-80, 104-108); post only: `edge_send` (:156-158,
+ * config 33); pre only: `edge_recv` + hc_pre (:160-163). */
+int ssb_mhc(const ssb_mhc_params* p, const void* x, const void* res, const float* post_in, const float* comb_in,
+            void* new_res, float* post_out, float* comb_out, void* y, int64_t T, void* stream);
+
 /* One NVFP4 MoE layer's device parameters (all pointers device memory, owned by the caller).
  * Experts 0..E-1 are routed, expert E is the shared expert (every token, weight 1). */
 typedef struct ssb_moe_layer {

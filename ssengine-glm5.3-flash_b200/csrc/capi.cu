@@ -153,6 +153,21 @@ int ssb_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64
   return ssb::launch_argmax_rows(logits, ld, N, n, out, static_cast<cudaStream_t>(stream));
 }
 
+int ssb_mhc(const ssb_mhc_params* p, const void* x, const void* res, const float* post_in, const float* comb_in,
+            void* new_res, float* post_out, float* comb_out, void* y, int64_t T, void* stream) {
+  if (p == nullptr || res == nullptr || T < 0) return kErrArgs;
+  const bool do_post = x != nullptr;
+  const bool do_pre = y != nullptr;
+  if (do_post && (post_in == nullptr || comb_in == nullptr || new_res == nullptr)) return kErrArgs;
+  if (do_pre && (p->fn == nullptr || p->scale == nullptr || p->base == nullptr || p->norm_weight == nullptr ||
+                 post_out == nullptr || comb_out == nullptr))
+    return kErrArgs;
+  if (p->hc_mult != 4) return kErrArgs;
+  return ssb::launch_mhc(do_post, do_pre, x, res, post_in, comb_in, new_res, p->fn, p->scale, p->base, p->norm_weight,
+                         post_out, comb_out, y, T, p->hidden, p->rms_eps, p->pre_eps, p->sinkhorn_eps, p->post_mult,
+                         p->sinkhorn_repeat, p->norm_eps, static_cast<cudaStream_t>(stream));
+}
+
 int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T) {
   MoeDims d;
   if (!dims_of(layer, T, d)) return -1;

@@ -74,6 +74,12 @@ int launch_rmsnorm(const void* x, int64_t H, const int64_t* rows, int64_t n, con
                    cudaStream_t stream);
 int launch_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, cudaStream_t stream);
 
+// mHC layer boundary (csrc/mhc.cu): do_post -> new_res; do_pre -> post_out, comb_out, y.
+int launch_mhc(bool do_post, bool do_pre, const void* x, const void* res, const float* post_in, const float* comb_in,
+               void* new_res, const float* fn, const float* scale, const float* base, const void* norm_w,
+               float* post_out, float* comb_out, void* y, int64_t T, int64_t H, float rms_eps, float pre_eps,
+               float sinkhorn_eps, float post_mult, int repeat, float norm_eps, cudaStream_t stream);
+
 int device_sm_count();
 
 }  // namespace ssb

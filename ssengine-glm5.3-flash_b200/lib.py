@@ -17,7 +17,7 @@ LIB_PATH = PKG / "libssengine_b200.so"
 EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_gemm", "ssb_moe_route",
            "ssb_moe_workspace_bytes", "ssb_moe_workspace_offsets", "ssb_moe_forward", "ssb_moe_forward_profiled",
            "ssb_moe_route_permute_noalloc", "ssb_topk_canonical", "ssb_stage_metadata", "ssb_embed_rows",
-           "ssb_rmsnorm", "ssb_argmax_rows")
+           "ssb_rmsnorm", "ssb_argmax_rows", "ssb_mhc")
 
 EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
 
@@ -45,6 +45,14 @@ class MoeLayerC(ctypes.Structure):
                 ("w2_alpha", ctypes.c_void_p), ("add_input", ctypes.c_int32)]
 
 
+class MhcParamsC(ctypes.Structure):
+    """Mirror of `ssb_mhc_params`."""
+    _fields_ = [("hidden", ctypes.c_int32), ("hc_mult", ctypes.c_int32), ("fn", ctypes.c_void_p),
+                ("scale", ctypes.c_void_p), ("base", ctypes.c_void_p), ("norm_weight", ctypes.c_void_p),
+                ("rms_eps", ctypes.c_float), ("pre_eps", ctypes.c_float), ("sinkhorn_eps", ctypes.c_float),
+                ("post_mult", ctypes.c_float), ("norm_eps", ctypes.c_float), ("sinkhorn_repeat", ctypes.c_int32)]
+
+
 _LIB = None
 
 _P, _I32, _I64, _F = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
@@ -66,6 +74,7 @@ _SIGS = {
     "ssb_embed_rows": ([_P, _I64, _I64, _P, _I64, _P, _P], ctypes.c_int),
     "ssb_rmsnorm": ([_P, _I64, _P, _I64, _P, _F, _P, _P], ctypes.c_int),
     "ssb_argmax_rows": ([_P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
+    "ssb_mhc": ([ctypes.POINTER(MhcParamsC), _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P], ctypes.c_int),
 }
 
 MOE_KERNELS = 9       # kernels ssb_moe_forward launches (+ a memset when F % 256 != 0)
