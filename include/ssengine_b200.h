@@ -111,6 +111,42 @@ typedef struct ssb_mhc_params {
 int ssb_mhc(const ssb_mhc_params* p, const void* x, const void* res, const float* post_in, const float* comb_in,
             void* new_res, float* post_out, float* comb_out, void* y, int64_t T, void* stream);
 
+/* One KDA layer of this stage (device pointers except the scalars). Head dim 128 (key = value). */
+typedef struct ssb_kda_layer {
+  int32_t heads;               /* H: KDA heads of this stage's layer */
+  int32_t head_dim;            /* 128 */
+  const void* conv_weight;     /* bf16 [3 * H * 128][4]: q | k | v channels, taps oldest row first */
+  const float* a_log;          /* fp32 [H] */
+  const float* dt_bias;        /* fp32 [H * 128] */
+  float lower_bound;           /* gate lower bound (-5) */
+  float scale;                 /* head_dim^-0.5 */
+  void* conv_state;            /* bf16 conv state blocks [blocks][3][3 * H * 128] (x rows end-3 .. end-1) */
+  int64_t conv_state_stride;   /* elements between blocks, % 8 == 0 */
+  float* rec_state;            /* fp32 recurrent state blocks [blocks][H][128 value][128 key] */
+  int64_t rec_state_stride;    /* elements between blocks */
+} ssb_kda_layer;
+
+/* KDA prefill of one layer over a microbatch: short conv (width 4, SiLU) of the in_proj rows x bf16 [T, ldx] (q | k |
+ * v in columns [0, 3 * H * 128)), gate lower_bound * sigmoid(exp(A_log) * (g + dt_bias)) from the raw rows g bf16 [T,
+ * ldg], ldg % 8 == 0), beta = sigmoid(raw beta bf16 [T, ldb]), q / k L2-normalised, chunked (64) delta-rule scan;
+ * out bf16 [T, ldo]
+ * (H * 128 columns). seqs int32 [R][4] device = {first row, end row, state block, has initial state}; a sequence
+ * without initial state starts from zero conv rows and a zero state. Each sequence's recurrent state block is read
+ * and written in place, then its conv state block (the sequence's last 3 x rows). Sequences are processed in table
+ * order (longest first balances the grid). Rows outside every sequence are not written. status (device int32, may be
+ * NULL) receives 4 if a chunk's row copies did not land within 1 s (that sequence's state block is then left as it
+ * was).
+ * Replaces `kda_prefill_forward` (ssengine/model/pp_patch.py:215-244: kda_conv.conv_qkv + kda_state.gather +
+ * FlashInfer persistent KDA `fwd` + kda_state.scatter; configs 4 and 5 at ssengine/kernels.py:87-101). */
+int ssb_kda_prefill(const ssb_kda_layer* layer, const void* x, int64_t ldx, const void* g, int64_t ldg,
+                    const void* beta, int64_t ldb, int64_t T, const int32_t* seqs, int64_t R, void* out, int64_t ldo,
+                    int32_t* status, void* stream);
+
+/* The short conv alone: q, k, v bf16 [T, H * 128] each (contiguous) and the conv state blocks updated; rows outside
+ * every sequence are written as 0. Replaces `kda_conv.conv_qkv` (ssengine/model/kda_conv.py:146-164). */
+int ssb_kda_conv(const ssb_kda_layer* layer, const void* x, int64_t ldx, int64_t T, const int32_t* seqs, int64_t R,
+                 void* q, void* k, void* v, void* stream);
+
 /* One NVFP4 MoE layer's device parameters (all pointers device memory, owned by the caller).
  * Experts 0..E-1 are routed, expert E is the shared expert (every token, weight 1). */
 typedef struct ssb_moe_layer {

@@ -168,6 +168,50 @@ int ssb_mhc(const ssb_mhc_params* p, const void* x, const void* res, const float
                          p->sinkhorn_repeat, p->norm_eps, static_cast<cudaStream_t>(stream));
 }
 
+static bool kda_args(const ssb_kda_layer* L, const void* x, int64_t ldx, const int32_t* seqs, int64_t R,
+                     ssb::KdaArgs& a) {
+  if (L == nullptr || L->head_dim != 128 || L->heads <= 0 || L->heads > 1024 || R < 0 || R > (1 << 20)) return false;
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ldx = ldx;
+  a.conv_w = static_cast<const __nv_bfloat16*>(L->conv_weight);
+  a.a_log = L->a_log;
+  a.dt_bias = L->dt_bias;
+  a.lower_bound = L->lower_bound;
+  a.scale = L->scale;
+  a.conv_state = static_cast<__nv_bfloat16*>(L->conv_state);
+  a.cs_stride = L->conv_state_stride;
+  a.rec_state = L->rec_state;
+  a.rs_stride = L->rec_state_stride;
+  a.seqs = seqs;
+  a.R = static_cast<int32_t>(R);
+  a.H = L->heads;
+  a.P = L->heads * 128;
+  return true;
+}
+
+int ssb_kda_prefill(const ssb_kda_layer* layer, const void* x, int64_t ldx, const void* g, int64_t ldg,
+                    const void* beta, int64_t ldb, int64_t T, const int32_t* seqs, int64_t R, void* out, int64_t ldo,
+                    int32_t* status, void* stream) {
+  ssb::KdaArgs a;
+  if (T < 0 || !kda_args(layer, x, ldx, seqs, R, a)) return kErrArgs;
+  a.g = static_cast<const __nv_bfloat16*>(g);
+  a.ldg = ldg;
+  a.beta = static_cast<const __nv_bfloat16*>(beta);
+  a.ldb = ldb;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.ldo = ldo;
+  a.status = status;
+  if (ldg < a.P || ldb < a.H) return kErrArgs;
+  return ssb::launch_kda_prefill(a, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_kda_conv(const ssb_kda_layer* layer, const void* x, int64_t ldx, int64_t T, const int32_t* seqs, int64_t R,
+                 void* q, void* k, void* v, void* stream) {
+  ssb::KdaArgs a;
+  if (T < 0 || !kda_args(layer, x, ldx, seqs, R, a)) return kErrArgs;
+  return ssb::launch_kda_conv(a, T, q, k, v, static_cast<cudaStream_t>(stream));
+}
+
 int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T) {
   MoeDims d;
   if (!dims_of(layer, T, d)) return -1;

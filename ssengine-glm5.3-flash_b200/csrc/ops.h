@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -79,6 +80,34 @@ int launch_mhc(bool do_post, bool do_pre, const void* x, const void* res, const 
                void* new_res, const float* fn, const float* scale, const float* base, const void* norm_w,
                float* post_out, float* comb_out, void* y, int64_t T, int64_t H, float rms_eps, float pre_eps,
                float sinkhorn_eps, float post_mult, int repeat, float norm_eps, cudaStream_t stream);
+
+// KDA prefill (csrc/kda.cu).
+struct KdaArgs {
+  const __nv_bfloat16* x = nullptr;    // in_proj rows [T, ldx]: q | k | v in columns [0, 3P)
+  int64_t ldx = 0;
+  const __nv_bfloat16* g = nullptr;    // raw gate rows [T, ldg], H * 128 columns
+  int64_t ldg = 0;
+  const __nv_bfloat16* beta = nullptr; // raw beta rows [T, ldb], H columns
+  int64_t ldb = 0;
+  const __nv_bfloat16* conv_w = nullptr;   // [3P][4]
+  const float* a_log = nullptr;        // [H]
+  const float* dt_bias = nullptr;      // [H * 128]
+  float lower_bound = -5.0f;
+  float scale = 0.0f;
+  __nv_bfloat16* conv_state = nullptr; // blocks of [3][3P]
+  int64_t cs_stride = 0;               // elements between blocks
+  float* rec_state = nullptr;          // blocks of [H][128 value][128 key]
+  int64_t rs_stride = 0;
+  const int32_t* seqs = nullptr;       // [R][4] = {first row, end row, state block, has initial state}
+  int32_t R = 0;
+  int32_t H = 0;
+  int32_t P = 0;                       // H * 128
+  __nv_bfloat16* out = nullptr;        // [T, ldo], H * 128 columns
+  int64_t ldo = 0;
+  int32_t* status = nullptr;           // device status word (bounded copy waits)
+};
+int launch_kda_prefill(const KdaArgs& a, cudaStream_t stream);
+int launch_kda_conv(const KdaArgs& a, int64_t T, void* q, void* k, void* v, cudaStream_t stream);
 
 int device_sm_count();
 

@@ -17,7 +17,7 @@ LIB_PATH = PKG / "libssengine_b200.so"
 EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_gemm", "ssb_moe_route",
            "ssb_moe_workspace_bytes", "ssb_moe_workspace_offsets", "ssb_moe_forward", "ssb_moe_forward_profiled",
            "ssb_moe_route_permute_noalloc", "ssb_topk_canonical", "ssb_stage_metadata", "ssb_embed_rows",
-           "ssb_rmsnorm", "ssb_argmax_rows", "ssb_mhc")
+           "ssb_rmsnorm", "ssb_argmax_rows", "ssb_mhc", "ssb_kda_prefill", "ssb_kda_conv")
 
 EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
 
@@ -43,6 +43,14 @@ class MoeLayerC(ctypes.Structure):
                 ("router_alpha", ctypes.c_float), ("w1_codes", ctypes.c_void_p), ("w1_sf", ctypes.c_void_p),
                 ("w1_alpha", ctypes.c_void_p), ("w2_codes", ctypes.c_void_p), ("w2_sf", ctypes.c_void_p),
                 ("w2_alpha", ctypes.c_void_p), ("add_input", ctypes.c_int32)]
+
+
+class KdaLayerC(ctypes.Structure):
+    """Mirror of `ssb_kda_layer`."""
+    _fields_ = [("heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("conv_weight", ctypes.c_void_p),
+                ("a_log", ctypes.c_void_p), ("dt_bias", ctypes.c_void_p), ("lower_bound", ctypes.c_float),
+                ("scale", ctypes.c_float), ("conv_state", ctypes.c_void_p), ("conv_state_stride", ctypes.c_int64),
+                ("rec_state", ctypes.c_void_p), ("rec_state_stride", ctypes.c_int64)]
 
 
 class MhcParamsC(ctypes.Structure):
@@ -75,6 +83,9 @@ _SIGS = {
     "ssb_rmsnorm": ([_P, _I64, _P, _I64, _P, _F, _P, _P], ctypes.c_int),
     "ssb_argmax_rows": ([_P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
     "ssb_mhc": ([ctypes.POINTER(MhcParamsC), _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P], ctypes.c_int),
+    "ssb_kda_prefill": ([ctypes.POINTER(KdaLayerC), _P, _I64, _P, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _P],
+                        ctypes.c_int),
+    "ssb_kda_conv": ([ctypes.POINTER(KdaLayerC), _P, _I64, _I64, _P, _I64, _P, _P, _P, _P], ctypes.c_int),
 }
 
 MOE_KERNELS = 9       # kernels ssb_moe_forward launches (+ a memset when F % 256 != 0)
