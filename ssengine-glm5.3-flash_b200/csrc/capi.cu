@@ -201,6 +201,7 @@ int ssb_kda_prefill(const ssb_kda_layer* layer, const void* x, int64_t ldx, cons
   a.out = static_cast<__nv_bfloat16*>(out);
   a.ldo = ldo;
   a.status = status;
+  a.T = T;
   if (ldg < a.P || ldb < a.H) return kErrArgs;
   return ssb::launch_kda_prefill(a, static_cast<cudaStream_t>(stream));
 }

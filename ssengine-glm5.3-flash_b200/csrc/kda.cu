@@ -129,21 +129,24 @@ SSB_DEVICE uint4 conv_row(const KdaArgs& a, int64_t t, int s, int e, int blk, in
 
 struct KdaSmem {
   static constexpr int QR = 0;             // raw conv q [64][128] bf16       | A_kk fp32 [64][64]
-  static constexpr int KR = 16384;         // raw conv k                      | A_qk bf16 [64][64], T bf16 [64][64]
+  static constexpr int KR = 16384;         // raw conv k                      | A_qk bf16 [64][64], T_II bf16 [64][64]
   static constexpr int TB = KR + 8192;
   static constexpr int QH = 32768;         // q exp(G - G_r)                  | W bf16 [64][128]
-  static constexpr int KH = 49152;         // k exp(G - G_r)                  | T fp32 [64][64]
-  static constexpr int KRB = 65536;        // k exp(G_r - G)                  | U bf16 [64][BV], solve scratch
-  static constexpr int PS = KRB + 8192;
-  static constexpr int KG = 81920;         // k exp(G)
+  static constexpr int KH = 49152;         // k exp(G - G_r)                  | -L bf16 [64][64], R bf16 [16][192]
+  static constexpr int LN = KH;
+  static constexpr int RB = KH + 8192;
+  static constexpr int KRB = 65536;        // k exp(G_r - G)                  | U bf16 [64][BV], u bf16 [64][BV]
+  static constexpr int UC = KRB + 8192;
+  static constexpr int KG = 81920;         // beta k exp(G)
   static constexpr int QT = 98304;         // scale q exp(G)
   static constexpr int KT = 114688;        // k exp(G_63 - G)
-  static constexpr int VR = 131072;        // raw conv v [64][BV]
+  static constexpr int VR = 131072;        // conv v [64][BV], then beta v
 };
 
 template <int BV>
 struct KdaLayout {
-  static constexpr int XW = 256 + BV;                       // raw x row in smem: q 128 | k 128 | v BV
+  static constexpr int NG = 32 + BV / 8;                    // 16-byte channel groups: q 16, k 16, v BV/8
+  static constexpr int XW = 8 * NG;                         // halo row: q 128 | k 128 | v BV
   static constexpr int S0 = KdaSmem::VR + kC * BV * 2;      // state bf16 [128][BV]
   static constexpr int BETA = S0 + kD * BV * 2;             // fp32 [64]
   static constexpr int RQ = BETA + 256;                     // fp32 [64]
@@ -152,12 +155,17 @@ struct KdaLayout {
   static constexpr int GB = GC + 512;                       // G at block starts [4][128]
   static constexpr int DD = GB + 2048;                      // exp(G_rI - G_rJ) [6][128]
   static constexpr int XCH = DD + 3072;                     // [2][128]
-  static constexpr int XT = XCH + 1024;                     // raw x rows of the chunk [64][XW] bf16 (bulk copies)
-  static constexpr int HX = XT + kC * XW * 2;               // the 3 x rows before the chunk [3][XW]
-  static constexpr int GT = HX + ((3 * XW * 2 + 127) / 128) * 128;   // raw gate rows [64][128] bf16
-  static constexpr int MBAR = GT + kC * kD * 2;             // mbarrier (8 B) + abort flag
+  static constexpr int XT = XCH + 1024;                     // raw rows: NG/8 x-tiles then 2 gate tiles, [64][64] bf16 each
+  static constexpr int NXT = NG / 8;
+  static constexpr int GT = XT + NXT * 8192;
+  static constexpr int HX = GT + 2 * 8192;                  // the 3 x rows before the chunk [3][XW]
+  static constexpr int WS = HX + ((3 * XW * 2 + 127) / 128) * 128;   // conv weights [NG][32] bf16
+  static constexpr int MBAR = WS + NG * 64;                 // mbarrier (8 B) + abort flag
   static constexpr int BYTES = MBAR + 16;
   static constexpr int NP = KdaSmem::KG;                    // per-row, per-group sums of squares [64][32] (aliases KG)
+  static constexpr uint32_t TX = (NXT + 2) * 8192;          // bytes landing per chunk
+  static_assert(XT % 128 == 0 && GT % 128 == 0, "TMA destinations");
+  static_assert(BYTES <= 232448, "shared memory");
 };
 
 SSB_DEVICE int dpair(int I, int J) { return I == 1 ? 0 : (I == 2 ? 1 + J : 3 + J); }   // (1,0)(2,0)(2,1)(3,0..2)
@@ -167,6 +175,13 @@ SSB_DEVICE float sigmoid_fast(float z) {
   return __fdividef(1.0f, 1.0f + ez);
 }
 
+SSB_DEVICE int sw192(int r, int c) { return r * 192 + ((((c >> 3) ^ (r & 7))) << 3) + (c & 7); }
+
+SSB_DEVICE void ldsm_x2_t(const void* p, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r0), "=r"(r1) : "r"(smem_u32(p)));
+}
+
 // x column (within the in_proj row) of channel group `grp` of this CTA: q 0..15, k 16..31, v 32..
 template <int BV>
 SSB_DEVICE int64_t group_col(int grp, int P, int h, int vb) {
@@ -174,28 +189,32 @@ SSB_DEVICE int64_t group_col(int grp, int P, int h, int vb) {
                   : (grp < 32 ? (int64_t)P + h * kD + (grp - 16) * 8 : 2 * (int64_t)P + h * kD + vb * BV + (grp - 32) * 8);
 }
 
-// Bulk copies of one chunk's raw rows (q, k, v segments of x and the gate row) into XT / GT, completing on `bar`;
-// thread tid copies segment (tid & 3) of row (tid >> 2). Thread 0 must have armed the barrier with the byte count.
+// One chunk's raw rows: the x tiles (q 0-63, q 64-127, k 0-63, k 64-127, v ...) and the 2 gate tiles, 64 rows from
+// t0 (rows past the tensor read as zeros), all completing on `bar`. Called by one thread.
 template <int BV>
-SSB_DEVICE void issue_chunk_copies(const KdaArgs& a, uint8_t* smem, uint32_t bar, int t0, int rows, int h, int vb) {
+SSB_DEVICE void issue_chunk_loads(const CUtensorMap* mx, const CUtensorMap* mg, uint8_t* smem, uint32_t bar, int t0,
+                                  int P, int h, int vb) {
   using Ly = KdaLayout<BV>;
-  const int i = threadIdx.x >> 2, seg = threadIdx.x & 3;
-  if (i >= rows) return;
-  const int64_t t = t0 + i;
-  const uint32_t xrow = smem_u32(smem + Ly::XT) + i * Ly::XW * 2;
-  if (seg == 0) bulk_load(xrow, a.x + t * a.ldx + (int64_t)h * kD, kD * 2, bar);
-  if (seg == 1) bulk_load(xrow + kD * 2, a.x + t * a.ldx + a.P + (int64_t)h * kD, kD * 2, bar);
-  if (seg == 2) bulk_load(xrow + 2 * kD * 2, a.x + t * a.ldx + 2 * (int64_t)a.P + (int64_t)h * kD + vb * BV, BV * 2, bar);
-  if (seg == 3) bulk_load(smem_u32(smem + Ly::GT) + i * kD * 2, a.g + t * a.ldg + (int64_t)h * kD, kD * 2, bar);
+  mbar_arrive_expect_tx(bar, Ly::TX);
+  const uint32_t xt = smem_u32(smem + Ly::XT), gt = smem_u32(smem + Ly::GT);
+#pragma unroll
+  for (int j = 0; j < Ly::NXT; ++j) {
+    const int col = j < 2 ? h * kD + 64 * j : (j < 4 ? P + h * kD + 64 * (j - 2) : 2 * P + h * kD + vb * BV + 64 * (j - 4));
+    tma_load_2d(xt + j * 8192, mx, col, t0, bar);
+  }
+  tma_load_2d(gt, mg, h * kD, t0, bar);
+  tma_load_2d(gt + 8192, mg, h * kD + 64, t0, bar);
 }
 
 template <int BV>
-__global__ void __launch_bounds__(kKdaThreads, 1) kda_prefill_kernel(KdaArgs a) {
+__global__ void __launch_bounds__(kKdaThreads, 1)
+    kda_prefill_kernel(const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap mg, KdaArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   using Ly = KdaLayout<BV>;
   constexpr int NVB = kD / BV;
-  constexpr int NG = 32 + BV / 8;           // 16-byte channel groups: q 16, k 16, v BV/8
-  constexpr uint32_t kRowBytes = (3 * kD + BV) * 2;
+  constexpr int NG = Ly::NG;
+  constexpr int kSeg = 6;                    // conv row segments: NG x 6 items <= 256 threads
+  static_assert(NG * kSeg <= kKdaThreads, "conv items");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;
   const int vb = blockIdx.x % NVB;
@@ -212,10 +231,11 @@ __global__ void __launch_bounds__(kKdaThreads, 1) kda_prefill_kernel(KdaArgs a) 
   __nv_bfloat16* QH = reinterpret_cast<__nv_bfloat16*>(smem + KdaSmem::QH);
   __nv_bfloat16* Ws = QH;
   __nv_bfloat16* KH = reinterpret_cast<__nv_bfloat16*>(smem + KdaSmem::KH);
-  float* TF = reinterpret_cast<float*>(smem + KdaSmem::KH);
+  __nv_bfloat16* LN = reinterpret_cast<__nv_bfloat16*>(smem + KdaSmem::LN);
+  __nv_bfloat16* RB = reinterpret_cast<__nv_bfloat16*>(smem + KdaSmem::RB);
   __nv_bfloat16* KRB = reinterpret_cast<__nv_bfloat16*>(smem + KdaSmem::KRB);
   __nv_bfloat16* Us = KRB;
-  float* PSs = reinterpret_cast<float*>(smem + KdaSmem::PS);
+  __nv_bfloat16* UC = reinterpret_cast<__nv_bfloat16*>(smem + KdaSmem::UC);
   __nv_bfloat16* KG = reinterpret_cast<__nv_bfloat16*>(smem + KdaSmem::KG);
   __nv_bfloat16* QT = reinterpret_cast<__nv_bfloat16*>(smem + KdaSmem::QT);
   __nv_bfloat16* KT = reinterpret_cast<__nv_bfloat16*>(smem + KdaSmem::KT);
@@ -229,8 +249,9 @@ __global__ void __launch_bounds__(kKdaThreads, 1) kda_prefill_kernel(KdaArgs a) 
   float* DD = reinterpret_cast<float*>(smem + Ly::DD);
   float* XCH = reinterpret_cast<float*>(smem + Ly::XCH);
   const __nv_bfloat16* XT = reinterpret_cast<const __nv_bfloat16*>(smem + Ly::XT);
-  __nv_bfloat16* HX = reinterpret_cast<__nv_bfloat16*>(smem + Ly::HX);
   const __nv_bfloat16* GT = reinterpret_cast<const __nv_bfloat16*>(smem + Ly::GT);
+  __nv_bfloat16* HX = reinterpret_cast<__nv_bfloat16*>(smem + Ly::HX);
+  __nv_bfloat16* WSm = reinterpret_cast<__nv_bfloat16*>(smem + Ly::WS);
   float* NP = reinterpret_cast<float*>(smem + Ly::NP);
   const uint32_t bar = smem_u32(smem + Ly::MBAR);
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + Ly::MBAR + 8);
@@ -248,7 +269,7 @@ __global__ void __launch_bounds__(kKdaThreads, 1) kda_prefill_kernel(KdaArgs a) 
     *reinterpret_cast<uint32_t*>(S0 + swv<BV>(16 * warp + g8, 8 * nt + 2 * t4)) = pack_bf16(st[nt][0], st[nt][1]);
     *reinterpret_cast<uint32_t*>(S0 + swv<BV>(16 * warp + g8 + 8, 8 * nt + 2 * t4)) = pack_bf16(st[nt][2], st[nt][3]);
   }
-  // the 3 rows before the sequence: its conv state, or zeros
+  // the 3 rows before the sequence (its conv state, or zeros) and this CTA's conv weights
   if (tid < 3 * NG) {
     const int j = tid / NG, grp = tid % NG;
     const int64_t col = group_col<BV>(grp, P, h, vb);
@@ -256,18 +277,21 @@ __global__ void __launch_bounds__(kKdaThreads, 1) kda_prefill_kernel(KdaArgs a) 
     if (init) v = *reinterpret_cast<const uint4*>(a.conv_state + (int64_t)blk * a.cs_stride + (int64_t)j * 3 * P + col);
     *reinterpret_cast<uint4*>(HX + j * Ly::XW + grp * 8) = v;
   }
+  if (tid < 4 * NG) {
+    const int grp = tid >> 2, part = tid & 3;
+    reinterpret_cast<uint4*>(WSm + grp * 32)[part] =
+        __ldg(reinterpret_cast<const uint4*>(a.conv_w + group_col<BV>(grp, P, h, vb) * 4) + part);
+  }
+  // raw beta of this thread's row of the coming chunk (threads 128..191)
+  float braw = 0.0f;
+  if (tid >= 128 && tid < 192 && s + (tid - 128) < e) braw = __bfloat162float(a.beta[(int64_t)(s + tid - 128) * a.ldb + h]);
   if (tid == 0) {
     mbar_init(bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
+    if (e > s) issue_chunk_loads<BV>(&mx, &mg, smem, bar, s, P, h, vb);
   }
-  // raw beta of this thread's row of the next chunk (threads 192..255)
-  float braw = 0.0f;
-  if (tid >= 192 && s + (tid - 192) < e) braw = __bfloat162float(a.beta[(int64_t)(s + tid - 192) * a.ldb + h]);
   __syncthreads();
-  if (tid == 0 && e > s) mbar_arrive_expect_tx(bar, (uint32_t)min(kC, e - s) * kRowBytes);
-  __syncthreads();
-  if (e > s) issue_chunk_copies<BV>(a, smem, bar, s, min(kC, e - s), h, vb);
 
   // per-thread constants of the gate phase: channel c, row half hf
   const int gc_c = tid & 127, hf = tid >> 7;
@@ -278,29 +302,35 @@ __global__ void __launch_bounds__(kKdaThreads, 1) kda_prefill_kernel(KdaArgs a) 
 
   for (int t0 = s; t0 < e; t0 += kC, phase ^= 1) {
     const int n = min(kC, e - t0);
-    const int n_next = min(kC, e - t0 - kC);          // <= 0: last chunk
+    const bool more = e - t0 > kC;                    // a chunk follows
     mbar_wait(bar, phase, abort_flag, a.status);
-    // ---- P1: conv of q, k (all 128 channels) and v (this CTA's BV channels) from smem; beta ---------------------
-    if (tid < NG * 4) {
-      const int grp = tid % NG, quarter = tid / NG;
+    // ---- P1: conv of q, k (all 128 channels) and v (this CTA's BV channels) from the landed tiles ---------------
+    if (tid < NG * kSeg) {
+      const int grp = tid % NG, seg = tid / NG;
+      const int i0 = (kC * seg) / kSeg, i1 = (kC * (seg + 1)) / kSeg;
       float wf[32];
-      load_w8(a.conv_w, group_col<BV>(grp, P, h, vb), wf);
-      const int i0 = 16 * quarter;
+#pragma unroll
+      for (int part = 0; part < 4; ++part) {
+        float f[8];
+        bf16x8_to_f32(reinterpret_cast<const uint4*>(WSm + grp * 32)[part], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wf[8 * part + j] = f[j];
+      }
+      const __nv_bfloat16* tile = XT + (grp >> 3) * 4096 + (grp & 7) * 8;
       auto xrow = [&](int i) -> uint4 {
-        return *reinterpret_cast<const uint4*>(i >= 0 ? XT + i * Ly::XW + grp * 8 : HX + (i + 3) * Ly::XW + grp * 8);
+        return *reinterpret_cast<const uint4*>(i >= 0 ? tile + i * 64 : HX + (i + 3) * Ly::XW + grp * 8);
       };
+      __nv_bfloat16* dst;
+      int dcol;
+      if (grp < 16) { dst = QRs; dcol = grp * 8; }
+      else if (grp < 32) { dst = KRs; dcol = (grp - 16) * 8; }
+      else { dst = VR; dcol = (grp - 32) * 8; }
       uint4 x0 = xrow(i0 - 3), x1 = xrow(i0 - 2), x2 = xrow(i0 - 1);
 #pragma unroll 4
-      for (int i = i0; i < i0 + 16; ++i) {
+      for (int i = i0; i < i1; ++i) {
         const uint4 x3 = xrow(i);
         const uint4 y = (i < n) ? conv8(x0, x1, x2, x3, wf) : make_uint4(0, 0, 0, 0);
-        if (grp < 16) {
-          *reinterpret_cast<uint4*>(QRs + sw128(i, grp * 8)) = y;
-        } else if (grp < 32) {
-          *reinterpret_cast<uint4*>(KRs + sw128(i, (grp - 16) * 8)) = y;
-        } else {
-          *reinterpret_cast<uint4*>(VR + swv<BV>(i, (grp - 32) * 8)) = y;
-        }
+        *reinterpret_cast<uint4*>(dst + (grp < 32 ? sw128(i, dcol) : swv<BV>(i, dcol))) = y;
         if (grp < 32) {
           float f[8];
           bf16x8_to_f32(y, f);
@@ -311,44 +341,43 @@ __global__ void __launch_bounds__(kKdaThreads, 1) kda_prefill_kernel(KdaArgs a) 
         }
         x0 = x1; x1 = x2; x2 = x3;
       }
-    } else if (tid >= 192) {
-      BETA[tid - 192] = (tid - 192 < n) ? sigmoid_fast(braw) : 0.0f;
     }
     __syncthreads();
     if (*abort_flag) break;
 
-    // ---- P2: L2 norms of the q / k rows; gate cumsum per channel (two 32-row halves); next chunk's copies -------
+    // ---- P2: L2 norms of the q / k rows, beta; gate cumsum per channel (two 32-row halves); next chunk's loads ---
     if (tid < 128) {
       const float* np = NP + (tid & 63) * 32 + (tid >> 6) * 16;
       float ss = 0.0f;
 #pragma unroll
       for (int c = 0; c < 16; ++c) ss += np[c];
       (tid < 64 ? RQ : RK)[tid & 63] = rsqrtf(ss + 1e-6f);
+    } else if (tid < 192) {
+      BETA[tid - 128] = (tid - 128 < n) ? sigmoid_fast(braw) : 0.0f;
+      if (more && tid - 128 < min(kC, e - t0 - kC))
+        braw = __bfloat162float(a.beta[(int64_t)(t0 + kC + tid - 128) * a.ldb + h]);
     }
     float G[32];
     {
+      const __nv_bfloat16* gcol = GT + (gc_c >> 6) * 4096 + (gc_c & 63);
       float run = 0.0f;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const int i = 32 * hf + j;
         float gk = 0.0f;
-        if (i < n) gk = lb * sigmoid_fast(eA * (__bfloat162float(GT[i * kD + gc_c]) + dtb));
+        if (i < n) gk = lb * sigmoid_fast(eA * (__bfloat162float(gcol[i * 64]) + dtb));
         run += gk;
         G[j] = run;
       }
       if (hf == 0) XCH[gc_c] = run;
     }
-    if (n_next > 0) {
-      if (tid < 3 * NG) {                                   // the next chunk's halo: this chunk's last 3 rows
-        const int j = tid / NG, grp = tid % NG;
-        *reinterpret_cast<uint4*>(HX + j * Ly::XW + grp * 8) =
-            *reinterpret_cast<const uint4*>(XT + (kC - 3 + j) * Ly::XW + grp * 8);
-      }
-      if (tid >= 192 && tid - 192 < n_next) braw = __bfloat162float(a.beta[(int64_t)(t0 + kC + tid - 192) * a.ldb + h]);
-      if (tid == 0) mbar_arrive_expect_tx(bar, (uint32_t)n_next * kRowBytes);
+    if (more && tid < 3 * NG) {                         // the next chunk's halo: this chunk's last 3 rows
+      const int j = tid / NG, grp = tid % NG;
+      *reinterpret_cast<uint4*>(HX + j * Ly::XW + grp * 8) =
+          *reinterpret_cast<const uint4*>(XT + (grp >> 3) * 4096 + (kC - 3 + j) * 64 + (grp & 7) * 8);
     }
     __syncthreads();
-    if (n_next > 0) issue_chunk_copies<BV>(a, smem, bar, t0 + kC, n_next, h, vb);
+    if (more && tid == 0) issue_chunk_loads<BV>(&mx, &mg, smem, bar, t0 + kC, P, h, vb);
     if (hf == 1) {
       const float base = XCH[gc_c];
 #pragma unroll
@@ -383,12 +412,17 @@ __global__ void __launch_bounds__(kKdaThreads, 1) kda_prefill_kernel(KdaArgs a) 
         QH[o] = __float2bfloat16_rn(qn * eI);
         KH[o] = __float2bfloat16_rn(kn * eI);
         KRB[o] = __float2bfloat16_rn(kn * eR);
-        KG[o] = __float2bfloat16_rn(kn * eG);
+        KG[o] = __float2bfloat16_rn(BETA[i] * kn * eG);
         QT[o] = __float2bfloat16_rn(scale * qn * eG);
         KT[o] = __float2bfloat16_rn(kn * eC);
+        if (gc_c < BV) {
+          const int ov = swv<BV>(i, gc_c);
+          VR[ov] = __float2bfloat16_rn(BETA[i] * __bfloat162float(VR[ov]));
+        }
       }
     }
     __syncthreads();
+
     // ---- P3: the 16x16 blocks of A_kk (strict lower, times beta_i) and A_qk (lower, times scale) -----------------
     {
 #pragma unroll 1
@@ -436,7 +470,7 @@ __global__ void __launch_bounds__(kKdaThreads, 1) kda_prefill_kernel(KdaArgs a) 
     }
     __syncthreads();
 
-    // ---- P4: T = (I + L)^-1 by 16x16 blocks; then T diag(beta) in bf16 -------------------------------------------
+    // ---- P4: diagonal blocks T_II = (I + L_II)^-1 (fp32 forward substitution) -> bf16; -L off the diagonal -------
     if (warp < 4 && lane < 16) {
       const int I = warp, c = lane;
       float tcol[16];
@@ -448,76 +482,80 @@ __global__ void __launch_bounds__(kKdaThreads, 1) kda_prefill_kernel(KdaArgs a) 
         tcol[i] = acc;
       }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) TF[(16 * I + i) * 64 + 16 * I + c] = tcol[i];
-    }
-    __syncthreads();
-#pragma unroll 1
-    for (int d = 1; d < 4; ++d) {
-      const int nb = 4 - d;
-      for (int el = tid; el < nb * 256; el += kKdaThreads) {
-        const int J = el >> 8, I = J + d, ii = (el >> 4) & 15, jj = el & 15;
-        float acc = 0.0f;
-        for (int M = J; M < I; ++M) {
-#pragma unroll
-          for (int m = 0; m < 16; ++m) acc += AKK[(16 * I + ii) * 64 + 16 * M + m] * TF[(16 * M + m) * 64 + 16 * J + jj];
-        }
-        PSs[el] = acc;
-      }
-      __syncthreads();
-      for (int el = tid; el < nb * 256; el += kKdaThreads) {
-        const int J = el >> 8, I = J + d, ii = (el >> 4) & 15, jj = el & 15;
-        float acc = 0.0f;
-#pragma unroll
-        for (int m = 0; m < 16; ++m) acc += TF[(16 * I + ii) * 64 + 16 * I + m] * PSs[(J << 8) + m * 16 + jj];
-        TF[(16 * I + ii) * 64 + 16 * J + jj] = -acc;
-      }
-      __syncthreads();
+      for (int i = 0; i < 16; ++i) TBs[sw64(16 * I + i, 16 * I + c)] = __float2bfloat16_rn(tcol[i]);
     }
     for (int el = tid; el < 64 * 32; el += kKdaThreads) {
       const int i = el >> 5, j = (el & 31) * 2;
-      const float v0 = j <= i ? TF[i * 64 + j] * BETA[j] : 0.0f;
-      const float v1 = j + 1 <= i ? TF[i * 64 + j + 1] * BETA[j + 1] : 0.0f;
-      *reinterpret_cast<uint32_t*>(TBs + sw64(i, j)) = pack_bf16(v0, v1);
+      const bool off = (j >> 4) < (i >> 4);
+      *reinterpret_cast<uint32_t*>(LN + sw64(i, j)) =
+          off ? pack_bf16(-AKK[i * 64 + j], -AKK[i * 64 + j + 1]) : 0u;
     }
     __syncthreads();
 
-    // ---- P5: W = T' (k exp G) [64 x 128] to smem; u = T' v [16 x BV/2 per warp] in registers -------------------
+    // ---- P5: [W | u] = (I + L)^-1 [beta k exp G | beta v] by 16-row blocks: R_I = B_I - sum_J L_IJ X_J,
+    //      X_I = T_II R_I (X = W bf16 [64][128] and u bf16 [64][BV]); 24 (or 32) column tiles of 8 over the warps --
+    constexpr int NT = (kD + BV) / 8;                   // column tiles of [W | u]
+    constexpr int TPW = (NT + 7) / 8;                   // tiles per warp
+#pragma unroll 1
+    for (int I = 0; I < 4; ++I) {
+      if (I > 0) {
+#pragma unroll
+        for (int q = 0; q < TPW; ++q) {
+          const int nt = warp * TPW + q;
+          if (nt >= NT) break;
+          const bool wcol = nt < 16;
+          const int c = wcol ? 8 * nt : 8 * (nt - 16);
+          const __nv_bfloat16* B = wcol ? KG : VR;
+          float acc[4];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int row = 16 * I + g8 + 8 * hh;
+            const int o = wcol ? sw128(row, c + 2 * t4) : swv<BV>(row, c + 2 * t4);
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(B + o));
+            acc[2 * hh] = f.x;
+            acc[2 * hh + 1] = f.y;
+          }
+          for (int J = 0; J < I; ++J) {
+            uint32_t a0, a1, a2, a3, b0, b1;
+            ldsm_x4(LN + sw64(16 * I + (lane & 15), 16 * J + (lane >> 4) * 8), a0, a1, a2, a3);
+            const int krow = 16 * J + (lane & 15);
+            ldsm_x2_t(wcol ? Ws + sw128(krow, c) : UC + swv<BV>(krow, c), b0, b1);
+            mma16816(acc, a0, a1, a2, a3, b0, b1);
+          }
+          *reinterpret_cast<uint32_t*>(RB + sw192(g8, 8 * nt + 2 * t4)) = pack_bf16(acc[0], acc[1]);
+          *reinterpret_cast<uint32_t*>(RB + sw192(g8 + 8, 8 * nt + 2 * t4)) = pack_bf16(acc[2], acc[3]);
+        }
+        __syncthreads();
+      }
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(TBs + sw64(16 * I + (lane & 15), 16 * I + (lane >> 4) * 8), a0, a1, a2, a3);
+#pragma unroll
+      for (int q = 0; q < TPW; ++q) {
+        const int nt = warp * TPW + q;
+        if (nt >= NT) break;
+        const bool wcol = nt < 16;
+        const int c = wcol ? 8 * nt : 8 * (nt - 16);
+        uint32_t b0, b1;
+        if (I > 0) {
+          ldsm_x2_t(RB + sw192(lane & 15, 8 * nt), b0, b1);
+        } else {
+          ldsm_x2_t(wcol ? KG + sw128(lane & 15, c) : VR + swv<BV>(lane & 15, c), b0, b1);
+        }
+        float acc[4] = {};
+        mma16816(acc, a0, a1, a2, a3, b0, b1);
+        __nv_bfloat16* X = wcol ? Ws : UC;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int row = 16 * I + g8 + 8 * hh;
+          const int o = wcol ? sw128(row, c + 2 * t4) : swv<BV>(row, c + 2 * t4);
+          *reinterpret_cast<uint32_t*>(X + o) = pack_bf16(acc[2 * hh], acc[2 * hh + 1]);
+        }
+      }
+      __syncthreads();
+    }
+
     const int m = warp & 3, nh = warp >> 2;
     constexpr int UN = BV / 16;              // n-tiles of 8 per warp in the [64 x BV] outputs (half the columns)
-    float uacc[UN][4] = {};
-    {
-      float wacc[8][4] = {};
-#pragma unroll
-      for (int kb = 0; kb < 4; ++kb) {
-        if (kb > m) break;
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(TBs + sw64(16 * m + (lane & 15), 16 * kb + (lane >> 4) * 8), a0, a1, a2, a3);
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(KG + sw128(16 * kb + (lane & 7) + ((lane >> 3) & 1) * 8, 64 * nh + 16 * p + (lane >> 4) * 8), b0,
-                    b1, b2, b3);
-          mma16816(wacc[2 * p], a0, a1, a2, a3, b0, b1);
-          mma16816(wacc[2 * p + 1], a0, a1, a2, a3, b2, b3);
-        }
-#pragma unroll
-        for (int p = 0; p < UN / 2; ++p) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(VR + swv<BV>(16 * kb + (lane & 7) + ((lane >> 3) & 1) * 8, (BV / 2) * nh + 16 * p + (lane >> 4) * 8),
-                    b0, b1, b2, b3);
-          mma16816(uacc[2 * p], a0, a1, a2, a3, b0, b1);
-          mma16816(uacc[2 * p + 1], a0, a1, a2, a3, b2, b3);
-        }
-      }
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const int c = 64 * nh + 8 * nt + 2 * t4;
-        *reinterpret_cast<uint32_t*>(Ws + sw128(16 * m + g8, c)) = pack_bf16(wacc[nt][0], wacc[nt][1]);
-        *reinterpret_cast<uint32_t*>(Ws + sw128(16 * m + g8 + 8, c)) = pack_bf16(wacc[nt][2], wacc[nt][3]);
-      }
-    }
-    __syncthreads();
-
     // ---- P6: U = u - W S -> smem bf16 ----------------------------------------------------------------------------
     {
       float pacc[UN][4] = {};
@@ -537,10 +575,12 @@ __global__ void __launch_bounds__(kKdaThreads, 1) kda_prefill_kernel(KdaArgs a) 
 #pragma unroll
       for (int nt = 0; nt < UN; ++nt) {
         const int c = (BV / 2) * nh + 8 * nt + 2 * t4;
-        *reinterpret_cast<uint32_t*>(Us + swv<BV>(16 * m + g8, c)) =
-            pack_bf16(uacc[nt][0] - pacc[nt][0], uacc[nt][1] - pacc[nt][1]);
-        *reinterpret_cast<uint32_t*>(Us + swv<BV>(16 * m + g8 + 8, c)) =
-            pack_bf16(uacc[nt][2] - pacc[nt][2], uacc[nt][3] - pacc[nt][3]);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int o = swv<BV>(16 * m + g8 + 8 * hh, c);
+          const float2 u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(UC + o));
+          *reinterpret_cast<uint32_t*>(Us + o) = pack_bf16(u.x - pacc[nt][2 * hh], u.y - pacc[nt][2 * hh + 1]);
+        }
       }
     }
     __syncthreads();
@@ -669,11 +709,16 @@ __global__ void kda_conv_qkv_kernel(KdaArgs a, int64_t T, __nv_bfloat16* q, __nv
 
 template <int BV>
 int launch_scan(const KdaArgs& a, cudaStream_t stream) {
+  CUtensorMap mx, mg;
+  int rc = make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, a.T, 3 * (int64_t)a.P, a.ldx * 2, 64, kC);
+  if (rc != kOk) return rc;
+  rc = make_map_2d(&mg, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.g, a.T, a.P, a.ldg * 2, 64, kC);
+  if (rc != kOk) return rc;
   const int smem = KdaLayout<BV>::BYTES;
   if (cudaFuncSetAttribute(kda_prefill_kernel<BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return kErrCuda;
   const int64_t grid = (int64_t)a.R * a.H * (kD / BV);
-  kda_prefill_kernel<BV><<<(unsigned)grid, kKdaThreads, smem, stream>>>(a);
+  kda_prefill_kernel<BV><<<(unsigned)grid, kKdaThreads, smem, stream>>>(mx, mg, a);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
@@ -697,7 +742,7 @@ int launch_kda_prefill(const KdaArgs& a, cudaStream_t stream) {
       (reinterpret_cast<uintptr_t>(a.g) & 15) || (a.ldg % 8) ||
       a.rs_stride < (int64_t)a.H * kD * kD)
     return kErrArgs;
-  if (a.R == 0) return kOk;
+  if (a.R == 0 || a.T == 0) return a.R == 0 ? kOk : kErrArgs;
   rc = launch_scan<64>(a, stream);
   if (rc != kOk) return rc;
   const int C = 3 * a.P;

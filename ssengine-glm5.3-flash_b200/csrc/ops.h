@@ -105,8 +105,14 @@ struct KdaArgs {
   __nv_bfloat16* out = nullptr;        // [T, ldo], H * 128 columns
   int64_t ldo = 0;
   int32_t* status = nullptr;           // device status word (bounded copy waits)
+  int64_t T = 0;                       // rows of x, g, beta, out
 };
 int launch_kda_prefill(const KdaArgs& a, cudaStream_t stream);
+
+// 2D tensor map (no swizzle) over [rows, width] elements of `dtype` (a CUtensorMapDataType) with row pitch ld_bytes;
+// box = box_cols x box_rows (csrc/gemm_nvfp4.cu).
+int make_map_2d(CUtensorMap* m, int dtype, const void* base, int64_t rows, int64_t width, int64_t ld_bytes,
+                int box_cols, int box_rows);
 int launch_kda_conv(const KdaArgs& a, int64_t T, void* q, void* k, void* v, cudaStream_t stream);
 
 int device_sm_count();
