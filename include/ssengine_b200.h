@@ -210,6 +210,30 @@ int ssb_moe_forward(const ssb_moe_layer* layer, const void* x, int64_t T, void* 
 int ssb_moe_forward_profiled(const ssb_moe_layer* layer, const void* x, int64_t T, void* out, void* ws,
                              int64_t ws_bytes, int32_t* status, void* stream, void* const* events);
 
+/* ---- stage edge over NVLink (replaces the reference's CePipe, ssengine/runtime/transport.py:205-335) ----------------
+ * The receiver's ring and flag words are mapped into the sender's process by CUDA IPC; the sender's kernels store rows
+ * straight into the peer slot, then a release write of ready[slot] = n; the receiver's stream waits on it with a
+ * bounded kernel. Flags count microbatches from 1 (slot = (n - 1) % K). */
+
+/* handle64 (64 bytes) = cudaIpcGetMemHandle of the allocation holding dev_ptr, *offset = dev_ptr - its base (a pointer
+ * from a caching allocator may sit inside a larger block) (CePipe._export, transport.py:281-283). */
+int ssb_ipc_export(const void* dev_ptr, uint8_t* handle64, int64_t* offset);
+/* Map a peer's exported allocation (lazy peer access) into this process; *dev_ptr = its base (add the exporter's
+ * offset) (CePipe._open, transport.py:285-290). */
+int ssb_ipc_open(const uint8_t* handle64, void** dev_ptr);
+int ssb_ipc_close(void* dev_ptr);
+/* On `stream`: wait until (int32)(*flag - value) >= 0 (flag: local or peer device memory, read with acquire at system
+ * scope). Replaces cuStreamWaitValue32 GEQ (CePipe._wait, transport.py:292-294), with a limit: after timeout_ns the
+ * kernel writes 4 to status (device int32, may be NULL) and returns, so the stream and the context stay usable. */
+int ssb_flag_wait(const uint32_t* flag, uint32_t value, int64_t timeout_ns, int32_t* status, void* stream);
+/* On `stream`: *flag = value after everything the stream did before is visible system-wide (release store).
+ * Replaces cuStreamWriteValue32 (CePipe._write, transport.py:296-298). */
+int ssb_flag_write(uint32_t* flag, uint32_t value, void* stream);
+/* On `stream`: copy bytes (% 16 == 0, both pointers 16-byte aligned) by SM stores; dst may be a peer mapping. Replaces
+ * the copy-engine cudaMemcpyAsync of CePipe.send (transport.py:326-327) where the producing kernel cannot write the
+ * peer slot itself. */
+int ssb_p2p_copy(void* dst, const void* src, int64_t bytes, void* stream);
+
 /* MoE routing + permutation that allocates nothing: the same routing as ssb_moe_route and the same permutation as
  * ssb_moe_forward (expert-major, tokens ascending, shared expert last, experts at 128-aligned offsets), for callers
  * that cannot allocate device memory -- a stage whose KV pool already took the free HBM at start-up, code that must
