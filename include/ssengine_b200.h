@@ -147,6 +147,25 @@ int ssb_kda_prefill(const ssb_kda_layer* layer, const void* x, int64_t ldx, cons
 int ssb_kda_conv(const ssb_kda_layer* layer, const void* x, int64_t ldx, int64_t T, const int32_t* seqs, int64_t R,
                  void* q, void* k, void* v, void* stream);
 
+/* DSA lightning-indexer logits: logits fp32 [T, ldl], row t, column p = sum_h w[t, h] * relu(q[t, h, :] . k[p, :]) for
+ * the pools p of row t's request (q bf16 [T, 32, 128], w fp32 [T, 32] 16-byte aligned; pool keys bf16 in pages of
+ * 32 pools: pool p of request r at row page_table[r * width + p / 32] * 32 + p % 32 of k_cache [pool_rows, 128]).
+ * groups int32 [G][4] device = {request, first query row, rows (<= 8, one request), pool tiles of 128 to compute};
+ * columns of a computed tile past a row's visible pools ((pos + 1) / 4) hold values of later pools: the top-k's key
+ * range [0, (pos + 1) / 4) excludes them. status (device int32, may be NULL) receives 4 if a bounded wait expired.
+ * Replaces the fork's DeepGEMM `fp8_mqa_logits` call of the kpool indexer (ssengine/kernels.py config 19;
+ * split `split_indexer_prefill_chunks`, ssengine/model/pp_patch.py:587-634). */
+int ssb_indexer_logits(const void* q, const float* w, int64_t T, const void* k_cache, int64_t pool_rows,
+                       const int32_t* page_table, int64_t width, const int32_t* groups, int64_t G, float* logits,
+                       int64_t ldl, int32_t* status, void* stream);
+
+/* Selected pools -> token indices: out int32 [rows, ldo >= 4k + 3]: column c < 4k = pool_ids[row, c / 4] * 4 + c % 4
+ * (-1 where the pool id is -1), then the tokens of the row's incomplete last pool (seq_len = positions[row] + 1:
+ * 4 * (seq_len / 4) .. seq_len - 1, -1 past them). Replaces `kpool_fast.expand_into` (ssengine/model/kpool_fast.py:
+ * 48-59, the fork's `expand_pools_and_append_tail`). */
+int ssb_indexer_expand(const int32_t* pool_ids, int64_t ldp, int32_t k, const int64_t* positions, int64_t rows,
+                       int32_t* out, int64_t ldo, void* stream);
+
 /* One NVFP4 MoE layer's device parameters (all pointers device memory, owned by the caller).
  * Experts 0..E-1 are routed, expert E is the shared expert (every token, weight 1). */
 typedef struct ssb_moe_layer {

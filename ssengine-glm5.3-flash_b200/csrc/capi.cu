@@ -213,6 +213,28 @@ int ssb_kda_conv(const ssb_kda_layer* layer, const void* x, int64_t ldx, int64_t
   return ssb::launch_kda_conv(a, T, q, k, v, static_cast<cudaStream_t>(stream));
 }
 
+int ssb_indexer_logits(const void* q, const float* w, int64_t T, const void* k_cache, int64_t pool_rows,
+                       const int32_t* page_table, int64_t width, const int32_t* groups, int64_t G, float* logits,
+                       int64_t ldl, int32_t* status, void* stream) {
+  if (width <= 0 || width > (1 << 24) || G < 0 || G > (1 << 28)) return kErrArgs;
+  ssb::IdxArgs a;
+  a.w = w;
+  a.T = T;
+  a.table = page_table;
+  a.width = static_cast<int32_t>(width);
+  a.groups = groups;
+  a.G = static_cast<int32_t>(G);
+  a.logits = logits;
+  a.ldl = ldl;
+  a.status = status;
+  return ssb::launch_indexer_logits(q, k_cache, pool_rows, a, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_indexer_expand(const int32_t* pool_ids, int64_t ldp, int32_t k, const int64_t* positions, int64_t rows,
+                       int32_t* out, int64_t ldo, void* stream) {
+  return ssb::launch_indexer_expand(pool_ids, ldp, k, positions, out, ldo, rows, static_cast<cudaStream_t>(stream));
+}
+
 int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T) {
   MoeDims d;
   if (!dims_of(layer, T, d)) return -1;

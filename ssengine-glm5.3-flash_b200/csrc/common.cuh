@@ -129,6 +129,15 @@ SSB_DEVICE void tc_mma_nvf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uin
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");
 }
+// D[tmem] (+)= A[smem] x B[smem], bf16 operands (kind::f16), fp32 accumulate.
+SSB_DEVICE void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 SSB_DEVICE void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
@@ -143,6 +152,13 @@ SSB_DEVICE void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 SSB_DEVICE void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Instruction descriptor of kind::f16 with bf16 A and B (format 1 in [7,10) and [10,13)), fp32 D (1 in [4,6)),
+// K-major both, N >> 3 in [17,23), M >> 4 in [24,29).
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
 
 // Shared-memory matrix descriptor (sm_100 format): start >> 4 in [0,14), LBO >> 4 in [16,30), SBO >> 4 in [32,46),
 // version 1 in [46,48), layout type in [61,64) (0 = no swizzle, 2 = 128-byte swizzle).

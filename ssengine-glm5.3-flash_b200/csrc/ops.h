@@ -115,6 +115,26 @@ int make_map_2d(CUtensorMap* m, int dtype, const void* base, int64_t rows, int64
                 int box_cols, int box_rows);
 int launch_kda_conv(const KdaArgs& a, int64_t T, void* q, void* k, void* v, cudaStream_t stream);
 
+// DSA indexer (csrc/indexer.cu).
+struct IdxArgs {
+  const float* w = nullptr;            // [T, 32] head weights
+  int64_t T = 0;                       // query rows
+  const int32_t* table = nullptr;      // [R, width] pool pages (= KV pages) of each request
+  int32_t width = 0;
+  const int32_t* groups = nullptr;     // [G][4] = {request, first query row, query rows (<= 8), pool tiles of 128}
+  int32_t G = 0;
+  float* logits = nullptr;             // [T, ldl]
+  int64_t ldl = 0;
+  int32_t* status = nullptr;
+};
+int launch_indexer_logits(const void* q, const void* k_cache, int64_t pool_rows, const IdxArgs& a,
+                          cudaStream_t stream);
+int launch_indexer_expand(const int32_t* pool_ids, int64_t ldp, int32_t k, const int64_t* positions, int32_t* out,
+                          int64_t ldo, int64_t rows, cudaStream_t stream);
+// bf16 map over [rows, width] elements (row pitch ld_bytes), box 64 x box_rows, 128-byte swizzle (csrc/gemm_nvfp4.cu).
+int make_map_2d_swizzled(CUtensorMap* m, const void* base, int64_t rows, int64_t width, int64_t ld_bytes,
+                         int box_rows);
+
 int device_sm_count();
 
 }  // namespace ssb
