@@ -166,6 +166,21 @@ int ssb_indexer_logits(const void* q, const float* w, int64_t T, const void* k_c
 int ssb_indexer_expand(const int32_t* pool_ids, int64_t ldp, int32_t k, const int64_t* positions, int64_t rows,
                        int32_t* out, int64_t ldo, void* stream);
 
+/* Sparse MLA prefill of one DSA layer (absorbed latent attention): out bf16 [T, 64, 512], row t, head h = softmax over
+ * the row's selected tokens of scale * q[t, h, :] . kv[s, :], times kv[s, 0:512]; q bf16 [T, 64, 576] (latent 512 +
+ * rope 64); kv_cache bf16 [slots, 576]; indices int32 [T, ld_idx], the first n_idx columns used (token positions of
+ * the row's request, -1 = none: the indexer's expanded selection); the request of row t is found in qsl int32 [R + 1]
+ * (first row of each request, ascending, qsl[0] = 0); slot of position p = page_table[r * width + p / 128] * 128 +
+ * p % 128. A row with no selected token gets zeros. Replaces the TRTLLM sparse MLA (ssengine/kernels.py config 25,
+ * split at 32,768 rows ssengine/model/pp_patch.py:643-672). */
+int ssb_sparse_mla(const void* q, int64_t T, const void* kv_cache, const int32_t* indices, int64_t ld_idx,
+                   int32_t n_idx, const int32_t* qsl, int32_t R, const int32_t* page_table, int64_t width, float scale,
+                   void* out, void* stream);
+
+/* MLA cache append: row t of src bf16 [T, 576] (row pitch lds elements, % 8 == 0) into kv_cache row slots[t] (int64,
+ * skipped when < 0). Replaces the fork's latent cache write (ssengine/kernels.py config 23). */
+int ssb_mla_cache_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, void* stream);
+
 /* One NVFP4 MoE layer's device parameters (all pointers device memory, owned by the caller).
  * Experts 0..E-1 are routed, expert E is the shared expert (every token, weight 1). */
 typedef struct ssb_moe_layer {

@@ -235,6 +235,30 @@ int ssb_indexer_expand(const int32_t* pool_ids, int64_t ldp, int32_t k, const in
   return ssb::launch_indexer_expand(pool_ids, ldp, k, positions, out, ldo, rows, static_cast<cudaStream_t>(stream));
 }
 
+int ssb_sparse_mla(const void* q, int64_t T, const void* kv_cache, const int32_t* indices, int64_t ld_idx,
+                   int32_t n_idx, const int32_t* qsl, int32_t R, const int32_t* page_table, int64_t width, float scale,
+                   void* out, void* stream) {
+  if (width <= 0 || width > (1 << 24)) return kErrArgs;
+  ssb::MlaArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.kv = static_cast<const __nv_bfloat16*>(kv_cache);
+  a.indices = indices;
+  a.ld_idx = ld_idx;
+  a.n_idx = n_idx;
+  a.qsl = qsl;
+  a.R = R;
+  a.table = page_table;
+  a.width = static_cast<int32_t>(width);
+  a.scale = scale;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.T = T;
+  return ssb::launch_sparse_mla(a, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_mla_cache_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, void* stream) {
+  return ssb::launch_mla_append(src, lds, slots, T, cache, static_cast<cudaStream_t>(stream));
+}
+
 int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T) {
   MoeDims d;
   if (!dims_of(layer, T, d)) return -1;

@@ -135,6 +135,24 @@ int launch_indexer_expand(const int32_t* pool_ids, int64_t ldp, int32_t k, const
 int make_map_2d_swizzled(CUtensorMap* m, const void* base, int64_t rows, int64_t width, int64_t ld_bytes,
                          int box_rows);
 
+// Sparse MLA prefill and latent-cache append (csrc/mla.cu).
+struct MlaArgs {
+  const __nv_bfloat16* q = nullptr;    // [T, 64, 576]
+  const __nv_bfloat16* kv = nullptr;   // latent cache [slots, 576]
+  const int32_t* indices = nullptr;    // [T, ld_idx] token positions (-1 = none)
+  int64_t ld_idx = 0;
+  int32_t n_idx = 0;                   // columns used
+  const int32_t* qsl = nullptr;        // [R + 1] first row of each request
+  int32_t R = 0;
+  const int32_t* table = nullptr;      // [R, width] KV pages (128 tokens)
+  int32_t width = 0;
+  float scale = 0.0f;
+  __nv_bfloat16* out = nullptr;        // [T, 64, 512]
+  int64_t T = 0;
+};
+int launch_sparse_mla(const MlaArgs& a, cudaStream_t stream);
+int launch_mla_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, cudaStream_t stream);
+
 int device_sm_count();
 
 }  // namespace ssb
