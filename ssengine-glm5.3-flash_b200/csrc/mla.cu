@@ -8,9 +8,11 @@
 // config 25; split at 32,768 rows, ssengine/model/pp_patch.py:643-672).
 //
 // One CTA per query row, 16 warps: the row's 64 x 576 query stays in shared memory; the selected tokens stream in
-// blocks of 32 gathered rows (cp.async 16-byte pieces, double-buffered, missing tokens zero-filled). Per block:
-// S = Q K^T (warp (head group, token group of 8): 36 mma.sync m16n8k16), an online softmax per head row (one warp per
-// 4 rows, one token per lane, exp2 with the scale folded), O += P V (warp (head group, 128 latent columns): 32 mma);
+// blocks of 32 gathered rows (cp.async 16-byte pieces, a 3-stage ring keeping two blocks in flight, missing tokens
+// zero-filled): the kernel is bound by the latency of those gathers, so bytes in flight matter more than the tensor
+// pipe. Per block: S = Q K^T (warp (head group, 8 tokens): 36 mma.sync m16n8k16 over 4 accumulators), an online
+// softmax per head row (one warp per 4 rows, one token per lane, exp2 with the scale folded), O += P V (warp (head
+// group, 128 latent columns): 32 mma);
 // O stays in registers (64 fp32 per thread) until the row's last block, then is normalised and stored as bf16.
 #include "common.cuh"
 #include "ops.h"
@@ -25,8 +27,9 @@ constexpr int kChunks = kRowBytes / 16;                  // 72 16-byte chunks pe
 constexpr int kQBytes = kHeads * kRowBytes;              // 73728
 constexpr int kKvBytes = kBlk * kRowBytes;               // 36864
 constexpr int kOffQ = 0;
-constexpr int kOffKv = kQBytes;                          // 2 buffers
-constexpr int kOffS = kOffKv + 2 * kKvBytes;             // fp32 [64][33]
+constexpr int kStagesKv = 3;                             // gather ring: two blocks in flight while one is used
+constexpr int kOffKv = kQBytes;
+constexpr int kOffS = kOffKv + kStagesKv * kKvBytes;     // fp32 [64][33] scores
 constexpr int kOffP = kOffS + kHeads * 33 * 4;           // bf16 [64][32] (swizzled, 64-byte rows)
 constexpr int kOffAlpha = kOffP + kHeads * kBlk * 2;     // fp32 [64]
 constexpr int kOffL = kOffAlpha + kHeads * 4;            // fp32 [64]
@@ -42,7 +45,7 @@ SSB_DEVICE void cp_async16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
 }
 SSB_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-SSB_DEVICE void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+SSB_DEVICE void cp_async_wait2() { asm volatile("cp.async.wait_group 2;" ::: "memory"); }
 SSB_DEVICE void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 SSB_DEVICE void ldsm4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -76,7 +79,7 @@ SSB_DEVICE void gather_block(uint8_t* smem, int buf, const __nv_bfloat16* kv, co
 
 __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(MlaArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ int64_t slots[2][kBlk];
+  __shared__ int64_t slots[kStagesKv][kBlk];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;
   const int64_t t = blockIdx.x;
@@ -122,9 +125,12 @@ __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(MlaArgs a) {
     }
     fill_slots(0, 0);
   }
+  if (nblk > 1) fill_slots(1, 1);
   __syncthreads();
   if (nblk > 0) gather_block(smem, 0, a.kv, slots[0], tid);
-  cp_async_commit();
+  cp_async_commit();                       // group: Q + block 0
+  if (nblk > 1) gather_block(smem, 1, a.kv, slots[1], tid);
+  cp_async_commit();                       // group: block 1
 
   const int rg = warp & 3;                 // head rows 16 rg .. 16 rg + 15
   const int cg = warp >> 2;                // S: tokens 8 cg .. 8 cg + 7 of the block; PV: latent columns 128 cg ..
@@ -137,33 +143,34 @@ __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(MlaArgs a) {
   const float sc = a.scale * 1.4426950408889634f;    // exp2 domain
 
   for (int b = 0; b < nblk; ++b) {
-    const int buf = b & 1;
-    if (b + 1 < nblk) {
-      fill_slots(b + 1, buf ^ 1);
+    const int buf = b % kStagesKv;
+    if (b + 2 < nblk) {                    // stage (b + 2) % 3 held block b - 1, finished last iteration
+      const int nb = (b + 2) % kStagesKv;
+      fill_slots(b + 2, nb);
       __syncthreads();
-      gather_block(smem, buf ^ 1, a.kv, slots[buf ^ 1], tid);
+      gather_block(smem, nb, a.kv, slots[nb], tid);
     }
     cp_async_commit();
-    cp_async_wait1();                      // block b (and Q) landed
+    cp_async_wait2();                      // block b (and Q) landed
     __syncthreads();
     const __nv_bfloat16* KV = reinterpret_cast<const __nv_bfloat16*>(smem + kOffKv + buf * kKvBytes);
 
-    // ---- S = Q K^T for head rows 16 rg.., tokens 8 cg.. ----
+    // ---- S = Q K^T for head rows 16 rg.., tokens 8 cg.. (4 accumulators over the 36 k-steps) ----
     {
-      float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 4
+      float s4[4][4] = {};
+#pragma unroll
       for (int ks = 0; ks < kDq / 16; ++ks) {
         uint32_t a0, a1, a2, a3, b0, b1;
         ldsm4(Q + swq(16 * rg + (lane & 15), 16 * ks + (lane >> 4) * 8), a0, a1, a2, a3);
         ldsm2(KV + swq(8 * cg + (lane & 7), 16 * ks + ((lane >> 3) & 1) * 8), b0, b1);
-        mma_bf16(s, a0, a1, a2, a3, b0, b1);
+        mma_bf16(s4[ks & 3], a0, a1, a2, a3, b0, b1);
       }
       const int j0 = 8 * cg + 2 * t4;
-      const bool v0 = slots[buf][j0] >= 0, v1 = slots[buf][j0 + 1] >= 0;
-      S[(16 * rg + g8) * 33 + j0] = v0 ? s[0] * sc : -INFINITY;
-      S[(16 * rg + g8) * 33 + j0 + 1] = v1 ? s[1] * sc : -INFINITY;
-      S[(16 * rg + g8 + 8) * 33 + j0] = v0 ? s[2] * sc : -INFINITY;
-      S[(16 * rg + g8 + 8) * 33 + j0 + 1] = v1 ? s[3] * sc : -INFINITY;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int row = 16 * rg + g8 + 8 * (q >> 1);
+        S[row * 33 + j0 + (q & 1)] = s4[0][q] + s4[1][q] + s4[2][q] + s4[3][q];
+      }
     }
     __syncthreads();
 
@@ -171,7 +178,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(MlaArgs a) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int row = 4 * warp + i;
-      const float x = S[row * 33 + lane];
+      const float x = slots[buf][lane] >= 0 ? S[row * 33 + lane] * sc : -INFINITY;
       float mb = x;
 #pragma unroll
       for (int off = 16; off; off >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
