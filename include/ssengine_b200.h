@@ -171,11 +171,12 @@ int ssb_indexer_expand(const int32_t* pool_ids, int64_t ldp, int32_t k, const in
  * rope 64); kv_cache bf16 [slots, 576]; indices int32 [T, ld_idx], the first n_idx columns used (token positions of
  * the row's request, -1 = none: the indexer's expanded selection); the request of row t is found in qsl int32 [R + 1]
  * (first row of each request, ascending, qsl[0] = 0); slot of position p = page_table[r * width + p / 128] * 128 +
- * p % 128. A row with no selected token gets zeros. Replaces the TRTLLM sparse MLA (ssengine/kernels.py config 25,
+ * p % 128. A row with no selected token gets zeros. status (device int32, may be NULL) receives 4 if a bounded wait
+ * expired. Replaces the TRTLLM sparse MLA (ssengine/kernels.py config 25,
  * split at 32,768 rows ssengine/model/pp_patch.py:643-672). */
 int ssb_sparse_mla(const void* q, int64_t T, const void* kv_cache, const int32_t* indices, int64_t ld_idx,
                    int32_t n_idx, const int32_t* qsl, int32_t R, const int32_t* page_table, int64_t width, float scale,
-                   void* out, void* stream);
+                   void* out, int32_t* status, void* stream);
 
 /* MLA cache append: row t of src bf16 [T, 576] (row pitch lds elements, % 8 == 0) into kv_cache row slots[t] (int64,
  * skipped when < 0). Replaces the fork's latent cache write (ssengine/kernels.py config 23). */

@@ -237,7 +237,7 @@ int ssb_indexer_expand(const int32_t* pool_ids, int64_t ldp, int32_t k, const in
 
 int ssb_sparse_mla(const void* q, int64_t T, const void* kv_cache, const int32_t* indices, int64_t ld_idx,
                    int32_t n_idx, const int32_t* qsl, int32_t R, const int32_t* page_table, int64_t width, float scale,
-                   void* out, void* stream) {
+                   void* out, int32_t* status, void* stream) {
   if (width <= 0 || width > (1 << 24)) return kErrArgs;
   ssb::MlaArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
@@ -252,6 +252,7 @@ int ssb_sparse_mla(const void* q, int64_t T, const void* kv_cache, const int32_t
   a.scale = scale;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.T = T;
+  a.status = status;
   return ssb::launch_sparse_mla(a, static_cast<cudaStream_t>(stream));
 }
 

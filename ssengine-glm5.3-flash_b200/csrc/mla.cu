@@ -7,87 +7,75 @@
 // request. Reference: the TRTLLM sparse MLA called through `trtllm_batch_decode_with_kv_cache_mla` (ssengine/kernels.py
 // config 25; split at 32,768 rows, ssengine/model/pp_patch.py:643-672).
 //
-// One CTA per query row, 16 warps: the row's 64 x 576 query stays in shared memory; the selected tokens stream in
-// blocks of 32 gathered rows (cp.async 16-byte pieces, a 3-stage ring keeping two blocks in flight, missing tokens
-// zero-filled): the kernel is bound by the latency of those gathers, so bytes in flight matter more than the tensor
-// pipe. Per block: S = Q K^T (warp (head group, 8 tokens): 36 mma.sync m16n8k16 over 4 accumulators), an online
-// softmax per head row (one warp per 4 rows, one token per lane, exp2 with the scale folded), O += P V (warp (head
-// group, 128 latent columns): 32 mma);
-// O stays in registers (64 fp32 per thread) until the row's last block, then is normalised and stored as bf16.
+// One CTA (4 warps) per query row; tcgen05 with the 64 heads as M = 64 (accumulator rows in lanes 0-15 of each
+// 32-lane sub-partition; a second M = 64 accumulator sits in lanes 16-31 of the same columns):
+//   Q [64 x 576] bf16 stays in shared memory (TMA, 9 K-major 128-byte-swizzled chunks);
+//   per block of 64 selected tokens, their rows are gathered by cp.async into 9 chunks [64 tokens x 64 dims] with the
+//   same swizzle, double-buffered (block b+1 lands while block b is used);
+//   S [64 x 64] = Q K^T (36 MMAs kind::f16, TMEM columns 0-63, lanes 0-15);
+//   softmax by the 64 threads that own the rows (one head row per thread, exp2, scale folded) with the running max
+//   kept stale until a block raises it by more than 2^8, so the accumulator is rescaled in TMEM only then;
+//   P [64 x 64] bf16 to shared memory (K-major); O += P V with V = the same chunks read MN-major: O columns 256-511,
+//   latent dims 0-255 in lanes 0-15 and dims 256-511 in lanes 16-31 (2 x 4 MMAs of N = 256 per block).
+// Bounded waits; on expiry the status word holds kErrTimeout, in-flight MMAs are drained and TMEM is freed.
 #include "common.cuh"
 #include "ops.h"
 
 namespace ssb {
 namespace {
 
-constexpr int kHeads = 64, kDq = 576, kDv = 512, kBlk = 32;
-constexpr int kMlaThreads = 512;
-constexpr int kRowBytes = kDq * 2;                       // 1152
-constexpr int kChunks = kRowBytes / 16;                  // 72 16-byte chunks per row
-constexpr int kQBytes = kHeads * kRowBytes;              // 73728
-constexpr int kKvBytes = kBlk * kRowBytes;               // 36864
+constexpr int kHeads = 64, kDq = 576, kDv = 512, kBlk = 64;
+constexpr int kMlaThreads = 128;
+constexpr int kChunk = kBlk * 128;                       // [64 rows x 64 bf16], 8 KB
+constexpr int kNChunks = kDq / 64;                       // 9
+constexpr int kQBytes = kNChunks * kChunk;               // 73728
+constexpr int kKvBytes = kNChunks * kChunk;              // 73728 per block buffer
 constexpr int kOffQ = 0;
-constexpr int kStagesKv = 3;                             // gather ring: two blocks in flight while one is used
-constexpr int kOffKv = kQBytes;
-constexpr int kOffS = kOffKv + kStagesKv * kKvBytes;     // fp32 [64][33] scores
-constexpr int kOffP = kOffS + kHeads * 33 * 4;           // bf16 [64][32] (swizzled, 64-byte rows)
-constexpr int kOffAlpha = kOffP + kHeads * kBlk * 2;     // fp32 [64]
-constexpr int kOffL = kOffAlpha + kHeads * 4;            // fp32 [64]
-constexpr int kMlaSmem = kOffL + kHeads * 4;
-
-// [rows][576] bf16 with the 16-byte chunk index XOR-ed by (row & 7) (72 chunks = 9 groups of 8)
-SSB_DEVICE int swq(int r, int c) { return r * kDq + ((((c >> 3) ^ (r & 7))) << 3) + (c & 7); }
-// [64][32] bf16: 4 chunks per row, XOR by ((row >> 1) & 3) so 8 rows of one ldmatrix hit distinct banks
-SSB_DEVICE int swp(int r, int c) { return r * kBlk + ((((c >> 3) ^ ((r >> 1) & 3))) << 3) + (c & 7); }
+constexpr int kOffKv = kQBytes;                          // 2 buffers
+constexpr int kOffP = kOffKv + 2 * kKvBytes;             // P [64 x 64] bf16, K-major swizzled
+constexpr int kOffSlots = kOffP + kChunk;                // int64 [2][64]
+constexpr int kOffBar = kOffSlots + 2 * kBlk * 8;        // bar_q, bar_s, bar_pv, bar_drain
+constexpr int kOffMisc = kOffBar + 32;                   // tmem slot, abort flag
+constexpr int kMlaSmem = kOffMisc + 16 + 1024;           // + alignment slack
+constexpr uint32_t kSCol = 0, kOCol = 256;
 
 SSB_DEVICE void cp_async16(uint32_t dst, const void* src, bool valid) {
   const int n = valid ? 16 : 0;
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
 }
 SSB_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-SSB_DEVICE void cp_async_wait2() { asm volatile("cp.async.wait_group 2;" ::: "memory"); }
 SSB_DEVICE void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-SSB_DEVICE void ldsm4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(smem_u32(p)));
-}
-SSB_DEVICE void ldsm2(const void* p, uint32_t& r0, uint32_t& r1) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(smem_u32(p)));
-}
-SSB_DEVICE void ldsm4t(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(smem_u32(p)));
-}
-SSB_DEVICE void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-               "{%0,%1,%2,%3};"
-               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// Gather block b's 32 token rows into buffer `buf` (token slot -1 -> zeros).
-SSB_DEVICE void gather_block(uint8_t* smem, int buf, const __nv_bfloat16* kv, const int64_t* slot_of, int tid) {
-  const uint32_t base = smem_u32(smem + kOffKv + buf * kKvBytes);
-  for (int c = tid; c < kBlk * kChunks; c += kMlaThreads) {
-    const int r = c / kChunks, ch = c - r * kChunks;
-    const int64_t slot = slot_of[r];
-    const int sch = (ch & ~7) | ((ch & 7) ^ (r & 7));
-    cp_async16(base + r * kRowBytes + sch * 16, kv + (slot >= 0 ? slot : 0) * kDq + ch * 8, slot >= 0);
+SSB_DEVICE void drain_bar(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitNs) break;
   }
 }
 
-__global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(MlaArgs a) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ int64_t slots[kStagesKv][kBlk];
+// Block b's 64 token rows -> chunks of buffer `buf` (rows of a missing token are zeros).
+SSB_DEVICE void gather_block(uint32_t kvb, const __nv_bfloat16* kv, const int64_t* slot_of, int tid) {
+  for (int c = tid; c < kBlk * kNChunks * 8; c += kMlaThreads) {
+    const int r = c / (kNChunks * 8), rem = c - r * (kNChunks * 8);
+    const int ch = rem >> 3, j = rem & 7;
+    const int64_t slot = slot_of[r];
+    cp_async16(kvb + ch * kChunk + r * 128 + ((j ^ (r & 7)) << 4), kv + (slot >= 0 ? slot : 0) * kDq + ch * 64 + j * 8,
+               slot >= 0);
+  }
+}
+
+__global__ void __launch_bounds__(kMlaThreads, 1)
+    sparse_mla_kernel(const __grid_constant__ CUtensorMap mq, const MlaArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g8 = lane >> 2, t4 = lane & 3;
   const int64_t t = blockIdx.x;
-  const __nv_bfloat16* Q = reinterpret_cast<const __nv_bfloat16*>(smem + kOffQ);
-  float* S = reinterpret_cast<float*>(smem + kOffS);
-  __nv_bfloat16* Pm = reinterpret_cast<__nv_bfloat16*>(smem + kOffP);
-  float* ALPHA = reinterpret_cast<float*>(smem + kOffAlpha);
-  float* LSUM = reinterpret_cast<float*>(smem + kOffL);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar_q = sbase + kOffBar, bar_s = bar_q + 8, bar_pv = bar_q + 16, bar_drain = bar_q + 24;
+  int64_t* slots = reinterpret_cast<int64_t*>(smem + kOffSlots);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + kOffMisc + 4);
+  uint8_t* Pb = smem + kOffP;
 
   // the row's request (binary search of the query start list) and its pages
   int lo = 0, hi = a.R - 1;
@@ -98,141 +86,200 @@ __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(MlaArgs a) {
   const int32_t* pages = a.table + (int64_t)lo * a.width;
   const int32_t* idx = a.indices + t * a.ld_idx;
   const int nblk = (a.n_idx + kBlk - 1) / kBlk;
-
-  auto fill_slots = [&](int b, int buf) {
+  auto fill_slots = [&](int b) {
     if (tid < kBlk) {
       const int j = b * kBlk + tid;
-      int64_t s = -1;
+      int64_t sl = -1;
       if (j < a.n_idx) {
         const int32_t pos = idx[j];
         if (pos >= 0 && (pos >> 7) < a.width) {
           const int32_t pg = pages[pos >> 7];
-          if (pg >= 0) s = (int64_t)pg * 128 + (pos & 127);
+          if (pg >= 0) sl = (int64_t)pg * 128 + (pos & 127);
         }
       }
-      slots[buf][tid] = s;
+      slots[(b & 1) * kBlk + tid] = sl;
     }
   };
 
-  // Q -> shared (swizzled), block 0's slots
-  {
-    const __nv_bfloat16* qrow = a.q + t * (int64_t)kHeads * kDq;
-    const uint32_t qb = smem_u32(smem + kOffQ);
-    for (int c = tid; c < kHeads * kChunks; c += kMlaThreads) {
-      const int r = c / kChunks, ch = c - r * kChunks;
-      const int sch = (ch & ~7) | ((ch & 7) ^ (r & 7));
-      cp_async16(qb + r * kRowBytes + sch * 16, qrow + r * kDq + ch * 8, true);
-    }
-    fill_slots(0, 0);
+  if (tid == 0) {
+    mbar_init(bar_q, 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_pv, 1);
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(bar_q, kQBytes);
+    for (int c = 0; c < kNChunks; ++c) tma_load_2d(sbase + kOffQ + c * kChunk, &mq, 64 * c, (int32_t)(t * kHeads), bar_q);
   }
-  if (nblk > 1) fill_slots(1, 1);
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (nblk > 0) fill_slots(0);
+  tc_fence_before();
   __syncthreads();
-  if (nblk > 0) gather_block(smem, 0, a.kv, slots[0], tid);
-  cp_async_commit();                       // group: Q + block 0
-  if (nblk > 1) gather_block(smem, 1, a.kv, slots[1], tid);
-  cp_async_commit();                       // group: block 1
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (nblk > 0) gather_block(sbase + kOffKv, a.kv, slots, tid);
+  cp_async_commit();
 
-  const int rg = warp & 3;                 // head rows 16 rg .. 16 rg + 15
-  const int cg = warp >> 2;                // S: tokens 8 cg .. 8 cg + 7 of the block; PV: latent columns 128 cg ..
-  float o[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
-  float m_run[4], l_run[4];                // softmax state of rows 4 warp .. 4 warp + 3 (lane-uniform)
-#pragma unroll
-  for (int i = 0; i < 4; ++i) { m_run[i] = -INFINITY; l_run[i] = 0.0f; }
-  const float sc = a.scale * 1.4426950408889634f;    // exp2 domain
+  constexpr uint32_t idesc_s = idesc_bf16(64, 64);
+  constexpr uint32_t idesc_pv = idesc_bf16(64, 256) | (1u << 16);      // B (V) MN-major
+  const float sc = a.scale * 1.4426950408889634f;                        // exp2 domain
+  const bool owner = lane < 16;                                          // lanes holding S / O_lo rows
+  const uint32_t tq = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  float m_used = -INFINITY, l_sum = 0.0f;
+  bool ok = true, any_mma = false;
 
-  for (int b = 0; b < nblk; ++b) {
-    const int buf = b % kStagesKv;
-    if (b + 2 < nblk) {                    // stage (b + 2) % 3 held block b - 1, finished last iteration
-      const int nb = (b + 2) % kStagesKv;
-      fill_slots(b + 2, nb);
-      __syncthreads();
-      gather_block(smem, nb, a.kv, slots[nb], tid);
+  for (int b = 0; b < nblk && ok; ++b) {
+    const int kb = b & 1;
+    const uint32_t kvb = sbase + kOffKv + kb * kKvBytes;
+    cp_async_wait0();                                    // block b landed (this thread's pieces)
+    fence_proxy_async_smem();                            // generic-proxy writes -> visible to the tensor core
+    __syncthreads();
+    if (tid == 0) {
+      if (b == 0) mbar_wait(bar_q, 0, abort_flag, a.status);
+      if (!*abort_flag) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < kNChunks; ++c) {
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t ad = smem_desc(sbase + kOffQ + c * kChunk + ks * 32, 0, 1024, 2);
+            const uint64_t bd = smem_desc(kvb + c * kChunk + ks * 32, 0, 1024, 2);
+            tc_mma_f16(tmem + kSCol, ad, bd, idesc_s, (c | ks) != 0 ? 1u : 0u);
+          }
+        }
+        any_mma = true;
+        tc_commit(bar_s);
+      }
     }
+    // PV of block b-1 done: its KV buffer, P and O are free / stable; gather block b+1 into that buffer
+    if (b >= 1) mbar_wait(bar_pv, (b - 1) & 1, abort_flag, a.status);
+    if (b + 1 < nblk) fill_slots(b + 1);
+    __syncthreads();
+    if (*abort_flag) { ok = false; break; }
+    if (b + 1 < nblk) gather_block(sbase + kOffKv + (kb ^ 1) * kKvBytes, a.kv, slots + (kb ^ 1) * kBlk, tid);
     cp_async_commit();
-    cp_async_wait2();                      // block b (and Q) landed
-    __syncthreads();
-    const __nv_bfloat16* KV = reinterpret_cast<const __nv_bfloat16*>(smem + kOffKv + buf * kKvBytes);
+    mbar_wait(bar_s, b & 1, abort_flag, a.status);      // a timeout raises the abort flag, checked after the next barrier
+    tc_fence_after();
 
-    // ---- S = Q K^T for head rows 16 rg.., tokens 8 cg.. (4 accumulators over the 36 k-steps) ----
-    {
-      float s4[4][4] = {};
+    // ---- softmax of the 64 head rows (owner lanes: row 16 warp + lane) ----
+    float v[64];
+    tmem_ld_32x32b_x32(tq + kSCol, *reinterpret_cast<float(*)[32]>(v));
+    tmem_ld_32x32b_x32(tq + kSCol + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+    tmem_ld_wait();
+    float alpha = 1.0f;
+    bool rescale = false;
+    if (owner) {
+      float mb = -INFINITY;
 #pragma unroll
-      for (int ks = 0; ks < kDq / 16; ++ks) {
-        uint32_t a0, a1, a2, a3, b0, b1;
-        ldsm4(Q + swq(16 * rg + (lane & 15), 16 * ks + (lane >> 4) * 8), a0, a1, a2, a3);
-        ldsm2(KV + swq(8 * cg + (lane & 7), 16 * ks + ((lane >> 3) & 1) * 8), b0, b1);
-        mma_bf16(s4[ks & 3], a0, a1, a2, a3, b0, b1);
+      for (int j = 0; j < 64; ++j) {
+        v[j] = slots[kb * kBlk + j] >= 0 ? v[j] * sc : -INFINITY;
+        mb = fmaxf(mb, v[j]);
       }
-      const int j0 = 8 * cg + 2 * t4;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int row = 16 * rg + g8 + 8 * (q >> 1);
-        S[row * 33 + j0 + (q & 1)] = s4[0][q] + s4[1][q] + s4[2][q] + s4[3][q];
+      if (m_used == -INFINITY) {
+        m_used = mb;                                     // nothing accumulated yet (O = 0, l = 0)
+      } else if (mb > m_used + 8.0f) {
+        alpha = exp2f(m_used - mb);
+        m_used = mb;
+        l_sum *= alpha;
+        rescale = true;
       }
+      const int row = 16 * warp + lane;
+      float ps = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float p[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          p[e] = (m_used == -INFINITY) ? 0.0f : exp2f(v[8 * c + e] - m_used);
+          ps += p[e];
+        }
+        uint4 pk;
+        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(p[2 * e], p[2 * e + 1]);
+          pw[e] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        *reinterpret_cast<uint4*>(Pb + row * 128 + ((c ^ (row & 7)) << 4)) = pk;
+      }
+      l_sum += ps;
     }
-    __syncthreads();
-
-    // ---- online softmax: warp w owns rows 4w .. 4w+3, lane = token ----
+    // rescale O rows in TMEM when a row's max moved (warp-collective; lanes 16-31 hold the rows' dims 256-511)
+    alpha = __shfl_sync(0xffffffffu, alpha, lane & 15);
+    if (__any_sync(0xffffffffu, rescale) && b > 0) {
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        float o[32];
+        tmem_ld_32x32b_x32(tq + kOCol + 32 * c, o);
+        tmem_ld_wait();
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int row = 4 * warp + i;
-      const float x = slots[buf][lane] >= 0 ? S[row * 33 + lane] * sc : -INFINITY;
-      float mb = x;
-#pragma unroll
-      for (int off = 16; off; off >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
-      const float m_new = fmaxf(m_run[i], mb);
-      const float p = (m_new == -INFINITY) ? 0.0f : exp2f(x - m_new);
-      float ps = p;
-#pragma unroll
-      for (int off = 16; off; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-      const float alpha = (m_run[i] == -INFINITY) ? 0.0f : exp2f(m_run[i] - m_new);
-      l_run[i] = l_run[i] * alpha + ps;
-      m_run[i] = m_new;
-      Pm[swp(row, lane)] = __float2bfloat16_rn(p);
-      if (lane == 0) ALPHA[row] = alpha;
+        for (int e = 0; e < 32; ++e) o[e] *= alpha;
+        tmem_st_32x32b_x32(tq + kOCol + 32 * c, o);
+      }
+      tmem_st_wait();
     }
+    fence_proxy_async_smem();                            // P (generic stores) -> visible to the tensor core
+    tc_fence_before();
     __syncthreads();
-
-    // ---- O = alpha O + P V for head rows 16 rg.., latent columns 128 cg .. ----
-    {
-      const float al = ALPHA[16 * rg + g8], ah = ALPHA[16 * rg + g8 + 8];
+    if (*abort_flag) { ok = false; break; }
+    if (tid == 0) {
+      tc_fence_after();
 #pragma unroll
-      for (int i = 0; i < 16; ++i) { o[i][0] *= al; o[i][1] *= al; o[i][2] *= ah; o[i][3] *= ah; }
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint64_t ad = smem_desc(sbase + kOffP + ks * 32, 0, 1024, 2);
 #pragma unroll
-      for (int ks = 0; ks < kBlk / 16; ++ks) {
-        uint32_t a0, a1, a2, a3;
-        ldsm4(Pm + swp(16 * rg + (lane & 15), 16 * ks + (lane >> 4) * 8), a0, a1, a2, a3);
-#pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          uint32_t b0, b1, b2, b3;
-          ldsm4t(KV + swq(16 * ks + (lane & 7) + ((lane >> 3) & 1) * 8, 128 * cg + 16 * p + (lane >> 4) * 8), b0, b1, b2,
-                 b3);
-          mma_bf16(o[2 * p], a0, a1, a2, a3, b0, b1);
-          mma_bf16(o[2 * p + 1], a0, a1, a2, a3, b2, b3);
+        for (int h = 0; h < 2; ++h) {
+          const uint64_t bd = smem_desc(kvb + 4 * h * kChunk + ks * 2048, kChunk, 1024, 2);
+          tc_mma_f16(tmem + (static_cast<uint32_t>(16 * h) << 16) + kOCol, ad, bd, idesc_pv,
+                     (b > 0 || ks > 0) ? 1u : 0u);
         }
       }
+      tc_commit(bar_pv);
     }
-    __syncthreads();                       // buffer `buf`, S and P are reused by the next block
   }
   cp_async_wait0();
 
-  // ---- normalise and store ----
-  if (lane == 0) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) LSUM[4 * warp + i] = l_run[i];
-  }
+  // ---- normalise and store (lanes 0-15: dims 0-255 of row 16 warp + lane; lanes 16-31: dims 256-511) ----
+  const bool have = ok && nblk > 0;
+  if (have) mbar_wait(bar_pv, (nblk - 1) & 1, abort_flag, a.status);
   __syncthreads();
-  const float ll = LSUM[16 * rg + g8], lh = LSUM[16 * rg + g8 + 8];
-  const float il = ll > 0.0f ? 1.0f / ll : 0.0f, ih = lh > 0.0f ? 1.0f / lh : 0.0f;
-  __nv_bfloat16* orow = a.out + t * (int64_t)kHeads * kDv;
+  if (*abort_flag) ok = false;
+  tc_fence_after();
+  const float l_row = __shfl_sync(0xffffffffu, l_sum, lane & 15);
+  const float inv = (ok && have && l_row > 0.0f) ? 1.0f / l_row : 0.0f;
+  const int row = 16 * warp + (lane & 15);
+  __nv_bfloat16* orow = a.out + (t * kHeads + row) * kDv + (lane >> 4) * 256;
+#pragma unroll 1
+  for (int c = 0; c < 8; ++c) {
+    float o[32];
+    if (have && ok) {
+      tmem_ld_32x32b_x32(tq + kOCol + 32 * c, o);
+      tmem_ld_wait();
+    }
+    uint4 pk[4];
+    uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int c = 128 * cg + 8 * i + 2 * t4;
-    *reinterpret_cast<__nv_bfloat162*>(orow + (16 * rg + g8) * kDv + c) = __floats2bfloat162_rn(o[i][0] * il, o[i][1] * il);
-    *reinterpret_cast<__nv_bfloat162*>(orow + (16 * rg + g8 + 8) * kDv + c) =
-        __floats2bfloat162_rn(o[i][2] * ih, o[i][3] * ih);
+    for (int e = 0; e < 16; ++e) {
+      const float x0 = (have && ok) ? o[2 * e] * inv : 0.0f, x1 = (have && ok) ? o[2 * e + 1] * inv : 0.0f;
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+      pw[e] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) reinterpret_cast<uint4*>(orow + 32 * c)[e] = pk[e];
+  }
+  if (*abort_flag && any_mma && tid == 0) {
+    tc_commit(bar_drain);
+    drain_bar(bar_drain, 0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -243,7 +290,7 @@ __global__ void mla_append_kernel(const __nv_bfloat16* src, int64_t lds, const i
   if (t >= T) return;
   const int64_t s = slots[t];
   if (s < 0) return;
-  for (int c = threadIdx.x; c < kChunks; c += blockDim.x)
+  for (int c = threadIdx.x; c < kDq / 8; c += blockDim.x)
     reinterpret_cast<uint4*>(cache + s * kDq)[c] = reinterpret_cast<const uint4*>(src + t * lds)[c];
 }
 
@@ -256,13 +303,16 @@ int launch_sparse_mla(const MlaArgs& a, cudaStream_t stream) {
        15))
     return kErrArgs;
   if (a.T == 0) return kOk;
+  CUtensorMap mq;
+  const int rc = make_map_2d_swizzled(&mq, a.q, a.T * kHeads, kDq, kDq * 2, 64);
+  if (rc != kOk) return rc;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(sparse_mla_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMlaSmem) != cudaSuccess)
       return kErrCuda;
     attr = true;
   }
-  sparse_mla_kernel<<<(unsigned)a.T, kMlaThreads, kMlaSmem, stream>>>(a);
+  sparse_mla_kernel<<<(unsigned)a.T, kMlaThreads, kMlaSmem, stream>>>(mq, a);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

@@ -149,6 +149,7 @@ struct MlaArgs {
   float scale = 0.0f;
   __nv_bfloat16* out = nullptr;        // [T, 64, 512]
   int64_t T = 0;
+  int32_t* status = nullptr;           // device status word (bounded waits)
 };
 int launch_sparse_mla(const MlaArgs& a, cudaStream_t stream);
 int launch_mla_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, cudaStream_t stream);

@@ -18,7 +18,7 @@ HEADS, DQ, DV = 64, 576, 512
 
 def sparse_mla(q: torch.Tensor, kv_cache: torch.Tensor, indices: torch.Tensor, qsl: torch.Tensor,
                page_table: torch.Tensor, scale: float, out: torch.Tensor, n_idx: int | None = None,
-               stream=None) -> torch.Tensor:
+               stream=None, status: torch.Tensor | None = None) -> torch.Tensor:
     """q bf16 [T, 64, 576], kv_cache bf16 [slots, 576], indices int32 [T, >= n_idx], qsl int32 [R + 1],
     page_table int32 [R, width] -> out bf16 [T, 64, 512]."""
     so = lib.load()
@@ -28,7 +28,7 @@ def sparse_mla(q: torch.Tensor, kv_cache: torch.Tensor, indices: torch.Tensor, q
     n = indices.shape[1] if n_idx is None else n_idx
     rc = so.ssb_sparse_mla(q.data_ptr(), q.shape[0], kv_cache.data_ptr(), indices.data_ptr(), indices.stride(0), n,
                            qsl.data_ptr(), qsl.shape[0] - 1, page_table.data_ptr(), page_table.shape[1], scale,
-                           out.data_ptr(), lib.stream_ptr(stream))
+                           out.data_ptr(), None if status is None else status.data_ptr(), lib.stream_ptr(stream))
     lib.check("ssb_sparse_mla", rc)
     return out
 
