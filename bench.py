@@ -45,6 +45,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true", help="skip the nvidia-smi window (profiling runs)")
+    ap.add_argument("--no-components", action="store_true", help="skip the per-component timings")
     return ap.parse_args()
 
 
@@ -233,6 +234,158 @@ def run_reference(args, rank: int) -> None:
     del np
 
 
+# ---------------------------------------------------------------------------------------------- components
+def _event_ms(fn, reps: int = 5, warm: int = 2) -> float:
+    """Median device time of fn() over reps launches (CUDA events on the current stream, L2 flushed between)."""
+    import torch
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    return statistics.median(ts)
+
+
+def attention_pair_requests(T: int = 32768, R: int = 8, seed: int = SEED):
+    """BASELINE config 3's microbatch: R requests whose new-token counts are lognormal (median 2k) summing to T,
+    appended to cached prefixes of 0-64k tokens."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    lens = rng.lognormal(np.log(2048), 1.0, R)
+    lens = np.maximum(1, (lens / lens.sum() * T).astype(np.int64))
+    lens[-1] += T - lens.sum()
+    prefix = rng.integers(0, 65536, R)
+    return lens, prefix
+
+
+def time_components(device, pk: dict) -> dict:
+    """Device time of the other hot-path kernels on BASELINE config 3 (KDA 32 x 128; DSA indexer 32 x 128 with
+    top-2048 tokens = top-512 pools of 4, sparse MLA 64 heads, latent 512 + rope 64) and mHC at the stage shape."""
+    import numpy as np
+    import torch
+
+    from ssengine_b200 import indexer, mla
+    from ssengine_b200.kda import KdaLayer, seq_table
+
+    out = {}
+    lens, prefix = attention_pair_requests()
+    T, R = int(lens.sum()), len(lens)
+    order = np.argsort(-lens)
+    starts = np.concatenate([[0], np.cumsum(lens)])
+    g = torch.Generator(device=device).manual_seed(SEED)
+    rnd = lambda *shape: torch.randn(*shape, device=device, generator=g)
+
+    # KDA layer: conv + chunked scan + state pages (every request continues a cached prefix: has initial state)
+    H, P = 32, 32 * 128
+    x = rnd(T, 3 * P).to(torch.bfloat16)
+    gr = rnd(T, P).to(torch.bfloat16)
+    beta = rnd(T, H).to(torch.bfloat16)
+    layer = KdaLayer((torch.rand(3 * P, 4, device=device, generator=g) - 0.5).to(torch.bfloat16),
+                     torch.rand(H, device=device, generator=g) * 2 - 1, rnd(P) * 0.5, -5.0)
+    cst = rnd(R + 1, 3, 3 * P).to(torch.bfloat16)
+    rst = rnd(R + 1, H, 128, 128) * 0.05
+    o = torch.empty(T, P, dtype=torch.bfloat16, device=device)
+    st = seq_table([(int(starts[i]), int(starts[i + 1]), 1 + int(i), 1) for i in order], device)
+    ms = _event_ms(lambda: layer.prefill(x, gr, beta, o, st, cst, rst))
+    byts = T * (5 * P * 2 + 2 * H) + 2 * R * H * 128 * 128 * 4
+    out["kda_prefill"] = {"ms": ms, "tokens": T, "heads": H, "requests": R, "bound": "hbm",
+                          "achieved_gbs": byts / ms / 1e6, "frac": byts / ms / 1e6 / pk["hbm_gbs"],
+                          "algorithmic_bytes": byts}
+    del x, gr, beta, layer, cst, rst, o
+    torch.cuda.empty_cache()
+
+    # DSA: indexer logits -> canonical top-512 pools -> tokens -> sparse MLA
+    positions = np.concatenate([np.arange(p0, p0 + n) for p0, n in zip(prefix, lens)]).astype(np.int64)
+    n_pages = [-(-(int(p0) + int(n)) // 128) for p0, n in zip(prefix, lens)]
+    width = max(n_pages)
+    table = np.full((R, width), -1, np.int32)
+    at = 1
+    for r, n in enumerate(n_pages):
+        table[r, :n] = np.arange(at, at + n)
+        at += n
+    qsl = starts.astype(np.int32)
+    pos = torch.from_numpy(positions).to(device)
+    tab = torch.from_numpy(table).to(device)
+    groups = torch.from_numpy(indexer.work_groups(qsl[:-1], lens, prefix)).to(device)
+    q_idx = rnd(T, 32, 128).to(torch.bfloat16)
+    w = torch.rand(T, 32, device=device, generator=g)
+    kpool = rnd(at * 32, 128).to(torch.bfloat16)
+    ldl = int(((positions.max() + 1) // 4 + 127) // 128 * 128)
+    logits = torch.empty(T, ldl, device=device)
+    ms = _event_ms(lambda: indexer.logits(q_idx, w, kpool, tab, groups, logits))
+    vis = float(((positions + 1) // 4).sum())
+    fl = vis * 32 * 128 * 2
+    out["indexer_logits"] = {"ms": ms, "bound": "tensor", "achieved_tflops": fl / ms / 1e9,
+                             "frac": fl / ms / 1e9 / pk["bf16_tflops"], "algorithmic_flop": fl,
+                             "peak": f"dense bf16 {pk['bf16_tflops']} TFLOP/s"}
+    ids = torch.empty(T, 512, dtype=torch.int32, device=device)
+    ms = _event_ms(lambda: indexer.topk(logits, pos, 512, ids))
+    byts = vis * 4 + T * 512 * 4
+    out["indexer_topk"] = {"ms": ms, "bound": "hbm", "achieved_gbs": byts / ms / 1e6,
+                           "frac": byts / ms / 1e6 / pk["hbm_gbs"], "algorithmic_bytes": byts}
+    tok = torch.empty(T, 2051 + 5, dtype=torch.int32, device=device)
+    out["indexer_expand"] = {"ms": _event_ms(lambda: indexer.expand(ids, pos, tok))}
+    del logits, q_idx, kpool
+    torch.cuda.empty_cache()
+    q = (rnd(T, 64, 576) * 0.5).to(torch.bfloat16)
+    kv = rnd(at * 128, 576).to(torch.bfloat16)
+    mo = torch.empty(T, 64, 512, dtype=torch.bfloat16, device=device)
+    qsl_d = torch.from_numpy(qsl).to(device)
+    ms = _event_ms(lambda: mla.sparse_mla(q, kv, tok, qsl_d, tab, 192 ** -0.5, mo, n_idx=2051), reps=3, warm=1)
+    sel = float((tok[:, :2051] >= 0).sum().item())
+    fl = sel * 64 * (576 + 512) * 2
+    out["sparse_mla"] = {"ms": ms, "bound": "tensor", "achieved_tflops": fl / ms / 1e9,
+                         "frac": fl / ms / 1e9 / pk["bf16_tflops"], "algorithmic_flop": fl,
+                         "selected_tokens_per_row": sel / T}
+    del q, kv, mo, tok, ids
+    torch.cuda.empty_cache()
+
+    # mHC layer boundary (post + pre + Sinkhorn + RMSNorm) at the stage shape, T = 8192, H = 4096
+    from ssengine_b200 import lib
+    import ctypes
+
+    Tm, Hm = 8192, 4096
+    xm = rnd(Tm, Hm).to(torch.bfloat16)
+    res = rnd(Tm, 4, Hm).to(torch.bfloat16)
+    pin = torch.rand(Tm, 4, device=device, generator=g) + 0.5
+    cin = torch.softmax(rnd(Tm, 4, 4), dim=1)
+    fn = rnd(24, 4 * Hm) / 128.0
+    scale = torch.tensor([0.8, 0.6, 1.5], device=device)
+    base = rnd(24) * 0.3
+    nw = torch.ones(Hm, device=device).to(torch.bfloat16)
+    nr = torch.empty_like(res)
+    po = torch.empty(Tm, 4, device=device)
+    co = torch.empty(Tm, 4, 4, device=device)
+    y = torch.empty_like(xm)
+    prm = lib.MhcParamsC(Hm, 4, fn.data_ptr(), scale.data_ptr(), base.data_ptr(), nw.data_ptr(), 1e-6, 1e-2, 1e-6,
+                         2.0, 1e-6, 20)
+    so = lib.load()
+
+    def mhc():
+        lib.check("ssb_mhc", so.ssb_mhc(ctypes.byref(prm), xm.data_ptr(), res.data_ptr(), pin.data_ptr(),
+                                        cin.data_ptr(), nr.data_ptr(), po.data_ptr(), co.data_ptr(), y.data_ptr(), Tm,
+                                        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+
+    ms = _event_ms(mhc)
+    byts = Tm * (4 * Hm * 2 * 2 + Hm * 2 * 2) + 24 * 4 * Hm * 4
+    out["mhc_post_pre"] = {"ms": ms, "tokens": Tm, "bound": "hbm", "achieved_gbs": byts / ms / 1e6,
+                           "frac": byts / ms / 1e6 / pk["hbm_gbs"], "algorithmic_bytes": byts}
+    out["workload"] = (f"BASELINE config 3 attention pair: {T} tokens from {R} requests (new tokens lognormal median "
+                       f"2k, cached prefixes 0-64k; KDA 32 x 128, DSA indexer 32 x 128 top-512 pools of 4, sparse MLA "
+                       f"64 heads latent 512 + rope 64, bf16 latent cache); mHC at T = 8192, H = 4096")
+    return out
+
+
 def main() -> None:
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -365,6 +518,8 @@ def main() -> None:
         if e2e_ms is not None:
             line["e2e"] = {"value": world * T * steps / (e2e_ms / 1e3), "unit": "tok/s",
                            "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2}
+        if world == 1 and not args.no_components:
+            line["components"] = time_components(device, pk)
         if world == 1 and not args.no_cpu_baseline:
             import numpy as np
 
