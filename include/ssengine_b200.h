@@ -159,6 +159,17 @@ int ssb_indexer_logits(const void* q, const float* w, int64_t T, const void* k_c
                        const int32_t* page_table, int64_t width, const int32_t* groups, int64_t G, float* logits,
                        int64_t ldl, int32_t* status, void* stream);
 
+/* Indexer key pools of one prefill microbatch: every pool of 4 tokens that a request's chunk completes, pool[p, c] =
+ * sum_j softmax_j(gate[4p+j, c] + ape[j, c]) * k[4p+j, c] (fp32, stored bf16) at row page_table[r * width + p / 32] *
+ * 32 + p % 32 of pool_cache [rows, 128]; tokens of the pool before the chunk's start come from the request's tail ring
+ * (bf16 [blocks][2 (k, gate)][4][128]); afterwards the ring holds the chunk's trailing incomplete pool. k, gate bf16
+ * [T, ld] (128 used), ape fp32 [4, 128]; reqs int32 [R][4] device = {first row, rows, start position, tail block};
+ * max_rows >= every request's rows (sizes the grid). Replaces `kpool_compress_insert` + `kpool_seed_tail_cache`
+ * (ssengine/model/pp_patch.py:415-534; the fork's `kpool_compress_and_write_cache`, configs 17-18). */
+int ssb_kpool_insert(const void* k, const void* gate, int64_t ld, const float* ape, const int32_t* reqs, int64_t R,
+                     int32_t max_rows, const int32_t* page_table, int64_t width, void* pool_cache, void* tail_ring,
+                     void* stream);
+
 /* Selected pools -> token indices: out int32 [rows, ldo >= 4k + 3]: column c < 4k = pool_ids[row, c / 4] * 4 + c % 4
  * (-1 where the pool id is -1), then the tokens of the row's incomplete last pool (seq_len = positions[row] + 1:
  * 4 * (seq_len / 4) .. seq_len - 1, -1 past them). Replaces `kpool_fast.expand_into` (ssengine/model/kpool_fast.py:

@@ -260,6 +260,24 @@ int ssb_mla_cache_append(const void* src, int64_t lds, const int64_t* slots, int
   return ssb::launch_mla_append(src, lds, slots, T, cache, static_cast<cudaStream_t>(stream));
 }
 
+int ssb_kpool_insert(const void* k, const void* gate, int64_t ld, const float* ape, const int32_t* reqs, int64_t R,
+                     int32_t max_rows, const int32_t* page_table, int64_t width, void* pool_cache, void* tail_ring,
+                     void* stream) {
+  if (R < 0 || R > (1 << 20) || width <= 0 || width > (1 << 24)) return kErrArgs;
+  ssb::KpoolArgs a;
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.gate = static_cast<const __nv_bfloat16*>(gate);
+  a.ld = ld;
+  a.ape = ape;
+  a.reqs = reqs;
+  a.R = static_cast<int32_t>(R);
+  a.table = page_table;
+  a.width = static_cast<int32_t>(width);
+  a.pool = static_cast<__nv_bfloat16*>(pool_cache);
+  a.tail = static_cast<__nv_bfloat16*>(tail_ring);
+  return ssb::launch_kpool_insert(a, max_rows, static_cast<cudaStream_t>(stream));
+}
+
 int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T) {
   MoeDims d;
   if (!dims_of(layer, T, d)) return -1;

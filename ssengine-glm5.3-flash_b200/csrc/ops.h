@@ -154,6 +154,21 @@ struct MlaArgs {
 int launch_sparse_mla(const MlaArgs& a, cudaStream_t stream);
 int launch_mla_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, cudaStream_t stream);
 
+// Indexer key pools (csrc/kpool.cu).
+struct KpoolArgs {
+  const __nv_bfloat16* k = nullptr;    // [T, ld] (128 used)
+  const __nv_bfloat16* gate = nullptr; // [T, ld]
+  int64_t ld = 0;
+  const float* ape = nullptr;          // [4, 128]
+  const int32_t* reqs = nullptr;       // [R][4] = {first row, rows, start position, tail block}
+  int32_t R = 0;
+  const int32_t* table = nullptr;      // [R, width] KV pages = pool pages
+  int32_t width = 0;
+  __nv_bfloat16* pool = nullptr;       // [pages * 32, 128]
+  __nv_bfloat16* tail = nullptr;       // [blocks][2][4][128]
+};
+int launch_kpool_insert(const KpoolArgs& a, int32_t max_rows, cudaStream_t stream);
+
 int device_sm_count();
 
 }  // namespace ssb

@@ -66,6 +66,19 @@ def topk(logit_rows: torch.Tensor, positions: torch.Tensor, k: int, out: torch.T
     return out
 
 
+def kpool_insert(k: torch.Tensor, gate: torch.Tensor, ape: torch.Tensor, reqs: torch.Tensor, max_rows: int,
+                 page_table: torch.Tensor, pool_cache: torch.Tensor, tail_ring: torch.Tensor, stream=None) -> None:
+    """Compress the pools the chunk completes into the pool-key cache and keep its trailing incomplete pool in the
+    tail ring (reqs int32 [R, 4] on the device: first row, rows, start position, tail block)."""
+    so = lib.load()
+    assert k.dtype == torch.bfloat16 and gate.dtype == torch.bfloat16 and k.stride(0) == gate.stride(0)
+    assert ape.dtype == torch.float32 and reqs.dtype == torch.int32 and pool_cache.dtype == torch.bfloat16
+    rc = so.ssb_kpool_insert(k.data_ptr(), gate.data_ptr(), k.stride(0), ape.data_ptr(), reqs.data_ptr(),
+                             reqs.shape[0], max_rows, page_table.data_ptr(), page_table.shape[1], pool_cache.data_ptr(),
+                             tail_ring.data_ptr(), lib.stream_ptr(stream))
+    lib.check("ssb_kpool_insert", rc)
+
+
 def expand(pool_ids: torch.Tensor, positions: torch.Tensor, out: torch.Tensor, stream=None) -> torch.Tensor:
     """Token indices int32 [rows, 4k + 3] of the selected pools plus the row's incomplete last pool."""
     so = lib.load()
