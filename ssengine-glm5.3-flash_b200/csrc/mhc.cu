@@ -27,8 +27,8 @@ constexpr int kMhcThreads = 256;
 constexpr int kMhcH = 64;         // hidden positions per K chunk (x 4 streams = 256 K)
 constexpr int kMhcK = 4 * kMhcH;
 constexpr int kMhcMix = 24;
-constexpr int kFnPitch = kMhcK + 1;   // padded rows: the 8 column groups read 8 different rows without conflicts
-constexpr int kZPitch = kMhcK + 1;    // padded rows: the 4 tokens of a warp read 4 different rows without conflicts
+constexpr int kFnPitch = kMhcK + 4;   // 16-byte rows; 260 = 4 (mod 32) spreads the 8 column groups' rows over the banks
+constexpr int kZPitch = kMhcK + 4;    // 16-byte rows; the 4 tokens of a warp read 4 different bank groups
 
 struct MhcArgs {
   const __nv_bfloat16* x;
@@ -52,7 +52,7 @@ SSB_DEVICE float sigmoidf(float v) { return 1.0f / (1.0f + expf(-v)); }
 
 template <bool POST, bool PRE>
 __global__ void __launch_bounds__(kMhcThreads) mhc_kernel(const MhcArgs a) {
-  extern __shared__ float smem_f[];
+  extern __shared__ __align__(16) float smem_f[];
   float* zs = smem_f;                                  // [32][257]
   float* fs = zs + kMhcTok * kZPitch;                  // [24][257]
   __shared__ float mix[kMhcTok][kMhcMix];
@@ -77,6 +77,13 @@ __global__ void __launch_bounds__(kMhcThreads) mhc_kernel(const MhcArgs a) {
   float acc[3] = {0.0f, 0.0f, 0.0f};
   float ss = 0.0f;
   const int cg = (tid & 7) * 3;                        // GEMM phase: mixes [cg, cg + 3) of token tl
+  // x / res rows of the next chunk are loaded while the current one is mixed (software pipeline over the K chunks)
+  uint4 rv_next[4], xv_next = make_uint4(0, 0, 0, 0);
+  if (tv) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) rv_next[i] = *reinterpret_cast<const uint4*>(a.res + (t * 4 + i) * H + seg);
+    if (POST) xv_next = *reinterpret_cast<const uint4*>(a.x + t * H + seg);
+  }
   for (int64_t h0 = 0; h0 < H; h0 += kMhcH) {
     // ---- new residual of this chunk (all 4 streams, 8 positions per thread) ----
     float nr[4][8];
@@ -84,9 +91,14 @@ __global__ void __launch_bounds__(kMhcThreads) mhc_kernel(const MhcArgs a) {
       const int64_t hh = h0 + seg;
       uint4 rv[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) rv[i] = *reinterpret_cast<const uint4*>(a.res + (t * 4 + i) * H + hh);
+      for (int i = 0; i < 4; ++i) rv[i] = rv_next[i];
+      const uint4 xv = xv_next;
+      if (h0 + kMhcH < H) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) rv_next[i] = *reinterpret_cast<const uint4*>(a.res + (t * 4 + i) * H + hh + kMhcH);
+        if (POST) xv_next = *reinterpret_cast<const uint4*>(a.x + t * H + hh + kMhcH);
+      }
       if (POST) {
-        const uint4 xv = *reinterpret_cast<const uint4*>(a.x + t * H + hh);
         const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -118,25 +130,36 @@ __global__ void __launch_bounds__(kMhcThreads) mhc_kernel(const MhcArgs a) {
     if (PRE) {
       // stage the chunk: z[tl][j * 64 + seg + e], fn rows [c][j * 64 + hh]
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < 4; ++j) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          zs[tl * kZPitch + j * kMhcH + seg + e] = nr[j][e];
-          ss = fmaf(nr[j][e], nr[j][e], ss);
-        }
-      for (int i = tid; i < kMhcMix * kMhcK; i += kMhcThreads) {
-        const int c = i / kMhcK, kk = i - c * kMhcK;
+        for (int e = 0; e < 8; ++e) ss = fmaf(nr[j][e], nr[j][e], ss);
+        *reinterpret_cast<float4*>(zs + tl * kZPitch + j * kMhcH + seg) = make_float4(nr[j][0], nr[j][1], nr[j][2], nr[j][3]);
+        *reinterpret_cast<float4*>(zs + tl * kZPitch + j * kMhcH + seg + 4) =
+            make_float4(nr[j][4], nr[j][5], nr[j][6], nr[j][7]);
+      }
+      for (int i = tid; i < kMhcMix * kMhcK / 4; i += kMhcThreads) {
+        const int c = i / (kMhcK / 4), kk = (i - c * (kMhcK / 4)) * 4;
         const int j = kk / kMhcH, hh = kk - j * kMhcH;
-        fs[c * kFnPitch + kk] = a.fn[static_cast<int64_t>(c) * 4 * H + j * H + h0 + hh];
+        *reinterpret_cast<float4*>(fs + c * kFnPitch + kk) =
+            __ldg(reinterpret_cast<const float4*>(a.fn + static_cast<int64_t>(c) * 4 * H + j * H + h0 + hh));
       }
       __syncthreads();
       const float* zr = zs + tl * kZPitch;
-#pragma unroll 8
-      for (int kk = 0; kk < kMhcK; ++kk) {
-        const float z = zr[kk];
-        acc[0] = fmaf(z, fs[(cg + 0) * kFnPitch + kk], acc[0]);
-        acc[1] = fmaf(z, fs[(cg + 1) * kFnPitch + kk], acc[1]);
-        acc[2] = fmaf(z, fs[(cg + 2) * kFnPitch + kk], acc[2]);
+      const float* f0 = fs + (cg + 0) * kFnPitch;
+      const float* f1 = fs + (cg + 1) * kFnPitch;
+      const float* f2 = fs + (cg + 2) * kFnPitch;
+#pragma unroll 4
+      for (int kk = 0; kk < kMhcK; kk += 4) {
+        const float4 z = *reinterpret_cast<const float4*>(zr + kk);
+        const float4 a0 = *reinterpret_cast<const float4*>(f0 + kk);
+        const float4 a1 = *reinterpret_cast<const float4*>(f1 + kk);
+        const float4 a2 = *reinterpret_cast<const float4*>(f2 + kk);
+        acc[0] = fmaf(z.x, a0.x, acc[0]); acc[0] = fmaf(z.y, a0.y, acc[0]);
+        acc[0] = fmaf(z.z, a0.z, acc[0]); acc[0] = fmaf(z.w, a0.w, acc[0]);
+        acc[1] = fmaf(z.x, a1.x, acc[1]); acc[1] = fmaf(z.y, a1.y, acc[1]);
+        acc[1] = fmaf(z.z, a1.z, acc[1]); acc[1] = fmaf(z.w, a1.w, acc[1]);
+        acc[2] = fmaf(z.x, a2.x, acc[2]); acc[2] = fmaf(z.y, a2.y, acc[2]);
+        acc[2] = fmaf(z.z, a2.z, acc[2]); acc[2] = fmaf(z.w, a2.w, acc[2]);
       }
       __syncthreads();
     }
@@ -209,35 +232,57 @@ __global__ void __launch_bounds__(kMhcThreads) mhc_kernel(const MhcArgs a) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) p[i] = tv ? pre_s[tl][i] : 0.0f;
   float ls = 0.0f;
-  for (int64_t hh = seg; tv && hh < H; hh += kMhcH) {
-    uint4 rv[4];
+  // two positions groups per iteration, all loads issued before the stores (the stores to y could alias src for all
+  // the compiler knows)
+  for (int64_t hh = seg; tv && hh < H; hh += 2 * kMhcH) {
+    const bool two = hh + kMhcH < H;
+    uint4 rv[2][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) rv[i] = *reinterpret_cast<const uint4*>(src + (t * 4 + i) * H + hh);
-    uint32_t w[4];
+    for (int u = 0; u < 2; ++u)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float v = 0.0f;
+      for (int i = 0; i < 4; ++i)
+        rv[u][i] = (u == 0 || two) ? *reinterpret_cast<const uint4*>(src + (t * 4 + i) * H + hh + u * kMhcH)
+                                   : make_uint4(0, 0, 0, 0);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v = fmaf(p[i], __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rv[i])[e]), v);
-      const __nv_bfloat16 b = __float2bfloat16(v);
-      const float bv = __bfloat162float(b);
-      ls = fmaf(bv, bv, ls);
-      if (e & 1) w[e >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(b)) << 16;
-      else w[e >> 1] = __bfloat16_as_ushort(b);
+    for (int u = 0; u < 2; ++u) {
+      if (u == 1 && !two) break;
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float v = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          v = fmaf(p[i], __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rv[u][i])[e]), v);
+        const __nv_bfloat16 b = __float2bfloat16(v);
+        const float bv = __bfloat162float(b);
+        ls = fmaf(bv, bv, ls);
+        if (e & 1) w[e >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(b)) << 16;
+        else w[e >> 1] = __bfloat16_as_ushort(b);
+      }
+      *reinterpret_cast<uint4*>(a.y + t * H + hh + u * kMhcH) = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    *reinterpret_cast<uint4*>(a.y + t * H + hh) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 #pragma unroll
   for (int off = 4; off > 0; off >>= 1) ls += __shfl_xor_sync(0xFFFFFFFFu, ls, off);
   const float inv = rsqrtf(ls / static_cast<float>(H) + a.norm_eps);
-  for (int64_t hh = seg; tv && hh < H; hh += kMhcH) {
-    uint4 v = *reinterpret_cast<const uint4*>(a.y + t * H + hh);
-    const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + hh);
-    __nv_bfloat16* vb = reinterpret_cast<__nv_bfloat16*>(&v);
-    const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv);
+  for (int64_t hh = seg; tv && hh < H; hh += 4 * kMhcH) {
+    uint4 v[4], wv[4];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) vb[e] = __float2bfloat16(__bfloat162float(vb[e]) * inv * __bfloat162float(wb[e]));
-    *reinterpret_cast<uint4*>(a.y + t * H + hh) = v;
+    for (int u = 0; u < 4; ++u) {
+      if (hh + u * kMhcH < H) {
+        v[u] = *reinterpret_cast<const uint4*>(a.y + t * H + hh + u * kMhcH);
+        wv[u] = *reinterpret_cast<const uint4*>(a.norm_w + hh + u * kMhcH);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (hh + u * kMhcH >= H) break;
+      __nv_bfloat16* vb = reinterpret_cast<__nv_bfloat16*>(&v[u]);
+      const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv[u]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) vb[e] = __float2bfloat16(__bfloat162float(vb[e]) * inv * __bfloat162float(wb[e]));
+      *reinterpret_cast<uint4*>(a.y + t * H + hh + u * kMhcH) = v[u];
+    }
   }
 }
 
