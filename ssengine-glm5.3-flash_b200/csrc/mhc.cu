@@ -51,7 +51,7 @@ struct MhcArgs {
 SSB_DEVICE float sigmoidf(float v) { return 1.0f / (1.0f + expf(-v)); }
 
 template <bool POST, bool PRE>
-__global__ void __launch_bounds__(kMhcThreads) mhc_kernel(const MhcArgs a) {
+__global__ void __launch_bounds__(kMhcThreads, 2) mhc_kernel(const MhcArgs a) {
   extern __shared__ __align__(16) float smem_f[];
   float* zs = smem_f;                                  // [32][257]
   float* fs = zs + kMhcTok * kZPitch;                  // [24][257]
@@ -74,9 +74,9 @@ __global__ void __launch_bounds__(kMhcThreads) mhc_kernel(const MhcArgs a) {
       for (int j = 0; j < 4; ++j) cm[i][j] = a.comb_in[t * 16 + i * 4 + j];
     }
   }
-  float acc[3] = {0.0f, 0.0f, 0.0f};
+  float macc[2][3][4] = {};                            // mix partials: token tiles x mix tiles (mma accumulators)
+  const int warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
   float ss = 0.0f;
-  const int cg = (tid & 7) * 3;                        // GEMM phase: mixes [cg, cg + 3) of token tl
   // x / res rows of the next chunk are loaded while the current one is mixed (software pipeline over the K chunks)
   uint4 rv_next[4], xv_next = make_uint4(0, 0, 0, 0);
   if (tv) {
@@ -144,22 +144,36 @@ __global__ void __launch_bounds__(kMhcThreads) mhc_kernel(const MhcArgs a) {
             __ldg(reinterpret_cast<const float4*>(a.fn + static_cast<int64_t>(c) * 4 * H + j * H + h0 + hh));
       }
       __syncthreads();
-      const float* zr = zs + tl * kZPitch;
-      const float* f0 = fs + (cg + 0) * kFnPitch;
-      const float* f1 = fs + (cg + 1) * kFnPitch;
-      const float* f2 = fs + (cg + 2) * kFnPitch;
-#pragma unroll 4
-      for (int kk = 0; kk < kMhcK; kk += 4) {
-        const float4 z = *reinterpret_cast<const float4*>(zr + kk);
-        const float4 a0 = *reinterpret_cast<const float4*>(f0 + kk);
-        const float4 a1 = *reinterpret_cast<const float4*>(f1 + kk);
-        const float4 a2 = *reinterpret_cast<const float4*>(f2 + kk);
-        acc[0] = fmaf(z.x, a0.x, acc[0]); acc[0] = fmaf(z.y, a0.y, acc[0]);
-        acc[0] = fmaf(z.z, a0.z, acc[0]); acc[0] = fmaf(z.w, a0.w, acc[0]);
-        acc[1] = fmaf(z.x, a1.x, acc[1]); acc[1] = fmaf(z.y, a1.y, acc[1]);
-        acc[1] = fmaf(z.z, a1.z, acc[1]); acc[1] = fmaf(z.w, a1.w, acc[1]);
-        acc[2] = fmaf(z.x, a2.x, acc[2]); acc[2] = fmaf(z.y, a2.y, acc[2]);
-        acc[2] = fmaf(z.z, a2.z, acc[2]); acc[2] = fmaf(z.w, a2.w, acc[2]);
+      // mixes[32 tokens x 24] += z[32 x 256] fn_chunk^T on the tensor cores (tf32 m16n8k8; z is bf16-exact in tf32):
+      // warp w takes k-steps 4w .. 4w + 3 for all 2 x 3 (token, mix) tiles
+#pragma unroll
+      for (int kq = 0; kq < 4; ++kq) {
+        const int k0 = (4 * warp + kq) * 8;
+        uint32_t af[2][4], bf[3][2];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          const float* zr0 = zs + (16 * mt + g8) * kZPitch + k0 + t4;
+          const float* zr1 = zr0 + 8 * kZPitch;
+          af[mt][0] = __float_as_uint(zr0[0]);
+          af[mt][1] = __float_as_uint(zr1[0]);
+          af[mt][2] = __float_as_uint(zr0[4]);
+          af[mt][3] = __float_as_uint(zr1[4]);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 3; ++nt) {
+          const float* fr = fs + (8 * nt + g8) * kFnPitch + k0 + t4;
+          asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(bf[nt][0]) : "f"(fr[0]));
+          asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(bf[nt][1]) : "f"(fr[4]));
+        }
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < 3; ++nt)
+            asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                         "{%0,%1,%2,%3};"
+                         : "+f"(macc[mt][nt][0]), "+f"(macc[mt][nt][1]), "+f"(macc[mt][nt][2]), "+f"(macc[mt][nt][3])
+                         : "r"(af[mt][0]), "r"(af[mt][1]), "r"(af[mt][2]), "r"(af[mt][3]), "r"(bf[nt][0]),
+                           "r"(bf[nt][1]));
       }
       __syncthreads();
     }
@@ -169,8 +183,23 @@ __global__ void __launch_bounds__(kMhcThreads) mhc_kernel(const MhcArgs a) {
 #pragma unroll
   for (int off = 4; off > 0; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);   // the 8 threads of a token
   if ((tid & 7) == 0) ssq[tl] = ss;
+  // the 8 warps' K-slice partials of the [32 x 24] mixes, summed through shared memory (fs is free now)
+  __syncthreads();
 #pragma unroll
-  for (int m = 0; m < 3; ++m) mix[tl][cg + m] = acc[m];
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt)
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        fs[warp * (kMhcTok * kMhcMix) + (16 * mt + g8 + 8 * (q >> 1)) * kMhcMix + 8 * nt + 2 * t4 + (q & 1)] =
+            macc[mt][nt][q];
+  __syncthreads();
+  for (int i = tid; i < kMhcTok * kMhcMix; i += kMhcThreads) {
+    float v = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kMhcThreads / 32; ++w) v += fs[w * (kMhcTok * kMhcMix) + i];
+    mix[i / kMhcMix][i % kMhcMix] = v;
+  }
   __syncthreads();
   if (tid < kMhcTok && t0 + tid < a.T) {
     const int64_t tt = t0 + tid;
