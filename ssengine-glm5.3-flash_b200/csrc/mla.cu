@@ -12,9 +12,10 @@
 //   Q [64 x 576] bf16 stays in shared memory (TMA, 9 K-major 128-byte-swizzled chunks);
 //   per block of 64 selected tokens, their rows are gathered by cp.async into 9 chunks [64 tokens x 64 dims] with the
 //   same swizzle, double-buffered (block b+1 lands while block b is used);
-//   S [64 x 64] = Q K^T (36 MMAs kind::f16, TMEM columns 0-63, lanes 0-15);
-//   softmax by the 64 threads that own the rows (one head row per thread, exp2, scale folded) with the running max
-//   kept stale until a block raises it by more than 2^8, so the accumulator is rescaled in TMEM only then;
+//   S [64 x 64] = Q K^T as two N = 32 halves (tokens 0-31 in lanes 0-15, 32-63 in lanes 16-31 of columns 0-31;
+//   2 x 36 MMAs kind::f16); softmax by all 128 threads (a head row's two halves combine max and sum with a shuffle;
+//   exp2, scale folded) with the running max kept stale until a block raises it by more than 2^8, so the accumulator
+//   is rescaled in TMEM only then;
 //   P [64 x 64] bf16 to shared memory (K-major); O += P V with V = the same chunks read MN-major: O columns 256-511,
 //   latent dims 0-255 in lanes 0-15 and dims 256-511 in lanes 16-31 (2 x 4 MMAs of N = 256 per block).
 // Bounded waits; on expiry the status word holds kErrTimeout, in-flight MMAs are drained and TMEM is freed.
@@ -53,15 +54,21 @@ SSB_DEVICE void drain_bar(uint32_t bar, uint32_t parity) {
   }
 }
 
-// Block b's 64 token rows -> chunks of buffer `buf` (rows of a missing token are zeros).
+// Block b's 64 token rows -> the 9 chunks of a buffer (a missing token reads row 0; its score is masked): thread t
+// copies half (t & 1) of row t >> 1, four 16-byte pieces per chunk, all offsets fixed at compile time.
 SSB_DEVICE void gather_block(uint32_t kvb, const __nv_bfloat16* kv, const int64_t* slot_of, int tid) {
-  for (int c = tid; c < kBlk * kNChunks * 8; c += kMlaThreads) {
-    const int r = c / (kNChunks * 8), rem = c - r * (kNChunks * 8);
-    const int ch = rem >> 3, j = rem & 7;
-    const int64_t slot = slot_of[r];
-    cp_async16(kvb + ch * kChunk + r * 128 + ((j ^ (r & 7)) << 4), kv + (slot >= 0 ? slot : 0) * kDq + ch * 64 + j * 8,
-               slot >= 0);
-  }
+  const int r = tid >> 1, hi = tid & 1;
+  const int64_t slot = slot_of[r];
+  const __nv_bfloat16* src = kv + (slot >= 0 ? slot : 0) * kDq + hi * 32;
+  const uint32_t dst = kvb + r * 128;
+  const int sw = r & 7;
+#pragma unroll
+  for (int ch = 0; ch < kNChunks; ++ch)
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = 4 * hi + jj;
+      cp_async16(dst + ch * kChunk + ((j ^ sw) << 4), src + ch * 64 + jj * 8, true);
+    }
 }
 
 __global__ void __launch_bounds__(kMlaThreads, 1)
@@ -124,10 +131,9 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   if (nblk > 0) gather_block(sbase + kOffKv, a.kv, slots, tid);
   cp_async_commit();
 
-  constexpr uint32_t idesc_s = idesc_bf16(64, 64);
+  constexpr uint32_t idesc_s = idesc_bf16(64, 32);                     // tokens 0-31 -> lanes 0-15, 32-63 -> 16-31
   constexpr uint32_t idesc_pv = idesc_bf16(64, 256) | (1u << 16);      // B (V) MN-major
   const float sc = a.scale * 1.4426950408889634f;                        // exp2 domain
-  const bool owner = lane < 16;                                          // lanes holding S / O_lo rows
   const uint32_t tq = tmem + (static_cast<uint32_t>(warp * 32) << 16);
   float m_used = -INFINITY, l_sum = 0.0f;
   bool ok = true, any_mma = false;
@@ -147,8 +153,11 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
             const uint64_t ad = smem_desc(sbase + kOffQ + c * kChunk + ks * 32, 0, 1024, 2);
-            const uint64_t bd = smem_desc(kvb + c * kChunk + ks * 32, 0, 1024, 2);
-            tc_mma_f16(tmem + kSCol, ad, bd, idesc_s, (c | ks) != 0 ? 1u : 0u);
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const uint64_t bd = smem_desc(kvb + c * kChunk + hh * 4096 + ks * 32, 0, 1024, 2);
+              tc_mma_f16(tmem + (static_cast<uint32_t>(16 * hh) << 16) + kSCol, ad, bd, idesc_s, (c | ks) != 0 ? 1u : 0u);
+            }
           }
         }
         any_mma = true;
@@ -165,20 +174,23 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     mbar_wait(bar_s, b & 1, abort_flag, a.status);      // a timeout raises the abort flag, checked after the next barrier
     tc_fence_after();
 
-    // ---- softmax of the 64 head rows (owner lanes: row 16 warp + lane) ----
-    float v[64];
-    tmem_ld_32x32b_x32(tq + kSCol, *reinterpret_cast<float(*)[32]>(v));
-    tmem_ld_32x32b_x32(tq + kSCol + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+    // ---- softmax: lane l holds row 16 warp + (l & 15), tokens 32 (l >> 4) .. + 31; the two halves of a row combine
+    //      their max and sum with one shuffle and keep identical running state ----
+    float v[32];
+    tmem_ld_32x32b_x32(tq + kSCol, v);
     tmem_ld_wait();
+    const int half = lane >> 4;
     float alpha = 1.0f;
     bool rescale = false;
-    if (owner) {
+    {
+      const int64_t* sl = slots + kb * kBlk + 32 * half;
       float mb = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        v[j] = slots[kb * kBlk + j] >= 0 ? v[j] * sc : -INFINITY;
+      for (int j = 0; j < 32; ++j) {
+        v[j] = sl[j] >= 0 ? v[j] * sc : -INFINITY;
         mb = fmaxf(mb, v[j]);
       }
+      mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 16));
       if (m_used == -INFINITY) {
         m_used = mb;                                     // nothing accumulated yet (O = 0, l = 0)
       } else if (mb > m_used + 8.0f) {
@@ -187,10 +199,10 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
         l_sum *= alpha;
         rescale = true;
       }
-      const int row = 16 * warp + lane;
+      const int row = 16 * warp + (lane & 15);
       float ps = 0.0f;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         float p[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -204,12 +216,12 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
           __nv_bfloat162 h2 = __floats2bfloat162_rn(p[2 * e], p[2 * e + 1]);
           pw[e] = *reinterpret_cast<uint32_t*>(&h2);
         }
-        *reinterpret_cast<uint4*>(Pb + row * 128 + ((c ^ (row & 7)) << 4)) = pk;
+        const int chunk = 4 * half + c;
+        *reinterpret_cast<uint4*>(Pb + row * 128 + ((chunk ^ (row & 7)) << 4)) = pk;
       }
-      l_sum += ps;
+      l_sum += ps + __shfl_xor_sync(0xffffffffu, ps, 16);
     }
-    // rescale O rows in TMEM when a row's max moved (warp-collective; lanes 16-31 hold the rows' dims 256-511)
-    alpha = __shfl_sync(0xffffffffu, alpha, lane & 15);
+    // rescale O rows in TMEM when a row's max moved (warp-collective; lanes 0-15 hold dims 0-255, 16-31 dims 256-511)
     if (__any_sync(0xffffffffu, rescale) && b > 0) {
 #pragma unroll 1
       for (int c = 0; c < 8; ++c) {
@@ -249,8 +261,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   __syncthreads();
   if (*abort_flag) ok = false;
   tc_fence_after();
-  const float l_row = __shfl_sync(0xffffffffu, l_sum, lane & 15);
-  const float inv = (ok && have && l_row > 0.0f) ? 1.0f / l_row : 0.0f;
+  const float inv = (ok && have && l_sum > 0.0f) ? 1.0f / l_sum : 0.0f;
   const int row = 16 * warp + (lane & 15);
   __nv_bfloat16* orow = a.out + (t * kHeads + row) * kDv + (lane >> 4) * 256;
 #pragma unroll 1
