@@ -86,6 +86,12 @@ int ssb_embed_rows(const void* table, int64_t vocab, int64_t H, const int64_t* i
 int ssb_rmsnorm(const void* x, int64_t H, const int64_t* rows, int64_t n, const void* w, float eps, void* y,
                 void* stream);
 
+/* KDA output norm per 128-channel head: y = x * rsqrt(mean(x^2) + eps) * w[c % 128] * sigmoid(gate) (x, gate, y bf16
+ * [rows, ld*] with heads * 128 columns; w bf16 [128]). Replaces the fork's FusedRMSNormGated(head_dim,
+ * activation="sigmoid") of the KDA layer (vLLM kimi_linear `o_norm`). */
+int ssb_gated_rmsnorm(const void* x, int64_t ldx, const void* gate, int64_t ldg, const void* w, float eps, void* y,
+                      int64_t ldy, int64_t rows, int32_t heads, void* stream);
+
 /* out int64 [n] = the lowest column of the maximum of logits fp32 [n, N] (row pitch ld; NaN never wins): the last
  * stage's greedy token (ssengine/model/stage.py:746-762 `head_logits` + argmax). */
 int ssb_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, void* stream);

@@ -105,3 +105,39 @@ def prefill(x, weight, conv_state, g, beta, a_log, dt_bias, lower_bound, rec_sta
     q, k, v, cst = conv(x, weight, conv_state, seqs, P)
     out, rst = recurrent(q, k, v, g, beta, a_log, dt_bias, lower_bound, D ** -0.5, rec_state, seqs, H, D)
     return out, cst, rst
+
+
+def gated_rmsnorm(o, gate, w, eps, D=128):
+    """Per D-channel head: o * rsqrt(mean(o^2) + eps) * w * sigmoid(gate) (the KDA output norm)."""
+    o = np.asarray(o, np.float64)
+    T, P = o.shape
+    oh = o.reshape(T, P // D, D)
+    inv = 1.0 / np.sqrt((oh * oh).mean(axis=2, keepdims=True) + eps)
+    g = 1.0 / (1.0 + np.exp(-np.asarray(gate, np.float64).reshape(T, P // D, D)))
+    return (oh * inv * np.asarray(w, np.float64)[None, None, :] * g).reshape(T, P)
+
+
+def nvfp4_linear(x, codes, sf, gs_w, gs_in):
+    """bf16-valued x [T, K] quantized to NVFP4 with gs_in, times the dequantized weights [N, K] -> float64 [T, N]."""
+    from . import nvfp4
+
+    xc, xs = nvfp4.quantize(np.asarray(x, np.float32), gs_in)
+    xq = nvfp4.dequantize(xc, xs, gs_in).astype(np.float64)
+    w = nvfp4.dequantize(codes, sf, gs_w).astype(np.float64)
+    return xq @ w.T
+
+
+def attention_block(y, p, conv_state, rec_state, seqs, heads, gs_in, eps, lower_bound=-5.0, D=128):
+    """The KDA attention block: in_proj -> f_b / g_b -> conv + recurrence -> gated RMSNorm -> o_proj, each projection
+    NVFP4 with its output rounded to bf16 (the device's rounding points). p: in_proj, f_b, g_b, o_proj as (codes, sf,
+    gs), conv_w, a_log, dt_bias, norm_w. -> (out bf16-valued [T, H], conv_state, rec_state)."""
+    P = heads * D
+    proj = bf16(nvfp4_linear(y, *p["in_proj"], gs_in))
+    f_a, g_a = proj[:, 3 * P:3 * P + 128], proj[:, 3 * P + 128:3 * P + 256]
+    beta = proj[:, 3 * P + 256:3 * P + 256 + heads]
+    gate = bf16(nvfp4_linear(f_a, *p["f_b"], gs_in))
+    ogate = bf16(nvfp4_linear(g_a, *p["g_b"], gs_in))
+    o, cst, rst = prefill(proj[:, :3 * P], p["conv_w"], conv_state, gate, beta, p["a_log"], p["dt_bias"], lower_bound,
+                          rec_state, seqs, heads, D)
+    o = bf16(gated_rmsnorm(bf16(o), ogate, p["norm_w"], eps, D))
+    return bf16(nvfp4_linear(o, *p["o_proj"], gs_in)), cst, rst

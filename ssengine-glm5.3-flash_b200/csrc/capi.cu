@@ -148,6 +148,11 @@ int ssb_rmsnorm(const void* x, int64_t H, const int64_t* rows, int64_t n, const 
   return ssb::launch_rmsnorm(x, H, rows, n, w, eps, y, static_cast<cudaStream_t>(stream));
 }
 
+int ssb_gated_rmsnorm(const void* x, int64_t ldx, const void* gate, int64_t ldg, const void* w, float eps, void* y,
+                      int64_t ldy, int64_t rows, int32_t heads, void* stream) {
+  return ssb::launch_gated_rmsnorm(x, ldx, gate, ldg, w, eps, y, ldy, rows, heads, static_cast<cudaStream_t>(stream));
+}
+
 int ssb_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, void* stream) {
   if (logits == nullptr || out == nullptr) return kErrArgs;
   return ssb::launch_argmax_rows(logits, ld, N, n, out, static_cast<cudaStream_t>(stream));

@@ -151,6 +151,42 @@ int grid_of(int64_t work, int threads) {
   return static_cast<int>(b < 1 ? 1 : b);
 }
 
+// Gated RMSNorm per 128-channel head group: y = x * rsqrt(mean(x^2) + eps) * w[c] * sigmoid(gate) (bf16 out); one warp
+// per (row, head), 4 channels a lane. The reference's KDA output norm (FusedRMSNormGated, activation sigmoid).
+__global__ void gated_rmsnorm_kernel(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* gate, int64_t ldg,
+                                     const __nv_bfloat16* w, float eps, __nv_bfloat16* y, int64_t ldy, int64_t rows,
+                                     int heads) {
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= rows * heads) return;
+  const int64_t t = gw / heads;
+  const int h = static_cast<int>(gw - t * heads);
+  const int c = h * 128 + lane * 4;
+  const uint2 xv = *reinterpret_cast<const uint2*>(x + t * ldx + c);
+  const uint2 gv = *reinterpret_cast<const uint2*>(gate + t * ldg + c);
+  const uint2 wv = *reinterpret_cast<const uint2*>(w + lane * 4);
+  const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
+  const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gv);
+  const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv);
+  float f[4], ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[i] = __bfloat162float(xb[i]);
+    ss = fmaf(f[i], f[i], ss);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = rsqrtf(ss / 128.0f + eps);
+  uint2 ov;
+  __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float gt = __bfloat162float(gb[i]);
+    ob[i] = __float2bfloat16(f[i] * inv * __bfloat162float(wb[i]) / (1.0f + expf(-gt)));
+  }
+  *reinterpret_cast<uint2*>(y + t * ldy + c) = ov;
+}
+
 }  // namespace
 
 int launch_stage_metadata(const int32_t* qsl, const int32_t* starts, const int32_t* page_ptr, const int32_t* pages,
@@ -190,6 +226,21 @@ int launch_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, in
   if (N <= 0 || n < 0 || ld < N) return kErrArgs;
   if (n == 0) return kOk;
   argmax_kernel<<<static_cast<unsigned>(n), 256, 0, stream>>>(logits, ld, N, n, out);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int launch_gated_rmsnorm(const void* x, int64_t ldx, const void* gate, int64_t ldg, const void* w, float eps, void* y,
+                         int64_t ldy, int64_t rows, int heads, cudaStream_t stream) {
+  if (x == nullptr || gate == nullptr || w == nullptr || y == nullptr || rows < 0 || heads <= 0 || ldx < heads * 128 ||
+      ldg < heads * 128 || ldy < heads * 128 || (ldx | ldg | ldy) % 4 != 0 ||
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(w) |
+        reinterpret_cast<uintptr_t>(y)) & 7))
+    return kErrArgs;
+  if (rows == 0) return kOk;
+  const int64_t warps = rows * heads;
+  gated_rmsnorm_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(gate), ldg,
+      static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(y), ldy, rows, heads);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
