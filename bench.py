@@ -380,6 +380,30 @@ def time_components(device, pk: dict) -> dict:
     byts = Tm * (4 * Hm * 2 * 2 + Hm * 2 * 2) + 24 * 4 * Hm * 4
     out["mhc_post_pre"] = {"ms": ms, "tokens": Tm, "bound": "hbm", "achieved_gbs": byts / ms / 1e6,
                            "frac": byts / ms / 1e6 / pk["hbm_gbs"], "algorithmic_bytes": byts}
+    del xm, res, nr, y
+    torch.cuda.empty_cache()
+
+    # one full KDA + MoE decoder layer at the stage shape (boundary, KDA attention 64 x 128 with NVFP4 projections,
+    # boundary, NVFP4 MoE 128 experts top-8 + shared), T = 8192 from 4 requests continuing cached prefixes
+    from ssengine_b200.layers import KdaDecoderLayer
+
+    Tl, heads = 8192, 64
+    layer = KdaDecoderLayer(SEED, 4096, heads, F, E, K_TOP, device)
+    lens_l = [3000, 2500, 1700, 992]
+    st_l = np.concatenate([[0], np.cumsum(lens_l)])
+    seqs_l = seq_table([(int(st_l[i]), int(st_l[i + 1]), i + 1, 1) for i in range(4)], device)
+    res_l = rnd(Tl, 4, 4096).to(torch.bfloat16)
+    x_l = rnd(Tl, 4096).to(torch.bfloat16)
+    post_l = torch.rand(Tl, 4, device=device, generator=g) + 0.5
+    comb_l = torch.softmax(rnd(Tl, 4, 4), dim=1)
+    cst_l = rnd(5, 3, 3 * heads * 128).to(torch.bfloat16)
+    rst_l = rnd(5, heads, 128, 128) * 0.05
+    st_w = torch.zeros(1, dtype=torch.int32, device=device)
+    ms = _event_ms(lambda: layer.forward(res_l, x_l, post_l, comb_l, seqs_l, cst_l, rst_l, st_w), reps=3, warm=1)
+    out["kda_decoder_layer"] = {"ms": ms, "tokens": Tl, "tok_per_s": Tl / ms * 1e3, "heads": heads,
+                                "note": "boundary + KDA attention (NVFP4 in_proj / f_b / g_b / o_proj, conv + scan, "
+                                        "gated norm) + boundary + NVFP4 MoE; a 12-layer stage slice of such layers "
+                                        "takes about 12 x this"}
     out["workload"] = (f"BASELINE config 3 attention pair: {T} tokens from {R} requests (new tokens lognormal median "
                        f"2k, cached prefixes 0-64k; KDA 32 x 128, DSA indexer 32 x 128 top-512 pools of 4, sparse MLA "
                        f"64 heads latent 512 + rope 64, bf16 latent cache); mHC at T = 8192, H = 4096")

@@ -124,3 +124,73 @@ class KdaAttention:
         if keep:
             self.parts["normed"] = o
         return out
+
+
+class MhcBoundary:
+    """One mHC layer boundary (4 streams): the previous sub-block's post and the next sub-block's pre + RMSNorm, in one
+    `ssb_mhc` launch (the reference's `MegaMhcPostPre`, ssengine/model/pp_patch.py:125-153)."""
+
+    def __init__(self, gen: torch.Generator, hidden: int, device, repeat: int = 20):
+        H = hidden
+        self.H = H
+        self.fn = (torch.randn(24, 4 * H, generator=gen, device=device) / (4 * H) ** 0.5).contiguous()
+        self.scale = torch.tensor([0.8, 0.6, 1.5], device=device)
+        self.base = torch.randn(24, generator=gen, device=device) * 0.3
+        self.norm_w = (torch.rand(H, generator=gen, device=device) + 0.5).to(torch.bfloat16)
+        self.eps = dict(rms_eps=1e-6, pre_eps=1e-2, sinkhorn_eps=1e-6, post_mult=2.0, norm_eps=1e-6)
+        self.repeat = repeat
+        self._c = lib.MhcParamsC(H, 4, self.fn.data_ptr(), self.scale.data_ptr(), self.base.data_ptr(),
+                                 self.norm_w.data_ptr(), self.eps["rms_eps"], self.eps["pre_eps"],
+                                 self.eps["sinkhorn_eps"], self.eps["post_mult"], self.eps["norm_eps"], repeat)
+        self._lib = lib.load()
+
+    def __call__(self, x, res, post_in, comb_in, new_res, post_out, comb_out, y, stream=None) -> None:
+        """x = None: pre only (the stage-edge receive) on res; else post of x into new_res, then pre of new_res."""
+        import ctypes
+
+        T = res.shape[0]
+        rc = self._lib.ssb_mhc(ctypes.byref(self._c), None if x is None else x.data_ptr(), res.data_ptr(),
+                               None if post_in is None else post_in.data_ptr(),
+                               None if comb_in is None else comb_in.data_ptr(),
+                               None if new_res is None else new_res.data_ptr(), post_out.data_ptr(),
+                               comb_out.data_ptr(), y.data_ptr(), T, lib.stream_ptr(stream))
+        lib.check("ssb_mhc", rc)
+
+
+class KdaDecoderLayer:
+    """One Glm5Next KDA + MoE decoder layer on the 4-stream residual: boundary A (post of the previous sub-block,
+    pre of attention) -> KDA attention -> boundary B (post of attention, pre of the FFN) -> NVFP4 MoE (routed top-k +
+    shared expert). The layer's output sub-block (the MoE rows, with their post / comb mixes) is folded into the
+    residual by the next boundary."""
+
+    def __init__(self, seed: int, hidden: int, heads: int, inter: int, experts: int, top_k: int, device):
+        from . import moe
+
+        dev = torch.device(device)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        self.H = hidden
+        self.bound_a = MhcBoundary(g, hidden, dev)
+        self.attn = KdaAttention(seed + 1, hidden, heads, dev)
+        self.bound_b = MhcBoundary(g, hidden, dev)
+        self.moe = moe.MoELayer.from_logical(weights.moe_logical(seed + 2, hidden, inter, experts, device=dev), top_k,
+                                             dev)
+        self.device = dev
+
+    def forward(self, res, x_prev, post_prev, comb_prev, seqs, conv_state, rec_state, status, stream=None):
+        """res bf16 [T, 4, H]; x_prev bf16 [T, H] with post_prev fp32 [T, 4] / comb_prev [T, 4, 4] (x_prev None: the
+        first layer of the stage, pre only). Returns (res after attention, MoE rows, post, comb) for the next
+        boundary."""
+        T, H, dev = res.shape[0], self.H, self.device
+        f32 = dict(dtype=torch.float32, device=dev)
+        res_a = torch.empty_like(res) if x_prev is not None else res
+        post_a, comb_a = torch.empty(T, 4, **f32), torch.empty(T, 4, 4, **f32)
+        y = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        self.bound_a(x_prev, res, post_prev, comb_prev, res_a if x_prev is not None else None, post_a, comb_a, y,
+                     stream)
+        x_a = self.attn.forward(y, seqs, conv_state, rec_state, status, stream=stream)
+        res_b = torch.empty_like(res)
+        post_b, comb_b = torch.empty(T, 4, **f32), torch.empty(T, 4, 4, **f32)
+        self.bound_b(x_a, res_a, post_a, comb_a, res_b, post_b, comb_b, y, stream)
+        x_b = self.moe.forward(y, stream=stream)
+        return res_b, x_b, post_b, comb_b
