@@ -92,6 +92,14 @@ int ssb_rmsnorm(const void* x, int64_t H, const int64_t* rows, int64_t n, const 
 int ssb_gated_rmsnorm(const void* x, int64_t ldx, const void* gate, int64_t ldg, const void* w, float eps, void* y,
                       int64_t ldy, int64_t rows, int32_t heads, void* stream);
 
+/* Stage 0's 4-stream residual: out bf16 [T, 4, H] = 4 copies of each embedding row x bf16 [T, H] (H % 8 == 0).
+ * Replaces `hc_expand_cat` (ssengine/model/pp_patch.py:169-183). */
+int ssb_hc_expand(const void* x, int64_t T, int64_t H, void* out, void* stream);
+
+/* out bf16 [n, H] = mean over the 4 streams of res bf16 [T, 4, H] at rows (int64 [n], or row r when NULL): the last
+ * stage's stream merge before the final norm (ssengine/model/stage.py:746-762 `head_logits`). */
+int ssb_hc_mean(const void* res, int64_t H, const int64_t* rows, int64_t n, void* out, void* stream);
+
 /* out int64 [n] = the lowest column of the maximum of logits fp32 [n, N] (row pitch ld; NaN never wins): the last
  * stage's greedy token (ssengine/model/stage.py:746-762 `head_logits` + argmax). */
 int ssb_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, void* stream);

@@ -153,6 +153,14 @@ int ssb_gated_rmsnorm(const void* x, int64_t ldx, const void* gate, int64_t ldg,
   return ssb::launch_gated_rmsnorm(x, ldx, gate, ldg, w, eps, y, ldy, rows, heads, static_cast<cudaStream_t>(stream));
 }
 
+int ssb_hc_expand(const void* x, int64_t T, int64_t H, void* out, void* stream) {
+  return ssb::launch_hc_expand(x, T, H, out, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_hc_mean(const void* res, int64_t H, const int64_t* rows, int64_t n, void* out, void* stream) {
+  return ssb::launch_hc_mean(res, H, rows, n, out, static_cast<cudaStream_t>(stream));
+}
+
 int ssb_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, void* stream) {
   if (logits == nullptr || out == nullptr) return kErrArgs;
   return ssb::launch_argmax_rows(logits, ld, N, n, out, static_cast<cudaStream_t>(stream));

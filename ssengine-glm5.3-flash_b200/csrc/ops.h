@@ -75,6 +75,8 @@ int launch_rmsnorm(const void* x, int64_t H, const int64_t* rows, int64_t n, con
                    cudaStream_t stream);
 int launch_gated_rmsnorm(const void* x, int64_t ldx, const void* gate, int64_t ldg, const void* w, float eps, void* y,
                          int64_t ldy, int64_t rows, int heads, cudaStream_t stream);
+int launch_hc_expand(const void* x, int64_t T, int64_t H, void* out, cudaStream_t stream);
+int launch_hc_mean(const void* res, int64_t H, const int64_t* rows, int64_t n, void* out, cudaStream_t stream);
 int launch_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, cudaStream_t stream);
 
 // mHC layer boundary (csrc/mhc.cu): do_post -> new_res; do_pre -> post_out, comb_out, y.

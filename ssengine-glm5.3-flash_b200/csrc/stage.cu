@@ -187,6 +187,30 @@ __global__ void gated_rmsnorm_kernel(const __nv_bfloat16* x, int64_t ldx, const 
   *reinterpret_cast<uint2*>(y + t * ldy + c) = ov;
 }
 
+// hc_expand: the 4 residual streams of a stage-0 row all start as its embedding (16-byte pieces).
+__global__ void hc_expand_kernel(const uint4* __restrict__ x, int64_t n16_row, int64_t T, uint4* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= T * n16_row) return;
+  const int64_t t = i / n16_row, c = i - t * n16_row;
+  const uint4 v = x[i];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) out[(t * 4 + s) * n16_row + c] = v;
+}
+
+// hc mean: out[r] = bf16(mean over the 4 streams of res[rows[r]]) (rows == nullptr: row r).
+__global__ void hc_mean_kernel(const __nv_bfloat16* __restrict__ res, int64_t H, const int64_t* __restrict__ rows,
+                               int64_t n, __nv_bfloat16* __restrict__ out) {
+  const int64_t r = blockIdx.x;
+  if (r >= n) return;
+  const int64_t t = rows != nullptr ? rows[r] : r;
+  for (int64_t h = threadIdx.x; h < H; h += blockDim.x) {
+    float v = 0.0f;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) v += __bfloat162float(res[(t * 4 + s) * H + h]);
+    out[r * H + h] = __float2bfloat16(v * 0.25f);
+  }
+}
+
 }  // namespace
 
 int launch_stage_metadata(const int32_t* qsl, const int32_t* starts, const int32_t* page_ptr, const int32_t* pages,
@@ -241,6 +265,25 @@ int launch_gated_rmsnorm(const void* x, int64_t ldx, const void* gate, int64_t l
   gated_rmsnorm_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(gate), ldg,
       static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(y), ldy, rows, heads);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int launch_hc_expand(const void* x, int64_t T, int64_t H, void* out, cudaStream_t stream) {
+  if (x == nullptr || out == nullptr || T < 0 || H <= 0 || H % 8 != 0 ||
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15))
+    return kErrArgs;
+  if (T == 0) return kOk;
+  const int64_t n16 = H / 8, total = T * n16;
+  hc_expand_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(static_cast<const uint4*>(x), n16, T,
+                                                                                    static_cast<uint4*>(out));
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int launch_hc_mean(const void* res, int64_t H, const int64_t* rows, int64_t n, void* out, cudaStream_t stream) {
+  if (res == nullptr || out == nullptr || n < 0 || H <= 0) return kErrArgs;
+  if (n == 0) return kOk;
+  hc_mean_kernel<<<static_cast<unsigned>(n), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(res), H, rows, n,
+                                                               static_cast<__nv_bfloat16*>(out));
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

@@ -13,10 +13,16 @@ Mirrors ssengine/model/stage.py:216-762 of the reference and its contract in sse
   chunk order; enqueues GPU work only, a fresh output per call;
 - `forward(plan, hidden_in) = run(prepare(plan), hidden_in)`; `tier_ranges()`.
 
-Layers built so far: NVFP4 MoE layers with a residual (x + MoE(x)); the hybrid model's mHC, KDA and DSA layers are
-not built yet, so `hidden_width` is the plain hidden size and the stage owns no KV tensors (`tier_ranges()` is empty).
-The last stage's head: RMSNorm of each request's last row, NVFP4 lm_head GEMM (fp32 logits), argmax (lowest index on
-ties).
+Two layer kinds (`StageConfig.layer_kind`):
+- "kda": Glm5Next KDA + MoE decoder layers on the 4-stream mHC residual (`layers.KdaDecoderLayer`: boundary, KDA
+  attention with NVFP4 projections, boundary, NVFP4 MoE); stage 0 expands its embeddings to 4 streams
+  (hc_expand), a later stage starts with a pre-only boundary on the received [T, 4H] rows (edge_recv), a stage that
+  is not the last ends with a post-only boundary (edge_send); each KDA layer owns its conv / recurrent state pools,
+  indexed by the chunk's `state_blocks[0]` (has state = the chunk continues its request). The DSA layers of the
+  hybrid split are not composed yet: a "kda" stage runs every layer of its range as a KDA layer.
+- "moe": NVFP4 MoE layers with a plain residual (x + MoE(x)), hidden [T, H], no state (BASELINE config 2's slice).
+The last stage's head: the mean of the 4 streams ("kda"), RMSNorm of each request's last row, NVFP4 lm_head GEMM
+(fp32 logits), argmax (lowest index on ties).
 """
 
 from __future__ import annotations
@@ -69,6 +75,9 @@ class StageConfig:
     num_blocks: int = 64
     seed: int = 0
     norm_eps: float = 1e-5
+    layer_kind: str = "moe"            # "moe": residual NVFP4 MoE layers, hidden [T, H]; "kda": KDA + MoE decoder
+                                       # layers on the 4-stream mHC residual, hidden [T, 4H] across stage edges
+    kda_heads: int = 64
 
 
 @dataclass
@@ -82,6 +91,7 @@ class Batch:
     last_rows: torch.Tensor            # int64 [#is_last], rows whose token the last stage returns, plan chunk order
     bucket: int | None = None
     keep: list = field(default_factory=list)   # host / device buffers that must outlive the queued work
+    kda_seqs: torch.Tensor | None = None       # int32 [R, 4] {first row, end row, KDA state block, has state}, device
 
 
 class _Pack:
@@ -120,14 +130,30 @@ class StageModel:
         self.first, self.last = stage == 0, stage == len(split) - 1
         start = sum(split[:stage])
         self.layer_range = range(start, start + split[stage])
-        self.hidden_width = cfg.hidden
+        self.kda = cfg.layer_kind == "kda"
+        if cfg.layer_kind not in ("moe", "kda"):
+            raise ValueError(f"layer_kind {cfg.layer_kind!r}")
+        self.hidden_width = 4 * cfg.hidden if self.kda else cfg.hidden
         self.num_blocks = (num_blocks if num_blocks is not None else cfg.num_blocks) + extra_blocks
         self.cuda_graphs = cfg.cuda_graphs if cuda_graphs is None else cuda_graphs
         self.ipc_kv = ipc_kv
         self._lib = lib.load()
         H, F, E = cfg.hidden, cfg.inter, cfg.experts
-        self.layers = [moe.MoELayer.from_logical(weights.moe_logical(cfg.seed * 1000 + i, H, F, E, device=self.device),
-                                                 cfg.top_k, self.device, add_input=True) for i in self.layer_range]
+        if self.kda:
+            from .layers import KdaDecoderLayer
+
+            P = cfg.kda_heads * 128
+            self.layers = [KdaDecoderLayer(cfg.seed * 1000 + 10 * i, H, cfg.kda_heads, F, E, cfg.top_k, self.device)
+                           for i in self.layer_range]
+            # per layer: KDA conv state [blocks, 3, 3P] bf16 and recurrent state [blocks, heads, 128, 128] fp32
+            self.kda_states = [(torch.zeros(self.num_blocks, 3, 3 * P, dtype=torch.bfloat16, device=self.device),
+                                torch.zeros(self.num_blocks, cfg.kda_heads, 128, 128, dtype=torch.float32,
+                                            device=self.device)) for _ in self.layers]
+            self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        else:
+            self.layers = [moe.MoELayer.from_logical(weights.moe_logical(cfg.seed * 1000 + i, H, F, E,
+                                                                         device=self.device),
+                                                     cfg.top_k, self.device, add_input=True) for i in self.layer_range]
         if self.first:
             g = torch.Generator(device=self.device)
             g.manual_seed(cfg.seed * 1000 + 999)
@@ -163,10 +189,11 @@ class StageModel:
         plan = Plan(-1, [Chunk("warmup", 0, n, pages, [0] * 6, True, [0] * n if self.first else None)])
         hidden = None if self.first else torch.zeros(n, self.hidden_width, dtype=torch.bfloat16, device=self.device)
         self.forward(plan, hidden)
-        ws = max(layer.workspace_bytes(self.cfg.mb_tokens) for layer in self.layers) if self.layers else 0
+        moes = [layer.moe if self.kda else layer for layer in self.layers]
+        ws = max(m.workspace_bytes(self.cfg.mb_tokens) for m in moes) if moes else 0
         shared = torch.empty(ws, dtype=torch.uint8, device=self.device) if ws else None
-        for layer in self.layers:
-            layer._ws = shared
+        for m in moes:
+            m._ws = shared
         torch.cuda.synchronize(self.device)
 
     # ---------------------------------------------------------------- the interface
@@ -201,6 +228,10 @@ class StageModel:
         h = {"qsl": pk.add(qsl.astype(np.int32)), "starts": pk.add(starts.astype(np.int32)),
              "page_ptr": pk.add(page_ptr.astype(np.int32)), "pages": pk.add(np.maximum(pages, 0).astype(np.int32)),
              "last": pk.add(last)}
+        if self.kda:
+            ks = np.array([(int(qsl[r]), int(qsl[r + 1]), int(chunks[i].state_blocks[0]), int(chunks[i].start > 0))
+                           for r, i in enumerate(order)], dtype=np.int32).reshape(-1, 4)
+            h["kda"] = pk.add(ks)
         if self.first:
             tok = np.concatenate([np.asarray(chunks[i].token_ids, dtype=np.int64) for i in order]) if R else \
                 np.zeros(0, dtype=np.int64)
@@ -218,9 +249,11 @@ class StageModel:
                                           positions.data_ptr(), slots.data_ptr(), table.data_ptr(), lib.stream_ptr())
         lib.check("ssb_stage_metadata", rc)
         return Batch(T, order, positions[:rows_out], slots[:rows_out], table[: R * width].view(R, width),
-                     v.get("tok"), v["last"], bucket, keep=[host, dev])
+                     v.get("tok"), v["last"], bucket, keep=[host, dev], kda_seqs=v.get("kda"))
 
     def run(self, batch: Batch, hidden_in: torch.Tensor | None) -> torch.Tensor:
+        if self.kda:
+            return self._run_kda(batch, hidden_in)
         T, H = batch.num_tokens, self.hidden_width
         s = lib.stream_ptr()
         if self.first:
@@ -237,16 +270,61 @@ class StageModel:
             return x
         return self._head(x, batch.last_rows)
 
+    def _run_kda(self, batch: Batch, hidden_in: torch.Tensor | None) -> torch.Tensor:
+        """KDA + MoE decoder layers on the 4-stream residual: stage 0 expands its embeddings (hc_expand), a later stage
+        starts from the received residual with a pre-only boundary (edge_recv); a stage that is not the last ends with
+        a post-only boundary into the [T, 4H] rows it sends (edge_send, ssengine/model/pp_patch.py:156-163); the last
+        stage folds the final MoE rows in, averages the streams of the returned rows and runs the head."""
+        T, H = batch.num_tokens, self.cfg.hidden
+        s = lib.stream_ptr()
+        if self.first:
+            x = torch.empty(T, H, dtype=torch.bfloat16, device=self.device)
+            lib.check("ssb_embed_rows", self._lib.ssb_embed_rows(self.embed.data_ptr(), self.cfg.vocab, H,
+                                                                 batch.token_ids.data_ptr(), T, x.data_ptr(), s))
+            res = torch.empty(T, 4, H, dtype=torch.bfloat16, device=self.device)
+            lib.check("ssb_hc_expand", self._lib.ssb_hc_expand(x.data_ptr(), T, H, res.data_ptr(), s))
+        else:
+            if hidden_in is None or tuple(hidden_in.shape) != (T, 4 * H) or hidden_in.dtype != torch.bfloat16:
+                raise ValueError(f"stage {self.stage} needs hidden_in bf16 [{T}, {4 * H}]")
+            res = hidden_in.view(T, 4, H)
+        x_prev = post = comb = None
+        for layer, (cst, rst) in zip(self.layers, self.kda_states):
+            res, x_prev, post, comb = layer.forward(res, x_prev, post, comb, batch.kda_seqs, cst, rst, self.status)
+        out = torch.empty(T, 4, H, dtype=torch.bfloat16, device=self.device)
+        if x_prev is None:
+            out.copy_(res)
+        else:
+            self._edge_post(x_prev, res, post, comb, out)
+        if not self.last:
+            return out.view(T, 4 * H)
+        n = batch.last_rows.shape[0]
+        merged = torch.empty(max(n, 1), H, dtype=torch.bfloat16, device=self.device)
+        lib.check("ssb_hc_mean", self._lib.ssb_hc_mean(out.data_ptr(), H, batch.last_rows.data_ptr(), n,
+                                                       merged.data_ptr(), s))
+        return self._head(merged[:n], torch.arange(n, dtype=torch.int64, device=self.device))
+
+    def _edge_post(self, x, res, post, comb, out) -> None:
+        """Post-only boundary: out = post * x + comb^T res (the last sub-block's rows folded into the residual)."""
+        import ctypes
+
+        b = self.layers[-1].bound_b
+        rc = self._lib.ssb_mhc(ctypes.byref(b._c), x.data_ptr(), res.data_ptr(), post.data_ptr(), comb.data_ptr(),
+                               out.data_ptr(), None, None, None, res.shape[0], lib.stream_ptr())
+        lib.check("ssb_mhc", rc)
+
     def forward(self, plan, hidden_in: torch.Tensor | None = None) -> torch.Tensor:
         return self.run(self.prepare(plan), hidden_in)
 
     def tier_ranges(self) -> list:
-        """Byte ranges of the stage's KV tensors for the capacity tiers: none yet (no KDA / DSA layers)."""
-        return []
+        """Byte ranges (device pointer, bytes) of the stage's state tensors for the capacity tiers: the KDA conv and
+        recurrent state pools of each KDA layer (none for MoE-only stages)."""
+        if not self.kda:
+            return []
+        return [(t.data_ptr(), t.numel() * t.element_size()) for pair in self.kda_states for t in pair]
 
     # ---------------------------------------------------------------- last stage
     def _head(self, x: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
-        n, H, V = rows.shape[0], self.hidden_width, self.cfg.vocab
+        n, H, V = rows.shape[0], self.cfg.hidden, self.cfg.vocab
         tokens = torch.empty(n, dtype=torch.int64, device=self.device)
         if n == 0:
             return tokens

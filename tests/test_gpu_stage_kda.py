@@ -1,0 +1,43 @@
+"""GPU checks of `StageModel` with KDA + MoE decoder layers on the 4-stream mHC residual (`layer_kind="kda"`): a model
+split into two stages (stage 0 sends its [T, 4H] rows after a post-only boundary, stage 1 starts with a pre-only
+boundary: the reference's edge_send / edge_recv, ssengine/model/pp_patch.py:156-163) returns the same tokens and
+bit-identical logits as the unsplit stage, for a first microbatch and for a second one that continues a request
+from its KDA state blocks."""
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def plans(vocab):
+    from ssengine_b200.messages import Chunk, Plan
+
+    rng = np.random.default_rng(9)
+    ta = rng.integers(0, vocab, 60).tolist()
+    tb = rng.integers(0, vocab, 30).tolist()
+    p1 = Plan(0, [Chunk("a", 0, 40, [3], [2, 0, 0, 0, 0, 0], False, ta[:40]),
+                  Chunk("b", 0, 30, [5], [3, 0, 0, 0, 0, 0], True, tb)])
+    p2 = Plan(1, [Chunk("a", 40, 20, [3], [2, 0, 0, 0, 0, 0], True, ta[40:])])
+    return p1, p2
+
+
+def test_two_stages_equal_one(cuda):
+    from ssengine_b200.stage import StageConfig, StageModel
+
+    base = dict(hidden=512, inter=256, experts=16, top_k=4, vocab=1000, num_blocks=8, mb_tokens=256, seed=4,
+                layer_kind="kda", kda_heads=2)
+    whole = StageModel(StageConfig(layer_split=(2,), **base), 0, cuda)
+    s0 = StageModel(StageConfig(layer_split=(1, 1), **base), 0, cuda)
+    s1 = StageModel(StageConfig(layer_split=(1, 1), **base), 1, cuda)
+    for plan in plans(1000):
+        t_whole = whole.forward(plan)
+        hidden = s0.forward(plan)
+        assert hidden.shape == (plan.num_tokens, 4 * 512)
+        t_split = s1.forward(plan, hidden)
+        torch.cuda.synchronize()
+        assert int(whole.status[0]) == 0 and int(s1.status[0]) == 0
+        assert torch.equal(t_whole, t_split)
+        assert torch.equal(whole.last_logits, s1.last_logits)
+        assert torch.isfinite(whole.last_logits).all()
