@@ -207,6 +207,36 @@ int ssb_sparse_mla(const void* q, int64_t T, const void* kv_cache, const int32_t
  * skipped when < 0). Replaces the fork's latent cache write (ssengine/kernels.py config 23). */
 int ssb_mla_cache_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, void* stream);
 
+/* Grouped NVFP4 GEMM (bf16 epilogue): for each tile {group g, first A row, rows, 0} of tiles int32 [num_tiles][4]
+ * (device; *num_tiles on the device, <= tile_cap), out[row, :N] = alpha[g] * A[row] . B[g * N + n] with A NVFP4
+ * [a_rows, K] (128x4 scale atoms) and B the groups' stacked NVFP4 rows [groups * N, K]; N % 256 == 0, K % 64 == 0.
+ * The per-head MLA GEMMs of a DSA layer: q absorb 64 x (k 192, n 512) and v_up 64 x (k 512, n 256) (the reference's
+ * torch.bmm, ssengine/kernels.py configs 22 and 26). */
+int ssb_nvfp4_gemm_grouped(int32_t epilogue, const uint8_t* a_codes, const uint8_t* a_sf, int64_t a_rows, int64_t K,
+                           const uint8_t* b_codes, const uint8_t* b_sf, int64_t N, int32_t groups, const float* alpha,
+                           const int32_t* tiles, const int32_t* num_tiles, int32_t tile_cap, void* out, int64_t ldo,
+                           int32_t* status, void* stream);
+
+/* y[r, :width] = x[r, :width] * rsqrt(mean(x^2) + eps) * w (bf16, row pitches ldx / ldy): the q and kv latent norms of
+ * a DSA layer on column slices of the fused down-projection (the fork's fused_q_kv_rmsnorm, config 13). */
+int ssb_rmsnorm_cols(const void* x, int64_t ldx, int32_t width, int64_t rows, const void* w, float eps, void* y,
+                     int64_t ldy, void* stream);
+
+/* In place: rotary embedding of the 64-dim slice at x + r * ldx + h * head_stride for each row r and head h < heads
+ * (pairs (i, i + 32), angle positions[r] * theta^(-i / 32)): the rope parts of the MLA query and key. */
+int ssb_rope(void* x, int64_t ldx, int32_t heads, int64_t head_stride, const int64_t* positions, int64_t rows,
+             float theta, void* stream);
+
+/* Head-major <-> row-major copies around the per-head GEMMs: to_heads: dst [heads, rows_pad, dim] (pad rows zero) =
+ * src[r, h * head_stride + :dim] (row pitch row_ld); else dst[r, h * head_stride + :dim] = src [heads, rows_pad, dim].
+ * dim, row_ld, head_stride % 8 == 0. */
+int ssb_transpose_heads(const void* src, void* dst, int64_t rows, int64_t rows_pad, int32_t heads, int32_t dim,
+                        int64_t row_ld, int64_t head_stride, int32_t to_heads, void* stream);
+
+/* out[r] = [a[r, :wa], b[r, :wb]] (bf16; widths and pitches % 8 == 0): the latent-cache rows (latent | rope key). */
+int ssb_concat_cols(const void* a, int64_t lda, int32_t wa, const void* b, int64_t ldb, int32_t wb, void* out,
+                    int64_t ldo, int64_t rows, void* stream);
+
 /* One NVFP4 MoE layer's device parameters (all pointers device memory, owned by the caller).
  * Experts 0..E-1 are routed, expert E is the shared expert (every token, weight 1). */
 typedef struct ssb_moe_layer {

@@ -9,7 +9,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libssengine_b200.so"
-SOURCES = ["gemm_nvfp4.cu", "moe_ops.cu", "capi.cu", "moe_noalloc.cu", "topk.cu", "stage.cu", "mhc.cu", "kda.cu", "edge.cu", "indexer.cu", "mla.cu", "kpool.cu"]
+SOURCES = ["gemm_nvfp4.cu", "moe_ops.cu", "capi.cu", "moe_noalloc.cu", "topk.cu", "stage.cu", "mhc.cu", "kda.cu", "edge.cu", "indexer.cu", "mla.cu", "kpool.cu", "dsa.cu"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
               "-shared"]
 

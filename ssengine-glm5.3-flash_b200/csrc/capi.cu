@@ -113,6 +113,53 @@ int ssb_nvfp4_gemm(int32_t epilogue, const uint8_t* a_codes, const uint8_t* a_sf
                                 static_cast<cudaStream_t>(stream));
 }
 
+int ssb_nvfp4_gemm_grouped(int32_t epilogue, const uint8_t* a_codes, const uint8_t* a_sf, int64_t a_rows, int64_t K,
+                           const uint8_t* b_codes, const uint8_t* b_sf, int64_t N, int32_t groups, const float* alpha,
+                           const int32_t* tiles, const int32_t* num_tiles, int32_t tile_cap, void* out, int64_t ldo,
+                           int32_t* status, void* stream) {
+  if (a_codes == nullptr || a_sf == nullptr || b_codes == nullptr || b_sf == nullptr || out == nullptr ||
+      tiles == nullptr || num_tiles == nullptr || alpha == nullptr || a_rows <= 0 || K <= 0 || N <= 0 || groups <= 0 ||
+      tile_cap <= 0 || epilogue != SSB_EPI_BF16 || ldo < N)
+    return kErrArgs;
+  if (!aligned16(a_codes) || !aligned16(b_codes) || !aligned16(out) || (K / 2) % 16 != 0) return kErrArgs;
+  ssb::GemmArgs g;
+  g.sfa = a_sf;
+  g.sfb = b_sf;
+  g.mtiles = tiles;
+  g.num_mtiles = num_tiles;
+  g.mtile_cap = tile_cap;
+  g.K = static_cast<int32_t>(K);
+  g.N = static_cast<int32_t>(N);
+  g.ncb_k = static_cast<int32_t>(ssb::sf_atom_cols(K));
+  g.alpha = alpha;
+  g.out = out;
+  g.ldo = ldo;
+  g.status = status;
+  return ssb::launch_gemm_nvfp4(epilogue, a_codes, a_rows, K / 2, b_codes, static_cast<int64_t>(groups) * N, K / 2, g,
+                                ssb::device_sm_count(), static_cast<cudaStream_t>(stream));
+}
+
+int ssb_rmsnorm_cols(const void* x, int64_t ldx, int32_t width, int64_t rows, const void* w, float eps, void* y,
+                     int64_t ldy, void* stream) {
+  return ssb::launch_rmsnorm_cols(x, ldx, width, rows, w, eps, y, ldy, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_rope(void* x, int64_t ldx, int32_t heads, int64_t head_stride, const int64_t* positions, int64_t rows,
+             float theta, void* stream) {
+  return ssb::launch_rope(x, ldx, heads, head_stride, positions, rows, theta, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_transpose_heads(const void* src, void* dst, int64_t rows, int64_t rows_pad, int32_t heads, int32_t dim,
+                        int64_t row_ld, int64_t head_stride, int32_t to_heads, void* stream) {
+  return ssb::launch_transpose_heads(src, dst, rows, rows_pad, heads, dim, row_ld, head_stride, to_heads != 0,
+                                     static_cast<cudaStream_t>(stream));
+}
+
+int ssb_concat_cols(const void* a, int64_t lda, int32_t wa, const void* b, int64_t ldb, int32_t wb, void* out,
+                    int64_t ldo, int64_t rows, void* stream) {
+  return ssb::launch_concat_cols(a, lda, wa, b, ldb, wb, out, ldo, rows, static_cast<cudaStream_t>(stream));
+}
+
 int ssb_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* ids, float* weights, void* stream) {
   if (logits == nullptr || ids == nullptr || weights == nullptr || T < 0) return kErrArgs;
   return ssb::launch_moe_route(logits, T, E, k, ids, weights, static_cast<cudaStream_t>(stream));

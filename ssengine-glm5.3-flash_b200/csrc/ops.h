@@ -173,6 +173,16 @@ struct KpoolArgs {
 };
 int launch_kpool_insert(const KpoolArgs& a, int32_t max_rows, cudaStream_t stream);
 
+// DSA block data movement (csrc/dsa.cu).
+int launch_rmsnorm_cols(const void* x, int64_t ldx, int width, int64_t rows, const void* g, float eps, void* y,
+                        int64_t ldy, cudaStream_t stream);
+int launch_rope(void* x, int64_t ldx, int heads, int64_t head_stride, const int64_t* positions, int64_t rows,
+                float theta, cudaStream_t stream);
+int launch_transpose_heads(const void* src, void* dst, int64_t rows, int64_t rows_pad, int heads, int dim,
+                           int64_t row_ld, int64_t head_stride, bool to_heads, cudaStream_t stream);
+int launch_concat_cols(const void* a, int64_t lda, int wa, const void* b, int64_t ldb, int wb, void* out, int64_t ldo,
+                       int64_t rows, cudaStream_t stream);
+
 int device_sm_count();
 
 }  // namespace ssb

@@ -194,3 +194,165 @@ class KdaDecoderLayer:
         self.bound_b(x_a, res_a, post_a, comb_a, res_b, post_b, comb_b, y, stream)
         x_b = self.moe.forward(y, stream=stream)
         return res_b, x_b, post_b, comb_b
+
+
+class Nvfp4Grouped:
+    """Per-head NVFP4 weights [heads, N, K] for the grouped GEMM (the MLA absorb / v_up bmm)."""
+
+    def __init__(self, gen: torch.Generator, heads: int, N: int, K: int, device, gs_in: float = weights.GS_X):
+        dev = torch.device(device)
+        codes = torch.randint(0, 16, (heads * N, K), generator=gen, device=dev, dtype=torch.uint8)
+        table = torch.tensor(weights.SCALE_CODES, dtype=torch.uint8, device=dev)
+        sf = table[torch.randint(0, len(weights.SCALE_CODES), (heads * N, K // 16), generator=gen, device=dev)]
+        self.heads, self.N, self.K = heads, N, K
+        self.gs_w = weights.unit_gs(K)
+        self.gs_in = gs_in
+        self.codes = layout.pack_codes(codes).contiguous()
+        self.sf = layout.sf_to_atoms(sf, K)
+        self.alpha = torch.full((heads,), 1.0 / (gs_in * self.gs_w), dtype=torch.float32, device=dev)
+        self.device = dev
+        self._lib = lib.load()
+        self._tiles = {}
+
+    def logical(self):
+        codes = layout.unpack_codes(self.codes).view(self.heads, self.N, self.K)
+        sf = layout.atoms_to_sf(self.sf, self.heads * self.N, self.K).view(self.heads, self.N, self.K // 16)
+        return codes, sf, self.gs_w
+
+    def _tile_table(self, rows_pad: int):
+        if rows_pad not in self._tiles:
+            t = [(h, h * rows_pad + 128 * m, 128, 0) for h in range(self.heads) for m in range(rows_pad // 128)]
+            tiles = torch.tensor(t, dtype=torch.int32).to(self.device)
+            self._tiles[rows_pad] = (tiles, torch.tensor([len(t)], dtype=torch.int32).to(self.device))
+        return self._tiles[rows_pad]
+
+    def __call__(self, x_heads: torch.Tensor, rows_pad: int, out: torch.Tensor, status: torch.Tensor, stream=None):
+        """x_heads bf16 [heads * rows_pad, K] (head-major) -> out bf16 [heads * rows_pad, N]."""
+        s = lib.stream_ptr(stream)
+        rows = self.heads * rows_pad
+        codes = torch.empty(rows, self.K // 2, dtype=torch.uint8, device=self.device)
+        sf = torch.zeros(rows // 128 * layout.sf_atom_cols(self.K) * 512, dtype=torch.uint8, device=self.device)
+        lib.check("ssb_nvfp4_quantize", self._lib.ssb_nvfp4_quantize(x_heads.data_ptr(), rows, self.K, self.K,
+                                                                     self.gs_in, codes.data_ptr(), self.K // 2,
+                                                                     sf.data_ptr(), s))
+        tiles, n = self._tile_table(rows_pad)
+        lib.check("ssb_nvfp4_gemm_grouped", self._lib.ssb_nvfp4_gemm_grouped(
+            lib.EPI_BF16, codes.data_ptr(), sf.data_ptr(), rows, self.K, self.codes.data_ptr(), self.sf.data_ptr(),
+            self.N, self.heads, self.alpha.data_ptr(), tiles.data_ptr(), n.data_ptr(), tiles.shape[0], out.data_ptr(),
+            self.N, status.data_ptr(), s))
+        return out
+
+
+class DsaAttention:
+    """The DSA (sparse MLA + lightning indexer) attention block of one layer. Fixed by the kernels: 64 heads, latent
+    512 + rope 64, indexer 32 heads x 128 over pools of 4 tokens, top-512 pools (2,051 tokens with the tail).
+
+    y -> a = [q_a | kv latent | k rope] (NVFP4) -> RMSNorm(q_a), RMSNorm(kv) -> q = q_b(q_a) [64 x (nope | rope)],
+    rope on the q and k rope slices -> latent cache rows [kv | k rope] at the rows' slots; q absorb (per-head NVFP4
+    GEMM nope -> 512) -> q_full [T, 64, 576]; indexer: q_idx = wq_idx(q_a) [32 x 128], [k_idx | weights | gate] =
+    idx_proj(y), pools of 4 into the pool-key cache, logits -> top-512 pools -> tokens; sparse MLA -> [T, 64, 512];
+    v_up (per-head NVFP4 GEMM 512 -> v_dim) -> o_proj. The reference's configs 12-27 (ssengine/kernels.py), with every
+    projection NVFP4."""
+
+    HEADS, LATENT, ROPE, IDX_HEADS, IDX_DIM, TOPK = 64, 512, 64, 32, 128, 512
+
+    def __init__(self, seed: int, hidden: int, device, q_lora: int = 1536, nope: int = 192, v_dim: int = 256,
+                 theta: float = 10000.0, eps: float = 1e-6):
+        dev = torch.device(device)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        H = hidden
+        self.H, self.q_lora, self.nope, self.v_dim, self.theta, self.eps = H, q_lora, nope, v_dim, theta, eps
+        self.qh = nope + self.ROPE
+        self.a_proj = Nvfp4Linear.random(g, q_lora + self.LATENT + self.ROPE, H, dev)
+        self.q_b = Nvfp4Linear.random(g, self.HEADS * self.qh, q_lora, dev)
+        self.w_uk = Nvfp4Grouped(g, self.HEADS, self.LATENT, nope, dev)
+        self.w_uv = Nvfp4Grouped(g, self.HEADS, v_dim, self.LATENT, dev)
+        self.o_proj = Nvfp4Linear.random(g, H, self.HEADS * v_dim, dev)
+        self.wq_idx = Nvfp4Linear.random(g, self.IDX_HEADS * self.IDX_DIM, q_lora, dev)
+        self.idx_proj = Nvfp4Linear.random(g, self.IDX_DIM + self.IDX_HEADS + self.IDX_DIM, H, dev)
+        self.q_norm = (torch.rand(q_lora, generator=g, device=dev) + 0.5).to(torch.bfloat16)
+        self.kv_norm = (torch.rand(self.LATENT, generator=g, device=dev) + 0.5).to(torch.bfloat16)
+        self.ape = torch.randn(4, self.IDX_DIM, generator=g, device=dev) * 0.5
+        self.scale = self.qh ** -0.5
+        self.device = dev
+        self._lib = lib.load()
+
+    def forward(self, y, positions, slots, qsl, page_table, kpool_reqs, max_rows, groups, kv_cache, pool_cache,
+                tail_ring, status, stream=None, keep: bool = False):
+        """y bf16 [T, H]; positions / slots int64 [T]; qsl int32 [R + 1]; page_table int32 [R, width] (KV pages);
+        kpool_reqs int32 [R, 4] {first row, rows, start position, tail block}; groups: the indexer's work groups
+        (int32 [G, 4]); kv_cache bf16 [pages * 128, 576], pool_cache bf16 [pages * 32, 128], tail_ring bf16
+        [blocks, 2, 4, 128] updated in place -> bf16 [T, H]."""
+        from . import indexer, mla
+
+        T, dev, s = y.shape[0], self.device, lib.stream_ptr(stream)
+        so, QL, L, RP, NH = self._lib, self.q_lora, self.LATENT, self.ROPE, self.HEADS
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        a = torch.empty(T, self.a_proj.N_pad, **bf)
+        self.a_proj(y, a, status, stream)
+        qa = torch.empty(T, QL, **bf)
+        kv_rows = torch.empty(T, L + RP, **bf)
+        lib.check("ssb_rmsnorm_cols", so.ssb_rmsnorm_cols(a.data_ptr(), a.stride(0), QL, T, self.q_norm.data_ptr(),
+                                                          self.eps, qa.data_ptr(), QL, s))
+        kvn = torch.empty(T, L, **bf)
+        lib.check("ssb_rmsnorm_cols", so.ssb_rmsnorm_cols(a[:, QL:].data_ptr(), a.stride(0), L, T,
+                                                          self.kv_norm.data_ptr(), self.eps, kvn.data_ptr(), L, s))
+        k_rope = a[:, QL + L:QL + L + RP]
+        lib.check("ssb_rope", so.ssb_rope(k_rope.data_ptr(), a.stride(0), 1, 0, positions.data_ptr(), T, self.theta, s))
+        lib.check("ssb_concat_cols", so.ssb_concat_cols(kvn.data_ptr(), L, L, k_rope.data_ptr(), a.stride(0), RP,
+                                                        kv_rows.data_ptr(), L + RP, T, s))
+        mla.cache_append(kv_rows, slots, kv_cache, stream)
+        # queries: q_b, rope on each head's rope slice, absorb of each head's nope part into the latent
+        q = torch.empty(T, NH * self.qh, **bf)
+        self.q_b(qa, q, status, stream)
+        lib.check("ssb_rope", so.ssb_rope(q[:, self.nope:].data_ptr(), q.stride(0), NH, self.qh, positions.data_ptr(),
+                                          T, self.theta, s))
+        Tp = _round(max(T, 1), 128)
+        qn = torch.empty(NH * Tp, self.nope, **bf)
+        lib.check("ssb_transpose_heads", so.ssb_transpose_heads(q.data_ptr(), qn.data_ptr(), T, Tp, NH, self.nope,
+                                                                q.stride(0), self.qh, 1, s))
+        q_lat = torch.empty(NH * Tp, L, **bf)
+        self.w_uk(qn, Tp, q_lat, status, stream)
+        q_full = torch.empty(T, NH, L + RP, **bf)
+        lib.check("ssb_transpose_heads", so.ssb_transpose_heads(q_lat.data_ptr(), q_full.data_ptr(), T, Tp, NH, L,
+                                                                NH * (L + RP), L + RP, 0, s))
+        qr = torch.empty(NH * Tp, RP, **bf)
+        lib.check("ssb_transpose_heads", so.ssb_transpose_heads(q[:, self.nope:].data_ptr(), qr.data_ptr(), T, Tp, NH,
+                                                                RP, q.stride(0), self.qh, 1, s))
+        lib.check("ssb_transpose_heads", so.ssb_transpose_heads(qr.data_ptr(), q_full[:, :, L:].data_ptr(), T, Tp, NH,
+                                                                RP, NH * (L + RP), L + RP, 0, s))
+        # indexer
+        q_idx = torch.empty(T, self.IDX_HEADS * self.IDX_DIM, **bf)
+        self.wq_idx(qa, q_idx, status, stream)
+        idx = torch.empty(T, self.idx_proj.N_pad, **bf)
+        self.idx_proj(y, idx, status, stream)
+        k_idx, gate = idx[:, :self.IDX_DIM], idx[:, self.IDX_DIM + self.IDX_HEADS:2 * self.IDX_DIM + self.IDX_HEADS]
+        w = idx[:, self.IDX_DIM:self.IDX_DIM + self.IDX_HEADS].float().contiguous()
+        indexer.kpool_insert(k_idx, gate, self.ape, kpool_reqs, max_rows, page_table, pool_cache, tail_ring, stream)
+        ldl = _round(int(page_table.shape[1]) * 32, 128)
+        logits = torch.empty(T, ldl, dtype=torch.float32, device=dev)
+        indexer.logits(q_idx.view(T, self.IDX_HEADS, self.IDX_DIM), w, pool_cache, page_table, groups, logits,
+                       status, stream)
+        ids = torch.empty(T, self.TOPK, dtype=torch.int32, device=dev)
+        indexer.topk(logits, positions, self.TOPK, ids, stream)
+        tok = torch.empty(T, 4 * self.TOPK + 3 + 5, dtype=torch.int32, device=dev)
+        indexer.expand(ids, positions, tok, stream)
+        # sparse MLA over the selected tokens, then v_up and o_proj
+        o_lat = torch.empty(T, NH, L, **bf)
+        mla.sparse_mla(q_full, kv_cache, tok, qsl, page_table, self.scale, o_lat, n_idx=4 * self.TOPK + 3,
+                       stream=stream, status=status)
+        oh = torch.empty(NH * Tp, L, **bf)
+        lib.check("ssb_transpose_heads", so.ssb_transpose_heads(o_lat.data_ptr(), oh.data_ptr(), T, Tp, NH, L, NH * L,
+                                                                L, 1, s))
+        v = torch.empty(NH * Tp, self.v_dim, **bf)
+        self.w_uv(oh, Tp, v, status, stream)
+        o_in = torch.empty(T, NH * self.v_dim, **bf)
+        lib.check("ssb_transpose_heads", so.ssb_transpose_heads(v.data_ptr(), o_in.data_ptr(), T, Tp, NH, self.v_dim,
+                                                                NH * self.v_dim, self.v_dim, 0, s))
+        out = torch.empty(T, self.H, **bf)
+        self.o_proj(o_in, out, status, stream)
+        if keep:
+            self.parts = dict(a=a, qa=qa, kvn=kvn, kv_rows=kv_rows, q=q, q_lat=q_lat, q_full=q_full, q_idx=q_idx,
+                              idx=idx, w=w, logits=logits, ids=ids, tok=tok, o_lat=o_lat, v=v, o_in=o_in)
+        return out
