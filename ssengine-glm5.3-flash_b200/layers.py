@@ -356,3 +356,41 @@ class DsaAttention:
             self.parts = dict(a=a, qa=qa, kvn=kvn, kv_rows=kv_rows, q=q, q_lat=q_lat, q_full=q_full, q_idx=q_idx,
                               idx=idx, w=w, logits=logits, ids=ids, tok=tok, o_lat=o_lat, v=v, o_in=o_in)
         return out
+
+
+class DsaDecoderLayer:
+    """One Glm5Next DSA + MoE decoder layer on the 4-stream residual: boundary A -> DSA attention -> boundary B ->
+    NVFP4 MoE (the same shape as `KdaDecoderLayer` with the sparse-attention block)."""
+
+    def __init__(self, seed: int, hidden: int, inter: int, experts: int, top_k: int, device, q_lora: int = 1536,
+                 nope: int = 192, v_dim: int = 256):
+        from . import moe
+
+        dev = torch.device(device)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        self.H = hidden
+        self.bound_a = MhcBoundary(g, hidden, dev)
+        self.attn = DsaAttention(seed + 1, hidden, dev, q_lora=q_lora, nope=nope, v_dim=v_dim)
+        self.bound_b = MhcBoundary(g, hidden, dev)
+        self.moe = moe.MoELayer.from_logical(weights.moe_logical(seed + 2, hidden, inter, experts, device=dev), top_k,
+                                             dev)
+        self.device = dev
+
+    def forward(self, res, x_prev, post_prev, comb_prev, meta: dict, caches: tuple, status, stream=None):
+        """meta: positions, slots, qsl, page_table, kpool_reqs, max_rows, groups (device tensors / ints); caches:
+        (latent cache, pool-key cache, tail ring). Returns (res after attention, MoE rows, post, comb)."""
+        T, H, dev = res.shape[0], self.H, self.device
+        f32 = dict(dtype=torch.float32, device=dev)
+        res_a = torch.empty_like(res) if x_prev is not None else res
+        post_a, comb_a = torch.empty(T, 4, **f32), torch.empty(T, 4, 4, **f32)
+        y = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        self.bound_a(x_prev, res, post_prev, comb_prev, res_a if x_prev is not None else None, post_a, comb_a, y,
+                     stream)
+        x_a = self.attn.forward(y, meta["positions"], meta["slots"], meta["qsl"], meta["page_table"],
+                                meta["kpool_reqs"], meta["max_rows"], meta["groups"], *caches, status, stream=stream)
+        res_b = torch.empty_like(res)
+        post_b, comb_b = torch.empty(T, 4, **f32), torch.empty(T, 4, 4, **f32)
+        self.bound_b(x_a, res_a, post_a, comb_a, res_b, post_b, comb_b, y, stream)
+        x_b = self.moe.forward(y, stream=stream)
+        return res_b, x_b, post_b, comb_b

@@ -13,13 +13,15 @@ Mirrors ssengine/model/stage.py:216-762 of the reference and its contract in sse
   chunk order; enqueues GPU work only, a fresh output per call;
 - `forward(plan, hidden_in) = run(prepare(plan), hidden_in)`; `tier_ranges()`.
 
-Two layer kinds (`StageConfig.layer_kind`):
-- "kda": Glm5Next KDA + MoE decoder layers on the 4-stream mHC residual (`layers.KdaDecoderLayer`: boundary, KDA
-  attention with NVFP4 projections, boundary, NVFP4 MoE); stage 0 expands its embeddings to 4 streams
-  (hc_expand), a later stage starts with a pre-only boundary on the received [T, 4H] rows (edge_recv), a stage that
-  is not the last ends with a post-only boundary (edge_send); each KDA layer owns its conv / recurrent state pools,
-  indexed by the chunk's `state_blocks[0]` (has state = the chunk continues its request). The DSA layers of the
-  hybrid split are not composed yet: a "kda" stage runs every layer of its range as a KDA layer.
+Layer kinds (`StageConfig.layer_kind`):
+- "hybrid": the Glm5Next split, decoder layers on the 4-stream mHC residual, DSA + MoE at layers 3, 7, ..., KDA + MoE
+  elsewhere (`layers.DsaDecoderLayer`, `layers.KdaDecoderLayer`: boundary, attention with NVFP4 projections,
+  boundary, NVFP4 MoE); stage 0 expands its embeddings to 4 streams (hc_expand), a later stage starts with a
+  pre-only boundary on the received [T, 4H] rows (edge_recv), a stage that is not the last ends with a post-only
+  boundary (edge_send). A KDA layer owns conv / recurrent state pools indexed by the chunk's `state_blocks[0]` (has
+  state = the chunk continues its request); a DSA layer owns its latent cache and pool-key cache (the chunk's
+  `kv_pages`) and the kpool tail ring (`state_blocks[5]`).
+- "kda": every layer KDA + MoE (no DSA layers).
 - "moe": NVFP4 MoE layers with a plain residual (x + MoE(x)), hidden [T, H], no state (BASELINE config 2's slice).
 The last stage's head: the mean of the 4 streams ("kda"), RMSNorm of each request's last row, NVFP4 lm_head GEMM
 (fp32 logits), argmax (lowest index on ties).
@@ -76,8 +78,12 @@ class StageConfig:
     seed: int = 0
     norm_eps: float = 1e-5
     layer_kind: str = "moe"            # "moe": residual NVFP4 MoE layers, hidden [T, H]; "kda": KDA + MoE decoder
-                                       # layers on the 4-stream mHC residual, hidden [T, 4H] across stage edges
+                                       # layers on the 4-stream mHC residual, hidden [T, 4H] across stage edges;
+                                       # "hybrid": as "kda" with every 4th layer (3, 7, ...) a DSA + MoE layer
     kda_heads: int = 64
+    q_lora: int = 1536
+    mla_nope: int = 192
+    mla_v_dim: int = 256
 
 
 @dataclass
@@ -92,6 +98,7 @@ class Batch:
     bucket: int | None = None
     keep: list = field(default_factory=list)   # host / device buffers that must outlive the queued work
     kda_seqs: torch.Tensor | None = None       # int32 [R, 4] {first row, end row, KDA state block, has state}, device
+    dsa: dict | None = None                    # DSA layers' metadata (positions, slots, qsl, page table, kpool, groups)
 
 
 class _Pack:
@@ -130,9 +137,10 @@ class StageModel:
         self.first, self.last = stage == 0, stage == len(split) - 1
         start = sum(split[:stage])
         self.layer_range = range(start, start + split[stage])
-        self.kda = cfg.layer_kind == "kda"
-        if cfg.layer_kind not in ("moe", "kda"):
+        self.kda = cfg.layer_kind in ("kda", "hybrid")
+        if cfg.layer_kind not in ("moe", "kda", "hybrid"):
             raise ValueError(f"layer_kind {cfg.layer_kind!r}")
+        self.is_dsa = [cfg.layer_kind == "hybrid" and i % 4 == 3 for i in self.layer_range]
         self.hidden_width = 4 * cfg.hidden if self.kda else cfg.hidden
         self.num_blocks = (num_blocks if num_blocks is not None else cfg.num_blocks) + extra_blocks
         self.cuda_graphs = cfg.cuda_graphs if cuda_graphs is None else cuda_graphs
@@ -140,15 +148,28 @@ class StageModel:
         self._lib = lib.load()
         H, F, E = cfg.hidden, cfg.inter, cfg.experts
         if self.kda:
-            from .layers import KdaDecoderLayer
+            from .layers import DsaDecoderLayer, KdaDecoderLayer
 
             P = cfg.kda_heads * 128
-            self.layers = [KdaDecoderLayer(cfg.seed * 1000 + 10 * i, H, cfg.kda_heads, F, E, cfg.top_k, self.device)
-                           for i in self.layer_range]
-            # per layer: KDA conv state [blocks, 3, 3P] bf16 and recurrent state [blocks, heads, 128, 128] fp32
-            self.kda_states = [(torch.zeros(self.num_blocks, 3, 3 * P, dtype=torch.bfloat16, device=self.device),
-                                torch.zeros(self.num_blocks, cfg.kda_heads, 128, 128, dtype=torch.float32,
-                                            device=self.device)) for _ in self.layers]
+            pages = self.num_blocks * (BLOCK_TOKENS // PAGE_TOKENS)
+            self.layers, self.kda_states = [], []
+            for i, dsa in zip(self.layer_range, self.is_dsa):
+                seed = cfg.seed * 1000 + 10 * i
+                if dsa:
+                    self.layers.append(DsaDecoderLayer(seed, H, F, E, cfg.top_k, self.device, q_lora=cfg.q_lora,
+                                                       nope=cfg.mla_nope, v_dim=cfg.mla_v_dim))
+                    # latent cache [pages * 128, 576], pool-key cache [pages * 32, 128], tail ring [blocks, 2, 4, 128]
+                    self.kda_states.append((
+                        torch.zeros(pages * PAGE_TOKENS, 576, dtype=torch.bfloat16, device=self.device),
+                        torch.zeros(pages * 32, 128, dtype=torch.bfloat16, device=self.device),
+                        torch.zeros(self.num_blocks, 2, 4, 128, dtype=torch.bfloat16, device=self.device)))
+                else:
+                    self.layers.append(KdaDecoderLayer(seed, H, cfg.kda_heads, F, E, cfg.top_k, self.device))
+                    # KDA conv state [blocks, 3, 3P] bf16 and recurrent state [blocks, heads, 128, 128] fp32
+                    self.kda_states.append((
+                        torch.zeros(self.num_blocks, 3, 3 * P, dtype=torch.bfloat16, device=self.device),
+                        torch.zeros(self.num_blocks, cfg.kda_heads, 128, 128, dtype=torch.float32,
+                                    device=self.device)))
             self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         else:
             self.layers = [moe.MoELayer.from_logical(weights.moe_logical(cfg.seed * 1000 + i, H, F, E,
@@ -232,6 +253,21 @@ class StageModel:
             ks = np.array([(int(qsl[r]), int(qsl[r + 1]), int(chunks[i].state_blocks[0]), int(chunks[i].start > 0))
                            for r, i in enumerate(order)], dtype=np.int32).reshape(-1, 4)
             h["kda"] = pk.add(ks)
+        if any(self.is_dsa):
+            from .indexer import work_groups
+
+            wp = max(1, max((len(p) for p in page_lists), default=1))
+            ptab = np.full((max(R, 1), wp), -1, dtype=np.int32)
+            for r, p in enumerate(page_lists):
+                ptab[r, :len(p)] = p
+            kreq = np.array([(int(qsl[r]), int(q_lens[r]), int(starts[r]), int(chunks[i].state_blocks[5]))
+                             for r, i in enumerate(order)], dtype=np.int32).reshape(-1, 4)
+            grp = work_groups(qsl[:-1], q_lens, starts)
+            h["dsa_qsl"] = pk.add(qsl.astype(np.int32))
+            h["dsa_pages"] = pk.add(ptab)
+            h["dsa_kreq"] = pk.add(kreq)
+            h["dsa_groups"] = pk.add(grp if grp.size else np.zeros((1, 4), np.int32))
+            dsa_max_rows, dsa_ng = int(q_lens.max()) if R else 0, int(grp.shape[0])
         if self.first:
             tok = np.concatenate([np.asarray(chunks[i].token_ids, dtype=np.int64) for i in order]) if R else \
                 np.zeros(0, dtype=np.int64)
@@ -248,8 +284,12 @@ class StageModel:
                                           v["pages"].data_ptr(), R, T, rows_out, PAGE_TOKENS, width,
                                           positions.data_ptr(), slots.data_ptr(), table.data_ptr(), lib.stream_ptr())
         lib.check("ssb_stage_metadata", rc)
+        dsa = None
+        if any(self.is_dsa):
+            dsa = dict(positions=positions[:T], slots=slots[:T], qsl=v["dsa_qsl"], page_table=v["dsa_pages"],
+                       kpool_reqs=v["dsa_kreq"], max_rows=dsa_max_rows, groups=v["dsa_groups"][:dsa_ng])
         return Batch(T, order, positions[:rows_out], slots[:rows_out], table[: R * width].view(R, width),
-                     v.get("tok"), v["last"], bucket, keep=[host, dev], kda_seqs=v.get("kda"))
+                     v.get("tok"), v["last"], bucket, keep=[host, dev], kda_seqs=v.get("kda"), dsa=dsa)
 
     def run(self, batch: Batch, hidden_in: torch.Tensor | None) -> torch.Tensor:
         if self.kda:
@@ -288,8 +328,11 @@ class StageModel:
                 raise ValueError(f"stage {self.stage} needs hidden_in bf16 [{T}, {4 * H}]")
             res = hidden_in.view(T, 4, H)
         x_prev = post = comb = None
-        for layer, (cst, rst) in zip(self.layers, self.kda_states):
-            res, x_prev, post, comb = layer.forward(res, x_prev, post, comb, batch.kda_seqs, cst, rst, self.status)
+        for layer, state, dsa in zip(self.layers, self.kda_states, self.is_dsa):
+            if dsa:
+                res, x_prev, post, comb = layer.forward(res, x_prev, post, comb, batch.dsa, state, self.status)
+            else:
+                res, x_prev, post, comb = layer.forward(res, x_prev, post, comb, batch.kda_seqs, *state, self.status)
         out = torch.empty(T, 4, H, dtype=torch.bfloat16, device=self.device)
         if x_prev is None:
             out.copy_(res)

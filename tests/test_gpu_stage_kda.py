@@ -41,3 +41,29 @@ def test_two_stages_equal_one(cuda):
         assert torch.equal(t_whole, t_split)
         assert torch.equal(whole.last_logits, s1.last_logits)
         assert torch.isfinite(whole.last_logits).all()
+
+
+def test_hybrid_two_stages_equal_one(cuda):
+    """The hybrid split (layer 3 DSA + MoE, the others KDA + MoE): two stages reproduce one, across a continuation."""
+    from ssengine_b200.messages import Chunk, Plan
+    from ssengine_b200.stage import StageConfig, StageModel
+
+    base = dict(hidden=512, inter=256, experts=16, top_k=4, vocab=1000, num_blocks=8, mb_tokens=256, seed=6,
+                layer_kind="hybrid", kda_heads=2, q_lora=256, mla_nope=64)
+    whole = StageModel(StageConfig(layer_split=(4,), **base), 0, cuda)
+    s0 = StageModel(StageConfig(layer_split=(2, 2), **base), 0, cuda)
+    s1 = StageModel(StageConfig(layer_split=(2, 2), **base), 1, cuda)
+    assert whole.is_dsa == [False, False, False, True] and s1.is_dsa == [False, True]
+    rng = np.random.default_rng(10)
+    ta, tb = rng.integers(0, 1000, 170).tolist(), rng.integers(0, 1000, 30).tolist()
+    plans = [Plan(0, [Chunk("a", 0, 130, [3, 4], [2, 0, 0, 0, 0, 2], False, ta[:130]),
+                      Chunk("b", 0, 30, [5], [3, 0, 0, 0, 0, 3], True, tb)]),
+             Plan(1, [Chunk("a", 130, 40, [3, 4], [2, 0, 0, 0, 0, 2], True, ta[130:])])]
+    for plan in plans:
+        t_whole = whole.forward(plan)
+        t_split = s1.forward(plan, s0.forward(plan))
+        torch.cuda.synchronize()
+        assert int(whole.status[0]) == 0 and int(s1.status[0]) == 0
+        assert torch.equal(t_whole, t_split)
+        assert torch.equal(whole.last_logits, s1.last_logits)
+        assert torch.isfinite(whole.last_logits).all()
