@@ -25,6 +25,8 @@ def sparse_mla(q, kv, indices, pages, scale):
     for i in range(q.shape[0]):
         sel = np.asarray(indices[i])
         sel = sel[sel >= 0]
+        sel = sel[(sel // 128 < len(pages))]
+        sel = sel[np.asarray(pages, np.int64)[sel // 128] >= 0]          # a token on a missing page is not read
         if sel.size == 0:
             continue
         k = kv[slot_of(pages, sel)]                       # [m, 576]

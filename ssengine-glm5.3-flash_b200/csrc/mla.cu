@@ -10,8 +10,10 @@
 // One CTA (4 warps) per query row; tcgen05 with the 64 heads as M = 64 (accumulator rows in lanes 0-15 of each
 // 32-lane sub-partition; a second M = 64 accumulator sits in lanes 16-31 of the same columns):
 //   Q [64 x 576] bf16 stays in shared memory (TMA, 9 K-major 128-byte-swizzled chunks);
-//   per block of 64 selected tokens, their rows are gathered by cp.async into 9 chunks [64 tokens x 64 dims] with the
-//   same swizzle, double-buffered (block b+1 lands while block b is used);
+//   the index columns are taken in blocks of 64; blocks without a selected token are skipped (listed up front), so a
+//   row near its request's start costs its own tokens, not the full top-k width;
+//   per block, the selected tokens' rows are gathered by cp.async into 9 chunks [64 tokens x 64 dims] with the same
+//   swizzle (missing tokens zero-filled without a read), double-buffered (block b+1 lands while block b is used);
 //   S [64 x 64] = Q K^T as two N = 32 halves (tokens 0-31 in lanes 0-15, 32-63 in lanes 16-31 of columns 0-31;
 //   2 x 36 MMAs kind::f16); softmax by all 128 threads (a head row's two halves combine max and sum with a shuffle;
 //   exp2, scale folded) with the running max kept stale until a block raises it by more than 2^8, so the accumulator
@@ -36,8 +38,11 @@ constexpr int kOffKv = kQBytes;                          // 2 buffers
 constexpr int kOffP = kOffKv + 2 * kKvBytes;             // P [64 x 64] bf16, K-major swizzled
 constexpr int kOffSlots = kOffP + kChunk;                // int64 [2][64]
 constexpr int kOffBar = kOffSlots + 2 * kBlk * 8;        // bar_q, bar_s, bar_pv, bar_drain
-constexpr int kOffMisc = kOffBar + 32;                   // tmem slot, abort flag
-constexpr int kMlaSmem = kOffMisc + 16 + 1024;           // + alignment slack
+constexpr int kOffMisc = kOffBar + 32;                   // tmem slot, abort flag, block count
+constexpr int kMaxBlocks = 256;                          // n_idx <= 16384
+constexpr int kOffMask = kOffMisc + 16;                  // uint64 [4]: blocks holding a selected token
+constexpr int kOffList = kOffMask + 32;                  // uint16 [256]: those blocks in order
+constexpr int kMlaSmem = kOffList + 2 * kMaxBlocks + 1024;   // + alignment slack
 constexpr uint32_t kSCol = 0, kOCol = 256;
 
 SSB_DEVICE void cp_async16(uint32_t dst, const void* src, bool valid) {
@@ -54,12 +59,13 @@ SSB_DEVICE void drain_bar(uint32_t bar, uint32_t parity) {
   }
 }
 
-// Block b's 64 token rows -> the 9 chunks of a buffer (a missing token reads row 0; its score is masked): thread t
-// copies half (t & 1) of row t >> 1, four 16-byte pieces per chunk, all offsets fixed at compile time.
+// Block b's 64 token rows -> the 9 chunks of a buffer (a missing token is zero-filled without a read; its score is
+// masked): thread t copies half (t & 1) of row t >> 1, four 16-byte pieces per chunk, offsets fixed at compile time.
 SSB_DEVICE void gather_block(uint32_t kvb, const __nv_bfloat16* kv, const int64_t* slot_of, int tid) {
   const int r = tid >> 1, hi = tid & 1;
   const int64_t slot = slot_of[r];
-  const __nv_bfloat16* src = kv + (slot >= 0 ? slot : 0) * kDq + hi * 32;
+  const bool valid = slot >= 0;
+  const __nv_bfloat16* src = kv + (valid ? slot : 0) * kDq + hi * 32;
   const uint32_t dst = kvb + r * 128;
   const int sw = r & 7;
 #pragma unroll
@@ -67,7 +73,7 @@ SSB_DEVICE void gather_block(uint32_t kvb, const __nv_bfloat16* kv, const int64_
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       const int j = 4 * hi + jj;
-      cp_async16(dst + ch * kChunk + ((j ^ sw) << 4), src + ch * 64 + jj * 8, true);
+      cp_async16(dst + ch * kChunk + ((j ^ sw) << 4), src + ch * 64 + jj * 8, valid);
     }
 }
 
@@ -92,23 +98,26 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   }
   const int32_t* pages = a.table + (int64_t)lo * a.width;
   const int32_t* idx = a.indices + t * a.ld_idx;
-  const int nblk = (a.n_idx + kBlk - 1) / kBlk;
-  auto fill_slots = [&](int b) {
+  unsigned long long* mask = reinterpret_cast<unsigned long long*>(smem + kOffMask);
+  uint16_t* blist = reinterpret_cast<uint16_t*>(smem + kOffList);
+  volatile int32_t* nblk_s = reinterpret_cast<volatile int32_t*>(smem + kOffMisc + 8);
+  auto slot_at = [&](int j) -> int64_t {
+    const int32_t pos = idx[j];
+    if (pos >= 0 && (pos >> 7) < a.width) {
+      const int32_t pg = pages[pos >> 7];
+      if (pg >= 0) return (int64_t)pg * 128 + (pos & 127);
+    }
+    return -1;
+  };
+  // list entry i (the i-th block of 64 index columns that holds a selected token) -> slot buffer (i & 1)
+  auto fill_slots = [&](int i) {
     if (tid < kBlk) {
-      const int j = b * kBlk + tid;
-      int64_t sl = -1;
-      if (j < a.n_idx) {
-        const int32_t pos = idx[j];
-        if (pos >= 0 && (pos >> 7) < a.width) {
-          const int32_t pg = pages[pos >> 7];
-          if (pg >= 0) sl = (int64_t)pg * 128 + (pos & 127);
-        }
-      }
-      slots[(b & 1) * kBlk + tid] = sl;
+      const int j = blist[i] * kBlk + tid;
+      slots[(i & 1) * kBlk + tid] = j < a.n_idx ? slot_at(j) : -1;
     }
   };
 
-  if (tid == 0) {
+  if (tid == 0) {                                       // Q lands while the index columns are scanned
     mbar_init(bar_q, 1);
     mbar_init(bar_s, 1);
     mbar_init(bar_pv, 1);
@@ -119,6 +128,21 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     mbar_arrive_expect_tx(bar_q, kQBytes);
     for (int c = 0; c < kNChunks; ++c) tma_load_2d(sbase + kOffQ + c * kChunk, &mq, 64 * c, (int32_t)(t * kHeads), bar_q);
   }
+  // blocks of index columns without a selected token are skipped: mark the others, then list them in order
+  if (tid < 4) mask[tid] = 0ull;
+  __syncthreads();
+  for (int j = tid; j < a.n_idx; j += kMlaThreads)
+    if (slot_at(j) >= 0) atomicOr(mask + (j >> 12), 1ull << ((j >> 6) & 63));
+  __syncthreads();
+  if (tid == 0) {
+    int n = 0;
+    for (int w = 0; w < 4; ++w)
+      for (unsigned long long m = mask[w]; m; m &= m - 1) blist[n++] = static_cast<uint16_t>(64 * w + __ffsll(m) - 1);
+    *nblk_s = n;
+  }
+  __syncthreads();
+  const int nblk = *nblk_s;
+
   if (warp == 0) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
@@ -258,6 +282,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   // ---- normalise and store (lanes 0-15: dims 0-255 of row 16 warp + lane; lanes 16-31: dims 256-511) ----
   const bool have = ok && nblk > 0;
   if (have) mbar_wait(bar_pv, (nblk - 1) & 1, abort_flag, a.status);
+  if (nblk == 0 && tid == 0) mbar_wait(bar_q, 0, abort_flag, a.status);   // no copy in flight at exit
   __syncthreads();
   if (*abort_flag) ok = false;
   tc_fence_after();
@@ -309,7 +334,8 @@ __global__ void mla_append_kernel(const __nv_bfloat16* src, int64_t lds, const i
 
 int launch_sparse_mla(const MlaArgs& a, cudaStream_t stream) {
   if (a.q == nullptr || a.kv == nullptr || a.indices == nullptr || a.qsl == nullptr || a.table == nullptr ||
-      a.out == nullptr || a.T < 0 || a.R <= 0 || a.width <= 0 || a.n_idx < 0 || a.ld_idx < a.n_idx ||
+      a.out == nullptr || a.T < 0 || a.R <= 0 || a.width <= 0 || a.n_idx < 0 || a.n_idx > kMaxBlocks * kBlk ||
+      a.ld_idx < a.n_idx ||
       ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.kv) | reinterpret_cast<uintptr_t>(a.out)) &
        15))
     return kErrArgs;

@@ -80,3 +80,42 @@ def test_cache_append(cuda):
         if s[t] >= 0:
             assert torch.equal(c[s[t]], x[t])
     assert int((c.abs().sum(1) > 0).sum()) == 49
+
+
+def test_sparse_mla_expanded_layout(cuda):
+    """The indexer's expanded layout at the full width (512 pools x 4 tokens + 3 tail columns): pool tokens first,
+    -1 padding up to column 2048, the incomplete pool's tokens after it. Rows near a request's start select a few
+    blocks of columns (one holding only tail tokens), long rows all 33; a page missing from the table drops its
+    tokens."""
+    from ssengine_b200 import mla
+
+    rng = np.random.default_rng(5)
+    K, n_idx = 512, 4 * 512 + 3
+    positions = [0, 2, 3, 6, 70, 1000, 2046, 2100, 5000, 9001]
+    T = len(positions)
+    width = max(positions) // 128 + 1
+    table = (rng.permutation(width + 3)[:width] + 1).astype(np.int32)[None, :]
+    table[0, 3] = -1                                               # tokens 384-511 unreadable
+    slots = (int(table.max()) + 1) * 128
+    kv = rng.standard_normal((slots, 576)).astype(np.float32)
+    q = rng.standard_normal((T, 64, 576)).astype(np.float32)
+    idx = np.full((T, n_idx), -1, np.int32)
+    for r, pos in enumerate(positions):
+        n_pools = (pos + 1) // 4
+        pools = np.sort(rng.choice(n_pools, size=min(K, n_pools), replace=False)) if n_pools else np.zeros(0, int)
+        for i, p in enumerate(pools):
+            idx[r, 4 * i:4 * i + 4] = 4 * p + np.arange(4)
+        tail0 = ((pos + 1) // 4) * 4
+        idx[r, 4 * K:4 * K + (pos + 1 - tail0)] = np.arange(tail0, pos + 1)
+    qsl = np.array([0, T], np.int32)
+    bf = lambda a: torch.from_numpy(a).to(torch.bfloat16).to(cuda)
+    qd, kvd = bf(q), bf(kv)
+    out = torch.full((T, 64, 512), float("nan"), dtype=torch.bfloat16, device=cuda)
+    mla.sparse_mla(qd, kvd, torch.from_numpy(idx).to(cuda), torch.from_numpy(qsl).to(cuda),
+                   torch.from_numpy(table).to(cuda), SCALE, out, n_idx=n_idx)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    want = omla.sparse_mla(qd.float().cpu().numpy(), kvd.float().cpu().numpy(), idx, table[0], SCALE)
+    for r in range(T):
+        err = np.linalg.norm(got[r] - want[r]) / np.linalg.norm(want[r])
+        assert err < 1e-2, (positions[r], err)
