@@ -156,6 +156,17 @@ int ssb_kda_prefill(const ssb_kda_layer* layer, const void* x, int64_t ldx, cons
                     const void* beta, int64_t ldb, int64_t T, const int32_t* seqs, int64_t R, void* out, int64_t ldo,
                     int32_t* status, void* stream);
 
+/* Device bytes of the chunk workspace of ssb_kda_prefill_ws for `heads` heads, T rows and R sequences whose rows sum
+ * to at most T (one 72.5 KB image per 64-row chunk and head, plus a header); -1 on bad arguments. */
+int64_t ssb_kda_workspace_bytes(int32_t heads, int64_t T, int64_t R);
+
+/* ssb_kda_prefill with a caller-owned workspace (16-byte aligned, >= ssb_kda_workspace_bytes; returns 3 when smaller),
+ * so that the call allocates nothing; ssb_kda_prefill allocates and frees one on `stream`. Sequences whose rows sum
+ * above T, or that reach outside [0, T), are rejected on the device (status 6 or 1; their state blocks untouched). */
+int ssb_kda_prefill_ws(const ssb_kda_layer* layer, const void* x, int64_t ldx, const void* g, int64_t ldg,
+                       const void* beta, int64_t ldb, int64_t T, const int32_t* seqs, int64_t R, void* out,
+                       int64_t ldo, void* workspace, int64_t ws_bytes, int32_t* status, void* stream);
+
 /* The short conv alone: q, k, v bf16 [T, H * 128] each (contiguous) and the conv state blocks updated; rows outside
  * every sequence are written as 0. Replaces `kda_conv.conv_qkv` (ssengine/model/kda_conv.py:146-164). */
 int ssb_kda_conv(const ssb_kda_layer* layer, const void* x, int64_t ldx, int64_t T, const int32_t* seqs, int64_t R,

@@ -249,9 +249,9 @@ static bool kda_args(const ssb_kda_layer* L, const void* x, int64_t ldx, const i
   return true;
 }
 
-int ssb_kda_prefill(const ssb_kda_layer* layer, const void* x, int64_t ldx, const void* g, int64_t ldg,
-                    const void* beta, int64_t ldb, int64_t T, const int32_t* seqs, int64_t R, void* out, int64_t ldo,
-                    int32_t* status, void* stream) {
+int ssb_kda_prefill_ws(const ssb_kda_layer* layer, const void* x, int64_t ldx, const void* g, int64_t ldg,
+                       const void* beta, int64_t ldb, int64_t T, const int32_t* seqs, int64_t R, void* out,
+                       int64_t ldo, void* workspace, int64_t ws_bytes, int32_t* status, void* stream) {
   ssb::KdaArgs a;
   if (T < 0 || !kda_args(layer, x, ldx, seqs, R, a)) return kErrArgs;
   a.g = static_cast<const __nv_bfloat16*>(g);
@@ -262,8 +262,21 @@ int ssb_kda_prefill(const ssb_kda_layer* layer, const void* x, int64_t ldx, cons
   a.ldo = ldo;
   a.status = status;
   a.T = T;
-  if (ldg < a.P || ldb < a.H) return kErrArgs;
+  a.ws = static_cast<uint8_t*>(workspace);
+  a.ws_bytes = ws_bytes;
+  if (ldg < a.P || ldb < a.H || (workspace != nullptr && ws_bytes <= 0)) return kErrArgs;
   return ssb::launch_kda_prefill(a, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_kda_prefill(const ssb_kda_layer* layer, const void* x, int64_t ldx, const void* g, int64_t ldg,
+                    const void* beta, int64_t ldb, int64_t T, const int32_t* seqs, int64_t R, void* out, int64_t ldo,
+                    int32_t* status, void* stream) {
+  return ssb_kda_prefill_ws(layer, x, ldx, g, ldg, beta, ldb, T, seqs, R, out, ldo, nullptr, 0, status, stream);
+}
+
+int64_t ssb_kda_workspace_bytes(int32_t heads, int64_t T, int64_t R) {
+  if (heads <= 0 || T < 0 || R < 0 || R > (1 << 30)) return -1;
+  return ssb::kda_workspace_bytes(heads, T, static_cast<int>(R));
 }
 
 int ssb_kda_conv(const ssb_kda_layer* layer, const void* x, int64_t ldx, int64_t T, const int32_t* seqs, int64_t R,

@@ -100,6 +100,13 @@ SSB_DEVICE void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_
                "l"(src), "r"(bytes), "r"(bar)
                : "memory");
 }
+// shared -> global bulk store (16-byte aligned addresses, size a multiple of 16), completed by bulk_wait0
+SSB_DEVICE void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
+SSB_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+SSB_DEVICE void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ---- tcgen05 ------------------------------------------------------------------------------------------------------
 SSB_DEVICE void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {

@@ -110,7 +110,11 @@ struct KdaArgs {
   int64_t ldo = 0;
   int32_t* status = nullptr;           // device status word (bounded copy waits)
   int64_t T = 0;                       // rows of x, g, beta, out
+  uint8_t* ws = nullptr;               // chunk workspace (kda_workspace_bytes); null: allocated on the stream
+  int64_t ws_bytes = 0;
+  int64_t ws_slots = 0;                // chunk slots the workspace holds (set by the launcher)
 };
+int64_t kda_workspace_bytes(int H, int64_t T, int R);
 int launch_kda_prefill(const KdaArgs& a, cudaStream_t stream);
 
 // 2D tensor map (no swizzle) over [rows, width] elements of `dtype` (a CUtensorMapDataType) with row pitch ld_bytes;

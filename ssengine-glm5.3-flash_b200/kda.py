@@ -19,6 +19,28 @@ from . import lib
 
 HEAD_DIM = 128
 
+_SCRATCH: dict = {}
+
+
+def workspace_bytes(heads: int, T: int, R: int) -> int:
+    """Device bytes of the chunk workspace of one prefill call (`ssb_kda_workspace_bytes`)."""
+    n = lib.load().ssb_kda_workspace_bytes(heads, T, R)
+    if n < 0:
+        raise ValueError(f"bad KDA workspace query: heads={heads}, T={T}, R={R}")
+    return int(n)
+
+
+def scratch(device, nbytes: int) -> torch.Tensor:
+    """A per-device uint8 workspace of at least `nbytes`, grown on demand and reused by every call on the device
+    (calls on one stream only, as a stage's layers run)."""
+    dev = torch.device(device)
+    key = (dev.type, dev.index)
+    t = _SCRATCH.get(key)
+    if t is None or t.numel() < nbytes:
+        t = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+        _SCRATCH[key] = t
+    return t
+
 
 def seq_table(seqs, device) -> torch.Tensor:
     """[(first row, end row, state block, has initial state)] -> int32 [R, 4] on `device` (the reference's
@@ -54,21 +76,27 @@ class KdaLayer:
                              rec_state.data_ptr(), rec_state.stride(0))
 
     def prefill(self, qkv: torch.Tensor, g: torch.Tensor, beta: torch.Tensor, out: torch.Tensor, seqs: torch.Tensor,
-                conv_state: torch.Tensor, rec_state: torch.Tensor, stream=None, status: torch.Tensor | None = None
-                ) -> None:
+                conv_state: torch.Tensor, rec_state: torch.Tensor, stream=None, status: torch.Tensor | None = None,
+                workspace: torch.Tensor | None = None) -> None:
         """qkv bf16 [T, >= 3P] (q | k | v first), g bf16 [T, >= P] raw gate, beta bf16 [T, >= H] raw; writes out bf16
         [T, >= P] for the rows of `seqs` (int32 [R, 4] on the device) and updates both state pages in place. `status`
-        (int32 [1] on the device) receives 4 if a bounded copy wait gave up."""
+        (int32 [1] on the device) receives 4 if a bounded copy wait gave up. `workspace`: uint8 device tensor of at
+        least `workspace_bytes(heads, T, R)` (default: the device's shared scratch)."""
         so = lib.load()
         T = qkv.shape[0]
         for t in (qkv, g, beta, out):
             assert t.dtype == torch.bfloat16 and t.stride(1) == 1 and t.shape[0] >= T
         assert seqs.dtype == torch.int32 and seqs.is_contiguous()
+        need = workspace_bytes(self.heads, T, seqs.shape[0])
+        if workspace is None:
+            workspace = scratch(qkv.device, need)
+        assert workspace.dtype == torch.uint8 and workspace.is_contiguous() and workspace.numel() >= need
         L = self.c_struct(conv_state, rec_state)
-        rc = so.ssb_kda_prefill(ctypes.byref(L), qkv.data_ptr(), qkv.stride(0), g.data_ptr(), g.stride(0),
-                                beta.data_ptr(), beta.stride(0), T, seqs.data_ptr(), seqs.shape[0], out.data_ptr(),
-                                out.stride(0), None if status is None else status.data_ptr(), lib.stream_ptr(stream))
-        lib.check("ssb_kda_prefill", rc)
+        rc = so.ssb_kda_prefill_ws(ctypes.byref(L), qkv.data_ptr(), qkv.stride(0), g.data_ptr(), g.stride(0),
+                                   beta.data_ptr(), beta.stride(0), T, seqs.data_ptr(), seqs.shape[0], out.data_ptr(),
+                                   out.stride(0), workspace.data_ptr(), workspace.numel(),
+                                   None if status is None else status.data_ptr(), lib.stream_ptr(stream))
+        lib.check("ssb_kda_prefill_ws", rc)
 
     def conv_qkv(self, qkv: torch.Tensor, seqs: torch.Tensor, conv_state: torch.Tensor, rec_state: torch.Tensor,
                  stream=None):

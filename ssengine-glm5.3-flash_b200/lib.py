@@ -17,7 +17,8 @@ LIB_PATH = PKG / "libssengine_b200.so"
 EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_gemm", "ssb_moe_route",
            "ssb_moe_workspace_bytes", "ssb_moe_workspace_offsets", "ssb_moe_forward", "ssb_moe_forward_profiled",
            "ssb_moe_route_permute_noalloc", "ssb_topk_canonical", "ssb_stage_metadata", "ssb_embed_rows",
-           "ssb_rmsnorm", "ssb_argmax_rows", "ssb_mhc", "ssb_kda_prefill", "ssb_kda_conv",
+           "ssb_rmsnorm", "ssb_argmax_rows", "ssb_mhc", "ssb_kda_prefill", "ssb_kda_prefill_ws",
+           "ssb_kda_workspace_bytes", "ssb_kda_conv",
            "ssb_ipc_export", "ssb_ipc_open", "ssb_ipc_close", "ssb_flag_wait", "ssb_flag_write", "ssb_p2p_copy",
            "ssb_indexer_logits", "ssb_indexer_expand", "ssb_sparse_mla", "ssb_mla_cache_append",
            "ssb_kpool_insert", "ssb_gated_rmsnorm", "ssb_hc_expand", "ssb_hc_mean",
@@ -89,6 +90,9 @@ _SIGS = {
     "ssb_mhc": ([ctypes.POINTER(MhcParamsC), _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P], ctypes.c_int),
     "ssb_kda_prefill": ([ctypes.POINTER(KdaLayerC), _P, _I64, _P, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _P],
                         ctypes.c_int),
+    "ssb_kda_prefill_ws": ([ctypes.POINTER(KdaLayerC), _P, _I64, _P, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _P,
+                            _I64, _P, _P], ctypes.c_int),
+    "ssb_kda_workspace_bytes": ([ctypes.c_int32, _I64, _I64], ctypes.c_int64),
     "ssb_kda_conv": ([ctypes.POINTER(KdaLayerC), _P, _I64, _I64, _P, _I64, _P, _P, _P, _P], ctypes.c_int),
     "ssb_ipc_export": ([_P, _P, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "ssb_ipc_open": ([_P, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),

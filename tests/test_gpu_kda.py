@@ -126,3 +126,75 @@ def test_split_request_equals_whole(cuda):
     want, _, _ = ok.prefill(d["x"][:, :3 * H * D], d["w"], d["cst"], d["g"], d["beta"], d["a_log"], d["dtb"], -5.0,
                             d["rst"], [(0, T, 1, 1)], H, D)
     assert rel(split, want) < 2e-2
+
+
+def test_workspace_paths_agree(cuda):
+    """The caller-workspace entry (exact size), the shared scratch and the self-allocating `ssb_kda_prefill` give the
+    same bits; a workspace one byte short is refused (code 3) before anything runs."""
+    import ctypes
+
+    from ssengine_b200 import lib
+    from ssengine_b200.kda import seq_table, workspace_bytes
+
+    H = 2
+    rng = np.random.default_rng(21)
+    T = 470
+    d = make(rng, T, H, 8)
+    outs = []
+    for mode in ("exact", "scratch", "alloc"):
+        L, dev = layer(cuda, d)
+        out = torch.zeros(T, H * D, dtype=torch.bfloat16, device=cuda)
+        st = seq_table(SEQS, cuda)
+        if mode == "alloc":
+            so = lib.load()
+            C = L.c_struct(dev["cst"], dev["rst"])
+            rc = so.ssb_kda_prefill(ctypes.byref(C), dev["x"].data_ptr(), dev["x"].stride(0), dev["g"].data_ptr(),
+                                    dev["g"].stride(0), dev["beta"].data_ptr(), dev["beta"].stride(0), T,
+                                    st.data_ptr(), st.shape[0], out.data_ptr(), out.stride(0), None,
+                                    lib.stream_ptr(None))
+            assert rc == 0
+        else:
+            ws = torch.empty(workspace_bytes(H, T, len(SEQS)), dtype=torch.uint8, device=cuda) if mode == "exact" \
+                else None
+            L.prefill(dev["x"], dev["g"], dev["beta"], out, st, dev["cst"], dev["rst"], workspace=ws)
+        torch.cuda.synchronize()
+        outs.append((out.cpu(), dev["rst"].cpu(), dev["cst"].cpu()))
+    for o, r, c in outs[1:]:
+        assert torch.equal(o, outs[0][0]) and torch.equal(r, outs[0][1]) and torch.equal(c, outs[0][2])
+
+    L, dev = layer(cuda, d)
+    st = seq_table(SEQS, cuda)
+    short = torch.empty(workspace_bytes(H, T, len(SEQS)) - 1, dtype=torch.uint8, device=cuda)
+    so = lib.load()
+    C = L.c_struct(dev["cst"], dev["rst"])
+    out = torch.zeros(T, H * D, dtype=torch.bfloat16, device=cuda)
+    rc = so.ssb_kda_prefill_ws(ctypes.byref(C), dev["x"].data_ptr(), dev["x"].stride(0), dev["g"].data_ptr(),
+                               dev["g"].stride(0), dev["beta"].data_ptr(), dev["beta"].stride(0), T, st.data_ptr(),
+                               st.shape[0], out.data_ptr(), out.stride(0), short.data_ptr(), short.numel(), None,
+                               lib.stream_ptr(None))
+    assert rc == 3
+
+
+def test_rejected_sequences_leave_state(cuda):
+    """Sequences whose chunks exceed the workspace (rows summing above T) raise status 6, a sequence reaching past T
+    raises 1; their state blocks stay as they were while the valid sequence is computed as usual."""
+    from ssengine_b200.kda import seq_table
+
+    H = 2
+    rng = np.random.default_rng(23)
+    T = 130
+    d = make(rng, T, H, 4)
+    for seqs, code in (([(0, 130, 1, 1), (0, 130, 2, 1)], 6), ([(0, 130, 1, 1), (100, 140, 2, 1)], 1)):
+        L, dev = layer(cuda, d)
+        out = torch.zeros(T, H * D, dtype=torch.bfloat16, device=cuda)
+        status = torch.zeros(1, dtype=torch.int32, device=cuda)
+        L.prefill(dev["x"], dev["g"], dev["beta"], out, seq_table(seqs, cuda), dev["cst"], dev["rst"], status=status)
+        torch.cuda.synchronize()
+        assert int(status.item()) == code
+        rst, cst = dev["rst"].cpu().numpy(), dev["cst"].float().cpu().numpy()
+        np.testing.assert_array_equal(rst[2], d["rst"][2])
+        np.testing.assert_array_equal(cst[2], d["cst"][2])
+        want, _, wrst = ok.prefill(d["x"][:, :3 * H * D], d["w"], d["cst"], d["g"], d["beta"], d["a_log"], d["dtb"],
+                                   -5.0, d["rst"], [(0, 130, 1, 1)], H, D)
+        assert rel(out.float().cpu().numpy(), want) < 2e-2
+        assert rel(rst[1], wrst[1]) < 2e-2
