@@ -202,21 +202,33 @@ int ssb_kpool_insert(const void* k, const void* gate, int64_t ld, const float* a
 int ssb_indexer_expand(const int32_t* pool_ids, int64_t ldp, int32_t k, const int64_t* positions, int64_t rows,
                        int32_t* out, int64_t ldo, void* stream);
 
-/* Sparse MLA prefill of one DSA layer (absorbed latent attention): out bf16 [T, 64, 512], row t, head h = softmax over
- * the row's selected tokens of scale * q[t, h, :] . kv[s, :], times kv[s, 0:512]; q bf16 [T, 64, 576] (latent 512 +
- * rope 64); kv_cache bf16 [slots, 576]; indices int32 [T, ld_idx], the first n_idx columns used (token positions of
- * the row's request, -1 = none: the indexer's expanded selection); the request of row t is found in qsl int32 [R + 1]
- * (first row of each request, ascending, qsl[0] = 0); slot of position p = page_table[r * width + p / 128] * 128 +
- * p % 128. A row with no selected token gets zeros. status (device int32, may be NULL) receives 4 if a bounded wait
- * expired. Replaces the TRTLLM sparse MLA (ssengine/kernels.py config 25,
- * split at 32,768 rows ssengine/model/pp_patch.py:643-672). */
+/* Sparse MLA prefill of one DSA layer (absorbed latent attention) over the FP8 latent cache: out bf16 [T, 64, 512],
+ * row t, head h = bmm2_scale * softmax over the row's selected tokens of bmm1_scale * q[t, h, :] . kv[s, :], times
+ * kv[s, 0:512]; q e4m3 [T, 64, 576] (latent 512 + rope 64, 16-byte aligned); kv_cache e4m3 [slots, 576];
+ * bmm1_scale = softmax scale * q_scale * k_scale, bmm2_scale = k_scale (the per-tensor scales of the FP8 query and
+ * cache); indices int32 [T, ld_idx], the first n_idx (<= 2304) columns used (token positions of the row's request,
+ * -1 = none: the indexer's expanded selection); the request of row t is found in qsl int32 [R + 1] (first row of each
+ * request, ascending, qsl[0] = 0); slot of position p = page_table[r * width + p / 128] * 128 + p % 128 (a negative
+ * page drops the token). The softmax weights enter the P.V product as e4m3 (like the reference's FP8 kernel). A row
+ * with no selected token gets zeros. status (device int32, may be NULL) receives 4 if a bounded wait expired.
+ * Replaces the TRTLLM sparse MLA with FP8 q and cache (ssengine/kernels.py config 25, bmm1 / bmm2 scales as vLLM's
+ * FlashInfer sparse MLA backend passes them; split at 32,768 rows ssengine/model/pp_patch.py:643-672). */
 int ssb_sparse_mla(const void* q, int64_t T, const void* kv_cache, const int32_t* indices, int64_t ld_idx,
-                   int32_t n_idx, const int32_t* qsl, int32_t R, const int32_t* page_table, int64_t width, float scale,
-                   void* out, int32_t* status, void* stream);
+                   int32_t n_idx, const int32_t* qsl, int32_t R, const int32_t* page_table, int64_t width,
+                   float bmm1_scale, float bmm2_scale, void* out, int32_t* status, void* stream);
 
 /* MLA cache append: row t of src bf16 [T, 576] (row pitch lds elements, % 8 == 0) into kv_cache row slots[t] (int64,
- * skipped when < 0). Replaces the fork's latent cache write (ssengine/kernels.py config 23). */
-int ssb_mla_cache_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, void* stream);
+ * skipped when < 0) as e4m3(x / k_scale), round to nearest even, saturating to +-448 (576 bytes a row). Replaces the
+ * fork's `concat_and_cache_mla` with kv_cache_dtype fp8_e4m3 (ssengine/kernels.py config 23). */
+int ssb_mla_cache_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, float k_scale,
+                         void* stream);
+
+/* FP8 query of the sparse MLA: q8[t, h, 0:512] = e4m3(lat[h * rows_pad + t, :] / q_scale) (the absorbed latent
+ * queries, head-major bf16 rows of 512) and q8[t, h, 512:576] = e4m3(rope[t * ldr + h * rope_stride + 0:64] / q_scale)
+ * (each head's rope slice of the q_b rows); e4m3 [T, 64, 576]. Replaces the reference's transpose into the query
+ * buffer and `scaled_fp8_quant` before the sparse MLA (ssengine/kernels.py `q_fp8_quant`). */
+int ssb_mla_q_pack(const void* lat, int64_t rows_pad, const void* rope, int64_t ldr, int64_t rope_stride, int64_t T,
+                   void* q8, float q_scale, void* stream);
 
 /* Grouped NVFP4 GEMM (bf16 epilogue): for each tile {group g, first A row, rows, 0} of tiles int32 [num_tiles][4]
  * (device; *num_tiles on the device, <= tile_cap), out[row, :N] = alpha[g] * A[row] . B[g * N + n] with A NVFP4

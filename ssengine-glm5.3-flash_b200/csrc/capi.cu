@@ -309,12 +309,12 @@ int ssb_indexer_expand(const int32_t* pool_ids, int64_t ldp, int32_t k, const in
 }
 
 int ssb_sparse_mla(const void* q, int64_t T, const void* kv_cache, const int32_t* indices, int64_t ld_idx,
-                   int32_t n_idx, const int32_t* qsl, int32_t R, const int32_t* page_table, int64_t width, float scale,
-                   void* out, int32_t* status, void* stream) {
+                   int32_t n_idx, const int32_t* qsl, int32_t R, const int32_t* page_table, int64_t width,
+                   float bmm1_scale, float bmm2_scale, void* out, int32_t* status, void* stream) {
   if (width <= 0 || width > (1 << 24)) return kErrArgs;
   ssb::MlaArgs a;
-  a.q = static_cast<const __nv_bfloat16*>(q);
-  a.kv = static_cast<const __nv_bfloat16*>(kv_cache);
+  a.q = static_cast<const uint8_t*>(q);
+  a.kv = static_cast<const uint8_t*>(kv_cache);
   a.indices = indices;
   a.ld_idx = ld_idx;
   a.n_idx = n_idx;
@@ -322,15 +322,23 @@ int ssb_sparse_mla(const void* q, int64_t T, const void* kv_cache, const int32_t
   a.R = R;
   a.table = page_table;
   a.width = static_cast<int32_t>(width);
-  a.scale = scale;
+  a.scale = bmm1_scale;
+  a.bmm2 = bmm2_scale;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.T = T;
   a.status = status;
   return ssb::launch_sparse_mla(a, static_cast<cudaStream_t>(stream));
 }
 
-int ssb_mla_cache_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, void* stream) {
-  return ssb::launch_mla_append(src, lds, slots, T, cache, static_cast<cudaStream_t>(stream));
+int ssb_mla_cache_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, float k_scale,
+                         void* stream) {
+  return ssb::launch_mla_append(src, lds, slots, T, cache, k_scale, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_mla_q_pack(const void* lat, int64_t rows_pad, const void* rope, int64_t ldr, int64_t rope_stride, int64_t T,
+                   void* q8, float q_scale, void* stream) {
+  return ssb::launch_mla_q_pack(lat, rows_pad, rope, ldr, rope_stride, T, q8, q_scale,
+                                static_cast<cudaStream_t>(stream));
 }
 
 int ssb_kpool_insert(const void* k, const void* gate, int64_t ld, const float* ape, const int32_t* reqs, int64_t R,

@@ -85,6 +85,22 @@ SSB_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int32_t* abort
   }
 }
 
+// ---- named barriers (id 1..15) over a subset of the CTA's warps ------------------------------------------------
+SSB_DEVICE void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+// Barrier that also returns the OR of `v` over the participating threads (a uniform decision for the group).
+SSB_DEVICE bool named_bar_or(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
 // ---- TMA / bulk copies (no cluster multicast anywhere in this library) ---------------------------------------------
 SSB_DEVICE void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -145,6 +161,15 @@ SSB_DEVICE void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[smem] x B[smem], e4m3 operands (kind::f8f6f4), fp32 accumulate.
+SSB_DEVICE void tc_mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 SSB_DEVICE void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
@@ -174,6 +199,12 @@ SSB_DEVICE void tmem_st_32x32b_x32(uint32_t taddr, const float (&v)[32]) {
       : "memory");
 }
 SSB_DEVICE void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Instruction descriptor of kind::f8f6f4 with e4m3 A and B (format 0), fp32 D (1 in [4,6)), K-major both (bit 16 set
+// by the caller for an MN-major B), N >> 3 in [17,23), M >> 4 in [24,29).
+__host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
 
 // Instruction descriptor of kind::f16 with bf16 A and B (format 1 in [7,10) and [10,13)), fp32 D (1 in [4,6)),
 // K-major both, N >> 3 in [17,23), M >> 4 in [24,29).

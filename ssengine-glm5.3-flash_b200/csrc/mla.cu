@@ -1,25 +1,29 @@
-// Sparse MLA prefill for sm_100a (absorbed-latent attention of one DSA layer) and the latent-cache append.
+// Sparse MLA prefill for sm_100a (absorbed-latent attention of one DSA layer) over an FP8 latent cache, the cache
+// append and the FP8 query pack.
 //
-//   out[t, h, :] = sum_j softmax_j(scale * q[t, h, :] . kv[s_j, :]) * kv[s_j, 0:512]      (h < 64 heads)
+//   out[t, h, :] = bmm2 * sum_j softmax_j(bmm1 * q8[t, h, :] . kv8[s_j, :]) * kv8[s_j, 0:512]      (h < 64 heads)
 //
 // over the row's selected tokens j (the indexer's expanded indices, -1 = none), each read from the paged latent cache
-// (latent 512 + rope 64 per token, bf16 rows of 576) at slot = pages[pos / 128] * 128 + pos % 128 of the row's
-// request. Reference: the TRTLLM sparse MLA called through `trtllm_batch_decode_with_kv_cache_mla` (ssengine/kernels.py
-// config 25; split at 32,768 rows, ssengine/model/pp_patch.py:643-672).
+// (e4m3 rows of 576 bytes: latent 512 + rope 64) at slot = pages[pos / 128] * 128 + pos % 128 of the row's request.
+// q8 = e4m3(q / q_scale), kv8 = e4m3(kv / k_scale), bmm1 = softmax scale * q_scale * k_scale, bmm2 = k_scale: the
+// reference's FP8 query and cache (vLLM kv_cache_dtype fp8_e4m3, `concat_and_cache_mla`; TRTLLM sparse MLA with
+// bmm1 / bmm2 scales: ssengine/kernels.py configs 23 and 25, ssengine/model/pp_patch.py:643-672).
 //
-// One CTA (4 warps) per query row; tcgen05 with the 64 heads as M = 64 (accumulator rows in lanes 0-15 of each
-// 32-lane sub-partition; a second M = 64 accumulator sits in lanes 16-31 of the same columns):
-//   Q [64 x 576] bf16 stays in shared memory (TMA, 9 K-major 128-byte-swizzled chunks);
-//   the index columns are taken in blocks of 64; blocks without a selected token are skipped (listed up front), so a
-//   row near its request's start costs its own tokens, not the full top-k width;
-//   per block, the selected tokens' rows are gathered by cp.async into 9 chunks [64 tokens x 64 dims] with the same
-//   swizzle (missing tokens zero-filled without a read), double-buffered (block b+1 lands while block b is used);
-//   S [64 x 64] = Q K^T as two N = 32 halves (tokens 0-31 in lanes 0-15, 32-63 in lanes 16-31 of columns 0-31;
-//   2 x 36 MMAs kind::f16); softmax by all 128 threads (a head row's two halves combine max and sum with a shuffle;
-//   exp2, scale folded) with the running max kept stale until a block raises it by more than 2^8, so the accumulator
-//   is rescaled in TMEM only then;
-//   P [64 x 64] bf16 to shared memory (K-major); O += P V with V = the same chunks read MN-major: O columns 256-511,
-//   latent dims 0-255 in lanes 0-15 and dims 256-511 in lanes 16-31 (2 x 4 MMAs of N = 256 per block).
+// One CTA per query row, 256 threads. Up front, every index column (n_idx <= 2304) is resolved to its cache row in
+// shared memory with all loads in flight; then three roles run over blocks of 128 index columns (blocks without a
+// selected token skipped):
+//   warps 5-7 gather: each block's 128 token rows by cp.async into 5 K-major 128-byte-swizzled chunks [128 x 128 B]
+//            (the 5th holds the 64 rope bytes), two buffers; missing tokens zero-filled without a read;
+//   warp 4 issues the MMAs (one thread, kind::f8f6f4, M = 64 heads): S [64 x 128] = Q K^T as two N = 64 halves
+//            (tokens 0-63 in lanes 0-15, 64-127 in lanes 16-31 of TMEM columns 0-63; 36 MMAs), then
+//            O += P V with V the same chunks read MN-major (dims 0-255 in lanes 0-15, 256-511 in lanes 16-31 of
+//            columns 256-511; 8 MMAs of N = 256);
+//   warps 0-3 softmax: one head row half per thread (64 scores), exp2 with the scale folded, running max kept stale
+//            until a block raises it by more than 2^3 (O rescaled in TMEM only then), so p <= 8 and 32 p fits e4m3
+//            (448) with normals down to p = 2^-11; P to e4m3 (K-major, swizzled) for the PV MMA; then the epilogue
+//            (O * bmm2 / (32 l) -> bf16).
+// Each tcgen05.commit tracks every earlier MMA of the issuing thread, so "S of block i done" also means "PV of block
+// i - 1 done": one S accumulator and one P buffer suffice, and O is stable whenever the softmax warps touch it.
 // Bounded waits; on expiry the status word holds kErrTimeout, in-flight MMAs are drained and TMEM is freed.
 #include "common.cuh"
 #include "ops.h"
@@ -27,23 +31,28 @@
 namespace ssb {
 namespace {
 
-constexpr int kHeads = 64, kDq = 576, kDv = 512, kBlk = 64;
-constexpr int kMlaThreads = 128;
-constexpr int kChunk = kBlk * 128;                       // [64 rows x 64 bf16], 8 KB
-constexpr int kNChunks = kDq / 64;                       // 9
-constexpr int kQBytes = kNChunks * kChunk;               // 73728
-constexpr int kKvBytes = kNChunks * kChunk;              // 73728 per block buffer
+constexpr int kHeads = 64, kDq = 576, kDv = 512, kBlk = 128;
+constexpr int kMlaThreads = 256;                  // warps 0-3 softmax + epilogue, warp 4 MMA, warps 5-7 gather
+constexpr int kGather = 96;                       // gather threads
+constexpr int kNC = 5;                            // 128-byte chunks of a 576-byte row
+constexpr int kQChunk = kHeads * 128;             // [64 heads x 128 B], 8 KB
+constexpr int kKvChunk = kBlk * 128;              // [128 tokens x 128 B], 16 KB
+constexpr int kKvBuf = kNC * kKvChunk;            // 80 KB
 constexpr int kOffQ = 0;
-constexpr int kOffKv = kQBytes;                          // 2 buffers
-constexpr int kOffP = kOffKv + 2 * kKvBytes;             // P [64 x 64] bf16, K-major swizzled
-constexpr int kOffSlots = kOffP + kChunk;                // int64 [2][64]
-constexpr int kOffBar = kOffSlots + 2 * kBlk * 8;        // bar_q, bar_s, bar_pv, bar_drain
-constexpr int kOffMisc = kOffBar + 32;                   // tmem slot, abort flag, block count
-constexpr int kMaxBlocks = 256;                          // n_idx <= 16384
-constexpr int kOffMask = kOffMisc + 16;                  // uint64 [4]: blocks holding a selected token
-constexpr int kOffList = kOffMask + 32;                  // uint16 [256]: those blocks in order
+constexpr int kOffKv = kNC * kQChunk;             // 2 buffers
+constexpr int kOffP = kOffKv + 2 * kKvBuf;        // P [64 heads x 128 tokens] e4m3, K-major swizzled
+constexpr int kMaxBlocks = 18;                    // n_idx <= 2304 (the reference selects 2,176)
+constexpr int kMaxIdx = kMaxBlocks * kBlk;
+constexpr int kOffSlots = kOffP + kHeads * 128;   // int32 [2304]: cache row of each index column (-1: none)
+constexpr int kOffMask = kOffSlots + 4 * kMaxIdx; // uint64 [36]: selected columns, 64 a word
+constexpr int kOffBar = kOffMask + 8 * 2 * kMaxBlocks;   // kv_full[2], kv_empty[2], s_full, p_full, o_done
+constexpr int kOffMisc = kOffBar + 64;            // tmem slot, abort flag, block count
+constexpr int kOffList = kOffMisc + 16;           // uint16 [18]: the blocks holding a selected column, in order
 constexpr int kMlaSmem = kOffList + 2 * kMaxBlocks + 1024;   // + alignment slack
+static_assert(kMlaSmem <= 232448, "shared memory");
 constexpr uint32_t kSCol = 0, kOCol = 256;
+constexpr float kLazy = 3.0f;                     // a block raising a row's max by more than 2^3 rescales O
+constexpr float kPScale = 32.0f;                  // P stored as e4m3(32 p): p <= 2^3 over a stale max -> <= 256
 
 SSB_DEVICE void cp_async16(uint32_t dst, const void* src, bool valid) {
   const int n = valid ? 16 : 0;
@@ -52,6 +61,20 @@ SSB_DEVICE void cp_async16(uint32_t dst, const void* src, bool valid) {
 SSB_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 SSB_DEVICE void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
+// Two floats -> two e4m3 bytes (round to nearest even, saturating to +-448): lo in the low byte.
+SSB_DEVICE uint32_t e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// 2^x by the MUFU instruction (flush-to-zero; ~2 ulp), plenty for weights that are rounded to e4m3 next.
+SSB_DEVICE float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 SSB_DEVICE void drain_bar(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
@@ -59,36 +82,37 @@ SSB_DEVICE void drain_bar(uint32_t bar, uint32_t parity) {
   }
 }
 
-// Block b's 64 token rows -> the 9 chunks of a buffer (a missing token is zero-filled without a read; its score is
-// masked): thread t copies half (t & 1) of row t >> 1, four 16-byte pieces per chunk, offsets fixed at compile time.
-SSB_DEVICE void gather_block(uint32_t kvb, const __nv_bfloat16* kv, const int64_t* slot_of, int tid) {
-  const int r = tid >> 1, hi = tid & 1;
-  const int64_t slot = slot_of[r];
-  const bool valid = slot >= 0;
-  const __nv_bfloat16* src = kv + (valid ? slot : 0) * kDq + hi * 32;
-  const uint32_t dst = kvb + r * 128;
-  const int sw = r & 7;
+SSB_DEVICE void tmem_ld_x64(uint32_t taddr, float (&v)[64]) {
+  float a[32], b[32];
+  tmem_ld_32x32b_x32(taddr, a);
+  tmem_ld_32x32b_x32(taddr + 32, b);
 #pragma unroll
-  for (int ch = 0; ch < kNChunks; ++ch)
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const int j = 4 * hi + jj;
-      cp_async16(dst + ch * kChunk + ((j ^ sw) << 4), src + ch * 64 + jj * 8, valid);
-    }
+  for (int i = 0; i < 32; ++i) {
+    v[i] = a[i];
+    v[32 + i] = b[i];
+  }
 }
 
-__global__ void __launch_bounds__(kMlaThreads, 1)
-    sparse_mla_kernel(const __grid_constant__ CUtensorMap mq, const MlaArgs a) {
+// Byte offset of 16-byte granule g (0-35) of row r in a buffer of 5 K-major 128-byte-swizzled chunks of `rows` rows.
+SSB_DEVICE uint32_t chunk_off(int r, int g, int chunk_bytes) {
+  const int c = g < 32 ? (g >> 3) : 4, gg = g < 32 ? (g & 7) : g - 32;
+  return c * chunk_bytes + r * 128 + ((gg ^ (r & 7)) << 4);
+}
+
+__global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(const MlaArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t t = blockIdx.x;
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar_q = sbase + kOffBar, bar_s = bar_q + 8, bar_pv = bar_q + 16, bar_drain = bar_q + 24;
-  int64_t* slots = reinterpret_cast<int64_t*>(smem + kOffSlots);
+  const uint32_t bar0 = sbase + kOffBar;
+  const uint32_t kv_full = bar0, kv_empty = bar0 + 16, s_full = bar0 + 32, p_full = bar0 + 40, o_done = bar0 + 48;
+  int32_t* slots = reinterpret_cast<int32_t*>(smem + kOffSlots);
+  unsigned long long* tmask = reinterpret_cast<unsigned long long*>(smem + kOffMask);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + kOffMisc + 4);
-  uint8_t* Pb = smem + kOffP;
+  volatile int32_t* nblk_s = reinterpret_cast<volatile int32_t*>(smem + kOffMisc + 8);
+  uint16_t* blist = reinterpret_cast<uint16_t*>(smem + kOffList);
 
   // the row's request (binary search of the query start list) and its pages
   int lo = 0, hi = a.R - 1;
@@ -98,218 +122,233 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   }
   const int32_t* pages = a.table + (int64_t)lo * a.width;
   const int32_t* idx = a.indices + t * a.ld_idx;
-  unsigned long long* mask = reinterpret_cast<unsigned long long*>(smem + kOffMask);
-  uint16_t* blist = reinterpret_cast<uint16_t*>(smem + kOffList);
-  volatile int32_t* nblk_s = reinterpret_cast<volatile int32_t*>(smem + kOffMisc + 8);
-  auto slot_at = [&](int j) -> int64_t {
-    const int32_t pos = idx[j];
-    if (pos >= 0 && (pos >> 7) < a.width) {
-      const int32_t pg = pages[pos >> 7];
-      if (pg >= 0) return (int64_t)pg * 128 + (pos & 127);
-    }
-    return -1;
-  };
-  // list entry i (the i-th block of 64 index columns that holds a selected token) -> slot buffer (i & 1)
-  auto fill_slots = [&](int i) {
-    if (tid < kBlk) {
-      const int j = blist[i] * kBlk + tid;
-      slots[(i & 1) * kBlk + tid] = j < a.n_idx ? slot_at(j) : -1;
-    }
-  };
 
-  if (tid == 0) {                                       // Q lands while the index columns are scanned
-    mbar_init(bar_q, 1);
-    mbar_init(bar_s, 1);
-    mbar_init(bar_pv, 1);
-    mbar_init(bar_drain, 1);
+  // Q (64 heads x 576 bytes) by cp.async into the 5 swizzled chunks, 9 granules a thread
+  {
+    const uint8_t* q = a.q + t * (kHeads * kDq);
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
+      const int p = tid + kMlaThreads * k, h = p / 36, g = p - h * 36;
+      cp_async16(sbase + kOffQ + chunk_off(h, g, kQChunk), q + h * kDq + g * 16, true);
+    }
+    cp_async_commit();
+  }
+  if (tid == 0) {
+    mbar_init(kv_full, kGather);
+    mbar_init(kv_full + 8, kGather);
+    mbar_init(kv_empty, 1);
+    mbar_init(kv_empty + 8, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
-    fence_proxy_async_smem();
-    mbar_arrive_expect_tx(bar_q, kQBytes);
-    for (int c = 0; c < kNChunks; ++c) tma_load_2d(sbase + kOffQ + c * kChunk, &mq, 64 * c, (int32_t)(t * kHeads), bar_q);
   }
-  // blocks of index columns without a selected token are skipped: mark the others, then list them in order
-  if (tid < 4) mask[tid] = 0ull;
-  __syncthreads();
-  for (int j = tid; j < a.n_idx; j += kMlaThreads)
-    if (slot_at(j) >= 0) atomicOr(mask + (j >> 12), 1ull << ((j >> 6) & 63));
-  __syncthreads();
-  if (tid == 0) {
-    int n = 0;
-    for (int w = 0; w < 4; ++w)
-      for (unsigned long long m = mask[w]; m; m &= m - 1) blist[n++] = static_cast<uint16_t>(64 * w + __ffsll(m) - 1);
-    *nblk_s = n;
-  }
-  __syncthreads();
-  const int nblk = *nblk_s;
-
+  if (tid < 2 * kMaxBlocks) tmask[tid] = 0ull;
   if (warp == 0) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
-  if (nblk > 0) fill_slots(0);
+  // every index column -> its cache row (the loads of all columns in flight at once), and the selected-column bits
+  {
+    constexpr int kPer = (kMaxIdx + kMlaThreads - 1) / kMlaThreads;   // 9
+    int32_t pos[kPer], pg[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int j = tid + kMlaThreads * k;
+      pos[k] = j < a.n_idx ? idx[j] : -1;
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) pg[k] = (pos[k] >= 0 && (pos[k] >> 7) < a.width) ? pages[pos[k] >> 7] : -1;
+    __syncthreads();                                     // the selected-column words are zeroed
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int j = tid + kMlaThreads * k;
+      if (j >= kMaxIdx) break;
+      const bool v = pg[k] >= 0 && pg[k] < (1 << 24);
+      slots[j] = v ? pg[k] * 128 + (pos[k] & 127) : -1;
+      if (v) atomicOr(tmask + (j >> 6), 1ull << (j & 63));
+    }
+  }
+  __syncthreads();
+  // blocks of index columns without a selected token are skipped: list the others in order
+  if (tid == 0) {
+    int n = 0;
+    for (int b = 0; b < kMaxBlocks; ++b)
+      if (tmask[2 * b] | tmask[2 * b + 1]) blist[n++] = static_cast<uint16_t>(b);
+    *nblk_s = n;
+  }
+  cp_async_wait0();
+  fence_proxy_async_smem();                              // Q (generic-proxy writes) -> visible to the tensor core
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  const int nblk = *nblk_s;
   const uint32_t tmem = *tmem_slot;
-  if (nblk > 0) gather_block(sbase + kOffKv, a.kv, slots, tid);
-  cp_async_commit();
 
-  constexpr uint32_t idesc_s = idesc_bf16(64, 32);                     // tokens 0-31 -> lanes 0-15, 32-63 -> 16-31
-  constexpr uint32_t idesc_pv = idesc_bf16(64, 256) | (1u << 16);      // B (V) MN-major
-  const float sc = a.scale * 1.4426950408889634f;                        // exp2 domain
-  const uint32_t tq = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  float m_used = -INFINITY, l_sum = 0.0f;
-  bool ok = true, any_mma = false;
-
-  for (int b = 0; b < nblk && ok; ++b) {
-    const int kb = b & 1;
-    const uint32_t kvb = sbase + kOffKv + kb * kKvBytes;
-    cp_async_wait0();                                    // block b landed (this thread's pieces)
-    fence_proxy_async_smem();                            // generic-proxy writes -> visible to the tensor core
-    __syncthreads();
-    if (tid == 0) {
-      if (b == 0) mbar_wait(bar_q, 0, abort_flag, a.status);
-      if (!*abort_flag) {
+  if (warp >= 5) {
+    // ---------------------------------------------------------------- gather
+    const int gt = tid - 160;
+    for (int i = 0; i < nblk; ++i) {
+      const int buf = i & 1;
+      bool ok = true;
+      if (i >= 2) ok = mbar_wait(kv_empty + 8 * buf, ((i >> 1) - 1) & 1, abort_flag, a.status);   // PV of i - 2
+      if (named_bar_or(1, kGather, !ok)) break;
+      const uint32_t kvb = sbase + kOffKv + buf * kKvBuf;
+      const int32_t* bs = slots + blist[i] * kBlk;
+#pragma unroll 4
+      for (int p = gt; p < kBlk * 36; p += kGather) {
+        const int tok = p / 36, g = p - tok * 36;
+        const int32_t sl = bs[tok];
+        const bool v = sl >= 0;
+        cp_async16(kvb + chunk_off(tok, g, kKvChunk), a.kv + (int64_t)(v ? sl : 0) * kDq + g * 16, v);
+      }
+      cp_async_commit();
+      cp_async_wait0();
+      fence_proxy_async_smem();
+      mbar_arrive(kv_full + 8 * buf);
+    }
+    cp_async_wait0();
+  } else if (warp == 4) {
+    // ---------------------------------------------------------------- MMA issue
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_e4m3(64, 64);                   // tokens 0-63 -> lanes 0-15, 64-127 -> 16-31
+      constexpr uint32_t idesc_pv = idesc_e4m3(64, 256) | (1u << 16);    // B (V) MN-major
+      int issued = 0;
+      for (int i = 0; i < nblk; ++i) {
+        const int buf = i & 1;
+        if (!mbar_wait(kv_full + 8 * buf, (i >> 1) & 1, abort_flag, a.status)) break;
         tc_fence_after();
+        const uint32_t kvb = sbase + kOffKv + buf * kKvBuf;
 #pragma unroll
-        for (int c = 0; c < kNChunks; ++c) {
+        for (int c = 0; c < kNC; ++c) {
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t ad = smem_desc(sbase + kOffQ + c * kChunk + ks * 32, 0, 1024, 2);
+            if (c == kNC - 1 && ks >= 2) break;                            // the rope chunk holds 64 bytes
+            const uint64_t ad = smem_desc(sbase + kOffQ + c * kQChunk + ks * 32, 0, 1024, 2);
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-              const uint64_t bd = smem_desc(kvb + c * kChunk + hh * 4096 + ks * 32, 0, 1024, 2);
-              tc_mma_f16(tmem + (static_cast<uint32_t>(16 * hh) << 16) + kSCol, ad, bd, idesc_s, (c | ks) != 0 ? 1u : 0u);
+              const uint64_t bd = smem_desc(kvb + c * kKvChunk + hh * 8192 + ks * 32, 0, 1024, 2);
+              tc_mma_f8(tmem + (static_cast<uint32_t>(16 * hh) << 16) + kSCol, ad, bd, idesc_s, (c | ks) != 0 ? 1u : 0u);
             }
           }
         }
-        any_mma = true;
-        tc_commit(bar_s);
+        tc_commit(s_full);
+        issued = 1;
+        if (!mbar_wait(p_full, i & 1, abort_flag, a.status)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t ad = smem_desc(sbase + kOffP + ks * 32, 0, 1024, 2);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint64_t bd = smem_desc(kvb + 2 * h * kKvChunk + ks * 4096, kKvChunk, 1024, 2);
+            tc_mma_f8(tmem + (static_cast<uint32_t>(16 * h) << 16) + kOCol, ad, bd, idesc_pv,
+                      (i > 0 || ks > 0) ? 1u : 0u);
+          }
+        }
+        tc_commit(kv_empty + 8 * buf);
       }
+      tc_commit(o_done);                                 // every MMA issued above has completed when this arrives
+      if (issued) drain_bar(o_done, 0);
     }
-    // PV of block b-1 done: its KV buffer, P and O are free / stable; gather block b+1 into that buffer
-    if (b >= 1) mbar_wait(bar_pv, (b - 1) & 1, abort_flag, a.status);
-    if (b + 1 < nblk) fill_slots(b + 1);
-    __syncthreads();
-    if (*abort_flag) { ok = false; break; }
-    if (b + 1 < nblk) gather_block(sbase + kOffKv + (kb ^ 1) * kKvBytes, a.kv, slots + (kb ^ 1) * kBlk, tid);
-    cp_async_commit();
-    mbar_wait(bar_s, b & 1, abort_flag, a.status);      // a timeout raises the abort flag, checked after the next barrier
-    tc_fence_after();
-
-    // ---- softmax: lane l holds row 16 warp + (l & 15), tokens 32 (l >> 4) .. + 31; the two halves of a row combine
-    //      their max and sum with one shuffle and keep identical running state ----
-    float v[32];
-    tmem_ld_32x32b_x32(tq + kSCol, v);
-    tmem_ld_wait();
-    const int half = lane >> 4;
-    float alpha = 1.0f;
-    bool rescale = false;
-    {
-      const int64_t* sl = slots + kb * kBlk + 32 * half;
+  } else {
+    // ---------------------------------------------------------------- softmax (warps 0-3)
+    const int half = lane >> 4, row = 16 * warp + (lane & 15);
+    const uint32_t tq = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const float sc = a.scale * 1.4426950408889634f;      // exp2 domain
+    uint8_t* Pb = smem + kOffP;
+    float m_used = -INFINITY, l_sum = 0.0f;
+    bool ok = true;
+    for (int i = 0; i < nblk; ++i) {
+      const bool w = mbar_wait(s_full, i & 1, abort_flag, a.status);
+      if (named_bar_or(2, 128, !w)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float v[64];
+      tmem_ld_x64(tq + kSCol, v);
+      tmem_ld_wait();
+      const unsigned long long vm = tmask[2 * blist[i] + half];
       float mb = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        v[j] = sl[j] >= 0 ? v[j] * sc : -INFINITY;
+      for (int j = 0; j < 64; ++j) {
+        v[j] = ((vm >> j) & 1ull) ? v[j] * sc : -INFINITY;
         mb = fmaxf(mb, v[j]);
       }
       mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 16));
+      float alpha = 1.0f;
+      bool rescale = false;
       if (m_used == -INFINITY) {
         m_used = mb;                                     // nothing accumulated yet (O = 0, l = 0)
-      } else if (mb > m_used + 8.0f) {
+      } else if (mb > m_used + kLazy) {
         alpha = exp2f(m_used - mb);
         m_used = mb;
         l_sum *= alpha;
         rescale = true;
       }
-      const int row = 16 * warp + (lane & 15);
+      // rescale O rows in TMEM when a row's max moved (warp-collective; PV of the previous block has completed)
+      if (__any_sync(0xffffffffu, rescale) && i > 0) {
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          float o[32];
+          tmem_ld_32x32b_x32(tq + kOCol + 32 * c, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] *= alpha;
+          tmem_st_32x32b_x32(tq + kOCol + 32 * c, o);
+        }
+        tmem_st_wait();
+      }
       float ps = 0.0f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float p[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          p[e] = (m_used == -INFINITY) ? 0.0f : exp2f(v[8 * c + e] - m_used);
-          ps += p[e];
-        }
-        uint4 pk;
-        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+      for (int g = 0; g < 4; ++g) {
+        uint32_t wd[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(p[2 * e], p[2 * e + 1]);
-          pw[e] = *reinterpret_cast<uint32_t*>(&h2);
+          float p[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float x = v[16 * g + 4 * e + u];
+            p[u] = (m_used == -INFINITY) ? 0.0f : ex2_approx(x - m_used);
+            ps += p[u];
+          }
+          wd[e] = e4m3x2(p[0] * kPScale, p[1] * kPScale) | (e4m3x2(p[2] * kPScale, p[3] * kPScale) << 16);
         }
-        const int chunk = 4 * half + c;
-        *reinterpret_cast<uint4*>(Pb + row * 128 + ((chunk ^ (row & 7)) << 4)) = pk;
+        const int gg = 4 * half + g;                     // 16-token granule of the row
+        *reinterpret_cast<uint4*>(Pb + row * 128 + ((gg ^ (row & 7)) << 4)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
       }
       l_sum += ps + __shfl_xor_sync(0xffffffffu, ps, 16);
+      fence_proxy_async_smem();                          // P (generic stores) -> visible to the tensor core
+      tc_fence_before();
+      mbar_arrive(p_full);
     }
-    // rescale O rows in TMEM when a row's max moved (warp-collective; lanes 0-15 hold dims 0-255, 16-31 dims 256-511)
-    if (__any_sync(0xffffffffu, rescale) && b > 0) {
+    // ---- epilogue: lanes 0-15 dims 0-255 of head row 16 warp + lane, lanes 16-31 dims 256-511 ----
+    const bool have = ok && nblk > 0;
+    if (have && !mbar_wait(o_done, 0, abort_flag, a.status)) ok = false;
+    tc_fence_after();
+    const bool good = have && ok && !*abort_flag;
+    const float inv = (good && l_sum > 0.0f) ? a.bmm2 / (l_sum * kPScale) : 0.0f;
+    __nv_bfloat16* orow = a.out + (t * kHeads + row) * kDv + half * 256;
 #pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
-        float o[32];
+    for (int c = 0; c < 8; ++c) {
+      float o[32];
+      if (good) {
         tmem_ld_32x32b_x32(tq + kOCol + 32 * c, o);
         tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] *= alpha;
-        tmem_st_32x32b_x32(tq + kOCol + 32 * c, o);
       }
-      tmem_st_wait();
-    }
-    fence_proxy_async_smem();                            // P (generic stores) -> visible to the tensor core
-    tc_fence_before();
-    __syncthreads();
-    if (*abort_flag) { ok = false; break; }
-    if (tid == 0) {
-      tc_fence_after();
+      uint4 pk[4];
+      uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const uint64_t ad = smem_desc(sbase + kOffP + ks * 32, 0, 1024, 2);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint64_t bd = smem_desc(kvb + 4 * h * kChunk + ks * 2048, kChunk, 1024, 2);
-          tc_mma_f16(tmem + (static_cast<uint32_t>(16 * h) << 16) + kOCol, ad, bd, idesc_pv,
-                     (b > 0 || ks > 0) ? 1u : 0u);
-        }
+      for (int e = 0; e < 16; ++e) {
+        const float x0 = good ? o[2 * e] * inv : 0.0f, x1 = good ? o[2 * e + 1] * inv : 0.0f;
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+        pw[e] = *reinterpret_cast<uint32_t*>(&h2);
       }
-      tc_commit(bar_pv);
-    }
-  }
-  cp_async_wait0();
-
-  // ---- normalise and store (lanes 0-15: dims 0-255 of row 16 warp + lane; lanes 16-31: dims 256-511) ----
-  const bool have = ok && nblk > 0;
-  if (have) mbar_wait(bar_pv, (nblk - 1) & 1, abort_flag, a.status);
-  if (nblk == 0 && tid == 0) mbar_wait(bar_q, 0, abort_flag, a.status);   // no copy in flight at exit
-  __syncthreads();
-  if (*abort_flag) ok = false;
-  tc_fence_after();
-  const float inv = (ok && have && l_sum > 0.0f) ? 1.0f / l_sum : 0.0f;
-  const int row = 16 * warp + (lane & 15);
-  __nv_bfloat16* orow = a.out + (t * kHeads + row) * kDv + (lane >> 4) * 256;
-#pragma unroll 1
-  for (int c = 0; c < 8; ++c) {
-    float o[32];
-    if (have && ok) {
-      tmem_ld_32x32b_x32(tq + kOCol + 32 * c, o);
-      tmem_ld_wait();
-    }
-    uint4 pk[4];
-    uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const float x0 = (have && ok) ? o[2 * e] * inv : 0.0f, x1 = (have && ok) ? o[2 * e + 1] * inv : 0.0f;
-      __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
-      pw[e] = *reinterpret_cast<uint32_t*>(&h2);
+      for (int e = 0; e < 4; ++e) reinterpret_cast<uint4*>(orow + 32 * c)[e] = pk[e];
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) reinterpret_cast<uint4*>(orow + 32 * c)[e] = pk[e];
-  }
-  if (*abort_flag && any_mma && tid == 0) {
-    tc_commit(bar_drain);
-    drain_bar(bar_drain, 0);
   }
   tc_fence_before();
   __syncthreads();
@@ -319,48 +358,91 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   }
 }
 
-// Latent cache append: row t of src (bf16 [T, 576], row pitch lds) -> cache row slots[t] (skipped when < 0).
+// Latent cache append: row t of src (bf16 [T, 576], row pitch lds) -> e4m3(x / k_scale) at cache row slots[t] (576
+// bytes; skipped when the slot is < 0). One warp per row, 8 values per lane step.
 __global__ void mla_append_kernel(const __nv_bfloat16* src, int64_t lds, const int64_t* slots, int64_t T,
-                                  __nv_bfloat16* cache) {
-  const int64_t t = blockIdx.x;
+                                  uint8_t* cache, float inv_scale) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
   const int64_t s = slots[t];
   if (s < 0) return;
-  for (int c = threadIdx.x; c < kDq / 8; c += blockDim.x)
-    reinterpret_cast<uint4*>(cache + s * kDq)[c] = reinterpret_cast<const uint4*>(src + t * lds)[c];
+  const int lane = threadIdx.x & 31;
+  for (int c = lane; c < kDq / 8; c += 32) {             // 72 groups of 8 values
+    const uint4 v = reinterpret_cast<const uint4*>(src + t * lds)[c];
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+    uint32_t w[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float2 f0 = __bfloat1622float2(b[2 * k]), f1 = __bfloat1622float2(b[2 * k + 1]);
+      w[k] = e4m3x2(f0.x * inv_scale, f0.y * inv_scale) | (e4m3x2(f1.x * inv_scale, f1.y * inv_scale) << 16);
+    }
+    reinterpret_cast<uint2*>(cache + s * kDq)[c] = make_uint2(w[0], w[1]);
+  }
 }
+
+// Query pack: q8[t, h, 0:512] = e4m3(lat[h, t, :] / q_scale) (head-major latent rows, rows_pad rows a head) and
+// q8[t, h, 512:576] = e4m3(rope[t, h * rope_stride + :64] / q_scale). One thread per 8 values.
+__global__ void mla_q_pack_kernel(const __nv_bfloat16* lat, int64_t rows_pad, const __nv_bfloat16* rope, int64_t ldr,
+                                  int64_t rope_stride, int64_t T, uint8_t* q8, float inv_scale) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= T * kHeads * (kDq / 8)) return;
+  const int g = static_cast<int>(i % (kDq / 8));
+  const int64_t th = i / (kDq / 8);
+  const int h = static_cast<int>(th % kHeads);
+  const int64_t t = th / kHeads;
+  const uint4 v = g < kDv / 8 ? reinterpret_cast<const uint4*>(lat + ((int64_t)h * rows_pad + t) * kDv)[g]
+                              : reinterpret_cast<const uint4*>(rope + t * ldr + h * rope_stride)[g - kDv / 8];
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+  uint32_t w[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float2 f0 = __bfloat1622float2(b[2 * k]), f1 = __bfloat1622float2(b[2 * k + 1]);
+    w[k] = e4m3x2(f0.x * inv_scale, f0.y * inv_scale) | (e4m3x2(f1.x * inv_scale, f1.y * inv_scale) << 16);
+  }
+  reinterpret_cast<uint2*>(q8 + th * kDq)[g] = make_uint2(w[0], w[1]);
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
 
 int launch_sparse_mla(const MlaArgs& a, cudaStream_t stream) {
   if (a.q == nullptr || a.kv == nullptr || a.indices == nullptr || a.qsl == nullptr || a.table == nullptr ||
-      a.out == nullptr || a.T < 0 || a.R <= 0 || a.width <= 0 || a.n_idx < 0 || a.n_idx > kMaxBlocks * kBlk ||
-      a.ld_idx < a.n_idx ||
-      ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.kv) | reinterpret_cast<uintptr_t>(a.out)) &
-       15))
+      a.out == nullptr || a.T < 0 || a.R <= 0 || a.width <= 0 || a.n_idx < 0 || a.n_idx > kMaxIdx ||
+      a.ld_idx < a.n_idx || !al16(a.q) || !al16(a.kv) || !al16(a.out))
     return kErrArgs;
   if (a.T == 0) return kOk;
-  CUtensorMap mq;
-  const int rc = make_map_2d_swizzled(&mq, a.q, a.T * kHeads, kDq, kDq * 2, 64);
-  if (rc != kOk) return rc;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(sparse_mla_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMlaSmem) != cudaSuccess)
       return kErrCuda;
     attr = true;
   }
-  sparse_mla_kernel<<<(unsigned)a.T, kMlaThreads, kMlaSmem, stream>>>(mq, a);
+  sparse_mla_kernel<<<(unsigned)a.T, kMlaThreads, kMlaSmem, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
-int launch_mla_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache,
+int launch_mla_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, float k_scale,
                       cudaStream_t stream) {
-  if (src == nullptr || slots == nullptr || cache == nullptr || T < 0 || lds < kDq || (lds % 8) ||
-      ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(cache)) & 15))
+  if (src == nullptr || slots == nullptr || cache == nullptr || T < 0 || lds < kDq || (lds % 8) || !al16(src) ||
+      !al16(cache) || !(k_scale > 0.0f))
     return kErrArgs;
   if (T == 0) return kOk;
-  mla_append_kernel<<<(unsigned)T, 96, 0, stream>>>(static_cast<const __nv_bfloat16*>(src), lds, slots, T,
-                                                    static_cast<__nv_bfloat16*>(cache));
+  mla_append_kernel<<<(unsigned)((T + 7) / 8), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(src), lds, slots, T,
+                                                                 static_cast<uint8_t*>(cache), 1.0f / k_scale);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int launch_mla_q_pack(const void* lat, int64_t rows_pad, const void* rope, int64_t ldr, int64_t rope_stride,
+                      int64_t T, void* q8, float q_scale, cudaStream_t stream) {
+  if (lat == nullptr || rope == nullptr || q8 == nullptr || T < 0 || rows_pad < T || (ldr % 8) || (rope_stride % 8) ||
+      !al16(lat) || !al16(rope) || !al16(q8) || !(q_scale > 0.0f))
+    return kErrArgs;
+  const int64_t n = T * kHeads * (kDq / 8);
+  if (n == 0) return kOk;
+  mla_q_pack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(lat), rows_pad, static_cast<const __nv_bfloat16*>(rope), ldr, rope_stride, T,
+      static_cast<uint8_t*>(q8), 1.0f / q_scale);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

@@ -145,8 +145,8 @@ int make_map_2d_swizzled(CUtensorMap* m, const void* base, int64_t rows, int64_t
 
 // Sparse MLA prefill and latent-cache append (csrc/mla.cu).
 struct MlaArgs {
-  const __nv_bfloat16* q = nullptr;    // [T, 64, 576]
-  const __nv_bfloat16* kv = nullptr;   // latent cache [slots, 576]
+  const uint8_t* q = nullptr;          // e4m3 [T, 64, 576]
+  const uint8_t* kv = nullptr;         // e4m3 latent cache [slots, 576]
   const int32_t* indices = nullptr;    // [T, ld_idx] token positions (-1 = none)
   int64_t ld_idx = 0;
   int32_t n_idx = 0;                   // columns used
@@ -154,13 +154,17 @@ struct MlaArgs {
   int32_t R = 0;
   const int32_t* table = nullptr;      // [R, width] KV pages (128 tokens)
   int32_t width = 0;
-  float scale = 0.0f;
+  float scale = 0.0f;                  // bmm1: softmax scale * q_scale * k_scale
+  float bmm2 = 1.0f;                   // k_scale
   __nv_bfloat16* out = nullptr;        // [T, 64, 512]
   int64_t T = 0;
   int32_t* status = nullptr;           // device status word (bounded waits)
 };
 int launch_sparse_mla(const MlaArgs& a, cudaStream_t stream);
-int launch_mla_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, cudaStream_t stream);
+int launch_mla_append(const void* src, int64_t lds, const int64_t* slots, int64_t T, void* cache, float k_scale,
+                      cudaStream_t stream);
+int launch_mla_q_pack(const void* lat, int64_t rows_pad, const void* rope, int64_t ldr, int64_t rope_stride,
+                      int64_t T, void* q8, float q_scale, cudaStream_t stream);
 
 // Indexer key pools (csrc/kpool.cu).
 struct KpoolArgs {

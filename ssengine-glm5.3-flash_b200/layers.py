@@ -248,8 +248,8 @@ class DsaAttention:
     512 + rope 64, indexer 32 heads x 128 over pools of 4 tokens, top-512 pools (2,051 tokens with the tail).
 
     y -> a = [q_a | kv latent | k rope] (NVFP4) -> RMSNorm(q_a), RMSNorm(kv) -> q = q_b(q_a) [64 x (nope | rope)],
-    rope on the q and k rope slices -> latent cache rows [kv | k rope] at the rows' slots; q absorb (per-head NVFP4
-    GEMM nope -> 512) -> q_full [T, 64, 576]; indexer: q_idx = wq_idx(q_a) [32 x 128], [k_idx | weights | gate] =
+    rope on the q and k rope slices -> latent cache rows e4m3([kv | k rope] / k_scale) at the rows' slots; q absorb
+    (per-head NVFP4 GEMM nope -> 512) -> q8 = e4m3([absorbed | rope] / q_scale) [T, 64, 576]; indexer: q_idx = wq_idx(q_a) [32 x 128], [k_idx | weights | gate] =
     idx_proj(y), pools of 4 into the pool-key cache, logits -> top-512 pools -> tokens; sparse MLA -> [T, 64, 512];
     v_up (per-head NVFP4 GEMM 512 -> v_dim) -> o_proj. The reference's configs 12-27 (ssengine/kernels.py), with every
     projection NVFP4."""
@@ -275,6 +275,7 @@ class DsaAttention:
         self.kv_norm = (torch.rand(self.LATENT, generator=g, device=dev) + 0.5).to(torch.bfloat16)
         self.ape = torch.randn(4, self.IDX_DIM, generator=g, device=dev) * 0.5
         self.scale = self.qh ** -0.5
+        self.q_scale, self.k_scale = 1.0, 1.0          # per-tensor FP8 scales of the query and the latent cache
         self.device = dev
         self._lib = lib.load()
 
@@ -282,7 +283,7 @@ class DsaAttention:
                 tail_ring, status, stream=None, keep: bool = False):
         """y bf16 [T, H]; positions / slots int64 [T]; qsl int32 [R + 1]; page_table int32 [R, width] (KV pages);
         kpool_reqs int32 [R, 4] {first row, rows, start position, tail block}; groups: the indexer's work groups
-        (int32 [G, 4]); kv_cache bf16 [pages * 128, 576], pool_cache bf16 [pages * 32, 128], tail_ring bf16
+        (int32 [G, 4]); kv_cache e4m3 bytes uint8 [pages * 128, 576], pool_cache bf16 [pages * 32, 128], tail_ring bf16
         [blocks, 2, 4, 128] updated in place -> bf16 [T, H]."""
         from . import indexer, mla
 
@@ -302,7 +303,7 @@ class DsaAttention:
         lib.check("ssb_rope", so.ssb_rope(k_rope.data_ptr(), a.stride(0), 1, 0, positions.data_ptr(), T, self.theta, s))
         lib.check("ssb_concat_cols", so.ssb_concat_cols(kvn.data_ptr(), L, L, k_rope.data_ptr(), a.stride(0), RP,
                                                         kv_rows.data_ptr(), L + RP, T, s))
-        mla.cache_append(kv_rows, slots, kv_cache, stream)
+        mla.cache_append(kv_rows, slots, kv_cache, self.k_scale, stream)
         # queries: q_b, rope on each head's rope slice, absorb of each head's nope part into the latent
         q = torch.empty(T, NH * self.qh, **bf)
         self.q_b(qa, q, status, stream)
@@ -314,14 +315,8 @@ class DsaAttention:
                                                                 q.stride(0), self.qh, 1, s))
         q_lat = torch.empty(NH * Tp, L, **bf)
         self.w_uk(qn, Tp, q_lat, status, stream)
-        q_full = torch.empty(T, NH, L + RP, **bf)
-        lib.check("ssb_transpose_heads", so.ssb_transpose_heads(q_lat.data_ptr(), q_full.data_ptr(), T, Tp, NH, L,
-                                                                NH * (L + RP), L + RP, 0, s))
-        qr = torch.empty(NH * Tp, RP, **bf)
-        lib.check("ssb_transpose_heads", so.ssb_transpose_heads(q[:, self.nope:].data_ptr(), qr.data_ptr(), T, Tp, NH,
-                                                                RP, q.stride(0), self.qh, 1, s))
-        lib.check("ssb_transpose_heads", so.ssb_transpose_heads(qr.data_ptr(), q_full[:, :, L:].data_ptr(), T, Tp, NH,
-                                                                RP, NH * (L + RP), L + RP, 0, s))
+        q8 = torch.empty(T, NH, L + RP, dtype=torch.uint8, device=dev)
+        mla.q_pack(q_lat, Tp, q[:, self.nope:], self.qh, T, q8, self.q_scale, stream)
         # indexer
         q_idx = torch.empty(T, self.IDX_HEADS * self.IDX_DIM, **bf)
         self.wq_idx(qa, q_idx, status, stream)
@@ -340,8 +335,8 @@ class DsaAttention:
         indexer.expand(ids, positions, tok, stream)
         # sparse MLA over the selected tokens, then v_up and o_proj
         o_lat = torch.empty(T, NH, L, **bf)
-        mla.sparse_mla(q_full, kv_cache, tok, qsl, page_table, self.scale, o_lat, n_idx=4 * self.TOPK + 3,
-                       stream=stream, status=status)
+        mla.sparse_mla(q8, kv_cache, tok, qsl, page_table, self.scale * self.q_scale * self.k_scale, o_lat,
+                       bmm2=self.k_scale, n_idx=4 * self.TOPK + 3, stream=stream, status=status)
         oh = torch.empty(NH * Tp, L, **bf)
         lib.check("ssb_transpose_heads", so.ssb_transpose_heads(o_lat.data_ptr(), oh.data_ptr(), T, Tp, NH, L, NH * L,
                                                                 L, 1, s))
@@ -353,7 +348,7 @@ class DsaAttention:
         out = torch.empty(T, self.H, **bf)
         self.o_proj(o_in, out, status, stream)
         if keep:
-            self.parts = dict(a=a, qa=qa, kvn=kvn, kv_rows=kv_rows, q=q, q_lat=q_lat, q_full=q_full, q_idx=q_idx,
+            self.parts = dict(a=a, qa=qa, kvn=kvn, kv_rows=kv_rows, q=q, q_lat=q_lat, q8=q8, q_idx=q_idx,
                               idx=idx, w=w, logits=logits, ids=ids, tok=tok, o_lat=o_lat, v=v, o_in=o_in)
         return out
 

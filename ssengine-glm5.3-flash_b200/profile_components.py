@@ -30,7 +30,8 @@ ldl = int(((positions.max() + 1) // 4 + 127) // 128 * 128); lg = torch.empty(T, 
 indexer.logits(q, w, kp, tab, groups, lg)
 ids = torch.empty(T, 512, dtype=torch.int32, device=dev); indexer.topk(lg, pos, 512, ids)
 tok = torch.empty(T, 2056, dtype=torch.int32, device=dev); indexer.expand(ids, pos, tok)
-qm = (rnd(T, 64, 576) * 0.5).to(torch.bfloat16); kv = rnd(at * 128, 576).to(torch.bfloat16)
+qm = (rnd(T, 64, 576) * 0.5).to(torch.float8_e4m3fn).view(torch.uint8)
+kv = rnd(at * 128, 576).to(torch.float8_e4m3fn).view(torch.uint8)
 mo = torch.empty(T, 64, 512, dtype=torch.bfloat16, device=dev)
 mla.sparse_mla(qm, kv, tok, torch.from_numpy(qsl).to(dev), tab, 192 ** -0.5, mo, n_idx=2051)
 torch.cuda.synchronize(); del qm, kv, mo, lg

@@ -158,9 +158,9 @@ class StageModel:
                 if dsa:
                     self.layers.append(DsaDecoderLayer(seed, H, F, E, cfg.top_k, self.device, q_lora=cfg.q_lora,
                                                        nope=cfg.mla_nope, v_dim=cfg.mla_v_dim))
-                    # latent cache [pages * 128, 576], pool-key cache [pages * 32, 128], tail ring [blocks, 2, 4, 128]
+                    # latent cache e4m3 [pages * 128, 576], pool-key cache [pages * 32, 128], tail ring [blocks, 2, 4, 128]
                     self.kda_states.append((
-                        torch.zeros(pages * PAGE_TOKENS, 576, dtype=torch.bfloat16, device=self.device),
+                        torch.zeros(pages * PAGE_TOKENS, 576, dtype=torch.uint8, device=self.device),
                         torch.zeros(pages * 32, 128, dtype=torch.bfloat16, device=self.device),
                         torch.zeros(self.num_blocks, 2, 4, 128, dtype=torch.bfloat16, device=self.device)))
                 else:
