@@ -44,7 +44,7 @@ constexpr int kOffP = kOffKv + 2 * kKvBuf;        // P [64 heads x 128 tokens] e
 constexpr int kMaxBlocks = 18;                    // n_idx <= 2304 (the reference selects 2,176)
 constexpr int kMaxIdx = kMaxBlocks * kBlk;
 constexpr int kOffSlots = kOffP + kHeads * 128;   // int32 [2304]: cache row of each index column (-1: none)
-constexpr int kOffMask = kOffSlots + 4 * kMaxIdx; // uint64 [36]: selected columns, 64 a word
+constexpr int kOffMask = kOffSlots + 4 * kMaxIdx; // uint32 [72] (read as uint64 [36]): selected columns
 constexpr int kOffBar = kOffMask + 8 * 2 * kMaxBlocks;   // kv_full[2], kv_empty[2], s_full, p_full, o_done
 constexpr int kOffMisc = kOffBar + 64;            // tmem slot, abort flag, block count
 constexpr int kOffList = kOffMisc + 16;           // uint16 [18]: the blocks holding a selected column, in order
@@ -144,7 +144,6 @@ __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(const MlaArg
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (tid < 2 * kMaxBlocks) tmask[tid] = 0ull;
   if (warp == 0) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
@@ -160,14 +159,15 @@ __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(const MlaArg
     }
 #pragma unroll
     for (int k = 0; k < kPer; ++k) pg[k] = (pos[k] >= 0 && (pos[k] >> 7) < a.width) ? pages[pos[k] >> 7] : -1;
-    __syncthreads();                                     // the selected-column words are zeroed
+    static_assert(kPer * kMlaThreads == kMaxIdx, "every column written");
+    uint32_t* tm32 = reinterpret_cast<uint32_t*>(tmask);
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
-      const int j = tid + kMlaThreads * k;
-      if (j >= kMaxIdx) break;
+      const int j = tid + kMlaThreads * k;           // a warp's 32 lanes: the 32 columns of word j >> 5
       const bool v = pg[k] >= 0 && pg[k] < (1 << 24);
       slots[j] = v ? pg[k] * 128 + (pos[k] & 127) : -1;
-      if (v) atomicOr(tmask + (j >> 6), 1ull << (j & 63));
+      const uint32_t bits = __ballot_sync(0xffffffffu, v);
+      if (lane == 0) tm32[j >> 5] = bits;
     }
   }
   __syncthreads();
