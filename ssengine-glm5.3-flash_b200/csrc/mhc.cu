@@ -9,11 +9,14 @@
 //         comb' = Sinkhorn(softmax_row(mixes[8:24] s2 + b)); y = RMSNorm(bf16(sum_i pre[i] new_res[i])) * w
 // Layout: x [T, H] bf16, res / new_res [T, 4, H] bf16, post [T, 4] fp32, comb [T, 4, 4] fp32, fn [24, 4H] fp32.
 //
-// CTA = 32 tokens, 256 threads; K (= 4H) is walked in chunks of 64 hidden positions x 4 streams: each thread
-// computes 8 positions x 4 streams of one token (16-byte vector loads of x and the 4 residual streams), stores the
-// new residual, and stages the chunk (fp32) and the chunk's 24 fn rows in shared memory; then each thread
-// accumulates 3 of the 32 x 24 mix dot products. HBM traffic per token: 40 KB in (x + res), 32 KB new residual and
-// 8 KB y out; the new residual is re-read from L2 for the layer input.
+// CTA = 32 tokens, 256 threads, up to 2 CTAs per SM. Main loop: warp w takes 16 tokens (tile w & 1) and a quarter of
+// the hidden positions (w >> 1); each lane covers 2 tokens x 8 consecutive positions of every 32-position group
+// (coalesced 16-byte loads of x and the 4 residual streams), forms the 4 new residual streams (bf16, stored) and feeds
+// them directly as tf32 mma.sync fragments against the fn rows (read through the read-only cache with the same
+// permutation of positions): no shared-memory staging and no block barrier in the loop. The quarters' partial mixes
+// are summed in a fixed order in shared memory; then per token the pre / post / Sinkhorn scalars and two passes for
+// the layer input and its RMSNorm. HBM traffic per token: 40 KB in (x + res), 32 KB new residual and 8 KB y out; the
+// new residual is re-read for the layer input.
 
 #include "common.cuh"
 #include "ops.h"
@@ -24,11 +27,8 @@ namespace {
 
 constexpr int kMhcTok = 32;       // tokens per CTA
 constexpr int kMhcThreads = 256;
-constexpr int kMhcH = 64;         // hidden positions per K chunk (x 4 streams = 256 K)
-constexpr int kMhcK = 4 * kMhcH;
+constexpr int kMhcH = 64;         // hidden positions per y-pass step of a thread group
 constexpr int kMhcMix = 24;
-constexpr int kFnPitch = kMhcK + 4;   // 16-byte rows; 260 = 4 (mod 32) spreads the 8 column groups' rows over the banks
-constexpr int kZPitch = kMhcK + 4;    // 16-byte rows; the 4 tokens of a warp read 4 different bank groups
 
 struct MhcArgs {
   const __nv_bfloat16* x;
@@ -52,154 +52,134 @@ SSB_DEVICE float sigmoidf(float v) { return 1.0f / (1.0f + expf(-v)); }
 
 template <bool POST, bool PRE>
 __global__ void __launch_bounds__(kMhcThreads, 2) mhc_kernel(const MhcArgs a) {
-  extern __shared__ __align__(16) float smem_f[];
-  float* zs = smem_f;                                  // [32][257]
-  float* fs = zs + kMhcTok * kZPitch;                  // [24][257]
+  __shared__ float part[4][kMhcTok][kMhcMix];          // per K-quarter partial mixes
+  __shared__ float ssp[4][kMhcTok];
+  __shared__ __align__(16) float coef[kMhcTok][4][8];  // token, output stream j: post[j], comb[0..3][j]
   __shared__ float mix[kMhcTok][kMhcMix];
   __shared__ float ssq[kMhcTok];
   __shared__ float pre_s[kMhcTok][4];
   const int tid = threadIdx.x;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kMhcTok;
-  const int tl = tid >> 3;                             // this thread's token in the tile (chunk phase)
-  const int seg = (tid & 7) * 8;                       // its 8 hidden positions inside the chunk
-  const int64_t t = t0 + tl;
-  const bool tv = t < a.T;
   const int64_t H = a.H;
-  float pm[4] = {0, 0, 0, 0}, cm[4][4];
-  if (POST && tv) {
+  const int warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
+  if (POST) {
+    for (int i = tid; i < kMhcTok * 4; i += kMhcThreads) {
+      const int tk = i >> 2, j = i & 3;
+      const int64_t tt = t0 + tk;
+      float* d = coef[tk][j];
+      const bool ok = tt < a.T;
+      d[0] = ok ? a.post_in[tt * 4 + j] : 0.0f;
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) d[1 + ii] = ok ? a.comb_in[tt * 16 + ii * 4 + j] : 0.0f;
+    }
+    __syncthreads();
+  }
+  // ---- main loop: warp -> 16 tokens (tile w & 1) x one quarter of the hidden positions (w >> 1); lane -> tokens
+  //      g8 and g8 + 8 of the tile and 8 consecutive positions h = g + 8 t4 .. + 7 of each 32-position group g, so a
+  //      quad of lanes reads 64 contiguous bytes of a row. The new residual goes straight into tf32 mma.sync
+  //      fragments: within stream j's 4 k-steps s of a group, MMA k index c < 4 is position g + 8 c + 2 s and c >= 4
+  //      is g + 8 (c - 4) + 2 s + 1 (a permutation of the 32 positions, applied to the fn rows alike). ----
+  const int tr0 = 16 * (warp & 1) + g8, tr1 = tr0 + 8, kq = warp >> 1;
+  const int64_t r0 = t0 + tr0, r1 = t0 + tr1;
+  const bool v0 = r0 < a.T, v1 = r1 < a.T;
+  float macc[3][4] = {};
+  float ss0 = 0.0f, ss1 = 0.0f;
+  const uint4 zero4 = make_uint4(0, 0, 0, 0);
+  for (int64_t g = kq * (H / 4); g < (kq + 1) * (H / 4); g += 32) {
+    const int64_t h = g + 8 * t4;
+    uint4 rv0[4], rv1[4], xv0 = zero4, xv1 = zero4;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      pm[i] = a.post_in[t * 4 + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) cm[i][j] = a.comb_in[t * 16 + i * 4 + j];
+      rv0[i] = v0 ? *reinterpret_cast<const uint4*>(a.res + (r0 * 4 + i) * H + h) : zero4;
+      rv1[i] = v1 ? *reinterpret_cast<const uint4*>(a.res + (r1 * 4 + i) * H + h) : zero4;
     }
-  }
-  float macc[2][3][4] = {};                            // mix partials: token tiles x mix tiles (mma accumulators)
-  const int warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
-  float ss = 0.0f;
-  // x / res rows of the next chunk are loaded while the current one is mixed (software pipeline over the K chunks)
-  uint4 rv_next[4], xv_next = make_uint4(0, 0, 0, 0);
-  if (tv) {
+    if (POST) {
+      if (v0) xv0 = *reinterpret_cast<const uint4*>(a.x + r0 * H + h);
+      if (v1) xv1 = *reinterpret_cast<const uint4*>(a.x + r1 * H + h);
+    }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) rv_next[i] = *reinterpret_cast<const uint4*>(a.res + (t * 4 + i) * H + seg);
-    if (POST) xv_next = *reinterpret_cast<const uint4*>(a.x + t * H + seg);
-  }
-  for (int64_t h0 = 0; h0 < H; h0 += kMhcH) {
-    // ---- new residual of this chunk (all 4 streams, 8 positions per thread) ----
-    float nr[4][8];
-    if (tv) {
-      const int64_t hh = h0 + seg;
-      uint4 rv[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) rv[i] = rv_next[i];
-      const uint4 xv = xv_next;
-      if (h0 + kMhcH < H) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) rv_next[i] = *reinterpret_cast<const uint4*>(a.res + (t * 4 + i) * H + hh + kMhcH);
-        if (POST) xv_next = *reinterpret_cast<const uint4*>(a.x + t * H + hh + kMhcH);
-      }
+    for (int j = 0; j < 4; ++j) {
+      float z0[8], z1[8];
       if (POST) {
-        const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        auto mixrow = [&](const uint4& xv, const uint4 (&rv)[4], const float* c, float (&z)[8]) -> uint4 {
+          const float4 ca = *reinterpret_cast<const float4*>(c), cb = *reinterpret_cast<const float4*>(c + 4);
+          const float cm[4] = {ca.y, ca.z, ca.w, cb.x};
+          const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            float v = pm[j] * __bfloat162float(xb[e]);
+            float v = ca.x * __bfloat162float(xb[e]);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) v = fmaf(cm[i][j], __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rv[i])[e]), v);
-            const __nv_bfloat16 b = __float2bfloat16(v);
-            nr[j][e] = __bfloat162float(b);
-            if (e & 1) w[e >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(b)) << 16;
-            else w[e >> 1] = __bfloat16_as_ushort(b);
+            for (int i = 0; i < 4; ++i)
+              v = fmaf(cm[i], __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rv[i])[e]), v);
+            const __nv_bfloat16 bv = __float2bfloat16(v);
+            z[e] = __bfloat162float(bv);
+            if (e & 1) w[e >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(bv)) << 16;
+            else w[e >> 1] = __bfloat16_as_ushort(bv);
           }
-          *reinterpret_cast<uint4*>(a.new_res + (t * 4 + j) * H + hh) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
+          return make_uint4(w[0], w[1], w[2], w[3]);
+        };
+        const uint4 n0 = mixrow(xv0, rv0, coef[tr0][j], z0);
+        const uint4 n1 = mixrow(xv1, rv1, coef[tr1][j], z1);
+        if (v0) *reinterpret_cast<uint4*>(a.new_res + (r0 * 4 + j) * H + h) = n0;
+        if (v1) *reinterpret_cast<uint4*>(a.new_res + (r1 * 4 + j) * H + h) = n1;
       } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) nr[j][e] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rv[j])[e]);
+        for (int e = 0; e < 8; ++e) {
+          z0[e] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rv0[j])[e]);
+          z1[e] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rv1[j])[e]);
+        }
       }
-    } else {
+      if (PRE) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) nr[j][e] = 0.0f;
-    }
-    if (PRE) {
-      // stage the chunk: z[tl][j * 64 + seg + e], fn rows [c][j * 64 + hh]
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ss = fmaf(nr[j][e], nr[j][e], ss);
-        *reinterpret_cast<float4*>(zs + tl * kZPitch + j * kMhcH + seg) = make_float4(nr[j][0], nr[j][1], nr[j][2], nr[j][3]);
-        *reinterpret_cast<float4*>(zs + tl * kZPitch + j * kMhcH + seg + 4) =
-            make_float4(nr[j][4], nr[j][5], nr[j][6], nr[j][7]);
-      }
-      for (int i = tid; i < kMhcMix * kMhcK / 4; i += kMhcThreads) {
-        const int c = i / (kMhcK / 4), kk = (i - c * (kMhcK / 4)) * 4;
-        const int j = kk / kMhcH, hh = kk - j * kMhcH;
-        *reinterpret_cast<float4*>(fs + c * kFnPitch + kk) =
-            __ldg(reinterpret_cast<const float4*>(a.fn + static_cast<int64_t>(c) * 4 * H + j * H + h0 + hh));
-      }
-      __syncthreads();
-      // mixes[32 tokens x 24] += z[32 x 256] fn_chunk^T on the tensor cores (tf32 m16n8k8; z is bf16-exact in tf32):
-      // warp w takes k-steps 4w .. 4w + 3 for all 2 x 3 (token, mix) tiles
-#pragma unroll
-      for (int kq = 0; kq < 4; ++kq) {
-        const int k0 = (4 * warp + kq) * 8;
-        uint32_t af[2][4], bf[3][2];
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          const float* zr0 = zs + (16 * mt + g8) * kZPitch + k0 + t4;
-          const float* zr1 = zr0 + 8 * kZPitch;
-          af[mt][0] = __float_as_uint(zr0[0]);
-          af[mt][1] = __float_as_uint(zr1[0]);
-          af[mt][2] = __float_as_uint(zr0[4]);
-          af[mt][3] = __float_as_uint(zr1[4]);
+        for (int e = 0; e < 8; ++e) {
+          ss0 = fmaf(z0[e], z0[e], ss0);
+          ss1 = fmaf(z1[e], z1[e], ss1);
         }
 #pragma unroll
         for (int nt = 0; nt < 3; ++nt) {
-          const float* fr = fs + (8 * nt + g8) * kFnPitch + k0 + t4;
-          asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(bf[nt][0]) : "f"(fr[0]));
-          asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(bf[nt][1]) : "f"(fr[4]));
-        }
+          const float* fr = a.fn + static_cast<int64_t>(8 * nt + g8) * 4 * H + j * H + h;
+          const float4 f0 = __ldg(reinterpret_cast<const float4*>(fr)), f1 = __ldg(reinterpret_cast<const float4*>(fr + 4));
+          const float fb[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int nt = 0; nt < 3; ++nt)
+          for (int st = 0; st < 4; ++st) {
+            uint32_t b0, b1;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(b0) : "f"(fb[2 * st]));
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(b1) : "f"(fb[2 * st + 1]));
+            // z is bf16-exact, so its fp32 bits are already tf32
             asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
                          "{%0,%1,%2,%3};"
-                         : "+f"(macc[mt][nt][0]), "+f"(macc[mt][nt][1]), "+f"(macc[mt][nt][2]), "+f"(macc[mt][nt][3])
-                         : "r"(af[mt][0]), "r"(af[mt][1]), "r"(af[mt][2]), "r"(af[mt][3]), "r"(bf[nt][0]),
-                           "r"(bf[nt][1]));
+                         : "+f"(macc[nt][0]), "+f"(macc[nt][1]), "+f"(macc[nt][2]), "+f"(macc[nt][3])
+                         : "r"(__float_as_uint(z0[2 * st])), "r"(__float_as_uint(z1[2 * st])),
+                           "r"(__float_as_uint(z0[2 * st + 1])), "r"(__float_as_uint(z1[2 * st + 1])), "r"(b0), "r"(b1));
+          }
+        }
       }
-      __syncthreads();
     }
   }
   if (!PRE) return;
-  // ---- per-token scalars ----
+  // ---- the 4 K-quarters' partials of the [32 x 24] mixes and of the sums of squares, summed in a fixed order ----
+  ss0 += __shfl_xor_sync(0xFFFFFFFFu, ss0, 1);
+  ss0 += __shfl_xor_sync(0xFFFFFFFFu, ss0, 2);
+  ss1 += __shfl_xor_sync(0xFFFFFFFFu, ss1, 1);
+  ss1 += __shfl_xor_sync(0xFFFFFFFFu, ss1, 2);
+  if (t4 == 0) {
+    ssp[kq][tr0] = ss0;
+    ssp[kq][tr1] = ss1;
+  }
 #pragma unroll
-  for (int off = 4; off > 0; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);   // the 8 threads of a token
-  if ((tid & 7) == 0) ssq[tl] = ss;
-  // the 8 warps' K-slice partials of the [32 x 24] mixes, summed through shared memory (fs is free now)
-  __syncthreads();
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int nt = 0; nt < 3; ++nt)
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        fs[warp * (kMhcTok * kMhcMix) + (16 * mt + g8 + 8 * (q >> 1)) * kMhcMix + 8 * nt + 2 * t4 + (q & 1)] =
-            macc[mt][nt][q];
+  for (int nt = 0; nt < 3; ++nt) {
+    part[kq][tr0][8 * nt + 2 * t4] = macc[nt][0];
+    part[kq][tr0][8 * nt + 2 * t4 + 1] = macc[nt][1];
+    part[kq][tr1][8 * nt + 2 * t4] = macc[nt][2];
+    part[kq][tr1][8 * nt + 2 * t4 + 1] = macc[nt][3];
+  }
   __syncthreads();
   for (int i = tid; i < kMhcTok * kMhcMix; i += kMhcThreads) {
-    float v = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kMhcThreads / 32; ++w) v += fs[w * (kMhcTok * kMhcMix) + i];
-    mix[i / kMhcMix][i % kMhcMix] = v;
+    const int tk = i / kMhcMix, c = i % kMhcMix;
+    mix[tk][c] = ((part[0][tk][c] + part[1][tk][c]) + part[2][tk][c]) + part[3][tk][c];
   }
+  if (tid < kMhcTok) ssq[tid] = ((ssp[0][tid] + ssp[1][tid]) + ssp[2][tid]) + ssp[3][tid];
   __syncthreads();
   if (tid < kMhcTok && t0 + tid < a.T) {
     const int64_t tt = t0 + tid;
@@ -254,6 +234,10 @@ __global__ void __launch_bounds__(kMhcThreads, 2) mhc_kernel(const MhcArgs a) {
       for (int j = 0; j < 4; ++j) a.comb_out[tt * 16 + i * 4 + j] = cb[i][j];
   }
   __syncthreads();
+  const int tl = tid >> 3;                             // this thread's token in the tile (y passes)
+  const int seg = (tid & 7) * 8;                       // its 8 hidden positions in each 64-position step
+  const int64_t t = t0 + tl;
+  const bool tv = t < a.T;
   // ---- layer input and its RMSNorm: token tl, positions seg + 64 m (two passes over the new residual, from L2) ----
   // (no early return: the 8 lanes of a token reduce with shuffles, so every lane of the warp stays)
   const __nv_bfloat16* src = POST ? a.new_res : a.res;
@@ -321,25 +305,17 @@ int launch_mhc(bool do_post, bool do_pre, const void* x, const void* res, const 
                void* new_res, const float* fn, const float* scale, const float* base, const void* norm_w,
                float* post_out, float* comb_out, void* y, int64_t T, int64_t H, float rms_eps, float pre_eps,
                float sinkhorn_eps, float post_mult, int repeat, float norm_eps, cudaStream_t stream) {
-  if (T < 0 || H <= 0 || H % kMhcH != 0 || repeat < 1 || (!do_post && !do_pre)) return kErrArgs;
+  if (T < 0 || H <= 0 || H % 128 != 0 || repeat < 1 || (!do_post && !do_pre)) return kErrArgs;
   if (T == 0) return kOk;
   MhcArgs a{reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(res), post_in, comb_in,
             reinterpret_cast<__nv_bfloat16*>(new_res), fn, scale, base,
             reinterpret_cast<const __nv_bfloat16*>(norm_w), post_out, comb_out, reinterpret_cast<__nv_bfloat16*>(y),
             T, H, rms_eps, pre_eps, sinkhorn_eps, post_mult, norm_eps, repeat};
   const int blocks = static_cast<int>((T + kMhcTok - 1) / kMhcTok);
-  const size_t smem = (static_cast<size_t>(kMhcTok) * kZPitch + kMhcMix * kFnPitch) * sizeof(float);
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(mhc_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
-        cudaFuncSetAttribute(mhc_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return kErrCuda;
-    attr = true;
-  }
   if (do_post && do_pre)
-    mhc_kernel<true, true><<<blocks, kMhcThreads, smem, stream>>>(a);
+    mhc_kernel<true, true><<<blocks, kMhcThreads, 0, stream>>>(a);
   else if (do_pre)
-    mhc_kernel<false, true><<<blocks, kMhcThreads, smem, stream>>>(a);
+    mhc_kernel<false, true><<<blocks, kMhcThreads, 0, stream>>>(a);
   else
     mhc_kernel<true, false><<<blocks, kMhcThreads, 0, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
