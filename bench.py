@@ -373,11 +373,13 @@ def time_components(device, pk: dict) -> dict:
     prm = lib.MhcParamsC(Hm, 4, fn.data_ptr(), scale.data_ptr(), base.data_ptr(), nw.data_ptr(), 1e-6, 1e-2, 1e-6,
                          2.0, 1e-6, 20)
     so = lib.load()
+    ws = torch.empty(int(so.ssb_mhc_workspace_bytes(Tm)), dtype=torch.uint8, device=device)
 
     def mhc():
-        lib.check("ssb_mhc", so.ssb_mhc(ctypes.byref(prm), xm.data_ptr(), res.data_ptr(), pin.data_ptr(),
-                                        cin.data_ptr(), nr.data_ptr(), po.data_ptr(), co.data_ptr(), y.data_ptr(), Tm,
-                                        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+        lib.check("ssb_mhc_ws", so.ssb_mhc_ws(ctypes.byref(prm), xm.data_ptr(), res.data_ptr(), pin.data_ptr(),
+                                              cin.data_ptr(), nr.data_ptr(), po.data_ptr(), co.data_ptr(),
+                                              y.data_ptr(), Tm, ws.data_ptr(), ws.numel(),
+                                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
 
     ms = _event_ms(mhc)
     byts = Tm * (4 * Hm * 2 * 2 + Hm * 2 * 2) + 24 * 4 * Hm * 4

@@ -116,7 +116,7 @@ typedef struct ssb_mhc_params {
   int32_t sinkhorn_repeat;
 } ssb_mhc_params;
 
-/* mHC at a layer boundary, one kernel. With x != NULL (post): new_res bf16 [T, 4, H] = post_in[j] * x + sum_i
+/* mHC at a layer boundary. With x != NULL (post): new_res bf16 [T, 4, H] = post_in[j] * x + sum_i
  * comb_in[i][j] * res[i] (x bf16 [T, H], post_in fp32 [T, 4], comb_in fp32 [T, 4, 4]). With y != NULL (pre, on new_res
  * or, without post, on res): post_out fp32 [T, 4], comb_out fp32 [T, 4, 4] (Sinkhorn) and y bf16 [T, H] = the next
  * layer's RMS-normed input. Both: the reference's fused boundary `MegaMhcPostPre` (ssengine/model/pp_patch.py:125-153,
@@ -124,6 +124,17 @@ typedef struct ssb_mhc_params {
  * config 33); pre only: `edge_recv` + hc_pre (:160-163). */
 int ssb_mhc(const ssb_mhc_params* p, const void* x, const void* res, const float* post_in, const float* comb_in,
             void* new_res, float* post_out, float* comb_out, void* y, int64_t T, void* stream);
+
+/* Device bytes of the partial-mix workspace of a pre step for T rows (4 x T x 25 fp32); -1 for T < 0. */
+int64_t ssb_mhc_workspace_bytes(int64_t T);
+
+/* ssb_mhc with a caller-owned workspace (16-byte aligned, >= ssb_mhc_workspace_bytes(T); returns 3 when smaller), so
+ * that the call allocates nothing; ssb_mhc allocates one on `stream` when it runs a pre step. A pre step is two
+ * launches: the partial mixes of each quarter of the 4H positions for 128-row tiles (post fused), then the
+ * quarters summed in a fixed order, Sinkhorn and the layer input. */
+int ssb_mhc_ws(const ssb_mhc_params* p, const void* x, const void* res, const float* post_in, const float* comb_in,
+               void* new_res, float* post_out, float* comb_out, void* y, int64_t T, void* workspace,
+               int64_t ws_bytes, void* stream);
 
 /* One KDA layer of this stage (device pointers except the scalars). Head dim 128 (key = value). */
 typedef struct ssb_kda_layer {

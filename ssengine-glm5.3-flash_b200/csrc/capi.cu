@@ -215,6 +215,14 @@ int ssb_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64
 
 int ssb_mhc(const ssb_mhc_params* p, const void* x, const void* res, const float* post_in, const float* comb_in,
             void* new_res, float* post_out, float* comb_out, void* y, int64_t T, void* stream) {
+  return ssb_mhc_ws(p, x, res, post_in, comb_in, new_res, post_out, comb_out, y, T, nullptr, 0, stream);
+}
+
+int64_t ssb_mhc_workspace_bytes(int64_t T) { return T < 0 ? -1 : ssb::mhc_workspace_bytes(T); }
+
+int ssb_mhc_ws(const ssb_mhc_params* p, const void* x, const void* res, const float* post_in, const float* comb_in,
+               void* new_res, float* post_out, float* comb_out, void* y, int64_t T, void* workspace,
+               int64_t ws_bytes, void* stream) {
   if (p == nullptr || res == nullptr || T < 0) return kErrArgs;
   const bool do_post = x != nullptr;
   const bool do_pre = y != nullptr;
@@ -225,7 +233,7 @@ int ssb_mhc(const ssb_mhc_params* p, const void* x, const void* res, const float
   if (p->hc_mult != 4) return kErrArgs;
   return ssb::launch_mhc(do_post, do_pre, x, res, post_in, comb_in, new_res, p->fn, p->scale, p->base, p->norm_weight,
                          post_out, comb_out, y, T, p->hidden, p->rms_eps, p->pre_eps, p->sinkhorn_eps, p->post_mult,
-                         p->sinkhorn_repeat, p->norm_eps, static_cast<cudaStream_t>(stream));
+                         p->sinkhorn_repeat, p->norm_eps, workspace, ws_bytes, static_cast<cudaStream_t>(stream));
 }
 
 static bool kda_args(const ssb_kda_layer* L, const void* x, int64_t ldx, const int32_t* seqs, int64_t R,

@@ -80,10 +80,12 @@ int launch_hc_mean(const void* res, int64_t H, const int64_t* rows, int64_t n, v
 int launch_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, cudaStream_t stream);
 
 // mHC layer boundary (csrc/mhc.cu): do_post -> new_res; do_pre -> post_out, comb_out, y.
+int64_t mhc_workspace_bytes(int64_t T);
 int launch_mhc(bool do_post, bool do_pre, const void* x, const void* res, const float* post_in, const float* comb_in,
                void* new_res, const float* fn, const float* scale, const float* base, const void* norm_w,
                float* post_out, float* comb_out, void* y, int64_t T, int64_t H, float rms_eps, float pre_eps,
-               float sinkhorn_eps, float post_mult, int repeat, float norm_eps, cudaStream_t stream);
+               float sinkhorn_eps, float post_mult, int repeat, float norm_eps, void* ws, int64_t ws_bytes,
+               cudaStream_t stream);
 
 // KDA prefill (csrc/kda.cu).
 struct KdaArgs {

@@ -19,9 +19,6 @@ from . import lib
 
 HEAD_DIM = 128
 
-_SCRATCH: dict = {}
-
-
 def workspace_bytes(heads: int, T: int, R: int) -> int:
     """Device bytes of the chunk workspace of one prefill call (`ssb_kda_workspace_bytes`)."""
     n = lib.load().ssb_kda_workspace_bytes(heads, T, R)
@@ -30,16 +27,6 @@ def workspace_bytes(heads: int, T: int, R: int) -> int:
     return int(n)
 
 
-def scratch(device, nbytes: int) -> torch.Tensor:
-    """A per-device uint8 workspace of at least `nbytes`, grown on demand and reused by every call on the device
-    (calls on one stream only, as a stage's layers run)."""
-    dev = torch.device(device)
-    key = (dev.type, dev.index)
-    t = _SCRATCH.get(key)
-    if t is None or t.numel() < nbytes:
-        t = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
-        _SCRATCH[key] = t
-    return t
 
 
 def seq_table(seqs, device) -> torch.Tensor:
@@ -89,7 +76,7 @@ class KdaLayer:
         assert seqs.dtype == torch.int32 and seqs.is_contiguous()
         need = workspace_bytes(self.heads, T, seqs.shape[0])
         if workspace is None:
-            workspace = scratch(qkv.device, need)
+            workspace = lib.scratch(qkv.device, need)
         assert workspace.dtype == torch.uint8 and workspace.is_contiguous() and workspace.numel() >= need
         L = self.c_struct(conv_state, rec_state)
         rc = so.ssb_kda_prefill_ws(ctypes.byref(L), qkv.data_ptr(), qkv.stride(0), g.data_ptr(), g.stride(0),

@@ -127,8 +127,8 @@ class KdaAttention:
 
 
 class MhcBoundary:
-    """One mHC layer boundary (4 streams): the previous sub-block's post and the next sub-block's pre + RMSNorm, in one
-    `ssb_mhc` launch (the reference's `MegaMhcPostPre`, ssengine/model/pp_patch.py:125-153)."""
+    """One mHC layer boundary (4 streams): the previous sub-block's post and the next sub-block's pre + RMSNorm
+    (`ssb_mhc_ws`: the reference's `MegaMhcPostPre`, ssengine/model/pp_patch.py:125-153)."""
 
     def __init__(self, gen: torch.Generator, hidden: int, device, repeat: int = 20):
         H = hidden
@@ -149,12 +149,14 @@ class MhcBoundary:
         import ctypes
 
         T = res.shape[0]
-        rc = self._lib.ssb_mhc(ctypes.byref(self._c), None if x is None else x.data_ptr(), res.data_ptr(),
-                               None if post_in is None else post_in.data_ptr(),
-                               None if comb_in is None else comb_in.data_ptr(),
-                               None if new_res is None else new_res.data_ptr(), post_out.data_ptr(),
-                               comb_out.data_ptr(), y.data_ptr(), T, lib.stream_ptr(stream))
-        lib.check("ssb_mhc", rc)
+        ws = lib.scratch(res.device, int(self._lib.ssb_mhc_workspace_bytes(T)))
+        rc = self._lib.ssb_mhc_ws(ctypes.byref(self._c), None if x is None else x.data_ptr(), res.data_ptr(),
+                                  None if post_in is None else post_in.data_ptr(),
+                                  None if comb_in is None else comb_in.data_ptr(),
+                                  None if new_res is None else new_res.data_ptr(), post_out.data_ptr(),
+                                  comb_out.data_ptr(), y.data_ptr(), T, ws.data_ptr(), ws.numel(),
+                                  lib.stream_ptr(stream))
+        lib.check("ssb_mhc_ws", rc)
 
 
 class KdaDecoderLayer:

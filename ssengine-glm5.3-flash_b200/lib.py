@@ -17,7 +17,7 @@ LIB_PATH = PKG / "libssengine_b200.so"
 EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_gemm", "ssb_moe_route",
            "ssb_moe_workspace_bytes", "ssb_moe_workspace_offsets", "ssb_moe_forward", "ssb_moe_forward_profiled",
            "ssb_moe_route_permute_noalloc", "ssb_topk_canonical", "ssb_stage_metadata", "ssb_embed_rows",
-           "ssb_rmsnorm", "ssb_argmax_rows", "ssb_mhc", "ssb_kda_prefill", "ssb_kda_prefill_ws",
+           "ssb_rmsnorm", "ssb_argmax_rows", "ssb_mhc", "ssb_mhc_ws", "ssb_mhc_workspace_bytes", "ssb_kda_prefill", "ssb_kda_prefill_ws",
            "ssb_kda_workspace_bytes", "ssb_kda_conv",
            "ssb_ipc_export", "ssb_ipc_open", "ssb_ipc_close", "ssb_flag_wait", "ssb_flag_write", "ssb_p2p_copy",
            "ssb_indexer_logits", "ssb_indexer_expand", "ssb_sparse_mla", "ssb_mla_cache_append", "ssb_mla_q_pack",
@@ -88,6 +88,8 @@ _SIGS = {
     "ssb_rmsnorm": ([_P, _I64, _P, _I64, _P, _F, _P, _P], ctypes.c_int),
     "ssb_argmax_rows": ([_P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
     "ssb_mhc": ([ctypes.POINTER(MhcParamsC), _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P], ctypes.c_int),
+    "ssb_mhc_ws": ([ctypes.POINTER(MhcParamsC), _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P, _I64, _P], ctypes.c_int),
+    "ssb_mhc_workspace_bytes": ([_I64], ctypes.c_int64),
     "ssb_kda_prefill": ([ctypes.POINTER(KdaLayerC), _P, _I64, _P, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _P],
                         ctypes.c_int),
     "ssb_kda_prefill_ws": ([ctypes.POINTER(KdaLayerC), _P, _I64, _P, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _P,
@@ -139,6 +141,23 @@ def load(path: Path | None = None):
     if path is None:
         _LIB = lib
     return lib
+
+
+_SCRATCH: dict = {}
+
+
+def scratch(device, nbytes: int):
+    """A per-device uint8 workspace of at least `nbytes`, grown on demand and shared by the calls that take one
+    (`ssb_kda_prefill_ws`, `ssb_mhc_ws`); for calls on one stream, as a stage's layers run."""
+    import torch
+
+    dev = torch.device(device)
+    key = (dev.type, dev.index)
+    t = _SCRATCH.get(key)
+    if t is None or t.numel() < nbytes:
+        t = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+        _SCRATCH[key] = t
+    return t
 
 
 def check(name: str, rc: int) -> None:

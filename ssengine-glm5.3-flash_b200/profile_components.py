@@ -43,7 +43,9 @@ fn = rnd(24, 4 * Hm) / 128; sc = torch.tensor([0.8, 0.6, 1.5], device=dev); base
 nw = torch.ones(Hm, device=dev).to(torch.bfloat16); nr = torch.empty_like(res); po = torch.empty(Tm, 4, device=dev)
 co = torch.empty(Tm, 4, 4, device=dev); y = torch.empty_like(xm)
 prm = lib.MhcParamsC(Hm, 4, fn.data_ptr(), sc.data_ptr(), base.data_ptr(), nw.data_ptr(), 1e-6, 1e-2, 1e-6, 2.0, 1e-6, 20)
-lib.check("mhc", lib.load().ssb_mhc(ctypes.byref(prm), xm.data_ptr(), res.data_ptr(), pin.data_ptr(), cin.data_ptr(),
-          nr.data_ptr(), po.data_ptr(), co.data_ptr(), y.data_ptr(), Tm, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+so = lib.load(); ws = torch.empty(int(so.ssb_mhc_workspace_bytes(Tm)), dtype=torch.uint8, device=dev)
+lib.check("mhc", so.ssb_mhc_ws(ctypes.byref(prm), xm.data_ptr(), res.data_ptr(), pin.data_ptr(), cin.data_ptr(),
+          nr.data_ptr(), po.data_ptr(), co.data_ptr(), y.data_ptr(), Tm, ws.data_ptr(), ws.numel(),
+          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
 torch.cuda.synchronize()
 print("ok")
