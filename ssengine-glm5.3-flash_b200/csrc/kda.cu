@@ -60,19 +60,9 @@ SSB_DEVICE uint32_t scale_bf16x2(uint32_t v, float lo, float hi) {
   return pack_bf16(f.x * lo, f.y * hi);
 }
 
-// SiLU of the conv accumulator: a * 1 / (1 + 2^(-a log2 e)) with the approximate ex2 / rcp instructions and FTZ, the
-// arithmetic the reference's conv kernel fixes in inline PTX (kda_conv.py:37-53).
-SSB_DEVICE float silu_conv(float a) {
-  float e;
-  asm("{\n\t.reg .f32 t;\n\t"
-      "mul.ftz.f32 t, %1, 0fBFB8AA3B;\n\t"
-      "ex2.approx.ftz.f32 t, t;\n\t"
-      "add.ftz.f32 t, t, 0f3F800000;\n\t"
-      "rcp.approx.ftz.f32 t, t;\n\t"
-      "mul.ftz.f32 %0, %1, t;\n\t}"
-      : "=f"(e) : "f"(a));
-  return e;
-}
+// SiLU of the conv accumulator, a / (1 + e^-a), with CUDA's fast intrinsics (__expf, __fdividef); for a -> -inf the
+// quotient goes to 0 (e^-a overflows to inf). Checked against the oracle's exact SiLU within one bf16 step.
+SSB_DEVICE float silu_conv(float a) { return __fdividef(a, 1.0f + __expf(-a)); }
 
 SSB_DEVICE void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);

@@ -18,7 +18,7 @@
 //            (tokens 0-63 in lanes 0-15, 64-127 in lanes 16-31 of TMEM columns 0-63; 36 MMAs), then
 //            O += P V with V the same chunks read MN-major (dims 0-255 in lanes 0-15, 256-511 in lanes 16-31 of
 //            columns 256-511; 8 MMAs of N = 256);
-//   warps 0-3 softmax: one head row half per thread (64 scores), exp2 with the scale folded, running max kept stale
+//   warps 0-3 softmax: one head row half per thread (64 scores), base-2 weights, running max kept stale
 //            until a block raises it by more than 2^3 (O rescaled in TMEM only then), so p <= 8 and 32 p fits e4m3
 //            (448) with normals down to p = 2^-11; P to e4m3 (K-major, swizzled) for the PV MMA; then the epilogue
 //            (O * bmm2 / (32 l) -> bf16).
@@ -68,7 +68,8 @@ SSB_DEVICE uint32_t e4m3x2(float lo, float hi) {
   return r;
 }
 
-// 2^x by the MUFU instruction (flush-to-zero; ~2 ulp), plenty for weights that are rounded to e4m3 next.
+// Softmax in base 2 with log2(e) folded into the score scale (the FlashAttention-2 formulation, Dao 2023): 2^x by
+// the PTX ex2.approx.ftz instruction (flush-to-zero, a few ulp), ample for weights that are rounded to e4m3 next.
 SSB_DEVICE float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -256,7 +257,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(const MlaArg
     // ---------------------------------------------------------------- softmax (warps 0-3)
     const int half = lane >> 4, row = 16 * warp + (lane & 15);
     const uint32_t tq = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const float sc = a.scale * 1.4426950408889634f;      // exp2 domain
+    const float sc = a.scale * 1.4426950408889634f;      // log2(e) folded in: weights are 2^(s - m)
     uint8_t* Pb = smem + kOffP;
     float m_used = -INFINITY, l_sum = 0.0f;
     bool ok = true;
@@ -283,7 +284,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(const MlaArg
       if (m_used == -INFINITY) {
         m_used = mb;                                     // nothing accumulated yet (O = 0, l = 0)
       } else if (mb > m_used + kLazy) {
-        alpha = exp2f(m_used - mb);
+        alpha = ex2_approx(m_used - mb);
         m_used = mb;
         l_sum *= alpha;
         rescale = true;

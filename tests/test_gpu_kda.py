@@ -2,8 +2,8 @@
 sequences (1 row, partial and whole 64-token chunks, several chunks), fresh and continued requests, rows outside every
 sequence, states of other blocks untouched, and a request split across two calls.
 
-Tolerances: conv outputs within one bf16 step of the oracle (the kernel's SiLU uses the approximate ex2 / rcp
-instructions, the oracle exact exp) and >= 99% bit-equal; conv state blocks bit-exact (copies); KDA outputs and final
+Tolerances: conv outputs within one bf16 step of the oracle (the kernel's SiLU uses the fast __expf / __fdividef
+intrinsics, the oracle exact exp) and >= 99% bit-equal; conv state blocks bit-exact (copies); KDA outputs and final
 recurrent states within 2e-2 relative L2 of the float64 token-by-token recurrence (the chunked scan rounds its
 tensor-core operands to bf16; measured on the CPU model of the same factorisation: ~3e-3)."""
 
