@@ -3,21 +3,25 @@
 //
 //   D[m, n] = alpha[g] * sum_k (a[m, k] * sfa[m, k/16]) * (b[g*N + n, k] * sfb[g*N + n, k/16])
 //
-// Roles (352 threads, one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer: A tile 128 x 256 (e2m1, 128-byte swizzle), B tile BN x 256, and their scale atoms by
-//               plain bulk copies; STAGES-deep ring of shared-memory stages guarded by full/empty mbarriers.
-//   warp 1      TMEM owner and MMA issuer (one thread): per k-block 4 MMAs of K = 64 reading that stage's scales
-//               from TMEM; tcgen05.commit frees the stage and, after the tile's last k-block, signals the accumulator
-//               full.
-//   warp 2      scale copies (one thread): per k-block the 4 A and 4 * BN / 128 B scale atoms of the stage into the
-//               stage's own TMEM columns (tcgen05.cp 32x128b.warpx4), then a commit on the stage's sf barrier. A copy
-//               costs about as much tensor-pipe time whatever its size; issued from their own warp into per-stage
-//               columns the copies overlap in part with the MMAs of the previous stage (measured: 7-10% faster than
-//               issuing them from the MMA thread); the per-stage columns are what makes that safe, since the two
-//               threads' tcgen05 operations are not ordered with each other.
+// Roles (448 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: per k-block first the stage's scale atoms (plain bulk copies, on the stage's sf_full
+//               barrier), then the A tile 128 x 256 (e2m1, 128-byte swizzle) and the B tile BN x 256 (on its full
+//               barrier); STAGES-deep ring of shared-memory stages freed through the empty barriers.
+//   warp 1      TMEM owner and MMA issuer (one thread): per k-block, once the stage's operands landed and its scales
+//               are in TMEM, 4 MMAs of K = 64; tcgen05.commit frees the stage and, after the tile's last k-block,
+//               signals the accumulator full.
+//   warps 2, 11-13  scale writers, one per TMEM lane quarter (warp % 4): per k-block each reads the stage's scale
+//               atoms from shared memory and writes with tcgen05.st exactly the words its quarter's MMA datapath
+//               reads (the scale of row m sits in lane m % 32 of every quarter, column m / 32: the A scales of the
+//               quarter's own 32 rows, the B scales of all BN rows), then arrives on the stage's sf barrier. This
+//               replaces 4 + 4 * BN / 128 tcgen05.cp copies per k-block, each of which held the tensor pipe about
+//               55 cycles beside 512 cycles of MMAs; the scales are loaded first so that the writers finish while
+//               the operand tiles are still landing.
 //   warps 3-10  epilogue: two warps per TMEM lane quadrant (32 rows), each owning half of the tile's columns; a warp
-//               copies its accumulator share to registers (tcgen05.ld), releases the accumulator at once so the MMAs
-//               of the next tile start, then runs the output stage from registers, overlapping the next mainloop.
+//               copies its accumulator share to registers (tcgen05.ld), releases the accumulator so the MMAs of the
+//               next tile start, then runs the output stage from registers, overlapping the next mainloop. The bf16
+//               output goes through a per-warp shared-memory buffer so that each store instruction writes whole
+//               128-byte row segments.
 // Tiles are M-major over N tiles (consecutive CTAs share the A row block and walk one expert's weights), so an
 // expert's weights stay in L2 while its row blocks are in flight.
 // Every wait is bounded (common.cuh); on expiry all roles leave, in-flight copies and MMAs are drained with bounded
@@ -32,33 +36,48 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBKBytes = 128;   // one k-block: 256 e2m1 elements = 128 bytes = one 128-byte swizzle row
-constexpr int kThreads = 352;   // warp 0 TMA, warp 1 MMA, warp 2 scale copies, warps 3-10 epilogue
+constexpr int kThreads = 448;   // warp 0 TMA, warp 1 MMA, warps 2 and 11-13 scale writers, warps 3-10 epilogue
 constexpr int kEpiWarp0 = 3;
+constexpr int kEpiWarps = 8;
+constexpr int kOutStage = 4096; // bf16 epilogue: per-warp staging buffer, 32 rows x 64 columns
 
-template <int BN>
+template <int BN, int EPI>
 struct Cfg {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  // the bf16 epilogue's staging buffers take the room of one stage
+  static constexpr int STAGES = BN == 256 ? (EPI == kEpiBF16 ? 3 : 4) : 6;
   static constexpr int A_BYTES = kBM * kBKBytes;               // 16 KB
   static constexpr int B_BYTES = BN * kBKBytes;
   static constexpr int SFA_BYTES = 2048;                        // 4 atoms (128 rows x 64 K each)
   static constexpr int SFB_BYTES = (BN / 128) * 2048;
-  static constexpr int TX_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  static constexpr int AB_TX = A_BYTES + B_BYTES;
+  static constexpr int SF_TX = SFA_BYTES + SFB_BYTES;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_SFA = OFF_B + STAGES * B_BYTES;
   static constexpr int OFF_SFB = OFF_SFA + STAGES * SFA_BYTES;
-  // full[S], empty[S], sf[S], acc_full, acc_empty, drain
-  static constexpr int OFF_BAR = OFF_SFB + STAGES * SFB_BYTES;
-  static constexpr int OFF_MISC = OFF_BAR + (3 * STAGES + 3) * 8;
+  static constexpr int OFF_OUT = OFF_SFB + STAGES * SFB_BYTES;
+  static constexpr int OUT_BYTES = EPI == kEpiBF16 ? kEpiWarps * kOutStage : 0;
+  // full[S], sf_full[S], sf[S], empty[S], acc_full, acc_empty, drain
+  static constexpr int OFF_BAR = OFF_OUT + OUT_BYTES;
+  static constexpr int OFF_MISC = OFF_BAR + (4 * STAGES + 3) * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;             // + alignment slack
+  static_assert(SMEM <= 232448, "shared memory per block");
   // TMEM columns: accumulator [0, BN); per stage s, at BN + s * SF_STRIDE: A scales 16 columns (4 per MMA),
   // B scales BN / 8 columns (BN / 32 per MMA)
   static constexpr int SF_STRIDE = 16 + BN / 8;
   static constexpr int SFA_COL = BN;
-  static constexpr int SFB_COL = BN + 16;
   static constexpr int TMEM_COLS = (BN + STAGES * SF_STRIDE) <= 256 ? 256 : 512;
   static_assert(BN + STAGES * SF_STRIDE <= 512, "TMEM columns");
 };
+
+SSB_DEVICE void tmem_st_x16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
 
 struct TileInfo {
   int group, row0, rows, nt;
@@ -102,16 +121,17 @@ template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const GemmArgs args) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar_full = sbase + C::OFF_BAR;
-  const uint32_t bar_empty = bar_full + C::STAGES * 8;
+  const uint32_t bar_full = sbase + C::OFF_BAR;                 // operand tiles landed (TMA)
+  const uint32_t bar_sf_full = bar_full + C::STAGES * 8;        // scale atoms landed (bulk copies)
+  const uint32_t bar_sf = bar_sf_full + C::STAGES * 8;          // scales written to TMEM (4 writer warps)
+  const uint32_t bar_empty = bar_sf + C::STAGES * 8;            // the stage's MMAs completed
   const uint32_t bar_acc_full = bar_empty + C::STAGES * 8;
   const uint32_t bar_acc_empty = bar_acc_full + 8;
   const uint32_t bar_drain = bar_acc_empty + 8;
-  const uint32_t bar_sf = bar_drain + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + C::OFF_MISC + 4);
 
@@ -121,8 +141,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_sf_full + 8 * s, 1);
+      mbar_init(bar_sf + 8 * s, 128);
       mbar_init(bar_empty + 8 * s, 1);
-      mbar_init(bar_sf + 8 * s, 1);
     }
     mbar_init(bar_acc_full, 1);
     mbar_init(bar_acc_empty, 8);
@@ -164,15 +185,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          const uint32_t fb = bar_full + 8 * stage;
-          mbar_arrive_expect_tx(fb, C::TX_BYTES);
-          tma_load_2d(sbase + C::OFF_A + stage * C::A_BYTES, &tmA, kb * kBKBytes, ti.row0, fb);
-          tma_load_2d(sbase + C::OFF_B + stage * C::B_BYTES, &tmB, kb * kBKBytes, brow0, fb);
-          bulk_load(sbase + C::OFF_SFA + stage * C::SFA_BYTES, sfa + (int64_t)kb * 2048, 2048, fb);
+          const uint32_t sb = bar_sf_full + 8 * stage;
+          mbar_arrive_expect_tx(sb, C::SF_TX);
+          bulk_load(sbase + C::OFF_SFA + stage * C::SFA_BYTES, sfa + (int64_t)kb * 2048, 2048, sb);
 #pragma unroll
           for (int j = 0; j < BN / 128; ++j)
             bulk_load(sbase + C::OFF_SFB + stage * C::SFB_BYTES + j * 2048,
-                      sfb + ((int64_t)j * args.ncb_k + kb * 4) * 512, 2048, fb);
+                      sfb + ((int64_t)j * args.ncb_k + kb * 4) * 512, 2048, sb);
+          const uint32_t fb = bar_full + 8 * stage;
+          mbar_arrive_expect_tx(fb, C::AB_TX);
+          tma_load_2d(sbase + C::OFF_A + stage * C::A_BYTES, &tmA, kb * kBKBytes, ti.row0, fb);
+          tma_load_2d(sbase + C::OFF_B + stage * C::B_BYTES, &tmB, kb * kBKBytes, brow0, fb);
           ++issued;
           if (++stage == C::STAGES) {
             stage = 0;
@@ -189,6 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             s = C::STAGES - 1;
             p ^= 1;
           }
+          drain_wait(bar_sf_full + 8 * s, p);
           drain_wait(bar_full + 8 * s, p);
         }
       }
@@ -211,8 +235,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         for (int kb = 0; kb < num_kb; ++kb) {
-          // the sf barrier completes after the stage's data landed and its scales reached TMEM
-          if (!mbar_wait(bar_sf + 8 * stage, phase, abort_flag, args.status)) {
+          if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, args.status) ||
+              !mbar_wait(bar_sf + 8 * stage, phase, abort_flag, args.status)) {
             ok = false;
             break;
           }
@@ -225,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t ad = smem_desc(sa + i * 32, 0, 1024, 2);
             const uint64_t bd = smem_desc(sb + i * 32, 0, 1024, 2);
             tc_mma_nvf4(tmem, ad, bd, idesc, (kb | i) != 0 ? 1u : 0u, tmem + sfo + C::SFA_COL + 4 * i,
-                        tmem + sfo + C::SFB_COL + (BN / 32) * i);
+                        tmem + sfo + C::SFA_COL + 16 + (BN / 32) * i);
           }
           any_mma = true;
           tc_commit(bar_empty + 8 * stage);
@@ -243,46 +267,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         drain_wait(bar_drain, 0);
       }
     }
-  } else if (warp == 2) {
-    if (lane == 0) {
-      // ---------------- scale copies ----------------
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      bool any_cp = false;
-      int last_s = 0;
-      uint32_t last_p = 0;
-      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-        TileInfo ti;
-        if (!tile_info(args, t, n_tiles, ti)) continue;
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, args.status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t ssfa = sbase + C::OFF_SFA + stage * C::SFA_BYTES;
-          const uint32_t ssfb = sbase + C::OFF_SFB + stage * C::SFB_BYTES;
-          const uint32_t sfo = stage * C::SF_STRIDE;
+  } else if (warp == 2 || warp >= kEpiWarp0 + kEpiWarps) {
+    // ---------------- scale writers (warps 2, 11, 12, 13: TMEM lane quarters 2, 3, 0, 1) ----------------
+    // Per stage, TMEM columns [SFA_COL, +16): A scales, 4 columns per MMA, every column of a group holding the
+    // quarter's own rows' word (the datapath of quarter q reads column q of the group); [SFA_COL + 16, + BN / 8): B
+    // scales, BN / 32 columns per MMA, column c holding rows 32 c + lane of the B tile, the same in every quarter.
+    // Source: the 128x4 atoms of the stage, whose 16-byte row l holds rows l, l + 32, l + 64, l + 96.
+    const int q = warp & 3;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+      TileInfo ti;
+      if (!tile_info(args, t, n_tiles, ti)) continue;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        // the stage's previous MMAs completed before its scale copies were issued, so its columns are free
+        if (!mbar_wait(bar_sf_full + 8 * stage, phase, abort_flag, args.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint8_t* ssfa = smem + C::OFF_SFA + stage * C::SFA_BYTES + 16 * lane;
+        const uint8_t* ssfb = smem + C::OFF_SFB + stage * C::SFB_BYTES + 16 * lane;
+        uint32_t w[16 + BN / 8];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            tc_cp_sf(tmem + sfo + C::SFA_COL + 4 * i, smem_desc(ssfa + i * 512, 0, 128, 0));
+        for (int i = 0; i < 4; ++i) {
+          const uint4 v = *reinterpret_cast<const uint4*>(ssfa + i * 512);
+          const uint32_t a = q == 0 ? v.x : q == 1 ? v.y : q == 2 ? v.z : v.w;
+          w[4 * i] = a;
+          w[4 * i + 1] = a;
+          w[4 * i + 2] = a;
+          w[4 * i + 3] = a;
 #pragma unroll
-            for (int j = 0; j < BN / 128; ++j)
-              tc_cp_sf(tmem + sfo + C::SFB_COL + (BN / 32) * i + 4 * j,
-                       smem_desc(ssfb + j * 2048 + i * 512, 0, 128, 0));
-          }
-          any_cp = true;
-          tc_commit(bar_sf + 8 * stage);
-          last_s = stage;
-          last_p = phase;
-          if (++stage == C::STAGES) {
-            stage = 0;
-            phase ^= 1;
+          for (int j = 0; j < BN / 128; ++j) {
+            const uint4 b = *reinterpret_cast<const uint4*>(ssfb + j * 2048 + i * 512);
+            w[16 + (BN / 32) * i + 4 * j] = b.x;
+            w[16 + (BN / 32) * i + 4 * j + 1] = b.y;
+            w[16 + (BN / 32) * i + 4 * j + 2] = b.z;
+            w[16 + (BN / 32) * i + 4 * j + 3] = b.w;
           }
         }
+        const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) + stage * C::SF_STRIDE + C::SFA_COL;
+#pragma unroll
+        for (int c = 0; c < (16 + BN / 8) / 16; ++c) tmem_st_x16(ta + 16 * c, w + 16 * c);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar_sf + 8 * stage);
+        if (++stage == C::STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
       }
-      if (!ok && any_cp) drain_wait(bar_sf + 8 * last_s, last_p);   // copies land before TMEM is freed
     }
   } else {
     // ---------------- epilogue (warps 3..10) ----------------
@@ -334,29 +369,58 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint32_t*>(args.out_sf + sf_atom_offset(row, col / 16, args.out_ncb)) = sfw;
         }
       } else if constexpr (EPI == kEpiBF16) {
-        // columns [128 half, +128)
-        float v[128];
+        // columns [128 half, +128), 64 per tcgen05.ld round: to bf16 pairs, through this warp's staging buffer (row
+        // r's 16-byte chunk c at chunk c ^ (r & 7): conflict-free both ways) to stores of whole 128-byte row segments,
+        // 4 rows per instruction. The first round is staged before the second is loaded (fewer live registers).
+        uint8_t* stg = smem + C::OFF_OUT + (warp - kEpiWarp0) * kOutStage;
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+        const int64_t base_row = (int64_t)ti.row0 + quad * 32;
+        const int col0 = ti.nt * BN + 128 * half;
+        uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          tmem_ld_32x32b_x32(tq + 128 * half + 32 * c, *reinterpret_cast<float(*)[32]>(v + 32 * c));
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_acc_empty);
-        if (valid) {
-          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
-          uint4* dst = reinterpret_cast<uint4*>(out + row * args.ldo + ti.nt * BN + 128 * half);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            uint32_t w[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * i + 2 * j] * alpha, v[8 * i + 2 * j + 1] * alpha);
-              w[j] = *reinterpret_cast<uint32_t*>(&b2);
-            }
-            dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int h = 0; h < 2; ++h) {
+          float v[64];
+          tmem_ld_32x32b_x32(tq + 128 * half + 64 * h, *reinterpret_cast<float(*)[32]>(v));
+          tmem_ld_32x32b_x32(tq + 128 * half + 64 * h + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+          tmem_ld_wait();
+          if (h == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_acc_empty);
           }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * j] * alpha, v[2 * j + 1] * alpha);
+            pk[j] = *reinterpret_cast<uint32_t*>(&b2);
+          }
+          if (h == 1) {
+            // round 0 is in the buffer: store it, then stage round 1
+            __syncwarp();
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+              const int r = 4 * it + (lane >> 3);
+              const int c = lane & 7;
+              const uint4 val = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
+              if (quad * 32 + r < ti.rows)
+                *reinterpret_cast<uint4*>(out + (base_row + r) * args.ldo + col0 + 8 * c) = val;
+            }
+            __syncwarp();
+          }
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
         }
+        __syncwarp();
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int r = 4 * it + (lane >> 3);
+          const int c = lane & 7;
+          const uint4 val = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
+          if (quad * 32 + r < ti.rows)
+            *reinterpret_cast<uint4*>(out + (base_row + r) * args.ldo + col0 + 64 + 8 * c) = val;
+        }
+        __syncwarp();
       } else {
         // columns [64 half, +64) of a 128-wide tile
         float v[64];
@@ -428,7 +492,7 @@ int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t width, int6
 
 template <int BN, int EPI>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int grid, cudaStream_t stream) {
-  using Cf = Cfg<BN>;
+  using Cf = Cfg<BN, EPI>;
   auto kern = gemm_nvfp4_kernel<BN, EPI>;
   static bool attr_set = false;
   if (!attr_set) {
