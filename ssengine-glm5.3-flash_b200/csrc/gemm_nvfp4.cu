@@ -20,8 +20,8 @@
 //   warps 3-10  epilogue: two warps per TMEM lane quadrant (32 rows), each owning half of the tile's columns; a warp
 //               copies its accumulator share to registers (tcgen05.ld), releases the accumulator so the MMAs of the
 //               next tile start, then runs the output stage from registers, overlapping the next mainloop. The bf16
-//               output goes through a per-warp shared-memory buffer so that each store instruction writes whole
-//               128-byte row segments.
+//               output goes through a per-warp shared-memory buffer in the 128-byte swizzle layout and leaves by TMA
+//               tensor stores (32 rows x 64 columns each), so the warp moves on while the copy engine writes.
 // Tiles are M-major over N tiles (consecutive CTAs share the A row block and walk one expert's weights), so an
 // expert's weights stay in L2 while its row blocks are in flight.
 // Every wait is bounded (common.cuh); on expiry all roles leave, in-flight copies and MMAs are drained with bounded
@@ -69,6 +69,15 @@ struct Cfg {
   static constexpr int TMEM_COLS = (BN + STAGES * SF_STRIDE) <= 256 ? 256 : 512;
   static_assert(BN + STAGES * SF_STRIDE <= 512, "TMEM columns");
 };
+
+// shared -> global tensor-map store of one box, tracked by the issuing thread's bulk groups
+SSB_DEVICE void tma_store_2d(const CUtensorMap* m, uint32_t src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+SSB_DEVICE void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 SSB_DEVICE void tmem_st_x16(uint32_t taddr, const uint32_t* v) {
   asm volatile(
@@ -120,7 +129,7 @@ SSB_DEVICE void drain_wait(uint32_t bar, uint32_t parity) {
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const GemmArgs args) {
+                      const __grid_constant__ CUtensorMap tmO, const GemmArgs args) {
   using C = Cfg<BN, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -369,14 +378,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint32_t*>(args.out_sf + sf_atom_offset(row, col / 16, args.out_ncb)) = sfw;
         }
       } else if constexpr (EPI == kEpiBF16) {
-        // columns [128 half, +128), 64 per tcgen05.ld round: to bf16 pairs, through this warp's staging buffer (row
-        // r's 16-byte chunk c at chunk c ^ (r & 7): conflict-free both ways) to stores of whole 128-byte row segments,
-        // 4 rows per instruction. The first round is staged before the second is loaded (fewer live registers).
-        uint8_t* stg = smem + C::OFF_OUT + (warp - kEpiWarp0) * kOutStage;
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
-        const int64_t base_row = (int64_t)ti.row0 + quad * 32;
-        const int col0 = ti.nt * BN + 128 * half;
-        uint32_t pk[32];
+        // columns [128 half, +128), 64 per tcgen05.ld round: to bf16 pairs, into this warp's staging buffer (row r's
+        // 16-byte chunk c at chunk c ^ (r & 7), the 128-byte swizzle of the output map; conflict-free), then one TMA
+        // store of the 32 x 64 box. Rows past the tile's valid rows are the group's padding rows (or past the map's
+        // rows, where the store is clipped).
+        const uint32_t stg = sbase + C::OFF_OUT + (warp - kEpiWarp0) * kOutStage;
+        const int y0 = ti.row0 + quad * 32;
+        const int x0 = ti.nt * BN + 128 * half;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float v[64];
@@ -388,39 +396,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_acc_empty);
           }
+          uint32_t pk[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * j] * alpha, v[2 * j + 1] * alpha);
             pk[j] = *reinterpret_cast<uint32_t*>(&b2);
           }
-          if (h == 1) {
-            // round 0 is in the buffer: store it, then stage round 1
-            __syncwarp();
+          if (lane == 0) bulk_wait_read0();             // the previous store has read the buffer
+          __syncwarp();
 #pragma unroll
-            for (int it = 0; it < 8; ++it) {
-              const int r = 4 * it + (lane >> 3);
-              const int c = lane & 7;
-              const uint4 val = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
-              if (quad * 32 + r < ti.rows)
-                *reinterpret_cast<uint4*>(out + (base_row + r) * args.ldo + col0 + 8 * c) = val;
-            }
-            __syncwarp();
+          for (int c = 0; c < 8; ++c) {
+            const uint32_t a = stg + lane * 128 + ((c ^ (lane & 7)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(pk[4 * c]), "r"(pk[4 * c + 1]),
+                         "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
+                         : "memory");
           }
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
-                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmO, stg, x0 + 64 * h, y0);
+            bulk_commit();
+          }
         }
-        __syncwarp();
-#pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          const int r = 4 * it + (lane >> 3);
-          const int c = lane & 7;
-          const uint4 val = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
-          if (quad * 32 + r < ti.rows)
-            *reinterpret_cast<uint4*>(out + (base_row + r) * args.ldo + col0 + 64 + 8 * c) = val;
-        }
-        __syncwarp();
       } else {
         // columns [64 half, +64) of a 128-wide tile
         float v[64];
@@ -446,6 +443,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       ++iter;
+    }
+    if constexpr (EPI == kEpiBF16) {
+      if (lane == 0) bulk_wait0();                     // the output stores completed before the CTA exits
     }
   }
 
@@ -491,7 +491,8 @@ int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t width, int6
 }
 
 template <int BN, int EPI>
-int launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int grid, cudaStream_t stream) {
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const GemmArgs& args, int grid,
+           cudaStream_t stream) {
   using Cf = Cfg<BN, EPI>;
   auto kern = gemm_nvfp4_kernel<BN, EPI>;
   static bool attr_set = false;
@@ -500,7 +501,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, i
       return kErrCuda;
     attr_set = true;
   }
-  kern<<<grid, kThreads, Cf::SMEM, stream>>>(ma, mb, args);
+  kern<<<grid, kThreads, Cf::SMEM, stream>>>(ma, mb, mo, args);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
@@ -570,11 +571,16 @@ int launch_gemm_nvfp4(int epilogue, const uint8_t* a, int64_t a_rows, int64_t ld
   }
   switch (epilogue) {
     case kEpiF32:
-      return launch<128, kEpiF32>(ma, mb, args, grid, stream);
-    case kEpiBF16:
-      return launch<256, kEpiBF16>(ma, mb, args, grid, stream);
+      return launch<128, kEpiF32>(ma, mb, ma, args, grid, stream);
+    case kEpiBF16: {
+      // output map: [a_rows, N] bf16 rows of pitch ldo, box 64 columns x 32 rows, 128-byte swizzle
+      CUtensorMap mo;
+      rc = make_map_2d_swizzled(&mo, args.out, a_rows, args.N, args.ldo * 2, 32);
+      if (rc != kOk) return rc;
+      return launch<256, kEpiBF16>(ma, mb, mo, args, grid, stream);
+    }
     case kEpiSwiGLU:
-      return launch<256, kEpiSwiGLU>(ma, mb, args, grid, stream);
+      return launch<256, kEpiSwiGLU>(ma, mb, ma, args, grid, stream);
     default:
       return kErrArgs;
   }
