@@ -32,7 +32,7 @@ SEED = 20261201
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch at T = 8192, from the ncu capture summarised in
 # profiles/gemm_nvfp4_moe_T8192_full.md (796.9 MB + 39.6 MB); None for other token counts
-GATE_UP_TRAFFIC_T8192 = 836.5e6
+GATE_UP_TRAFFIC_T8192 = 836.4e6
 
 
 def parse():
@@ -439,7 +439,7 @@ def time_components(device, pk: dict) -> dict:
     torch.cuda.empty_cache()
     out["workload"] = (f"BASELINE config 3 attention pair: {T} tokens from {R} requests (new tokens lognormal median "
                        f"2k, cached prefixes 0-64k; KDA 32 x 128, DSA indexer 32 x 128 top-512 pools of 4, sparse MLA "
-                       f"64 heads latent 512 + rope 64, bf16 latent cache); mHC at T = 8192, H = 4096")
+                       f"64 heads latent 512 + rope 64, FP8 e4m3 query and latent cache); mHC at T = 8192, H = 4096")
     return out
 
 
