@@ -308,8 +308,9 @@ int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T);
 #define SSB_WS_OFFSETS 7     /* int32 [E+2] first permuted row per expert (128-aligned), total rows last */
 #define SSB_WS_MASKS 8
 #define SSB_WS_BLOCKS 9
-#define SSB_WS_MTILES 10     /* int32 [cap, 4] GEMM row tiles {expert, first row, rows, 0} */
-#define SSB_WS_NUM_MTILES 11 /* int32 [1] */
+#define SSB_WS_MTILES 10     /* int32 [cap, 4] GEMM row tiles {expert, first row, rows, 0}, then int32 [pair cap, 4]
+                                CTA-pair tiles {expert, first row, rows of the first 128, rows of the next 128} */
+#define SSB_WS_NUM_MTILES 11 /* int32 [2]: row tiles, CTA-pair tiles */
 #define SSB_WS_XQ_PERM 12    /* uint8 [cap*128, H/2] permuted input codes */
 #define SSB_WS_XSF_PERM 13
 #define SSB_WS_ACT 14        /* uint8 [cap*128, F/2] SwiGLU output codes */

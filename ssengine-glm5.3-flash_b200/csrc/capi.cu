@@ -17,7 +17,7 @@ int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 struct MoeDims {
-  int64_t T, H, F, E, k, Tpad, rcap, mtile_cap, nblocks, ncbH, ncbF;
+  int64_t T, H, F, E, k, Tpad, rcap, mtile_cap, mpair_cap, nblocks, ncbH, ncbF;
 };
 
 bool dims_of(const ssb_moe_layer* L, int64_t T, MoeDims& d) {
@@ -34,6 +34,7 @@ bool dims_of(const ssb_moe_layer* L, int64_t T, MoeDims& d) {
   d.rcap = ceil_div(T * (d.k + 1) + (d.E + 1) * 127, 128) * 128;
   if (d.rcap < 128) d.rcap = 128;
   d.mtile_cap = d.rcap / 128;
+  d.mpair_cap = (d.mtile_cap + d.E + 1) / 2 + 1;   // sum over experts of ceil(tiles / 2)
   d.nblocks = ceil_div(T > 0 ? T : 1, 256);
   d.ncbH = ssb::sf_atom_cols(d.H);
   d.ncbF = ssb::sf_atom_cols(d.F);
@@ -52,7 +53,7 @@ void layout(const MoeDims& d, int64_t* off) {
   sz[SSB_WS_OFFSETS] = (d.E + 2) * 4;
   sz[SSB_WS_MASKS] = d.nblocks * d.E * 8 * 4;
   sz[SSB_WS_BLOCKS] = d.nblocks * d.E * 4;
-  sz[SSB_WS_MTILES] = d.mtile_cap * 16;
+  sz[SSB_WS_MTILES] = (d.mtile_cap + d.mpair_cap) * 16;   // tile table, then the CTA-pair table
   sz[SSB_WS_NUM_MTILES] = 16;
   sz[SSB_WS_XQ_PERM] = d.rcap * d.H / 2;
   sz[SSB_WS_XSF_PERM] = (d.rcap / 128) * d.ncbH * 512;
@@ -461,8 +462,10 @@ int moe_forward(const ssb_moe_layer* L, const void* x, int64_t T, void* out, voi
   rc = ssb::launch_moe_count(ids, T, static_cast<int32_t>(d.E), static_cast<int32_t>(d.k), masks, bcounts, stream);
   if (rc != kOk) return rc;
   mark(4);
+  int32_t* mpairs = mtiles + 4 * d.mtile_cap;
   rc = ssb::launch_moe_offsets(T, static_cast<int32_t>(d.E), bcounts, counts, offsets, mtiles, num_mtiles,
-                               static_cast<int32_t>(d.mtile_cap), status, stream);
+                               static_cast<int32_t>(d.mtile_cap), mpairs, static_cast<int32_t>(d.mpair_cap), status,
+                               stream);
   if (rc != kOk) return rc;
   mark(5);
   rc = ssb::launch_moe_scatter(ids, T, static_cast<int32_t>(d.E), static_cast<int32_t>(d.k), masks, bcounts, offsets,
@@ -505,6 +508,12 @@ int moe_forward(const ssb_moe_layer* L, const void* x, int64_t T, void* out, voi
     g.mtiles = mtiles;
     g.num_mtiles = num_mtiles;
     g.mtile_cap = static_cast<int32_t>(d.mtile_cap);
+    // CTA pairs: five 38 KB stages instead of three 54 KB ones (this GEMM's bf16 staging takes a stage's room), which
+    // its short K (4 k-blocks a tile) needs; the gate_up GEMM measured slower paired (half-empty pairs on odd tile
+    // counts cost more than the deeper ring gives)
+    g.mpairs = mpairs;
+    g.num_mpairs = num_mtiles + 1;
+    g.mpair_cap = static_cast<int32_t>(d.mpair_cap);
     g.K = static_cast<int32_t>(d.F);
     g.N = static_cast<int32_t>(d.H);
     g.ncb_k = static_cast<int32_t>(d.ncbF);

@@ -41,15 +41,17 @@ constexpr int kEpiWarp0 = 3;
 constexpr int kEpiWarps = 8;
 constexpr int kOutStage = 4096; // bf16 epilogue: per-warp staging buffer, 32 rows x 64 columns
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR>
 struct Cfg {
-  // the bf16 epilogue's staging buffers take the room of one stage
-  static constexpr int STAGES = BN == 256 ? (EPI == kEpiBF16 ? 3 : 4) : 6;
+  // PAIR: the two CTAs of a cluster share each MMA (cta_group::2, M = 256): each holds its own 128 A rows and half of
+  // the BN B rows, so a stage is 38 KB instead of 54 and five fit. Otherwise the bf16 epilogue's staging buffers take
+  // the room of one stage.
+  static constexpr int STAGES = PAIR ? 5 : BN == 256 ? (EPI == kEpiBF16 ? 3 : 4) : 6;
   static constexpr int A_BYTES = kBM * kBKBytes;               // 16 KB
-  static constexpr int B_BYTES = BN * kBKBytes;
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * kBKBytes;
   static constexpr int SFA_BYTES = 2048;                        // 4 atoms (128 rows x 64 K each)
   static constexpr int SFB_BYTES = (BN / 128) * 2048;
-  static constexpr int AB_TX = A_BYTES + B_BYTES;
+  static constexpr int AB_TX = A_BYTES + B_BYTES;               // one CTA's operand bytes per stage
   static constexpr int SF_TX = SFA_BYTES + SFB_BYTES;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
@@ -78,6 +80,84 @@ SSB_DEVICE void tma_store_2d(const CUtensorMap* m, uint32_t src, int32_t x, int3
                : "memory");
 }
 SSB_DEVICE void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
+// ---- CTA pairs (cluster of 2, cta_group::2) ----
+SSB_DEVICE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of this CTA's shared-memory location `a` in cluster CTA `rank`
+SSB_DEVICE uint32_t map_to_rank(uint32_t a, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+SSB_DEVICE void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+SSB_DEVICE bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait on a barrier that the other CTA of the pair arrives on (cluster-scope acquire)
+SSB_DEVICE bool mbar_wait_cl(uint32_t bar, uint32_t parity, volatile int32_t* abort_flag, int32_t* status) {
+  if (mbar_try_wait_cl(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait_cl(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitNs) {
+      *abort_flag = 1;
+      raise_status(status, kErrTimeout);
+      return false;
+    }
+  }
+}
+template <bool PAIR>
+SSB_DEVICE void release_acc(uint32_t bar) {
+  if constexpr (PAIR) mbar_arrive_remote(bar);
+  else mbar_arrive(bar);
+}
+template <bool PAIR>
+SSB_DEVICE bool wait_bar(uint32_t bar, uint32_t parity, volatile int32_t* abort_flag, int32_t* status) {
+  if constexpr (PAIR) return mbar_wait_cl(bar, parity, abort_flag, status);
+  else return mbar_wait(bar, parity, abort_flag, status);
+}
+// TMA tile load into this CTA's shared memory whose completion is counted on `bar` in either CTA of the pair (no
+// multicast: each CTA loads its own tiles)
+SSB_DEVICE void tma_load_2d_pair(uint32_t dst, const CUtensorMap* m, int32_t x, int32_t y, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+// D (+)= A x B over both CTAs: A rows 0-127 and B rows 0-BN/2 from the leader's shared memory, the rest from the
+// peer's at the same offsets; each CTA's TMEM holds its own 128 rows of D and their scales
+SSB_DEVICE void tc_mma_nvf4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate,
+                                 uint32_t sfa_tmem, uint32_t sfb_tmem) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+SSB_DEVICE void tc_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+SSB_DEVICE void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 SSB_DEVICE void tmem_st_x16(uint32_t taddr, const uint32_t* v) {
   asm volatile(
@@ -118,6 +198,30 @@ SSB_DEVICE int total_tiles(const GemmArgs& a, int n_tiles) {
   return num_m * n_tiles;
 }
 
+// The CTA's t-th output tile. PAIR: t indexes pair tiles {group, first row, leader rows, peer rows} x N tiles; the
+// leader (rank 0) takes rows [first, +128), the peer the next 128 (its rows may be 0: it still feeds the MMA, and its
+// epilogue stores nothing). Returns false for a tile to skip (no rows).
+template <bool PAIR>
+SSB_DEVICE bool step_tile(const GemmArgs& a, int t, int n_tiles, uint32_t rank, TileInfo& ti) {
+  if constexpr (!PAIR) {
+    return tile_info(a, t, n_tiles, ti);
+  } else {
+    const int mp = t / n_tiles;
+    ti.nt = t - mp * n_tiles;
+    const int4 e = reinterpret_cast<const int4*>(a.mpairs)[mp];
+    ti.group = e.x;
+    ti.row0 = e.y + (rank != 0 ? kBM : 0);
+    ti.rows = rank != 0 ? e.w : e.z;
+    return e.z > 0;
+  }
+}
+
+template <bool PAIR>
+SSB_DEVICE int total_steps(const GemmArgs& a, int n_tiles) {
+  if constexpr (!PAIR) return total_tiles(a, n_tiles);
+  else return min(*a.num_mpairs, a.mpair_cap) * n_tiles;
+}
+
 // Bounded wait that ignores the abort flag: used only to drain copies / MMAs already in flight before exit.
 SSB_DEVICE void drain_wait(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer();
@@ -126,11 +230,11 @@ SSB_DEVICE void drain_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmO, const GemmArgs args) {
-  using C = Cfg<BN, EPI>;
+  using C = Cfg<BN, EPI, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -146,33 +250,44 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // PAIR: rank 0 (the leader) issues the MMAs of both CTAs and owns the full / sf / acc_empty barriers they use
+  const uint32_t rank = PAIR ? cluster_rank() : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_sf_full + 8 * s, 1);
-      mbar_init(bar_sf + 8 * s, 128);
+      mbar_init(bar_sf + 8 * s, PAIR ? 8 : 4);          // one arrive per scale-writer warp
       mbar_init(bar_empty + 8 * s, 1);
     }
     mbar_init(bar_acc_full, 1);
-    mbar_init(bar_acc_empty, 8);
+    mbar_init(bar_acc_empty, PAIR ? 2 * kEpiWarps : kEpiWarps);
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(C::TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();               // both CTAs' barriers initialized before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   const int n_tiles = EPI == kEpiF32 ? (args.N + BN - 1) / BN : args.N / BN;
   const int num_kb = (args.K + 255) / 256;
-  const int total = total_tiles(args, n_tiles);
+  const int total = total_steps<PAIR>(args, n_tiles);
+  const int first = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int stride = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -183,14 +298,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+      for (int t = first; ok && t < total; t += stride) {
         TileInfo ti;
-        if (!tile_info(args, t, n_tiles, ti)) continue;
+        if (!step_tile<PAIR>(args, t, n_tiles, rank, ti)) continue;
         const int brow0 = ti.group * args.N + ti.nt * BN;
-        const uint8_t* sfa = args.sfa + (int64_t)(ti.row0 / kBM) * args.ncb_k * 512;
+        // a peer tile without rows reads the leader's scale rows (it may lie past the scale buffer's end)
+        const int srow0 = ti.rows > 0 ? ti.row0 : ti.row0 - kBM;
+        const uint8_t* sfa = args.sfa + (int64_t)(srow0 / kBM) * args.ncb_k * 512;
         const uint8_t* sfb = args.sfb + (int64_t)(brow0 / kBM) * args.ncb_k * 512;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1, abort_flag, args.status)) {
+          if (!wait_bar<PAIR>(bar_empty + 8 * stage, phase ^ 1, abort_flag, args.status)) {
             ok = false;
             break;
           }
@@ -202,9 +319,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             bulk_load(sbase + C::OFF_SFB + stage * C::SFB_BYTES + j * 2048,
                       sfb + ((int64_t)j * args.ncb_k + kb * 4) * 512, 2048, sb);
           const uint32_t fb = bar_full + 8 * stage;
-          mbar_arrive_expect_tx(fb, C::AB_TX);
-          tma_load_2d(sbase + C::OFF_A + stage * C::A_BYTES, &tmA, kb * kBKBytes, ti.row0, fb);
-          tma_load_2d(sbase + C::OFF_B + stage * C::B_BYTES, &tmB, kb * kBKBytes, brow0, fb);
+          if constexpr (PAIR) {
+            // both CTAs' operand bytes complete on the leader's full barrier, which the leader arms for both
+            const uint32_t fbl = map_to_rank(fb, 0);
+            if (rank == 0) mbar_arrive_expect_tx(fb, 2 * C::AB_TX);
+            tma_load_2d_pair(sbase + C::OFF_A + stage * C::A_BYTES, &tmA, kb * kBKBytes, ti.row0, fbl);
+            tma_load_2d_pair(sbase + C::OFF_B + stage * C::B_BYTES, &tmB, kb * kBKBytes,
+                             brow0 + static_cast<int>(rank) * (BN / 2), fbl);
+          } else {
+            mbar_arrive_expect_tx(fb, C::AB_TX);
+            tma_load_2d(sbase + C::OFF_A + stage * C::A_BYTES, &tmA, kb * kBKBytes, ti.row0, fb);
+            tma_load_2d(sbase + C::OFF_B + stage * C::B_BYTES, &tmB, kb * kBKBytes, brow0, fb);
+          }
           ++issued;
           if (++stage == C::STAGES) {
             stage = 0;
@@ -222,30 +348,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             p ^= 1;
           }
           drain_wait(bar_sf_full + 8 * s, p);
-          drain_wait(bar_full + 8 * s, p);
+          if (rank == 0) drain_wait(bar_full + 8 * s, p);     // PAIR: counts the peer's bytes too
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = idesc_nvf4(kBM, BN);
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (PAIR: the leader's, for both CTAs) ----------------
+      constexpr uint32_t idesc = idesc_nvf4(PAIR ? 2 * kBM : kBM, BN);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t iter = 0;
       bool ok = true;
       bool any_mma = false;
-      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+      for (int t = first; ok && t < total; t += stride) {
         TileInfo ti;
-        if (!tile_info(args, t, n_tiles, ti)) continue;
-        if (!mbar_wait(bar_acc_empty, (iter & 1) ^ 1, abort_flag, args.status)) {
+        if (!step_tile<PAIR>(args, t, n_tiles, rank, ti)) continue;
+        if (!wait_bar<PAIR>(bar_acc_empty, (iter & 1) ^ 1, abort_flag, args.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, args.status) ||
-              !mbar_wait(bar_sf + 8 * stage, phase, abort_flag, args.status)) {
+          if (!wait_bar<PAIR>(bar_full + 8 * stage, phase, abort_flag, args.status) ||
+              !wait_bar<PAIR>(bar_sf + 8 * stage, phase, abort_flag, args.status)) {
             ok = false;
             break;
           }
@@ -257,22 +383,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 4; ++i) {
             const uint64_t ad = smem_desc(sa + i * 32, 0, 1024, 2);
             const uint64_t bd = smem_desc(sb + i * 32, 0, 1024, 2);
-            tc_mma_nvf4(tmem, ad, bd, idesc, (kb | i) != 0 ? 1u : 0u, tmem + sfo + C::SFA_COL + 4 * i,
-                        tmem + sfo + C::SFA_COL + 16 + (BN / 32) * i);
+            if constexpr (PAIR)
+              tc_mma_nvf4_pair(tmem, ad, bd, idesc, (kb | i) != 0 ? 1u : 0u, tmem + sfo + C::SFA_COL + 4 * i,
+                               tmem + sfo + C::SFA_COL + 16 + (BN / 32) * i);
+            else
+              tc_mma_nvf4(tmem, ad, bd, idesc, (kb | i) != 0 ? 1u : 0u, tmem + sfo + C::SFA_COL + 4 * i,
+                          tmem + sfo + C::SFA_COL + 16 + (BN / 32) * i);
           }
           any_mma = true;
-          tc_commit(bar_empty + 8 * stage);
+          if constexpr (PAIR) {
+            tc_commit_pair(map_to_rank(bar_empty + 8 * stage, 0));
+            tc_commit_pair(map_to_rank(bar_empty + 8 * stage, 1));
+          } else {
+            tc_commit(bar_empty + 8 * stage);
+          }
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit(bar_acc_full);
+        if constexpr (PAIR) {
+          tc_commit_pair(map_to_rank(bar_acc_full, 0));
+          tc_commit_pair(map_to_rank(bar_acc_full, 1));
+        } else {
+          tc_commit(bar_acc_full);
+        }
         ++iter;
       }
       if (!ok && any_mma) {
-        tc_commit(bar_drain);
+        if constexpr (PAIR) tc_commit_pair(map_to_rank(bar_drain, 0));
+        else tc_commit(bar_drain);
         drain_wait(bar_drain, 0);
       }
     }
@@ -286,9 +427,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+    for (int t = first; ok && t < total; t += stride) {
       TileInfo ti;
-      if (!tile_info(args, t, n_tiles, ti)) continue;
+      if (!step_tile<PAIR>(args, t, n_tiles, rank, ti)) continue;
       for (int kb = 0; kb < num_kb; ++kb) {
         // the stage's previous MMAs completed before its scale copies were issued, so its columns are free
         if (!mbar_wait(bar_sf_full + 8 * stage, phase, abort_flag, args.status)) {
@@ -321,7 +462,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < (16 + BN / 8) / 16; ++c) tmem_st_x16(ta + 16 * c, w + 16 * c);
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(bar_sf + 8 * stage);
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (PAIR) mbar_arrive_remote(map_to_rank(bar_sf + 8 * stage, 0));
+          else mbar_arrive(bar_sf + 8 * stage);
+        }
         if (++stage == C::STAGES) {
           stage = 0;
           phase ^= 1;
@@ -335,10 +480,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int rl = quad * 32 + lane;                       // row inside the tile = TMEM lane
     const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     uint32_t iter = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    // PAIR: the accumulator is released on the leader's barrier
+    const uint32_t acc_empty = PAIR ? map_to_rank(bar_acc_empty, 0) : bar_acc_empty;
+    for (int t = first; t < total; t += stride) {
       TileInfo ti;
-      if (!tile_info(args, t, n_tiles, ti)) continue;
-      if (!mbar_wait(bar_acc_full, iter & 1, abort_flag, args.status)) break;
+      if (!step_tile<PAIR>(args, t, n_tiles, rank, ti)) continue;
+      if (!wait_bar<PAIR>(bar_acc_full, iter & 1, abort_flag, args.status)) break;
       tc_fence_after();
       const float alpha = args.alpha != nullptr ? args.alpha[ti.group] : args.alpha_scalar;
       const bool valid = rl < ti.rows;
@@ -353,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar_acc_empty);
+        if (lane == 0) release_acc<PAIR>(acc_empty);
         uint8_t* codes = reinterpret_cast<uint8_t*>(args.out);
         uint32_t pk[8], sfw = 0;
 #pragma unroll
@@ -394,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (h == 1) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar_acc_empty);
+            if (lane == 0) release_acc<PAIR>(acc_empty);
           }
           uint32_t pk[32];
 #pragma unroll
@@ -413,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) {
+          if (lane == 0 && ti.rows > 0) {                // a PAIR peer tile without rows stores nothing
             tma_store_2d(&tmO, stg, x0 + 64 * h, y0);
             bulk_commit();
           }
@@ -426,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar_acc_empty);
+        if (lane == 0) release_acc<PAIR>(acc_empty);
         if (valid) {
           float* out = reinterpret_cast<float*>(args.out);
           const int col0 = ti.nt * BN + 64 * half;
@@ -451,8 +598,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();              // no CTA leaves while its peer may still signal it
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
+    else
+      tmem_dealloc(tmem, C::TMEM_COLS);
+  }
 }
 
 // ---- host side ------------------------------------------------------------------------------------------------------
@@ -490,18 +643,34 @@ int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t width, int6
   return r == CUDA_SUCCESS ? kOk : kErrArgs;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const GemmArgs& args, int grid,
            cudaStream_t stream) {
-  using Cf = Cfg<BN, EPI>;
-  auto kern = gemm_nvfp4_kernel<BN, EPI>;
+  using Cf = Cfg<BN, EPI, PAIR>;
+  auto kern = gemm_nvfp4_kernel<BN, EPI, PAIR>;
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM) != cudaSuccess)
       return kErrCuda;
     attr_set = true;
   }
-  kern<<<grid, kThreads, Cf::SMEM, stream>>>(ma, mb, mo, args);
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid & ~1);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cf::SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mo, args) != cudaSuccess) return kErrCuda;
+  } else {
+    kern<<<grid, kThreads, Cf::SMEM, stream>>>(ma, mb, mo, args);
+  }
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
@@ -558,10 +727,13 @@ int launch_gemm_nvfp4(int epilogue, const uint8_t* a, int64_t a_rows, int64_t ld
   if (epilogue == kEpiSwiGLU && (args.ldo % 16 != 0 || args.out_ncb != sf_atom_cols(args.N / 2))) return kErrArgs;
   if (epilogue == kEpiBF16 && args.ldo % 8 != 0) return kErrArgs;
   if (args.mtiles == nullptr && args.M <= 0) return kOk;
+  // CTA pairs for the grouped 256-wide epilogues when the caller gives a pair table
+  const bool pair = args.mpairs != nullptr && epilogue != kEpiF32 && num_sms >= 2;
+  if (args.mpairs != nullptr && (args.num_mpairs == nullptr || args.mpair_cap <= 0)) return kErrArgs;
   CUtensorMap ma, mb;
   int rc = make_map(&ma, a, a_rows, args.K / 2, lda, kBM);
   if (rc != kOk) return rc;
-  rc = make_map(&mb, b, b_rows, args.K / 2, ldb, BN);
+  rc = make_map(&mb, b, b_rows, args.K / 2, ldb, pair ? BN / 2 : BN);
   if (rc != kOk) return rc;
   int grid = num_sms;
   if (args.mtiles == nullptr) {
@@ -571,16 +743,18 @@ int launch_gemm_nvfp4(int epilogue, const uint8_t* a, int64_t a_rows, int64_t ld
   }
   switch (epilogue) {
     case kEpiF32:
-      return launch<128, kEpiF32>(ma, mb, ma, args, grid, stream);
+      return launch<128, kEpiF32, false>(ma, mb, ma, args, grid, stream);
     case kEpiBF16: {
       // output map: [a_rows, N] bf16 rows of pitch ldo, box 64 columns x 32 rows, 128-byte swizzle
       CUtensorMap mo;
       rc = make_map_2d_swizzled(&mo, args.out, a_rows, args.N, args.ldo * 2, 32);
       if (rc != kOk) return rc;
-      return launch<256, kEpiBF16>(ma, mb, mo, args, grid, stream);
+      return pair ? launch<256, kEpiBF16, true>(ma, mb, mo, args, grid, stream)
+                  : launch<256, kEpiBF16, false>(ma, mb, mo, args, grid, stream);
     }
     case kEpiSwiGLU:
-      return launch<256, kEpiSwiGLU>(ma, mb, ma, args, grid, stream);
+      return pair ? launch<256, kEpiSwiGLU, true>(ma, mb, ma, args, grid, stream)
+                  : launch<256, kEpiSwiGLU, false>(ma, mb, ma, args, grid, stream);
     default:
       return kErrArgs;
   }

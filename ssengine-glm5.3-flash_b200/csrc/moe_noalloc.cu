@@ -104,7 +104,7 @@ extern "C" int ssb_moe_route_permute_noalloc(const float* logits, int64_t T, int
   if (rc != ssb::kOk) return rc;
   rc = ssb::launch_moe_count(ids, T, E, k, masks, block_counts, stream);
   if (rc != ssb::kOk) return rc;
-  rc = ssb::launch_moe_offsets(T, E, block_counts, counts, offsets, tiles, num_tiles, cap, status, stream);
+  rc = ssb::launch_moe_offsets(T, E, block_counts, counts, offsets, tiles, num_tiles, cap, nullptr, 0, status, stream);
   if (rc != ssb::kOk) return rc;
   const int64_t n = T * k;
   const int threads = 256;

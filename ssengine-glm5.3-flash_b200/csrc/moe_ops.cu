@@ -141,11 +141,15 @@ __global__ void moe_count_kernel(const int32_t* __restrict__ ids, int64_t T, int
 }
 
 // ---- expert offsets, block bases, GEMM tile table (one block) ------------------------------------------------------
+// With `mpairs`, also the CTA-pair table of the grouped GEMM: per expert ceil(tiles / 2) entries {expert, first row,
+// rows of the first 128, rows of the next 128} (the second half may be 0 rows: the next expert's first tile), count
+// in num_mtiles[1].
 __global__ void moe_offsets_kernel(int64_t T, int E, int nblocks, int32_t* __restrict__ block_counts,
                                    int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
                                    int32_t* __restrict__ mtiles, int32_t* __restrict__ num_mtiles, int cap,
-                                   int32_t* status) {
-  extern __shared__ int32_t sh[];     // [E + 1] padded sizes
+                                   int32_t* __restrict__ mpairs, int pair_cap, int32_t* status) {
+  extern __shared__ int32_t sh[];     // [E + 1] padded sizes, then [E + 1] first pair per expert
+  int32_t* psh = sh + (E + 1);
   for (int e = threadIdx.x; e <= E; e += blockDim.x) {
     int run = 0;
     if (e < E) {
@@ -162,17 +166,23 @@ __global__ void moe_offsets_kernel(int64_t T, int E, int nblocks, int32_t* __res
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    int acc = 0;
+    int acc = 0, pacc = 0;
     for (int e = 0; e <= E; ++e) {
       const int p = sh[e];
       sh[e] = acc;
       offsets[e] = acc;
       acc += p;
+      psh[e] = pacc;
+      pacc += (p / 128 + 1) / 2;
     }
     offsets[E + 1] = acc;
     const int n = acc / 128;
     *num_mtiles = n;
     if (n > cap) raise_status(status, kErrCapacity);
+    if (mpairs != nullptr) {
+      num_mtiles[1] = pacc;
+      if (pacc > pair_cap) raise_status(status, kErrCapacity);
+    }
   }
   __syncthreads();
   for (int e = threadIdx.x; e <= E; e += blockDim.x) {
@@ -183,6 +193,14 @@ __global__ void moe_offsets_kernel(int64_t T, int E, int nblocks, int32_t* __res
       if (tile < cap) {
         int4 v = make_int4(e, base + 128 * i, min(128, c - 128 * i), 0);
         reinterpret_cast<int4*>(mtiles)[tile] = v;
+      }
+    }
+    if (mpairs != nullptr) {
+      for (int j = 0; j * 256 < c; ++j) {
+        const int pair = psh[e] + j;
+        if (pair < pair_cap)
+          reinterpret_cast<int4*>(mpairs)[pair] =
+              make_int4(e, base + 256 * j, min(128, c - 256 * j), max(0, min(128, c - 256 * j - 128)));
       }
     }
   }
@@ -335,10 +353,11 @@ int launch_moe_count(const int32_t* ids, int64_t T, int32_t E, int32_t k, uint32
 }
 
 int launch_moe_offsets(int64_t T, int32_t E, int32_t* block_counts, int32_t* counts, int32_t* offsets,
-                       int32_t* mtiles, int32_t* num_mtiles, int32_t mtile_cap, int32_t* status, cudaStream_t stream) {
+                       int32_t* mtiles, int32_t* num_mtiles, int32_t mtile_cap, int32_t* mpairs, int32_t mpair_cap,
+                       int32_t* status, cudaStream_t stream) {
   const int nblocks = static_cast<int>((T + kBlockTokens - 1) / kBlockTokens);
-  moe_offsets_kernel<<<1, 512, (E + 1) * 4, stream>>>(T, E, nblocks, block_counts, counts, offsets, mtiles,
-                                                      num_mtiles, mtile_cap, status);
+  moe_offsets_kernel<<<1, 512, (E + 1) * 8, stream>>>(T, E, nblocks, block_counts, counts, offsets, mtiles,
+                                                      num_mtiles, mtile_cap, mpairs, mpair_cap, status);
   return last_error();
 }
 

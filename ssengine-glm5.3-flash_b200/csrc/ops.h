@@ -22,6 +22,12 @@ struct GemmArgs {
   const int32_t* mtiles = nullptr;     // grouped: [cap][4] = {group, first A row, valid rows, 0}; nullptr = dense
   const int32_t* num_mtiles = nullptr; // grouped: device count of valid entries
   int32_t mtile_cap = 0;
+  // grouped, CTA pairs (BN 256 epilogues): [cap][4] = {group, first row, rows of the first 128, rows of the next 128},
+  // both 128-row halves inside the group's rows or its padding; when set, the GEMM runs on clusters of 2 CTAs that
+  // share each MMA (M = 256), and `mtiles` is not read
+  const int32_t* mpairs = nullptr;
+  const int32_t* num_mpairs = nullptr;
+  int32_t mpair_cap = 0;
   int32_t M = 0;                       // dense: rows of A
   int32_t K = 0;                       // reduction length (elements)
   int32_t N = 0;                       // B rows per group
@@ -50,8 +56,10 @@ int launch_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32
 int launch_moe_count(const int32_t* ids, int64_t T, int32_t E, int32_t k, uint32_t* masks, int32_t* block_counts,
                      cudaStream_t stream);
 
+// mpairs (nullptr: none): the CTA-pair tile table of the grouped GEMM, count in num_mtiles[1]
 int launch_moe_offsets(int64_t T, int32_t E, int32_t* block_counts, int32_t* counts, int32_t* offsets,
-                       int32_t* mtiles, int32_t* num_mtiles, int32_t mtile_cap, int32_t* status, cudaStream_t stream);
+                       int32_t* mtiles, int32_t* num_mtiles, int32_t mtile_cap, int32_t* mpairs, int32_t mpair_cap,
+                       int32_t* status, cudaStream_t stream);
 
 int launch_moe_scatter(const int32_t* ids, int64_t T, int32_t E, int32_t k, const uint32_t* masks,
                        const int32_t* block_base, const int32_t* offsets, int32_t* rows, const uint8_t* xq,

@@ -59,6 +59,14 @@ def test_moe_layer_matches_oracle(cuda, T, H, F, E, k):
     want = [(e, offsets[e] + 128 * i, min(128, counts[e] - 128 * i), 0)
             for e in range(E + 1) for i in range(-(-int(counts[e]) // 128))]
     assert [tuple(r) for r in tiles.tolist()] == want
+    # the CTA-pair table after the tile table (capacity rcap / 128 tiles): per expert ceil(tiles / 2) pairs
+    # {expert, first row, rows of the first 128, rows of the next 128}
+    cap = -(-(T * (k + 1) + (E + 1) * 127) // 128)
+    n_pairs = int(layer.ws_view("NUM_MTILES", T, torch.int32, (2,)).cpu().numpy()[1])
+    both = layer.ws_view("MTILES", T, torch.int32, (cap + n_pairs, 4)).cpu().numpy()
+    want_pairs = [(e, offsets[e] + 256 * j, min(128, counts[e] - 256 * j), max(0, min(128, counts[e] - 256 * j - 128)))
+                  for e in range(E + 1) for j in range(-(-int(counts[e]) // 256))]
+    assert [tuple(r) for r in both[cap:].tolist()] == want_pairs
 
     # the layer output, on the layer's own routing and on the oracle's own
     o = out.float().cpu().numpy()
