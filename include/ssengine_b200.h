@@ -316,7 +316,8 @@ int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T);
 #define SSB_WS_ACT 14        /* uint8 [cap*128, F/2] SwiGLU output codes */
 #define SSB_WS_ACT_SF 15
 #define SSB_WS_Y 16          /* bf16 [cap*128, H] expert outputs per permuted row */
-#define SSB_WS_END 17
+#define SSB_WS_ROW_SRC 17    /* int32 [cap*128] source token of each permuted row (padding rows unwritten) */
+#define SSB_WS_END 18
 int ssb_moe_workspace_offsets(const ssb_moe_layer* layer, int64_t T, int64_t* offsets, int32_t n);
 
 /* Whole MoE layer on `stream`: quantize x -> router GEMM -> top-k routing -> permutation + gather -> grouped NVFP4

@@ -60,6 +60,7 @@ void layout(const MoeDims& d, int64_t* off) {
   sz[SSB_WS_ACT] = d.rcap * d.F / 2;
   sz[SSB_WS_ACT_SF] = (d.rcap / 128) * d.ncbF * 512;
   sz[SSB_WS_Y] = d.rcap * d.H * 2;
+  sz[SSB_WS_ROW_SRC] = d.rcap * 4;
   int64_t o = 0;
   for (int i = 0; i < SSB_WS_END; ++i) {
     off[i] = o;
@@ -421,6 +422,7 @@ int moe_forward(const ssb_moe_layer* L, const void* x, int64_t T, void* out, voi
   int32_t* mtiles = reinterpret_cast<int32_t*>(at(SSB_WS_MTILES));
   int32_t* num_mtiles = reinterpret_cast<int32_t*>(at(SSB_WS_NUM_MTILES));
   uint8_t* xqp = at(SSB_WS_XQ_PERM);
+  int32_t* row_src = reinterpret_cast<int32_t*>(at(SSB_WS_ROW_SRC));
   uint8_t* xsfp = at(SSB_WS_XSF_PERM);
   uint8_t* act = at(SSB_WS_ACT);
   uint8_t* asf = at(SSB_WS_ACT_SF);
@@ -469,7 +471,10 @@ int moe_forward(const ssb_moe_layer* L, const void* x, int64_t T, void* out, voi
   if (rc != kOk) return rc;
   mark(5);
   rc = ssb::launch_moe_scatter(ids, T, static_cast<int32_t>(d.E), static_cast<int32_t>(d.k), masks, bcounts, offsets,
-                               rows, xq, xsf, d.H, xqp, xsfp, stream);
+                               rows, row_src, xq, d.H, xqp, stream);
+  if (rc != kOk) return rc;
+  rc = ssb::launch_moe_sf_gather(row_src, mtiles, num_mtiles, static_cast<int32_t>(d.mtile_cap), xsf, d.H, xsfp,
+                                 stream);
   if (rc != kOk) return rc;
   // 5. grouped gate_up GEMM, SwiGLU + NVFP4 requant epilogue. When F is not a multiple of 256 the down GEMM's last
   //    k-block reads scale atoms past F that the epilogue never writes: they must hold zeros (finite scales times the

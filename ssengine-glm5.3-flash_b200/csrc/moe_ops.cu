@@ -206,18 +206,17 @@ __global__ void moe_offsets_kernel(int64_t T, int E, int nblocks, int32_t* __res
   }
 }
 
-// ---- permuted rows + gather of the token's NVFP4 codes and scales into its k + 1 rows -------------------------------
-// One warp per token: lanes 0..k-1 rank the token's routed slots, lane k takes the shared expert row; then the warp
-// copies the token's code row (16-byte vectors) and scale words into each destination row.
+// ---- permuted rows, the row map and the code rows of the token's k + 1 rows ----------------------------------------
+// One warp per token: lanes 0..k-1 rank the token's routed slots, lane k takes the shared expert row; every row records
+// its source token in row_src, and the warp copies the token's code row (16-byte vectors) into each destination row.
 __global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int64_t T, int E, int k,
                                    const uint32_t* __restrict__ masks, const int32_t* __restrict__ block_base,
                                    const int32_t* __restrict__ offsets, int32_t* __restrict__ rows,
-                                   const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsf, int64_t H,
-                                   uint8_t* __restrict__ xq_perm, uint8_t* __restrict__ xsf_perm) {
+                                   int32_t* __restrict__ row_src, const uint8_t* __restrict__ xq, int64_t H,
+                                   uint8_t* __restrict__ xq_perm) {
   const int lane = threadIdx.x & 31;
   const int64_t t = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
-  const int64_t ncb = sf_atom_cols(H);
   const int64_t row_bytes = H / 2;
   const int64_t b = t / kBlockTokens;
   const int i = static_cast<int>(t - b * kBlockTokens);
@@ -233,6 +232,7 @@ __global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int64_t T, i
     rows[t * k + lane] = my_row;
   }
   if (lane == k) my_row = offsets[E] + static_cast<int>(t);   // shared expert
+  if (lane <= k) row_src[my_row] = static_cast<int32_t>(t);
   const uint4* src = reinterpret_cast<const uint4*>(xq + t * row_bytes);
   const int nvec = static_cast<int>(row_bytes / 16);
   constexpr int kVecPerLane = 8;                               // up to H = 8192 in registers
@@ -240,10 +240,6 @@ __global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int64_t T, i
 #pragma unroll
   for (int j = 0; j < kVecPerLane; ++j)
     if (lane + 32 * j < nvec) reg[j] = __ldg(src + lane + 32 * j);
-  uint32_t sw[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    if (lane + 32 * j < ncb) sw[j] = *reinterpret_cast<const uint32_t*>(xsf + sf_atom_offset(t, (lane + 32 * j) * 4, ncb));
   for (int d = 0; d <= k; ++d) {
     const int64_t dst_row = __shfl_sync(0xFFFFFFFFu, my_row, d);
     uint4* dst = reinterpret_cast<uint4*>(xq_perm + dst_row * row_bytes);
@@ -251,14 +247,29 @@ __global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int64_t T, i
     for (int j = 0; j < kVecPerLane; ++j)
       if (lane + 32 * j < nvec) dst[lane + 32 * j] = reg[j];
     for (int v = lane + 32 * kVecPerLane; v < nvec; v += 32) dst[v] = src[v];
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if (lane + 32 * j < ncb)
-        *reinterpret_cast<uint32_t*>(xsf_perm + sf_atom_offset(dst_row, (lane + 32 * j) * 4, ncb)) = sw[j];
-    for (int a = lane + 128; a < ncb; a += 32)
-      *reinterpret_cast<uint32_t*>(xsf_perm + sf_atom_offset(dst_row, a * 4, ncb)) =
-          *reinterpret_cast<const uint32_t*>(xsf + sf_atom_offset(t, a * 4, ncb));
   }
+}
+
+// ---- permuted scale atoms, gathered: one thread per 16-byte atom line -------------------------------------------------
+// Atom (row block rb, column c) line l holds the words of rows 128 rb + l + 32 q, q = 0..3; the thread reads those four
+// rows' source-token words (token order, L2-resident) and writes the line, so a warp writes one whole 512-byte atom.
+// Rows past the tile's valid rows (the expert's padding) get zeros.
+__global__ void moe_sf_gather_kernel(const int32_t* __restrict__ row_src, const int32_t* __restrict__ mtiles,
+                                     const int32_t* __restrict__ num_mtiles, int cap, const uint8_t* __restrict__ xsf,
+                                     int64_t ncb, uint8_t* __restrict__ xsf_perm) {
+  const int64_t rb = blockIdx.x;
+  if (rb >= min(*num_mtiles, cap)) return;
+  const int64_t c = static_cast<int64_t>(blockIdx.y) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (c >= ncb) return;
+  const int l = threadIdx.x & 31;
+  const int valid = mtiles[rb * 4 + 2];
+  uint32_t w[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int r = l + 32 * q;
+    w[q] = r < valid ? *reinterpret_cast<const uint32_t*>(xsf + sf_atom_offset(row_src[rb * 128 + r], c * 4, ncb)) : 0u;
+  }
+  *reinterpret_cast<uint4*>(xsf_perm + (rb * ncb + c) * 512 + l * 16) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 // ---- weighted combine: out[t] = (x[t]) + sum_j w[t, j] y[rows[t, j]] + y[shared row of t], fp32 accumulate -----
@@ -362,13 +373,22 @@ int launch_moe_offsets(int64_t T, int32_t E, int32_t* block_counts, int32_t* cou
 }
 
 int launch_moe_scatter(const int32_t* ids, int64_t T, int32_t E, int32_t k, const uint32_t* masks,
-                       const int32_t* block_base, const int32_t* offsets, int32_t* rows, const uint8_t* xq,
-                       const uint8_t* xsf, int64_t H, uint8_t* xq_perm, uint8_t* xsf_perm, cudaStream_t stream) {
+                       const int32_t* block_base, const int32_t* offsets, int32_t* rows, int32_t* row_src,
+                       const uint8_t* xq, int64_t H, uint8_t* xq_perm, cudaStream_t stream) {
   if (k >= 32 || H % 32 != 0) return kErrArgs;
   if (T == 0) return kOk;
   const int64_t blocks = (T + 7) / 8;   // 8 warps per block, one token per warp
   moe_scatter_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ids, T, E, k, masks, block_base, offsets, rows,
-                                                                        xq, xsf, H, xq_perm, xsf_perm);
+                                                                        row_src, xq, H, xq_perm);
+  return last_error();
+}
+
+int launch_moe_sf_gather(const int32_t* row_src, const int32_t* mtiles, const int32_t* num_mtiles, int32_t mtile_cap,
+                         const uint8_t* xsf, int64_t H, uint8_t* xsf_perm, cudaStream_t stream) {
+  if (H % 64 != 0 || mtile_cap <= 0) return kErrArgs;
+  const int64_t ncb = sf_atom_cols(H);
+  const dim3 grid(static_cast<unsigned>(mtile_cap), static_cast<unsigned>((ncb + 7) / 8));
+  moe_sf_gather_kernel<<<grid, 256, 0, stream>>>(row_src, mtiles, num_mtiles, mtile_cap, xsf, ncb, xsf_perm);
   return last_error();
 }
 

@@ -61,9 +61,15 @@ int launch_moe_offsets(int64_t T, int32_t E, int32_t* block_counts, int32_t* cou
                        int32_t* mtiles, int32_t* num_mtiles, int32_t mtile_cap, int32_t* mpairs, int32_t mpair_cap,
                        int32_t* status, cudaStream_t stream);
 
+// rows[t, j] = permuted row of (token t, slot j); row_src[row] = t and the token's code row copied for each of its
+// k + 1 rows
 int launch_moe_scatter(const int32_t* ids, int64_t T, int32_t E, int32_t k, const uint32_t* masks,
-                       const int32_t* block_base, const int32_t* offsets, int32_t* rows, const uint8_t* xq,
-                       const uint8_t* xsf, int64_t H, uint8_t* xq_perm, uint8_t* xsf_perm, cudaStream_t stream);
+                       const int32_t* block_base, const int32_t* offsets, int32_t* rows, int32_t* row_src,
+                       const uint8_t* xq, int64_t H, uint8_t* xq_perm, cudaStream_t stream);
+// The permuted scale atoms of the *num_mtiles row tiles: row r's words from token row_src[r] of xsf, zeros past a
+// tile's valid rows
+int launch_moe_sf_gather(const int32_t* row_src, const int32_t* mtiles, const int32_t* num_mtiles, int32_t mtile_cap,
+                         const uint8_t* xsf, int64_t H, uint8_t* xsf_perm, cudaStream_t stream);
 
 // out = (residual if not null) + sum_j w[t, j] y[rows[t, j]] + y[shared row of t]
 int launch_moe_combine(const void* y, int64_t H, const int32_t* rows, const float* weights, const int32_t* offsets,

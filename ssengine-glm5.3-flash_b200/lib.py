@@ -27,7 +27,7 @@ EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_g
 EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
 
 WS = dict(XQ=0, XSF=1, LOGITS=2, IDS=3, WEIGHTS=4, ROWS=5, COUNTS=6, OFFSETS=7, MASKS=8, BLOCKS=9, MTILES=10,
-          NUM_MTILES=11, XQ_PERM=12, XSF_PERM=13, ACT=14, ACT_SF=15, Y=16, END=17)
+          NUM_MTILES=11, XQ_PERM=12, XSF_PERM=13, ACT=14, ACT_SF=15, Y=16, ROW_SRC=17, END=18)
 
 STATUS = {0: "ok", 1: "bad arguments", 2: "CUDA launch error", 3: "workspace too small",
           4: "a bounded device wait expired", 5: "cuTensorMapEncodeTiled unavailable", 6: "device table overflow",

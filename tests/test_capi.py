@@ -42,8 +42,9 @@ def test_workspace_layout_on_the_host():
     so = lib.load()
     L = layer_c()
     n = so.ssb_moe_workspace_bytes(ctypes.byref(L), 8192)
-    arr = (ctypes.c_int64 * 18)()
-    assert so.ssb_moe_workspace_offsets(ctypes.byref(L), 8192, arr, 18) == 0
+    n_off = lib.WS["END"] + 1
+    arr = (ctypes.c_int64 * n_off)()
+    assert so.ssb_moe_workspace_offsets(ctypes.byref(L), 8192, arr, n_off) == 0
     off = list(arr)
     assert off[-1] == n and all(o % 256 == 0 for o in off) and off == sorted(off)
     rcap = -(-(8192 * 9 + 129 * 127) // 128) * 128
