@@ -22,40 +22,40 @@ constexpr int kMaskWords = kBlockTokens / 32;
 __global__ void nvfp4_quantize_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t K, int64_t ldx,
                                       float gs, uint8_t* __restrict__ codes, int64_t ldc, uint8_t* __restrict__ sf,
                                       int64_t ncb) {
-  const int64_t total = rows * ncb;
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = idx / ncb;
-    const int64_t a = idx - r * ncb;
-    const int64_t k0 = a * 64;
-    const int64_t left = K - k0;
-    const int ng = left <= 0 ? 0 : (left >= 64 ? 4 : static_cast<int>(left / 16));
-    uint4 v[8];
-    const uint4* src = reinterpret_cast<const uint4*>(x + r * ldx + k0);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = (i >> 1) < ng ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
-    uint32_t word = 0;
-    uint32_t pk[8];
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v[2 * g]);
-      float f[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) f[i] = __bfloat162float(b[i]);
-      uint32_t p[2];
-      const uint32_t s = nvfp4_quant16(f, gs, p);
-      pk[2 * g] = p[0];
-      pk[2 * g + 1] = p[1];
-      if (g < ng) word |= s << (8 * g);
+  // one warp per 512 elements of a row, lane l quantizing the 16-element block l: its two 16-byte loads are half of
+  // a 1 KB span per instruction, its 8 code bytes a quarter of a 256-byte store; the 4 scale bytes of each atom column
+  // (64 elements) are assembled in the column's first lane. Atom columns past K (up to the 256-element padding) get
+  // zero scale words.
+  const int lane = threadIdx.x & 31;
+  const int64_t chunks = (K + 511) / 512;
+  const int64_t total = rows * chunks;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {
+    const int64_t r = w / chunks;
+    const int64_t k0 = (w - r * chunks) * 512 + lane * 16;
+    const bool valid = k0 + 16 <= K;
+    uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
+    if (valid) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + r * ldx + k0);
+      v0 = __ldg(src);
+      v1 = __ldg(src + 1);
     }
-    uint8_t* dst = codes + r * ldc + k0 / 2;
-    if (ng == 4) {
-      *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      *reinterpret_cast<uint4*>(dst + 16) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-    } else {
-      for (int g = 0; g < ng; ++g) *reinterpret_cast<uint2*>(dst + 8 * g) = make_uint2(pk[2 * g], pk[2 * g + 1]);
+    float f[16];
+    const __nv_bfloat16* b0 = reinterpret_cast<const __nv_bfloat16*>(&v0);
+    const __nv_bfloat16* b1 = reinterpret_cast<const __nv_bfloat16*>(&v1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      f[i] = __bfloat162float(b0[i]);
+      f[8 + i] = __bfloat162float(b1[i]);
     }
-    *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(r, a * 4, ncb)) = word;
+    uint32_t p[2];
+    const uint32_t sc = valid ? nvfp4_quant16(f, gs, p) : 0u;
+    if (valid) *reinterpret_cast<uint2*>(codes + r * ldc + k0 / 2) = make_uint2(p[0], p[1]);
+    uint32_t word = sc;
+    word |= __shfl_down_sync(0xFFFFFFFFu, sc, 1) << 8;
+    word |= __shfl_down_sync(0xFFFFFFFFu, sc, 2) << 16;
+    word |= __shfl_down_sync(0xFFFFFFFFu, sc, 3) << 24;
+    if ((lane & 3) == 0 && k0 < ncb * 64) *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(r, k0 / 16, ncb)) = word;
   }
 }
 
@@ -153,10 +153,17 @@ __global__ void moe_offsets_kernel(int64_t T, int E, int nblocks, int32_t* __res
   for (int e = threadIdx.x; e <= E; e += blockDim.x) {
     int run = 0;
     if (e < E) {
-      for (int b = 0; b < nblocks; ++b) {
-        const int c = block_counts[(int64_t)b * E + e];
-        block_counts[(int64_t)b * E + e] = run;   // exclusive base of block b inside expert e
-        run += c;
+      // exclusive base of block b inside expert e; the counts of 16 blocks are loaded before any is overwritten, so
+      // the loads overlap instead of each waiting for the previous store
+      for (int b0 = 0; b0 < nblocks; b0 += 16) {
+        int c[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) c[j] = b0 + j < nblocks ? block_counts[(int64_t)(b0 + j) * E + e] : 0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (b0 + j < nblocks) block_counts[(int64_t)(b0 + j) * E + e] = run;
+          run += c[j];
+        }
       }
     } else {
       run = static_cast<int>(T);                  // the shared expert takes every token
@@ -333,7 +340,7 @@ int launch_nvfp4_quantize(const void* x, int64_t rows, int64_t K, int64_t ldx, f
   if (rows == 0) return kOk;
   const int64_t ncb = sf_atom_cols(K);
   const int threads = 256;
-  nvfp4_quantize_kernel<<<grid_for(rows * ncb, threads), threads, 0, stream>>>(
+  nvfp4_quantize_kernel<<<grid_for(rows * ((K + 511) / 512) * 32, threads), threads, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), rows, K, ldx, gs, codes, ldc, sf, ncb);
   return last_error();
 }
