@@ -198,9 +198,10 @@ SSB_DEVICE int total_tiles(const GemmArgs& a, int n_tiles) {
   return num_m * n_tiles;
 }
 
-// The CTA's t-th output tile. PAIR: t indexes pair tiles {group, first row, leader rows, peer rows} x N tiles; the
-// leader (rank 0) takes rows [first, +128), the peer the next 128 (its rows may be 0: it still feeds the MMA, and its
-// epilogue stores nothing). Returns false for a tile to skip (no rows).
+// The CTA's t-th output tile. PAIR: t indexes pair tiles x N tiles, a pair tile being {group, first row, leader rows,
+// peer rows} from `mpairs`, or (dense, no tables) row blocks 2 p and 2 p + 1; the leader (rank 0) takes rows
+// [first, +128), the peer the next 128 (its rows may be 0 or fewer: it still feeds the MMA, and its epilogue stores
+// nothing). Returns false for a tile to skip (no rows).
 template <bool PAIR>
 SSB_DEVICE bool step_tile(const GemmArgs& a, int t, int n_tiles, uint32_t rank, TileInfo& ti) {
   if constexpr (!PAIR) {
@@ -208,6 +209,13 @@ SSB_DEVICE bool step_tile(const GemmArgs& a, int t, int n_tiles, uint32_t rank, 
   } else {
     const int mp = t / n_tiles;
     ti.nt = t - mp * n_tiles;
+    if (a.mpairs == nullptr) {
+      const int lead0 = 2 * mp * kBM;
+      ti.group = 0;
+      ti.row0 = lead0 + (rank != 0 ? kBM : 0);
+      ti.rows = min(kBM, a.M - ti.row0);
+      return a.M - lead0 > 0;
+    }
     const int4 e = reinterpret_cast<const int4*>(a.mpairs)[mp];
     ti.group = e.x;
     ti.row0 = e.y + (rank != 0 ? kBM : 0);
@@ -219,6 +227,7 @@ SSB_DEVICE bool step_tile(const GemmArgs& a, int t, int n_tiles, uint32_t rank, 
 template <bool PAIR>
 SSB_DEVICE int total_steps(const GemmArgs& a, int n_tiles) {
   if constexpr (!PAIR) return total_tiles(a, n_tiles);
+  else if (a.mpairs == nullptr) return ((a.M + 2 * kBM - 1) / (2 * kBM)) * n_tiles;
   else return min(*a.num_mpairs, a.mpair_cap) * n_tiles;
 }
 
@@ -727,8 +736,10 @@ int launch_gemm_nvfp4(int epilogue, const uint8_t* a, int64_t a_rows, int64_t ld
   if (epilogue == kEpiSwiGLU && (args.ldo % 16 != 0 || args.out_ncb != sf_atom_cols(args.N / 2))) return kErrArgs;
   if (epilogue == kEpiBF16 && args.ldo % 8 != 0) return kErrArgs;
   if (args.mtiles == nullptr && args.M <= 0) return kOk;
-  // CTA pairs for the grouped 256-wide epilogues when the caller gives a pair table
-  const bool pair = args.mpairs != nullptr && epilogue != kEpiF32 && num_sms >= 2;
+  // CTA pairs: the grouped 256-wide epilogues when the caller gives a pair table; dense bf16 GEMMs of more than one
+  // row block (their 3-stage single-CTA ring leaves the MMAs waiting for operands)
+  const bool pair = num_sms >= 2 && ((args.mpairs != nullptr && epilogue != kEpiF32) ||
+                                     (args.mtiles == nullptr && epilogue == kEpiBF16 && args.M > kBM));
   if (args.mpairs != nullptr && (args.num_mpairs == nullptr || args.mpair_cap <= 0)) return kErrArgs;
   CUtensorMap ma, mb;
   int rc = make_map(&ma, a, a_rows, args.K / 2, lda, kBM);
@@ -738,7 +749,8 @@ int launch_gemm_nvfp4(int epilogue, const uint8_t* a, int64_t a_rows, int64_t ld
   int grid = num_sms;
   if (args.mtiles == nullptr) {
     const int n_tiles = (args.N + BN - 1) / BN;
-    const int tiles = ((args.M + kBM - 1) / kBM) * n_tiles;
+    const int m_units = pair ? 2 * ((args.M + 2 * kBM - 1) / (2 * kBM)) : (args.M + kBM - 1) / kBM;
+    const int tiles = m_units * n_tiles;
     grid = tiles < num_sms ? tiles : num_sms;
   }
   switch (epilogue) {
