@@ -9,11 +9,13 @@
 // reference's FP8 query and cache (vLLM kv_cache_dtype fp8_e4m3, `concat_and_cache_mla`; TRTLLM sparse MLA with
 // bmm1 / bmm2 scales: ssengine/kernels.py configs 23 and 25, ssengine/model/pp_patch.py:643-672).
 //
-// One CTA per query row, 256 threads. Up front, every index column (n_idx <= 2304) is resolved to its cache row in
+// One CTA per query row, 352 threads. Up front, every index column (n_idx <= 2304) is resolved to its cache row in
 // shared memory with all loads in flight; then three roles run over blocks of 128 index columns (blocks without a
 // selected token skipped):
-//   warps 5-7 gather: each block's 128 token rows by cp.async into 5 K-major 128-byte-swizzled chunks [128 x 128 B]
-//            (the 5th holds the 64 rope bytes), two buffers; missing tokens zero-filled without a read;
+//   warps 5-10 gather: each block's 128 token rows by cp.async into 5 K-major 128-byte-swizzled chunks [128 x 128 B]
+//            (the 5th holds the 64 rope bytes), two buffers; missing tokens zero-filled without a read; each
+//            thread's arrive on the buffer's full barrier fires when its copies land (cp.async.mbarrier.arrive), so
+//            the next block's copies are issued while the previous block's are in flight;
 //   warp 4 issues the MMAs (one thread, kind::f8f6f4, M = 64 heads): S [64 x 128] = Q K^T as two N = 64 halves
 //            (tokens 0-63 in lanes 0-15, 64-127 in lanes 16-31 of TMEM columns 0-63; 36 MMAs), then
 //            O += P V with V the same chunks read MN-major (dims 0-255 in lanes 0-15, 256-511 in lanes 16-31 of
@@ -32,8 +34,9 @@ namespace ssb {
 namespace {
 
 constexpr int kHeads = 64, kDq = 576, kDv = 512, kBlk = 128;
-constexpr int kMlaThreads = 256;                  // warps 0-3 softmax + epilogue, warp 4 MMA, warps 5-7 gather
-constexpr int kGather = 96;                       // gather threads
+constexpr int kMlaThreads = 352;                  // warps 0-3 softmax + epilogue, warp 4 MMA, warps 5-10 gather
+constexpr int kGather = 192;                      // gather threads
+constexpr int kPro = 256;                         // threads 0-255 load Q and resolve the index columns
 constexpr int kNC = 5;                            // 128-byte chunks of a 576-byte row
 constexpr int kQChunk = kHeads * 128;             // [64 heads x 128 B], 8 KB
 constexpr int kKvChunk = kBlk * 128;              // [128 tokens x 128 B], 16 KB
@@ -59,6 +62,10 @@ SSB_DEVICE void cp_async16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
 }
 SSB_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// an arrive on `bar` (one of its expected arrivals) once this thread's earlier cp.async copies have landed
+SSB_DEVICE void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
 SSB_DEVICE void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // Two floats -> two e4m3 bytes (round to nearest even, saturating to +-448): lo in the low byte.
@@ -127,10 +134,12 @@ __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(const MlaArg
   // Q (64 heads x 576 bytes) by cp.async into the 5 swizzled chunks, 9 granules a thread
   {
     const uint8_t* q = a.q + t * (kHeads * kDq);
+    if (tid < kPro) {
 #pragma unroll
-    for (int k = 0; k < 9; ++k) {
-      const int p = tid + kMlaThreads * k, h = p / 36, g = p - h * 36;
-      cp_async16(sbase + kOffQ + chunk_off(h, g, kQChunk), q + h * kDq + g * 16, true);
+      for (int k = 0; k < 9; ++k) {
+        const int p = tid + kPro * k, h = p / 36, g = p - h * 36;
+        cp_async16(sbase + kOffQ + chunk_off(h, g, kQChunk), q + h * kDq + g * 16, true);
+      }
     }
     cp_async_commit();
   }
@@ -150,21 +159,22 @@ __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(const MlaArg
     tmem_relinquish();
   }
   // every index column -> its cache row (the loads of all columns in flight at once), and the selected-column bits
-  {
-    constexpr int kPer = (kMaxIdx + kMlaThreads - 1) / kMlaThreads;   // 9
+  if (tid < kPro) {
+    constexpr int kPer = (kMaxIdx + kPro - 1) / kPro;   // 9
     int32_t pos[kPer], pg[kPer];
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
-      const int j = tid + kMlaThreads * k;
+      const int j = tid + kPro * k;
       pos[k] = j < a.n_idx ? idx[j] : -1;
     }
 #pragma unroll
     for (int k = 0; k < kPer; ++k) pg[k] = (pos[k] >= 0 && (pos[k] >> 7) < a.width) ? pages[pos[k] >> 7] : -1;
-    static_assert(kPer * kMlaThreads == kMaxIdx, "every column written");
+    static_assert(kPer * kPro == kMaxIdx, "every column written");
+    static_assert(kPro % 32 == 0 && kPro <= kMlaThreads, "whole warps resolve the columns");
     uint32_t* tm32 = reinterpret_cast<uint32_t*>(tmask);
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
-      const int j = tid + kMlaThreads * k;           // a warp's 32 lanes: the 32 columns of word j >> 5
+      const int j = tid + kPro * k;                  // a warp's 32 lanes: the 32 columns of word j >> 5
       const bool v = pg[k] >= 0 && pg[k] < (1 << 24);
       slots[j] = v ? pg[k] * 128 + (pos[k] & 127) : -1;
       const uint32_t bits = __ballot_sync(0xffffffffu, v);
@@ -204,10 +214,9 @@ __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(const MlaArg
         const bool v = sl >= 0;
         cp_async16(kvb + chunk_off(tok, g, kKvChunk), a.kv + (int64_t)(v ? sl : 0) * kDq + g * 16, v);
       }
-      cp_async_commit();
-      cp_async_wait0();
-      fence_proxy_async_smem();
-      mbar_arrive(kv_full + 8 * buf);
+      // the arrive fires when this thread's copies have landed: the gather moves on to the other buffer meanwhile
+      // (the MMA thread orders the copies before its tensor-core reads with a proxy fence)
+      cp_async_arrive_noinc(kv_full + 8 * buf);
     }
     cp_async_wait0();
   } else if (warp == 4) {
@@ -219,6 +228,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1) sparse_mla_kernel(const MlaArg
       for (int i = 0; i < nblk; ++i) {
         const int buf = i & 1;
         if (!mbar_wait(kv_full + 8 * buf, (i >> 1) & 1, abort_flag, a.status)) break;
+        fence_proxy_async_smem();                          // the gathered rows (cp.async) -> the tensor core
         tc_fence_after();
         const uint32_t kvb = sbase + kOffKv + buf * kKvBuf;
 #pragma unroll
