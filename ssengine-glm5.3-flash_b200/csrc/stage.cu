@@ -187,6 +187,64 @@ __global__ void gated_rmsnorm_kernel(const __nv_bfloat16* x, int64_t ldx, const 
   *reinterpret_cast<uint2*>(y + t * ldy + c) = ov;
 }
 
+// The same arithmetic with 16 elements a lane (two 16-byte loads and stores; 8 lanes a head, 4 heads a warp): lane j
+// of a head holds the elements of the 4 lanes 4 j .. 4 j + 3 of the warp-per-head form above, and its sum of squares
+// is reduced in that form's tree order (lane xor 16, 8, 4 across the 8 lanes, then xor 2, 1 inside the lane), so the
+// results are identical.
+__global__ void gated_rmsnorm16_kernel(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* gate, int64_t ldg,
+                                       const __nv_bfloat16* w, float eps, __nv_bfloat16* y, int64_t ldy,
+                                       int64_t rows, int heads) {
+  const int lane = threadIdx.x & 31;
+  const int64_t grp = ((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * 4 + (lane >> 3);
+  const bool live = grp < rows * heads;
+  const int64_t t = live ? grp / heads : 0;
+  const int h = live ? static_cast<int>(grp - t * heads) : 0;
+  const int j = lane & 7;
+  const int c = h * 128 + j * 16;
+  uint4 xv[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, gv[2] = {xv[0], xv[0]}, wv[2] = {xv[0], xv[0]};
+  if (live) {
+    xv[0] = *reinterpret_cast<const uint4*>(x + t * ldx + c);
+    xv[1] = *reinterpret_cast<const uint4*>(x + t * ldx + c + 8);
+    gv[0] = *reinterpret_cast<const uint4*>(gate + t * ldg + c);
+    gv[1] = *reinterpret_cast<const uint4*>(gate + t * ldg + c + 8);
+    wv[0] = *reinterpret_cast<const uint4*>(w + j * 16);
+    wv[1] = *reinterpret_cast<const uint4*>(w + j * 16 + 8);
+  }
+  const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(xv);
+  const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(gv);
+  const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(wv);
+  float f[16], p[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    p[q] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[4 * q + i] = __bfloat162float(xb[4 * q + i]);
+      p[q] = fmaf(f[4 * q + i], f[4 * q + i], p[q]);
+    }
+  }
+#pragma unroll
+  for (int o = 4; o; o >>= 1)                          // the per-head form's lane xor 16, 8, 4
+#pragma unroll
+    for (int q = 0; q < 4; ++q) p[q] += __shfl_xor_sync(0xffffffffu, p[q], o);
+  float p2[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) p2[q] = p[q] + p[q ^ 2];  // lane xor 2
+  const float ss = p2[0] + p2[1];                      // lane xor 1
+  const float inv = rsqrtf(ss / 128.0f + eps);
+  uint4 ov[2];
+  __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(ov);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float gt = __bfloat162float(gb[i]);
+    ob[i] = __float2bfloat16(f[i] * inv * __bfloat162float(wb[i]) / (1.0f + expf(-gt)));
+  }
+  if (live) {
+    *reinterpret_cast<uint4*>(y + t * ldy + c) = ov[0];
+    *reinterpret_cast<uint4*>(y + t * ldy + c + 8) = ov[1];
+  }
+}
+
 // hc_expand: the 4 residual streams of a stage-0 row all start as its embedding (16-byte pieces).
 __global__ void hc_expand_kernel(const uint4* __restrict__ x, int64_t n16_row, int64_t T, uint4* __restrict__ out) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -261,6 +319,14 @@ int launch_gated_rmsnorm(const void* x, int64_t ldx, const void* gate, int64_t l
         reinterpret_cast<uintptr_t>(y)) & 7))
     return kErrArgs;
   if (rows == 0) return kOk;
+  if ((ldx | ldg | ldy) % 8 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gate) |
+                                       reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) & 15) == 0) {
+    const int64_t warps16 = (rows * heads + 3) / 4;
+    gated_rmsnorm16_kernel<<<static_cast<unsigned>((warps16 * 32 + 255) / 256), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(gate), ldg,
+        static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(y), ldy, rows, heads);
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  }
   const int64_t warps = rows * heads;
   gated_rmsnorm_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(gate), ldg,
