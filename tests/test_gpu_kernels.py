@@ -88,17 +88,22 @@ def test_gemm_f32_epilogue(cuda, M, K, N):
     np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-5 * scale)
 
 
-def test_gemm_bf16_epilogue(cuda):
-    M, K, N = 300, 4096, 512
-    rng = np.random.default_rng(11)
+@pytest.mark.parametrize("M,K,N", [(300, 4096, 512), (1, 1024, 256), (129, 1024, 512), (513, 1024, 256)])
+def test_gemm_bf16_epilogue(cuda, M, K, N):
+    """Dense bf16 GEMMs of more than one 128-row block run on CTA pairs (row blocks 2p, 2p + 1): M = 129 gives a pair
+    whose second half holds one row, M = 300 and 513 a last pair whose second half is past M, M = 1 a single CTA.
+    The output rows past M and the columns past N of a wider row pitch must keep their sentinel."""
+    rng = np.random.default_rng(11 + M)
     ac, asf = _rand_operand(rng, M, K)
     bc, bsf = _rand_operand(rng, N, K)
-    out = torch.zeros((M, N), dtype=torch.bfloat16, device=cuda)
+    ldo, sentinel = N + 64, 12288.0
+    buf = torch.full((M + 40, ldo), sentinel, dtype=torch.bfloat16, device=cuda)
     _gemm(1, _dev(nvfp4.pack(ac)), _dev(nvfp4.sf_to_atoms(asf)), M, K, _dev(nvfp4.pack(bc)),
-          _dev(nvfp4.sf_to_atoms(bsf)), N, 1e-2, out, N)
+          _dev(nvfp4.sf_to_atoms(bsf)), N, 1e-2, buf, ldo)
     ref = 1e-2 * (nvfp4.dequantize(ac, asf, 1.0).astype(np.float64) @ nvfp4.dequantize(bc, bsf, 1.0).T)
-    got = out.float().cpu().numpy()
-    np.testing.assert_allclose(got, ref, rtol=8e-3, atol=1e-3 * np.abs(ref).max())
+    full = buf.float().cpu().numpy()
+    np.testing.assert_allclose(full[:M, :N], ref, rtol=8e-3, atol=1e-3 * np.abs(ref).max())
+    assert (full[M:] == sentinel).all() and (full[:M, N:] == sentinel).all()
 
 
 def test_gemm_swiglu_requant_epilogue(cuda):
