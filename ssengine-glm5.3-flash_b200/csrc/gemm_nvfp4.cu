@@ -26,9 +26,9 @@
 // expert's weights stay in L2 while its row blocks are in flight.
 // CTA pairs (PAIR; the grouped down projection over a pair table, dense bf16 GEMMs over row blocks 2p, 2p + 1): a
 // cluster of two CTAs computes 256 rows x BN with tcgen05.mma.cta_group::2 issued by the leader (rank 0). Each CTA
-// TMA-loads its own 128 A rows and half of the B tile (no multicast), both completing on the leader's full barrier,
-// which the leader arms for both; each CTA's scale writers fill its own TMEM (its A rows, all BN B rows) and arrive on
-// the leader's sf barrier; the leader's commits signal the empty / accumulator barriers of both CTAs; each CTA's
+// TMA-loads its own 128 A rows and half of the B tile into its own shared memory, both completing on the leader's
+// full barrier, which the leader arms for both; each CTA's scale writers fill its own TMEM (its A rows, all BN B
+// rows) and arrive on the leader's sf barrier; the leader's commits signal the empty / accumulator barriers of both CTAs; each CTA's
 // epilogue drains its own 128 rows and releases the accumulator on the leader's barrier. A stage is then 38 KB
 // instead of 54, so five fit. Cross-CTA arrives use the default (CTA-scope release) form: a cluster-scope release
 // measured ~1,400 cycles each.
@@ -139,8 +139,8 @@ SSB_DEVICE bool wait_bar(uint32_t bar, uint32_t parity, volatile int32_t* abort_
   if constexpr (PAIR) return mbar_wait_cl(bar, parity, abort_flag, status);
   else return mbar_wait(bar, parity, abort_flag, status);
 }
-// TMA tile load into this CTA's shared memory whose completion is counted on `bar` in either CTA of the pair (no
-// multicast: each CTA loads its own tiles)
+// TMA tile load into this CTA's shared memory whose completion is counted on `bar` in either CTA of the pair (each
+// CTA loads its own tiles)
 SSB_DEVICE void tma_load_2d_pair(uint32_t dst, const CUtensorMap* m, int32_t x, int32_t y, uint32_t bar_cluster) {
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
