@@ -119,7 +119,7 @@ _SIGS = {
     "ssb_concat_cols": ([_P, _I64, _I32, _P, _I64, _I32, _P, _I64, _I64, _P], ctypes.c_int),
 }
 
-MOE_KERNELS = 9       # kernels ssb_moe_forward launches (+ a memset when F % 256 != 0)
+MOE_KERNELS = 10      # kernels ssb_moe_forward launches (+ a memset when F % 256 != 0)
 MOE_STEPS = ("quantize", "router_gemm", "route", "count", "offsets", "scatter", "gate_up_gemm", "down_gemm",
              "combine")
 
