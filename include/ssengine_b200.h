@@ -92,6 +92,15 @@ int ssb_rmsnorm(const void* x, int64_t H, const int64_t* rows, int64_t n, const 
 int ssb_gated_rmsnorm(const void* x, int64_t ldx, const void* gate, int64_t ldg, const void* w, float eps, void* y,
                       int64_t ldy, int64_t rows, int32_t heads, void* stream);
 
+/* The same norm with its output quantized for the next NVFP4 GEMM (the KDA o_proj): codes uint8 [rows, ldc] (two e2m1
+ * per byte, ldc >= heads * 64) and ue4m3 scale atoms (128x4 layout, heads * 128 columns) of y / gs, equal byte for
+ * byte to ssb_gated_rmsnorm followed by ssb_nvfp4_quantize; scale atoms past heads * 128 columns (up to the
+ * 256-column padding) and past `rows` are left as they are (pass a zeroed buffer); the bf16 y is not written.
+ * Replaces, where ssb_gated_rmsnorm stands, the fork's o_norm followed by the o_proj's `scaled_fp4_quant` (vLLM
+ * kimi_linear). */
+int ssb_gated_rmsnorm_nvfp4(const void* x, int64_t ldx, const void* gate, int64_t ldg, const void* w, float eps,
+                            float gs, void* codes, int64_t ldc, void* sf, int64_t rows, int32_t heads, void* stream);
+
 /* Stage 0's 4-stream residual: out bf16 [T, 4, H] = 4 copies of each embedding row x bf16 [T, H] (H % 8 == 0).
  * Replaces `hc_expand_cat` (ssengine/model/pp_patch.py:169-183). */
 int ssb_hc_expand(const void* x, int64_t T, int64_t H, void* out, void* stream);

@@ -202,6 +202,12 @@ int ssb_gated_rmsnorm(const void* x, int64_t ldx, const void* gate, int64_t ldg,
   return ssb::launch_gated_rmsnorm(x, ldx, gate, ldg, w, eps, y, ldy, rows, heads, static_cast<cudaStream_t>(stream));
 }
 
+int ssb_gated_rmsnorm_nvfp4(const void* x, int64_t ldx, const void* gate, int64_t ldg, const void* w, float eps,
+                            float gs, void* codes, int64_t ldc, void* sf, int64_t rows, int32_t heads, void* stream) {
+  return ssb::launch_gated_rmsnorm_nvfp4(x, ldx, gate, ldg, w, eps, gs, static_cast<uint8_t*>(codes), ldc,
+                                         static_cast<uint8_t*>(sf), rows, heads, static_cast<cudaStream_t>(stream));
+}
+
 int ssb_hc_expand(const void* x, int64_t T, int64_t H, void* out, void* stream) {
   return ssb::launch_hc_expand(x, T, H, out, static_cast<cudaStream_t>(stream));
 }

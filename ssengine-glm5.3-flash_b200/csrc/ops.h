@@ -89,6 +89,11 @@ int launch_rmsnorm(const void* x, int64_t H, const int64_t* rows, int64_t n, con
                    cudaStream_t stream);
 int launch_gated_rmsnorm(const void* x, int64_t ldx, const void* gate, int64_t ldg, const void* w, float eps, void* y,
                          int64_t ldy, int64_t rows, int heads, cudaStream_t stream);
+// The gated RMSNorm quantized to NVFP4 (codes [rows, ldc] bytes, scale atoms of heads * 128 columns, global scale gs):
+// the same codes and scales as launch_gated_rmsnorm followed by launch_nvfp4_quantize.
+int launch_gated_rmsnorm_nvfp4(const void* x, int64_t ldx, const void* gate, int64_t ldg, const void* w, float eps,
+                               float gs, uint8_t* codes, int64_t ldc, uint8_t* sf, int64_t rows, int heads,
+                               cudaStream_t stream);
 int launch_hc_expand(const void* x, int64_t T, int64_t H, void* out, cudaStream_t stream);
 int launch_hc_mean(const void* res, int64_t H, const int64_t* rows, int64_t n, void* out, cudaStream_t stream);
 int launch_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64_t* out, cudaStream_t stream);

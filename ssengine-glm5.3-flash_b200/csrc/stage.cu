@@ -245,6 +245,70 @@ __global__ void gated_rmsnorm16_kernel(const __nv_bfloat16* x, int64_t ldx, cons
   }
 }
 
+// The gated RMSNorm with its output quantized to NVFP4 for the next GEMM (the KDA o_proj): the arithmetic of
+// gated_rmsnorm16_kernel up to the bf16 rounding of each element, then each lane's 16 elements (one NVFP4 block) are
+// quantized exactly as the activation quantizer does (nvfp4_quant16 on the bf16 values, global scale gs), so the codes
+// and scale atoms equal those of the two-step path; the 4 scale bytes of an atom column come from lanes j .. j + 3 of
+// the head. Codes [rows, ldc] bytes, scale atoms of the 128-row blocks (sf_atom_offset layout, ncb atom columns).
+__global__ void gated_rmsnorm_nvfp4_kernel(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* gate,
+                                           int64_t ldg, const __nv_bfloat16* w, float eps, float gs, uint8_t* codes,
+                                           int64_t ldc, uint8_t* sf, int64_t ncb, int64_t rows, int heads) {
+  const int lane = threadIdx.x & 31;
+  const int64_t grp = ((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * 4 + (lane >> 3);
+  const bool live = grp < rows * heads;
+  const int64_t t = live ? grp / heads : 0;
+  const int h = live ? static_cast<int>(grp - t * heads) : 0;
+  const int j = lane & 7;
+  const int c = h * 128 + j * 16;
+  uint4 xv[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, gv[2] = {xv[0], xv[0]}, wv[2] = {xv[0], xv[0]};
+  if (live) {
+    xv[0] = *reinterpret_cast<const uint4*>(x + t * ldx + c);
+    xv[1] = *reinterpret_cast<const uint4*>(x + t * ldx + c + 8);
+    gv[0] = *reinterpret_cast<const uint4*>(gate + t * ldg + c);
+    gv[1] = *reinterpret_cast<const uint4*>(gate + t * ldg + c + 8);
+    wv[0] = *reinterpret_cast<const uint4*>(w + j * 16);
+    wv[1] = *reinterpret_cast<const uint4*>(w + j * 16 + 8);
+  }
+  const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(xv);
+  const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(gv);
+  const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(wv);
+  float f[16], p[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    p[q] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[4 * q + i] = __bfloat162float(xb[4 * q + i]);
+      p[q] = fmaf(f[4 * q + i], f[4 * q + i], p[q]);
+    }
+  }
+#pragma unroll
+  for (int o = 4; o; o >>= 1)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) p[q] += __shfl_xor_sync(0xffffffffu, p[q], o);
+  float p2[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) p2[q] = p[q] + p[q ^ 2];
+  const float ss = p2[0] + p2[1];
+  const float inv = rsqrtf(ss / 128.0f + eps);
+  float yv[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float gt = __bfloat162float(gb[i]);
+    yv[i] = __bfloat162float(__float2bfloat16(f[i] * inv * __bfloat162float(wb[i]) / (1.0f + expf(-gt))));
+  }
+  uint32_t pk[2];
+  const uint32_t s8 = live ? nvfp4_quant16(yv, gs, pk) : 0u;
+  uint32_t word = s8;
+  word |= __shfl_down_sync(0xffffffffu, s8, 1) << 8;
+  word |= __shfl_down_sync(0xffffffffu, s8, 2) << 16;
+  word |= __shfl_down_sync(0xffffffffu, s8, 3) << 24;
+  if (live) {
+    *reinterpret_cast<uint2*>(codes + t * ldc + c / 2) = make_uint2(pk[0], pk[1]);
+    if ((j & 3) == 0) *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(t, c / 16, ncb)) = word;
+  }
+}
+
 // hc_expand: the 4 residual streams of a stage-0 row all start as its embedding (16-byte pieces).
 __global__ void hc_expand_kernel(const uint4* __restrict__ x, int64_t n16_row, int64_t T, uint4* __restrict__ out) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -331,6 +395,24 @@ int launch_gated_rmsnorm(const void* x, int64_t ldx, const void* gate, int64_t l
   gated_rmsnorm_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(gate), ldg,
       static_cast<const __nv_bfloat16*>(w), eps, static_cast<__nv_bfloat16*>(y), ldy, rows, heads);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int launch_gated_rmsnorm_nvfp4(const void* x, int64_t ldx, const void* gate, int64_t ldg, const void* w, float eps,
+                               float gs, uint8_t* codes, int64_t ldc, uint8_t* sf, int64_t rows, int heads,
+                               cudaStream_t stream) {
+  if (x == nullptr || gate == nullptr || w == nullptr || codes == nullptr || sf == nullptr || rows < 0 || heads <= 0 ||
+      ldx < heads * 128 || ldg < heads * 128 || ldc < heads * 64 || (ldx | ldg) % 8 != 0 || ldc % 8 != 0 ||
+      !(gs > 0.0f) ||
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(w)) & 15) ||
+      (reinterpret_cast<uintptr_t>(codes) & 7) || (reinterpret_cast<uintptr_t>(sf) & 3))
+    return kErrArgs;
+  if (rows == 0) return kOk;
+  const int64_t warps = (rows * heads + 3) / 4;
+  gated_rmsnorm_nvfp4_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(gate), ldg,
+      static_cast<const __nv_bfloat16*>(w), eps, gs, codes, ldc, sf, sf_atom_cols(static_cast<int64_t>(heads) * 128),
+      rows, heads);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

@@ -56,20 +56,31 @@ class Nvfp4Linear:
         sf = layout.atoms_to_sf(self.sf, self.N_pad, self.K)[:self.N]
         return codes, sf, 1.0 / (self.alpha * self.gs_in)
 
-    def __call__(self, x: torch.Tensor, out: torch.Tensor, status: torch.Tensor, stream=None) -> torch.Tensor:
-        """x bf16 [T, >= K] (row pitch x.stride(0)), out bf16 [T, >= N_pad] (row pitch out.stride(0))."""
-        T = x.shape[0]
-        s = lib.stream_ptr(stream)
+    def input_buffers(self, T: int) -> tuple:
+        """Empty NVFP4 input buffers for T rows: codes uint8 [T padded to 128, K / 2], zeroed scale atoms."""
         rows = _round(max(T, 1), 128)
         codes = torch.empty(rows, self.K // 2, dtype=torch.uint8, device=self.device)
         sf = torch.zeros(rows // 128 * layout.sf_atom_cols(self.K) * 512, dtype=torch.uint8, device=self.device)
-        lib.check("ssb_nvfp4_quantize", self._lib.ssb_nvfp4_quantize(x.data_ptr(), T, self.K, x.stride(0), self.gs_in,
-                                                                     codes.data_ptr(), self.K // 2, sf.data_ptr(), s))
+        return codes, sf
+
+    def gemm(self, codes: torch.Tensor, sf: torch.Tensor, T: int, out: torch.Tensor, status: torch.Tensor,
+             stream=None) -> torch.Tensor:
+        """out bf16 [T, >= N_pad] from an input already quantized with `gs_in` (codes and scale atoms as
+        `input_buffers` lays them out)."""
         lib.check("ssb_nvfp4_gemm", self._lib.ssb_nvfp4_gemm(lib.EPI_BF16, codes.data_ptr(), sf.data_ptr(), T, self.K,
                                                              self.codes.data_ptr(), self.sf.data_ptr(), self.N_pad,
                                                              self.alpha, out.data_ptr(), out.stride(0), None, 1.0,
-                                                             status.data_ptr(), s))
+                                                             status.data_ptr(), lib.stream_ptr(stream)))
         return out
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor, status: torch.Tensor, stream=None) -> torch.Tensor:
+        """x bf16 [T, >= K] (row pitch x.stride(0)), out bf16 [T, >= N_pad] (row pitch out.stride(0))."""
+        T = x.shape[0]
+        codes, sf = self.input_buffers(T)
+        lib.check("ssb_nvfp4_quantize", self._lib.ssb_nvfp4_quantize(x.data_ptr(), T, self.K, x.stride(0), self.gs_in,
+                                                                     codes.data_ptr(), self.K // 2, sf.data_ptr(),
+                                                                     lib.stream_ptr(stream)))
+        return self.gemm(codes, sf, T, out, status, stream)
 
 
 class KdaAttention:
@@ -115,14 +126,23 @@ class KdaAttention:
         self.kda.prefill(proj, gate, beta, o, seqs, conv_state, rec_state, stream=stream, status=status)
         if keep:
             self.parts = dict(proj=proj, gate=gate, ogate=ogate, o=o.clone())
-        lib.check("ssb_gated_rmsnorm", self._lib.ssb_gated_rmsnorm(o.data_ptr(), P, ogate.data_ptr(), P,
-                                                                   self.norm_w.data_ptr(), self.norm_eps, o.data_ptr(),
-                                                                   P, T, self.heads, s))
         if out is None:
             out = torch.empty(T, self.H, dtype=torch.bfloat16, device=dev)
-        self.o_proj(o, out, status, stream)
         if keep:
+            # the bf16 normed rows are kept for checks, then quantized as the o_proj's input
+            lib.check("ssb_gated_rmsnorm", self._lib.ssb_gated_rmsnorm(o.data_ptr(), P, ogate.data_ptr(), P,
+                                                                       self.norm_w.data_ptr(), self.norm_eps,
+                                                                       o.data_ptr(), P, T, self.heads, s))
+            self.o_proj(o, out, status, stream)
             self.parts["normed"] = o
+        else:
+            # the norm writes the o_proj's NVFP4 input directly (same bytes as norm + quantize)
+            codes, sf = self.o_proj.input_buffers(T)
+            lib.check("ssb_gated_rmsnorm_nvfp4",
+                      self._lib.ssb_gated_rmsnorm_nvfp4(o.data_ptr(), P, ogate.data_ptr(), P, self.norm_w.data_ptr(),
+                                                        self.norm_eps, self.o_proj.gs_in, codes.data_ptr(), P // 2,
+                                                        sf.data_ptr(), T, self.heads, s))
+            self.o_proj.gemm(codes, sf, T, out, status, stream)
         return out
 
 

@@ -21,7 +21,7 @@ EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_g
            "ssb_kda_workspace_bytes", "ssb_kda_conv",
            "ssb_ipc_export", "ssb_ipc_open", "ssb_ipc_close", "ssb_flag_wait", "ssb_flag_write", "ssb_p2p_copy",
            "ssb_indexer_logits", "ssb_indexer_expand", "ssb_sparse_mla", "ssb_mla_cache_append", "ssb_mla_q_pack",
-           "ssb_kpool_insert", "ssb_gated_rmsnorm", "ssb_hc_expand", "ssb_hc_mean",
+           "ssb_kpool_insert", "ssb_gated_rmsnorm", "ssb_gated_rmsnorm_nvfp4", "ssb_hc_expand", "ssb_hc_mean",
            "ssb_nvfp4_gemm_grouped", "ssb_rmsnorm_cols", "ssb_rope", "ssb_transpose_heads", "ssb_concat_cols")
 
 EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
@@ -109,6 +109,7 @@ _SIGS = {
     "ssb_mla_q_pack": ([_P, _I64, _P, _I64, _I64, _I64, _P, _F, _P], ctypes.c_int),
     "ssb_kpool_insert": ([_P, _P, _I64, _P, _P, _I64, _I32, _P, _I64, _P, _P, _P], ctypes.c_int),
     "ssb_gated_rmsnorm": ([_P, _I64, _P, _I64, _P, _F, _P, _I64, _I64, _I32, _P], ctypes.c_int),
+    "ssb_gated_rmsnorm_nvfp4": ([_P, _I64, _P, _I64, _P, _F, _F, _P, _I64, _P, _I64, _I32, _P], ctypes.c_int),
     "ssb_hc_expand": ([_P, _I64, _I64, _P, _P], ctypes.c_int),
     "ssb_hc_mean": ([_P, _I64, _P, _I64, _P, _P], ctypes.c_int),
     "ssb_nvfp4_gemm_grouped": ([_I32, _P, _P, _I64, _I64, _P, _P, _I64, _I32, _P, _P, _P, _I32, _P, _I64, _P, _P],

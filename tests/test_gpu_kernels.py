@@ -146,3 +146,32 @@ def test_route_indices_bit_exact(cuda, T, E, k):
     rid, rw = omoe.route_softmax_topk(logits, k)
     np.testing.assert_array_equal(ids.cpu().numpy(), rid)
     np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("rows,heads", [(300, 8), (1, 64), (1000, 64), (129, 3)])
+def test_gated_rmsnorm_nvfp4_equals_norm_then_quantize(cuda, rows, heads):
+    """ssb_gated_rmsnorm_nvfp4 writes the same codes and scale atoms as ssb_gated_rmsnorm followed by
+    ssb_nvfp4_quantize (heads = 3: 384 columns, the atom columns up to the 256-column padding stay zero)."""
+    lib, so = _lib()
+    P = heads * 128
+    gen = torch.Generator(device=cuda).manual_seed(rows + heads)
+    x = (torch.randn(rows, P, device=cuda, generator=gen) * 3).to(torch.bfloat16)
+    gate = torch.randn(rows, P, device=cuda, generator=gen).to(torch.bfloat16)
+    w = (torch.rand(128, device=cuda, generator=gen) + 0.5).to(torch.bfloat16)
+    gs, eps = 448.0 * 6.0 / 12.0, 1e-5
+    rp = -(-rows // 128) * 128
+    nsf = rp // 128 * so.ssb_sf_atom_cols(P) * 512
+    y = torch.empty_like(x)
+    lib.check("ssb_gated_rmsnorm", so.ssb_gated_rmsnorm(x.data_ptr(), P, gate.data_ptr(), P, w.data_ptr(), eps,
+                                                        y.data_ptr(), P, rows, heads, _stream()))
+    c1 = torch.zeros(rp, P // 2, dtype=torch.uint8, device=cuda)
+    s1 = torch.zeros(nsf, dtype=torch.uint8, device=cuda)
+    lib.check("ssb_nvfp4_quantize", so.ssb_nvfp4_quantize(y.data_ptr(), rows, P, P, gs, c1.data_ptr(), P // 2,
+                                                          s1.data_ptr(), _stream()))
+    c2 = torch.zeros_like(c1)
+    s2 = torch.zeros_like(s1)
+    lib.check("ssb_gated_rmsnorm_nvfp4", so.ssb_gated_rmsnorm_nvfp4(x.data_ptr(), P, gate.data_ptr(), P, w.data_ptr(),
+                                                                    eps, gs, c2.data_ptr(), P // 2, s2.data_ptr(),
+                                                                    rows, heads, _stream()))
+    torch.cuda.synchronize()
+    assert torch.equal(c1, c2) and torch.equal(s1, s2)
