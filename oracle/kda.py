@@ -18,7 +18,7 @@ Interface followed (the reference's `kda_prefill_forward`, ssengine/model/pp_pat
 The recurrence itself lives in a third-party kernel absent from the reference tree (FlashInfer persistent KDA). It is
 restated from the published KDA/gated-delta-rule algorithm as the upstream vLLM 0.22.0 FLA port states it
 (vllm/model_executor/layers/fla/ops/fused_recurrent.py `fused_recurrent_gated_delta_rule_fwd_kernel` with IS_KDA,
-kda.py `chunk_kda` with `use_qk_l2norm_in_kernel=True` as vLLM's Kimi layer calls it) -- an unpinned cross-check:
+kda.py `chunk_kda` with `use_qk_l2norm_in_kernel=True` as vLLM's Kimi layer calls it):
 
   q, k <- q / sqrt(|q|^2 + 1e-6), k / sqrt(|k|^2 + 1e-6)          (per head row)
   gk   = lower_bound * sigmoid(exp(A_log[h]) * (g + dt_bias))    (per key channel; the bounded "safe" gate)
@@ -26,7 +26,9 @@ kda.py `chunk_kda` with `use_qk_l2norm_in_kernel=True` as vLLM's Kimi layer call
   S    <- diag(exp(gk)) S                                         (S: [key, value])
   u    = b * (v - S^T k);  S <- S + k u^T;  o = scale * S^T q
 
-Parity: unpinned against the reference (its KDA kernels are third-party libraries absent here).
+Parity: cross-checked against vLLM 0.22.0's `chunk_kda` run on a B200 (tests/golden/kda_vllm.npz,
+tests/test_oracle_vllm_golden.py: outputs and final states within 1e-2 relative L2, chunk_kda keeping its operands in
+bf16); the reference's own KDA kernel is a third-party library absent here.
 """
 
 from __future__ import annotations

@@ -6,7 +6,7 @@ residual, post mix, comb mix, layer input; RMSNorm with the layer's norm weight)
 (`edge_send` = the last layer's hc_post flattened to [T, 4 * H], `edge_recv` = a standalone hc_pre, :156-163). The
 arithmetic inside those library calls (DeepGEMM `mega_mhc`, vLLM TileLang) is absent from the reference tree; this
 follows the published algorithm as the upstream vLLM 0.22.0 CPU path states it
-(vllm/model_executor/kernels/mhc/torch.py `mhc_pre_torch` / `mhc_post_torch`, an unpinned cross-check):
+(vllm/model_executor/kernels/mhc/torch.py `mhc_pre_torch` / `mhc_post_torch`):
 
   post:  new_res[j] = post[j] * x + sum_i comb[i, j] * res[i]                 (bf16 out)
   pre:   z = new_res flattened [4H] (fp32 of the bf16 values); mixes = (z @ fn.T) * rsqrt(mean(z^2) + rms_eps)
@@ -16,7 +16,9 @@ follows the published algorithm as the upstream vLLM 0.22.0 CPU path states it
          comb = comb / (colsum + sinkhorn_eps); then (repeat - 1) x: row-normalise, column-normalise (+ eps)
          y    = RMSNorm(sum_i pre[i] * new_res[i]) * norm_weight                (bf16 out; the layer input)
 
-Parity: unpinned against the reference (its kernels are third-party libraries absent here).
+Parity: pinned to the outputs of vLLM 0.22.0's `mhc_pre_torch` / `mhc_post_torch` on seeded inputs
+(tests/golden/mhc_vllm.npz, tests/test_oracle_vllm_golden.py); the reference's own fused kernels are third-party
+libraries absent here.
 """
 
 from __future__ import annotations
@@ -45,8 +47,9 @@ def post(x, res, post_mix, comb):
     return bf16((mixed + np.asarray(post_mix, np.float64)[:, :, None] * x[:, None, :].astype(np.float64)))
 
 
-def pre(res, fn, scale, base, rms_eps, pre_eps, sinkhorn_eps, post_mult, repeat, norm_w, norm_eps):
-    """res [T, 4, H] (bf16 values) -> (post_mix [T, 4], comb [T, 4, 4], y [T, H] bf16-valued)."""
+def pre_mixes(res, fn, scale, base, rms_eps, pre_eps, sinkhorn_eps, post_mult, repeat):
+    """The pre step up to its layer input: res [T, 4, H] (bf16 values) -> (post_mix [T, 4], comb [T, 4, 4],
+    layer input [T, H] bf16-valued, before the layer's RMSNorm) -- the outputs of vLLM's `mhc_pre_torch`."""
     res = np.asarray(res, np.float32)
     T, hc, H = res.shape
     z = res.reshape(T, hc * H).astype(np.float64)
@@ -64,9 +67,15 @@ def pre(res, fn, scale, base, rms_eps, pre_eps, sinkhorn_eps, post_mult, repeat,
         comb = comb / (comb.sum(axis=1, keepdims=True) + sinkhorn_eps)
     li = (pre_mix[:, :, None] * res.astype(np.float64)).sum(axis=1)
     li = bf16(li)                                        # the op's layer input is bf16 before the norm
+    return post_mix.astype(np.float32), comb.astype(np.float32), li
+
+
+def pre(res, fn, scale, base, rms_eps, pre_eps, sinkhorn_eps, post_mult, repeat, norm_w, norm_eps):
+    """res [T, 4, H] (bf16 values) -> (post_mix [T, 4], comb [T, 4, 4], y [T, H] bf16-valued)."""
+    post_mix, comb, li = pre_mixes(res, fn, scale, base, rms_eps, pre_eps, sinkhorn_eps, post_mult, repeat)
     inv = 1.0 / np.sqrt((li.astype(np.float64) ** 2).mean(axis=1, keepdims=True) + norm_eps)
     y = bf16(li * inv * np.asarray(norm_w, np.float64))
-    return post_mix.astype(np.float32), comb.astype(np.float32), y
+    return post_mix, comb, y
 
 
 def post_pre(x, res, post_mix, comb, *args):

@@ -14,15 +14,21 @@ operations with `__fdiv_rn` / `__fmul_rn`, produces the same bytes:
     amax = max |x| over the 16-block
     sf   = e4m3_rne_satfinite((amax / 6) * gs)
     r    = gs / float(sf)                      (codes are 0 when sf decodes to 0)
-    code = e2m1_rne_satfinite(x * r)           (ties to the even code; a code of magnitude 0 carries no sign)
+    code = e2m1_rne_satfinite(x * r)           (ties to the even code; the sign bit is the sign of x * r, so a
+                                                value that rounds to zero keeps its sign, as the hardware
+                                                conversion cvt.rn.satfinite.e2m1x2 and vLLM's quantizer give it;
+                                                with sf = 0, r = 0 and every code is a signed zero)
 
 Scale-factor storage ("128x4 atoms", the operand layout of the tcgen05 block-scaled MMA): rows padded to a multiple
 of 128, K padded to a multiple of 256 (one GEMM k-block: 4 atom columns of 64 elements); the 128-row x 4-scale atom
 (row block rb, atom column cb) is 512 contiguous bytes at ((rb * n_cb) + cb) * 512, and inside it scale (r, c) sits at
 byte (r % 32) * 16 + ((r // 32) % 4) * 4 + c % 4.
 
-Parity: pinned by known-answer tests of the format (tests/test_oracle_nvfp4.py); no reference implementation of the
-quantizer exists in the reference tree.
+Parity: known-answer tests of the format (tests/test_oracle_nvfp4.py), and a cross-check against the quantizer the
+reference calls, upstream vLLM 0.22.0 `scaled_fp4_quant`, run on a B200 (tests/golden/nvfp4_vllm.npz,
+tests/test_oracle_vllm_golden.py): the swizzled scale layout is identical to the 128x4 atoms; scales and codes are
+byte-identical except for blocks whose (amax / 6) * gs sits on an e4m3 rounding midpoint, where vLLM's
+reciprocal-multiply (amax * (1/6)) can land on the other side and the whole block then differs by one scale step.
 """
 
 from __future__ import annotations
@@ -93,12 +99,13 @@ def e4m3_decode(c) -> np.ndarray:
 
 
 def e2m1_encode(a) -> np.ndarray:
-    """fp32 -> e2m1 code (0..15), round to nearest, ties to the even code, saturating at +-6; NaN -> 0."""
+    """fp32 -> e2m1 code (0..15), round to nearest, ties to the even code, saturating at +-6, the sign bit the sign
+    of the input (-0.1 and -0.0 give code 8, negative zero); NaN -> 0."""
     a = np.asarray(a, dtype=np.float32)
     m = np.abs(a)
     idx = ((m > 0.25).astype(np.uint8) + (m >= 0.75) + (m > 1.25) + (m >= 1.75) + (m > 2.5) + (m >= 3.5)
            + (m > 5.0)).astype(np.uint8)
-    neg = (a < 0) & (idx > 0)
+    neg = np.signbit(a) & ~np.isnan(a)
     return (idx | (neg.astype(np.uint8) << 3)).astype(np.uint8)
 
 
@@ -118,8 +125,7 @@ def quantize(x, gs: float) -> tuple[np.ndarray, np.ndarray]:
     sfv = e4m3_decode(sf)
     with np.errstate(divide="ignore", invalid="ignore"):
         r = np.where(sfv > 0, gs / np.where(sfv > 0, sfv, np.float32(1.0)), np.float32(0.0)).astype(np.float32)
-    codes = e2m1_encode((blk * r[:, :, None]).astype(np.float32))
-    codes[(sfv == 0)] = 0
+    codes = e2m1_encode((blk * r[:, :, None]).astype(np.float32))      # r = 0: signed zeros
     return codes.reshape(R, K), sf
 
 

@@ -232,14 +232,6 @@ __host__ __device__ constexpr uint32_t idesc_nvf4(uint32_t M, uint32_t N) {
 }
 
 // ---- NVFP4 codec --------------------------------------------------------------------------------------------------
-// e2m1 round to nearest, ties to the even code, saturating at 6; a code of magnitude 0 carries no sign.
-SSB_DEVICE uint32_t e2m1_encode(float a) {
-  const float m = fabsf(a);
-  uint32_t idx = (m > 0.25f) + (m >= 0.75f) + (m > 1.25f) + (m >= 1.75f) + (m > 2.5f) + (m >= 3.5f) + (m > 5.0f);
-  const uint32_t neg = (a < 0.0f && idx != 0u) ? 8u : 0u;
-  return idx | neg;
-}
-
 SSB_DEVICE float e2m1_value(uint32_t code) {
   const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
   const float v = mag[code & 7u];
@@ -256,16 +248,15 @@ SSB_DEVICE float e4m3_value(uint32_t code) {
 }
 
 // Eight e2m1 codes (a 32-bit word, element i in nibble i) of a[0..7], round to nearest even, saturating at 6, by the
-// hardware conversion (cvt.rn.satfinite.e2m1x2.f32); then a code of magnitude 0 loses its sign, as in e2m1_encode.
+// hardware conversion (cvt.rn.satfinite.e2m1x2.f32); a value that rounds to zero keeps its sign (code 8 for a
+// negative one), as vLLM's NVFP4 quantizer, which converts with the same instruction, writes it.
 SSB_DEVICE uint32_t e2m1x8(const float* a) {
   uint32_t w = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i)
     w |= static_cast<uint32_t>(__nv_cvt_float2_to_fp4x2(make_float2(a[2 * i], a[2 * i + 1]), __NV_E2M1,
                                                         cudaRoundNearest)) << (8 * i);
-  const uint32_t m = w & 0x77777777u;
-  const uint32_t nz = (m | (m >> 1) | (m >> 2)) & 0x11111111u;
-  return m | (w & (nz << 3));
+  return w;
 }
 
 // Quantize 16 values with global scale gs: returns the scale byte, writes 8 bytes of packed codes (element 2i in the

@@ -14,12 +14,13 @@ def test_e2m1_grid_and_ties():
             6.0]
     np.testing.assert_array_equal(nvfp4.e2m1_decode(nvfp4.e2m1_encode(vals)), np.array(want, dtype=np.float32))
     np.testing.assert_array_equal(nvfp4.e2m1_decode(nvfp4.e2m1_encode(-vals)), -np.array(want, dtype=np.float32))
-    # every grid value maps to its own code; zero never carries a sign
+    # every grid value maps to its own code, negative zero included; a value that rounds to zero keeps its sign (the
+    # hardware conversion's and vLLM's quantizer's convention)
     codes = np.arange(16, dtype=np.uint8)
     v = nvfp4.e2m1_decode(codes)
-    back = nvfp4.e2m1_encode(v)
-    np.testing.assert_array_equal(back[codes != 8], codes[codes != 8])
-    assert back[8] == 0 and nvfp4.e2m1_encode(np.float32(-0.1)) == 0
+    v[8] = -0.0
+    np.testing.assert_array_equal(nvfp4.e2m1_encode(v), codes)
+    assert nvfp4.e2m1_encode(np.float32(-0.1)) == 8 and nvfp4.e2m1_encode(np.float32(0.1)) == 0
 
 
 def test_e4m3_every_code_and_midpoints():

@@ -1,0 +1,80 @@
+"""The oracle against the library implementations the reference's mHC, KDA and NVFP4 steps come from: upstream vLLM
+0.22.0's `mhc_pre_torch` / `mhc_post_torch`, FLA `chunk_kda` and `scaled_fp4_quant`, whose outputs on seeded inputs are
+committed under tests/golden/ (made by tests/golden/make_vllm_golden.py; the inputs are regenerated here from the
+same seeds). Tolerances are stated per assert, each with the margin over the measured difference."""
+
+import sys
+from pathlib import Path
+
+import numpy as np
+
+from oracle import kda, mhc, nvfp4
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+sys.path.insert(0, str(GOLDEN))
+import make_vllm_golden as gen  # noqa: E402
+
+BF16_STEP = 2.0 ** -7          # one bf16 step relative to the value, at most
+
+
+def test_mhc_pre_matches_vllm():
+    f = np.load(GOLDEN / "mhc_vllm.npz")
+    i, e = gen.mhc_inputs(), gen.MHC_EPS
+    post_mix, comb, li = mhc.pre_mixes(i["res"], i["fn"], i["scale"], i["base"], e["rms_eps"], e["pre_eps"],
+                                       e["sinkhorn_eps"], e["post_mult"], e["repeat"])
+    # fp32 (vLLM) against float64 (oracle): measured 2.7e-7 of the largest value
+    np.testing.assert_allclose(post_mix, f["pre_post_mix"], rtol=0, atol=2e-6 * np.abs(f["pre_post_mix"]).max())
+    np.testing.assert_allclose(comb, f["pre_comb"], rtol=0, atol=2e-6 * np.abs(f["pre_comb"]).max())
+    # the bf16 layer input: measured identical
+    np.testing.assert_array_equal(li, f["pre_layer_input"])
+
+
+def test_mhc_post_matches_vllm():
+    f = np.load(GOLDEN / "mhc_vllm.npz")
+    i = gen.mhc_inputs()
+    got, want = mhc.post(i["x"], i["res"], i["post_mix"], i["comb"]), f["post_new_res"]
+    diff = got != want
+    # fp32 and float64 sums round to bf16 alike but where they straddle a rounding boundary: measured 1 of 6,144
+    assert diff.mean() <= 1e-3, diff.sum()
+    assert (np.abs(got - want)[diff] <= BF16_STEP * np.abs(want)[diff]).all()
+
+
+def test_kda_recurrence_matches_vllm_chunk_kda():
+    f = np.load(GOLDEN / "kda_vllm.npz")
+    i = gen.kda_inputs()
+    H, D = i["H"], i["D"]
+    out, state = kda.recurrent(i["q"], i["k"], i["v"], i["g"], i["beta"], i["a_log"], i["dt_bias"],
+                               gen.KDA_LOWER_BOUND, D ** -0.5, i["state"], gen.KDA_SEQS, H, D)
+
+    def rel(a, b):
+        return np.linalg.norm(a - b) / np.linalg.norm(b)
+
+    # chunk_kda keeps q, k, v and the solved triangular block in bf16: measured 4.0e-3 (output), 3.2e-3 (states)
+    assert rel(out, f["chunk_o"]) < 1e-2
+    for n, (s, e, blk, _) in enumerate(gen.KDA_SEQS):
+        assert rel(out[s:e], f["chunk_o"][s:e]) < 1e-2, n
+        assert rel(state[blk], f["chunk_state"][n]) < 1e-2, n
+
+
+def test_nvfp4_quantizer_matches_vllm_scaled_fp4_quant():
+    f = np.load(GOLDEN / "nvfp4_vllm.npz")
+    i = gen.nvfp4_inputs()
+    x, gs = i["x"], i["gs"]
+    codes, sf = nvfp4.quantize(x, gs)
+    # the swizzled scale layout vLLM writes is the 128x4-atom layout of the GEMM operands
+    np.testing.assert_array_equal(nvfp4.sf_to_atoms(f["sf"]), f["sf_swizzled"])
+    # scales: identical except where (amax / 6) * gs sits on an e4m3 rounding midpoint (measured 4 of 6,400 blocks):
+    # there vLLM's amax * (1/6) lands on the other side, one scale step away
+    differ = sf != f["sf"]
+    assert differ.sum() <= 8, differ.sum()
+    amax = np.abs(x).reshape(x.shape[0], -1, 16).max(axis=2)
+    for r, b in np.argwhere(differ):
+        lo, hi = sorted(nvfp4.e4m3_decode(np.array([sf[r, b], f["sf"][r, b]])))
+        assert abs(int(sf[r, b]) - int(f["sf"][r, b])) == 1
+        sf_f = np.float32(amax[r, b] / np.float32(6.0)) * np.float32(gs)
+        assert abs(sf_f - (lo + hi) / 2) <= 4 * np.spacing(np.float32(sf_f)), (r, b)
+    # codes: byte-identical, signed zeros included, in every block whose scale agrees
+    same = np.repeat(~differ, 16, axis=1)
+    vcodes = nvfp4.unpack(f["codes"])
+    np.testing.assert_array_equal(codes[same], vcodes[same])
+    assert (vcodes == 8).any()          # the fixture holds negative zeros
