@@ -21,8 +21,11 @@ Permutation (bit-exact contract with the CUDA path): expert-major, tokens ascend
 expert last; expert e's rows start at offset[e] = sum over e' < e of ceil(n_e' / 128) * 128 (so every 128-row tile
 belongs to one expert).
 
-Parity: unpinned against the reference itself (the library is absent); the routing rule is pinned by known-answer
-tests of the rule (tests/test_oracle_moe.py).
+Parity: the reference's library is absent; the routing rule is pinned by known-answer tests of the rule
+(tests/test_oracle_moe.py), and the expert path is cross-checked against vLLM 0.22.0's CUTLASS NVFP4 MoE run on a
+B200 on the same codes, scales, global scales and routing (tests/golden/moe_vllm.npz, tests/test_oracle_vllm_golden.py):
+with vLLM's bf16 intermediates restated (`intermediates="bf16"`) the outputs agree to about 1e-4 relative L2; with this
+layer's fp32 intermediates they differ by 2.4e-2, the requant of the bf16-rounded SwiGLU product accounting for it.
 """
 
 from __future__ import annotations
@@ -76,15 +79,27 @@ def permutation(ids, num_experts: int, shared: bool = True):
     return counts.astype(np.int32), offsets, rows, shared_rows
 
 
+def _bf16(a) -> np.ndarray:
+    """Round fp32 to bf16 (nearest even), returned as fp32 values."""
+    u = np.asarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    return (((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16).astype(np.uint32).view(np.float32)
+
+
 def silu(g):
     g = np.asarray(g, dtype=np.float32)
     return (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
 
 
-def expert_ffn(xd, w1d, w2d, gs_h: float, F: int) -> np.ndarray:
-    """xd [n, H] fp32 (dequantized input rows), w1d [2F, H], w2d [H, F] -> y [n, H] fp32."""
+def expert_ffn(xd, w1d, w2d, gs_h: float, F: int, intermediates: str = "fp32") -> np.ndarray:
+    """xd [n, H] fp32 (dequantized input rows), w1d [2F, H], w2d [H, F] -> y [n, H] fp32.
+    intermediates "bf16": the gate_up output and the SwiGLU product are rounded to bf16 before the requant, as vLLM's
+    CUTLASS NVFP4 MoE keeps them (used only to cross-check against it); "fp32" is this layer's own rule."""
     gu = xd @ w1d.T
+    if intermediates == "bf16":
+        gu = _bf16(gu)
     h = silu(gu[:, :F]) * gu[:, F:]
+    if intermediates == "bf16":
+        h = _bf16(h)
     hq, hs = nvfp4.quantize(h, gs_h)
     return nvfp4.dequantize(hq, hs, gs_h) @ w2d.T
 
@@ -97,12 +112,15 @@ def dequantize_params(p: dict) -> dict:
     return {"router": nvfp4.dequantize(rc, rs, rg), "experts": experts}
 
 
-def moe_forward(x, p: dict, k: int, ids=None, weights=None, return_parts: bool = False, dense: dict | None = None):
+def moe_forward(x, p: dict, k: int, ids=None, weights=None, return_parts: bool = False, dense: dict | None = None,
+                intermediates: str = "fp32"):
     """x fp32 [T, H] (bf16 values) and the layer's logical NVFP4 parameters `p` (see `ssengine_b200.weights`):
     p["gs_x"], p["gs_h"], p["router"] = (codes [E, H], sf [E, H/16], gs), p["experts"] = list of E + 1 tuples
     (w1 codes [2F, H], w1 sf, w1 gs, w2 codes [H, F], w2 sf, w2 gs), the shared expert last.
     `ids` / `weights` override the routing (to check the FFN path on the CUDA path's own routing); `dense` is
-    `dequantize_params(p)` when the caller holds it already."""
+    `dequantize_params(p)` when the caller holds it already. `intermediates` "bf16" restates vLLM's CUTLASS NVFP4 MoE
+    (bf16 gate_up output, bf16 SwiGLU product, bf16 expert rows, weights and products in the combine, a bf16 sum) to
+    cross-check the algorithm against it; the layer's own rule keeps all of them in fp32."""
     x = np.asarray(x, dtype=np.float32)
     T, H = x.shape
     E = len(p["experts"]) - 1
@@ -129,15 +147,21 @@ def moe_forward(x, p: dict, k: int, ids=None, weights=None, return_parts: bool =
         if tok.size == 0:
             continue
         w1d, w2d = dense["experts"][e]
-        y = expert_ffn(xd[tok], w1d, w2d, p["gs_h"], F)
+        y = expert_ffn(xd[tok], w1d, w2d, p["gs_h"], F, intermediates)
         if e < E:
             y_routed[tok, slot] = y
         else:
             y_shared = y
     # combine in a fixed order: the k routed slots in rank order, the shared expert last
-    for j in range(k):
-        out += weights[:, j:j + 1] * y_routed[:, j]
-    out += y_shared
+    if intermediates == "bf16":
+        ws = _bf16(weights)
+        for j in range(k):
+            out += _bf16(ws[:, j:j + 1] * _bf16(y_routed[:, j]))
+        out = _bf16(out + _bf16(y_shared))
+    else:
+        for j in range(k):
+            out += weights[:, j:j + 1] * y_routed[:, j]
+        out += y_shared
     if return_parts:
         return out, {"logits": logits, "ids": ids.astype(np.int32), "weights": weights, "y_routed": y_routed,
                      "y_shared": y_shared}
