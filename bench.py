@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Prefill-stage benchmark on B200: one NVFP4 MoE layer over an 8,192-token microbatch.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--tokens T]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|vllm-cutlass] [--tokens T]
 
 One JSON line on rank 0. A step is one forward of the layer (quantize -> router GEMM -> top-8 routing -> permutation
 -> grouped NVFP4 gate_up GEMM + SwiGLU + requant -> grouped down GEMM -> weighted combine + shared expert) over T
@@ -11,6 +11,9 @@ steps' copies and forwards overlapped on three streams, as a serving loop runs t
 runs its own replica on its own microbatch (weak scaling, no collective on the data path); the time is the max over
 ranks. `--impl reference` times the CPU restatement of the path (the reference has no CPU implementation of its
 own; its GPU path needs a vLLM fork and FlashInfer builds absent here) on the host cores, rank 0 only.
+`--impl vllm-cutlass` is a library comparison on the GPU, rank 0 only: the same experts (same NVFP4 codes, scales
+and global scales, the routing of our router) through the NVFP4 MoE of the vLLM 0.22.0 installed in the image
+(`run_cutlass_moe_fp4`, CUTLASS sm_100 grouped GEMMs); its line reports the expert path, and ours beside it.
 """
 
 from __future__ import annotations
@@ -40,7 +43,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "vllm-cutlass"], default="ours")
     ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--cpu-tokens", type=int, default=1024, help="CPU baseline sample (tokens)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -233,6 +236,118 @@ def run_reference(args, rank: int) -> None:
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     del np
+
+
+def run_vllm_cutlass(args, rank: int) -> None:
+    """Library comparison: the layer's experts through vLLM 0.22.0's `run_cutlass_moe_fp4` (row shuffle, activation
+    NVFP4 quant, CUTLASS grouped GEMM, fused SiLU-and-mul + requant, grouped GEMM, unshuffle, weighted combine in
+    torch), on the same weights and on the routing our router chose, the shared expert as expert E with weight 1.
+    Timed like ours (CUDA events over K steps after W warm-up steps, weights and workspaces larger than L2); the line
+    carries our own expert-path time (every step but the router GEMM and the routing) of the same run beside it."""
+    if rank != 0:
+        return
+    import torch
+    from vllm.model_executor.layers.fused_moe.activation import MoEActivation
+    from vllm.model_executor.layers.fused_moe.experts.cutlass_moe import run_cutlass_moe_fp4
+    from vllm.model_executor.layers.quantization.utils.nvfp4_utils import swizzle_blockscale
+
+    from ssengine_b200 import lib, moe, weights
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    T, steps, warm = args.tokens, args.steps, max(3, args.warmup)
+    p = weights.moe_logical(SEED, H, F, E, device=device)
+    layer = moe.MoELayer.from_logical(p, K_TOP, device)
+    x = weights.hidden_states(SEED + 1, T, H, device=device)
+    out = torch.empty_like(x)
+    for _ in range(warm):
+        layer.forward(x, out)
+    nst = len(lib.MOE_STEPS)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nst + 1)] for _ in range(steps)]
+    for row in evs:
+        for e in row:
+            e.record()                              # creates the CUDA event the library records into
+    for i in range(steps):
+        layer.forward_profiled(x, out, evs[i])
+    torch.cuda.synchronize()
+    layer.check_status()
+    ours = {name: sum(evs[i][s].elapsed_time(evs[i][s + 1]) for i in range(steps)) / steps
+            for s, name in enumerate(lib.MOE_STEPS)}
+    ours_experts = sum(v for n, v in ours.items() if n not in ("router_gemm", "route"))
+    ids = layer.ws_view("IDS", T, torch.int32, (T, K_TOP)).clone()
+    wts = layer.ws_view("WEIGHTS", T, torch.float32, (T, K_TOP)).clone()
+    del layer
+    torch.cuda.empty_cache()
+
+    def pack(c):                                   # one code per byte -> two per byte, the even element low
+        return (c[:, 0::2] | (c[:, 1::2] << 4)).contiguous()
+
+    ex = p["experts"]
+    w1 = torch.stack([pack(e[0]) for e in ex])
+    s1 = swizzle_blockscale(torch.stack([e[1] for e in ex]).view(torch.float8_e4m3fn))
+    w2 = torch.stack([pack(e[3]) for e in ex])
+    s2 = swizzle_blockscale(torch.stack([e[4] for e in ex]).view(torch.float8_e4m3fn))
+    gs1 = torch.tensor([e[2] for e in ex], dtype=torch.float32, device=device)
+    gs2 = torch.tensor([e[5] for e in ex], dtype=torch.float32, device=device)
+    del p, ex
+    ne, kk = E + 1, K_TOP + 1
+    a1 = torch.full((ne,), weights.GS_X, dtype=torch.float32, device=device)
+    a2 = torch.full((ne,), weights.GS_H, dtype=torch.float32, device=device)
+    al1, al2 = 1.0 / (a1 * gs1), 1.0 / (a2 * gs2)
+    topk_ids = torch.cat([ids, torch.full((T, 1), E, dtype=torch.int32, device=device)], dim=1).contiguous()
+    topk_w = torch.cat([wts, torch.ones((T, 1), dtype=torch.float32, device=device)], dim=1).contiguous()
+    vout = torch.empty_like(x)
+    ws13 = torch.empty(T * kk * max(2 * F, H), dtype=torch.bfloat16, device=device)
+    ws2 = torch.empty(T * kk * F, dtype=torch.bfloat16, device=device)
+
+    def step():
+        run_cutlass_moe_fp4(vout, x, a1, w1, s1, al1, a2, w2, s2, al2, topk_w, topk_ids, MoEActivation.SILU, ws13,
+                            ws2, T, F, H, ne, device)
+
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    rel = float((vout.float() - out.float()).norm() / out.float().norm())
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    eager_ms = start.elapsed_time(end) / steps
+    # the same step replayed from a CUDA graph, so that host-side launch and allocation costs do not count
+    graph_ms, graph_err = None, None
+    try:
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        with torch.cuda.graph(g):
+            step()
+        for _ in range(warm):
+            g.replay()
+        start.record()
+        for _ in range(steps):
+            g.replay()
+        end.record()
+        torch.cuda.synchronize()
+        graph_ms = start.elapsed_time(end) / steps
+    except Exception as exc:                        # noqa: BLE001 -- reported in the line
+        graph_err = f"{type(exc).__name__}: {str(exc)[:160]}"
+    ms = min(eager_ms, graph_ms) if graph_ms else eager_ms
+    line = {"impl": "vllm-cutlass", "metric": "prefill tok/s", "value": T / ms * 1e3, "unit": "tok/s", "n_gpus": 1,
+            "steps": steps, "warmup": warm, "ms_per_step": ms, "eager_ms_per_step": eager_ms,
+            "graph_ms_per_step": graph_ms, "graph_error": graph_err, "higher_is_better": True,
+            "dtype": "nvfp4 x nvfp4",
+            "scope": "experts only: routing given (our router's), shared expert as expert E; vLLM 0.22.0 "
+                     "run_cutlass_moe_fp4",
+            "ours_experts_ms_per_step": ours_experts, "ours_layer_ms_per_step": sum(ours.values()),
+            "rel_l2_vs_ours": rel, "data": "synthetic: hidden N(0,1) bf16, seeded random-init NVFP4 weights",
+            "config": {"workload": workload(T),
+                       "l2": "inputs larger than L2 (0.9 GB of expert weights + workspaces per step)"}}
+    print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------------------------- components
@@ -455,6 +570,9 @@ def main() -> None:
     __graft_entry__.import_package()
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.impl == "vllm-cutlass":
+        run_vllm_cutlass(args, rank)
         return
 
     from ssengine_b200 import lib
