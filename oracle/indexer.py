@@ -2,8 +2,10 @@
 
 - Logits over pooled keys (kpool = 4 tokens): logit[t, p] = sum_h w[t, h] * relu(q[t, h, :] . k_pool[p, :]) for the
   pools p < (pos_t + 1) // 4 that row t may see (the fork's kpool indexer calling DeepGEMM `fp8_mqa_logits`,
-  ssengine/kernels.py config 19; the score is the DeepSeek-V3.2 lightning-indexer formula). Parity: unpinned against
-  the reference (the fork and DeepGEMM are absent); this build keeps q / k in bf16.
+  ssengine/kernels.py config 19; the score is the DeepSeek-V3.2 lightning-indexer formula). Parity: the fork and
+  DeepGEMM are absent; the score and the pool visibility are cross-checked against DeepGEMM's own reference of the
+  score as vLLM 0.22.0 vendors it (`fp8_mqa_logits_torch`, fixture tests/golden/indexer_vllm.npz: same masked
+  columns, values within 3.2e-3 of each row's largest logit, its bf16 score rounding); this build keeps q / k in bf16.
 - Pool -> token expansion: restated from ssengine/model/kpool_fast.py:23-41 (`_expand_rows_kernel`; pure index
   arithmetic, the fork's `expand_pools_and_append_tail`).
 - Pool keys paged like the KV: pool p of a request sits in its KV page p // 32 at row page * 32 + p % 32.

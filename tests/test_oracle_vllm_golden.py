@@ -1,6 +1,7 @@
 """The oracle against the library implementations the reference's mHC, KDA and NVFP4 steps come from: upstream vLLM
-0.22.0's `mhc_pre_torch` / `mhc_post_torch`, FLA `chunk_kda`, `scaled_fp4_quant` and the CUTLASS NVFP4 MoE
-(`run_cutlass_moe_fp4`), whose outputs on seeded inputs are
+0.22.0's `mhc_pre_torch` / `mhc_post_torch`, `fp8_mqa_logits_torch` (DeepGEMM's reference of the indexer score),
+FLA `chunk_kda`, `scaled_fp4_quant` and the CUTLASS NVFP4 MoE (`run_cutlass_moe_fp4`), whose outputs on seeded inputs
+are
 committed under tests/golden/ (made by tests/golden/make_vllm_golden.py; the inputs are regenerated here from the
 same seeds). Tolerances are stated per assert, each with the margin over the measured difference."""
 
@@ -104,3 +105,20 @@ def test_moe_experts_match_vllm_cutlass_nvfp4_moe():
     assert rel(got, same) < 1e-3
     # the layer's own fp32 intermediates: measured 2.4e-2, inside the per-layer bar of 3e-2
     assert rel(got, ref) < 3e-2
+
+
+def test_indexer_logits_match_deepgemm_reference():
+    from oracle import indexer
+
+    f = np.load(GOLDEN / "indexer_vllm.npz")["logits"]
+    i = gen.indexer_inputs()
+    pages = np.arange(i["k"].shape[0] // indexer.POOLS_PER_PAGE)     # pool p at cache row p
+    rows = indexer.logits(i["q"], i["w"], i["k"], pages, i["positions"])
+    assert any(len(r) == 0 for r in rows) and max(len(r) for r in rows) > 50
+    for r, row in enumerate(rows):
+        n = len(row)
+        # the same visibility: pools < (pos + 1) / 4 are scored, the rest masked to -inf
+        assert np.isfinite(f[r, :n]).all() and np.isneginf(f[r, n:]).all(), r
+        # the reference rounds each head's score to bf16 before the ReLU: measured 3.2e-3 of the row's largest logit
+        if n:
+            assert np.abs(row - f[r, :n]).max() <= 1e-2 * np.abs(row).max(), r
