@@ -1,7 +1,9 @@
 """Stage-level pieces of the oracle (TEST INFRASTRUCTURE ONLY; see oracle/__init__.py): RMSNorm, the NVFP4 lm_head
 and the greedy token, restating the reference's `head_logits` / argmax (ssengine/model/stage.py:746-762): the last
 row of each finished request -> final RMSNorm -> lm_head -> argmax (the lowest index among equal maxima).
-Parity: unpinned against the reference (its lm_head runs in the absent vLLM fork); rule KATs only."""
+Parity: the lm_head runs in the absent vLLM fork; the RMSNorm is cross-checked against vLLM 0.22.0's `rms_norm`
+(tests/golden/norms_vllm.npz: identical bytes with vLLM's rounding of the normalized row before the weight multiply
+restated, within one bf16 step with this build's single rounding); the head and argmax by rule KATs."""
 
 from __future__ import annotations
 
