@@ -4,6 +4,10 @@ pool[p, c] = sum_j softmax_j(gate[4p+j, c] + ape[j, c]) * k[4p+j, c], the refere
 (tests/test_kpool_cpu.py:20-25); tokens of a pool before a chunk's start come from the request's tail ring, seeded
 with the previous chunk's trailing tokens (pp_patch.py:415-534, `ref_seed` tests/test_kpool_cpu.py:28-38). The
 reference's property: any chunking of a prompt writes the pools of the unsplit prefill.
+
+Parity: pinned to the reference's own insert path run here (pp_patch `kpool_heads` / `kpool_compress_insert` /
+`kpool_seed_tail_cache` with its torch reference ops; tests/golden/kpool_ref.npz): pools within 2.2e-7 and the tail
+ring identical, over chunked prefills of three requests that start inside pools and share microbatches.
 """
 
 from __future__ import annotations

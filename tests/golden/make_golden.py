@@ -10,6 +10,10 @@ It imports (never copies) these reference functions and records their outputs on
 - ssengine/model/metadata.py:65-76    `graph_rows`                -> (in g0_table.npz)
 - ssengine/model/stage.py:63-69       `GRAPH_BUCKETS`, `graph_bucket` -> buckets.json
 - ssengine/engine/kv.py:60-75         `block_pages`, `kv_pages_for`   -> (in g0_table.npz)
+- ssengine/model/pp_patch.py          `kpool_heads`, `kpool_compress_insert`, `kpool_seed_tail_cache`, driven as the
+  reference's tests/test_kpool_cpu.py drives them (`indexer_call`, with its torch reference ops `ref_compress` /
+  `ref_seed`): pools written by chunked prefills that start inside a pool, several requests in one microbatch
+                                                                       -> kpool_ref.npz (`--parts kpool`)
 The fixtures are small (tens of KB) and committed; the tests never read the reference at run time.
 """
 
@@ -25,10 +29,53 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 
 
+# (request, start, tokens) microbatches over prompts of KPOOL_LENS tokens; chunk starts inside pools, a request resumed
+# right after another's rows, a microbatch shorter than one pool
+KPOOL_LENS = [40, 24, 30]
+KPOOL_SCHEDULE = [[(0, 0, 13), (2, 0, 13)], [(2, 13, 3)], [(0, 13, 14), (1, 0, 24), (2, 16, 14)], [(0, 27, 13)]]
+
+
+def kpool_inputs(seed: int = 20261207):
+    """Per request bf16 key and gate rows [L, 8] and the pool position embedding ape [4, 8] (fp32)."""
+    rng = np.random.default_rng(seed)
+
+    def b16(a):
+        import torch
+
+        return torch.from_numpy(a.astype(np.float32)).to(torch.bfloat16).float().numpy()
+
+    k = [b16(rng.standard_normal((n, 8))) for n in KPOOL_LENS]
+    g = [b16(rng.standard_normal((n, 8))) for n in KPOOL_LENS]
+    return k, g, rng.standard_normal((4, 8)).astype(np.float32)
+
+
+def make_kpool(ref: str) -> None:
+    import torch
+
+    sys.path.insert(0, str(Path(ref) / "tests"))
+    import test_kpool_cpu as rk                  # the reference's own CPU driver and torch reference ops
+
+    k, g, ape = kpool_inputs()
+    k_all = [torch.from_numpy(a).to(torch.bfloat16) for a in k]
+    g_all = [torch.from_numpy(a).to(torch.bfloat16) for a in g]
+    cache = torch.zeros(10000 * len(KPOOL_LENS), rk.HD)
+    tail = torch.zeros(len(KPOOL_LENS), 2, rk.KPOOL, rk.HD, dtype=torch.bfloat16)
+    for mb in KPOOL_SCHEDULE:
+        rk.indexer_call(mb, k_all, g_all, torch.from_numpy(ape), cache, tail)
+    pools = np.concatenate([cache[r * 10000:r * 10000 + n // rk.KPOOL].numpy() for r, n in enumerate(KPOOL_LENS)])
+    np.savez_compressed(HERE / "kpool_ref.npz", pools=pools, tail=tail.float().numpy())
+
+
 def main() -> None:
     ref = os.environ.get("REF")
     if not ref:
         raise SystemExit("set REF to the reference checkout")
+    if sys.argv[1:] == ["--parts", "kpool"]:
+        os.environ.setdefault("SSENGINE_HANDOFF", "/tmp/empty_handoff")
+        sys.path.insert(0, ref)
+        make_kpool(ref)
+        print("wrote kpool_ref.npz")
+        return
     os.environ.setdefault("SSENGINE_HANDOFF", "/tmp/empty_handoff")
     sys.path.insert(0, ref)
     import torch
