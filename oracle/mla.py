@@ -7,8 +7,10 @@ kv8 = e4m3(kv / k_scale), bmm1 = softmax scale * q_scale * k_scale, bmm2 = k_sca
 cache (ssengine/model/stage.py:88 kv_cache_dtype "fp8_e4m3"; ssengine/kernels.py configs 23 `concat_and_cache_mla`
 and 25, the TRTLLM sparse MLA "FP8 q and cache", scales as vLLM 0.22's FlashInfer sparse MLA backend passes them,
 vllm/v1/attention/backends/mla/flashinfer_mla_sparse.py `forward_mqa`). slot(p) = pages[p // 128] * 128 + p % 128;
-a token on a missing page (negative entry) is not read. The kernel itself is third-party and absent here: parity of
-the attention is unpinned; the e4m3 codec is pinned to torch's float8_e4m3fn cast (tests/test_oracle_mla.py).
+a token on a missing page (negative entry) is not read. The kernel itself is third-party and absent here; the
+attention over e4m3 inputs is cross-checked against FlashMLA's reference of sparse MLA prefill as vLLM 0.22.0 vendors
+it (`reference_mla_sparse_prefill`, tests/golden/mla_vllm.npz: 2e-7 relative, -1 fills, repeated tokens and short rows
+included); the e4m3 codec is pinned to torch's float8_e4m3fn cast (tests/test_oracle_mla.py).
 
 E4M3 (OCP FP8): 1 sign, 4 exponent bits (bias 7), 3 mantissa bits; normals (1 + m / 8) 2^(e - 7), subnormals
 m 2^-9, largest finite 448; encoding rounds to nearest, ties to even, and saturates to +-448 (the device's

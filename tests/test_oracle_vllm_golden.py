@@ -1,6 +1,6 @@
 """The oracle against the library implementations the reference's mHC, KDA and NVFP4 steps come from: upstream vLLM
 0.22.0's `mhc_pre_torch` / `mhc_post_torch`, `rms_norm` and the KDA gated norm, `fp8_mqa_logits_torch` (DeepGEMM's
-reference of the indexer score),
+reference of the indexer score), `reference_mla_sparse_prefill` (FlashMLA's reference of sparse MLA prefill),
 FLA `chunk_kda`, `scaled_fp4_quant` and the CUTLASS NVFP4 MoE (`run_cutlass_moe_fp4`), whose outputs on seeded inputs
 are
 committed under tests/golden/ (made by tests/golden/make_vllm_golden.py; the inputs are regenerated here from the
@@ -140,3 +140,15 @@ def test_norms_match_vllm():
     np.testing.assert_array_equal(bf16(bf16(x * inv) * i["w"]), f["rms"])
     ours = bf16(stage.rmsnorm(i["x"], i["w"], i["eps"]))
     assert (np.abs(ours - f["rms"]) <= BF16_STEP * np.abs(f["rms"])).all()
+
+
+def test_sparse_mla_matches_flashmla_reference():
+    from oracle import mla
+
+    f = np.load(GOLDEN / "mla_vllm.npz")
+    i = gen.mla_inputs()
+    pages = np.arange(3)                           # position p at cache row p (three 128-token pages)
+    got = mla.sparse_mla(i["q8"], i["kv8"], i["indices"], pages, i["bmm1"], 1.0)
+    # -1 fills skipped, repeated tokens counted twice, rows shorter than the selection: fp32 reference against the
+    # float64 oracle, measured 2.0e-7 relative L2 (5.1e-7 absolute on values up to 2)
+    np.testing.assert_allclose(got, f["out"], rtol=0, atol=5e-6)
