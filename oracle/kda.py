@@ -26,9 +26,10 @@ kda.py `chunk_kda` with `use_qk_l2norm_in_kernel=True` as vLLM's Kimi layer call
   S    <- diag(exp(gk)) S                                         (S: [key, value])
   u    = b * (v - S^T k);  S <- S + k u^T;  o = scale * S^T q
 
-Parity: cross-checked against vLLM 0.22.0's `chunk_kda` run on a B200 (tests/golden/kda_vllm.npz,
-tests/test_oracle_vllm_golden.py: outputs and final states within 1e-2 relative L2, chunk_kda keeping its operands in
-bf16); the reference's own KDA kernel is a third-party library absent here.
+Parity: pinned to flash-linear-attention 0.5.1's fp32 references (`naive_kda_lowerbound_gate`,
+`naive_recurrent_kda`; tests/golden/kda_fla.npz: gate within 6.5e-7, outputs and final states within 1.4e-7 relative
+L2) and cross-checked against vLLM 0.22.0's `chunk_kda` run on a B200 (tests/golden/kda_vllm.npz: within 4e-3, its
+operands in bf16); the reference's own KDA kernel is a third-party library absent here.
 """
 
 from __future__ import annotations

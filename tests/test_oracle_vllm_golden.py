@@ -1,8 +1,9 @@
 """The oracle against the library implementations the reference's mHC, KDA and NVFP4 steps come from: upstream vLLM
 0.22.0's `mhc_pre_torch` / `mhc_post_torch`, `rms_norm` and the KDA gated norm, `fp8_mqa_logits_torch` (DeepGEMM's
 reference of the indexer score), `reference_mla_sparse_prefill` (FlashMLA's reference of sparse MLA prefill),
-FLA `chunk_kda`, `scaled_fp4_quant` and the CUTLASS NVFP4 MoE (`run_cutlass_moe_fp4`), whose outputs on seeded inputs
-are
+FLA `chunk_kda` (and flash-linear-attention 0.5.1's own fp32 references `naive_recurrent_kda` /
+`naive_kda_lowerbound_gate`), `scaled_fp4_quant` and the CUTLASS NVFP4 MoE (`run_cutlass_moe_fp4`), whose outputs on
+seeded inputs are
 committed under tests/golden/ (made by tests/golden/make_vllm_golden.py; the inputs are regenerated here from the
 same seeds). Tolerances are stated per assert, each with the margin over the measured difference."""
 
@@ -152,3 +153,22 @@ def test_sparse_mla_matches_flashmla_reference():
     # -1 fills skipped, repeated tokens counted twice, rows shorter than the selection: fp32 reference against the
     # float64 oracle, measured 2.0e-7 relative L2 (5.1e-7 absolute on values up to 2)
     np.testing.assert_allclose(got, f["out"], rtol=0, atol=5e-6)
+
+
+def test_kda_gate_and_recurrence_match_fla_naive_reference():
+    f = np.load(GOLDEN / "kda_fla.npz")
+    i = gen.kda_inputs()
+    H, D, T = i["H"], i["D"], i["q"].shape[0]
+    # the lower-bound gate: measured 6.5e-7 absolute (fp32 against float64) on decays in [-5, 0]
+    g = kda.gate(i["g"], i["a_log"], i["dt_bias"], gen.KDA_LOWER_BOUND, H, D).reshape(T, H * D)
+    np.testing.assert_allclose(g, f["gate"], rtol=0, atol=5e-6)
+    out, state = kda.recurrent(i["q"], i["k"], i["v"], i["g"], i["beta"], i["a_log"], i["dt_bias"],
+                               gen.KDA_LOWER_BOUND, D ** -0.5, i["state"], gen.KDA_SEQS, H, D)
+
+    def rel(a, b):
+        return np.linalg.norm(a - b) / np.linalg.norm(b)
+
+    # FLA's fp32 token-by-token reference: measured 1.4e-7 (outputs) and 9e-8 (final states) relative L2
+    assert rel(out, f["o"]) < 1e-5
+    for n, (_, _, blk, _) in enumerate(gen.KDA_SEQS):
+        assert rel(state[blk], f["state"][n]) < 1e-5, n
