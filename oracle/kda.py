@@ -47,9 +47,12 @@ def silu(a):
     return a / (1.0 + np.exp(-a))
 
 
-def conv(x, weight, conv_state, seqs, P):
+def conv(x, weight, conv_state, seqs, P, bf16_products: bool = False):
     """x [T, >= 3P] bf16 values, weight [3P, 4] bf16 values, conv_state [blocks, 3, 3P] bf16 values (copied, not
-    modified), seqs [(start, end, block, init)] -> (q, k, v [T, P] bf16-valued float32, new conv_state)."""
+    modified), seqs [(start, end, block, init)] -> (q, k, v [T, P] bf16-valued float32, new conv_state).
+    Products of bf16 values are exact in fp32, as Dao's channel-last kernel forms them (the reference's conv is
+    bitwise that kernel's per sequence); `bf16_products` rounds each product to bf16 first, as vLLM's Triton
+    `causal_conv1d_fn` does (used only to cross-check against it)."""
     x = np.asarray(x, np.float32)
     w = np.asarray(weight, np.float32)
     st = np.array(conv_state, dtype=np.float32, copy=True)
@@ -61,7 +64,8 @@ def conv(x, weight, conv_state, seqs, P):
         rows = np.concatenate([prev, x[s:e, :C]], axis=0)                  # [n + 3, C]
         acc = np.zeros((n, C), np.float32)
         for j in range(WIDTH):                                              # products of bf16 values are exact
-            acc = (acc + w[:, j][None, :] * rows[j:j + n]).astype(np.float32)
+            prod = (w[:, j][None, :] * rows[j:j + n]).astype(np.float32)
+            acc = (acc + (bf16(prod) if bf16_products else prod)).astype(np.float32)
         out[s:e] = bf16(silu(acc))
         st[blk] = rows[n:n + WIDTH - 1]                                     # last 3 rows (old state if n < 3)
     return out[:, :P], out[:, P:2 * P], out[:, 2 * P:], st

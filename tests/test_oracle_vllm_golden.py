@@ -2,7 +2,7 @@
 0.22.0's `mhc_pre_torch` / `mhc_post_torch`, `rms_norm` and the KDA gated norm, `fp8_mqa_logits_torch` (DeepGEMM's
 reference of the indexer score), `reference_mla_sparse_prefill` (FlashMLA's reference of sparse MLA prefill),
 FLA `chunk_kda` (and flash-linear-attention 0.5.1's own fp32 references `naive_recurrent_kda` /
-`naive_kda_lowerbound_gate`), `scaled_fp4_quant` and the CUTLASS NVFP4 MoE (`run_cutlass_moe_fp4`), whose outputs on
+`naive_kda_lowerbound_gate`), `causal_conv1d_fn`, `scaled_fp4_quant` and the CUTLASS NVFP4 MoE (`run_cutlass_moe_fp4`), whose outputs on
 seeded inputs are
 committed under tests/golden/ (made by tests/golden/make_vllm_golden.py; the inputs are regenerated here from the
 same seeds). Tolerances are stated per assert, each with the margin over the measured difference."""
@@ -172,3 +172,18 @@ def test_kda_gate_and_recurrence_match_fla_naive_reference():
     assert rel(out, f["o"]) < 1e-5
     for n, (_, _, blk, _) in enumerate(gen.KDA_SEQS):
         assert rel(state[blk], f["state"][n]) < 1e-5, n
+
+
+def test_kda_conv_matches_vllm_causal_conv1d():
+    f = np.load(GOLDEN / "conv_vllm.npz")
+    i = gen.conv_inputs()
+    # the window, the conv-state read for a continuing sequence, zeros for a fresh one, the write-back of the last three
+    # rows: with vLLM's rounding of each product to bf16 restated, identical bytes and states
+    q, k, v, st = kda.conv(i["x"], i["w"], i["state"], gen.KDA_SEQS, i["P"], bf16_products=True)
+    np.testing.assert_array_equal(np.concatenate([q, k, v], axis=1), f["out"])
+    for n, (_, _, blk, _) in enumerate(gen.KDA_SEQS):
+        np.testing.assert_array_equal(st[blk], f["state"][n])
+    # exact fp32 products (Dao's channel-last arithmetic, which the reference's conv reproduces bitwise): measured
+    # 0.031 absolute on outputs up to 4.1
+    q, k, v, _ = kda.conv(i["x"], i["w"], i["state"], gen.KDA_SEQS, i["P"])
+    assert np.abs(np.concatenate([q, k, v], axis=1) - f["out"]).max() <= 0.02 * np.abs(f["out"]).max()
