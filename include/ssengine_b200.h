@@ -266,7 +266,9 @@ int ssb_rmsnorm_cols(const void* x, int64_t ldx, int32_t width, int64_t rows, co
                      int64_t ldy, void* stream);
 
 /* In place: rotary embedding of the 64-dim slice at x + r * ldx + h * head_stride for each row r and head h < heads
- * (pairs (i, i + 32), angle positions[r] * theta^(-i / 32)): the rope parts of the MLA query and key. */
+ * (interleaved pairs (2i, 2i + 1), angle positions[r] * theta^(-i / 32), as DeepSeek-V3.2-style MLA applies it --
+ * vLLM's GlmMoeDsa / DeepseekV2 attention, is_neox_style=False): the rope parts of the MLA query and key. x + r * ldx
+ * + h * head_stride must be 4-byte aligned. */
 int ssb_rope(void* x, int64_t ldx, int32_t heads, int64_t head_stride, const int64_t* positions, int64_t rows,
              float theta, void* stream);
 

@@ -3,8 +3,10 @@
 The block follows the reference's op order for a DSA layer (ssengine/kernels.py configs 12-27: fused q/kv
 down-projection, q / kv latent RMSNorm, q_b, q absorb bmm, MLA cache append, indexer projections, kpool insert, logits,
 top-k, expansion, sparse MLA, v_up bmm, o_proj); the per-op arithmetic is restated from the published DeepSeek-V3.2 /
-MLA definitions (parity unpinned: the fork and its kernels are absent). Rotary embedding: rotate-half pairs (i, i + 32)
-of each 64-dim rope slice, angle pos * theta^(-i / 32).
+MLA definitions (parity unpinned: the fork and its kernels are absent). Rotary embedding: interleaved pairs
+(2i, 2i + 1) of each 64-dim rope slice, angle pos * theta^(-i / 32) -- the MLA rope as upstream vLLM 0.22.0 builds
+GLM-5's DSA layers (vllm/model_executor/models/deepseek_v2.py: `GlmMoeDsaForCausalLM` is the DeepSeek-V2/V3.2 model,
+whose MLA rotary embedding has is_neox_style=False).
 """
 
 from __future__ import annotations
@@ -28,8 +30,11 @@ def rope(x, positions, theta):
     if x.ndim == 3:
         ang = ang[:, None, :]
     c, s = np.cos(ang), np.sin(ang)
-    a, b = x[..., :32], x[..., 32:]
-    return np.concatenate([a * c - b * s, b * c + a * s], axis=-1)
+    a, b = x[..., 0::2], x[..., 1::2]
+    out = np.empty_like(x)
+    out[..., 0::2] = a * c - b * s
+    out[..., 1::2] = b * c + a * s
+    return out
 
 
 def grouped_linear(x_heads, codes, sf, gs_w, gs_in):

@@ -35,8 +35,9 @@ __global__ void rmsnorm_cols_kernel(const __nv_bfloat16* __restrict__ x, int64_t
     y[r * ldy + c] = __float2bfloat16(__bfloat162float(xr[c]) * inv * __bfloat162float(g[c]));
 }
 
-// In-place rotary embedding (rotate-half pairing) of a 64-dim slice per head: for i < 32, with
-// angle = pos * theta^(-i / 32): (a, b) = (x[i], x[i + 32]) -> (a cos - b sin, b cos + a sin).
+// In-place rotary embedding of a 64-dim slice per head with interleaved pairs (the MLA rope of DeepSeek-V3.2-style
+// DSA layers, GPT-J pairing): for i < 32, with angle = pos * theta^(-i / 32):
+// (a, b) = (x[2i], x[2i + 1]) -> (a cos - b sin, b cos + a sin).
 __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, int64_t ldx, int heads, int64_t head_stride,
                             const int64_t* __restrict__ positions, int64_t rows, float theta) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -50,9 +51,9 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, int64_t ldx, int head
   const float ang = static_cast<float>(positions[r]) * inv_freq;
   float sn, cs;
   sincosf(ang, &sn, &cs);
-  const float a = __bfloat162float(p[d]), b = __bfloat162float(p[d + 32]);
-  p[d] = __float2bfloat16(a * cs - b * sn);
-  p[d + 32] = __float2bfloat16(b * cs + a * sn);
+  const __nv_bfloat162 ab = *reinterpret_cast<const __nv_bfloat162*>(p + 2 * d);
+  const float a = __low2float(ab), b = __high2float(ab);
+  *reinterpret_cast<__nv_bfloat162*>(p + 2 * d) = __floats2bfloat162_rn(a * cs - b * sn, b * cs + a * sn);
 }
 
 // dst[h, r, :dim] = src[r, h * src_head_stride + :dim] (to_heads) or dst[r, h * dst_head_stride + :dim] =
@@ -111,6 +112,8 @@ int launch_rmsnorm_cols(const void* x, int64_t ldx, int width, int64_t rows, con
 int launch_rope(void* x, int64_t ldx, int heads, int64_t head_stride, const int64_t* positions, int64_t rows,
                 float theta, cudaStream_t stream) {
   if (x == nullptr || positions == nullptr || heads <= 0 || rows < 0 || theta <= 0.0f) return kErrArgs;
+  // each lane moves one bf16 pair with a 4-byte access: every slice must start on an even element
+  if ((reinterpret_cast<uintptr_t>(x) & 3u) != 0 || (ldx & 1) != 0 || (head_stride & 1) != 0) return kErrArgs;
   if (rows == 0) return kOk;
   const int64_t n = rows * heads * 32;
   rope_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(static_cast<__nv_bfloat16*>(x), ldx, heads, head_stride,
