@@ -3,7 +3,10 @@
  * Conventions (the style of the reference's only native ABI, ssengine/native/kda_split_heads.cpp:17-19: plain
  * pointers and sizes, an int return code, out-parameters):
  * - every pointer argument named *_codes, *_sf, x, out, ws, logits, ids, weights, status is DEVICE memory owned by
- *   the caller; the library never allocates device memory;
+ *   the caller. Entry points that need scratch take it from the caller (`ws`, `workspace`), except three forms that
+ *   allocate: ssb_kda_prefill and ssb_mhc (one stream-ordered cudaMallocAsync + cudaFreeAsync per call; their `_ws`
+ *   forms take a caller workspace and allocate nothing) and ssb_ipc_open (maps a peer's buffer). No other entry point
+ *   allocates device memory;
  * - `stream` is a cudaStream_t passed as void*; every entry point only enqueues work on it (no host sync);
  * - return 0 on success, else an ssb status code (1 bad arguments, 2 CUDA launch error, 3 workspace too small,
  *   5 driver entry point missing, 7 size beyond ssb_moe_route_permute_noalloc's limits); device-side failures (4 a bounded wait expired, 6 a table overflowed) are written
@@ -278,6 +281,13 @@ int ssb_rope(void* x, int64_t ldx, int32_t heads, int64_t head_stride, const int
 int ssb_transpose_heads(const void* src, void* dst, int64_t rows, int64_t rows_pad, int32_t heads, int32_t dim,
                         int64_t row_ld, int64_t head_stride, int32_t to_heads, void* stream);
 
+/* Tile table of ssb_nvfp4_gemm_grouped for per-head GEMMs over head-major rows padded to rows_pad (% 128 == 0):
+ * tiles int32 [heads * rows_pad / 128][4] = {head, head * rows_pad + 128 * m, 128, 0} and *num_tiles, written on the
+ * device (tile_cap entries available; tiles 16-byte aligned), so a microbatch's table costs no host work or copy.
+ * Replaces the batch strides the reference's torch.bmm takes (ssengine/kernels.py configs 22 and 26). */
+int ssb_head_tiles(int32_t heads, int64_t rows_pad, int32_t* tiles, int64_t tile_cap, int32_t* num_tiles,
+                   void* stream);
+
 /* out[r] = [a[r, :wa], b[r, :wb]] (bf16; widths and pitches % 8 == 0): the latent-cache rows (latent | rope key). */
 int ssb_concat_cols(const void* a, int64_t lda, int32_t wa, const void* b, int64_t ldb, int32_t wb, void* out,
                     int64_t ldo, int64_t rows, void* stream);
@@ -379,7 +389,8 @@ int ssb_p2p_copy(void* dst, const void* src, int64_t bytes, void* stream);
  * (token, slot)), counts int32 [E+1], offsets int32 [E+2]. Its scratch is one static device array of about 1.25 MiB
  * that every GPU loading the library holds until exit; limits T <= 16384, E <= 512, k <= 31, beyond which it returns
  * 7 before any launch. Calls share that array: calls whose work overlaps on the GPU race. The first call on a device
- * looks up the array's address and should come before any stream capture.
+ * looks up the array's address and should come before any stream capture. `status` may be null. With T == 0 it
+ * writes zero counts and offsets and nothing else.
  * No counterpart in the reference. */
 int ssb_moe_route_permute_noalloc(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* ids, float* weights,
                                   int32_t* rows, int32_t* counts, int32_t* offsets, int32_t* status, void* stream);

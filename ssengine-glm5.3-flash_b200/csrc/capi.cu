@@ -162,6 +162,11 @@ int ssb_concat_cols(const void* a, int64_t lda, int32_t wa, const void* b, int64
   return ssb::launch_concat_cols(a, lda, wa, b, ldb, wb, out, ldo, rows, static_cast<cudaStream_t>(stream));
 }
 
+int ssb_head_tiles(int32_t heads, int64_t rows_pad, int32_t* tiles, int64_t tile_cap, int32_t* num_tiles,
+                   void* stream) {
+  return ssb::launch_head_tiles(heads, rows_pad, tiles, tile_cap, num_tiles, static_cast<cudaStream_t>(stream));
+}
+
 int ssb_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* ids, float* weights, void* stream) {
   if (logits == nullptr || ids == nullptr || weights == nullptr || T < 0) return kErrArgs;
   return ssb::launch_moe_route(logits, T, E, k, ids, weights, static_cast<cudaStream_t>(stream));

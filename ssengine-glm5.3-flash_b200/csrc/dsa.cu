@@ -92,6 +92,21 @@ __global__ void concat_cols_kernel(const __nv_bfloat16* __restrict__ a, int64_t 
   reinterpret_cast<uint4*>(out + r * ldo)[c] = v;
 }
 
+// Tile table of a per-head grouped GEMM over head-major rows padded to rows_pad: tile i = {head, first row, 128, 0}
+// with head = i / (rows_pad / 128); *num = heads * rows_pad / 128.
+__global__ void head_tiles_kernel(int heads, int64_t rows_pad, int32_t* __restrict__ tiles, int32_t* __restrict__ num) {
+  const int64_t per = rows_pad / 128;
+  const int64_t n = per * heads;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t h = i / per;
+    const int64_t m = i - h * per;
+    reinterpret_cast<int4*>(tiles)[i] =
+        make_int4(static_cast<int>(h), static_cast<int>(h * rows_pad + 128 * m), 128, 0);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *num = static_cast<int32_t>(n);
+}
+
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 unsigned blocks_for(int64_t n, int t) { return static_cast<unsigned>((n + t - 1) / t); }
@@ -131,6 +146,16 @@ int launch_transpose_heads(const void* src, void* dst, int64_t rows, int64_t row
   transpose_heads_kernel<<<blocks_for(total, 256), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(src), static_cast<__nv_bfloat16*>(dst), rows, rows_pad, heads, dim / 8, row_ld,
       head_stride, to_heads ? 1 : 0);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int launch_head_tiles(int heads, int64_t rows_pad, int32_t* tiles, int64_t tile_cap, int32_t* num,
+                      cudaStream_t stream) {
+  if (tiles == nullptr || num == nullptr || heads <= 0 || rows_pad < 0 || rows_pad % 128 != 0 || !al16(tiles))
+    return kErrArgs;
+  const int64_t n = rows_pad / 128 * heads;
+  if (n > tile_cap || rows_pad * heads >= (int64_t(1) << 31)) return kErrArgs;
+  head_tiles_kernel<<<static_cast<unsigned>(n / 256 + 1), 256, 0, stream>>>(heads, rows_pad, tiles, num);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

@@ -14,7 +14,8 @@
 // table and its count), so nothing needs clearing; but calls whose work overlaps on the GPU (two streams, or two
 // threads on one device without ordering) race on the array. The first call on a device looks up the array's
 // device address (cudaGetSymbolAddress, with that device current) and caches it; make that first call before any
-// stream capture.
+// stream capture. `status` may be null (the offsets step then drops its table-overflow report). With T == 0 the call
+// still writes `counts` (all zero) and `offsets` (all zero).
 
 #include <mutex>
 
@@ -92,7 +93,6 @@ extern "C" int ssb_moe_route_permute_noalloc(const float* logits, int64_t T, int
   void* base = nullptr;
   int rc = scratch_address(&base);
   if (rc != ssb::kOk) return rc;
-  if (T == 0) return ssb::kOk;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   uint8_t* s = static_cast<uint8_t*>(base);
   uint32_t* masks = reinterpret_cast<uint32_t*>(s + kOffMasks);
@@ -100,12 +100,16 @@ extern "C" int ssb_moe_route_permute_noalloc(const float* logits, int64_t T, int
   int32_t* tiles = reinterpret_cast<int32_t*>(s + kOffTiles);
   int32_t* num_tiles = reinterpret_cast<int32_t*>(s + kOffNumTiles);
   const int32_t cap = static_cast<int32_t>((T * (k + 1) + (static_cast<int64_t>(E) + 1) * 127 + 127) / 128);
-  rc = ssb::launch_moe_route(logits, T, E, k, ids, weights, stream);
-  if (rc != ssb::kOk) return rc;
-  rc = ssb::launch_moe_count(ids, T, E, k, masks, block_counts, stream);
-  if (rc != ssb::kOk) return rc;
+  // with no tokens only the offsets step runs: it writes zero counts and offsets (no block reads)
+  if (T > 0) {
+    rc = ssb::launch_moe_route(logits, T, E, k, ids, weights, stream);
+    if (rc != ssb::kOk) return rc;
+    rc = ssb::launch_moe_count(ids, T, E, k, masks, block_counts, stream);
+    if (rc != ssb::kOk) return rc;
+  }
   rc = ssb::launch_moe_offsets(T, E, block_counts, counts, offsets, tiles, num_tiles, cap, nullptr, 0, status, stream);
   if (rc != ssb::kOk) return rc;
+  if (T == 0) return ssb::kOk;
   const int64_t n = T * k;
   const int threads = 256;
   int64_t blocks = (n + threads - 1) / threads;

@@ -209,6 +209,8 @@ int launch_rope(void* x, int64_t ldx, int heads, int64_t head_stride, const int6
                 float theta, cudaStream_t stream);
 int launch_transpose_heads(const void* src, void* dst, int64_t rows, int64_t rows_pad, int heads, int dim,
                            int64_t row_ld, int64_t head_stride, bool to_heads, cudaStream_t stream);
+int launch_head_tiles(int heads, int64_t rows_pad, int32_t* tiles, int64_t tile_cap, int32_t* num,
+                      cudaStream_t stream);
 int launch_concat_cols(const void* a, int64_t lda, int wa, const void* b, int64_t ldb, int wb, void* out, int64_t ldo,
                        int64_t rows, cudaStream_t stream);
 

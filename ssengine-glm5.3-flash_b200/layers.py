@@ -234,19 +234,24 @@ class Nvfp4Grouped:
         self.alpha = torch.full((heads,), 1.0 / (gs_in * self.gs_w), dtype=torch.float32, device=dev)
         self.device = dev
         self._lib = lib.load()
-        self._tiles = {}
+        self._tiles = None                  # int32 [cap, 4] tile table + [1] count, rebuilt on the device per call
 
     def logical(self):
         codes = layout.unpack_codes(self.codes).view(self.heads, self.N, self.K)
         sf = layout.atoms_to_sf(self.sf, self.heads * self.N, self.K).view(self.heads, self.N, self.K // 16)
         return codes, sf, self.gs_w
 
-    def _tile_table(self, rows_pad: int):
-        if rows_pad not in self._tiles:
-            t = [(h, h * rows_pad + 128 * m, 128, 0) for h in range(self.heads) for m in range(rows_pad // 128)]
-            tiles = torch.tensor(t, dtype=torch.int32).to(self.device)
-            self._tiles[rows_pad] = (tiles, torch.tensor([len(t)], dtype=torch.int32).to(self.device))
-        return self._tiles[rows_pad]
+    def _tile_table(self, rows_pad: int, stream=None):
+        """The grouped GEMM's tile table for `rows_pad` rows a head, written on the device (`ssb_head_tiles`, no host
+        copy); the buffer grows only when a larger microbatch arrives."""
+        n = self.heads * rows_pad // 128
+        if self._tiles is None or self._tiles[0].shape[0] < n:
+            self._tiles = (torch.empty(max(n, 1), 4, dtype=torch.int32, device=self.device),
+                           torch.empty(1, dtype=torch.int32, device=self.device))
+        tiles, num = self._tiles
+        lib.check("ssb_head_tiles", self._lib.ssb_head_tiles(self.heads, rows_pad, tiles.data_ptr(), tiles.shape[0],
+                                                             num.data_ptr(), lib.stream_ptr(stream)))
+        return tiles, num, n
 
     def __call__(self, x_heads: torch.Tensor, rows_pad: int, out: torch.Tensor, status: torch.Tensor, stream=None):
         """x_heads bf16 [heads * rows_pad, K] (head-major) -> out bf16 [heads * rows_pad, N]."""
@@ -257,10 +262,10 @@ class Nvfp4Grouped:
         lib.check("ssb_nvfp4_quantize", self._lib.ssb_nvfp4_quantize(x_heads.data_ptr(), rows, self.K, self.K,
                                                                      self.gs_in, codes.data_ptr(), self.K // 2,
                                                                      sf.data_ptr(), s))
-        tiles, n = self._tile_table(rows_pad)
+        tiles, num, n = self._tile_table(rows_pad, stream)
         lib.check("ssb_nvfp4_gemm_grouped", self._lib.ssb_nvfp4_gemm_grouped(
             lib.EPI_BF16, codes.data_ptr(), sf.data_ptr(), rows, self.K, self.codes.data_ptr(), self.sf.data_ptr(),
-            self.N, self.heads, self.alpha.data_ptr(), tiles.data_ptr(), n.data_ptr(), tiles.shape[0], out.data_ptr(),
+            self.N, self.heads, self.alpha.data_ptr(), tiles.data_ptr(), num.data_ptr(), n, out.data_ptr(),
             self.N, status.data_ptr(), s))
         return out
 

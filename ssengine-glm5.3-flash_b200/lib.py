@@ -22,7 +22,8 @@ EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_g
            "ssb_ipc_export", "ssb_ipc_open", "ssb_ipc_close", "ssb_flag_wait", "ssb_flag_write", "ssb_p2p_copy",
            "ssb_indexer_logits", "ssb_indexer_expand", "ssb_sparse_mla", "ssb_mla_cache_append", "ssb_mla_q_pack",
            "ssb_kpool_insert", "ssb_gated_rmsnorm", "ssb_gated_rmsnorm_nvfp4", "ssb_hc_expand", "ssb_hc_mean",
-           "ssb_nvfp4_gemm_grouped", "ssb_rmsnorm_cols", "ssb_rope", "ssb_transpose_heads", "ssb_concat_cols")
+           "ssb_nvfp4_gemm_grouped", "ssb_rmsnorm_cols", "ssb_rope", "ssb_transpose_heads", "ssb_concat_cols",
+           "ssb_head_tiles")
 
 EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
 
@@ -118,6 +119,7 @@ _SIGS = {
     "ssb_rope": ([_P, _I64, _I32, _I64, _P, _I64, _F, _P], ctypes.c_int),
     "ssb_transpose_heads": ([_P, _P, _I64, _I64, _I32, _I32, _I64, _I64, _I32, _P], ctypes.c_int),
     "ssb_concat_cols": ([_P, _I64, _I32, _P, _I64, _I32, _P, _I64, _I64, _P], ctypes.c_int),
+    "ssb_head_tiles": ([_I32, _I64, _P, _I64, _P, _P], ctypes.c_int),
 }
 
 MOE_KERNELS = 10      # kernels ssb_moe_forward launches (+ a memset when F % 256 != 0)
