@@ -83,9 +83,10 @@ def l2norm(x):
     return x / np.sqrt((x * x).sum(axis=-1, keepdims=True) + L2_EPS)
 
 
-def recurrent(q, k, v, g, beta, a_log, dt_bias, lower_bound, scale, rec_state, seqs, H, D):
+def recurrent(q, k, v, g, beta, a_log, dt_bias, lower_bound, scale, rec_state, seqs, H, D, heads=None):
     """Token-by-token KDA over each sequence. q, k, v [T, H*D] (conv outputs), g [T, H*D] raw gate, beta [T, H] raw;
-    rec_state [blocks, H, D(value), D(key)] (copied) -> (out [T, H*D] float64, new rec_state float32)."""
+    rec_state [blocks, H, D(value), D(key)] (copied) -> (out [T, H*D] float64, new rec_state float32). `heads`: only
+    these heads are computed (the others' outputs stay 0 and their states as given), for large cases."""
     T = q.shape[0]
     qn = l2norm(np.asarray(q, np.float64).reshape(T, H, D))
     kn = l2norm(np.asarray(k, np.float64).reshape(T, H, D))
@@ -95,7 +96,7 @@ def recurrent(q, k, v, g, beta, a_log, dt_bias, lower_bound, scale, rec_state, s
     st = np.array(rec_state, dtype=np.float32, copy=True)
     out = np.zeros((T, H, D), np.float64)
     for s, e, blk, init in seqs:
-        for h in range(H):
+        for h in (range(H) if heads is None else heads):
             S = st[blk, h].astype(np.float64).T.copy() if init else np.zeros((D, D))   # [key, value]
             for t in range(s, e):
                 S *= gk[t, h][:, None]

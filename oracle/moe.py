@@ -51,6 +51,46 @@ def route_softmax_topk(logits, k: int) -> tuple[np.ndarray, np.ndarray]:
     return order, w
 
 
+def route_sigmoid_bias(logits, k: int, bias, n_group: int = 1, topk_group: int = 1, scale: float = 1.0):
+    """The reference model's routing (ssengine/kernels.py:182-187 "DeepSeek-V3 routing, scale 5/2"; its CPU test
+    selects (logits.sigmoid() + bias).topk(8), tests/test_moe_tuning_cpu.py:63), restated from the published
+    DeepSeek-V3 rule: score = sigmoid(logit) (evaluated in float64, rounded to fp32 once), choice = score + bias (fp32);
+    with n_group > 1, a group's rank is the sum of its two largest choices and only the topk_group best groups stay
+    eligible (ties: lower group); ids = the k largest eligible choices (ties: lower expert), slots in rank order;
+    weights = the selected unbiased scores / their sum (fp32, summed in rank order) * scale.
+    logits fp32 [T, E], bias fp32 [E] -> (ids int32 [T, k], weights fp32 [T, k])."""
+    logits = np.asarray(logits, dtype=np.float32)
+    T, E = logits.shape
+    score = (1.0 / (1.0 + np.exp(-logits.astype(np.float64)))).astype(np.float32)
+    score = np.where(np.isnan(logits), np.float32(0), score)
+    choice = (score + np.asarray(bias, np.float32)[None, :]).astype(np.float32)
+    choice = np.where(np.isnan(logits), np.float32(-np.inf), choice)
+    if n_group > 1:
+        gs = E // n_group
+        grp = np.sort(choice.reshape(T, n_group, gs), axis=2)
+        gscore = (grp[:, :, -1] + grp[:, :, -2]).astype(np.float32)
+        keep = np.argsort(-gscore, axis=1, kind="stable")[:, :topk_group]
+        mask = np.zeros((T, n_group), bool)
+        np.put_along_axis(mask, keep, True, axis=1)
+        choice = np.where(np.repeat(mask, gs, axis=1), choice, np.float32(-np.inf))
+    ids = np.argsort(-choice, axis=1, kind="stable")[:, :k].astype(np.int32)
+    sel = np.take_along_axis(score, ids, axis=1)
+    tot = np.zeros(T, np.float32)
+    for j in range(k):
+        tot = (tot + sel[:, j]).astype(np.float32)
+    w = ((sel / tot[:, None]).astype(np.float32) * np.float32(scale)).astype(np.float32)
+    return ids, w
+
+
+def route(logits, k: int, p: dict):
+    """The layer's routing rule: p["route"] = {"bias", "n_group", "topk_group", "scale"} selects the sigmoid rule,
+    otherwise softmax top-k."""
+    r = p.get("route")
+    if r is None:
+        return route_softmax_topk(logits, k)
+    return route_sigmoid_bias(logits, k, r["bias"], r["n_group"], r["topk_group"], r["scale"])
+
+
 def permutation(ids, num_experts: int, shared: bool = True):
     """Expert-major permutation. ids int32 [T, k] (experts 0..E-1). Returns
     (counts int32 [E(+1)], offsets int64 [E(+1) + 1] padded to 128-row tiles, rows int64 [T, k], shared_rows int64 [T]
@@ -118,20 +158,26 @@ def moe_forward(x, p: dict, k: int, ids=None, weights=None, return_parts: bool =
     p["gs_x"], p["gs_h"], p["router"] = (codes [E, H], sf [E, H/16], gs), p["experts"] = list of E + 1 tuples
     (w1 codes [2F, H], w1 sf, w1 gs, w2 codes [H, F], w2 sf, w2 gs), the shared expert last.
     `ids` / `weights` override the routing (to check the FFN path on the CUDA path's own routing); `dense` is
-    `dequantize_params(p)` when the caller holds it already. `intermediates` "bf16" restates vLLM's CUTLASS NVFP4 MoE
-    (bf16 gate_up output, bf16 SwiGLU product, bf16 expert rows, weights and products in the combine, a bf16 sum) to
-    cross-check the algorithm against it; the layer's own rule keeps all of them in fp32."""
+    `dequantize_params(p)` when the caller holds it already, or "lazy" to dequantize one expert at a time.
+    `intermediates` "bf16" restates vLLM's CUTLASS NVFP4 MoE (bf16 gate_up output, bf16 SwiGLU product, bf16 expert
+    rows, weights and products in the combine, a bf16 sum) to cross-check the algorithm against it; the layer's own
+    rule keeps all of them in fp32."""
     x = np.asarray(x, dtype=np.float32)
     T, H = x.shape
     E = len(p["experts"]) - 1
     F = p["experts"][0][0].shape[0] // 2
     xq, xs = nvfp4.quantize(x, p["gs_x"])
     xd = nvfp4.dequantize(xq, xs, p["gs_x"])
-    if dense is None:
+    lazy = isinstance(dense, str) and dense == "lazy"
+    if lazy:
+        # one expert's fp32 weights at a time (full-size layers on a row sample: 129 experts of 12.6M elements would
+        # take 6.5 GB at once)
+        dense = {"router": nvfp4.dequantize(*p["router"]), "experts": None}
+    elif dense is None:
         dense = dequantize_params(p)
     logits = (xd @ dense["router"].T).astype(np.float32)
     if ids is None:
-        ids, weights = route_softmax_topk(logits, k)
+        ids, weights = route(logits, k, p)
     ids = np.asarray(ids, dtype=np.int64)
     weights = np.asarray(weights, dtype=np.float32)
     out = np.zeros((T, H), dtype=np.float32)
@@ -146,7 +192,11 @@ def moe_forward(x, p: dict, k: int, ids=None, weights=None, return_parts: bool =
             tok = np.arange(T)
         if tok.size == 0:
             continue
-        w1d, w2d = dense["experts"][e]
+        if lazy:
+            c1, s1, g1, c2, s2, g2 = p["experts"][e]
+            w1d, w2d = nvfp4.dequantize(c1, s1, g1), nvfp4.dequantize(c2, s2, g2)
+        else:
+            w1d, w2d = dense["experts"][e]
         y = expert_ffn(xd[tok], w1d, w2d, p["gs_h"], F, intermediates)
         if e < E:
             y_routed[tok, slot] = y
