@@ -312,7 +312,16 @@ typedef struct ssb_moe_layer {
   const uint8_t* w2_sf;        /* atoms of [(E+1) * H, F] */
   const float* w2_alpha;       /* [E+1]: 1 / (gs_h * gs_w2[e]) */
   int32_t add_input;           /* nonzero: out = x + MoE(x) (the residual add fused into the combine) */
+  int32_t routing;             /* SSB_ROUTE_SOFTMAX or SSB_ROUTE_SIGMOID_BIAS */
+  int32_t n_group;             /* sigmoid routing: expert groups (1 = no grouping) */
+  int32_t topk_group;          /* sigmoid routing: groups kept */
+  float routed_scale;          /* sigmoid routing: routed scaling factor applied to the normalized weights */
+  const float* route_bias;     /* sigmoid routing: [E] fp32 correction bias */
 } ssb_moe_layer;
+
+/* Routing rules of ssb_moe_layer.routing. */
+#define SSB_ROUTE_SOFTMAX 0       /* BASELINE configs: softmax over the k largest logits */
+#define SSB_ROUTE_SIGMOID_BIAS 1  /* the reference model's rule (DeepSeek-V3 style), see ssb_moe_route_sigmoid */
 
 /* Workspace of ssb_moe_forward for T tokens, in bytes (one caller-owned device buffer, 256-byte aligned). */
 int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T);
@@ -340,6 +349,17 @@ int64_t ssb_moe_workspace_bytes(const ssb_moe_layer* layer, int64_t T);
 #define SSB_WS_ROW_SRC 17    /* int32 [cap*128] source token of each permuted row (padding rows unwritten) */
 #define SSB_WS_END 18
 int ssb_moe_workspace_offsets(const ssb_moe_layer* layer, int64_t T, int64_t* offsets, int32_t n);
+
+/* Sigmoid + correction-bias grouped routing (the reference model's rule: "DeepSeek-V3 routing, scale 5/2",
+ * ssengine/kernels.py:182-187, checked by its CPU test as (logits.sigmoid() + bias).topk(8),
+ * tests/test_moe_tuning_cpu.py:63 of the reference): score = sigmoid(logit) (double, rounded to fp32 once),
+ * choice = score + bias[e]; with n_group > 1 only the topk_group groups with the largest sums of their two best
+ * choices stay eligible (ties: lower group); ids = the k largest eligible choices (ties: lower expert), in rank order;
+ * weights = score[id] / sum of the k scores (rank order) * scale. logits fp32 [T, E], bias fp32 [E]; E <= 512,
+ * k <= 32, n_group <= 32 dividing E. Replaces the routing inside FlashInfer `trtllm_fp4_block_scale_moe`
+ * (routing_method DeepSeekV3, ssengine/kernels.py config 30). */
+int ssb_moe_route_sigmoid(const float* logits, int64_t T, int32_t E, int32_t k, const float* bias, int32_t n_group,
+                          int32_t topk_group, float scale, int32_t* ids, float* weights, void* stream);
 
 /* Whole MoE layer on `stream`: quantize x -> router GEMM -> top-k routing -> permutation + gather -> grouped NVFP4
  * gate_up GEMM with SwiGLU + NVFP4 requant epilogue -> grouped down GEMM -> weighted combine (+ shared expert).

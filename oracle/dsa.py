@@ -48,4 +48,10 @@ def grouped_linear(x_heads, codes, sf, gs_w, gs_in):
     return np.stack(out)
 
 
-__all__ = ["rmsnorm", "rope", "grouped_linear", "bf16"]
+def grouped_linear_bf16(x_heads, w):
+    """x_heads [heads, T, K] bf16 values, w [heads, N, K] bf16 values -> [heads, T, N] float64 (the BF16 batched
+    GEMM of the MLA absorb / v_up)."""
+    return np.einsum("htk,hnk->htn", np.asarray(x_heads, np.float64), np.asarray(w, np.float64))
+
+
+__all__ = ["rmsnorm", "rope", "grouped_linear", "grouped_linear_bf16", "bf16"]

@@ -31,7 +31,7 @@ def logits(q, w, k_cache, pages, positions):
     out = []
     for i in range(q.shape[0]):
         n = (int(positions[i]) + 1) // POOL
-        k = np.asarray(k_cache, np.float64)[pool_rows(pages, n)]                 # [n, 128]
+        k = np.asarray(k_cache)[pool_rows(pages, n)].astype(np.float64)        # [n, 128]
         s = np.asarray(q[i], np.float64) @ k.T                                    # [32, n]
         out.append((np.maximum(s, 0.0) * np.asarray(w[i], np.float64)[:, None]).sum(axis=0))
     return out

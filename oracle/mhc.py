@@ -29,11 +29,11 @@ HC = 4
 
 
 def bf16(x) -> np.ndarray:
-    """Round fp32 to bf16 (nearest even) and back to fp32."""
-    x = np.asarray(x, dtype=np.float32)
-    u = x.view(np.uint32).astype(np.uint64)
-    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
-    return r.astype(np.uint32).view(np.float32)
+    """Round fp32 to bf16 (nearest even) and back to fp32 (32-bit integer arithmetic; only NaN bit patterns wrap)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32)
+    r = (u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)
+    return r.view(np.float32)
 
 
 def sigmoid(v):

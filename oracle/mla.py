@@ -26,7 +26,26 @@ E4M3_MAX = 448.0
 
 
 def e4m3_encode(x) -> np.ndarray:
-    """float values -> e4m3 bytes (round to nearest even, saturating)."""
+    """fp32 values -> e4m3 bytes (round to nearest even, saturating to +-448, the sign of zero kept), by integer
+    arithmetic on the fp32 bits: normals (|x| >= 2^-6) round their 23-bit mantissa to 3 bits, smaller values are
+    multiples of 2^-9 (rint of |x| * 512; 8 of them is the smallest normal, code 0x08). Same bytes as
+    `e4m3_encode_reference` below (tested) at a fraction of its cost."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32)
+    sign = ((u >> np.uint32(31)).astype(np.uint8) << np.uint8(7))
+    a = u & np.uint32(0x7FFFFFFF)
+    r = (a + np.uint32(0x7FFFF) + ((a >> np.uint32(20)) & np.uint32(1))) & np.uint32(0xFFF00000)
+    e4 = (r >> np.uint32(23)).astype(np.int32) - 120                  # biased e4m3 exponent (127 - 7)
+    normal = ((e4 << 3) | ((r >> np.uint32(20)) & np.uint32(7)).astype(np.int32)).clip(0, 0x7E).astype(np.uint8)
+    sub = np.rint(np.abs(x) * np.float32(512.0)).astype(np.uint8)     # 0..8
+    code = np.where(a >= np.uint32(0x3C800000), normal, sub)           # 2^-6
+    code = np.where(a >= np.uint32(0x43E00000), np.uint8(0x7E), code)  # >= 448: saturate
+    return (code | sign).astype(np.uint8)
+
+
+def e4m3_encode_reference(x) -> np.ndarray:
+    """float values -> e4m3 bytes (round to nearest even, saturating) in float64 arithmetic: the slow restatement the
+    fast encoder is checked against."""
     x = np.asarray(x, np.float64)
     sign = np.signbit(x).astype(np.uint8) << 7
     a = np.minimum(np.abs(x), E4M3_MAX)
@@ -59,12 +78,56 @@ def slot_of(pages, pos):
     return np.asarray(pages, np.int64)[pos // 128] * 128 + pos % 128
 
 
-def sparse_mla(q8, kv8, indices, pages, bmm1: float, bmm2: float):
+BLOCK = 128            # index columns per block of the FP8 attention
+LAZY = 3.0             # a block raising a row's (base-2) max by more than this rescales the accumulated output
+P_SCALE = 32.0         # P enters the P.V product as e4m3(32 p)
+
+
+def sparse_mla_fp8p(q, kv8, cols, pages, bmm1: float, bmm2: float) -> np.ndarray:
+    """One query row with its softmax weights rounded to e4m3 where the FP8 attention rounds them (the activation
+    quantization point of the P.V product, as the reference's FP8 sparse MLA kernel has one): the row's index
+    columns in blocks of 128 (blocks without a selected token skipped); base-2 scores x = s * bmm1 * log2(e) (fp32);
+    a running max m kept until a block raises it by more than 2^3 (then the accumulated output and sum are scaled by
+    2^(m_old - m_new)); p = 2^(x - m) (fp32); the sum of p unrounded; the product with e4m3(32 p) / 32.
+    q [64, 576] float64 (the decoded e4m3 query), cols [m] (-1 = none) -> float64 [64, 512]."""
+    H = q.shape[0]
+    o = np.zeros((H, DV))
+    l = np.zeros(H)
+    m = np.full(H, -np.inf, np.float32)
+    sc = np.float32(bmm1 * 1.4426950408889634)
+    pg = np.asarray(pages, np.int64)
+    for b0 in range(0, len(cols), BLOCK):
+        c = np.asarray(cols[b0:b0 + BLOCK], np.int64)
+        c = c[(c >= 0) & (c // 128 < len(pg))]
+        c = c[pg[c // 128] >= 0] if c.size else c
+        if c.size == 0:
+            continue
+        k = e4m3_decode(kv8[slot_of(pg, c)])                               # [mb, 576]
+        x = ((q @ k.T).astype(np.float32) * sc).astype(np.float32)         # [64, mb]
+        mb = x.max(axis=1)
+        fresh = m == -np.inf
+        jump = ~fresh & (mb > m + np.float32(LAZY))
+        alpha = np.where(jump, np.exp2((m - mb).astype(np.float32)), 1.0)
+        o *= alpha[:, None]
+        l *= alpha
+        m = np.where(fresh | jump, mb, m).astype(np.float32)
+        p = np.exp2((x - m[:, None]).astype(np.float32)).astype(np.float32)
+        l += p.astype(np.float64).sum(axis=1)
+        pq = e4m3_decode(e4m3_encode(p * np.float32(P_SCALE)))
+        o += pq @ k[:, :DV]
+    return np.where(l[:, None] > 0, o * (bmm2 / (np.maximum(l, 1e-300)[:, None] * P_SCALE)), 0.0)
+
+
+def sparse_mla(q8, kv8, indices, pages, bmm1: float, bmm2: float, p_fp8: bool = False):
     """q8 [n, 64, 576] e4m3 bytes of one request's rows, kv8 [slots, 576] e4m3 bytes, indices [n, m] positions
-    (-1 = none) -> float64 [n, 64, 512]."""
+    (-1 = none) -> float64 [n, 64, 512]. p_fp8: the softmax weights rounded to e4m3 as the FP8 attention rounds them
+    (`sparse_mla_fp8p`); else the exact softmax."""
     q = e4m3_decode(q8)
-    kv = e4m3_decode(kv8)
     out = np.zeros((q.shape[0], q.shape[1], DV))
+    if p_fp8:
+        for i in range(q.shape[0]):
+            out[i] = sparse_mla_fp8p(q[i], kv8, indices[i], pages, bmm1, bmm2)
+        return out
     for i in range(q.shape[0]):
         sel = np.asarray(indices[i])
         sel = sel[sel >= 0]
@@ -72,7 +135,7 @@ def sparse_mla(q8, kv8, indices, pages, bmm1: float, bmm2: float):
         sel = sel[np.asarray(pages, np.int64)[sel // 128] >= 0]          # a token on a missing page is not read
         if sel.size == 0:
             continue
-        k = kv[slot_of(pages, sel)]                       # [m, 576]
+        k = e4m3_decode(kv8[slot_of(pages, sel)])         # [m, 576] (only the selected rows are decoded)
         s = bmm1 * (q[i] @ k.T)                           # [64, m]
         s -= s.max(axis=1, keepdims=True)
         p = np.exp(s)

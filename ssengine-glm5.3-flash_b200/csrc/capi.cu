@@ -167,6 +167,13 @@ int ssb_head_tiles(int32_t heads, int64_t rows_pad, int32_t* tiles, int64_t tile
   return ssb::launch_head_tiles(heads, rows_pad, tiles, tile_cap, num_tiles, static_cast<cudaStream_t>(stream));
 }
 
+int ssb_moe_route_sigmoid(const float* logits, int64_t T, int32_t E, int32_t k, const float* bias, int32_t n_group,
+                          int32_t topk_group, float scale, int32_t* ids, float* weights, void* stream) {
+  if (logits == nullptr || ids == nullptr || weights == nullptr || T < 0) return kErrArgs;
+  return ssb::launch_moe_route_sigmoid(logits, T, E, k, bias, n_group, topk_group, scale, ids, weights,
+                                       static_cast<cudaStream_t>(stream));
+}
+
 int ssb_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* ids, float* weights, void* stream) {
   if (logits == nullptr || ids == nullptr || weights == nullptr || T < 0) return kErrArgs;
   return ssb::launch_moe_route(logits, T, E, k, ids, weights, static_cast<cudaStream_t>(stream));
@@ -469,7 +476,13 @@ int moe_forward(const ssb_moe_layer* L, const void* x, int64_t T, void* out, voi
   }
   // 3. routing, 4. permutation
   mark(2);
-  rc = ssb::launch_moe_route(logits, T, static_cast<int32_t>(d.E), static_cast<int32_t>(d.k), ids, wts, stream);
+  if (L->routing == SSB_ROUTE_SIGMOID_BIAS)
+    rc = ssb::launch_moe_route_sigmoid(logits, T, static_cast<int32_t>(d.E), static_cast<int32_t>(d.k), L->route_bias,
+                                       L->n_group, L->topk_group, L->routed_scale, ids, wts, stream);
+  else if (L->routing == SSB_ROUTE_SOFTMAX)
+    rc = ssb::launch_moe_route(logits, T, static_cast<int32_t>(d.E), static_cast<int32_t>(d.k), ids, wts, stream);
+  else
+    rc = kErrArgs;
   if (rc != kOk) return rc;
   mark(3);
   rc = ssb::launch_moe_count(ids, T, static_cast<int32_t>(d.E), static_cast<int32_t>(d.k), masks, bcounts, stream);

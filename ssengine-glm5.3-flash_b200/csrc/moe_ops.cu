@@ -115,6 +115,118 @@ __global__ void moe_route_kernel(const float* __restrict__ logits, int64_t T, in
   }
 }
 
+// ---- routing: sigmoid scores + correction bias, grouped top-k (the DeepSeek-V3 rule), one warp per token -----------
+// score[e] = sigmoid(logit[e]) (evaluated in double and rounded to fp32 once, so that the CPU restatement reproduces
+// every bit); choice[e] = score[e] + bias[e] (fp32). With n_group > 1 the experts form n_group equal groups, a group's
+// rank is the sum of its two largest choices, and only the topk_group best groups (ties: lower group) stay eligible.
+// Selection: k rounds of a warp arg-max over the eligible choices with (value desc, expert index asc), slots in that
+// rank order. Weights: the unbiased scores of the selected experts, divided by their sum (summed in rank order) and
+// multiplied by `scale` (the routed scaling factor).
+template <int EPL>
+__global__ void moe_route_sigmoid_kernel(const float* __restrict__ logits, int64_t T, int E, int k,
+                                         const float* __restrict__ bias, int n_group, int topk_group, float scale,
+                                         int32_t* __restrict__ ids, float* __restrict__ weights) {
+  extern __shared__ float choice_sh[];          // [warps][E] (only with n_group > 1)
+  const int lane = threadIdx.x & 31;
+  const int64_t t = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  float sc[EPL], v[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = lane + 32 * j;
+    sc[j] = 0.0f;
+    v[j] = -INFINITY;
+    if (e < E) {
+      const float x = logits[t * E + e];
+      if (x == x) {                              // NaN never outranks a number
+        sc[j] = static_cast<float>(1.0 / (1.0 + exp(-static_cast<double>(x))));
+        v[j] = __fadd_rn(sc[j], bias[e]);
+      }
+    }
+  }
+  if (n_group > 1) {
+    float* ch = choice_sh + (threadIdx.x >> 5) * E;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j)
+      if (lane + 32 * j < E) ch[lane + 32 * j] = v[j];
+    __syncwarp();
+    const int gsize = E / n_group;
+    float gscore = -INFINITY;
+    if (lane < n_group) {
+      float a = -INFINITY, b = -INFINITY;       // the group's two largest choices
+      for (int i = 0; i < gsize; ++i) {
+        const float c = ch[lane * gsize + i];
+        if (c > a) {
+          b = a;
+          a = c;
+        } else if (c > b) {
+          b = c;
+        }
+      }
+      gscore = __fadd_rn(a, b);
+    }
+    uint32_t keep = 0;
+    for (int r = 0; r < topk_group; ++r) {
+      float bv = (keep >> lane) & 1u ? -INFINITY : gscore;
+      int bi = lane < n_group && !((keep >> lane) & 1u) ? lane : 0x7FFFFFFF;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+        const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if (bi < 32) keep |= 1u << bi;
+    }
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && !((keep >> (e / gsize)) & 1u)) v[j] = -INFINITY;
+    }
+  }
+  uint32_t taken = 0;
+  int my_id = -1;
+  float my_w = 0.0f;
+  for (int r = 0; r < k; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7FFFFFFF;
+    float bs = 0.0f;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && !((taken >> j) & 1u) && (v[j] > bv || (v[j] == bv && e < bi))) {
+        bv = v[j];
+        bi = e;
+        bs = sc[j];
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+      const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
+      const float os = __shfl_xor_sync(0xFFFFFFFFu, bs, off);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+        bs = os;
+      }
+    }
+    if (bi < E && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (lane == r) {
+      my_id = bi < E ? bi : -1;
+      my_w = bi < E ? bs : 0.0f;
+    }
+  }
+  float sum = 0.0f;
+  for (int r = 0; r < k; ++r) sum = __fadd_rn(sum, __shfl_sync(0xFFFFFFFFu, my_w, r));
+  if (lane < k) {
+    ids[t * k + lane] = my_id;
+    weights[t * k + lane] = __fmul_rn(__fdiv_rn(my_w, sum), scale);
+  }
+}
+
 // ---- per-block expert masks and counts ------------------------------------------------------------------------------
 __global__ void moe_count_kernel(const int32_t* __restrict__ ids, int64_t T, int E, int k, uint32_t* __restrict__ masks,
                                  int32_t* __restrict__ block_counts) {
@@ -411,6 +523,28 @@ int launch_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32
     moe_route_kernel<8><<<blocks, threads, 0, stream>>>(logits, T, E, k, ids, weights);
   else
     moe_route_kernel<16><<<blocks, threads, 0, stream>>>(logits, T, E, k, ids, weights);
+  return last_error();
+}
+
+int launch_moe_route_sigmoid(const float* logits, int64_t T, int32_t E, int32_t k, const float* bias, int32_t n_group,
+                             int32_t topk_group, float scale, int32_t* ids, float* weights, cudaStream_t stream) {
+  if (E <= 0 || E > 512 || k <= 0 || k > 32 || k > E || bias == nullptr) return kErrArgs;
+  if (n_group < 1 || n_group > 32 || E % n_group != 0 || topk_group < 1 || topk_group > n_group) return kErrArgs;
+  if (n_group > 1 && (E / n_group < 2 || (E / n_group) * topk_group < k)) return kErrArgs;
+  if (T == 0) return kOk;
+  const int threads = 256;
+  const int64_t blocks = (T + 7) / 8;
+  const size_t sm = n_group > 1 ? static_cast<size_t>(threads / 32) * E * 4 : 0;
+  const int epl = (E + 31) / 32;
+  if (epl <= 4)
+    moe_route_sigmoid_kernel<4><<<blocks, threads, sm, stream>>>(logits, T, E, k, bias, n_group, topk_group, scale, ids,
+                                                                 weights);
+  else if (epl <= 8)
+    moe_route_sigmoid_kernel<8><<<blocks, threads, sm, stream>>>(logits, T, E, k, bias, n_group, topk_group, scale, ids,
+                                                                 weights);
+  else
+    moe_route_sigmoid_kernel<16><<<blocks, threads, sm, stream>>>(logits, T, E, k, bias, n_group, topk_group, scale,
+                                                                  ids, weights);
   return last_error();
 }
 

@@ -52,6 +52,8 @@ int launch_nvfp4_quantize(const void* x, int64_t rows, int64_t K, int64_t ldx, f
 
 int launch_moe_route(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* ids, float* weights,
                      cudaStream_t stream);
+int launch_moe_route_sigmoid(const float* logits, int64_t T, int32_t E, int32_t k, const float* bias, int32_t n_group,
+                             int32_t topk_group, float scale, int32_t* ids, float* weights, cudaStream_t stream);
 
 int launch_moe_count(const int32_t* ids, int64_t T, int32_t E, int32_t k, uint32_t* masks, int32_t* block_counts,
                      cudaStream_t stream);

@@ -43,12 +43,12 @@ class Nvfp4Linear:
         self._lib = lib.load()
 
     @classmethod
-    def random(cls, gen: torch.Generator, N: int, K: int, device, gs_in: float = weights.GS_X, in_sq_mean: float = 1.0):
-        """Random-init NVFP4 weights (BASELINE recipe) scaled for unit-variance outputs."""
-        codes = torch.randint(0, 16, (N, K), generator=gen, device=device, dtype=torch.uint8)
-        table = torch.tensor(weights.SCALE_CODES, dtype=torch.uint8, device=device)
-        sf = table[torch.randint(0, len(weights.SCALE_CODES), (N, K // 16), generator=gen, device=device)]
-        return cls(codes, sf, weights.unit_gs(K, in_sq_mean), device, gs_in)
+    def random(cls, gen: torch.Generator, N: int, K: int, device, gs_in: float = weights.GS_X, in_sq_mean: float = 1.0,
+               init: str = "uniform", std: float = 0.02):
+        """Random-init NVFP4 weights: BASELINE's recipe scaled for unit-variance outputs ("uniform"), or N(0, std)
+        values quantized ("normal")."""
+        codes, sf, gs = weights.nvfp4_tensor(gen, N, K, device, init, in_sq_mean, std)
+        return cls(codes, sf, gs, device, gs_in)
 
     def logical(self):
         """(codes [N, K], sf [N, K / 16], gs_w) as stored (for the checker)."""
@@ -83,20 +83,75 @@ class Nvfp4Linear:
         return self.gemm(codes, sf, T, out, status, stream)
 
 
+class DenseFfn:
+    """The dense SwiGLU FFN of the reference model's leading layers (`first_kda_dense`, `kda_dense`: layers 0-2,
+    ssengine/kernels.py:283-289): gate_up k H n 2F and down k F n H, NVFP4 with the activation quantized on the way
+    in (configs 8-11: `scaled_fp4_quant` -> `mm_fp4` gate_up -> `scaled_fp4_quant` -> `mm_fp4` down, 4096 -> 24576 ->
+    4096 in the reference). Here: input quant -> gate_up GEMM whose epilogue applies SwiGLU and writes the down GEMM's
+    NVFP4 input (codes + scale atoms, global scale GS_H) -> down GEMM with a bf16 epilogue: three launches."""
+
+    def __init__(self, seed: int, hidden: int, inter: int, device, init: str = "uniform", std: float = 0.02):
+        dev = torch.device(device)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        H, F = hidden, inter
+        if F % 128 != 0 or H % 256 != 0:
+            raise ValueError(f"dense FFN dims H={H} (% 256), F={F} (% 128)")
+        self.H, self.F = H, F
+        c1, s1, self.gs_w1 = weights.nvfp4_tensor(g, 2 * F, H, dev, init, std=std)
+        c2, s2, self.gs_w2 = weights.nvfp4_tensor(g, H, F, dev, init, weights.SILU_U_SQ_MEAN, std=std)
+        self.w1_codes = layout.pack_codes(layout.gate_up_interleave(c1)).contiguous()
+        self.w1_sf = layout.sf_to_atoms(layout.gate_up_interleave(s1), H)
+        self.w2 = Nvfp4Linear(c2, s2, self.gs_w2, dev, gs_in=weights.GS_H)
+        self.alpha1 = float(1.0 / (weights.GS_X * self.gs_w1))
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.device = dev
+        self._lib = lib.load()
+
+    def logical(self):
+        """(w1 codes [2F, H] gate rows then up rows, w1 sf, gs_w1, w2 codes [H, F], w2 sf, gs_w2) for the checker."""
+        c1 = layout.gate_up_deinterleave(layout.unpack_codes(self.w1_codes))
+        s1 = layout.gate_up_deinterleave(layout.atoms_to_sf(self.w1_sf, 2 * self.F, self.H))
+        c2, s2, g2 = self.w2.logical()
+        return c1, s1, self.gs_w1, c2, s2, g2
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """x bf16 [T, H] -> bf16 [T, H]."""
+        T, H, F, dev = x.shape[0], self.H, self.F, self.device
+        s = lib.stream_ptr(stream)
+        rows = _round(max(T, 1), 128)
+        xc = torch.empty(rows, H // 2, dtype=torch.uint8, device=dev)
+        xs = torch.zeros(rows // 128 * layout.sf_atom_cols(H) * 512, dtype=torch.uint8, device=dev)
+        lib.check("ssb_nvfp4_quantize", self._lib.ssb_nvfp4_quantize(x.data_ptr(), T, H, x.stride(0), weights.GS_X,
+                                                                     xc.data_ptr(), H // 2, xs.data_ptr(), s))
+        hc, hs = self.w2.input_buffers(T)
+        lib.check("ssb_nvfp4_gemm", self._lib.ssb_nvfp4_gemm(lib.EPI_SWIGLU, xc.data_ptr(), xs.data_ptr(), T, H,
+                                                             self.w1_codes.data_ptr(), self.w1_sf.data_ptr(), 2 * F,
+                                                             self.alpha1, hc.data_ptr(), F // 2, hs.data_ptr(),
+                                                             weights.GS_H, self.status.data_ptr(), s))
+        if out is None:
+            out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        return self.w2.gemm(hc, hs, T, out, self.status, stream)
+
+    __call__ = forward
+
+
 class KdaAttention:
     """The KDA attention block of one layer: hidden H, `heads` heads of 128 (P = heads * 128)."""
 
-    def __init__(self, seed: int, hidden: int, heads: int, device, lower_bound: float = -5.0, norm_eps: float = 1e-5):
+    def __init__(self, seed: int, hidden: int, heads: int, device, lower_bound: float = -5.0, norm_eps: float = 1e-5,
+                 init: str = "uniform", std: float = 0.02):
         dev = torch.device(device)
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
         H, P = hidden, heads * HEAD_DIM
         self.H, self.heads, self.P = H, heads, P
         self.in_cols = 3 * P + 2 * LOW_RANK + heads
-        self.in_proj = Nvfp4Linear.random(g, self.in_cols, H, dev)
-        self.f_b = Nvfp4Linear.random(g, P, LOW_RANK, dev)
-        self.g_b = Nvfp4Linear.random(g, P, LOW_RANK, dev)
-        self.o_proj = Nvfp4Linear.random(g, H, P, dev)
+        w = dict(init=init, std=std)
+        self.in_proj = Nvfp4Linear.random(g, self.in_cols, H, dev, **w)
+        self.f_b = Nvfp4Linear.random(g, P, LOW_RANK, dev, **w)
+        self.g_b = Nvfp4Linear.random(g, P, LOW_RANK, dev, **w)
+        self.o_proj = Nvfp4Linear.random(g, H, P, dev, **w)
         conv_w = ((torch.rand(3 * P, 4, generator=g, device=dev) - 0.5) * 1.2).to(torch.bfloat16)
         a_log = torch.rand(heads, generator=g, device=dev) * 2 - 1
         dt_bias = torch.randn(P, generator=g, device=dev) * 0.5
@@ -185,18 +240,20 @@ class KdaDecoderLayer:
     shared expert). The layer's output sub-block (the MoE rows, with their post / comb mixes) is folded into the
     residual by the next boundary."""
 
-    def __init__(self, seed: int, hidden: int, heads: int, inter: int, experts: int, top_k: int, device):
-        from . import moe
-
+    def __init__(self, seed: int, hidden: int, heads: int, inter: int, experts: int, top_k: int, device,
+                 ffn: str = "moe", routing: dict | None = None, init: str = "uniform", std: float = 0.02):
+        """ffn "moe" (F = inter, `experts` routed top-`top_k` + shared; `routing`: moe_logical's routing keywords) or
+        "dense" (the reference's leading layers: a dense SwiGLU FFN of intermediate `inter`); init / std: the NVFP4
+        weights' recipe (weights.nvfp4_tensor)."""
         dev = torch.device(device)
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
         self.H = hidden
         self.bound_a = MhcBoundary(g, hidden, dev)
-        self.attn = KdaAttention(seed + 1, hidden, heads, dev)
+        self.attn = KdaAttention(seed + 1, hidden, heads, dev, init=init, std=std)
         self.bound_b = MhcBoundary(g, hidden, dev)
-        self.moe = moe.MoELayer.from_logical(weights.moe_logical(seed + 2, hidden, inter, experts, device=dev), top_k,
-                                             dev)
+        self.ffn = _make_ffn(seed + 2, hidden, inter, experts, top_k, dev, ffn, routing, init, std)
+        self.moe = self.ffn                  # the FFN sub-block (MoELayer or DenseFfn)
         self.device = dev
 
     def forward(self, res, x_prev, post_prev, comb_prev, seqs, conv_state, rec_state, status, stream=None):
@@ -218,16 +275,60 @@ class KdaDecoderLayer:
         return res_b, x_b, post_b, comb_b
 
 
+def _make_ffn(seed: int, hidden: int, inter: int, experts: int, top_k: int, device, ffn: str, routing: dict | None,
+              init: str = "uniform", std: float = 0.02):
+    from . import moe
+
+    if ffn == "dense":
+        return DenseFfn(seed, hidden, inter, device, init, std)
+    if ffn != "moe":
+        raise ValueError(f"ffn {ffn!r}")
+    p = weights.moe_logical(seed, hidden, inter, experts, device=device, init=init, std=std, **(routing or {}))
+    return moe.MoELayer.from_logical(p, top_k, device)
+
+
+class Bf16Grouped:
+    """Per-head BF16 weights [heads, N, K] for the MLA absorb / v_up batched GEMMs, kept in BF16 as the reference
+    keeps them (ssengine/kernels.py configs 22 and 26: torch.bmm over 64 heads); a plain batched library GEMM (cuBLAS
+    through torch.bmm) with bf16 output."""
+
+    def __init__(self, gen: torch.Generator, heads: int, N: int, K: int, device, init: str = "uniform",
+                 std: float = 0.02):
+        dev = torch.device(device)
+        w = torch.randn(heads, N, K, generator=gen, device=dev)
+        self.w = (w * (std if init == "normal" else K ** -0.5)).to(torch.bfloat16)
+        self.wt = self.w.transpose(1, 2)                 # [heads, K, N] view
+        self.heads, self.N, self.K = heads, N, K
+        self.device = dev
+
+    def logical(self):
+        """The bf16 weights [heads, N, K] (for the checker)."""
+        return (self.w,)
+
+    def __call__(self, x_heads: torch.Tensor, rows_pad: int, out: torch.Tensor, status=None, stream=None):
+        """x_heads bf16 [heads * rows_pad, K] (head-major) -> out bf16 [heads * rows_pad, N]."""
+        with torch.cuda.stream(stream) if stream is not None else _null():
+            torch.bmm(x_heads.view(self.heads, rows_pad, self.K), self.wt,
+                      out=out.view(self.heads, rows_pad, self.N))
+        return out
+
+
+class _null:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *a):
+        return False
+
+
 class Nvfp4Grouped:
     """Per-head NVFP4 weights [heads, N, K] for the grouped GEMM (the MLA absorb / v_up bmm)."""
 
-    def __init__(self, gen: torch.Generator, heads: int, N: int, K: int, device, gs_in: float = weights.GS_X):
+    def __init__(self, gen: torch.Generator, heads: int, N: int, K: int, device, gs_in: float = weights.GS_X,
+                 init: str = "uniform", std: float = 0.02):
         dev = torch.device(device)
-        codes = torch.randint(0, 16, (heads * N, K), generator=gen, device=dev, dtype=torch.uint8)
-        table = torch.tensor(weights.SCALE_CODES, dtype=torch.uint8, device=dev)
-        sf = table[torch.randint(0, len(weights.SCALE_CODES), (heads * N, K // 16), generator=gen, device=dev)]
+        codes, sf, self.gs_w = weights.nvfp4_tensor(gen, heads * N, K, dev, init, std=std)
         self.heads, self.N, self.K = heads, N, K
-        self.gs_w = weights.unit_gs(K)
         self.gs_in = gs_in
         self.codes = layout.pack_codes(codes).contiguous()
         self.sf = layout.sf_to_atoms(sf, K)
@@ -284,20 +385,21 @@ class DsaAttention:
     HEADS, LATENT, ROPE, IDX_HEADS, IDX_DIM, TOPK = 64, 512, 64, 32, 128, 512
 
     def __init__(self, seed: int, hidden: int, device, q_lora: int = 1536, nope: int = 192, v_dim: int = 256,
-                 theta: float = 10000.0, eps: float = 1e-6):
+                 theta: float = 10000.0, eps: float = 1e-6, init: str = "uniform", std: float = 0.02):
         dev = torch.device(device)
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
         H = hidden
         self.H, self.q_lora, self.nope, self.v_dim, self.theta, self.eps = H, q_lora, nope, v_dim, theta, eps
         self.qh = nope + self.ROPE
-        self.a_proj = Nvfp4Linear.random(g, q_lora + self.LATENT + self.ROPE, H, dev)
-        self.q_b = Nvfp4Linear.random(g, self.HEADS * self.qh, q_lora, dev)
-        self.w_uk = Nvfp4Grouped(g, self.HEADS, self.LATENT, nope, dev)
-        self.w_uv = Nvfp4Grouped(g, self.HEADS, v_dim, self.LATENT, dev)
-        self.o_proj = Nvfp4Linear.random(g, H, self.HEADS * v_dim, dev)
-        self.wq_idx = Nvfp4Linear.random(g, self.IDX_HEADS * self.IDX_DIM, q_lora, dev)
-        self.idx_proj = Nvfp4Linear.random(g, self.IDX_DIM + self.IDX_HEADS + self.IDX_DIM, H, dev)
+        w = dict(init=init, std=std)
+        self.a_proj = Nvfp4Linear.random(g, q_lora + self.LATENT + self.ROPE, H, dev, **w)
+        self.q_b = Nvfp4Linear.random(g, self.HEADS * self.qh, q_lora, dev, **w)
+        self.w_uk = Bf16Grouped(g, self.HEADS, self.LATENT, nope, dev, **w)
+        self.w_uv = Bf16Grouped(g, self.HEADS, v_dim, self.LATENT, dev, **w)
+        self.o_proj = Nvfp4Linear.random(g, H, self.HEADS * v_dim, dev, **w)
+        self.wq_idx = Nvfp4Linear.random(g, self.IDX_HEADS * self.IDX_DIM, q_lora, dev, **w)
+        self.idx_proj = Nvfp4Linear.random(g, self.IDX_DIM + self.IDX_HEADS + self.IDX_DIM, H, dev, **w)
         self.q_norm = (torch.rand(q_lora, generator=g, device=dev) + 0.5).to(torch.bfloat16)
         self.kv_norm = (torch.rand(self.LATENT, generator=g, device=dev) + 0.5).to(torch.bfloat16)
         self.ape = torch.randn(4, self.IDX_DIM, generator=g, device=dev) * 0.5
@@ -385,18 +487,17 @@ class DsaDecoderLayer:
     NVFP4 MoE (the same shape as `KdaDecoderLayer` with the sparse-attention block)."""
 
     def __init__(self, seed: int, hidden: int, inter: int, experts: int, top_k: int, device, q_lora: int = 1536,
-                 nope: int = 192, v_dim: int = 256):
-        from . import moe
-
+                 nope: int = 192, v_dim: int = 256, ffn: str = "moe", routing: dict | None = None,
+                 init: str = "uniform", std: float = 0.02):
         dev = torch.device(device)
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
         self.H = hidden
         self.bound_a = MhcBoundary(g, hidden, dev)
-        self.attn = DsaAttention(seed + 1, hidden, dev, q_lora=q_lora, nope=nope, v_dim=v_dim)
+        self.attn = DsaAttention(seed + 1, hidden, dev, q_lora=q_lora, nope=nope, v_dim=v_dim, init=init, std=std)
         self.bound_b = MhcBoundary(g, hidden, dev)
-        self.moe = moe.MoELayer.from_logical(weights.moe_logical(seed + 2, hidden, inter, experts, device=dev), top_k,
-                                             dev)
+        self.ffn = _make_ffn(seed + 2, hidden, inter, experts, top_k, dev, ffn, routing, init, std)
+        self.moe = self.ffn                  # the FFN sub-block (MoELayer or DenseFfn)
         self.device = dev
 
     def forward(self, res, x_prev, post_prev, comb_prev, meta: dict, caches: tuple, status, stream=None):

@@ -23,9 +23,10 @@ EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_g
            "ssb_indexer_logits", "ssb_indexer_expand", "ssb_sparse_mla", "ssb_mla_cache_append", "ssb_mla_q_pack",
            "ssb_kpool_insert", "ssb_gated_rmsnorm", "ssb_gated_rmsnorm_nvfp4", "ssb_hc_expand", "ssb_hc_mean",
            "ssb_nvfp4_gemm_grouped", "ssb_rmsnorm_cols", "ssb_rope", "ssb_transpose_heads", "ssb_concat_cols",
-           "ssb_head_tiles")
+           "ssb_head_tiles", "ssb_moe_route_sigmoid")
 
 EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
+ROUTE_SOFTMAX, ROUTE_SIGMOID_BIAS = 0, 1
 
 WS = dict(XQ=0, XSF=1, LOGITS=2, IDS=3, WEIGHTS=4, ROWS=5, COUNTS=6, OFFSETS=7, MASKS=8, BLOCKS=9, MTILES=10,
           NUM_MTILES=11, XQ_PERM=12, XSF_PERM=13, ACT=14, ACT_SF=15, Y=16, ROW_SRC=17, END=18)
@@ -48,7 +49,9 @@ class MoeLayerC(ctypes.Structure):
                 ("router_codes", ctypes.c_void_p), ("router_sf", ctypes.c_void_p), ("router_rows", ctypes.c_int64),
                 ("router_alpha", ctypes.c_float), ("w1_codes", ctypes.c_void_p), ("w1_sf", ctypes.c_void_p),
                 ("w1_alpha", ctypes.c_void_p), ("w2_codes", ctypes.c_void_p), ("w2_sf", ctypes.c_void_p),
-                ("w2_alpha", ctypes.c_void_p), ("add_input", ctypes.c_int32)]
+                ("w2_alpha", ctypes.c_void_p), ("add_input", ctypes.c_int32), ("routing", ctypes.c_int32),
+                ("n_group", ctypes.c_int32), ("topk_group", ctypes.c_int32), ("routed_scale", ctypes.c_float),
+                ("route_bias", ctypes.c_void_p)]
 
 
 class KdaLayerC(ctypes.Structure):
@@ -76,6 +79,7 @@ _SIGS = {
     "ssb_nvfp4_quantize": ([_P, _I64, _I64, _I64, _F, _P, _I64, _P, _P], ctypes.c_int),
     "ssb_nvfp4_gemm": ([_I32, _P, _P, _I64, _I64, _P, _P, _I64, _F, _P, _I64, _P, _F, _P, _P], ctypes.c_int),
     "ssb_moe_route": ([_P, _I64, _I32, _I32, _P, _P, _P], ctypes.c_int),
+    "ssb_moe_route_sigmoid": ([_P, _I64, _I32, _I32, _P, _I32, _I32, _F, _P, _P, _P], ctypes.c_int),
     "ssb_moe_workspace_bytes": ([ctypes.POINTER(MoeLayerC), _I64], _I64),
     "ssb_moe_workspace_offsets": ([ctypes.POINTER(MoeLayerC), _I64, ctypes.POINTER(ctypes.c_int64), _I32],
                                   ctypes.c_int),

@@ -16,7 +16,9 @@ from . import layout, lib
 
 class MoELayer:
     def __init__(self, H: int, F: int, E: int, k: int, gs_x: float, gs_h: float, router: tuple, w1: tuple,
-                 w2: tuple, device, add_input: bool = False):
+                 w2: tuple, device, add_input: bool = False, route: dict | None = None):
+        """route: None for softmax top-k routing, else the sigmoid + correction-bias rule
+        {"bias": fp32 [E] device tensor, "n_group", "topk_group", "scale"} (the reference model's)."""
         self.H, self.F, self.E, self.k = H, F, E, k
         self.gs_x, self.gs_h = float(gs_x), float(gs_h)
         self.device = torch.device(device)
@@ -29,6 +31,13 @@ class MoELayer:
                                 self.w1_codes.data_ptr(), self.w1_sf.data_ptr(), self.w1_alpha.data_ptr(),
                                 self.w2_codes.data_ptr(), self.w2_sf.data_ptr(), self.w2_alpha.data_ptr(),
                                 1 if add_input else 0)
+        self.route = route
+        if route is not None:
+            self.route_bias = route["bias"].to(self.device, torch.float32).contiguous()
+            self._c.routing = lib.ROUTE_SIGMOID_BIAS
+            self._c.n_group, self._c.topk_group = int(route["n_group"]), int(route["topk_group"])
+            self._c.routed_scale = float(route["scale"])
+            self._c.route_bias = self.route_bias.data_ptr()
         self.add_input = add_input
         self._ws = None
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -60,7 +69,12 @@ class MoELayer:
               torch.tensor(a1, dtype=torch.float32, device=dev))
         w2 = (torch.cat(w2c).contiguous(), torch.cat(w2s).contiguous(),
               torch.tensor(a2, dtype=torch.float32, device=dev))
-        return cls(H, F, E, k, p["gs_x"], p["gs_h"], router, w1, w2, dev, add_input)
+        route = None
+        if p.get("route") is not None:
+            r = p["route"]
+            bias = r["bias"] if isinstance(r["bias"], torch.Tensor) else torch.as_tensor(r["bias"])
+            route = {**r, "bias": bias.to(dev, torch.float32)}
+        return cls(H, F, E, k, p["gs_x"], p["gs_h"], router, w1, w2, dev, add_input, route)
 
     # ---------------------------------------------------------------- forward
     def workspace_bytes(self, T: int) -> int:
@@ -146,5 +160,9 @@ class MoELayer:
             sc2 = layout.atoms_to_sf(self.w2_sf[e * s2:(e + 1) * s2], H, F)
             experts.append((c1.cpu().numpy(), sc1.cpu().numpy(), float(1.0 / (a1[e] * self.gs_x)), c2.cpu().numpy(),
                             sc2.cpu().numpy(), float(1.0 / (a2[e] * self.gs_h))))
-        return {"H": H, "F": F, "E": E, "gs_x": self.gs_x, "gs_h": self.gs_h,
-                "router": (rc, rs, float(1.0 / (self.router_alpha * self.gs_x))), "experts": experts}
+        out = {"H": H, "F": F, "E": E, "gs_x": self.gs_x, "gs_h": self.gs_h,
+               "router": (rc, rs, float(1.0 / (self.router_alpha * self.gs_x))), "experts": experts}
+        if self.route is not None:
+            out["route"] = {"bias": self.route_bias.cpu().numpy(), "n_group": self.route["n_group"],
+                            "topk_group": self.route["topk_group"], "scale": self.route["scale"]}
+        return out

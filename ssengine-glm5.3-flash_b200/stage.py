@@ -18,12 +18,15 @@ Layer kinds (`StageConfig.layer_kind`):
   elsewhere (`layers.DsaDecoderLayer`, `layers.KdaDecoderLayer`: boundary, attention with NVFP4 projections,
   boundary, NVFP4 MoE); stage 0 expands its embeddings to 4 streams (hc_expand), a later stage starts with a
   pre-only boundary on the received [T, 4H] rows (edge_recv), a stage that is not the last ends with a post-only
-  boundary (edge_send). A KDA layer owns conv / recurrent state pools indexed by the chunk's `state_blocks[0]` (has
-  state = the chunk continues its request); a DSA layer owns its latent cache and pool-key cache (the chunk's
-  `kv_pages`) and the kpool tail ring (`state_blocks[5]`).
+  boundary (edge_send). The KV and state pages follow the reference's block layout (`kvpages.StageKv`): a DSA
+  layer's latent rows and pool keys are addressed through the chunk's `kv_pages`, its kpool tail ring by
+  `state_blocks[5]`; a KDA layer of state group g (its ordinal among the model's KDA layers, mod 5) keeps its conv and
+  recurrent state in block `state_blocks[g]` of the latent tensor it aliases (has state = the chunk continues its
+  request). With `dense_layers` > 0 the leading layers carry a dense SwiGLU FFN instead of the MoE (the reference
+  model's layers 0-2); `routing` "sigmoid" selects the reference model's MoE routing.
 - "kda": every layer KDA + MoE (no DSA layers).
 - "moe": NVFP4 MoE layers with a plain residual (x + MoE(x)), hidden [T, H], no state (BASELINE config 2's slice).
-The last stage's head: the mean of the 4 streams ("kda"), RMSNorm of each request's last row, NVFP4 lm_head GEMM
+The last stage's head: the mean of the 4 streams ("kda"), RMSNorm of each request's last row, BF16 lm_head GEMM
 (fp32 logits), argmax (lowest index on ties).
 """
 
@@ -62,6 +65,31 @@ def table_width(blocks: int, page_tokens: int = PAGE_TOKENS, block_tokens: int =
     return (1 << max(blocks - 1, 0).bit_length()) * per_block
 
 
+def check_blocks(chunks, num_blocks: int) -> None:
+    """The block contract the state pages rely on (ssengine/model/kv_tensors.py:1-14: a block holds a request's KV
+    pages or one of its states, never both): every non-null state block of the plan belongs to one (request, group)
+    only and is no request's KV block; blocks within the pool. Block 0 is the null block (a dummy request may use it
+    for every state). Raises ValueError."""
+    seen = {}
+    kv_blocks = set()
+    for c in chunks:
+        if len(c.state_blocks) < 6:
+            raise ValueError(f"chunk {c.req_id}: {len(c.state_blocks)} state blocks (6 needed)")
+        for g, b in enumerate(c.state_blocks[:6]):
+            b = int(b)
+            if not 0 <= b < num_blocks:
+                raise ValueError(f"chunk {c.req_id}: state block {b} outside the pool of {num_blocks}")
+            if b == 0:
+                continue
+            if b in seen and seen[b] != (c.req_id, g):
+                raise ValueError(f"state block {b} held twice: {seen[b]} and {(c.req_id, g)}")
+            seen[b] = (c.req_id, g)
+        kv_blocks.update(int(p) // (BLOCK_TOKENS // PAGE_TOKENS) for p in c.kv_pages)
+    both = kv_blocks.intersection(seen)
+    if both:
+        raise ValueError(f"blocks {sorted(both)[:8]} are both KV and state blocks")
+
+
 @dataclass
 class StageConfig:
     """What a stage reads of the run config (the reference's RunConfig fields `layer_split`, `scheduler.mb_tokens`,
@@ -84,6 +112,16 @@ class StageConfig:
     q_lora: int = 1536
     mla_nope: int = 192
     mla_v_dim: int = 256
+    dense_layers: int = 0              # leading layers with a dense SwiGLU FFN instead of the MoE (the reference model:
+                                       # 3, `first_kda_dense` / `kda_dense`, ssengine/kernels.py:283-289)
+    dense_inter: int = 12288           # their intermediate size (gate_up 4096 -> 2 x 12288)
+    routing: str = "softmax"           # MoE routing: "softmax" or "sigmoid" (the reference model:
+                                       # sigmoid + correction bias, routed scale 5/2)
+    n_group: int = 1
+    topk_group: int = 1
+    weight_init: str = "uniform"       # NVFP4 weights: "uniform" (codes uniform, scales
+                                       # log-uniform) or "normal" (N(0, init_std) quantized)
+    init_std: float = 0.02
 
 
 @dataclass
@@ -97,7 +135,8 @@ class Batch:
     last_rows: torch.Tensor            # int64 [#is_last], rows whose token the last stage returns, plan chunk order
     bucket: int | None = None
     keep: list = field(default_factory=list)   # host / device buffers that must outlive the queued work
-    kda_seqs: torch.Tensor | None = None       # int32 [R, 4] {first row, end row, KDA state block, has state}, device
+    kda_seqs: torch.Tensor | None = None       # int32 [5, R, 4] per KDA state group g2..g6: {first row, end row,
+                                               # state_blocks[g], has state}, device
     dsa: dict | None = None                    # DSA layers' metadata (positions, slots, qsl, page table, kpool, groups)
 
 
@@ -140,36 +179,42 @@ class StageModel:
         self.kda = cfg.layer_kind in ("kda", "hybrid")
         if cfg.layer_kind not in ("moe", "kda", "hybrid"):
             raise ValueError(f"layer_kind {cfg.layer_kind!r}")
-        self.is_dsa = [cfg.layer_kind == "hybrid" and i % 4 == 3 for i in self.layer_range]
+        self.is_dsa = [self.layer_is_dsa(i) for i in self.layer_range]
         self.hidden_width = 4 * cfg.hidden if self.kda else cfg.hidden
         self.num_blocks = (num_blocks if num_blocks is not None else cfg.num_blocks) + extra_blocks
         self.cuda_graphs = cfg.cuda_graphs if cuda_graphs is None else cuda_graphs
         self.ipc_kv = ipc_kv
+        self.layer_hook = None          # optional callable(layer, res, x_prev, post, comb) after each layer (checks)
         self._lib = lib.load()
         H, F, E = cfg.hidden, cfg.inter, cfg.experts
         if self.kda:
+            from .kvpages import StageKv
             from .layers import DsaDecoderLayer, KdaDecoderLayer
 
-            P = cfg.kda_heads * 128
-            pages = self.num_blocks * (BLOCK_TOKENS // PAGE_TOKENS)
-            self.layers, self.kda_states = [], []
+            # KV and state pages in the reference's block layout: KDA group g2..g6 states alias the DSA layers'
+            # latent blocks (kvpages.StageKv)
+            self.kv = StageKv(list(self.layer_range), self.layer_is_dsa, self.num_blocks, cfg.kda_heads, self.device)
+            route = None if cfg.routing == "softmax" else dict(routing=cfg.routing, n_group=cfg.n_group,
+                                                               topk_group=cfg.topk_group)
+            self.layers, self.kda_states, self.kda_group = [], [], []
             for i, dsa in zip(self.layer_range, self.is_dsa):
                 seed = cfg.seed * 1000 + 10 * i
+                dense = i < cfg.dense_layers
+                ffn = dict(ffn="dense" if dense else "moe", routing=route, init=cfg.weight_init, std=cfg.init_std)
+                inter = cfg.dense_inter if dense else F
                 if dsa:
-                    self.layers.append(DsaDecoderLayer(seed, H, F, E, cfg.top_k, self.device, q_lora=cfg.q_lora,
-                                                       nope=cfg.mla_nope, v_dim=cfg.mla_v_dim))
-                    # latent cache e4m3 [pages * 128, 576], pool-key cache [pages * 32, 128], tail ring [blocks, 2, 4, 128]
-                    self.kda_states.append((
-                        torch.zeros(pages * PAGE_TOKENS, 576, dtype=torch.uint8, device=self.device),
-                        torch.zeros(pages * 32, 128, dtype=torch.bfloat16, device=self.device),
-                        torch.zeros(self.num_blocks, 2, 4, 128, dtype=torch.bfloat16, device=self.device)))
+                    self.layers.append(DsaDecoderLayer(seed, H, inter, E, cfg.top_k, self.device, q_lora=cfg.q_lora,
+                                                       nope=cfg.mla_nope, v_dim=cfg.mla_v_dim, **ffn))
+                    # latent cache e4m3 [slots, 576], pool-key cache [pages * 32, 128], tail ring [blocks, 2, 4, 128]
+                    self.kda_states.append((self.kv.latent(i), self.kv.pool_keys(i), self.kv.tail_ring(i)))
+                    self.kda_group.append(None)
                 else:
-                    self.layers.append(KdaDecoderLayer(seed, H, cfg.kda_heads, F, E, cfg.top_k, self.device))
-                    # KDA conv state [blocks, 3, 3P] bf16 and recurrent state [blocks, heads, 128, 128] fp32
-                    self.kda_states.append((
-                        torch.zeros(self.num_blocks, 3, 3 * P, dtype=torch.bfloat16, device=self.device),
-                        torch.zeros(self.num_blocks, cfg.kda_heads, 128, 128, dtype=torch.float32,
-                                    device=self.device)))
+                    self.layers.append(KdaDecoderLayer(seed, H, cfg.kda_heads, inter, E, cfg.top_k, self.device,
+                                                       **ffn))
+                    # KDA conv state [blocks, 3, 3P] bf16 and recurrent state [blocks, heads, 128, 128] fp32, views
+                    # into the aliased latent pages
+                    self.kda_states.append((self.kv.conv_state(i), self.kv.rec_state(i)))
+                    self.kda_group.append(self.kv.group[i])
             self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         else:
             self.layers = [moe.MoELayer.from_logical(weights.moe_logical(cfg.seed * 1000 + i, H, F, E,
@@ -184,21 +229,20 @@ class StageModel:
         if warmup:
             self._warm()
 
+    def layer_is_dsa(self, i: int) -> bool:
+        """Model layer i is a DSA layer: layers 3, 7, ..., 43 of the hybrid interleave (ssengine/kernels.py:278)."""
+        return self.cfg.layer_kind == "hybrid" and i % 4 == 3
+
     # ---------------------------------------------------------------- construction helpers
     def _init_head(self) -> None:
+        """The lm_head in BF16, as the reference keeps it (ssengine/kernels.py:203-205, config 35: BF16 `F.linear` on
+        the finished rows; its NVFP4 GEMMs are the dense FFN and the experts): weights N(0, 1 / H) for unit-variance
+        logits ("uniform" recipe) or N(0, init_std) ("normal")."""
         cfg, H, V = self.cfg, self.cfg.hidden, self.cfg.vocab
         g = torch.Generator(device=self.device)
         g.manual_seed(cfg.seed * 1000 + 998)
-        rows = -(-V // 128) * 128
-        codes = torch.zeros(rows, H, dtype=torch.uint8, device=self.device)
-        codes[:V] = torch.randint(0, 16, (V, H), generator=g, device=self.device, dtype=torch.uint8)
-        table = torch.tensor(weights.SCALE_CODES, dtype=torch.uint8, device=self.device)
-        sf = torch.zeros(rows, H // 16, dtype=torch.uint8, device=self.device)
-        sf[:V] = table[torch.randint(0, len(weights.SCALE_CODES), (V, H // 16), generator=g, device=self.device)]
-        self.head_gs = weights.unit_gs(H)
-        self.head_codes = layout.pack_codes(codes).contiguous()
-        self.head_sf = layout.sf_to_atoms(sf, H)
-        self.head_alpha = float(1.0 / (weights.GS_X * self.head_gs))
+        std = cfg.init_std if cfg.weight_init == "normal" else H ** -0.5
+        self.head_w = (torch.randn(V, H, generator=g, device=self.device) * std).to(torch.bfloat16)
         self.norm_weight = torch.ones(H, dtype=torch.bfloat16, device=self.device)
 
     def _warm(self) -> None:
@@ -211,6 +255,7 @@ class StageModel:
         hidden = None if self.first else torch.zeros(n, self.hidden_width, dtype=torch.bfloat16, device=self.device)
         self.forward(plan, hidden)
         moes = [layer.moe if self.kda else layer for layer in self.layers]
+        moes = [m for m in moes if isinstance(m, moe.MoELayer)]
         ws = max(m.workspace_bytes(self.cfg.mb_tokens) for m in moes) if moes else 0
         shared = torch.empty(ws, dtype=torch.uint8, device=self.device) if ws else None
         for m in moes:
@@ -250,8 +295,11 @@ class StageModel:
              "page_ptr": pk.add(page_ptr.astype(np.int32)), "pages": pk.add(np.maximum(pages, 0).astype(np.int32)),
              "last": pk.add(last)}
         if self.kda:
-            ks = np.array([(int(qsl[r]), int(qsl[r + 1]), int(chunks[i].state_blocks[0]), int(chunks[i].start > 0))
-                           for r, i in enumerate(order)], dtype=np.int32).reshape(-1, 4)
+            check_blocks(chunks, self.num_blocks)
+            # one sequence table per KDA state group g2..g6: the chunk's state_blocks[g] (has state = the chunk
+            # continues its request)
+            ks = np.array([[(int(qsl[r]), int(qsl[r + 1]), int(chunks[i].state_blocks[g]), int(chunks[i].start > 0))
+                            for r, i in enumerate(order)] for g in range(5)], dtype=np.int32).reshape(5, -1, 4)
             h["kda"] = pk.add(ks)
         if any(self.is_dsa):
             from .indexer import work_groups
@@ -328,11 +376,14 @@ class StageModel:
                 raise ValueError(f"stage {self.stage} needs hidden_in bf16 [{T}, {4 * H}]")
             res = hidden_in.view(T, 4, H)
         x_prev = post = comb = None
-        for layer, state, dsa in zip(self.layers, self.kda_states, self.is_dsa):
+        for layer, state, dsa, grp in zip(self.layers, self.kda_states, self.is_dsa, self.kda_group):
             if dsa:
                 res, x_prev, post, comb = layer.forward(res, x_prev, post, comb, batch.dsa, state, self.status)
             else:
-                res, x_prev, post, comb = layer.forward(res, x_prev, post, comb, batch.kda_seqs, *state, self.status)
+                res, x_prev, post, comb = layer.forward(res, x_prev, post, comb, batch.kda_seqs[grp], *state,
+                                                        self.status)
+            if self.layer_hook is not None:
+                self.layer_hook(layer, res, x_prev, post, comb)
         out = torch.empty(T, 4, H, dtype=torch.bfloat16, device=self.device)
         if x_prev is None:
             out.copy_(res)
@@ -359,11 +410,11 @@ class StageModel:
         return self.run(self.prepare(plan), hidden_in)
 
     def tier_ranges(self) -> list:
-        """Byte ranges (device pointer, bytes) of the stage's state tensors for the capacity tiers: the KDA conv and
-        recurrent state pools of each KDA layer (none for MoE-only stages)."""
+        """Byte ranges (device pointer, bytes) of the stage's KV and state tensors for the capacity tiers: every
+        latent / state page tensor, pool-key cache and tail ring (none for MoE-only stages)."""
         if not self.kda:
             return []
-        return [(t.data_ptr(), t.numel() * t.element_size()) for pair in self.kda_states for t in pair]
+        return self.kv.ranges()
 
     # ---------------------------------------------------------------- last stage
     def _head(self, x: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
@@ -375,17 +426,9 @@ class StageModel:
         y = torch.empty(n, H, dtype=torch.bfloat16, device=self.device)
         lib.check("ssb_rmsnorm", self._lib.ssb_rmsnorm(x.data_ptr(), H, rows.data_ptr(), n, self.norm_weight.data_ptr(),
                                                        self.cfg.norm_eps, y.data_ptr(), s))
-        npad = -(-n // 128) * 128
-        codes = torch.empty(npad, H // 2, dtype=torch.uint8, device=self.device)
-        sf = torch.zeros(npad // 128 * layout.sf_atom_cols(H) * 512, dtype=torch.uint8, device=self.device)
-        lib.check("ssb_nvfp4_quantize", self._lib.ssb_nvfp4_quantize(y.data_ptr(), n, H, H, weights.GS_X,
-                                                                     codes.data_ptr(), H // 2, sf.data_ptr(), s))
-        logits = torch.empty(n, V, dtype=torch.float32, device=self.device)
-        status = torch.zeros(1, dtype=torch.int32, device=self.device)
-        lib.check("ssb_nvfp4_gemm", self._lib.ssb_nvfp4_gemm(lib.EPI_F32, codes.data_ptr(), sf.data_ptr(), n, H,
-                                                             self.head_codes.data_ptr(), self.head_sf.data_ptr(), V,
-                                                             self.head_alpha, logits.data_ptr(), V, None, 1.0,
-                                                             status.data_ptr(), s))
+        # BF16 x BF16 -> fp32 logits of the finished rows: a plain library GEMM (cuBLAS through torch.mm), like the
+        # reference's lm_head call
+        logits = torch.mm(y, self.head_w.t(), out_dtype=torch.float32)
         lib.check("ssb_argmax_rows", self._lib.ssb_argmax_rows(logits.data_ptr(), V, V, n, tokens.data_ptr(), s))
-        self.last_logits, self.last_normed, self.last_status = logits, y, status
+        self.last_logits, self.last_normed = logits, y
         return tokens

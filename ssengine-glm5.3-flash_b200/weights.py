@@ -41,6 +41,40 @@ def unit_gs(K: int, in_sq_mean: float = 1.0) -> float:
     return math.sqrt(K * in_sq_mean * E2M1_SQ_MEAN * SCALE_SQ_MEAN)
 
 
+E2M1_MIDPOINTS = (0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0)
+
+
+def quantize_weight(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, float]:
+    """A real-valued weight [N, K] -> NVFP4 (codes [N, K] one per byte, e4m3 scales [N, K / 16], global scale gs) with
+    gs = 448 * 6 / max|w| (the largest block scale at the top of the e4m3 range), sf = e4m3((amax16 / 6) * gs) and
+    each code the nearest e2m1 magnitude of |w| * gs / sf (midpoints to the smaller one) with w's sign. Weights are
+    data: the checker reads these codes back, so the rounding rule only needs to be deterministic."""
+    N, K = w.shape
+    w = w.float()
+    gs = float(448.0 * 6.0 / max(float(w.abs().max()), 1e-30))
+    blocks = w.view(N, K // 16, 16)
+    sf = (blocks.abs().amax(-1) / 6.0 * gs).to(torch.float8_e4m3fn)
+    sfv = sf.float()
+    r = torch.where(sfv > 0, gs / sfv.clamp_min(1e-30), torch.zeros_like(sfv))
+    mag = blocks.abs() * r[..., None]
+    idx = torch.bucketize(mag, torch.tensor(E2M1_MIDPOINTS, device=w.device))
+    codes = (idx + 8 * (blocks < 0).to(idx.dtype)).to(torch.uint8).view(N, K)
+    return codes, sf.view(torch.uint8), gs
+
+
+def nvfp4_tensor(gen, N: int, K: int, device, init: str = "uniform", in_sq_mean: float = 1.0, std: float = 0.02,
+                 factor: float = 1.0):
+    """(codes [N, K], sf [N, K / 16], gs) of one random-init NVFP4 weight. init "uniform": BASELINE's recipe (codes
+    uniform over the 16 e2m1 codes, scales log-uniform over the e4m3 codes in [2^-8, 1], gs for unit-variance outputs
+    on inputs of mean square `in_sq_mean`, divided by `factor`); "normal": BASELINE config 1's recipe (N(0, std)
+    values quantized by `quantize_weight`)."""
+    if init == "uniform":
+        return _codes(gen, (N, K), device), _scales(gen, (N, K // 16), device), unit_gs(K, in_sq_mean) * factor
+    if init == "normal":
+        return quantize_weight(torch.randn(N, K, generator=gen, device=device) * std)
+    raise ValueError(f"init {init!r}")
+
+
 def _codes(gen, shape, device):
     return torch.randint(0, 16, shape, generator=gen, device=device, dtype=torch.uint8)
 
@@ -50,19 +84,33 @@ def _scales(gen, shape, device):
     return table[torch.randint(0, len(SCALE_CODES), shape, generator=gen, device=device)]
 
 
-def moe_logical(seed: int, H: int, F: int, E: int, device="cpu") -> dict:
-    """Logical parameters of one MoE layer: E routed experts + the shared expert (index E)."""
+# the reference model's routing (ssengine/kernels.py:182-187): sigmoid scores + a per-expert correction bias, top-8,
+# routed scaling factor 5/2; the bias is drawn like the reference's routing test draws it (12.4 + U[0, 0.52),
+# tests/test_moe_tuning_cpu.py:62: "the checkpoint's widest spread is 0.58")
+SIGMOID_ROUTE = dict(n_group=1, topk_group=1, scale=2.5, bias_base=12.4, bias_spread=0.52)
+
+
+def moe_logical(seed: int, H: int, F: int, E: int, device="cpu", routing: str = "softmax",
+                n_group: int = 1, topk_group: int = 1, init: str = "uniform", std: float = 0.02) -> dict:
+    """Logical parameters of one MoE layer: E routed experts + the shared expert (index E). routing "softmax"
+    or "sigmoid" (the reference model's rule; adds p["route"]); init: see `nvfp4_tensor`."""
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
-    g_r = unit_gs(H)
-    router = (_codes(gen, (E, H), device), _scales(gen, (E, H // 16), device), g_r)
+    router = nvfp4_tensor(gen, E, H, device, init, std=std)
     experts = []
     for e in range(E + 1):
         f = 1.0 + 0.25 * (e % 3)
-        w1 = (_codes(gen, (2 * F, H), device), _scales(gen, (2 * F, H // 16), device), unit_gs(H) * f)
-        w2 = (_codes(gen, (H, F), device), _scales(gen, (H, F // 16), device), unit_gs(F, SILU_U_SQ_MEAN) * f)
+        w1 = nvfp4_tensor(gen, 2 * F, H, device, init, std=std, factor=f)
+        w2 = nvfp4_tensor(gen, H, F, device, init, SILU_U_SQ_MEAN, std=std, factor=f)
         experts.append(w1 + w2)
-    return {"H": H, "F": F, "E": E, "gs_x": GS_X, "gs_h": GS_H, "router": router, "experts": experts}
+    p = {"H": H, "F": F, "E": E, "gs_x": GS_X, "gs_h": GS_H, "router": router, "experts": experts}
+    if routing == "sigmoid":
+        r = SIGMOID_ROUTE
+        bias = r["bias_base"] + torch.rand(E, generator=gen, device=device) * r["bias_spread"]
+        p["route"] = {"bias": bias.float(), "n_group": n_group, "topk_group": topk_group, "scale": r["scale"]}
+    elif routing != "softmax":
+        raise ValueError(f"routing {routing!r}")
+    return p
 
 
 def hidden_states(seed: int, T: int, H: int, device="cpu") -> torch.Tensor:
@@ -77,4 +125,7 @@ def to_numpy(p: dict) -> dict:
     def n(t):
         return t.cpu().numpy() if isinstance(t, torch.Tensor) else t
 
-    return {**p, "router": tuple(n(v) for v in p["router"]), "experts": [tuple(n(v) for v in e) for e in p["experts"]]}
+    out = {**p, "router": tuple(n(v) for v in p["router"]), "experts": [tuple(n(v) for v in e) for e in p["experts"]]}
+    if "route" in p:
+        out["route"] = {k: n(v) for k, v in p["route"].items()}
+    return out

@@ -14,6 +14,9 @@ It imports (never copies) these reference functions and records their outputs on
   reference's tests/test_kpool_cpu.py drives them (`indexer_call`, with its torch reference ops `ref_compress` /
   `ref_seed`): pools written by chunked prefills that start inside a pool, several requests in one microbatch
                                                                        -> kpool_ref.npz (`--parts kpool`)
+- ssengine/model/moe_tuning.py         `scale_hist`, `forced_logits`, with the reference's own routing check
+  `(logits.sigmoid() + bias).topk(8)` as tests/test_moe_tuning_cpu.py:55-64 runs it (512 tokens, 288 experts, a bias
+  of 12.4 + U[0, 0.52))                                                -> routing_ref.npz (`--parts routing`)
 The fixtures are small (tens of KB) and committed; the tests never read the reference at run time.
 """
 
@@ -66,10 +69,41 @@ def make_kpool(ref: str) -> None:
     np.savez_compressed(HERE / "kpool_ref.npz", pools=pools, tail=tail.float().numpy())
 
 
+def make_routing() -> None:
+    """The reference's routing test case (tests/test_moe_tuning_cpu.py:55-64): a Pareto-shaped expert histogram scaled
+    to 512 tokens, the logits `forced_logits` builds for it (+-30), a layer bias, and the experts the reference's rule
+    `(logits.sigmoid() + bias).topk(8)` selects (stored sorted per token; torch.topk's slot order is not part of the
+    rule)."""
+    import random
+
+    import torch
+
+    from ssengine.model import moe_tuning as mt
+
+    rnd = random.Random(0)
+    tokens = 512
+    w = [rnd.paretovariate(1.2) for _ in range(288)]
+    h = mt.scale_hist([int(x * 100) + 1 for x in w], tokens)
+    logits = mt.forced_logits(h, tokens, torch.float32, "cpu")
+    gen = torch.Generator().manual_seed(0)
+    bias = 12.4 + torch.rand(288, generator=gen) * 0.52
+    ids = (logits.sigmoid() + bias).topk(8, dim=1).indices
+    assert torch.bincount(ids.flatten(), minlength=288).tolist() == h
+    np.savez_compressed(HERE / "routing_ref.npz", selected=np.packbits((logits > 0).numpy(), axis=1),
+                        bias=bias.numpy().astype(np.float32), hist=np.asarray(h, np.int32),
+                        ids_sorted=np.sort(ids.numpy(), axis=1).astype(np.int32))
+
+
 def main() -> None:
     ref = os.environ.get("REF")
     if not ref:
         raise SystemExit("set REF to the reference checkout")
+    if sys.argv[1:] == ["--parts", "routing"]:
+        os.environ.setdefault("SSENGINE_HANDOFF", "/tmp/empty_handoff")
+        sys.path.insert(0, ref)
+        make_routing()
+        print("wrote routing_ref.npz")
+        return
     if sys.argv[1:] == ["--parts", "kpool"]:
         os.environ.setdefault("SSENGINE_HANDOFF", "/tmp/empty_handoff")
         sys.path.insert(0, ref)

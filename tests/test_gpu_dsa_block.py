@@ -79,8 +79,7 @@ def test_dsa_block_stagewise(cuda):
     q_ref[:, :, 64:] = od.bf16(od.rope(q_ref[:, :, 64:], positions, blk.theta))
     assert rel(P["q"].reshape(T, 64, 128), q_ref) < 2e-2
     qh = P["q"].reshape(T, 64, 128)[:, :, :64].transpose(1, 0, 2)
-    c, s_, g_ = (v.cpu().numpy() if torch.is_tensor(v) else v for v in blk.w_uk.logical())
-    lat = od.bf16(od.grouped_linear(qh, c, s_, g_, gs))                              # [64, T, 512]
+    lat = od.bf16(od.grouped_linear_bf16(qh, blk.w_uk.w.float().cpu().numpy()))     # [64, T, 512]
     Tp = P["q_lat"].shape[0] // 64
     assert rel(P["q_lat"].reshape(64, Tp, 512)[:, :T], lat) < 1e-3
     q_cat = np.concatenate([P["q_lat"].reshape(64, Tp, 512)[:, :T].transpose(1, 0, 2),
@@ -118,8 +117,7 @@ def test_dsa_block_stagewise(cuda):
                                blk.scale * blk.q_scale * blk.k_scale, blk.k_scale)
         for i in range(nr):
             assert rel(P["o_lat"][qsl[r] + i], want[i]) < 3e-2, (r, i)
-    c, s_, g_ = (v.cpu().numpy() if torch.is_tensor(v) else v for v in blk.w_uv.logical())
-    v_ref = od.bf16(od.grouped_linear(P["o_lat"].transpose(1, 0, 2), c, s_, g_, gs))
+    v_ref = od.bf16(od.grouped_linear_bf16(P["o_lat"].transpose(1, 0, 2), blk.w_uv.w.float().cpu().numpy()))
     assert rel(P["v"].reshape(64, Tp, 256)[:, :T], v_ref) < 1e-3
     np.testing.assert_array_equal(P["o_in"].reshape(T, 64, 256), P["v"].reshape(64, Tp, 256)[:, :T].transpose(1, 0, 2))
     assert rel(n(out), od.bf16(lin(P["o_in"], blk.o_proj))) < 1e-3

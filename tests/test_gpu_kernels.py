@@ -148,6 +148,49 @@ def test_route_indices_bit_exact(cuda, T, E, k):
     np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize("T,E,k,n_group,topk_group", [(8192, 288, 8, 1, 1), (1000, 256, 8, 8, 4), (77, 64, 6, 4, 3),
+                                                      (33, 512, 31, 1, 1)])
+def test_sigmoid_route_bit_exact(cuda, T, E, k, n_group, topk_group):
+    """ssb_moe_route_sigmoid (the reference model's routing) against the oracle: ids bit-exact (ties to the lower
+    expert / group included), weights within one fp32 ulp (the same fp32 operations; the sigmoid goes through a
+    double-precision exp on both sides)."""
+    lib, so = _lib()
+    rng = np.random.default_rng(T + E + n_group)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    logits[: T // 2] = np.round(logits[: T // 2] * 2) / 2        # many exact ties
+    bias = (12.4 + rng.uniform(0, 0.52, E)).astype(np.float32) if n_group == 1 else \
+        (np.round(rng.uniform(0, 0.1, E) * 8) / 8).astype(np.float32)
+    ids = torch.zeros((T, k), dtype=torch.int32, device=cuda)
+    w = torch.zeros((T, k), dtype=torch.float32, device=cuda)
+    lg, bs = _dev(logits), _dev(bias)              # held until the kernel has run
+    lib.check("ssb_moe_route_sigmoid", so.ssb_moe_route_sigmoid(lg.data_ptr(), T, E, k, bs.data_ptr(), n_group,
+                                                                topk_group, 2.5, ids.data_ptr(), w.data_ptr(),
+                                                                _stream()))
+    torch.cuda.synchronize()
+    rid, rw = omoe.route_sigmoid_bias(logits, k, bias, n_group, topk_group, 2.5)
+    np.testing.assert_array_equal(ids.cpu().numpy(), rid)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=1.2e-7, atol=0)
+
+
+def test_sigmoid_route_reference_case(cuda):
+    """The reference's own routing test case (tests/golden/routing_ref.npz, from its moe_tuning `forced_logits`):
+    the kernel selects exactly the experts the reference's rule selects."""
+    from pathlib import Path
+
+    lib, so = _lib()
+    f = np.load(Path(__file__).resolve().parent / "golden" / "routing_ref.npz")
+    sel = np.unpackbits(f["selected"], axis=1)[:, :288].astype(bool)
+    logits = np.where(sel, np.float32(30.0), np.float32(-30.0))
+    T = logits.shape[0]
+    ids = torch.zeros((T, 8), dtype=torch.int32, device=cuda)
+    w = torch.zeros((T, 8), dtype=torch.float32, device=cuda)
+    lg, bs = _dev(logits), _dev(f["bias"])        # held until the kernel has run
+    lib.check("ssb_moe_route_sigmoid", so.ssb_moe_route_sigmoid(lg.data_ptr(), T, 288, 8, bs.data_ptr(), 1, 1, 2.5,
+                                                                ids.data_ptr(), w.data_ptr(), _stream()))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(np.sort(ids.cpu().numpy(), axis=1), f["ids_sorted"])
+
+
 @pytest.mark.parametrize("rows,heads", [(300, 8), (1, 64), (1000, 64), (129, 3)])
 def test_gated_rmsnorm_nvfp4_equals_norm_then_quantize(cuda, rows, heads):
     """ssb_gated_rmsnorm_nvfp4 writes the same codes and scale atoms as ssb_gated_rmsnorm followed by

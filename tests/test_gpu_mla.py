@@ -5,7 +5,8 @@ shuffled page order, ragged selections (-1 padding, rows with one token, rows wi
 
 Tolerances: outputs within 3e-2 relative L2 per row of the float64 attention over the same e4m3 query and cache
 bytes (the softmax weights enter the P.V product as e4m3, as in the reference's FP8 kernel: ~1.5e-2 measured on the
-CPU model of that rounding); rows with no token are zeros; the cache append and the query pack bit-exact."""
+CPU model of that rounding), and within 8e-3 of the oracle that rounds them at the same point
+(oracle/mla.sparse_mla_fp8p); rows with no token are zeros; the cache append and the query pack bit-exact."""
 
 import numpy as np
 import pytest
@@ -19,6 +20,7 @@ REQS = [(0, 40), (500, 17), (2000, 9)]          # (position of the first query r
 NIDX = 600
 SCALE = 192 ** -0.5
 TOL = 3e-2
+TOL_FP8P = 8e-3       # against the oracle that rounds the softmax weights where the kernel does (sparse_mla_fp8p)
 
 
 def _paged(rng, reqs):
@@ -69,6 +71,7 @@ def test_sparse_mla_matches_oracle(cuda, q_scale, k_scale):
     for r, (s, n) in enumerate(REQS):
         sl = slice(qsl[r], qsl[r + 1])
         want = omla.sparse_mla(q8[sl], kv8, idx[sl, :NIDX], table[r], bmm1, bmm2)
+        want8 = omla.sparse_mla(q8[sl], kv8, idx[sl, :NIDX], table[r], bmm1, bmm2, p_fp8=True)
         for i in range(n):
             g, w = got[qsl[r] + i], want[i]
             if not (idx[qsl[r] + i, :NIDX] >= 0).any():
@@ -76,6 +79,8 @@ def test_sparse_mla_matches_oracle(cuda, q_scale, k_scale):
                 continue
             err = np.linalg.norm(g - w) / np.linalg.norm(w)
             assert err < TOL, (r, i, err)
+            err8 = np.linalg.norm(g - want8[i]) / np.linalg.norm(want8[i])
+            assert err8 < TOL_FP8P, (r, i, err8)
 
 
 def test_sparse_mla_expanded_layout(cuda):
@@ -104,9 +109,12 @@ def test_sparse_mla_expanded_layout(cuda):
     qsl = np.array([0, T], np.int32)
     got = _run(cuda, q8, kv8, idx, qsl, table, SCALE, 1.0, n_idx)
     want = omla.sparse_mla(q8, kv8, idx, table[0], SCALE, 1.0)
+    want8 = omla.sparse_mla(q8, kv8, idx, table[0], SCALE, 1.0, p_fp8=True)
     for r in range(T):
         err = np.linalg.norm(got[r] - want[r]) / np.linalg.norm(want[r])
         assert err < TOL, (positions[r], err)
+        err8 = np.linalg.norm(got[r] - want8[r]) / np.linalg.norm(want8[r])
+        assert err8 < TOL_FP8P, (positions[r], err8)
 
 
 @pytest.mark.parametrize("k_scale", [1.0, 0.37])

@@ -77,6 +77,40 @@ def test_moe_layer_matches_oracle(cuda, T, H, F, E, k):
     assert rel < LAYER_TOL, rel
 
 
+@pytest.mark.parametrize("T,H,F,E,k,n_group,topk_group", [
+    (600, 512, 256, 288, 8, 1, 1),     # the reference model's routing with its 288 experts (H, F scaled down)
+    (300, 256, 128, 64, 4, 8, 4),      # grouped selection
+])
+def test_moe_layer_sigmoid_routing(cuda, T, H, F, E, k, n_group, topk_group):
+    """The whole layer with the reference model's routing (sigmoid scores + correction bias, scale 5/2): routing and
+    permutation bit-exact against the oracle on the layer's own logits, the output within the per-layer bar."""
+    from ssengine_b200 import moe, weights
+
+    p = weights.moe_logical(9, H, F, E, routing="sigmoid", n_group=n_group, topk_group=topk_group)
+    x = weights.hidden_states(10, T, H)
+    layer = moe.MoELayer.from_logical(p, k, cuda)
+    out = layer(x.to(cuda))
+    torch.cuda.synchronize()
+    layer.check_status()
+    pn = weights.to_numpy(p)
+    logits = layer.ws_view("LOGITS", T, torch.float32, (T, E)).cpu().numpy()
+    ids = layer.ws_view("IDS", T, torch.int32, (T, k)).cpu().numpy()
+    wts = layer.ws_view("WEIGHTS", T, torch.float32, (T, k)).cpu().numpy()
+    r = pn["route"]
+    rid, rw = omoe.route_sigmoid_bias(logits, k, r["bias"], n_group, topk_group, r["scale"])
+    np.testing.assert_array_equal(ids, rid)
+    np.testing.assert_allclose(wts, rw, rtol=1.2e-7, atol=0)
+    counts, offsets, rows, _ = omoe.permutation(ids, E)
+    np.testing.assert_array_equal(layer.ws_view("ROWS", T, torch.int32, (T, k)).cpu().numpy(), rows)
+    np.testing.assert_array_equal(layer.ws_view("OFFSETS", T, torch.int32, (E + 2,)).cpu().numpy(), offsets)
+    o = out.float().cpu().numpy()
+    xf = x.float().numpy()
+    ref_same = omoe.moe_forward(xf, pn, k, ids=ids, weights=wts)
+    assert np.linalg.norm(o - ref_same) / np.linalg.norm(ref_same) < LAYER_TOL
+    ref = omoe.moe_forward(xf, pn, k)
+    assert np.linalg.norm(o - ref) / np.linalg.norm(ref) < LAYER_TOL
+
+
 def test_moe_layer_is_deterministic(cuda):
     layer, p, x, out = run_layer(cuda, 777, 512, 256, 16, 4, seed=5)
     again = layer(x.to(cuda))

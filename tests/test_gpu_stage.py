@@ -61,7 +61,6 @@ def plan_of(rng, lens, vocab):
 
 
 def test_two_stage_forward_matches_oracle(cuda):
-    from ssengine_b200 import layout, weights
     from ssengine_b200.stage import StageModel
 
     cfg = tiny_cfg()
@@ -78,7 +77,6 @@ def test_two_stage_forward_matches_oracle(cuda):
     for s in (s0, s1):
         for layer in s.layers:
             layer.check_status()
-    assert int(s1.last_status.item()) == 0
 
     # stage 0 in the oracle: embedding rows in row order, then x + MoE(x)
     ids = np.concatenate([np.asarray(plan.chunks[i].token_ids) for i in b0.order])
@@ -94,10 +92,9 @@ def test_two_stage_forward_matches_oracle(cuda):
     assert s1.prepare(plan).last_rows.cpu().tolist() == last_rows
     logits = s1.last_logits.cpu().numpy()
     np.testing.assert_array_equal(tokens.cpu().numpy(), ostage.argmax_lowest(logits))
-    codes = layout.unpack_codes(s1.head_codes)[: cfg.vocab].cpu().numpy()
-    sf = layout.atoms_to_sf(s1.head_sf, s1.head_codes.shape[0], cfg.hidden)[: cfg.vocab].cpu().numpy()
-    ref_logits = ostage.head_logits(s1.last_normed.float().cpu().numpy(), codes, sf, s1.head_gs, weights.GS_X)
-    assert np.linalg.norm(logits - ref_logits) / np.linalg.norm(ref_logits) < 1e-3
+    # the BF16 lm_head: fp32 logits of the bf16 normed rows against float64 (cuBLAS accumulates in fp32)
+    ref_logits = s1.last_normed.double().cpu().numpy() @ s1.head_w.double().cpu().numpy().T
+    assert np.linalg.norm(logits - ref_logits) / np.linalg.norm(ref_logits) < 1e-4
     normed_ref = ostage.rmsnorm(s1.layers[0](hidden).float().cpu().numpy()[last_rows], np.ones(cfg.hidden), 1e-5)
     assert np.abs(s1.last_normed.float().cpu().numpy() - normed_ref).max() < 2e-2 * np.abs(normed_ref).max()
     assert tokens.dtype == torch.int64 and tokens.shape == (3,)

@@ -17,16 +17,17 @@ def plans(vocab):
     rng = np.random.default_rng(9)
     ta = rng.integers(0, vocab, 60).tolist()
     tb = rng.integers(0, vocab, 30).tolist()
-    p1 = Plan(0, [Chunk("a", 0, 40, [3], [2, 0, 0, 0, 0, 0], False, ta[:40]),
-                  Chunk("b", 0, 30, [5], [3, 0, 0, 0, 0, 0], True, tb)])
-    p2 = Plan(1, [Chunk("a", 40, 20, [3], [2, 0, 0, 0, 0, 0], True, ta[40:])])
+    # KV pages in block 1; six distinct state blocks per request (the reference's block contract)
+    p1 = Plan(0, [Chunk("a", 0, 40, [67], [2, 3, 4, 5, 6, 7], False, ta[:40]),
+                  Chunk("b", 0, 30, [69], [8, 9, 10, 11, 12, 13], True, tb)])
+    p2 = Plan(1, [Chunk("a", 40, 20, [67], [2, 3, 4, 5, 6, 7], True, ta[40:])])
     return p1, p2
 
 
 def test_two_stages_equal_one(cuda):
     from ssengine_b200.stage import StageConfig, StageModel
 
-    base = dict(hidden=512, inter=256, experts=16, top_k=4, vocab=1000, num_blocks=8, mb_tokens=256, seed=4,
+    base = dict(hidden=512, inter=256, experts=16, top_k=4, vocab=1000, num_blocks=14, mb_tokens=256, seed=4,
                 layer_kind="kda", kda_heads=2)
     whole = StageModel(StageConfig(layer_split=(2,), **base), 0, cuda)
     s0 = StageModel(StageConfig(layer_split=(1, 1), **base), 0, cuda)
@@ -48,7 +49,7 @@ def test_hybrid_two_stages_equal_one(cuda):
     from ssengine_b200.messages import Chunk, Plan
     from ssengine_b200.stage import StageConfig, StageModel
 
-    base = dict(hidden=512, inter=256, experts=16, top_k=4, vocab=1000, num_blocks=8, mb_tokens=256, seed=6,
+    base = dict(hidden=512, inter=256, experts=16, top_k=4, vocab=1000, num_blocks=14, mb_tokens=256, seed=6,
                 layer_kind="hybrid", kda_heads=2, q_lora=256, mla_nope=64)
     whole = StageModel(StageConfig(layer_split=(4,), **base), 0, cuda)
     s0 = StageModel(StageConfig(layer_split=(2, 2), **base), 0, cuda)
@@ -56,9 +57,9 @@ def test_hybrid_two_stages_equal_one(cuda):
     assert whole.is_dsa == [False, False, False, True] and s1.is_dsa == [False, True]
     rng = np.random.default_rng(10)
     ta, tb = rng.integers(0, 1000, 170).tolist(), rng.integers(0, 1000, 30).tolist()
-    plans = [Plan(0, [Chunk("a", 0, 130, [3, 4], [2, 0, 0, 0, 0, 2], False, ta[:130]),
-                      Chunk("b", 0, 30, [5], [3, 0, 0, 0, 0, 3], True, tb)]),
-             Plan(1, [Chunk("a", 130, 40, [3, 4], [2, 0, 0, 0, 0, 2], True, ta[130:])])]
+    plans = [Plan(0, [Chunk("a", 0, 130, [67, 68], [2, 3, 4, 5, 6, 7], False, ta[:130]),
+                      Chunk("b", 0, 30, [69], [8, 9, 10, 11, 12, 13], True, tb)]),
+             Plan(1, [Chunk("a", 130, 40, [67, 68], [2, 3, 4, 5, 6, 7], True, ta[130:])])]
     for plan in plans:
         t_whole = whole.forward(plan)
         t_split = s1.forward(plan, s0.forward(plan))

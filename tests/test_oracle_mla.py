@@ -32,3 +32,13 @@ def test_e4m3_saturates():
 def test_quantize_scale_in_fp32():
     x = np.array([1.0, 3.0, 100.0], np.float32)
     np.testing.assert_array_equal(omla.quantize(x, 3.0), omla.e4m3_encode(x * (np.float32(1) / np.float32(3.0))))
+
+
+def test_fast_e4m3_encoder_equals_the_float64_restatement():
+    rng = np.random.default_rng(12)
+    x = np.concatenate([rng.standard_normal(200_000).astype(np.float32) * s for s in (1e-4, 1e-2, 1.0, 40.0, 600.0)])
+    codes = np.arange(256, dtype=np.uint8)
+    vals = omla.e4m3_decode(codes[(codes & 0x7F) != 0x7F]).astype(np.float32)
+    x = np.concatenate([x, vals, np.nextafter(vals, np.float32(np.inf)), np.nextafter(vals, np.float32(-np.inf)),
+                        np.array([0.0, -0.0, 464.0, 480.0, -1e9], np.float32)])
+    np.testing.assert_array_equal(omla.e4m3_encode(x), omla.e4m3_encode_reference(x))

@@ -36,3 +36,57 @@ def test_plan_fields_mirror_the_reference_messages():
     assert Plan(7, [c, c]).num_tokens == 6
     assert list(Chunk.__dataclass_fields__) == ["req_id", "start", "num_tokens", "kv_pages", "state_blocks", "is_last",
                                                 "token_ids"]
+
+
+def test_kda_state_groups_match_the_reference_known_answer():
+    """The reference's known answer for its 45-layer split (tests/test_model_cpu.py:147-160 of the reference): KDA
+    state group 0 (g2, state_blocks[0]) holds layers 0, 6, 13, 20, 26, 33, 40; every KDA layer has a group 0..4."""
+    from ssengine_b200.kvpages import kda_group
+
+    dsa = lambda i: i % 4 == 3
+    groups = {i: kda_group(i, dsa) for i in range(45) if not dsa(i)}
+    assert [i for i, g in groups.items() if g == 0] == [0, 6, 13, 20, 26, 33, 40]
+    assert set(groups.values()) == {0, 1, 2, 3, 4}
+
+
+def test_state_pages_alias_the_dsa_latent_blocks():
+    """Stage 0 of the 12/11/11/11 split: the i-th KDA layer of group g keeps its state in the i-th DSA layer's latent
+    tensor, block state_blocks[g]: conv state at the block's start, recurrent state after it (256-byte aligned: 3 x 3 x 256 bf16 = 4,608 bytes for 2 heads)."""
+    import torch
+
+    from ssengine_b200.kvpages import BLOCK_TOKENS, LATENT_ROW, StageKv
+
+    kv = StageKv(range(12), lambda i: i % 4 == 3, 3, 2, "cpu")
+    assert kv.dsa_layers == [3, 7, 11] and len(kv.pages) == 3
+    assert [kv.group[i] for i in kv.kda_layers] == [0, 1, 2, 3, 4, 0, 1, 2, 3]
+    assert [kv.slot[i] for i in kv.kda_layers] == [0, 0, 0, 0, 0, 1, 1, 1, 1]
+    page = BLOCK_TOKENS * LATENT_ROW
+    base = kv.pages[1].data_ptr()
+    conv, rec = kv.conv_state(6), kv.rec_state(6)          # layer 6: group 0, second of its group -> DSA layer 7
+    assert conv[2].data_ptr() - base == 2 * page and kv.state_offsets(6, 2) == (2 * page, 2 * page + 4608)
+    assert rec[2].data_ptr() - base == 2 * page + 4608
+    assert conv.shape == (3, 3, 768) and rec.shape == (3, 2, 128, 128) and rec[1].is_contiguous()
+    assert kv.latent(7).shape == (3 * BLOCK_TOKENS, LATENT_ROW) and kv.latent(7).data_ptr() == base
+    rec[1].fill_(1.0)
+    conv[1].fill_(2.0)
+    raw = kv.pages[1][1]
+    assert torch.equal(raw[4608:4608 + 2 * 128 * 128 * 4].view(torch.float32), torch.ones(2 * 128 * 128))
+    assert (raw[:4608].view(torch.bfloat16) == 2.0).all() and not raw[4608 + 2 * 128 * 128 * 4:].any()
+
+
+def test_block_contract_is_checked():
+    import pytest
+
+    from ssengine_b200.messages import Chunk
+    from ssengine_b200.stage import check_blocks
+
+    ok = [Chunk("a", 0, 3, [67], [2, 3, 4, 5, 6, 7], True, None), Chunk("b", 0, 3, [68], [8, 9, 10, 11, 12, 13], True,
+                                                                     None)]
+    check_blocks(ok, 14)
+    check_blocks([Chunk("w", 0, 3, [1], [0] * 6, True, None)], 2)           # the null block for a dummy request
+    with pytest.raises(ValueError, match="held twice"):
+        check_blocks([ok[0], Chunk("b", 0, 3, [68], [2, 9, 10, 11, 12, 13], True, None)], 14)
+    with pytest.raises(ValueError, match="both KV and state"):
+        check_blocks([Chunk("a", 0, 3, [67 * 2], [2, 3, 4, 5, 6, 7], True, None)], 14)
+    with pytest.raises(ValueError, match="outside the pool"):
+        check_blocks([Chunk("a", 0, 3, [67], [2, 3, 4, 5, 6, 70], True, None)], 14)
