@@ -131,7 +131,7 @@ def nvfp4_linear(x, codes, sf, gs_w, gs_in):
 
     xc, xs = nvfp4.quantize(np.asarray(x, np.float32), gs_in)
     xq = nvfp4.dequantize(xc, xs, gs_in).astype(np.float64)
-    w = nvfp4.dequantize(codes, sf, gs_w).astype(np.float64)
+    w = nvfp4.dequantize_weight(codes, sf, gs_w, np.float64)
     return xq @ w.T
 
 

@@ -43,7 +43,8 @@ def dense_ffn(y, w, gs_x: float, gs_h: float) -> np.ndarray:
     xq, xs = nvfp4.quantize(np.asarray(y, np.float32), gs_x)
     xd = nvfp4.dequantize(xq, xs, gs_x)
     F = c1.shape[0] // 2
-    return bf16(omoe.expert_ffn(xd, nvfp4.dequantize(c1, s1, g1), nvfp4.dequantize(c2, s2, g2), gs_h, F))
+    return bf16(omoe.expert_ffn(xd, nvfp4.dequantize_weight(c1, s1, g1), nvfp4.dequantize_weight(c2, s2, g2), gs_h,
+                                F))
 
 
 def dsa_block(y, p, positions, reqs, kv_cache, pool_cache, tail, gs_in: float):

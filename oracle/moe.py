@@ -172,7 +172,7 @@ def moe_forward(x, p: dict, k: int, ids=None, weights=None, return_parts: bool =
     if lazy:
         # one expert's fp32 weights at a time (full-size layers on a row sample: 129 experts of 12.6M elements would
         # take 6.5 GB at once)
-        dense = {"router": nvfp4.dequantize(*p["router"]), "experts": None}
+        dense = {"router": nvfp4.dequantize_weight(*p["router"]), "experts": None}
     elif dense is None:
         dense = dequantize_params(p)
     logits = (xd @ dense["router"].T).astype(np.float32)
@@ -194,7 +194,7 @@ def moe_forward(x, p: dict, k: int, ids=None, weights=None, return_parts: bool =
             continue
         if lazy:
             c1, s1, g1, c2, s2, g2 = p["experts"][e]
-            w1d, w2d = nvfp4.dequantize(c1, s1, g1), nvfp4.dequantize(c2, s2, g2)
+            w1d, w2d = nvfp4.dequantize_weight(c1, s1, g1), nvfp4.dequantize_weight(c2, s2, g2)
         else:
             w1d, w2d = dense["experts"][e]
         y = expert_ffn(xd[tok], w1d, w2d, p["gs_h"], F, intermediates)

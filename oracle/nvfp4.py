@@ -137,6 +137,23 @@ def dequantize(codes, sf, gs: float) -> np.ndarray:
     return (v / np.float32(gs)).astype(np.float32).reshape(R, K)
 
 
+# Weight dequantization memo for timing runs (the CPU baseline dequantizes its weights once, in its warm-up, and then
+# times the arithmetic): None = off (the default; tests never use it), else a dict keyed by the arrays' identities.
+# The caller keeps the weight arrays alive while the memo is on and clears it afterwards.
+WEIGHT_MEMO: dict | None = None
+
+
+def dequantize_weight(codes, sf, gs: float, dtype=np.float32) -> np.ndarray:
+    """`dequantize` of a weight tensor (as `dtype`), through WEIGHT_MEMO when it is on."""
+    if WEIGHT_MEMO is None:
+        return dequantize(codes, sf, gs).astype(dtype, copy=False)
+    key = (id(codes), id(sf), float(gs), np.dtype(dtype).str)
+    w = WEIGHT_MEMO.get(key)
+    if w is None:
+        w = WEIGHT_MEMO[key] = dequantize(codes, sf, gs).astype(dtype, copy=False)
+    return w
+
+
 def pack(codes) -> np.ndarray:
     """codes [R, K] -> bytes [R, K // 2], element 2i in the low nibble."""
     codes = np.asarray(codes, dtype=np.uint8)

@@ -271,8 +271,25 @@ class KdaDecoderLayer:
         res_b = torch.empty_like(res)
         post_b, comb_b = torch.empty(T, 4, **f32), torch.empty(T, 4, 4, **f32)
         self.bound_b(x_a, res_a, post_a, comb_a, res_b, post_b, comb_b, y, stream)
-        x_b = self.moe.forward(y, stream=stream)
+        x_b = _ffn_forward(self, y, stream)
         return res_b, x_b, post_b, comb_b
+
+
+def _ffn_forward(layer, y, stream):
+    """The decoder layer's FFN; with `layer.moe_profile` a list, a MoE layer runs its per-step profiled form and
+    appends its events (len(lib.MOE_STEPS) + 1, recorded around each launch step)."""
+    from . import moe
+
+    prof = getattr(layer, "moe_profile", None)
+    if prof is None or not isinstance(layer.moe, moe.MoELayer):
+        return layer.moe.forward(y, stream=stream)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(lib.MOE_STEPS) + 1)]
+    for e in evs:
+        e.record()                                      # creates the events the library records into
+    out = torch.empty_like(y)
+    layer.moe.forward_profiled(y, out, evs, stream=stream)
+    prof.append(evs)
+    return out
 
 
 def _make_ffn(seed: int, hidden: int, inter: int, experts: int, top_k: int, device, ffn: str, routing: dict | None,
@@ -515,5 +532,5 @@ class DsaDecoderLayer:
         res_b = torch.empty_like(res)
         post_b, comb_b = torch.empty(T, 4, **f32), torch.empty(T, 4, 4, **f32)
         self.bound_b(x_a, res_a, post_a, comb_a, res_b, post_b, comb_b, y, stream)
-        x_b = self.moe.forward(y, stream=stream)
+        x_b = _ffn_forward(self, y, stream)
         return res_b, x_b, post_b, comb_b

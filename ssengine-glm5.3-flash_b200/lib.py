@@ -72,6 +72,38 @@ class MhcParamsC(ctypes.Structure):
 
 _LIB = None
 
+# Kernels each entry point launches (1 unless listed), for the count of this library's launches in a timed region
+KERNELS_PER_CALL = {"ssb_moe_forward": 10, "ssb_moe_forward_profiled": 10, "ssb_mhc_ws": 2,
+                    "ssb_kda_prefill": 2, "ssb_kda_prefill_ws": 2, "ssb_kpool_insert": 2, "ssb_stage_metadata": 2}
+
+
+class _Counting:
+    """The loaded library with a launch counter: every entry-point call adds its kernel count to `launches` while
+    `on` is set."""
+
+    def __init__(self, lib):
+        self._lib = lib
+        self.on = False
+        self.launches = 0
+        self._wrapped = {}
+
+    def __getattr__(self, name):
+        fn = getattr(self._lib, name)
+        if not name.startswith("ssb_"):
+            return fn
+        w = self._wrapped.get(name)
+        if w is None:
+            k = KERNELS_PER_CALL.get(name, 1)
+            counter = self
+
+            def w(*args, _fn=fn, _k=k):
+                if counter.on:
+                    counter.launches += _k
+                return _fn(*args)
+
+            self._wrapped[name] = w
+        return w
+
 _P, _I32, _I64, _F = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
 _SIGS = {
     "ssb_version": ([], ctypes.c_char_p),
@@ -132,7 +164,8 @@ MOE_STEPS = ("quantize", "router_gemm", "route", "count", "offsets", "scatter", 
 
 
 def load(path: Path | None = None):
-    """Load the library (once). Raises FileNotFoundError / AttributeError when it is missing or incomplete."""
+    """Load the library (once). Raises FileNotFoundError / AttributeError when it is missing or incomplete. The shared
+    instance counts this library's kernel launches while `load().on` is set (`load().launches`)."""
     global _LIB
     if _LIB is not None and path is None:
         return _LIB
@@ -146,7 +179,8 @@ def load(path: Path | None = None):
         fn.argtypes = args
         fn.restype = res
     if path is None:
-        _LIB = lib
+        _LIB = _Counting(lib)
+        return _LIB
     return lib
 
 

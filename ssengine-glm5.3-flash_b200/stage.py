@@ -185,6 +185,7 @@ class StageModel:
         self.cuda_graphs = cfg.cuda_graphs if cuda_graphs is None else cuda_graphs
         self.ipc_kv = ipc_kv
         self.layer_hook = None          # optional callable(layer, res, x_prev, post, comb) after each layer (checks)
+        self.moe_profile = None         # optional list: each MoE layer's forward records per-step CUDA events into it
         self._lib = lib.load()
         H, F, E = cfg.hidden, cfg.inter, cfg.experts
         if self.kda:
@@ -339,9 +340,13 @@ class StageModel:
         return Batch(T, order, positions[:rows_out], slots[:rows_out], table[: R * width].view(R, width),
                      v.get("tok"), v["last"], bucket, keep=[host, dev], kda_seqs=v.get("kda"), dsa=dsa)
 
-    def run(self, batch: Batch, hidden_in: torch.Tensor | None) -> torch.Tensor:
+    def run(self, batch: Batch, hidden_in: torch.Tensor | None, edge_out=None) -> torch.Tensor | None:
+        """edge_out: a device address, or a callable returning one when called right before the last kernel (the
+        next stage's receive slot, a peer pointer), into which a non-last hybrid stage's final boundary kernel stores
+        its [T, 4H] rows directly (the fused stage edge); the call then returns None. Without it the rows come back as
+        a fresh tensor (the reference's contract)."""
         if self.kda:
-            return self._run_kda(batch, hidden_in)
+            return self._run_kda(batch, hidden_in, edge_out)
         T, H = batch.num_tokens, self.hidden_width
         s = lib.stream_ptr()
         if self.first:
@@ -358,7 +363,7 @@ class StageModel:
             return x
         return self._head(x, batch.last_rows)
 
-    def _run_kda(self, batch: Batch, hidden_in: torch.Tensor | None) -> torch.Tensor:
+    def _run_kda(self, batch: Batch, hidden_in: torch.Tensor | None, edge_out=None):
         """KDA + MoE decoder layers on the 4-stream residual: stage 0 expands its embeddings (hc_expand), a later stage
         starts from the received residual with a pre-only boundary (edge_recv); a stage that is not the last ends with
         a post-only boundary into the [T, 4H] rows it sends (edge_send, ssengine/model/pp_patch.py:156-163); the last
@@ -376,6 +381,8 @@ class StageModel:
                 raise ValueError(f"stage {self.stage} needs hidden_in bf16 [{T}, {4 * H}]")
             res = hidden_in.view(T, 4, H)
         x_prev = post = comb = None
+        for layer in self.layers:
+            layer.moe_profile = self.moe_profile
         for layer, state, dsa, grp in zip(self.layers, self.kda_states, self.is_dsa, self.kda_group):
             if dsa:
                 res, x_prev, post, comb = layer.forward(res, x_prev, post, comb, batch.dsa, state, self.status)
@@ -384,11 +391,15 @@ class StageModel:
                                                         self.status)
             if self.layer_hook is not None:
                 self.layer_hook(layer, res, x_prev, post, comb)
+        if edge_out is not None and not self.last and x_prev is not None:
+            dst = edge_out() if callable(edge_out) else edge_out
+            self._edge_post(x_prev, res, post, comb, dst)              # straight into the peer's receive slot
+            return None
         out = torch.empty(T, 4, H, dtype=torch.bfloat16, device=self.device)
         if x_prev is None:
             out.copy_(res)
         else:
-            self._edge_post(x_prev, res, post, comb, out)
+            self._edge_post(x_prev, res, post, comb, out.data_ptr())
         if not self.last:
             return out.view(T, 4 * H)
         n = batch.last_rows.shape[0]
@@ -397,13 +408,12 @@ class StageModel:
                                                        merged.data_ptr(), s))
         return self._head(merged[:n], torch.arange(n, dtype=torch.int64, device=self.device))
 
-    def _edge_post(self, x, res, post, comb, out) -> None:
-        """Post-only boundary: out = post * x + comb^T res (the last sub-block's rows folded into the residual)."""
-        import ctypes
-
+    def _edge_post(self, x, res, post, comb, out_ptr: int) -> None:
+        """Post-only boundary: out = post * x + comb^T res (the last sub-block's rows folded into the residual), stored
+        at device address out_ptr ([T, 4, H] bf16)."""
         b = self.layers[-1].bound_b
         rc = self._lib.ssb_mhc(ctypes.byref(b._c), x.data_ptr(), res.data_ptr(), post.data_ptr(), comb.data_ptr(),
-                               out.data_ptr(), None, None, None, res.shape[0], lib.stream_ptr())
+                               out_ptr, None, None, None, res.shape[0], lib.stream_ptr())
         lib.check("ssb_mhc", rc)
 
     def forward(self, plan, hidden_in: torch.Tensor | None = None) -> torch.Tensor:

@@ -90,3 +90,27 @@ def test_block_contract_is_checked():
         check_blocks([Chunk("a", 0, 3, [67 * 2], [2, 3, 4, 5, 6, 7], True, None)], 14)
     with pytest.raises(ValueError, match="outside the pool"):
         check_blocks([Chunk("a", 0, 3, [67], [2, 3, 4, 5, 6, 70], True, None)], 14)
+
+
+def test_microbatch_former_covers_every_token_and_keeps_the_block_contract():
+    import numpy as np
+
+    from ssengine_b200.schedule import blocks_needed, microbatches, prompt_lengths
+    from ssengine_b200.stage import check_blocks
+
+    lens = prompt_lengths(40, seed=3)
+    assert lens.max() <= 131072 and 4000 < np.median(lens) < 16000
+    plans, high = microbatches(lens, 8192, 10_000, vocab=100)
+    assert blocks_needed(plans) <= high + 1
+    seen = {}
+    for p in plans:
+        assert sum(c.num_tokens for c in p.chunks) <= 8192
+        check_blocks(p.chunks, high + 1)
+        for c in p.chunks:
+            assert c.start == seen.get(c.req_id, 0) and len(c.token_ids) == c.num_tokens
+            assert len(c.kv_pages) * 128 >= c.start + c.num_tokens
+            seen[c.req_id] = c.start + c.num_tokens
+            if c.is_last:
+                assert seen[c.req_id] == lens[int(c.req_id[1:])]
+    assert sorted(seen.values()) == sorted(lens.tolist())          # every prompt fully prefilled
+    assert all(sum(c.num_tokens for c in p.chunks) == 8192 for p in plans[:-1])
