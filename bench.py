@@ -1,19 +1,30 @@
 #!/usr/bin/env python
-"""Prefill-stage benchmark on B200: one NVFP4 MoE layer over an 8,192-token microbatch.
+"""Prefill benchmark on B200s: the Glm5Next NVFP4 model as a pipeline of stages, one process per
+GPU; or one NVFP4 MoE layer (`--workload moe-layer`).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|vllm-cutlass] [--tokens T]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|vllm-cutlass] [--workload ...]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...      (N > 1)
 
-One JSON line on rank 0. A step is one forward of the layer (quantize -> router GEMM -> top-8 routing -> permutation
--> grouped NVFP4 gate_up GEMM + SwiGLU + requant -> grouped down GEMM -> weighted combine + shared expert) over T
-tokens with the inputs resident in HBM; `e2e` is the same metric through the public API (`MoELayer.forward`) with
-every step's input copied from pinned host memory and its output read back inside the timed region (consecutive
-steps' copies and forwards overlapped on three streams, as a serving loop runs them). At N > 1 every rank
-runs its own replica on its own microbatch (weak scaling, no collective on the data path); the time is the max over
-ranks. `--impl reference` times the CPU restatement of the path (the reference has no CPU implementation of its
-own; its GPU path needs a vLLM fork and FlashInfer builds absent here) on the host cores, rank 0 only.
-`--impl vllm-cutlass` is a library comparison on the GPU, rank 0 only: the same experts (same NVFP4 codes, scales
-and global scales, the routing of our router) through the NVFP4 MoE of the vLLM 0.22.0 installed in the image
-(`run_cutlass_moe_fp4`, CUTLASS sm_100 grouped GEMMs); its line reports the expert path, and ours beside it.
+Pipeline workload (the default; the metric "prefill tok/s, 1 stage + PP2/4/8"): the 45-layer random-init Glm5Next
+(hidden 4096; KDA layers with 64 heads of 128; DSA layers 3, 7, ..., 43 with 64 MLA heads, latent 512 + rope 64 in
+e4m3, indexer 32 x 128 top-512 pools; layers 0-2 with the dense SwiGLU FFN 4096 -> 2 x 12288 -> 4096; the others 128
+experts top-8 + 1 shared, F 1024, with the model's sigmoid + correction-bias routing; vocab 151,552) split into N
+pipeline stages -- N = 1: the whole model as one stage; 2: 23/22; 4: 12/11/11/11; 8: 6/6/6/6/6/5/5/5 -- one stage per
+GPU, joined by the P2P stage edge (each stage's last kernel stores its [T, 16384] rows into the next GPU's receive
+slot; bounded flag waits; no NCCL on the activation path; gloo only for start-up and the timing reductions). The
+input stream: 256 cold prompts with lognormal lengths (median 8,192, capped at 131,072), uniform token ids, cut
+first-come-first-served into 8,192-token microbatches with KV pages and state blocks from one block pool
+(`ssengine_b200.schedule`). A step is one microbatch; K microbatches are timed after W warm-up microbatches, the
+time being each rank's CUDA-event span from its first timed microbatch to its last, the maximum over ranks; `value`
+= the K microbatches' tokens / that time (strong scaling: the model is fixed, N stages share it). The line also
+carries the pipeline-bubble fraction, stage 0's 12-layer slice (the PP4 stage-0 layers, timed inside the N = 1 run),
+the MoE gate_up GEMM's roofline and the model's algorithmic FLOP rate. `e2e`: the same K microbatches through the
+public path with each microbatch's plan metadata and token ids packed on the host and copied in (`prepare`) and the
+last stage's greedy tokens copied back to pinned host memory, inside the timed region.
+
+`--impl reference` times the reference's path on the host cores: the reference has no CPU implementation (its GPU path
+needs a vLLM fork and FlashInfer builds absent here), so it times this repository's CPU restatement (oracle/) of each
+layer kind on a bounded sample of a microbatch (rank 0 only), with weights built on the host without the CUDA library.
 """
 
 from __future__ import annotations
@@ -32,20 +43,26 @@ sys.path.insert(0, str(ROOT))
 
 H, F, E, K_TOP = 4096, 1024, 128, 8
 SEED = 20261201
-PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch at T = 8192, from the ncu capture summarised in
 # profiles/gemm_nvfp4_moe_T8192_full.md (796.9 MB + 39.6 MB); None for other token counts
 GATE_UP_TRAFFIC_T8192 = 836.4e6
+BASELINE_PP4_TOK_S = 138_400.0        # the reference's saturated 8k prefill at PP4 on 4 x B200
+N_LAYERS, MB_TOKENS, N_PROMPTS = 45, 8192, 256
+MODEL = dict(hidden=4096, inter=1024, experts=128, top_k=8, vocab=151_552, kda_heads=64, q_lora=1536, mla_nope=192,
+             mla_v_dim=256, dense_layers=3, dense_inter=12288, routing="sigmoid", layer_kind="hybrid")
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["ours", "reference", "vllm-cutlass"], default="ours")
-    ap.add_argument("--tokens", type=int, default=8192)
-    ap.add_argument("--cpu-tokens", type=int, default=1024, help="CPU baseline sample (tokens)")
+    ap.add_argument("--workload", choices=["pipeline", "moe-layer"], default="pipeline")
+    ap.add_argument("--layers", type=int, default=N_LAYERS, help="pipeline: model layers (45 = BASELINE config 4)")
+    ap.add_argument("--tokens", type=int, default=MB_TOKENS, help="tokens per microbatch")
+    ap.add_argument("--cpu-tokens", type=int, default=16, help="CPU baseline sample (tokens)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true", help="skip the nvidia-smi window (profiling runs)")
@@ -186,7 +203,344 @@ def time_oracle(p: dict, dense: dict, x_np, reps: int = 1) -> float:
     return (time.perf_counter() - t0) / reps
 
 
-# ---------------------------------------------------------------------------------------------- runs
+
+
+# ---------------------------------------------------------------------------------------------- pipeline workload
+def split_for(n_stages: int, layers: int = N_LAYERS) -> tuple:
+    """Layers per stage: even splits with the remainder on the first stages -- the reference's 12/11/11/11 at PP4
+    (ssengine/kernels.py:277), 23/22 at PP2, 6/6/6/6/6/5/5/5 at PP8, all 45 layers as one stage at N = 1."""
+    base, extra = divmod(layers, n_stages)
+    return tuple(base + (1 if s < extra else 0) for s in range(n_stages))
+
+
+def pipeline_plans(n_mb: int, mb_tokens: int, vocab):
+    """The first n_mb microbatches of BASELINE config 4's prompt stream and the block pool they need."""
+    from ssengine_b200 import schedule
+
+    lengths = schedule.prompt_lengths(N_PROMPTS, SEED)
+    plans, high = schedule.microbatches(lengths, mb_tokens, n_mb, vocab=vocab, seed=SEED)
+    return plans, high + 2                              # the null block and one spare
+
+
+def pipeline_workload(args, world: int) -> str:
+    return (f"BASELINE config 4: random-init Glm5Next NVFP4, {args.layers} layers (KDA 64 x 128; DSA at 3, 7, ...: "
+            f"64 MLA heads, e4m3 latent 512 + rope 64, indexer 32 x 128 top-512 pools; dense SwiGLU FFN in layers 0-2; "
+            f"128 experts top-8 + shared, F {F}, sigmoid + bias routing; vocab {MODEL['vocab']}), PP{world} split "
+            f"{'/'.join(map(str, split_for(world, args.layers)))}, {args.tokens}-token microbatches of {N_PROMPTS} cold "
+            f"prompts (lognormal lengths, median 8,192, max 131,072)")
+
+
+def microbatch_flops(plan, cfg, layers: int) -> float:
+    """Algorithmic FLOPs of one microbatch through `layers` layers and the head: 2 K N per token for every
+    projection, expert and FFN GEMM (router, 8 routed experts + the shared one, absorb / v_up, indexer projections),
+    the mHC mixes, the KDA chunked recurrence at ~4 products of 128 x 128 per token and head, the indexer score
+    32 x 128 x 2 per visible pool ((pos + 1) // 4) and the sparse MLA 64 heads x (576 + 512) x 2 per selected token
+    (min(2,051, pos + 1)), and the head on the finished rows."""
+    import numpy as np
+
+    Hd, P, nh = cfg.hidden, cfg.kda_heads * 128, cfg.kda_heads
+    pos = np.concatenate([np.arange(c.start, c.start + c.num_tokens) for c in plan.chunks]).astype(np.float64)
+    T = float(len(pos))
+    sel = float(np.minimum(2051, pos + 1).sum())
+    pools = float(((pos + 1) // 4).sum())
+    kda = 2 * Hd * (3 * P + 256 + nh) + 2 * 2 * 128 * P + 2 * P * Hd + 2 * 4 * 128 * 128 * nh
+    qh = cfg.mla_nope + 64
+    dsa = (2 * Hd * (cfg.q_lora + 576) + 2 * cfg.q_lora * 64 * qh + 2 * 64 * cfg.mla_nope * 512
+           + 2 * 64 * 512 * cfg.mla_v_dim + 2 * 64 * cfg.mla_v_dim * Hd + 2 * cfg.q_lora * 4096 + 2 * Hd * 288)
+    moe = 2 * Hd * cfg.experts + (cfg.top_k + 1) * (2 * Hd * 2 * cfg.inter + 2 * cfg.inter * Hd)
+    dense = 2 * Hd * 2 * cfg.dense_inter + 2 * cfg.dense_inter * Hd
+    mhc = 2 * 2 * 24 * 4 * Hd
+    total = 0.0
+    for i in range(layers):
+        is_dsa = i % 4 == 3
+        total += T * (mhc + (dsa if is_dsa else kda) + (dense if i < cfg.dense_layers else moe))
+        if is_dsa:
+            total += sel * 64 * (576 + 512) * 2 + pools * 32 * 128 * 2
+    n_last = sum(1 for c in plan.chunks if c.is_last)
+    return total + n_last * 2 * Hd * cfg.vocab
+
+
+def run_pipeline(args, rank: int, world: int, local: int) -> None:
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from ssengine_b200 import lib
+    from ssengine_b200.edge import P2pPipe
+    from ssengine_b200.stage import StageConfig, StageModel
+    from ssengine_b200.worker import StageWorker
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=180))
+    split = split_for(world, args.layers)
+    W, K = max(3, args.warmup), args.steps
+    plans, nb = pipeline_plans(W + K, args.tokens, MODEL["vocab"] if rank == 0 else None)
+    if len(plans) < W + K:
+        raise SystemExit(f"the prompt stream gives only {len(plans)} microbatches")
+    cfg = StageConfig(layer_split=split, mb_tokens=args.tokens, num_blocks=nb, seed=SEED % 997, **MODEL)
+    stage = StageModel(cfg, rank, device)
+    pipe = None
+    if world > 1:
+        pipe = P2pPipe(rank, world, device, None, max_in_flight=4, max_rows=args.tokens, width=stage.hidden_width,
+                       init_group=False, wait_ns=60_000_000_000)
+    worker = StageWorker(stage, pipe, events=True)
+    batches = [stage.prepare(p) for p in plans]
+    pack_bytes = [int(b.keep[0].numel()) for b in batches[W:]]
+    for b in batches[:W]:
+        worker.step(b)
+    torch.cuda.synchronize()
+    if pipe is not None:
+        pipe.check()
+    if int(stage.status.item()):
+        raise lib.SsbError("stage device status", int(stage.status.item()))
+
+    # N = 1: stage 0 of the PP4 split (layers 0-11) timed inside the forward by an event after layer 11
+    slice_ev = []
+    if world == 1 and len(stage.layers) >= 12:
+        eleventh = stage.layers[11]
+
+        def hook(layer, *_):
+            if layer is eleventh:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                slice_ev.append(ev)
+
+        stage.layer_hook = hook
+    marks = []
+    if rank == 0:
+        stage.moe_profile = []
+    clocks = Clocks(_gpu_id(device)) if rank == 0 and not args.no_clocks else None
+    if clocks is not None:
+        clocks.start()
+        time.sleep(0.3)
+    worker.spans.clear()
+    so = lib.load()
+    so.launches = 0
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    so.on = True
+    t0.record()
+    for b in batches[W:]:
+        if rank == 0:
+            marks.append(len(stage.moe_profile))
+        worker.step(b)
+    t1.record()
+    so.on = False
+    torch.cuda.synchronize()
+    clk = clocks.stop() if clocks is not None else None
+    if pipe is not None:
+        pipe.check()
+    if int(stage.status.item()):
+        raise lib.SsbError("stage device status", int(stage.status.item()))
+    elapsed = t0.elapsed_time(t1)
+    busy = worker.busy_ms()
+    launches = so.launches
+    slice_ms = sum(a.elapsed_time(e) for (a, _), e in zip(worker.spans, slice_ev)) if slice_ev else None
+    gate = None
+    if rank == 0:
+        marks.append(len(stage.moe_profile))
+        g_ms = g_fl = 0.0
+        for i in range(K):
+            T = batches[W + i].num_tokens
+            for evs in stage.moe_profile[marks[i]:marks[i + 1]]:
+                g_ms += evs[6].elapsed_time(evs[7])
+                g_fl += 2.0 * T * (K_TOP + 1) * 2 * F * H
+        gate = (g_ms, g_fl, marks[-1] - marks[0])
+        stage.moe_profile = None
+    stage.layer_hook = None
+
+    e2e_ms, d2h = None, 0
+    if not args.no_e2e:
+        worker.events = False
+        host_tok = torch.empty(4096, dtype=torch.int64, pin_memory=True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for p in plans[W:]:
+            out = worker.step(p)                       # plan -> pinned pack -> one H2D copy -> forward
+            if out is not None and out.numel():
+                host_tok[:out.numel()].copy_(out, non_blocking=True)
+                d2h += out.numel() * 8
+        e1.record()
+        torch.cuda.synchronize()
+        if pipe is not None:
+            pipe.check()
+        e2e_ms = e0.elapsed_time(e1)
+
+    mine = {"rank": rank, "elapsed": elapsed, "busy": busy, "e2e": e2e_ms, "launches": launches, "d2h": d2h}
+    allr = [mine]
+    if world > 1:
+        allr = [None] * world
+        dist.all_gather_object(allr, mine)
+    if rank == 0:
+        pk, src = peaks()
+        tokens = sum(b.num_tokens for b in batches[W:])
+        t_max = max(r["elapsed"] for r in allr)
+        value = tokens / (t_max / 1e3)
+        flops = sum(microbatch_flops(p, cfg, args.layers) for p in plans[W:])
+        sus = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+        fp4_sus = 4.0 * sus
+        g_ms, g_fl, n_g = gate
+        achieved = g_fl / (g_ms / 1e3) / 1e12 if g_ms else None
+        line = {
+            "metric": "prefill tok/s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": t_max / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": value / BASELINE_PP4_TOK_S if world == 4 else None,
+            "dtype": "nvfp4 (e2m1 x e2m1, ue4m3 per-16 scales) GEMMs; e4m3 attention; bf16 residual; fp32 KDA state",
+            "data": "synthetic: uniform token ids, lognormal prompt lengths, seeded random-init weights",
+            "config": {"workload": pipeline_workload(args, world), "global_batch": args.tokens,
+                       "seq_len": "lognormal median 8192, max 131072", "parallelism": f"pp{world}",
+                       "layer_split": list(split), "tokens_timed": tokens,
+                       "l2": "inputs larger than L2 (each stage streams >= 10 GB of weights per microbatch)"},
+            "pipeline": {"max_rank_ms": t_max, "per_rank_ms": [r["elapsed"] for r in allr],
+                         "per_rank_busy_ms": [r["busy"] for r in allr],
+                         "bubble_fraction": 1.0 - sum(r["busy"] for r in allr) / (world * t_max),
+                         "edge": "last boundary kernel stores into the next GPU's slot (P2P over NVLink), bounded "
+                                 "flag waits, no NCCL"},
+            "roofline": {"kernel": "MoE gate_up grouped NVFP4 GEMM (SwiGLU + requant epilogue), rank 0's MoE layers",
+                         "bound": "tensor", "achieved": achieved, "peak": fp4_sus, "unit": "TFLOP/s",
+                         "frac": achieved / fp4_sus if achieved else None,
+                         "traffic": GATE_UP_TRAFFIC_T8192 if args.tokens == 8192 else None,
+                         "traffic_unit": "bytes per launch at T = 8192 (ncu capture)", "launches": n_g,
+                         "peak_source": f"4 x {src} sustained dense bf16 {sus} TFLOP/s (timed inside a long step; "
+                                        f"B200's dense NVFP4 rate is 4x bf16)"},
+            "model_flop_rate": {"tflops": flops / (t_max / 1e3) / 1e12,
+                                "frac_of_nvfp4_sustained": flops / (t_max / 1e3) / 1e12 / (world * fp4_sus),
+                                "algorithmic_flop": flops},
+            "gpu_launches": sum(r["launches"] for r in allr),
+            "clocks": clk,
+        }
+        if slice_ms:
+            line["stage0_slice"] = {"layers": "0-11 (PP4 stage 0: 3 dense-FFN layers, 6 KDA + MoE, 3 DSA + MoE)",
+                                    "tok_per_s": tokens / (slice_ms / 1e3), "ms_per_microbatch": slice_ms / K,
+                                    "reference_stage0_target_ms": 57.0}
+        if e2e_ms is not None:
+            e2e_max = max(r["e2e"] for r in allr)
+            line["e2e"] = {"value": tokens / (e2e_max / 1e3), "unit": "tok/s",
+                           "h2d_bytes_per_step": sum(pack_bytes) / K * world,
+                           "d2h_bytes_per_step": sum(r["d2h"] for r in allr) / K,
+                           "path": "StageWorker.step(plan): host pack of the plan's metadata and token ids, one "
+                                   "pinned H2D copy per stage, forward, greedy tokens read back to pinned memory"}
+        if world == 1 and not args.no_components:
+            del worker, batches, stage
+            torch.cuda.empty_cache()
+            line["components"] = time_components(device, pk)
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_model_baseline(args.cpu_tokens, steps=2, warm=1, layers=args.layers)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.cuda.synchronize()
+        if pipe is not None:
+            pipe.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _gpu_id(device) -> str:
+    import torch
+
+    props = torch.cuda.get_device_properties(device)
+    gid = str(getattr(props, "uuid", device.index))
+    return gid if gid.startswith("GPU-") or not gid.count("-") else "GPU-" + gid
+
+
+# ---------------------------------------------------------------------------------------------- CPU baseline
+def cpu_model_baseline(sample: int, steps: int, warm: int, layers: int = N_LAYERS) -> dict:
+    """CPU time of the model per token through the oracle (oracle/), each piece timed on `sample` rows of a
+    microbatch and summed over the model's layers: an mHC boundary (two per layer), a KDA attention block continuing a
+    request (random recurrent and conv state), a DSA attention block on rows at the end of an 8,192-token prompt
+    (random e4m3 latent cache and pool keys for the prefix: the indexer over ~2,044 pools, top-512, sparse MLA over
+    2,051 tokens), the MoE (128 experts top-8 + shared), the dense FFN. Weights are built on the host with torch's
+    CPU generator (no CUDA library involved) and dequantized once, in the warm-up (oracle/nvfp4.WEIGHT_MEMO); numpy
+    uses every host thread."""
+    import numpy as np
+    import torch
+
+    from oracle import kda as ok
+    from oracle import mhc as omhc
+    from oracle import model as omodel
+    from oracle import moe as omoe
+    from oracle import nvfp4
+    from oracle.mhc import bf16
+    from ssengine_b200 import weights
+
+    torch.set_num_threads(cpu_threads())
+    g = torch.Generator().manual_seed(SEED)
+    rng = np.random.default_rng(SEED)
+    n, Hd, nh = sample, H, MODEL["kda_heads"]
+    P = nh * 128
+
+    def lin(N, K):
+        c, s, gs = weights.nvfp4_tensor(g, N, K, "cpu")
+        return c.numpy(), s.numpy(), gs
+
+    kda_p = dict(in_proj=lin(3 * P + 256 + nh, Hd), f_b=lin(P, 128), g_b=lin(P, 128), o_proj=lin(Hd, P),
+                 conv_w=bf16(rng.uniform(-0.6, 0.6, (3 * P, 4))), a_log=rng.uniform(-1, 1, nh),
+                 dt_bias=rng.standard_normal(P) * 0.5, norm_w=np.ones(128), heads=nh, eps=1e-5)
+    ql, nope, vd = MODEL["q_lora"], MODEL["mla_nope"], MODEL["mla_v_dim"]
+    dsa_p = dict(a_proj=lin(ql + 576, Hd), q_b=lin(64 * (nope + 64), ql), wq_idx=lin(4096, ql), idx_proj=lin(288, Hd),
+                 o_proj=lin(Hd, 64 * vd), w_uk=(bf16(rng.standard_normal((64, 512, nope)) / nope ** 0.5),),
+                 w_uv=(bf16(rng.standard_normal((64, vd, 512)) / 512 ** 0.5),), q_norm=np.ones(ql),
+                 kv_norm=np.ones(512), ape=rng.standard_normal((4, 128)) * 0.5, q_lora=ql, nope=nope, v_dim=vd,
+                 theta=10000.0, eps=1e-6, scale=(nope + 64) ** -0.5, q_scale=1.0, k_scale=1.0)
+    moe_p = weights.to_numpy(weights.moe_logical(SEED, Hd, F, E, routing="sigmoid"))
+    dense_w = lin(2 * MODEL["dense_inter"], Hd) + lin(Hd, MODEL["dense_inter"])
+    bound = (rng.standard_normal((24, 4 * Hd)) / (4 * Hd) ** 0.5, np.array([0.8, 0.6, 1.5]),
+             rng.standard_normal(24) * 0.3, 1e-6, 1e-2, 1e-6, 2.0, 20, np.ones(Hd), 1e-6)
+    y = bf16(rng.standard_normal((n, Hd)))
+    res = bf16(rng.standard_normal((n, 4, Hd)))
+    post = rng.uniform(0.5, 1.5, (n, 4)).astype(np.float32)
+    comb = np.full((n, 4, 4), 0.25, np.float32)
+    cst = bf16(rng.standard_normal((2, 3, 3 * P)))
+    rst = (rng.standard_normal((2, nh, 128, 128)) * 0.05).astype(np.float32)
+    L = 8192
+    pages = np.arange(1, L // 128 + 1)
+    kv = rng.integers(0, 0x7E, ((int(pages.max()) + 1) * 128, 576)).astype(np.uint8)
+    kv |= (rng.integers(0, 2, kv.shape) << 7).astype(np.uint8)
+    pool = bf16(rng.standard_normal(((int(pages.max()) + 1) * 32, 128)))
+    tail = bf16(rng.standard_normal((2, 2, 4, 128)))
+    positions = np.arange(L - n, L)
+    counts = {"mhc": 2 * layers, "kda": sum(1 for i in range(layers) if i % 4 != 3),
+              "dsa": sum(1 for i in range(layers) if i % 4 == 3), "dense": min(3, layers),
+              "moe": layers - min(3, layers)}
+    pieces = {
+        "mhc": lambda: omhc.post_pre(y, res, post, comb, *bound),
+        "kda": lambda: ok.attention_block(y, kda_p, cst, rst, [(0, n, 1, 1)], nh, weights.GS_X, 1e-5),
+        "dsa": lambda: omodel.dsa_block(y, dsa_p, positions, [(0, n, L - n, pages, 1)], kv, pool, tail.copy(),
+                                        weights.GS_X),
+        "moe": lambda: omoe.moe_forward(y, moe_p, K_TOP, dense="lazy"),
+        "dense": lambda: omodel.dense_ffn(y, dense_w, weights.GS_X, weights.GS_H),
+    }
+    nvfp4.WEIGHT_MEMO = {}
+    try:
+        for _ in range(warm):
+            for fn in pieces.values():
+                fn()
+        per = {k: [] for k in pieces}
+        for _ in range(steps):
+            for k, fn in pieces.items():
+                t = time.perf_counter()
+                fn()
+                per[k].append(time.perf_counter() - t)
+    finally:
+        nvfp4.WEIGHT_MEMO = None
+    sec = {k: statistics.mean(v) for k, v in per.items()}
+    per_token = sum(counts[k] * sec[k] for k in sec) / n
+    return {"value": 1.0 / per_token, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
+            "sample": f"{n} rows of a microbatch through each layer piece of oracle/ (numpy, weights dequantized "
+                      f"before timing), summed over the {layers}-layer model: "
+                      + ", ".join(f"{k} {sec[k] * 1e3:.0f} ms x {counts[k]}" for k in sec),
+            "step_seconds": sum(sec.values())}
+
+
+# ---------------------------------------------------------------------------------------------- moe-layer workload
 def build_layer(device, T: int, rank: int):
     import __graft_entry__
 
@@ -201,25 +555,34 @@ def build_layer(device, T: int, rank: int):
 
 
 def run_reference(args, rank: int) -> None:
-    """CPU restatement of the path on the host cores (rank 0 only)."""
+    """The reference arm: the CPU restatement of the path on the host cores (rank 0 only), weights built on the host
+    with torch's CPU generator (no CUDA library), dequantized before timing."""
     if rank != 0:
         return
-    import numpy as np
+    if args.workload == "pipeline":
+        W, K = max(1, args.warmup), args.steps
+        cb = cpu_model_baseline(args.cpu_tokens, steps=K, warm=W, layers=args.layers)
+        v = cb["value"]
+        line = {"impl": "reference", "metric": "prefill tok/s", "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+                "steps": K, "warmup": W, "ms_per_step": cb["step_seconds"] * 1e3, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f64 / f32 (dequantized NVFP4 weights)",
+                "data": "synthetic: uniform token ids, seeded random-init weights",
+                "config": {"workload": pipeline_workload(args, args.gpus), "sample_tokens": args.cpu_tokens},
+                "cpu_baseline": cb,
+                "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     import torch
 
-    torch.set_num_threads(cpu_threads())
-    device = "cuda:0" if torch.cuda.is_available() else "cpu"
-    layer_T = args.tokens
-    sample = min(args.cpu_tokens, layer_T)
+    from oracle import moe as omoe
     from ssengine_b200 import weights
 
-    if device == "cpu":
-        raise SystemExit(json.dumps({"impl": "reference", "unavailable": "needs the GPU box to build the weights"}))
-    layer, x = build_layer(device, layer_T, 0)
-    p, dense = dense_on_host(layer)
-    x_np = x[:sample].float().cpu().numpy()
-    del layer
-    torch.cuda.empty_cache()
+    torch.set_num_threads(cpu_threads())
+    layer_T = args.tokens
+    sample = min(max(args.cpu_tokens, 256), layer_T)
+    p = weights.to_numpy(weights.moe_logical(SEED, H, F, E))
+    dense = omoe.dequantize_params(p)
+    x_np = weights.hidden_states(SEED + 1, sample, H).float().numpy()
     for _ in range(args.warmup):
         time_oracle(p, dense, x_np)
     t = [time_oracle(p, dense, x_np) for _ in range(args.steps)]
@@ -232,10 +595,9 @@ def run_reference(args, rank: int) -> None:
             "config": {"workload": workload(layer_T), "sample_tokens": sample},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
                              "sample": f"{sample} of the {layer_T} tokens per step through oracle.moe.moe_forward "
-                                       f"(numpy fp32, weights dequantized before timing)"},
+                                       f"(numpy fp32, weights built on the host and dequantized before timing)"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
-    del np
 
 
 def run_vllm_cutlass(args, rank: int) -> None:
@@ -534,13 +896,14 @@ def time_components(device, pk: dict) -> dict:
     from ssengine_b200.stage import StageConfig, StageModel
 
     scfg = StageConfig(layer_split=(4, 4, 4), hidden=4096, inter=F, experts=E, top_k=K_TOP, vocab=1024,
-                       num_blocks=6, mb_tokens=8192, layer_kind="hybrid", kda_heads=64)
+                       num_blocks=26, mb_tokens=8192, layer_kind="hybrid", kda_heads=64)
     stage = StageModel(scfg, 1, device)
-    at = 1
+    at = 67                                          # KV pages in block 1; six distinct state blocks per request
     chunks = []
     for i, n_tok in enumerate(lens_l):
         npg = -(-n_tok // 128)
-        chunks.append(Chunk(f"r{i}", 0, n_tok, list(range(at, at + npg)), [i + 1] * 6, True, None))
+        chunks.append(Chunk(f"r{i}", 0, n_tok, list(range(at, at + npg)), [2 + 6 * i + g for g in range(6)], True,
+                            None))
         at += npg
     plan = Plan(0, chunks)
     hid = rnd(Tl, 4 * 4096).to(torch.bfloat16)
@@ -558,22 +921,10 @@ def time_components(device, pk: dict) -> dict:
     return out
 
 
-def main() -> None:
-    args = parse()
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def run_moe_layer(args, rank: int, world: int, local: int) -> None:
     import torch
-
-    import __graft_entry__
-
-    __graft_entry__.import_package()
-    if args.impl == "reference":
-        run_reference(args, rank)
-        return
-    if args.impl == "vllm-cutlass":
-        run_vllm_cutlass(args, rank)
-        return
 
     from ssengine_b200 import lib
 
@@ -727,7 +1078,7 @@ def main() -> None:
 
             torch.set_num_threads(cpu_threads())
             p, dense = dense_on_host(layer)
-            sample = min(args.cpu_tokens, T)
+            sample = min(max(args.cpu_tokens, 1024), T)
             x_np = x[:sample].float().cpu().numpy()
             time_oracle(p, dense, x_np[: min(64, sample)])
             sec = time_oracle(p, dense, x_np)
@@ -739,6 +1090,27 @@ def main() -> None:
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+
+def main() -> None:
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import __graft_entry__
+
+    __graft_entry__.import_package()
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if args.impl == "vllm-cutlass":
+        run_vllm_cutlass(args, rank)
+        return
+    if args.workload == "moe-layer":
+        run_moe_layer(args, rank, world, local)
+    else:
+        run_pipeline(args, rank, world, local)
 
 
 if __name__ == "__main__":
