@@ -14,11 +14,13 @@ GPU, joined by the P2P stage edge (each stage's last kernel stores its [T, 16384
 slot; bounded flag waits; no NCCL on the activation path; gloo only for start-up and the timing reductions). The
 input stream: 256 cold prompts with lognormal lengths (median 8,192, capped at 131,072), uniform token ids, cut
 first-come-first-served into 8,192-token microbatches with KV pages and state blocks from one block pool
-(`ssengine_b200.schedule`). A step is one microbatch; K microbatches are timed after W warm-up microbatches, the
-time being each rank's CUDA-event span from its first timed microbatch to its last, the maximum over ranks; `value`
-= the K microbatches' tokens / that time (strong scaling: the model is fixed, N stages share it). The line also
+(`ssengine_b200.schedule`). A step feeds `--mb-per-step` microbatches (default 4) into the pipeline; K steps (the
+same K x 4 microbatches of the stream at every N) are timed after W warm-up steps, the time being each rank's
+CUDA-event span from its first timed microbatch to its last, the maximum over ranks, with the pipeline's fill and
+drain inside it; `value` = the timed microbatches' tokens / that time (strong scaling: the model and the timed
+tokens are fixed, N stages share them). The line also
 carries the pipeline-bubble fraction, stage 0's 12-layer slice (the PP4 stage-0 layers, timed inside the N = 1 run),
-the MoE gate_up GEMM's roofline and the model's algorithmic FLOP rate. `e2e`: the same K microbatches through the
+the MoE gate_up GEMM's roofline and the model's algorithmic FLOP rate. `e2e`: the same timed microbatches through the
 public path with each microbatch's plan metadata and token ids packed on the host and copied in (`prepare`) and the
 last stage's greedy tokens copied back to pinned host memory, inside the timed region.
 
@@ -49,6 +51,7 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 GATE_UP_TRAFFIC_T8192 = 836.4e6
 BASELINE_PP4_TOK_S = 138_400.0        # the reference's saturated 8k prefill at PP4 on 4 x B200
 N_LAYERS, MB_TOKENS, N_PROMPTS = 45, 8192, 256
+MB_PER_STEP = 4                       # pipeline: a step = 4 microbatches, so K = 20 steps time 80 microbatches
 MODEL = dict(hidden=4096, inter=1024, experts=128, top_k=8, vocab=151_552, kda_heads=64, q_lora=1536, mla_nope=192,
              mla_v_dim=256, dense_layers=3, dense_inter=12288, routing="sigmoid", layer_kind="hybrid")
 
@@ -62,6 +65,8 @@ def parse():
     ap.add_argument("--workload", choices=["pipeline", "moe-layer"], default="pipeline")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="pipeline: model layers (45 = BASELINE config 4)")
     ap.add_argument("--tokens", type=int, default=MB_TOKENS, help="tokens per microbatch")
+    ap.add_argument("--mb-per-step", type=int, default=MB_PER_STEP,
+                    help="pipeline: microbatches a step feeds the pipeline (the same timed set at every N)")
     ap.add_argument("--cpu-tokens", type=int, default=16, help="CPU baseline sample (tokens)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -276,9 +281,10 @@ def run_pipeline(args, rank: int, world: int, local: int) -> None:
     if world > 1:
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=180))
     split = split_for(world, args.layers)
-    W, K = max(3, args.warmup), args.steps
-    plans, nb = pipeline_plans(W + K, args.tokens, MODEL["vocab"] if rank == 0 else None)
-    if len(plans) < W + K:
+    W, K, M = max(3, args.warmup), args.steps, max(1, args.mb_per_step)
+    n_warm, n_timed = W * M, K * M
+    plans, nb = pipeline_plans(n_warm + n_timed, args.tokens, MODEL["vocab"] if rank == 0 else None)
+    if len(plans) < n_warm + n_timed:
         raise SystemExit(f"the prompt stream gives only {len(plans)} microbatches")
     cfg = StageConfig(layer_split=split, mb_tokens=args.tokens, num_blocks=nb, seed=SEED % 997, **MODEL)
     stage = StageModel(cfg, rank, device)
@@ -288,8 +294,8 @@ def run_pipeline(args, rank: int, world: int, local: int) -> None:
                        init_group=False, wait_ns=60_000_000_000)
     worker = StageWorker(stage, pipe, events=True)
     batches = [stage.prepare(p) for p in plans]
-    pack_bytes = [int(b.keep[0].numel()) for b in batches[W:]]
-    for b in batches[:W]:
+    pack_bytes = [int(b.keep[0].numel()) for b in batches[n_warm:]]
+    for b in batches[:n_warm]:
         worker.step(b)
     torch.cuda.synchronize()
     if pipe is not None:
@@ -325,7 +331,7 @@ def run_pipeline(args, rank: int, world: int, local: int) -> None:
         dist.barrier()
     so.on = True
     t0.record()
-    for b in batches[W:]:
+    for b in batches[n_warm:]:
         if rank == 0:
             marks.append(len(stage.moe_profile))
         worker.step(b)
@@ -345,8 +351,8 @@ def run_pipeline(args, rank: int, world: int, local: int) -> None:
     if rank == 0:
         marks.append(len(stage.moe_profile))
         g_ms = g_fl = 0.0
-        for i in range(K):
-            T = batches[W + i].num_tokens
+        for i in range(n_timed):
+            T = batches[n_warm + i].num_tokens
             for evs in stage.moe_profile[marks[i]:marks[i + 1]]:
                 g_ms += evs[6].elapsed_time(evs[7])
                 g_fl += 2.0 * T * (K_TOP + 1) * 2 * F * H
@@ -363,7 +369,7 @@ def run_pipeline(args, rank: int, world: int, local: int) -> None:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for p in plans[W:]:
+        for p in plans[n_warm:]:
             out = worker.step(p)                       # plan -> pinned pack -> one H2D copy -> forward
             if out is not None and out.numel():
                 host_tok[:out.numel()].copy_(out, non_blocking=True)
@@ -381,10 +387,10 @@ def run_pipeline(args, rank: int, world: int, local: int) -> None:
         dist.all_gather_object(allr, mine)
     if rank == 0:
         pk, src = peaks()
-        tokens = sum(b.num_tokens for b in batches[W:])
+        tokens = sum(b.num_tokens for b in batches[n_warm:])
         t_max = max(r["elapsed"] for r in allr)
         value = tokens / (t_max / 1e3)
-        flops = sum(microbatch_flops(p, cfg, args.layers) for p in plans[W:])
+        flops = sum(microbatch_flops(p, cfg, args.layers) for p in plans[n_warm:])
         sus = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
         fp4_sus = 4.0 * sus
         g_ms, g_fl, n_g = gate
@@ -395,12 +401,15 @@ def run_pipeline(args, rank: int, world: int, local: int) -> None:
             "vs_baseline": value / BASELINE_PP4_TOK_S if world == 4 else None,
             "dtype": "nvfp4 (e2m1 x e2m1, ue4m3 per-16 scales) GEMMs; e4m3 attention; bf16 residual; fp32 KDA state",
             "data": "synthetic: uniform token ids, lognormal prompt lengths, seeded random-init weights",
-            "config": {"workload": pipeline_workload(args, world), "global_batch": args.tokens,
+            "config": {"workload": pipeline_workload(args, world), "global_batch": args.tokens * M,
+                       "step": f"{M} microbatches of {args.tokens} tokens fed into the pipeline (the same "
+                               f"{n_timed} timed microbatches at every N; fill and drain inside the timed region)",
                        "seq_len": "lognormal median 8192, max 131072", "parallelism": f"pp{world}",
                        "layer_split": list(split), "tokens_timed": tokens,
                        "l2": "inputs larger than L2 (each stage streams >= 10 GB of weights per microbatch)"},
             "pipeline": {"max_rank_ms": t_max, "per_rank_ms": [r["elapsed"] for r in allr],
-                         "per_rank_busy_ms": [r["busy"] for r in allr],
+                         "per_rank_busy_ms": [r["busy"] for r in allr], "microbatches_timed": n_timed,
+                         "busiest_stage_tok_s": tokens / (max(r["busy"] for r in allr) / 1e3),
                          "bubble_fraction": 1.0 - sum(r["busy"] for r in allr) / (world * t_max),
                          "edge": "last boundary kernel stores into the next GPU's slot (P2P over NVLink), bounded "
                                  "flag waits, no NCCL"},
@@ -419,7 +428,7 @@ def run_pipeline(args, rank: int, world: int, local: int) -> None:
         }
         if slice_ms:
             line["stage0_slice"] = {"layers": "0-11 (PP4 stage 0: 3 dense-FFN layers, 6 KDA + MoE, 3 DSA + MoE)",
-                                    "tok_per_s": tokens / (slice_ms / 1e3), "ms_per_microbatch": slice_ms / K,
+                                    "tok_per_s": tokens / (slice_ms / 1e3), "ms_per_microbatch": slice_ms / n_timed,
                                     "reference_stage0_target_ms": 57.0}
         if e2e_ms is not None:
             e2e_max = max(r["e2e"] for r in allr)

@@ -400,6 +400,7 @@ class DsaAttention:
     projection NVFP4."""
 
     HEADS, LATENT, ROPE, IDX_HEADS, IDX_DIM, TOPK = 64, 512, 64, 32, 128, 512
+    POOLS_PER_PAGE = 32                # pools of 4 tokens in a 128-token KV page
 
     def __init__(self, seed: int, hidden: int, device, q_lora: int = 1536, nope: int = 192, v_dim: int = 256,
                  theta: float = 10000.0, eps: float = 1e-6, init: str = "uniform", std: float = 0.02):
@@ -422,6 +423,7 @@ class DsaAttention:
         self.ape = torch.randn(4, self.IDX_DIM, generator=g, device=dev) * 0.5
         self.scale = self.qh ** -0.5
         self.q_scale, self.k_scale = 1.0, 1.0          # per-tensor FP8 scales of the query and the latent cache
+        self.logits_ws = None          # optional fp32 buffer the logits rows are cut from (a stage's shared one)
         self.device = dev
         self._lib = lib.load()
 
@@ -471,8 +473,12 @@ class DsaAttention:
         k_idx, gate = idx[:, :self.IDX_DIM], idx[:, self.IDX_DIM + self.IDX_HEADS:2 * self.IDX_DIM + self.IDX_HEADS]
         w = idx[:, self.IDX_DIM:self.IDX_DIM + self.IDX_HEADS].float().contiguous()
         indexer.kpool_insert(k_idx, gate, self.ape, kpool_reqs, max_rows, page_table, pool_cache, tail_ring, stream)
-        ldl = _round(int(page_table.shape[1]) * 32, 128)
-        logits = torch.empty(T, ldl, dtype=torch.float32, device=dev)
+        ldl = _round(int(page_table.shape[1]) * self.POOLS_PER_PAGE, 128)
+        ws = self.logits_ws
+        if ws is not None and ws.numel() >= T * ldl:
+            logits = ws[:T * ldl].view(T, ldl)
+        else:
+            logits = torch.empty(T, ldl, dtype=torch.float32, device=dev)
         indexer.logits(q_idx.view(T, self.IDX_HEADS, self.IDX_DIM), w, pool_cache, page_table, groups, logits,
                        status, stream)
         ids = torch.empty(T, self.TOPK, dtype=torch.int32, device=dev)

@@ -122,6 +122,8 @@ class StageConfig:
     weight_init: str = "uniform"       # NVFP4 weights: "uniform" (codes uniform, scales
                                        # log-uniform) or "normal" (N(0, init_std) quantized)
     init_std: float = 0.02
+    max_context: int = 131_072         # the longest context a request reaches (sizes the indexer's logits buffer)
+    reserve_reqs: int = 64             # requests per microbatch the KDA chunk workspace is reserved for
 
 
 @dataclass
@@ -247,10 +249,29 @@ class StageModel:
         self.norm_weight = torch.ones(H, dtype=torch.bfloat16, device=self.device)
 
     def _warm(self) -> None:
-        """One forward of a small dummy plan: loads every kernel and sizes the shared workspace."""
+        """Reserves the device memory a microbatch needs, so that no forward maps new memory (a cudaMalloc inside a
+        forward stalls the host for up to tens of milliseconds while the GPU drains its queue): the indexer's logits
+        rows at `max_context` (one buffer the stage's DSA layers share; they run in order on one stream), the KDA /
+        mHC chunk workspace for `reserve_reqs` requests, and one forward of a dummy request of a full microbatch
+        (written into the null block's pages and state) that loads every kernel and leaves its temporaries in the
+        caching allocator for the next microbatches; then the MoE layers' shared workspace."""
         from .messages import Chunk, Plan
 
-        n = min(256, self.cfg.mb_tokens)
+        cfg = self.cfg
+        if any(self.is_dsa):
+            from .layers import DsaAttention
+
+            width = -(-(-(-cfg.max_context // PAGE_TOKENS) * DsaAttention.POOLS_PER_PAGE) // 128) * 128
+            logits_ws = torch.empty(cfg.mb_tokens * width, dtype=torch.float32, device=self.device)
+            for layer, dsa in zip(self.layers, self.is_dsa):
+                if dsa:
+                    layer.attn.logits_ws = logits_ws
+        if self.kda:
+            from . import kda
+
+            lib.scratch(self.device, max(kda.workspace_bytes(cfg.kda_heads, cfg.mb_tokens, cfg.reserve_reqs),
+                                         int(self._lib.ssb_mhc_workspace_bytes(cfg.mb_tokens))))
+        n = min(cfg.mb_tokens, (BLOCK_TOKENS // PAGE_TOKENS - 1) * PAGE_TOKENS)
         pages = list(range(1, -(-n // PAGE_TOKENS) + 1))
         plan = Plan(-1, [Chunk("warmup", 0, n, pages, [0] * 6, True, [0] * n if self.first else None)])
         hidden = None if self.first else torch.zeros(n, self.hidden_width, dtype=torch.bfloat16, device=self.device)
