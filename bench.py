@@ -62,7 +62,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["ours", "reference", "vllm-cutlass"], default="ours")
-    ap.add_argument("--workload", choices=["pipeline", "moe-layer"], default="pipeline")
+    ap.add_argument("--workload", choices=["pipeline", "moe-layer", "components"], default="pipeline",
+                    help="components: the attention-pair kernels and the mHC boundary alone (profiling runs)")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="pipeline: model layers (45 = BASELINE config 4)")
     ap.add_argument("--tokens", type=int, default=MB_TOKENS, help="tokens per microbatch")
     ap.add_argument("--mb-per-step", type=int, default=MB_PER_STEP,
@@ -899,31 +900,6 @@ def time_components(device, pk: dict) -> dict:
     del layer, res_l, x_l, cst_l, rst_l
     torch.cuda.empty_cache()
 
-    # a middle stage of the hybrid split: 4 decoder layers (KDA, KDA, KDA, DSA; each + MoE) at the stage shape,
-    # one 8,192-token microbatch of 4 fresh requests, received [T, 4H] rows in, sent [T, 4H] rows out
-    from ssengine_b200.messages import Chunk, Plan
-    from ssengine_b200.stage import StageConfig, StageModel
-
-    scfg = StageConfig(layer_split=(4, 4, 4), hidden=4096, inter=F, experts=E, top_k=K_TOP, vocab=1024,
-                       num_blocks=26, mb_tokens=8192, layer_kind="hybrid", kda_heads=64)
-    stage = StageModel(scfg, 1, device)
-    at = 67                                          # KV pages in block 1; six distinct state blocks per request
-    chunks = []
-    for i, n_tok in enumerate(lens_l):
-        npg = -(-n_tok // 128)
-        chunks.append(Chunk(f"r{i}", 0, n_tok, list(range(at, at + npg)), [2 + 6 * i + g for g in range(6)], True,
-                            None))
-        at += npg
-    plan = Plan(0, chunks)
-    hid = rnd(Tl, 4 * 4096).to(torch.bfloat16)
-    ms = _event_ms(lambda: stage.forward(plan, hid), reps=3, warm=1)
-    out["stage_slice_hybrid"] = {"ms": ms, "tokens": Tl, "tok_per_s": Tl / ms * 1e3, "layers": 4,
-                                 "kinds": ["kda", "kda", "kda", "dsa"],
-                                 "note": "StageModel.forward of a middle stage (prepare + 4 decoder layers + edge "
-                                         "boundary); the reference's 12-layer stage-0 target is about 57 ms per "
-                                         "8,192-token microbatch"}
-    del stage, hid
-    torch.cuda.empty_cache()
     out["workload"] = (f"BASELINE config 3 attention pair: {T} tokens from {R} requests (new tokens lognormal median "
                        f"2k, cached prefixes 0-64k; KDA 32 x 128, DSA indexer 32 x 128 top-512 pools of 4, sparse MLA "
                        f"64 heads latent 512 + rope 64, FP8 e4m3 query and latent cache); mHC at T = 8192, H = 4096")
@@ -1118,6 +1094,12 @@ def main() -> None:
         return
     if args.workload == "moe-layer":
         run_moe_layer(args, rank, world, local)
+    elif args.workload == "components":
+        import torch
+
+        torch.cuda.set_device(local)
+        pk, src = peaks()
+        print(json.dumps({"components": time_components(torch.device("cuda", local), pk), "peaks": src}), flush=True)
     else:
         run_pipeline(args, rank, world, local)
 
