@@ -118,7 +118,7 @@ int ssb_argmax_rows(const float* logits, int64_t ld, int64_t N, int64_t n, int64
 
 /* mHC (4-stream hyper-connection) parameters of one layer boundary (device pointers except the scalars). */
 typedef struct ssb_mhc_params {
-  int32_t hidden;              /* H, % 64 == 0 */
+  int32_t hidden;              /* H, % 128 == 0 (% 256 == 0 for a pre step) */
   int32_t hc_mult;             /* streams: 4 */
   const float* fn;             /* [24, 4H] fp32: mixes = z @ fn^T */
   const float* scale;          /* [3] fp32 */
@@ -126,6 +126,7 @@ typedef struct ssb_mhc_params {
   const void* norm_weight;     /* [H] bf16, the next layer's input RMSNorm */
   float rms_eps, pre_eps, sinkhorn_eps, post_mult, norm_eps;
   int32_t sinkhorn_repeat;
+  int32_t* status;             /* device int32 status word or NULL: receives 4 if a bounded wait of a pre step expired */
 } ssb_mhc_params;
 
 /* mHC at a layer boundary. With x != NULL (post): new_res bf16 [T, 4, H] = post_in[j] * x + sum_i
@@ -137,13 +138,13 @@ typedef struct ssb_mhc_params {
 int ssb_mhc(const ssb_mhc_params* p, const void* x, const void* res, const float* post_in, const float* comb_in,
             void* new_res, float* post_out, float* comb_out, void* y, int64_t T, void* stream);
 
-/* Device bytes of the partial-mix workspace of a pre step for T rows (4 x T x 25 fp32); -1 for T < 0. */
+/* Device bytes of the partial-mix workspace of a pre step for T rows (16 x T x 25 fp32); -1 for T < 0. */
 int64_t ssb_mhc_workspace_bytes(int64_t T);
 
 /* ssb_mhc with a caller-owned workspace (16-byte aligned, >= ssb_mhc_workspace_bytes(T); returns 3 when smaller), so
  * that the call allocates nothing; ssb_mhc allocates one on `stream` when it runs a pre step. A pre step is two
- * launches: the partial mixes of each quarter of the 4H positions for 128-row tiles (post fused), then the
- * quarters summed in a fixed order, Sinkhorn and the layer input. */
+ * launches: the partial mixes of 64-row tiles over eighths of the hidden positions (post fused; one persistent CTA per
+ * SM fed by TMA), then the partials summed in a fixed order, Sinkhorn and the layer input. */
 int ssb_mhc_ws(const ssb_mhc_params* p, const void* x, const void* res, const float* post_in, const float* comb_in,
                void* new_res, float* post_out, float* comb_out, void* y, int64_t T, void* workspace,
                int64_t ws_bytes, void* stream);

@@ -253,7 +253,8 @@ int ssb_mhc_ws(const ssb_mhc_params* p, const void* x, const void* res, const fl
   if (p->hc_mult != 4) return kErrArgs;
   return ssb::launch_mhc(do_post, do_pre, x, res, post_in, comb_in, new_res, p->fn, p->scale, p->base, p->norm_weight,
                          post_out, comb_out, y, T, p->hidden, p->rms_eps, p->pre_eps, p->sinkhorn_eps, p->post_mult,
-                         p->sinkhorn_repeat, p->norm_eps, workspace, ws_bytes, static_cast<cudaStream_t>(stream));
+                         p->sinkhorn_repeat, p->norm_eps, workspace, ws_bytes, p->status,
+                         static_cast<cudaStream_t>(stream));
 }
 
 static bool kda_args(const ssb_kda_layer* L, const void* x, int64_t ldx, const int32_t* seqs, int64_t R,

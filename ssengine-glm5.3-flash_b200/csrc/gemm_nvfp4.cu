@@ -708,6 +708,21 @@ int make_map_2d_swizzled(CUtensorMap* m, const void* base, int64_t rows, int64_t
   return r == CUDA_SUCCESS ? kOk : kErrArgs;
 }
 
+int make_map_2d_ex(CUtensorMap* m, int dtype, const void* base, int64_t rows, int64_t width, int64_t ld_bytes,
+                   int box_cols, int box_rows, int swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return kErrNoDriver;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld_bytes & 15) || width <= 0 || rows <= 0) return kErrArgs;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, static_cast<CUtensorMapDataType>(dtype), 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, static_cast<CUtensorMapSwizzle>(swizzle),
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrArgs;
+}
+
 int make_map_2d(CUtensorMap* m, int dtype, const void* base, int64_t rows, int64_t width, int64_t ld_bytes,
                 int box_cols, int box_rows) {
   EncodeTiledFn fn = encode_fn();

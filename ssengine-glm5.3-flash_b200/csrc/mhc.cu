@@ -46,6 +46,7 @@ struct MhcArgs {
   int64_t T, H;
   float rms_eps, pre_eps, sinkhorn_eps, post_mult, norm_eps;
   int repeat;
+  int32_t* status;
 };
 
 SSB_DEVICE float sigmoidf(float v) { return 1.0f / (1.0f + expf(-v)); }
@@ -299,145 +300,225 @@ __global__ void __launch_bounds__(kMhcThreads, 2) mhc_kernel(const MhcArgs a) {
   }
 }
 
-// ---- split pre path: the mix kernel (post + partial mixes over one quarter of the hidden positions for 128 tokens,
-//      the fn rows of each 32-position group staged once in shared memory for all 8 warps) and the finalize kernel
-//      (the quarters' partials summed in a fixed order, Sinkhorn, the layer input and its RMSNorm) ----
-constexpr int kMixTok = 128;                     // tokens per CTA of the mix kernel: 8 warps x 16
-constexpr int kFnStride = 132;                   // floats per staged fn row: 528 B, conflict-free 16-byte fragment loads
-constexpr int kFnStage = kMhcMix * kFnStride;    // one group: 24 rows x [4 streams x 32 positions]
-
-SSB_DEVICE void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
+// ---- split pre path: the mix kernel (post + partial mixes) and the finalize kernel (the partials summed in a fixed
+//      order, Sinkhorn, the layer input and its RMSNorm) ----
+//
+// Mix: persistent, one CTA per SM over work items of 64 tokens x one eighth of the hidden positions (of every
+// stream). A producer thread streams each 32-position group of an item through a 4-stage ring by TMA: the 4 residual
+// streams [64 tokens x 32 positions] bf16 (one box per stream, so a stream's rows are adjacent: conflict-free reads),
+// x (post) and the fn rows [24 x 32] fp32 of the 4 streams (128-byte swizzle). Eight consumer warps: warp w takes
+// tokens 16 (w & 3) .. + 15 and output streams 2 (w >> 2), + 1; each lane covers 2 tokens x 8 consecutive positions
+// (the MMA fragment layout), forms the new residual of its streams (bf16, stored straight to HBM) and feeds it as tf32
+// mma.sync fragments against the fn rows; the sums of squares go alongside. Partial mixes of (eighth, stream half)
+// go to the workspace: kMixParts partials per token, summed by the finalize kernel in a fixed order.
+constexpr int kMixTok = 64;                      // tokens per work item
+constexpr int kMixEighths = 8;                   // position ranges per item row
+constexpr int kMixParts = 2 * kMixEighths;       // partials per token: (eighth, stream half)
+constexpr int kMixStages = 4;
+constexpr int kMixConsumers = 8;                 // consumer warps
+constexpr int kMixThreads = 32 * (kMixConsumers + 1);
+constexpr int kMixRes = 0;                       // stage: res [4][64][32] bf16, 4 KB a stream
+constexpr int kMixX = 4 * 4096;                  // x [64][32] bf16
+constexpr int kMixFn = kMixX + 4096;             // fn [4][24][32] fp32, 3 KB a stream, 128-byte swizzle
+constexpr int kMixStage = kMixFn + 4 * 3072;     // 32 KB
+constexpr int kMixBar = kMixStages * kMixStage;  // full[4], empty[4], abort flag
+constexpr int kMixSmem = kMixBar + 128 + 1024;   // + alignment slack (1024-byte aligned stages)
 
 template <bool POST>
-__global__ void __launch_bounds__(kMhcThreads, 2) mhc_mix_kernel(const MhcArgs a, float* part, float* part_ss) {
-  __shared__ __align__(16) float fns[2][kFnStage];
-  __shared__ __align__(16) float coef[POST ? kMixTok : 1][4][8];   // token, output stream j: post[j], comb[0..3][j]
+__global__ void __launch_bounds__(kMixThreads, 1)
+    mhc_mix_kernel(const __grid_constant__ CUtensorMap mres, const __grid_constant__ CUtensorMap mx,
+                   const __grid_constant__ CUtensorMap mfn, const MhcArgs a, float* part, float* part_ss) {
+  extern __shared__ uint8_t mix_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(mix_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = smem_u32(smem);
+  const uint32_t full0 = sb + kMixBar, empty0 = full0 + 8 * kMixStages;
+  volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + kMixBar + 16 * kMixStages);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
-  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kMixTok;
-  const int kq = blockIdx.y;
   const int64_t H = a.H;
-  const int64_t gb = kq * (H / 4), ge = gb + H / 4;
-  auto stage_fn = [&](int64_t g, int st) {           // 768 pieces of 16 B: row, stream, 4 positions
-    for (int i = tid; i < kMhcMix * 32; i += kMhcThreads) {
-      const int row = i >> 5, j = (i >> 3) & 3, pc = i & 7;
-      cp_async16(smem_u32(&fns[st][row * kFnStride + j * 32 + pc * 4]),
-                 a.fn + static_cast<int64_t>(row) * 4 * H + j * H + g + pc * 4);
+  const int groups = static_cast<int>(H / kMixEighths / 32);       // 32-position groups of an item
+  const int64_t n_items = (a.T + kMixTok - 1) / kMixTok * kMixEighths;
+  if (tid == 0) {
+    for (int s = 0; s < kMixStages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, kMixConsumers);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-  stage_fn(gb, 0);
-  if (POST) {
-    for (int i = tid; i < kMixTok * 4; i += kMhcThreads) {
-      const int tk = i >> 2, j = i & 3;
-      const int64_t tt = t0 + tk;
-      float* d = coef[tk][j];
-      const bool ok = tt < a.T;
-      d[0] = ok ? a.post_in[tt * 4 + j] : 0.0f;
-#pragma unroll
-      for (int ii = 0; ii < 4; ++ii) d[1 + ii] = ok ? a.comb_in[tt * 16 + ii * 4 + j] : 0.0f;
-    }
+    *abort_flag = 0;
+    fence_barrier_init();
   }
-  const int tr0 = 16 * warp + g8, tr1 = tr0 + 8;
-  const int64_t r0 = t0 + tr0, r1 = t0 + tr1;
-  const bool v0 = r0 < a.T, v1 = r1 < a.T;
-  float macc[3][4] = {};
-  float ss0 = 0.0f, ss1 = 0.0f;
-  const uint4 zero4 = make_uint4(0, 0, 0, 0);
-  int st = 0;
-  for (int64_t g = gb; g < ge; g += 32, st ^= 1) {
-    const int64_t h = g + 8 * t4;
-    uint4 rv0[4], rv1[4], xv0 = zero4, xv1 = zero4;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      rv0[i] = v0 ? *reinterpret_cast<const uint4*>(a.res + (r0 * 4 + i) * H + h) : zero4;
-      rv1[i] = v1 ? *reinterpret_cast<const uint4*>(a.res + (r1 * 4 + i) * H + h) : zero4;
-    }
-    if (POST) {
-      if (v0) xv0 = *reinterpret_cast<const uint4*>(a.x + r0 * H + h);
-      if (v1) xv1 = *reinterpret_cast<const uint4*>(a.x + r1 * H + h);
-    }
-    if (g + 32 < ge) {
-      stage_fn(g + 32, st ^ 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
-    __syncthreads();                                   // this group's fn rows (and the coefficients) visible
-    const float* fs = fns[st];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float z0[8], z1[8];
-      if (POST) {
-        auto mixrow = [&](const uint4& xv, const uint4 (&rv)[4], const float* c, float (&z)[8]) -> uint4 {
-          const float4 ca = *reinterpret_cast<const float4*>(c), cb = *reinterpret_cast<const float4*>(c + 4);
-          const float cm[4] = {ca.y, ca.z, ca.w, cb.x};
-          const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            float v = ca.x * __bfloat162float(xb[e]);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              v = fmaf(cm[i], __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rv[i])[e]), v);
-            const __nv_bfloat16 bv = __float2bfloat16(v);
-            z[e] = __bfloat162float(bv);
-            if (e & 1) w[e >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(bv)) << 16;
-            else w[e >> 1] = __bfloat16_as_ushort(bv);
+  __syncthreads();
+
+  if (warp == kMixConsumers) {
+    // ---------------------------------------------------------------- producer (one thread)
+    if (lane == 0) {
+      tma_prefetch_desc(&mres);
+      tma_prefetch_desc(&mfn);
+      if (POST) tma_prefetch_desc(&mx);
+      constexpr uint32_t kBytes = 4 * 4096 + (POST ? 4096 : 0) + 4 * 3072;
+      int64_t n = 0;                                           // groups issued so far
+      bool ok = true;
+      for (int64_t it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+        const int32_t t0 = static_cast<int32_t>((it / kMixEighths) * kMixTok);
+        const int32_t g0 = static_cast<int32_t>((it % kMixEighths) * (H / kMixEighths));
+        for (int gi = 0; gi < groups; ++gi, ++n) {
+          const int s = static_cast<int>(n % kMixStages);
+          if (n >= kMixStages &&
+              !mbar_wait(empty0 + 8 * s, static_cast<uint32_t>((n / kMixStages - 1) & 1), abort_flag, a.status)) {
+            ok = false;
+            break;
           }
-          return make_uint4(w[0], w[1], w[2], w[3]);
-        };
-        const uint4 n0 = mixrow(xv0, rv0, coef[POST ? tr0 : 0][j], z0);
-        const uint4 n1 = mixrow(xv1, rv1, coef[POST ? tr1 : 0][j], z1);
-        if (v0) *reinterpret_cast<uint4*>(a.new_res + (r0 * 4 + j) * H + h) = n0;
-        if (v1) *reinterpret_cast<uint4*>(a.new_res + (r1 * 4 + j) * H + h) = n1;
-      } else {
+          const uint32_t st = sb + s * kMixStage, fb = full0 + 8 * s;
+          const int32_t g = g0 + 32 * gi;
+          mbar_arrive_expect_tx(fb, kBytes);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          z0[e] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rv0[j])[e]);
-          z1[e] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rv1[j])[e]);
+          for (int i = 0; i < 4; ++i) {
+            tma_load_2d(st + kMixRes + i * 4096, &mres, static_cast<int32_t>(i * H) + g, t0, fb);
+            tma_load_2d(st + kMixFn + i * 3072, &mfn, static_cast<int32_t>(i * H) + g, 0, fb);
+          }
+          if (POST) tma_load_2d(st + kMixX, &mx, g, t0, fb);
         }
       }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        ss0 = fmaf(z0[e], z0[e], ss0);
-        ss1 = fmaf(z1[e], z1[e], ss1);
-      }
-#pragma unroll
-      for (int nt = 0; nt < 3; ++nt) {
-        const float* fr = fs + (8 * nt + g8) * kFnStride + j * 32 + 8 * t4;
-        const float4 f0 = *reinterpret_cast<const float4*>(fr), f1 = *reinterpret_cast<const float4*>(fr + 4);
-        const float fb[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
-#pragma unroll
-        for (int s2 = 0; s2 < 4; ++s2) {
-          uint32_t b0, b1;
-          asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(b0) : "f"(fb[2 * s2]));
-          asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(b1) : "f"(fb[2 * s2 + 1]));
-          asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                       "{%0,%1,%2,%3};"
-                       : "+f"(macc[nt][0]), "+f"(macc[nt][1]), "+f"(macc[nt][2]), "+f"(macc[nt][3])
-                       : "r"(__float_as_uint(z0[2 * s2])), "r"(__float_as_uint(z1[2 * s2])),
-                         "r"(__float_as_uint(z0[2 * s2 + 1])), "r"(__float_as_uint(z1[2 * s2 + 1])), "r"(b0), "r"(b1));
+      // the copies in flight land before the CTA exits (bounded; normally every stage was consumed already)
+      for (int64_t m = n > kMixStages ? n - kMixStages : 0; m < n; ++m) {
+        const uint32_t fb = full0 + 8 * static_cast<int>(m % kMixStages);
+        const uint32_t par = static_cast<uint32_t>((m / kMixStages) & 1);
+        const unsigned long long w0 = globaltimer();
+        while (!mbar_try_wait(fb, par) && globaltimer() - w0 < kWaitNs) {
         }
       }
     }
-    __syncthreads();                                   // all warps done with this stage before it is refilled
+    return;
   }
-  // partials of this quarter: mixes [T][24] and sums of squares [T]
-  ss0 += __shfl_xor_sync(0xFFFFFFFFu, ss0, 1);
-  ss0 += __shfl_xor_sync(0xFFFFFFFFu, ss0, 2);
-  ss1 += __shfl_xor_sync(0xFFFFFFFFu, ss1, 1);
-  ss1 += __shfl_xor_sync(0xFFFFFFFFu, ss1, 2);
-  float* pq = part + static_cast<int64_t>(kq) * a.T * kMhcMix;
-  if (t4 == 0) {
-    if (v0) part_ss[kq * a.T + r0] = ss0;
-    if (v1) part_ss[kq * a.T + r1] = ss1;
-  }
+
+  // ------------------------------------------------------------------ consumers
+  const int tr0 = 16 * (warp & 3) + g8, tr1 = tr0 + 8, sh = warp >> 2;
+  int64_t n = 0;
+  for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
+    const int64_t t0 = (it / kMixEighths) * kMixTok;
+    const int e = static_cast<int>(it % kMixEighths);
+    const int64_t r0 = t0 + tr0, r1 = t0 + tr1;
+    const bool v0 = r0 < a.T, v1 = r1 < a.T;
+    // post[j] and comb[i][j] of this lane's two tokens for its two output streams j = 2 sh, 2 sh + 1
+    float c0[2][5], c1[2][5];
+    if (POST) {
 #pragma unroll
-  for (int nt = 0; nt < 3; ++nt) {
-    if (v0) *reinterpret_cast<float2*>(pq + r0 * kMhcMix + 8 * nt + 2 * t4) = make_float2(macc[nt][0], macc[nt][1]);
-    if (v1) *reinterpret_cast<float2*>(pq + r1 * kMhcMix + 8 * nt + 2 * t4) = make_float2(macc[nt][2], macc[nt][3]);
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = 2 * sh + jj;
+        c0[jj][0] = v0 ? a.post_in[r0 * 4 + j] : 0.0f;
+        c1[jj][0] = v1 ? a.post_in[r1 * 4 + j] : 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          c0[jj][1 + i] = v0 ? a.comb_in[r0 * 16 + i * 4 + j] : 0.0f;
+          c1[jj][1 + i] = v1 ? a.comb_in[r1 * 16 + i * 4 + j] : 0.0f;
+        }
+      }
+    }
+    float macc[3][4] = {};
+    float ss0 = 0.0f, ss1 = 0.0f;
+    bool ok = true;
+    for (int gi = 0; gi < groups; ++gi, ++n) {
+      const int s = static_cast<int>(n % kMixStages);
+      if (!mbar_wait(full0 + 8 * s, static_cast<uint32_t>((n / kMixStages) & 1), abort_flag, a.status)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* st = smem + s * kMixStage;
+      const int64_t h = (e * (H / kMixEighths)) + 32 * gi + 8 * t4;   // this lane's first position
+      uint4 rv0[4], rv1[4], xv0, xv1;
+      if (POST) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          rv0[i] = *reinterpret_cast<const uint4*>(st + kMixRes + i * 4096 + tr0 * 64 + t4 * 16);
+          rv1[i] = *reinterpret_cast<const uint4*>(st + kMixRes + i * 4096 + tr1 * 64 + t4 * 16);
+        }
+        xv0 = *reinterpret_cast<const uint4*>(st + kMixX + tr0 * 64 + t4 * 16);
+        xv1 = *reinterpret_cast<const uint4*>(st + kMixX + tr1 * 64 + t4 * 16);
+      }
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = 2 * sh + jj;
+        float z0[8], z1[8];
+        if (POST) {
+          auto mixrow = [&](const uint4& xv, const uint4 (&rv)[4], const float (&c)[5], float (&z)[8]) -> uint4 {
+            const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
+            uint32_t w[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float v[2];
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                const int el = 2 * q + u;
+                float acc = c[0] * __bfloat162float(xb[el]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  acc = fmaf(c[1 + i], __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rv[i])[el]), acc);
+                v[u] = acc;
+              }
+              const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[0], v[1]);
+              w[q] = *reinterpret_cast<const uint32_t*>(&b2);
+              z[2 * q] = __uint_as_float(w[q] << 16);
+              z[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u);
+            }
+            return make_uint4(w[0], w[1], w[2], w[3]);
+          };
+          const uint4 n0 = mixrow(xv0, rv0, c0[jj], z0);
+          const uint4 n1 = mixrow(xv1, rv1, c1[jj], z1);
+          if (v0) *reinterpret_cast<uint4*>(a.new_res + (r0 * 4 + j) * H + h) = n0;
+          if (v1) *reinterpret_cast<uint4*>(a.new_res + (r1 * 4 + j) * H + h) = n1;
+        } else {
+          const uint4 q0 = *reinterpret_cast<const uint4*>(st + kMixRes + j * 4096 + tr0 * 64 + t4 * 16);
+          const uint4 q1 = *reinterpret_cast<const uint4*>(st + kMixRes + j * 4096 + tr1 * 64 + t4 * 16);
+#pragma unroll
+          for (int el = 0; el < 8; ++el) {
+            z0[el] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&q0)[el]);
+            z1[el] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&q1)[el]);
+          }
+        }
+#pragma unroll
+        for (int el = 0; el < 8; ++el) {
+          ss0 = fmaf(z0[el], z0[el], ss0);
+          ss1 = fmaf(z1[el], z1[el], ss1);
+        }
+        const uint8_t* fs = st + kMixFn + j * 3072;
+#pragma unroll
+        for (int nt = 0; nt < 3; ++nt) {
+          const int row = 8 * nt + g8;
+          const float4 f0 = *reinterpret_cast<const float4*>(fs + row * 128 + (((2 * t4) ^ (row & 7)) << 4));
+          const float4 f1 = *reinterpret_cast<const float4*>(fs + row * 128 + (((2 * t4 + 1) ^ (row & 7)) << 4));
+          const float fb[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+#pragma unroll
+          for (int s2 = 0; s2 < 4; ++s2) {
+            uint32_t b0, b1;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(b0) : "f"(fb[2 * s2]));
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(b1) : "f"(fb[2 * s2 + 1]));
+            asm volatile(
+                "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%0,%1,%2,%3};"
+                : "+f"(macc[nt][0]), "+f"(macc[nt][1]), "+f"(macc[nt][2]), "+f"(macc[nt][3])
+                : "r"(__float_as_uint(z0[2 * s2])), "r"(__float_as_uint(z1[2 * s2])),
+                  "r"(__float_as_uint(z0[2 * s2 + 1])), "r"(__float_as_uint(z1[2 * s2 + 1])), "r"(b0), "r"(b1));
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8 * s);               // this warp is done with the stage
+    }
+    if (!ok) break;
+    // this item's partial (eighth e, stream half sh): mixes [T][24] and the sum of squares [T]
+    ss0 += __shfl_xor_sync(0xFFFFFFFFu, ss0, 1);
+    ss0 += __shfl_xor_sync(0xFFFFFFFFu, ss0, 2);
+    ss1 += __shfl_xor_sync(0xFFFFFFFFu, ss1, 1);
+    ss1 += __shfl_xor_sync(0xFFFFFFFFu, ss1, 2);
+    const int p = 2 * e + sh;
+    float* pq = part + static_cast<int64_t>(p) * a.T * kMhcMix;
+    if (t4 == 0) {
+      if (v0) part_ss[p * a.T + r0] = ss0;
+      if (v1) part_ss[p * a.T + r1] = ss1;
+    }
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt) {
+      if (v0) *reinterpret_cast<float2*>(pq + r0 * kMhcMix + 8 * nt + 2 * t4) = make_float2(macc[nt][0], macc[nt][1]);
+      if (v1) *reinterpret_cast<float2*>(pq + r1 * kMhcMix + 8 * nt + 2 * t4) = make_float2(macc[nt][2], macc[nt][3]);
+    }
   }
 }
 
@@ -454,11 +535,21 @@ __global__ void __launch_bounds__(kMhcThreads, 2) mhc_final_kernel(const MhcArgs
   for (int i = tid; i < kMhcTok * kMhcMix; i += kMhcThreads) {
     const int tk = i / kMhcMix, c = i % kMhcMix;
     const int64_t o = (t0 + tk) * kMhcMix + c;
-    mix[tk][c] = t0 + tk < a.T ? ((part[o] + part[QT + o]) + part[2 * QT + o]) + part[3 * QT + o] : 0.0f;
+    float v = 0.0f;                                    // the mix kernel's partials in a fixed order
+    if (t0 + tk < a.T) {
+#pragma unroll
+      for (int q = 0; q < kMixParts; ++q) v += part[q * QT + o];
+    }
+    mix[tk][c] = v;
   }
   if (tid < kMhcTok) {
     const int64_t tt = t0 + tid;
-    ssq[tid] = tt < a.T ? ((part_ss[tt] + part_ss[a.T + tt]) + part_ss[2 * a.T + tt]) + part_ss[3 * a.T + tt] : 0.0f;
+    float v = 0.0f;
+    if (tt < a.T) {
+#pragma unroll
+      for (int q = 0; q < kMixParts; ++q) v += part_ss[q * a.T + tt];
+    }
+    ssq[tid] = v;
   }
   __syncthreads();
   if (tid < kMhcTok && t0 + tid < a.T) {
@@ -581,23 +672,26 @@ __global__ void __launch_bounds__(kMhcThreads, 2) mhc_final_kernel(const MhcArgs
 
 }  // namespace
 
-int64_t mhc_workspace_bytes(int64_t T) { return T <= 0 ? 0 : 4 * T * (kMhcMix + 1) * static_cast<int64_t>(sizeof(float)); }
+int64_t mhc_workspace_bytes(int64_t T) {
+  return T <= 0 ? 0 : kMixParts * T * (kMhcMix + 1) * static_cast<int64_t>(sizeof(float));
+}
 
 int launch_mhc(bool do_post, bool do_pre, const void* x, const void* res, const float* post_in, const float* comb_in,
                void* new_res, const float* fn, const float* scale, const float* base, const void* norm_w,
                float* post_out, float* comb_out, void* y, int64_t T, int64_t H, float rms_eps, float pre_eps,
                float sinkhorn_eps, float post_mult, int repeat, float norm_eps, void* ws, int64_t ws_bytes,
-               cudaStream_t stream) {
+               int32_t* status, cudaStream_t stream) {
   if (T < 0 || H <= 0 || H % 128 != 0 || repeat < 1 || (!do_post && !do_pre)) return kErrArgs;
   if (T == 0) return kOk;
   MhcArgs a{reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(res), post_in, comb_in,
             reinterpret_cast<__nv_bfloat16*>(new_res), fn, scale, base,
             reinterpret_cast<const __nv_bfloat16*>(norm_w), post_out, comb_out, reinterpret_cast<__nv_bfloat16*>(y),
-            T, H, rms_eps, pre_eps, sinkhorn_eps, post_mult, norm_eps, repeat};
+            T, H, rms_eps, pre_eps, sinkhorn_eps, post_mult, norm_eps, repeat, status};
   if (!do_pre) {
     mhc_kernel<true, false><<<static_cast<unsigned>((T + kMhcTok - 1) / kMhcTok), kMhcThreads, 0, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
   }
+  if (H % (kMixEighths * 32) != 0) return kErrArgs;   // a pre step covers the positions in eighths of 32-wide groups
   const int64_t need = mhc_workspace_bytes(T);
   bool own = false;
   if (ws == nullptr) {                                   // no caller workspace: a stream-ordered allocation
@@ -607,17 +701,44 @@ int launch_mhc(bool do_post, bool do_pre, const void* x, const void* res, const 
     return kErrWorkspace;
   }
   float* part = static_cast<float*>(ws);
-  float* part_ss = part + 4 * T * kMhcMix;
-  const dim3 gmix(static_cast<unsigned>((T + kMixTok - 1) / kMixTok), 4);
-  const unsigned gfin = static_cast<unsigned>((T + kMhcTok - 1) / kMhcTok);
-  if (do_post) {
-    mhc_mix_kernel<true><<<gmix, kMhcThreads, 0, stream>>>(a, part, part_ss);
-    mhc_final_kernel<true><<<gfin, kMhcThreads, 0, stream>>>(a, part, part_ss);
-  } else {
-    mhc_mix_kernel<false><<<gmix, kMhcThreads, 0, stream>>>(a, part, part_ss);
-    mhc_final_kernel<false><<<gfin, kMhcThreads, 0, stream>>>(a, part, part_ss);
+  float* part_ss = part + kMixParts * T * kMhcMix;
+  int rc = kOk;
+  // tensor maps: the residual as [T, 4H] bf16 (one 32 x 64 box per stream), x as [T, H], fn as [24, 4H] fp32 (one
+  // 32 x 24 box per stream, 128-byte swizzle); T and H are the only extents (rows past T read as zeros)
+  CUtensorMap mres, mx, mfn;
+  if (reinterpret_cast<uintptr_t>(fn) & 15) rc = kErrArgs;
+  if (rc == kOk)
+    rc = make_map_2d(&mres, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, res, T, 4 * H, 4 * H * 2, 32, kMixTok);
+  if (rc == kOk)
+    rc = make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, do_post ? x : res, T, H, (do_post ? H : 4 * H) * 2, 32,
+                     kMixTok);
+  if (rc == kOk) rc = make_map_2d_ex(&mfn, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, fn, kMhcMix, 4 * H, 4 * H * 4, 32,
+                                     kMhcMix, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc == kOk) {
+    static bool attr = false;
+    if (!attr) {
+      if (cudaFuncSetAttribute(mhc_mix_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMixSmem) !=
+              cudaSuccess ||
+          cudaFuncSetAttribute(mhc_mix_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMixSmem) !=
+              cudaSuccess)
+        rc = kErrCuda;
+      else
+        attr = true;
+    }
   }
-  int rc = cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  if (rc == kOk) {
+    const int64_t items = (T + kMixTok - 1) / kMixTok * kMixEighths;
+    const unsigned gmix = static_cast<unsigned>(std::min<int64_t>(items, device_sm_count()));
+    const unsigned gfin = static_cast<unsigned>((T + kMhcTok - 1) / kMhcTok);
+    if (do_post) {
+      mhc_mix_kernel<true><<<gmix, kMixThreads, kMixSmem, stream>>>(mres, mx, mfn, a, part, part_ss);
+      mhc_final_kernel<true><<<gfin, kMhcThreads, 0, stream>>>(a, part, part_ss);
+    } else {
+      mhc_mix_kernel<false><<<gmix, kMixThreads, kMixSmem, stream>>>(mres, mx, mfn, a, part, part_ss);
+      mhc_final_kernel<false><<<gfin, kMhcThreads, 0, stream>>>(a, part, part_ss);
+    }
+    rc = cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+  }
   if (own && cudaFreeAsync(ws, stream) != cudaSuccess && rc == kOk) rc = kErrCuda;
   return rc;
 }

@@ -106,7 +106,7 @@ int launch_mhc(bool do_post, bool do_pre, const void* x, const void* res, const 
                void* new_res, const float* fn, const float* scale, const float* base, const void* norm_w,
                float* post_out, float* comb_out, void* y, int64_t T, int64_t H, float rms_eps, float pre_eps,
                float sinkhorn_eps, float post_mult, int repeat, float norm_eps, void* ws, int64_t ws_bytes,
-               cudaStream_t stream);
+               int32_t* status, cudaStream_t stream);
 
 // KDA prefill (csrc/kda.cu).
 struct KdaArgs {
@@ -144,6 +144,9 @@ int launch_kda_prefill(const KdaArgs& a, cudaStream_t stream);
 // box = box_cols x box_rows (csrc/gemm_nvfp4.cu).
 int make_map_2d(CUtensorMap* m, int dtype, const void* base, int64_t rows, int64_t width, int64_t ld_bytes,
                 int box_cols, int box_rows);
+// The same with a CUtensorMapSwizzle mode (csrc/gemm_nvfp4.cu).
+int make_map_2d_ex(CUtensorMap* m, int dtype, const void* base, int64_t rows, int64_t width, int64_t ld_bytes,
+                   int box_cols, int box_rows, int swizzle);
 int launch_kda_conv(const KdaArgs& a, int64_t T, void* q, void* k, void* v, cudaStream_t stream);
 
 // DSA indexer (csrc/indexer.cu).

@@ -219,11 +219,13 @@ class MhcBoundary:
                                  self.eps["sinkhorn_eps"], self.eps["post_mult"], self.eps["norm_eps"], repeat)
         self._lib = lib.load()
 
-    def __call__(self, x, res, post_in, comb_in, new_res, post_out, comb_out, y, stream=None) -> None:
-        """x = None: pre only (the stage-edge receive) on res; else post of x into new_res, then pre of new_res."""
+    def __call__(self, x, res, post_in, comb_in, new_res, post_out, comb_out, y, stream=None, status=None) -> None:
+        """x = None: pre only (the stage-edge receive) on res; else post of x into new_res, then pre of new_res.
+        `status` (int32 [1] on the device) receives 4 if a bounded wait of the pre step expired."""
         import ctypes
 
         T = res.shape[0]
+        self._c.status = None if status is None else status.data_ptr()
         ws = lib.scratch(res.device, int(self._lib.ssb_mhc_workspace_bytes(T)))
         rc = self._lib.ssb_mhc_ws(ctypes.byref(self._c), None if x is None else x.data_ptr(), res.data_ptr(),
                                   None if post_in is None else post_in.data_ptr(),
@@ -266,11 +268,11 @@ class KdaDecoderLayer:
         post_a, comb_a = torch.empty(T, 4, **f32), torch.empty(T, 4, 4, **f32)
         y = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
         self.bound_a(x_prev, res, post_prev, comb_prev, res_a if x_prev is not None else None, post_a, comb_a, y,
-                     stream)
+                     stream, status=status)
         x_a = self.attn.forward(y, seqs, conv_state, rec_state, status, stream=stream)
         res_b = torch.empty_like(res)
         post_b, comb_b = torch.empty(T, 4, **f32), torch.empty(T, 4, 4, **f32)
-        self.bound_b(x_a, res_a, post_a, comb_a, res_b, post_b, comb_b, y, stream)
+        self.bound_b(x_a, res_a, post_a, comb_a, res_b, post_b, comb_b, y, stream, status=status)
         x_b = _ffn_forward(self, y, stream)
         return res_b, x_b, post_b, comb_b
 
@@ -532,11 +534,11 @@ class DsaDecoderLayer:
         post_a, comb_a = torch.empty(T, 4, **f32), torch.empty(T, 4, 4, **f32)
         y = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
         self.bound_a(x_prev, res, post_prev, comb_prev, res_a if x_prev is not None else None, post_a, comb_a, y,
-                     stream)
+                     stream, status=status)
         x_a = self.attn.forward(y, meta["positions"], meta["slots"], meta["qsl"], meta["page_table"],
                                 meta["kpool_reqs"], meta["max_rows"], meta["groups"], *caches, status, stream=stream)
         res_b = torch.empty_like(res)
         post_b, comb_b = torch.empty(T, 4, **f32), torch.empty(T, 4, 4, **f32)
-        self.bound_b(x_a, res_a, post_a, comb_a, res_b, post_b, comb_b, y, stream)
+        self.bound_b(x_a, res_a, post_a, comb_a, res_b, post_b, comb_b, y, stream, status=status)
         x_b = _ffn_forward(self, y, stream)
         return res_b, x_b, post_b, comb_b

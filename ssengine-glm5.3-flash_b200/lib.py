@@ -67,7 +67,8 @@ class MhcParamsC(ctypes.Structure):
     _fields_ = [("hidden", ctypes.c_int32), ("hc_mult", ctypes.c_int32), ("fn", ctypes.c_void_p),
                 ("scale", ctypes.c_void_p), ("base", ctypes.c_void_p), ("norm_weight", ctypes.c_void_p),
                 ("rms_eps", ctypes.c_float), ("pre_eps", ctypes.c_float), ("sinkhorn_eps", ctypes.c_float),
-                ("post_mult", ctypes.c_float), ("norm_eps", ctypes.c_float), ("sinkhorn_repeat", ctypes.c_int32)]
+                ("post_mult", ctypes.c_float), ("norm_eps", ctypes.c_float), ("sinkhorn_repeat", ctypes.c_int32),
+                ("status", ctypes.c_void_p)]
 
 
 _LIB = None
