@@ -47,9 +47,37 @@ struct MhcArgs {
   float rms_eps, pre_eps, sinkhorn_eps, post_mult, norm_eps;
   int repeat;
   int32_t* status;
+  int ranges;                // pre step: position ranges of a mix work item (8, or 4 when H % 512 != 0)
 };
 
 SSB_DEVICE float sigmoidf(float v) { return 1.0f / (1.0f + expf(-v)); }
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE single-precision operations per instruction, each rounded as
+// the scalar one would be).
+SSB_DEVICE uint64_t f2pack(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+SSB_DEVICE void f2unpack(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+SSB_DEVICE uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+SSB_DEVICE uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// bf16 pair (low element in the low half) -> packed fp32 {lo, hi}; packed fp32 -> bf16 pair, round to nearest even
+SSB_DEVICE uint64_t bf2_f2(uint32_t w) { return f2pack(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u)); }
+SSB_DEVICE uint32_t f2_bf2(uint64_t v) {
+  float lo, hi;
+  f2unpack(v, lo, hi);
+  const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&b);
+}
 
 template <bool POST, bool PRE>
 __global__ void __launch_bounds__(kMhcThreads, 2) mhc_kernel(const MhcArgs a) {
@@ -314,13 +342,14 @@ __global__ void __launch_bounds__(kMhcThreads, 2) mhc_kernel(const MhcArgs a) {
 constexpr int kMixTok = 64;                      // tokens per work item
 constexpr int kMixEighths = 8;                   // position ranges per item row
 constexpr int kMixParts = 2 * kMixEighths;       // partials per token: (eighth, stream half)
-constexpr int kMixStages = 4;
+constexpr int kMixStages = 3;
 constexpr int kMixConsumers = 8;                 // consumer warps
 constexpr int kMixThreads = 32 * (kMixConsumers + 1);
-constexpr int kMixRes = 0;                       // stage: res [4][64][32] bf16, 4 KB a stream
-constexpr int kMixX = 4 * 4096;                  // x [64][32] bf16
-constexpr int kMixFn = kMixX + 4096;             // fn [4][24][32] fp32, 3 KB a stream, 128-byte swizzle
-constexpr int kMixStage = kMixFn + 4 * 3072;     // 32 KB
+constexpr int kMixHalves = 2;                    // a stage holds 2 x 32 positions: 128 contiguous bytes of every row
+constexpr int kMixRes = 0;                       // stage: res [half][4][64][32] bf16, 4 KB a box
+constexpr int kMixX = kMixHalves * 4 * 4096;     // x [half][64][32] bf16
+constexpr int kMixFn = kMixX + kMixHalves * 4096;        // fn [half][4][24][32] fp32, 3 KB a box, 128-byte swizzle
+constexpr int kMixStage = kMixFn + kMixHalves * 4 * 3072;   // 64 KB
 constexpr int kMixBar = kMixStages * kMixStage;  // full[4], empty[4], abort flag
 constexpr int kMixSmem = kMixBar + 128 + 1024;   // + alignment slack (1024-byte aligned stages)
 
@@ -335,8 +364,9 @@ __global__ void __launch_bounds__(kMixThreads, 1)
   volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + kMixBar + 16 * kMixStages);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
   const int64_t H = a.H;
-  const int groups = static_cast<int>(H / kMixEighths / 32);       // 32-position groups of an item
-  const int64_t n_items = (a.T + kMixTok - 1) / kMixTok * kMixEighths;
+  const int ranges = a.ranges;                                     // position ranges an item row is cut into
+  const int groups = static_cast<int>(H / ranges / (32 * kMixHalves));    // 64-position groups of an item
+  const int64_t n_items = (a.T + kMixTok - 1) / kMixTok * ranges;
   if (tid == 0) {
     for (int s = 0; s < kMixStages; ++s) {
       mbar_init(full0 + 8 * s, 1);
@@ -353,12 +383,12 @@ __global__ void __launch_bounds__(kMixThreads, 1)
       tma_prefetch_desc(&mres);
       tma_prefetch_desc(&mfn);
       if (POST) tma_prefetch_desc(&mx);
-      constexpr uint32_t kBytes = 4 * 4096 + (POST ? 4096 : 0) + 4 * 3072;
+      constexpr uint32_t kBytes = kMixHalves * (4 * 4096 + (POST ? 4096 : 0) + 4 * 3072);
       int64_t n = 0;                                           // groups issued so far
       bool ok = true;
       for (int64_t it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
-        const int32_t t0 = static_cast<int32_t>((it / kMixEighths) * kMixTok);
-        const int32_t g0 = static_cast<int32_t>((it % kMixEighths) * (H / kMixEighths));
+        const int32_t t0 = static_cast<int32_t>((it / ranges) * kMixTok);
+        const int32_t g0 = static_cast<int32_t>((it % ranges) * (H / ranges));
         for (int gi = 0; gi < groups; ++gi, ++n) {
           const int s = static_cast<int>(n % kMixStages);
           if (n >= kMixStages &&
@@ -367,14 +397,22 @@ __global__ void __launch_bounds__(kMixThreads, 1)
             break;
           }
           const uint32_t st = sb + s * kMixStage, fb = full0 + 8 * s;
-          const int32_t g = g0 + 32 * gi;
+          const int32_t g = g0 + 32 * kMixHalves * gi;
           mbar_arrive_expect_tx(fb, kBytes);
+          // the two halves of a row back to back: one 128-byte run of each row per stage
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            tma_load_2d(st + kMixRes + i * 4096, &mres, static_cast<int32_t>(i * H) + g, t0, fb);
-            tma_load_2d(st + kMixFn + i * 3072, &mfn, static_cast<int32_t>(i * H) + g, 0, fb);
-          }
-          if (POST) tma_load_2d(st + kMixX, &mx, g, t0, fb);
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int hb = 0; hb < kMixHalves; ++hb)
+              tma_load_2d(st + kMixRes + (hb * 4 + i) * 4096, &mres, static_cast<int32_t>(i * H) + g + 32 * hb, t0, fb);
+          if (POST)
+#pragma unroll
+            for (int hb = 0; hb < kMixHalves; ++hb) tma_load_2d(st + kMixX + hb * 4096, &mx, g + 32 * hb, t0, fb);
+#pragma unroll
+          for (int hb = 0; hb < kMixHalves; ++hb)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              tma_load_2d(st + kMixFn + (hb * 4 + i) * 3072, &mfn, static_cast<int32_t>(i * H) + g + 32 * hb, 0, fb);
         }
       }
       // the copies in flight land before the CTA exits (bounded; normally every stage was consumed already)
@@ -393,27 +431,29 @@ __global__ void __launch_bounds__(kMixThreads, 1)
   const int tr0 = 16 * (warp & 3) + g8, tr1 = tr0 + 8, sh = warp >> 2;
   int64_t n = 0;
   for (int64_t it = blockIdx.x; it < n_items; it += gridDim.x) {
-    const int64_t t0 = (it / kMixEighths) * kMixTok;
-    const int e = static_cast<int>(it % kMixEighths);
+    const int64_t t0 = (it / ranges) * kMixTok;
+    const int e = static_cast<int>(it % ranges);
     const int64_t r0 = t0 + tr0, r1 = t0 + tr1;
     const bool v0 = r0 < a.T, v1 = r1 < a.T;
-    // post[j] and comb[i][j] of this lane's two tokens for its two output streams j = 2 sh, 2 sh + 1
-    float c0[2][5], c1[2][5];
+    // post[j] and comb[i][j] of this lane's two tokens for its two output streams j = 2 sh, 2 sh + 1, as pairs
+    uint64_t c0[2][5], c1[2][5];
     if (POST) {
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
         const int j = 2 * sh + jj;
-        c0[jj][0] = v0 ? a.post_in[r0 * 4 + j] : 0.0f;
-        c1[jj][0] = v1 ? a.post_in[r1 * 4 + j] : 0.0f;
+        const float p0 = v0 ? a.post_in[r0 * 4 + j] : 0.0f, p1 = v1 ? a.post_in[r1 * 4 + j] : 0.0f;
+        c0[jj][0] = f2pack(p0, p0);
+        c1[jj][0] = f2pack(p1, p1);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          c0[jj][1 + i] = v0 ? a.comb_in[r0 * 16 + i * 4 + j] : 0.0f;
-          c1[jj][1 + i] = v1 ? a.comb_in[r1 * 16 + i * 4 + j] : 0.0f;
+          const float q0 = v0 ? a.comb_in[r0 * 16 + i * 4 + j] : 0.0f, q1 = v1 ? a.comb_in[r1 * 16 + i * 4 + j] : 0.0f;
+          c0[jj][1 + i] = f2pack(q0, q0);
+          c1[jj][1 + i] = f2pack(q1, q1);
         }
       }
     }
     float macc[3][4] = {};
-    float ss0 = 0.0f, ss1 = 0.0f;
+    uint64_t ss0 = 0, ss1 = 0;                                  // packed sums of squares (even, odd positions)
     bool ok = true;
     for (int gi = 0; gi < groups; ++gi, ++n) {
       const int s = static_cast<int>(n % kMixStages);
@@ -421,64 +461,65 @@ __global__ void __launch_bounds__(kMixThreads, 1)
         ok = false;
         break;
       }
-      const uint8_t* st = smem + s * kMixStage;
-      const int64_t h = (e * (H / kMixEighths)) + 32 * gi + 8 * t4;   // this lane's first position
-      uint4 rv0[4], rv1[4], xv0, xv1;
+#pragma unroll 1
+      for (int hb = 0; hb < kMixHalves; ++hb) {
+      const uint8_t* st0 = smem + s * kMixStage;
+      const uint8_t* st = st0 + kMixRes + hb * (4 * 4096);              // this half's residual boxes
+      const uint8_t* stx = st0 + kMixX + hb * 4096;                     // its x box
+      const uint8_t* stf = st0 + kMixFn + hb * (4 * 3072);              // its fn boxes
+      const int64_t h = e * (H / ranges) + 32 * (kMixHalves * gi + hb) + 8 * t4;   // this lane's first position
+      // the new residual of this lane's two output streams, bf16 pairs: w[token][stream][pair]
+      uint32_t w[2][2][4];
       if (POST) {
+        auto mix_token = [&](int tr, const uint64_t (&c)[2][5], uint32_t (&wt)[2][4]) {
+          const uint4 xv = *reinterpret_cast<const uint4*>(stx + tr * 64 + t4 * 16);
+          uint4 rv[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          rv0[i] = *reinterpret_cast<const uint4*>(st + kMixRes + i * 4096 + tr0 * 64 + t4 * 16);
-          rv1[i] = *reinterpret_cast<const uint4*>(st + kMixRes + i * 4096 + tr1 * 64 + t4 * 16);
+          for (int i = 0; i < 4; ++i) rv[i] = *reinterpret_cast<const uint4*>(st + i * 4096 + tr * 64 + t4 * 16);
+          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint64_t xf = bf2_f2(xw[q]);
+            uint64_t rf[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) rf[i] = bf2_f2(reinterpret_cast<const uint32_t*>(&rv[i])[q]);
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+              uint64_t acc = mul2(c[jj][0], xf);                // post[j] x + sum_i comb[i][j] res_i, in that order
+#pragma unroll
+              for (int i = 0; i < 4; ++i) acc = fma2(c[jj][1 + i], rf[i], acc);
+              wt[jj][q] = f2_bf2(acc);
+            }
+          }
+        };
+        mix_token(tr0, c0, w[0]);
+        mix_token(tr1, c1, w[1]);
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j = 2 * sh + jj;
+          if (v0) *reinterpret_cast<uint4*>(a.new_res + (r0 * 4 + j) * H + h) = make_uint4(w[0][jj][0], w[0][jj][1], w[0][jj][2], w[0][jj][3]);
+          if (v1) *reinterpret_cast<uint4*>(a.new_res + (r1 * 4 + j) * H + h) = make_uint4(w[1][jj][0], w[1][jj][1], w[1][jj][2], w[1][jj][3]);
         }
-        xv0 = *reinterpret_cast<const uint4*>(st + kMixX + tr0 * 64 + t4 * 16);
-        xv1 = *reinterpret_cast<const uint4*>(st + kMixX + tr1 * 64 + t4 * 16);
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j = 2 * sh + jj;
+          const uint4 q0 = *reinterpret_cast<const uint4*>(st + j * 4096 + tr0 * 64 + t4 * 16);
+          const uint4 q1 = *reinterpret_cast<const uint4*>(st + j * 4096 + tr1 * 64 + t4 * 16);
+          w[0][jj][0] = q0.x; w[0][jj][1] = q0.y; w[0][jj][2] = q0.z; w[0][jj][3] = q0.w;
+          w[1][jj][0] = q1.x; w[1][jj][1] = q1.y; w[1][jj][2] = q1.z; w[1][jj][3] = q1.w;
+        }
       }
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
         const int j = 2 * sh + jj;
-        float z0[8], z1[8];
-        if (POST) {
-          auto mixrow = [&](const uint4& xv, const uint4 (&rv)[4], const float (&c)[5], float (&z)[8]) -> uint4 {
-            const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xv);
-            uint32_t w[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float v[2];
-#pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                const int el = 2 * q + u;
-                float acc = c[0] * __bfloat162float(xb[el]);
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                  acc = fmaf(c[1 + i], __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&rv[i])[el]), acc);
-                v[u] = acc;
-              }
-              const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[0], v[1]);
-              w[q] = *reinterpret_cast<const uint32_t*>(&b2);
-              z[2 * q] = __uint_as_float(w[q] << 16);
-              z[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u);
-            }
-            return make_uint4(w[0], w[1], w[2], w[3]);
-          };
-          const uint4 n0 = mixrow(xv0, rv0, c0[jj], z0);
-          const uint4 n1 = mixrow(xv1, rv1, c1[jj], z1);
-          if (v0) *reinterpret_cast<uint4*>(a.new_res + (r0 * 4 + j) * H + h) = n0;
-          if (v1) *reinterpret_cast<uint4*>(a.new_res + (r1 * 4 + j) * H + h) = n1;
-        } else {
-          const uint4 q0 = *reinterpret_cast<const uint4*>(st + kMixRes + j * 4096 + tr0 * 64 + t4 * 16);
-          const uint4 q1 = *reinterpret_cast<const uint4*>(st + kMixRes + j * 4096 + tr1 * 64 + t4 * 16);
-#pragma unroll
-          for (int el = 0; el < 8; ++el) {
-            z0[el] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&q0)[el]);
-            z1[el] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&q1)[el]);
-          }
+        for (int q = 0; q < 4; ++q) {
+          const uint64_t z0 = bf2_f2(w[0][jj][q]), z1 = bf2_f2(w[1][jj][q]);
+          ss0 = fma2(z0, z0, ss0);
+          ss1 = fma2(z1, z1, ss1);
         }
-#pragma unroll
-        for (int el = 0; el < 8; ++el) {
-          ss0 = fmaf(z0[el], z0[el], ss0);
-          ss1 = fmaf(z1[el], z1[el], ss1);
-        }
-        const uint8_t* fs = st + kMixFn + j * 3072;
+        const uint8_t* fs = stf + j * 3072;
 #pragma unroll
         for (int nt = 0; nt < 3; ++nt) {
           const int row = 8 * nt + g8;
@@ -490,29 +531,36 @@ __global__ void __launch_bounds__(kMixThreads, 1)
             uint32_t b0, b1;
             asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(b0) : "f"(fb[2 * s2]));
             asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(b1) : "f"(fb[2 * s2 + 1]));
+            // k index t4: position 2 s2 of the lane's 8, k index t4 + 4: position 2 s2 + 1 (bf16 bits are exact tf32)
             asm volatile(
                 "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
                 "{%0,%1,%2,%3};"
                 : "+f"(macc[nt][0]), "+f"(macc[nt][1]), "+f"(macc[nt][2]), "+f"(macc[nt][3])
-                : "r"(__float_as_uint(z0[2 * s2])), "r"(__float_as_uint(z1[2 * s2])),
-                  "r"(__float_as_uint(z0[2 * s2 + 1])), "r"(__float_as_uint(z1[2 * s2 + 1])), "r"(b0), "r"(b1));
+                : "r"(w[0][jj][s2] << 16), "r"(w[1][jj][s2] << 16), "r"(w[0][jj][s2] & 0xFFFF0000u),
+                  "r"(w[1][jj][s2] & 0xFFFF0000u), "r"(b0), "r"(b1));
           }
         }
+      }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8 * s);               // this warp is done with the stage
     }
     if (!ok) break;
     // this item's partial (eighth e, stream half sh): mixes [T][24] and the sum of squares [T]
-    ss0 += __shfl_xor_sync(0xFFFFFFFFu, ss0, 1);
-    ss0 += __shfl_xor_sync(0xFFFFFFFFu, ss0, 2);
-    ss1 += __shfl_xor_sync(0xFFFFFFFFu, ss1, 1);
-    ss1 += __shfl_xor_sync(0xFFFFFFFFu, ss1, 2);
+    float ssa, ssb, sq0, sq1;
+    f2unpack(ss0, ssa, ssb);
+    sq0 = ssa + ssb;
+    f2unpack(ss1, ssa, ssb);
+    sq1 = ssa + ssb;
+    sq0 += __shfl_xor_sync(0xFFFFFFFFu, sq0, 1);
+    sq0 += __shfl_xor_sync(0xFFFFFFFFu, sq0, 2);
+    sq1 += __shfl_xor_sync(0xFFFFFFFFu, sq1, 1);
+    sq1 += __shfl_xor_sync(0xFFFFFFFFu, sq1, 2);
     const int p = 2 * e + sh;
     float* pq = part + static_cast<int64_t>(p) * a.T * kMhcMix;
     if (t4 == 0) {
-      if (v0) part_ss[p * a.T + r0] = ss0;
-      if (v1) part_ss[p * a.T + r1] = ss1;
+      if (v0) part_ss[p * a.T + r0] = sq0;
+      if (v1) part_ss[p * a.T + r1] = sq1;
     }
 #pragma unroll
     for (int nt = 0; nt < 3; ++nt) {
@@ -538,7 +586,8 @@ __global__ void __launch_bounds__(kMhcThreads, 2) mhc_final_kernel(const MhcArgs
     float v = 0.0f;                                    // the mix kernel's partials in a fixed order
     if (t0 + tk < a.T) {
 #pragma unroll
-      for (int q = 0; q < kMixParts; ++q) v += part[q * QT + o];
+      for (int q = 0; q < kMixParts; ++q)
+        if (q < 2 * a.ranges) v += part[q * QT + o];
     }
     mix[tk][c] = v;
   }
@@ -547,7 +596,8 @@ __global__ void __launch_bounds__(kMhcThreads, 2) mhc_final_kernel(const MhcArgs
     float v = 0.0f;
     if (tt < a.T) {
 #pragma unroll
-      for (int q = 0; q < kMixParts; ++q) v += part_ss[q * a.T + tt];
+      for (int q = 0; q < kMixParts; ++q)
+        if (q < 2 * a.ranges) v += part_ss[q * a.T + tt];
     }
     ssq[tid] = v;
   }
@@ -686,12 +736,13 @@ int launch_mhc(bool do_post, bool do_pre, const void* x, const void* res, const 
   MhcArgs a{reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(res), post_in, comb_in,
             reinterpret_cast<__nv_bfloat16*>(new_res), fn, scale, base,
             reinterpret_cast<const __nv_bfloat16*>(norm_w), post_out, comb_out, reinterpret_cast<__nv_bfloat16*>(y),
-            T, H, rms_eps, pre_eps, sinkhorn_eps, post_mult, norm_eps, repeat, status};
+            T, H, rms_eps, pre_eps, sinkhorn_eps, post_mult, norm_eps, repeat, status,
+            H % (kMixEighths * 64) == 0 ? kMixEighths : kMixEighths / 2};
   if (!do_pre) {
     mhc_kernel<true, false><<<static_cast<unsigned>((T + kMhcTok - 1) / kMhcTok), kMhcThreads, 0, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
   }
-  if (H % (kMixEighths * 32) != 0) return kErrArgs;   // a pre step covers the positions in eighths of 32-wide groups
+  if (H % (kMixEighths / 2 * 64) != 0) return kErrArgs;   // a pre step covers H in 4 or 8 ranges of 64-wide groups
   const int64_t need = mhc_workspace_bytes(T);
   bool own = false;
   if (ws == nullptr) {                                   // no caller workspace: a stream-ordered allocation
@@ -727,7 +778,7 @@ int launch_mhc(bool do_post, bool do_pre, const void* x, const void* res, const 
     }
   }
   if (rc == kOk) {
-    const int64_t items = (T + kMixTok - 1) / kMixTok * kMixEighths;
+    const int64_t items = (T + kMixTok - 1) / kMixTok * a.ranges;
     const unsigned gmix = static_cast<unsigned>(std::min<int64_t>(items, device_sm_count()));
     const unsigned gfin = static_cast<unsigned>((T + kMhcTok - 1) / kMhcTok);
     if (do_post) {
