@@ -10,10 +10,11 @@
 // fp32 in TMEM). Pools are the MMA's M, so each TMEM lane is one pool and its 256 columns are the 8 queries' 32 heads:
 // the weighted ReLU sum over heads runs in one thread's registers, with no cross-lane reduction.
 // Work unit: a group of <= 8 consecutive query rows of one request (host table, longest first); its Q tile stays in
-// shared memory while its pool tiles stream through a 4-stage ring. Roles (192 threads, persistent):
+// shared memory while its pool tiles stream through a 4-stage ring. Roles (320 threads, persistent):
 //   warp 0 TMA producer (Q tile: 2 boxes of 256 x 64; pool tile: 2 x 4 page boxes of 32 x 64, 128-byte swizzle),
 //   warp 1 TMEM owner + MMA issuer (8 MMAs of K = 16 per tile; two 256-column accumulators alternate),
-//   warps 2-5 epilogue (lane quadrant = warp % 4): tcgen05.ld, ReLU, weights, fp32 logits rows.
+//   warps 2-9 epilogue (lane quadrant = warp % 4, two warps a quadrant taking 4 of the 8 queries each): tcgen05.ld of
+//   two queries' 32 heads at a time, ReLU, weights, four partial sums over the heads, fp32 logits rows.
 // Every wait is bounded; on expiry the roles leave, in-flight copies / MMAs are drained, TMEM is freed and the
 // status word holds kErrTimeout. No cluster multicast.
 #include "common.cuh"
@@ -22,7 +23,8 @@
 namespace ssb {
 namespace {
 
-constexpr int kIdxThreads = 192;
+constexpr int kIdxEpiWarps = 8;             // two per TMEM lane quadrant, 4 of the 8 queries each
+constexpr int kIdxThreads = 64 + 32 * kIdxEpiWarps;
 constexpr int kStages = 4;
 constexpr int kAChunk = 128 * 128;          // one 64-dim k-chunk of a pool tile: 128 rows x 128 B
 constexpr int kABytes = 2 * kAChunk;        // 32 KB
@@ -68,7 +70,7 @@ __global__ void __launch_bounds__(kIdxThreads, 1)
     mbar_init(bar_qempty, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_accf + 8 * b, 1);
-      mbar_init(bar_acce + 8 * b, 4);
+      mbar_init(bar_acce + 8 * b, kIdxEpiWarps);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -172,8 +174,8 @@ __global__ void __launch_bounds__(kIdxThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int quad = warp & 3;
+    // ---------------- epilogue (warps 2..9: lane quadrant warp % 4, queries 4 half .. 4 half + 3) ----------------
+    const int quad = warp & 3, half = (warp - 2) >> 2;
     const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     uint32_t iter = 0;
     bool ok = true;
@@ -185,22 +187,29 @@ __global__ void __launch_bounds__(kIdxThreads, 1)
         if (!mbar_wait(bar_accf + 8 * buf, (iter >> 1) & 1, abort_flag, a.status)) { ok = false; break; }
         tc_fence_after();
         const int64_t pool = (int64_t)m * 128 + quad * 32 + lane;
-        for (int j = 0; j < gr.z; ++j) {
-          float v[32];
-          tmem_ld_32x32b_x32(tq + buf * 256 + j * 32, v);
+        // two queries per TMEM wait; four partial sums over the heads (h % 4), added in a fixed order
+        for (int j0 = 4 * half; j0 < min(gr.z, 4 * half + 4); j0 += 2) {
+          const bool two = j0 + 1 < gr.z;
+          float v[2][32];
+          tmem_ld_32x32b_x32(tq + buf * 256 + j0 * 32, v[0]);
+          if (two) tmem_ld_32x32b_x32(tq + buf * 256 + (j0 + 1) * 32, v[1]);
           tmem_ld_wait();
-          const int64_t q = gr.y + j;
-          const float4* wq = reinterpret_cast<const float4*>(a.w + q * 32);
-          float acc = 0.0f;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 w4 = __ldg(wq + i);
-            acc = __fmaf_rn(fmaxf(v[4 * i], 0.0f), w4.x, acc);
-            acc = __fmaf_rn(fmaxf(v[4 * i + 1], 0.0f), w4.y, acc);
-            acc = __fmaf_rn(fmaxf(v[4 * i + 2], 0.0f), w4.z, acc);
-            acc = __fmaf_rn(fmaxf(v[4 * i + 3], 0.0f), w4.w, acc);
+          for (int u = 0; u < 2; ++u) {
+            if (u == 1 && !two) break;
+            const int64_t q = gr.y + j0 + u;
+            const float4* wq = reinterpret_cast<const float4*>(a.w + q * 32);
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 w4 = __ldg(wq + i);
+              acc[0] = __fmaf_rn(fmaxf(v[u][4 * i], 0.0f), w4.x, acc[0]);
+              acc[1] = __fmaf_rn(fmaxf(v[u][4 * i + 1], 0.0f), w4.y, acc[1]);
+              acc[2] = __fmaf_rn(fmaxf(v[u][4 * i + 2], 0.0f), w4.z, acc[2]);
+              acc[3] = __fmaf_rn(fmaxf(v[u][4 * i + 3], 0.0f), w4.w, acc[3]);
+            }
+            if (pool < a.ldl) a.logits[q * a.ldl + pool] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
           }
-          if (pool < a.ldl) a.logits[q * a.ldl + pool] = acc;
         }
         tc_fence_before();
         __syncwarp();
