@@ -806,7 +806,7 @@ def time_components(device, pk: dict) -> dict:
     tab = torch.from_numpy(table).to(device)
     groups = torch.from_numpy(indexer.work_groups(qsl[:-1], lens, prefix)).to(device)
     q_idx = rnd(T, 32, 128).to(torch.bfloat16)
-    w = torch.rand(T, 32, device=device, generator=g)
+    w = torch.rand(T, 32, device=device, generator=g).to(torch.bfloat16)
     kpool = rnd(at * 32, 128).to(torch.bfloat16)
     ldl = int(((positions.max() + 1) // 4 + 127) // 128 * 128)
     logits = torch.empty(T, ldl, device=device)

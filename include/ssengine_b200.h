@@ -197,14 +197,15 @@ int ssb_kda_conv(const ssb_kda_layer* layer, const void* x, int64_t ldx, int64_t
                  void* q, void* k, void* v, void* stream);
 
 /* DSA lightning-indexer logits: logits fp32 [T, ldl], row t, column p = sum_h w[t, h] * relu(q[t, h, :] . k[p, :]) for
- * the pools p of row t's request (q bf16 [T, 32, 128], w fp32 [T, 32] 16-byte aligned; pool keys bf16 in pages of
+ * the pools p of row t's request (q bf16 [T, 32, 128]; w bf16 [T, ldw], the 32 head weights of each row read in place
+ * from the indexer projection's output, 16-byte aligned, ldw % 8 == 0; pool keys bf16 in pages of
  * 32 pools: pool p of request r at row page_table[r * width + p / 32] * 32 + p % 32 of k_cache [pool_rows, 128]).
  * groups int32 [G][4] device = {request, first query row, rows (<= 8, one request), pool tiles of 128 to compute};
  * columns of a computed tile past a row's visible pools ((pos + 1) / 4) hold values of later pools: the top-k's key
  * range [0, (pos + 1) / 4) excludes them. status (device int32, may be NULL) receives 4 if a bounded wait expired.
  * Replaces the fork's DeepGEMM `fp8_mqa_logits` call of the kpool indexer (ssengine/kernels.py config 19;
  * split `split_indexer_prefill_chunks`, ssengine/model/pp_patch.py:587-634). */
-int ssb_indexer_logits(const void* q, const float* w, int64_t T, const void* k_cache, int64_t pool_rows,
+int ssb_indexer_logits(const void* q, const void* w, int64_t ldw, int64_t T, const void* k_cache, int64_t pool_rows,
                        const int32_t* page_table, int64_t width, const int32_t* groups, int64_t G, float* logits,
                        int64_t ldl, int32_t* status, void* stream);
 

@@ -315,12 +315,13 @@ int ssb_kda_conv(const ssb_kda_layer* layer, const void* x, int64_t ldx, int64_t
   return ssb::launch_kda_conv(a, T, q, k, v, static_cast<cudaStream_t>(stream));
 }
 
-int ssb_indexer_logits(const void* q, const float* w, int64_t T, const void* k_cache, int64_t pool_rows,
+int ssb_indexer_logits(const void* q, const void* w, int64_t ldw, int64_t T, const void* k_cache, int64_t pool_rows,
                        const int32_t* page_table, int64_t width, const int32_t* groups, int64_t G, float* logits,
                        int64_t ldl, int32_t* status, void* stream) {
   if (width <= 0 || width > (1 << 24) || G < 0 || G > (1 << 28)) return kErrArgs;
   ssb::IdxArgs a;
   a.w = w;
+  a.ldw = ldw;
   a.T = T;
   a.table = page_table;
   a.width = static_cast<int32_t>(width);

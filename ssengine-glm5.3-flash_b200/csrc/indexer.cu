@@ -35,7 +35,9 @@ constexpr int kOffA = kBBytes;
 constexpr int kOffBar = kOffA + kStages * kABytes;
 // bars: full[S], empty[S], q_full, q_empty, acc_full[2], acc_empty[2], drain
 constexpr int kOffMisc = kOffBar + (2 * kStages + 7) * 8;
-constexpr int kIdxSmem = kOffMisc + 16 + 1024;
+constexpr int kOffW = (kOffMisc + 16 + 127) & ~127;   // fp32 head weights of a group's 8 queries, two buffers [2][8][32]
+static_assert(kOffW % 16 == 0, "float4 reads of the staged weights");
+constexpr int kIdxSmem = kOffW + 2 * 8 * 32 * 4 + 1024;
 
 SSB_DEVICE void drain(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer();
@@ -175,13 +177,27 @@ __global__ void __launch_bounds__(kIdxThreads, 1)
     }
   } else {
     // ---------------- epilogue (warps 2..9: lane quadrant warp % 4, queries 4 half .. 4 half + 3) ----------------
-    const int quad = warp & 3, half = (warp - 2) >> 2;
+    const int quad = warp & 3, half = (warp - 2) >> 2, et = threadIdx.x - 64;
     const uint32_t tq = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    uint32_t iter = 0;
+    float* wsm = reinterpret_cast<float*>(smem + kOffW);
+    uint32_t iter = 0, gcount = 0;
     bool ok = true;
-    for (int gi = blockIdx.x; ok && gi < a.G; gi += gridDim.x) {
+    for (int gi = blockIdx.x; gi < a.G; gi += gridDim.x) {
       const int4 gr = reinterpret_cast<const int4*>(a.groups)[gi];
       if (gr.w <= 0) continue;
+      // the group's head weights (bf16, read in place) -> fp32 in shared memory, one per epilogue thread; buffer
+      // gcount & 1 was last read two groups ago, by warps that have all passed the previous group's barrier. The
+      // barrier also carries a failed wait of any epilogue warp, so that all of them leave together.
+      float* wg = wsm + (gcount & 1) * 256;
+      {
+        const int j = et >> 5, hd = et & 31;
+        if (ok && j < gr.z) {
+          const uint16_t wb = static_cast<const uint16_t*>(a.w)[(int64_t)(gr.y + j) * a.ldw + hd];
+          wg[et] = __uint_as_float(static_cast<uint32_t>(wb) << 16);
+        }
+      }
+      if (named_bar_or(3, 32 * kIdxEpiWarps, !ok)) break;
+      ++gcount;
       for (int m = 0; m < gr.w; ++m) {
         const int buf = iter & 1;
         if (!mbar_wait(bar_accf + 8 * buf, (iter >> 1) & 1, abort_flag, a.status)) { ok = false; break; }
@@ -198,11 +214,11 @@ __global__ void __launch_bounds__(kIdxThreads, 1)
           for (int u = 0; u < 2; ++u) {
             if (u == 1 && !two) break;
             const int64_t q = gr.y + j0 + u;
-            const float4* wq = reinterpret_cast<const float4*>(a.w + q * 32);
+            const float4* wq = reinterpret_cast<const float4*>(wg + (j0 + u) * 32);
             float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const float4 w4 = __ldg(wq + i);
+              const float4 w4 = wq[i];                        // heads 4i .. 4i + 3 (a broadcast read)
               acc[0] = __fmaf_rn(fmaxf(v[u][4 * i], 0.0f), w4.x, acc[0]);
               acc[1] = __fmaf_rn(fmaxf(v[u][4 * i + 1], 0.0f), w4.y, acc[1]);
               acc[2] = __fmaf_rn(fmaxf(v[u][4 * i + 2], 0.0f), w4.z, acc[2]);
@@ -255,7 +271,7 @@ int launch_indexer_logits(const void* q, const void* k_cache, int64_t pool_rows,
                           cudaStream_t stream) {
   if (q == nullptr || k_cache == nullptr || a.w == nullptr || a.table == nullptr || a.groups == nullptr ||
       a.logits == nullptr || a.T <= 0 || pool_rows <= 0 || a.width <= 0 || a.G < 0 || a.ldl <= 0 ||
-      (reinterpret_cast<uintptr_t>(a.w) & 15))
+      (reinterpret_cast<uintptr_t>(a.w) & 15) || a.ldw < 32 || (a.ldw % 8))
     return kErrArgs;
   if (a.G == 0) return kOk;
   CUtensorMap mq, mk;

@@ -151,7 +151,8 @@ int launch_kda_conv(const KdaArgs& a, int64_t T, void* q, void* k, void* v, cuda
 
 // DSA indexer (csrc/indexer.cu).
 struct IdxArgs {
-  const float* w = nullptr;            // [T, 32] head weights
+  const void* w = nullptr;             // bf16 [T, ldw] head weights (32 used)
+  int64_t ldw = 0;
   int64_t T = 0;                       // query rows
   const int32_t* table = nullptr;      // [R, width] pool pages (= KV pages) of each request
   int32_t width = 0;

@@ -42,13 +42,15 @@ def key_ranges(positions: torch.Tensor):
 
 def logits(q: torch.Tensor, w: torch.Tensor, k_cache: torch.Tensor, page_table: torch.Tensor, groups: torch.Tensor,
            out: torch.Tensor, status: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-    """q bf16 [T, 32, 128], w fp32 [T, 32], k_cache bf16 [pages * 32, 128], page_table int32 [R, width], groups int32
+    """q bf16 [T, 32, 128], w bf16 [T, >= 32] head weights (a column view of the projection output: unit column
+    stride, row stride a multiple of 8), k_cache bf16 [pages * 32, 128], page_table int32 [R, width], groups int32
     [G, 4] (device), out fp32 [T, ldl]."""
     so = lib.load()
     assert q.dtype == torch.bfloat16 and q.is_contiguous() and q.shape[1:] == (HEADS, DIM)
-    assert w.dtype == torch.float32 and w.is_contiguous() and k_cache.dtype == torch.bfloat16
+    assert w.dtype == torch.bfloat16 and w.stride(1) == 1 and w.shape[1] >= HEADS and k_cache.dtype == torch.bfloat16
     assert page_table.dtype == torch.int32 and groups.dtype == torch.int32 and out.dtype == torch.float32
-    rc = so.ssb_indexer_logits(q.data_ptr(), w.data_ptr(), q.shape[0], k_cache.data_ptr(), k_cache.shape[0],
+    rc = so.ssb_indexer_logits(q.data_ptr(), w.data_ptr(), w.stride(0), q.shape[0], k_cache.data_ptr(),
+                               k_cache.shape[0],
                                page_table.data_ptr(), page_table.shape[1], groups.data_ptr(), groups.shape[0],
                                out.data_ptr(), out.stride(0), None if status is None else status.data_ptr(),
                                lib.stream_ptr(stream))

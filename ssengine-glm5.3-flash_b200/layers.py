@@ -473,7 +473,7 @@ class DsaAttention:
         idx = torch.empty(T, self.idx_proj.N_pad, **bf)
         self.idx_proj(y, idx, status, stream)
         k_idx, gate = idx[:, :self.IDX_DIM], idx[:, self.IDX_DIM + self.IDX_HEADS:2 * self.IDX_DIM + self.IDX_HEADS]
-        w = idx[:, self.IDX_DIM:self.IDX_DIM + self.IDX_HEADS].float().contiguous()
+        w = idx[:, self.IDX_DIM:self.IDX_DIM + self.IDX_HEADS]          # bf16 head weights, read in place
         indexer.kpool_insert(k_idx, gate, self.ape, kpool_reqs, max_rows, page_table, pool_cache, tail_ring, stream)
         ldl = _round(int(page_table.shape[1]) * self.POOLS_PER_PAGE, 128)
         ws = self.logits_ws

@@ -140,7 +140,7 @@ _SIGS = {
     "ssb_flag_wait": ([_P, ctypes.c_uint32, _I64, _P, _P], ctypes.c_int),
     "ssb_flag_write": ([_P, ctypes.c_uint32, _P], ctypes.c_int),
     "ssb_p2p_copy": ([_P, _P, _I64, _P], ctypes.c_int),
-    "ssb_indexer_logits": ([_P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P], ctypes.c_int),
+    "ssb_indexer_logits": ([_P, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P], ctypes.c_int),
     "ssb_indexer_expand": ([_P, _I64, _I32, _P, _I64, _P, _I64, _P], ctypes.c_int),
     "ssb_sparse_mla": ([_P, _I64, _P, _P, _I64, _I32, _P, _I32, _P, _I64, _F, _F, _P, _P, _P], ctypes.c_int),
     "ssb_mla_cache_append": ([_P, _I64, _P, _I64, _P, _F, _P], ctypes.c_int),

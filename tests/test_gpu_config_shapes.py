@@ -142,7 +142,7 @@ def test_indexer_selection_beyond_16k(cuda):
     positions = np.concatenate([np.arange(s, s + n) for s, n in reqs]).astype(np.int64)
     assert ((positions + 1) // 4).min() > 4 * 512          # every row sees more pools than it selects
     q = bf16(rng.standard_normal((T, 32, 128)))
-    w = rng.uniform(0, 1, (T, 32)).astype(np.float32)
+    w = bf16(rng.uniform(0, 1, (T, 32)))                  # the head weights arrive as bf16
     kc = bf16(rng.standard_normal((n_pages * 32, 128)))
     d = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a)).to(dt).to(cuda)
     groups = indexer.work_groups(qsl[:-1], [n for _, n in reqs], [s for s, _ in reqs])
@@ -150,7 +150,7 @@ def test_indexer_selection_beyond_16k(cuda):
     logits = torch.full((T, ldl), float("nan"), dtype=torch.float32, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
     pos = d(positions, torch.int64)
-    indexer.logits(d(q, torch.bfloat16), d(w, torch.float32), d(kc, torch.bfloat16), d(table, torch.int32),
+    indexer.logits(d(q, torch.bfloat16), d(w, torch.bfloat16), d(kc, torch.bfloat16), d(table, torch.int32),
                    d(groups, torch.int32), logits, status)
     ids = torch.empty(T, 512, dtype=torch.int32, device=cuda)
     indexer.topk(logits, pos, 512, ids)

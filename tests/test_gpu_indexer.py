@@ -36,7 +36,8 @@ def setup(cuda, seed=0):
     k = rng.standard_normal((rows, 128)).astype(np.float32)
     w = rng.uniform(-1, 1, (T, 32)).astype(np.float32)
     bf = lambda a: torch.from_numpy(a).to(torch.bfloat16).to(cuda)
-    dev = dict(q=bf(q), k=bf(k), w=torch.from_numpy(w).to(cuda), table=torch.from_numpy(table).to(cuda),
+    w = bf(w).float().cpu().numpy()                          # the head weights arrive as bf16
+    dev = dict(q=bf(q), k=bf(k), w=bf(w), table=torch.from_numpy(table).to(cuda),
                pos=torch.from_numpy(positions).to(cuda))
     host = dict(q=dev["q"].float().cpu().numpy(), k=dev["k"].float().cpu().numpy(), w=w, table=table,
                 pos=positions, q_starts=q_starts)
