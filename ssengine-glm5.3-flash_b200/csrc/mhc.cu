@@ -570,17 +570,21 @@ __global__ void __launch_bounds__(kMixThreads, 1)
   }
 }
 
+// Finalize: 16 tokens per CTA, 16 threads a token in the y passes (two 128-position steps of loads in flight), up
+// to four CTAs an SM: at T = 8192 every CTA is resident at once.
+constexpr int kFinTok = 16;
+
 template <bool POST>
-__global__ void __launch_bounds__(kMhcThreads, 2) mhc_final_kernel(const MhcArgs a, const float* part,
+__global__ void __launch_bounds__(kMhcThreads, 4) mhc_final_kernel(const MhcArgs a, const float* part,
                                                                     const float* part_ss) {
-  __shared__ float mix[kMhcTok][kMhcMix];
-  __shared__ float ssq[kMhcTok];
-  __shared__ float pre_s[kMhcTok][4];
+  __shared__ float mix[kFinTok][kMhcMix];
+  __shared__ float ssq[kFinTok];
+  __shared__ float pre_s[kFinTok][4];
   const int tid = threadIdx.x;
-  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kMhcTok;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kFinTok;
   const int64_t H = a.H;
   const int64_t QT = a.T * kMhcMix;
-  for (int i = tid; i < kMhcTok * kMhcMix; i += kMhcThreads) {
+  for (int i = tid; i < kFinTok * kMhcMix; i += kMhcThreads) {
     const int tk = i / kMhcMix, c = i % kMhcMix;
     const int64_t o = (t0 + tk) * kMhcMix + c;
     float v = 0.0f;                                    // the mix kernel's partials in a fixed order
@@ -591,7 +595,7 @@ __global__ void __launch_bounds__(kMhcThreads, 2) mhc_final_kernel(const MhcArgs
     }
     mix[tk][c] = v;
   }
-  if (tid < kMhcTok) {
+  if (tid < kFinTok) {
     const int64_t tt = t0 + tid;
     float v = 0.0f;
     if (tt < a.T) {
@@ -602,7 +606,7 @@ __global__ void __launch_bounds__(kMhcThreads, 2) mhc_final_kernel(const MhcArgs
     ssq[tid] = v;
   }
   __syncthreads();
-  if (tid < kMhcTok && t0 + tid < a.T) {
+  if (tid < kFinTok && t0 + tid < a.T) {
     const int64_t tt = t0 + tid;
     const float rinv = rsqrtf(ssq[tid] / static_cast<float>(4 * H) + a.rms_eps);
     float mx[kMhcMix];
@@ -655,31 +659,31 @@ __global__ void __launch_bounds__(kMhcThreads, 2) mhc_final_kernel(const MhcArgs
       for (int j = 0; j < 4; ++j) a.comb_out[tt * 16 + i * 4 + j] = cb[i][j];
   }
   __syncthreads();
-  const int tl = tid >> 3;                             // this thread's token in the tile (y passes)
-  const int seg = (tid & 7) * 8;                       // its 8 hidden positions in each 64-position step
+  const int tl = tid >> 4;                             // this thread's token in the tile (y passes)
+  const int seg = (tid & 15) * 8;                      // its 8 hidden positions in each 128-position step
   const int64_t t = t0 + tl;
   const bool tv = t < a.T;
-  // ---- layer input and its RMSNorm: token tl, positions seg + 64 m (two passes over the new residual, from L2) ----
-  // (no early return: the 8 lanes of a token reduce with shuffles, so every lane of the warp stays)
+  constexpr int kStep = 128, kU = 2;
+  // ---- layer input and its RMSNorm: token tl, positions seg + 128 m (two passes over the new residual, from L2) ----
+  // (no early return: the 16 lanes of a token reduce with shuffles, so every lane of the warp stays)
   const __nv_bfloat16* src = POST ? a.new_res : a.res;
   float p[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) p[i] = tv ? pre_s[tl][i] : 0.0f;
   float ls = 0.0f;
-  // two positions groups per iteration, all loads issued before the stores (the stores to y could alias src for all
-  // the compiler knows)
-  for (int64_t hh = seg; tv && hh < H; hh += 2 * kMhcH) {
-    const bool two = hh + kMhcH < H;
-    uint4 rv[2][4];
+  // kU steps per iteration, all loads issued before the stores (the stores to y could alias src for all the compiler
+  // knows)
+  for (int64_t hh = seg; tv && hh < H; hh += kU * kStep) {
+    uint4 rv[kU][4];
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
+    for (int u = 0; u < kU; ++u)
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        rv[u][i] = (u == 0 || two) ? *reinterpret_cast<const uint4*>(src + (t * 4 + i) * H + hh + u * kMhcH)
-                                   : make_uint4(0, 0, 0, 0);
+        rv[u][i] = hh + u * kStep < H ? *reinterpret_cast<const uint4*>(src + (t * 4 + i) * H + hh + u * kStep)
+                                      : make_uint4(0, 0, 0, 0);
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      if (u == 1 && !two) break;
+    for (int u = 0; u < kU; ++u) {
+      if (hh + u * kStep >= H) break;
       uint32_t w[4];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -693,29 +697,29 @@ __global__ void __launch_bounds__(kMhcThreads, 2) mhc_final_kernel(const MhcArgs
         if (e & 1) w[e >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(b)) << 16;
         else w[e >> 1] = __bfloat16_as_ushort(b);
       }
-      *reinterpret_cast<uint4*>(a.y + t * H + hh + u * kMhcH) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(a.y + t * H + hh + u * kStep) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 #pragma unroll
-  for (int off = 4; off > 0; off >>= 1) ls += __shfl_xor_sync(0xFFFFFFFFu, ls, off);
+  for (int off = 8; off > 0; off >>= 1) ls += __shfl_xor_sync(0xFFFFFFFFu, ls, off);
   const float inv = rsqrtf(ls / static_cast<float>(H) + a.norm_eps);
-  for (int64_t hh = seg; tv && hh < H; hh += 4 * kMhcH) {
-    uint4 v[4], wv[4];
+  for (int64_t hh = seg; tv && hh < H; hh += kU * kStep) {
+    uint4 v[kU], wv[kU];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (hh + u * kMhcH < H) {
-        v[u] = *reinterpret_cast<const uint4*>(a.y + t * H + hh + u * kMhcH);
-        wv[u] = *reinterpret_cast<const uint4*>(a.norm_w + hh + u * kMhcH);
+    for (int u = 0; u < kU; ++u) {
+      if (hh + u * kStep < H) {
+        v[u] = *reinterpret_cast<const uint4*>(a.y + t * H + hh + u * kStep);
+        wv[u] = *reinterpret_cast<const uint4*>(a.norm_w + hh + u * kStep);
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (hh + u * kMhcH >= H) break;
+    for (int u = 0; u < kU; ++u) {
+      if (hh + u * kStep >= H) break;
       __nv_bfloat16* vb = reinterpret_cast<__nv_bfloat16*>(&v[u]);
       const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv[u]);
 #pragma unroll
       for (int e = 0; e < 8; ++e) vb[e] = __float2bfloat16(__bfloat162float(vb[e]) * inv * __bfloat162float(wb[e]));
-      *reinterpret_cast<uint4*>(a.y + t * H + hh + u * kMhcH) = v[u];
+      *reinterpret_cast<uint4*>(a.y + t * H + hh + u * kStep) = v[u];
     }
   }
 }
@@ -780,7 +784,7 @@ int launch_mhc(bool do_post, bool do_pre, const void* x, const void* res, const 
   if (rc == kOk) {
     const int64_t items = (T + kMixTok - 1) / kMixTok * a.ranges;
     const unsigned gmix = static_cast<unsigned>(std::min<int64_t>(items, device_sm_count()));
-    const unsigned gfin = static_cast<unsigned>((T + kMhcTok - 1) / kMhcTok);
+    const unsigned gfin = static_cast<unsigned>((T + kFinTok - 1) / kFinTok);
     if (do_post) {
       mhc_mix_kernel<true><<<gmix, kMixThreads, kMixSmem, stream>>>(mres, mx, mfn, a, part, part_ss);
       mhc_final_kernel<true><<<gfin, kMhcThreads, 0, stream>>>(a, part, part_ss);
