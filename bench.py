@@ -291,8 +291,9 @@ def run_pipeline(args, rank: int, world: int, local: int) -> None:
     stage = StageModel(cfg, rank, device)
     pipe = None
     if world > 1:
-        pipe = P2pPipe(rank, world, device, None, max_in_flight=4, max_rows=args.tokens, width=stage.hidden_width,
-                       init_group=False, wait_ns=60_000_000_000)
+        # up to world + 2 microbatches in flight: every stage busy, with slack for the edge hop and uneven stages
+        pipe = P2pPipe(rank, world, device, None, max_in_flight=world + 2, max_rows=args.tokens,
+                       width=stage.hidden_width, init_group=False, wait_ns=60_000_000_000)
     worker = StageWorker(stage, pipe, events=True)
     batches = [stage.prepare(p) for p in plans]
     pack_bytes = [int(b.keep[0].numel()) for b in batches[n_warm:]]
