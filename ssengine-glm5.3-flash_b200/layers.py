@@ -326,9 +326,16 @@ class Bf16Grouped:
 
     def __call__(self, x_heads: torch.Tensor, rows_pad: int, out: torch.Tensor, status=None, stream=None):
         """x_heads bf16 [heads * rows_pad, K] (head-major) -> out bf16 [heads * rows_pad, N]."""
+        return self.bmm(x_heads.view(self.heads, rows_pad, self.K), out.view(self.heads, rows_pad, self.N), stream)
+
+    def bmm(self, x: torch.Tensor, out: torch.Tensor, stream=None) -> torch.Tensor:
+        """x bf16 [heads, rows, K], out bf16 [heads, rows, N], each with unit column stride and any row / head
+        strides (e.g. a head's slice of token-major rows, x[h] = rows[:, h, :K]): the batched GEMM reads and writes
+        them in place (cuBLAS strided batched, leading dimension = the row stride, batch stride = the head stride),
+        so no head transposes run around it."""
+        assert x.dtype == torch.bfloat16 and x.stride(2) == 1 and out.stride(2) == 1
         with torch.cuda.stream(stream) if stream is not None else _null():
-            torch.bmm(x_heads.view(self.heads, rows_pad, self.K), self.wt,
-                      out=out.view(self.heads, rows_pad, self.N))
+            torch.bmm(x, self.wt, out=out)
         return out
 
 
@@ -459,14 +466,11 @@ class DsaAttention:
         self.q_b(qa, q, status, stream)
         lib.check("ssb_rope", so.ssb_rope(q[:, self.nope:].data_ptr(), q.stride(0), NH, self.qh, positions.data_ptr(),
                                           T, self.theta, s))
-        Tp = _round(max(T, 1), 128)
-        qn = torch.empty(NH * Tp, self.nope, **bf)
-        lib.check("ssb_transpose_heads", so.ssb_transpose_heads(q.data_ptr(), qn.data_ptr(), T, Tp, NH, self.nope,
-                                                                q.stride(0), self.qh, 1, s))
-        q_lat = torch.empty(NH * Tp, L, **bf)
-        self.w_uk(qn, Tp, q_lat, status, stream)
+        # absorb: each head's nope slice read in place from the token-major q rows, head-major latent out
+        q_lat = torch.empty(NH * T, L, **bf)
+        self.w_uk.bmm(q.view(T, NH, self.qh)[:, :, :self.nope].permute(1, 0, 2), q_lat.view(NH, T, L), stream)
         q8 = torch.empty(T, NH, L + RP, dtype=torch.uint8, device=dev)
-        mla.q_pack(q_lat, Tp, q[:, self.nope:], self.qh, T, q8, self.q_scale, stream)
+        mla.q_pack(q_lat, T, q[:, self.nope:], self.qh, T, q8, self.q_scale, stream)
         # indexer
         q_idx = torch.empty(T, self.IDX_HEADS * self.IDX_DIM, **bf)
         self.wq_idx(qa, q_idx, status, stream)
@@ -491,14 +495,11 @@ class DsaAttention:
         o_lat = torch.empty(T, NH, L, **bf)
         mla.sparse_mla(q8, kv_cache, tok, qsl, page_table, self.scale * self.q_scale * self.k_scale, o_lat,
                        bmm2=self.k_scale, n_idx=4 * self.TOPK + 3, stream=stream, status=status)
-        oh = torch.empty(NH * Tp, L, **bf)
-        lib.check("ssb_transpose_heads", so.ssb_transpose_heads(o_lat.data_ptr(), oh.data_ptr(), T, Tp, NH, L, NH * L,
-                                                                L, 1, s))
-        v = torch.empty(NH * Tp, self.v_dim, **bf)
-        self.w_uv(oh, Tp, v, status, stream)
+        # v_up: each head's latent rows read in place from the token-major attention output, written straight into
+        # the token-major o_proj input
         o_in = torch.empty(T, NH * self.v_dim, **bf)
-        lib.check("ssb_transpose_heads", so.ssb_transpose_heads(v.data_ptr(), o_in.data_ptr(), T, Tp, NH, self.v_dim,
-                                                                NH * self.v_dim, self.v_dim, 0, s))
+        v = o_in.view(T, NH, self.v_dim).permute(1, 0, 2)
+        self.w_uv.bmm(o_lat.permute(1, 0, 2), v, stream)
         out = torch.empty(T, self.H, **bf)
         self.o_proj(o_in, out, status, stream)
         if keep:
