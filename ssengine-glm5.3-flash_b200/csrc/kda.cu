@@ -302,10 +302,36 @@ __global__ void __launch_bounds__(kKdaThreads, 2)
   __syncthreads();
   if (*abort_flag) return;
   if (item) {
+    // the taps of each channel pair and the window rows as packed fp32 pairs: every row is unpacked once, the four
+    // products of a pair run as fp32x2 FMAs (each element rounded as the scalar chain w0 a + w1 b + w2 c + w3 d)
+    uint64_t w2[16], xa[4], xb[4], xc[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+      for (int tap = 0; tap < 4; ++tap) w2[4 * q + tap] = f2pack(wf[(2 * q) * 4 + tap], wf[(2 * q + 1) * 4 + tap]);
+      xa[q] = bf2_f2((&x0.x)[q]);
+      xb[q] = bf2_f2((&x1.x)[q]);
+      xc[q] = bf2_f2((&x2.x)[q]);
+    }
 #pragma unroll 1
     for (int i = i0; i < i1; ++i) {
       const uint4 x3 = *trow(i);
-      const uint4 y = (i < n) ? conv8(x0, x1, x2, x3, wf) : make_uint4(0, 0, 0, 0);
+      uint64_t xd[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) xd[q] = bf2_f2((&x3.x)[q]);
+      uint4 y = make_uint4(0, 0, 0, 0);
+      if (i < n) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint64_t acc = fma2(w2[4 * q], xa[q], 0ull);
+          acc = fma2(w2[4 * q + 1], xb[q], acc);
+          acc = fma2(w2[4 * q + 2], xc[q], acc);
+          acc = fma2(w2[4 * q + 3], xd[q], acc);
+          float lo, hi;
+          f2unpack(acc, lo, hi);
+          (&y.x)[q] = pack_bf16(silu_conv(lo), silu_conv(hi));
+        }
+      }
       *trow(i) = y;
       if (grp < 32) {
         float f[8];
@@ -315,9 +341,12 @@ __global__ void __launch_bounds__(kKdaThreads, 2)
         for (int c = 0; c < 8; ++c) ss = __fmaf_rn(f[c], f[c], ss);
         NP[i * 32 + grp] = ss;
       }
-      x0 = x1;
-      x1 = x2;
-      x2 = x3;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        xa[q] = xb[q];
+        xb[q] = xc[q];
+        xc[q] = xd[q];
+      }
     }
   }
   __syncthreads();

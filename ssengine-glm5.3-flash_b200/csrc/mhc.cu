@@ -52,32 +52,6 @@ struct MhcArgs {
 
 SSB_DEVICE float sigmoidf(float v) { return 1.0f / (1.0f + expf(-v)); }
 
-// Packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE single-precision operations per instruction, each rounded as
-// the scalar one would be).
-SSB_DEVICE uint64_t f2pack(float lo, float hi) {
-  uint64_t d;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
-  return d;
-}
-SSB_DEVICE void f2unpack(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
-SSB_DEVICE uint64_t mul2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-SSB_DEVICE uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-// bf16 pair (low element in the low half) -> packed fp32 {lo, hi}; packed fp32 -> bf16 pair, round to nearest even
-SSB_DEVICE uint64_t bf2_f2(uint32_t w) { return f2pack(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u)); }
-SSB_DEVICE uint32_t f2_bf2(uint64_t v) {
-  float lo, hi;
-  f2unpack(v, lo, hi);
-  const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&b);
-}
 
 template <bool POST, bool PRE>
 __global__ void __launch_bounds__(kMhcThreads, 2) mhc_kernel(const MhcArgs a) {

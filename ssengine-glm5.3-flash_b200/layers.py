@@ -73,14 +73,20 @@ class Nvfp4Linear:
                                                              status.data_ptr(), lib.stream_ptr(stream)))
         return out
 
-    def __call__(self, x: torch.Tensor, out: torch.Tensor, status: torch.Tensor, stream=None) -> torch.Tensor:
-        """x bf16 [T, >= K] (row pitch x.stride(0)), out bf16 [T, >= N_pad] (row pitch out.stride(0))."""
+    def quantize(self, x: torch.Tensor, stream=None) -> tuple:
+        """x bf16 [T, >= K] -> (codes, scale atoms) of its NVFP4 form with `gs_in`, reusable by every projection of
+        the same K and global scale."""
         T = x.shape[0]
         codes, sf = self.input_buffers(T)
         lib.check("ssb_nvfp4_quantize", self._lib.ssb_nvfp4_quantize(x.data_ptr(), T, self.K, x.stride(0), self.gs_in,
                                                                      codes.data_ptr(), self.K // 2, sf.data_ptr(),
                                                                      lib.stream_ptr(stream)))
-        return self.gemm(codes, sf, T, out, status, stream)
+        return codes, sf
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor, status: torch.Tensor, stream=None) -> torch.Tensor:
+        """x bf16 [T, >= K] (row pitch x.stride(0)), out bf16 [T, >= N_pad] (row pitch out.stride(0))."""
+        codes, sf = self.quantize(x, stream)
+        return self.gemm(codes, sf, x.shape[0], out, status, stream)
 
 
 class DenseFfn:
@@ -448,7 +454,10 @@ class DsaAttention:
         so, QL, L, RP, NH = self._lib, self.q_lora, self.LATENT, self.ROPE, self.HEADS
         bf = dict(dtype=torch.bfloat16, device=dev)
         a = torch.empty(T, self.a_proj.N_pad, **bf)
-        self.a_proj(y, a, status, stream)
+        # y feeds a_proj and idx_proj, qa feeds q_b and wq_idx: each quantized once (same K, same static scale)
+        assert self.a_proj.gs_in == self.idx_proj.gs_in and self.q_b.gs_in == self.wq_idx.gs_in
+        y_q = self.a_proj.quantize(y, stream)
+        self.a_proj.gemm(*y_q, T, a, status, stream)
         qa = torch.empty(T, QL, **bf)
         kv_rows = torch.empty(T, L + RP, **bf)
         lib.check("ssb_rmsnorm_cols", so.ssb_rmsnorm_cols(a.data_ptr(), a.stride(0), QL, T, self.q_norm.data_ptr(),
@@ -463,7 +472,8 @@ class DsaAttention:
         mla.cache_append(kv_rows, slots, kv_cache, self.k_scale, stream)
         # queries: q_b, rope on each head's rope slice, absorb of each head's nope part into the latent
         q = torch.empty(T, NH * self.qh, **bf)
-        self.q_b(qa, q, status, stream)
+        qa_q = self.q_b.quantize(qa, stream)
+        self.q_b.gemm(*qa_q, T, q, status, stream)
         lib.check("ssb_rope", so.ssb_rope(q[:, self.nope:].data_ptr(), q.stride(0), NH, self.qh, positions.data_ptr(),
                                           T, self.theta, s))
         # absorb: each head's nope slice read in place from the token-major q rows, head-major latent out
@@ -473,9 +483,9 @@ class DsaAttention:
         mla.q_pack(q_lat, T, q[:, self.nope:], self.qh, T, q8, self.q_scale, stream)
         # indexer
         q_idx = torch.empty(T, self.IDX_HEADS * self.IDX_DIM, **bf)
-        self.wq_idx(qa, q_idx, status, stream)
+        self.wq_idx.gemm(*qa_q, T, q_idx, status, stream)
         idx = torch.empty(T, self.idx_proj.N_pad, **bf)
-        self.idx_proj(y, idx, status, stream)
+        self.idx_proj.gemm(*y_q, T, idx, status, stream)
         k_idx, gate = idx[:, :self.IDX_DIM], idx[:, self.IDX_DIM + self.IDX_HEADS:2 * self.IDX_DIM + self.IDX_HEADS]
         w = idx[:, self.IDX_DIM:self.IDX_DIM + self.IDX_HEADS]          # bf16 head weights, read in place
         indexer.kpool_insert(k_idx, gate, self.ape, kpool_reqs, max_rows, page_table, pool_cache, tail_ring, stream)
