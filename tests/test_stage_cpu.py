@@ -114,3 +114,26 @@ def test_microbatch_former_covers_every_token_and_keeps_the_block_contract():
                 assert seen[c.req_id] == lens[int(c.req_id[1:])]
     assert sorted(seen.values()) == sorted(lens.tolist())          # every prompt fully prefilled
     assert all(sum(c.num_tokens for c in p.chunks) == 8192 for p in plans[:-1])
+
+
+def test_head_batched_gemm_reads_and_writes_token_major_rows_in_place():
+    """The DSA absorb / v_up GEMMs take each head's slice of token-major rows as a strided batch (no transposes):
+    q[t, h, :nope] -> head-major latent rows, and o_lat[t, h, :] -> the token-major o_proj input o_in[t, h * v + j]."""
+    import torch
+
+    from ssengine_b200.layers import Bf16Grouped
+
+    g = torch.Generator().manual_seed(5)
+    T, NH, qh, nope, L, vd = 37, 4, 24, 16, 32, 8
+    q = torch.randn(T, NH * qh, generator=g).to(torch.bfloat16)
+    uk = Bf16Grouped(g, NH, L, nope, "cpu")
+    lat = torch.empty(NH * T, L, dtype=torch.bfloat16)
+    uk.bmm(q.view(T, NH, qh)[:, :, :nope].permute(1, 0, 2), lat.view(NH, T, L))
+    want = torch.einsum("thk,hlk->htl", q.view(T, NH, qh)[:, :, :nope].float(), uk.w.float())
+    torch.testing.assert_close(lat.view(NH, T, L).float(), want, rtol=2e-2, atol=2e-2)
+    uv = Bf16Grouped(g, NH, vd, L, "cpu")
+    o_lat = torch.randn(T, NH, L, generator=g).to(torch.bfloat16)
+    o_in = torch.full((T, NH * vd), float("nan"), dtype=torch.bfloat16)
+    uv.bmm(o_lat.permute(1, 0, 2), o_in.view(T, NH, vd).permute(1, 0, 2))
+    want = torch.einsum("thl,hvl->thv", o_lat.float(), uv.w.float()).reshape(T, NH * vd)
+    torch.testing.assert_close(o_in.float(), want, rtol=2e-2, atol=2e-2)
