@@ -320,8 +320,13 @@ class StageModel:
             check_blocks(chunks, self.num_blocks)
             # one sequence table per KDA state group g2..g6: the chunk's state_blocks[g] (has state = the chunk
             # continues its request)
-            ks = np.array([[(int(qsl[r]), int(qsl[r + 1]), int(chunks[i].state_blocks[g]), int(chunks[i].start > 0))
-                            for r, i in enumerate(order)] for g in range(5)], dtype=np.int32).reshape(5, -1, 4)
+            # Rows longest first: the scan runs one CTA per (sequence, head, value half) in table order, so the longest
+            # sequences start first (an LPT order, in the place of the reference's head-split plan); each sequence's
+            # result does not depend on its place in the table.
+            lpt = sorted(range(R), key=lambda r: -int(q_lens[r]))
+            ks = np.array([[(int(qsl[r]), int(qsl[r + 1]), int(chunks[order[r]].state_blocks[g]),
+                             int(chunks[order[r]].start > 0)) for r in lpt] for g in range(5)],
+                          dtype=np.int32).reshape(5, -1, 4)
             h["kda"] = pk.add(ks)
         if any(self.is_dsa):
             from .indexer import work_groups
