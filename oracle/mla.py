@@ -107,7 +107,7 @@ def sparse_mla_fp8p(q, kv8, cols, pages, bmm1: float, bmm2: float) -> np.ndarray
         mb = x.max(axis=1)
         fresh = m == -np.inf
         jump = ~fresh & (mb > m + np.float32(LAZY))
-        alpha = np.where(jump, np.exp2((m - mb).astype(np.float32)), 1.0)
+        alpha = np.where(jump, np.exp2(np.where(jump, m - mb, 0).astype(np.float32)), 1.0)
         o *= alpha[:, None]
         l *= alpha
         m = np.where(fresh | jump, mb, m).astype(np.float32)
