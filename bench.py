@@ -49,7 +49,8 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch at T = 8192, from the ncu capture summarised in
 # profiles/gemm_nvfp4_moe_T8192_full.md (796.9 MB + 39.6 MB); None for other token counts
 GATE_UP_TRAFFIC_T8192 = 836.4e6
-BASELINE_PP4_TOK_S = 138_400.0        # the reference's saturated 8k prefill at PP4 on 4 x B200
+BASELINE_PP4_TOK_S = 138_400.0        # the reference's published saturated 8k prefill at PP4 on 4 x B200
+                                      # (its docs/results/fp8.md:59)
 N_LAYERS, MB_TOKENS, N_PROMPTS = 45, 8192, 256
 MB_PER_STEP = 4                       # pipeline: a step = 4 microbatches, so K = 20 steps time 80 microbatches
 MODEL = dict(hidden=4096, inter=1024, experts=128, top_k=8, vocab=151_552, kda_heads=64, q_lora=1536, mla_nope=192,

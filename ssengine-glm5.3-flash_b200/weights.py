@@ -1,5 +1,5 @@
 """Seeded random-init NVFP4 parameters (there is no checkpoint in this setting; the CUDA path and the CPU checker are
-fed from the same generator so that parity is judged on identical quantized weights).
+fed from the same generator so that parity is checked on identical quantized weights).
 
 MoE layer: e2m1 codes uniform over the 16 codes; e4m3 block scales uniform over the e4m3 codes
 whose value lies in [2^-8, 2^0] (55 codes: evenly spaced in log2 within each binade, a log-uniform draw on the
