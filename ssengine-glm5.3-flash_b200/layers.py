@@ -439,8 +439,14 @@ class DsaAttention:
         self.scale = self.qh ** -0.5
         self.q_scale, self.k_scale = 1.0, 1.0          # per-tensor FP8 scales of the query and the latent cache
         self.logits_ws = None          # optional fp32 buffer the logits rows are cut from (a stage's shared one)
+        self._side = None              # the indexer branch's stream (created on first use)
         self.device = dev
         self._lib = lib.load()
+
+    def _side_stream(self) -> torch.cuda.Stream:
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=self.device)
+        return self._side
 
     def forward(self, y, positions, slots, qsl, page_table, kpool_reqs, max_rows, groups, kv_cache, pool_cache,
                 tail_ring, status, stream=None, keep: bool = False):
@@ -470,37 +476,47 @@ class DsaAttention:
         lib.check("ssb_concat_cols", so.ssb_concat_cols(kvn.data_ptr(), L, L, k_rope.data_ptr(), a.stride(0), RP,
                                                         kv_rows.data_ptr(), L + RP, T, s))
         mla.cache_append(kv_rows, slots, kv_cache, self.k_scale, stream)
-        # queries: q_b, rope on each head's rope slice, absorb of each head's nope part into the latent
+        # buffers of both branches, allocated on the layer's stream before the fork
         q = torch.empty(T, NH * self.qh, **bf)
-        qa_q = self.q_b.quantize(qa, stream)
-        self.q_b.gemm(*qa_q, T, q, status, stream)
-        lib.check("ssb_rope", so.ssb_rope(q[:, self.nope:].data_ptr(), q.stride(0), NH, self.qh, positions.data_ptr(),
-                                          T, self.theta, s))
-        # absorb: each head's nope slice read in place from the token-major q rows, head-major latent out
         q_lat = torch.empty(NH * T, L, **bf)
-        self.w_uk.bmm(q.view(T, NH, self.qh)[:, :, :self.nope].permute(1, 0, 2), q_lat.view(NH, T, L), stream)
         q8 = torch.empty(T, NH, L + RP, dtype=torch.uint8, device=dev)
-        mla.q_pack(q_lat, T, q[:, self.nope:], self.qh, T, q8, self.q_scale, stream)
-        # indexer
         q_idx = torch.empty(T, self.IDX_HEADS * self.IDX_DIM, **bf)
-        self.wq_idx.gemm(*qa_q, T, q_idx, status, stream)
         idx = torch.empty(T, self.idx_proj.N_pad, **bf)
-        self.idx_proj.gemm(*y_q, T, idx, status, stream)
-        k_idx, gate = idx[:, :self.IDX_DIM], idx[:, self.IDX_DIM + self.IDX_HEADS:2 * self.IDX_DIM + self.IDX_HEADS]
-        w = idx[:, self.IDX_DIM:self.IDX_DIM + self.IDX_HEADS]          # bf16 head weights, read in place
-        indexer.kpool_insert(k_idx, gate, self.ape, kpool_reqs, max_rows, page_table, pool_cache, tail_ring, stream)
         ldl = _round(int(page_table.shape[1]) * self.POOLS_PER_PAGE, 128)
         ws = self.logits_ws
         if ws is not None and ws.numel() >= T * ldl:
             logits = ws[:T * ldl].view(T, ldl)
         else:
             logits = torch.empty(T, ldl, dtype=torch.float32, device=dev)
-        indexer.logits(q_idx.view(T, self.IDX_HEADS, self.IDX_DIM), w, pool_cache, page_table, groups, logits,
-                       status, stream)
         ids = torch.empty(T, self.TOPK, dtype=torch.int32, device=dev)
-        indexer.topk(logits, positions, self.TOPK, ids, stream)
         tok = torch.empty(T, 4 * self.TOPK + 3 + 5, dtype=torch.int32, device=dev)
-        indexer.expand(ids, positions, tok, stream)
+        qa_q = self.q_b.quantize(qa, stream)
+        # the indexer branch (projections, pool insert, logits, top-k, expansion) on a side stream, beside the query
+        # branch; the layer's stream waits for it before the sparse MLA, so everything after stays ordered
+        main = stream if stream is not None else torch.cuda.current_stream(dev)
+        side = self._side_stream()
+        fork = torch.cuda.Event()
+        fork.record(main)
+        side.wait_event(fork)
+        self.wq_idx.gemm(*qa_q, T, q_idx, status, side)
+        self.idx_proj.gemm(*y_q, T, idx, status, side)
+        k_idx, gate = idx[:, :self.IDX_DIM], idx[:, self.IDX_DIM + self.IDX_HEADS:2 * self.IDX_DIM + self.IDX_HEADS]
+        w = idx[:, self.IDX_DIM:self.IDX_DIM + self.IDX_HEADS]          # bf16 head weights, read in place
+        indexer.kpool_insert(k_idx, gate, self.ape, kpool_reqs, max_rows, page_table, pool_cache, tail_ring, side)
+        indexer.logits(q_idx.view(T, self.IDX_HEADS, self.IDX_DIM), w, pool_cache, page_table, groups, logits,
+                       status, side)
+        indexer.topk(logits, positions, self.TOPK, ids, side)
+        indexer.expand(ids, positions, tok, side)
+        join = torch.cuda.Event()
+        join.record(side)
+        # queries: q_b, rope on each head's rope slice, absorb of each head's nope part into the latent
+        self.q_b.gemm(*qa_q, T, q, status, stream)
+        lib.check("ssb_rope", so.ssb_rope(q[:, self.nope:].data_ptr(), q.stride(0), NH, self.qh, positions.data_ptr(),
+                                          T, self.theta, s))
+        # absorb: each head's nope slice read in place from the token-major q rows, head-major latent out
+        self.w_uk.bmm(q.view(T, NH, self.qh)[:, :, :self.nope].permute(1, 0, 2), q_lat.view(NH, T, L), stream)
+        mla.q_pack(q_lat, T, q[:, self.nope:], self.qh, T, q8, self.q_scale, stream)
+        main.wait_event(join)
         # sparse MLA over the selected tokens, then v_up and o_proj
         o_lat = torch.empty(T, NH, L, **bf)
         mla.sparse_mla(q8, kv_cache, tok, qsl, page_table, self.scale * self.q_scale * self.k_scale, o_lat,
