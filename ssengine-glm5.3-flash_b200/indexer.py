@@ -58,10 +58,13 @@ def logits(q: torch.Tensor, w: torch.Tensor, k_cache: torch.Tensor, page_table: 
     return out
 
 
-def topk(logit_rows: torch.Tensor, positions: torch.Tensor, k: int, out: torch.Tensor, stream=None) -> torch.Tensor:
-    """Canonical top-k pool ids per row over [0, (pos + 1) // 4) (-1 fill), int32 [rows, k]."""
+def topk(logit_rows: torch.Tensor, positions: torch.Tensor, k: int, out: torch.Tensor, stream=None,
+         ranges: tuple | None = None) -> torch.Tensor:
+    """Canonical top-k pool ids per row over [0, (pos + 1) // 4) (-1 fill), int32 [rows, k]. `ranges`: the rows' (ks,
+    ke) from `key_ranges`, computed beforehand on a stream ordered before `stream` (when the call runs on a stream
+    other than the current one, whose torch ops would not be ordered with it)."""
     so = lib.load()
-    ks, ke = key_ranges(positions)
+    ks, ke = ranges if ranges is not None else key_ranges(positions)
     rc = so.ssb_topk_canonical(logit_rows.data_ptr(), logit_rows.shape[0], logit_rows.stride(0), ks.data_ptr(),
                                ke.data_ptr(), k, out.data_ptr(), logit_rows.shape[1], lib.stream_ptr(stream))
     lib.check("ssb_topk_canonical", rc)

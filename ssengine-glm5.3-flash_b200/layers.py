@@ -492,8 +492,12 @@ class DsaAttention:
         tok = torch.empty(T, 4 * self.TOPK + 3 + 5, dtype=torch.int32, device=dev)
         qa_q = self.q_b.quantize(qa, stream)
         # the indexer branch (projections, pool insert, logits, top-k, expansion) on a side stream, beside the query
-        # branch; the layer's stream waits for it before the sparse MLA, so everything after stays ordered
+        # branch; the layer's stream waits for it before the sparse MLA, so everything after stays ordered. Nothing
+        # on the side stream allocates or runs a torch op: its inputs and outputs are made here, on the layer's
+        # stream, and live until the join (the top-k's key ranges included)
         main = stream if stream is not None else torch.cuda.current_stream(dev)
+        with torch.cuda.stream(main):
+            ranges = indexer.key_ranges(positions)
         side = self._side_stream()
         fork = torch.cuda.Event()
         fork.record(main)
@@ -505,7 +509,7 @@ class DsaAttention:
         indexer.kpool_insert(k_idx, gate, self.ape, kpool_reqs, max_rows, page_table, pool_cache, tail_ring, side)
         indexer.logits(q_idx.view(T, self.IDX_HEADS, self.IDX_DIM), w, pool_cache, page_table, groups, logits,
                        status, side)
-        indexer.topk(logits, positions, self.TOPK, ids, side)
+        indexer.topk(logits, positions, self.TOPK, ids, side, ranges=ranges)
         indexer.expand(ids, positions, tok, side)
         join = torch.cuda.Event()
         join.record(side)
