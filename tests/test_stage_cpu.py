@@ -137,3 +137,30 @@ def test_head_batched_gemm_reads_and_writes_token_major_rows_in_place():
     uv.bmm(o_lat.permute(1, 0, 2), o_in.view(T, NH, vd).permute(1, 0, 2))
     want = torch.einsum("thl,hvl->thv", o_lat.float(), uv.w.float()).reshape(T, NH * vd)
     torch.testing.assert_close(o_in.float(), want, rtol=2e-2, atol=2e-2)
+
+
+def test_indexer_work_groups_cover_every_row_with_visible_pools_once():
+    """The indexer's host work table: groups of <= 8 consecutive query rows of one request, each row that sees at
+    least one complete pool in exactly one group, the group's pool tiles those of its last (furthest) row, longest
+    groups first."""
+    import numpy as np
+
+    from ssengine_b200.indexer import POOL, TILE, work_groups
+
+    q_lens = np.array([50, 13, 70, 21, 1, 3])
+    starts = np.array([0, 37, 300, 1400, 3, 0])
+    q_starts = np.concatenate([[0], np.cumsum(q_lens)[:-1]])
+    g = work_groups(q_starts, q_lens, starts)
+    assert g.dtype == np.int32 and g.shape[1] == 4
+    covered = np.zeros(int(q_lens.sum()), np.int32)
+    for r, q0, nq, tiles in g:
+        assert 1 <= nq <= 8 and q_starts[r] <= q0 and q0 + nq <= q_starts[r] + q_lens[r]
+        covered[q0:q0 + nq] += 1
+        last_pos = starts[r] + (q0 + nq - 1 - q_starts[r])
+        assert tiles == -(-((last_pos + 1) // POOL) // TILE) > 0
+    pos = np.concatenate([np.arange(s, s + n) for s, n in zip(starts, q_lens)])
+    sees = (pos + 1) // POOL > 0
+    # every row that sees a pool is in exactly one group (a row that sees none may ride along in a group whose last
+    # row sees one; its logits columns are outside its key range)
+    assert covered.max() <= 1 and (covered[sees] == 1).all()
+    assert (np.diff(g[:, 3]) <= 0).all()
