@@ -1,4 +1,4 @@
-// mHC (4-stream hyper-connections) at a layer boundary, one fused kernel (sm_100a).
+// mHC (4-stream hyper-connections) at a layer boundary (sm_100a).
 //
 // The reference runs DeepGEMM `mega_mhc` here (ssengine/model/pp_patch.py:125-153: the previous layer's post, the
 // next layer's pre and its RMSNorm in one persistent launch); the stage edge uses a standalone pre (edge_recv) and a
@@ -9,6 +9,9 @@
 //         comb' = Sinkhorn(softmax_row(mixes[8:24] s2 + b)); y = RMSNorm(bf16(sum_i pre[i] new_res[i])) * w
 // Layout: x [T, H] bf16, res / new_res [T, 4, H] bf16, post [T, 4] fp32, comb [T, 4, 4] fp32, fn [24, 4H] fp32.
 //
+// A pre step (post + pre, or pre only) is two launches: the persistent TMA-fed mix kernel (the new residual and the
+// partial mixes) and the finalize kernel (Sinkhorn, the layer input and its RMSNorm), described at their definitions
+// below. A post-only boundary (the stage edge's send) is one launch of `mhc_kernel<true, false>`:
 // CTA = 32 tokens, 256 threads, up to 2 CTAs per SM. Main loop: warp w takes 16 tokens (tile w & 1) and a quarter of
 // the hidden positions (w >> 1); each lane covers 2 tokens x 8 consecutive positions of every 32-position group
 // (coalesced 16-byte loads of x and the 4 residual streams), forms the 4 new residual streams (bf16, stored) and feeds
