@@ -1,0 +1,55 @@
+"""Host-side logic of the pipeline benchmark on CPU: the layer splits, the config-4 microbatch stream that
+`--steps 20 --warmup 5` times (100 microbatches), the block contract of every plan against the pool it sizes, and the
+algorithmic FLOP count."""
+
+import numpy as np
+
+
+def test_layer_splits_are_the_reference_ones():
+    import bench
+
+    assert bench.split_for(1) == (45,)
+    assert bench.split_for(2) == (23, 22)
+    assert bench.split_for(4) == (12, 11, 11, 11)
+    assert bench.split_for(8) == (6, 6, 6, 6, 6, 5, 5, 5)
+    assert all(sum(bench.split_for(n)) == 45 for n in (1, 2, 3, 4, 5, 6, 7, 8))
+
+
+def test_stream_of_the_timed_microbatches_keeps_the_block_contract():
+    import bench
+    from ssengine_b200.kvpages import BLOCK_TOKENS, PAGE_TOKENS
+    from ssengine_b200.stage import check_blocks
+
+    W, K, M = 5, 20, bench.MB_PER_STEP
+    plans, nb = bench.pipeline_plans((W + K) * M, bench.MB_TOKENS, None)
+    assert len(plans) == (W + K) * M
+    seen = {}
+    for p in plans:
+        n = sum(c.num_tokens for c in p.chunks)
+        assert 0 < n <= bench.MB_TOKENS
+        check_blocks(p.chunks, nb)
+        for c in p.chunks:
+            # the pages cover the chunk's positions; a request's chunks continue where the last one ended
+            assert len(c.kv_pages) * PAGE_TOKENS >= c.start + c.num_tokens
+            assert max(c.kv_pages) // (BLOCK_TOKENS // PAGE_TOKENS) < nb
+            assert seen.get(c.req_id, 0) == c.start
+            seen[c.req_id] = c.start + c.num_tokens
+    # the timed microbatches reach long contexts (the stream's 128k-token prompt)
+    ctx = [max(c.start + c.num_tokens for c in p.chunks) for p in plans[W * M:]]
+    assert max(ctx) == 131_072
+
+
+def test_microbatch_flops_count_the_projections_and_attention():
+    import bench
+    from ssengine_b200.messages import Chunk, Plan
+    from ssengine_b200.stage import StageConfig
+
+    cfg = StageConfig(layer_split=(45,), **bench.MODEL)
+    short = Plan(0, [Chunk("a", 0, 8192, list(range(64)), [1] * 6, True, None)])
+    long = Plan(1, [Chunk("b", 100_000, 8192, list(range(900)), [1] * 6, True, None)])
+    f_short, f_long = bench.microbatch_flops(short, cfg, 45), bench.microbatch_flops(long, cfg, 45)
+    # at least the MoE experts of 42 layers (9 rows of 25.17 MFLOP a token) and at most a few times that
+    moe = 42 * 8192 * 9 * 25.17e6
+    assert moe < f_short < 4 * moe
+    assert f_long > f_short                               # the indexer and the selected tokens grow with the context
+    assert np.isfinite(f_long)
