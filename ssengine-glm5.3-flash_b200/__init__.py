@@ -9,6 +9,9 @@ modules are the host side: device memory, layouts, the random-init generator, an
 - `weights`  seeded random-init NVFP4 parameters
 - `moe`      `MoELayer`: one NVFP4 MoE layer through `ssb_moe_forward`
 - `stage`    `StageModel`: the reference's stage interface (prepare / run / forward) over the library
+- `worker`, `edge`  the stage worker loop and the P2P stage edge
+- `scheduler`, `pagepool`, `dispatch`  the control plane on stage 0's host: microbatch forming (FIFO / SRPT, budgets,
+             force-schedule), the page pool with the exact prefix cache, and when to form (host only, no device code)
 """
 
 __all__ = ["lib", "layout", "weights", "moe"]
