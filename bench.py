@@ -63,8 +63,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["ours", "reference", "vllm-cutlass"], default="ours")
-    ap.add_argument("--workload", choices=["pipeline", "moe-layer", "components"], default="pipeline",
-                    help="components: the attention-pair kernels and the mHC boundary alone (profiling runs)")
+    ap.add_argument("--workload", choices=["pipeline", "moe-layer", "components", "sessions"], default="pipeline",
+                    help="components: the attention-pair kernels and the mHC boundary alone (profiling runs); "
+                         "sessions: the pipeline serving BASELINE config 5's closed-loop session load (TTFT)")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="pipeline: model layers (45 = BASELINE config 4)")
     ap.add_argument("--tokens", type=int, default=MB_TOKENS, help="tokens per microbatch")
     ap.add_argument("--mb-per-step", type=int, default=MB_PER_STEP,
@@ -74,6 +75,16 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true", help="skip the nvidia-smi window (profiling runs)")
     ap.add_argument("--no-components", action="store_true", help="skip the per-component timings")
+    ap.add_argument("--sessions", type=int, default=400, help="sessions: concurrent closed-loop sessions")
+    ap.add_argument("--session-s", type=float, default=60.0, help="sessions: seconds of arrivals")
+    ap.add_argument("--session-warm-s", type=float, default=20.0,
+                    help="sessions: rounds arriving in the first seconds are served but not measured")
+    ap.add_argument("--think-s", type=float, default=5.0, help="sessions: mean think time")
+    ap.add_argument("--start-ctx", type=int, default=16_384,
+                    help="sessions: a session's first round brings a context uniform in [0, start-ctx)")
+    ap.add_argument("--pool-gb", type=float, default=100.0,
+                    help="sessions: device memory per stage for KV and state blocks (the pool size follows)")
+    ap.add_argument("--force-after-ms", type=float, default=60_000.0, help="sessions: force-schedule bound")
     return ap.parse_args()
 
 
@@ -449,6 +460,115 @@ def run_pipeline(args, rank: int, world: int, local: int) -> None:
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.cuda.synchronize()
+        if pipe is not None:
+            pipe.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def session_pool_blocks(split, pool_bytes: float, kda_heads: int = MODEL["kda_heads"], cap: int = 7143) -> int:
+    """Usable blocks of the session run's pool: what `pool_bytes` holds on the stage whose blocks cost the most (one
+    block-id space serves every stage), at most the reference's 7,143 (7,144 with the null block)."""
+    from ssengine_b200.kvpages import block_bytes
+
+    start, worst = 0, 0
+    for n in split:
+        worst = max(worst, block_bytes(list(range(start, start + n)), lambda i: i % 4 == 3, kda_heads))
+        start += n
+    return max(1, min(cap, int(pool_bytes // worst)))
+
+
+def run_sessions(args, rank: int, world: int, local: int) -> None:
+    """The pipeline serving a closed-loop session load (BASELINE config 5's shape): stage 0's host runs the scheduler
+    (SRPT, `--tokens` microbatches, force-schedule) over the page pool with the exact prefix cache and sends each plan
+    to the other stages; TTFT = the round's greedy token on stage 0's host minus its arrival."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from ssengine_b200 import lib
+    from ssengine_b200.controller import Controller, Reporter, SessionLoad, StoreChannel, cuda_step, serve_stage
+    from ssengine_b200.edge import P2pPipe
+    from ssengine_b200.pagepool import KvManager
+    from ssengine_b200.scheduler import Scheduler, SchedulerConfig
+    from ssengine_b200.stage import StageConfig, StageModel
+    from ssengine_b200.worker import StageWorker
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    split = split_for(world, args.layers)
+    blocks = session_pool_blocks(split, args.pool_gb * 1e9)
+    cfg = StageConfig(layer_split=split, mb_tokens=args.tokens, num_blocks=blocks + 1, seed=SEED % 997, **MODEL)
+    stage = StageModel(cfg, rank, device)
+    gate = world + 2
+    pipe = None
+    if world > 1:
+        pipe = P2pPipe(rank, world, device, None, max_in_flight=gate, max_rows=args.tokens,
+                       width=stage.hidden_width, init_group=False, wait_ns=60_000_000_000)
+    worker = StageWorker(stage, pipe, events=True)
+    step = cuda_step(worker, device)
+    chan = None
+    if world > 1:
+        chan = StoreChannel(dist.PrefixStore("ctl/", dist.distributed_c10d._get_default_store()))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    so = lib.load()
+    so.launches, so.on = 0, True
+    init = (lambda: torch.cuda.set_device(local))
+    summary = None
+    if rank == 0:
+        kv = KvManager(blocks, keep_sessions=True)
+        sched = Scheduler(kv, SchedulerConfig(order="srpt", mb_tokens=args.tokens, force_after_ms=args.force_after_ms),
+                          None, gate + 1, 1)
+        load = SessionLoad(sessions=args.sessions, seed=SEED, vocab=MODEL["vocab"], think_s=args.think_s,
+                           start_ctx_max=args.start_ctx, stagger_s=min(5.0, args.session_warm_s))
+        ctl = Controller(sched, load, world)
+        rep = Reporter(0, ctl.local.put, init=init)
+        summary = ctl.run(step, rep, chan, duration_s=args.session_s, warm_s=args.session_warm_s)
+        rep.close()
+        summary["kv"] = {k: int(v) for k, v in kv.stats.items()}
+        busy = [m.get("busy0", 0) for m in ctl.microbatches]
+        summary["stage0_busy_s"] = sum(busy) / 1e9
+    else:
+        sink = chan.put_report if rank == world - 1 else (lambda rep: None)
+        serve_stage(step, chan, Reporter(rank, sink, init=init))
+    so.on = False
+    torch.cuda.synchronize()
+    if pipe is not None:
+        pipe.check()
+    if int(stage.status.item()):
+        raise lib.SsbError("stage device status", int(stage.status.item()))
+    mine = {"rank": rank, "launches": so.launches}
+    allr = [mine]
+    if world > 1:
+        allr = [None] * world
+        dist.all_gather_object(allr, mine)
+    if rank == 0:
+        line = {
+            "metric": "TTFT p50 under the synthetic session load", "value": summary["ttft_s"]["p50"], "unit": "s",
+            "higher_is_better": False, "n_gpus": world, "ttft_s": summary["ttft_s"],
+            "rounds_per_s": summary["rounds_per_s"], "computed_tok_s": summary["computed_tok_s"],
+            "new_tok_s": summary["new_tok_s"], "prefix_hit_share": summary["prefix_hit_share"],
+            "dtype": "nvfp4 GEMMs; e4m3 attention; bf16 residual; fp32 KDA state",
+            "data": "synthetic: closed-loop sessions, uniform token ids from a seeded hash stream, random-init weights",
+            "config": {"workload": f"config 5 shape: {args.sessions} sessions, appends lognormal median 600 max 8192, "
+                                   f"context cap 131072, think Exp({args.think_s} s), first contexts U[0, "
+                                   f"{args.start_ctx}), {args.session_s:.0f} s of arrivals, rounds arriving after "
+                                   f"{args.session_warm_s:.0f} s measured",
+                       "parallelism": f"pp{world}", "layer_split": list(split),
+                       "scheduler": f"srpt, {args.tokens}-token microbatches, force after {args.force_after_ms} ms, "
+                                    f"in-flight gate {gate} on the GPU",
+                       "pool": f"{blocks} blocks per stage (HBM only: no DRAM / SSD tier), kept sessions LRU"},
+            "rounds": summary["rounds"], "unfinished": summary["unfinished"], "microbatches": summary["microbatches"],
+            "kv": summary["kv"], "stage0_busy_s": summary["stage0_busy_s"],
+            "gpu_launches": sum(r["launches"] for r in allr),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
         if pipe is not None:
             pipe.close()
         dist.barrier()
@@ -1102,6 +1222,8 @@ def main() -> None:
         torch.cuda.set_device(local)
         pk, src = peaks()
         print(json.dumps({"components": time_components(torch.device("cuda", local), pk), "peaks": src}), flush=True)
+    elif args.workload == "sessions":
+        run_sessions(args, rank, world, local)
     else:
         run_pipeline(args, rank, world, local)
 

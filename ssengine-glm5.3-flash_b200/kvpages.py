@@ -52,6 +52,28 @@ def kda_state_bytes(heads: int) -> tuple[int, int, int]:
     return conv, rec_off, -(-(rec_off + rec) // STATE_ALIGN) * STATE_ALIGN
 
 
+def _latent_slots(layers, is_dsa) -> tuple[list, dict, dict, int]:
+    """(DSA layers, KDA group per KDA layer, slot per KDA layer, block-sized tensors needed) of a stage."""
+    dsa = [i for i in layers if is_dsa(i)]
+    group, slot, seen = {}, {}, [0] * KDA_GROUPS
+    for i in layers:
+        if not is_dsa(i):
+            g = kda_group(i, is_dsa)
+            group[i], slot[i] = g, seen[g]
+            seen[g] += 1
+    return dsa, group, slot, max([len(dsa)] + [s + 1 for s in slot.values()])
+
+
+def block_bytes(layers, is_dsa, kda_heads: int) -> int:
+    """Device bytes one block id costs a stage holding `layers`: the latent (or state-only) block of every slot, plus
+    each DSA layer's pool-key rows and tail ring for that block."""
+    dsa, _, _, n_slots = _latent_slots(layers, is_dsa)
+    state_page = kda_state_bytes(kda_heads)[2]
+    latent_page = BLOCK_TOKENS * LATENT_ROW
+    pages = sum(latent_page if j < len(dsa) else state_page for j in range(n_slots))
+    return pages + len(dsa) * (PAGES_PER_BLOCK * 32 * POOL_ROW * 2 + 2 * 4 * POOL_ROW * 2)
+
+
 class StageKv:
     """The pages of one stage's layers `layers` (model layer ids; `is_dsa(i)` for the kind) over `num_blocks` blocks.
 
@@ -65,15 +87,8 @@ class StageKv:
         self.num_blocks = num_blocks
         self.kda_heads = kda_heads
         self.conv_bytes, self.rec_off, state_page = kda_state_bytes(kda_heads)
-        self.dsa_layers = [i for i in layers if is_dsa(i)]
+        self.dsa_layers, self.group, self.slot, n_slots = _latent_slots(layers, is_dsa)
         self.kda_layers = [i for i in layers if not is_dsa(i)]
-        self.group, self.slot = {}, {}
-        seen = [0] * KDA_GROUPS
-        for i in self.kda_layers:
-            g = kda_group(i, is_dsa)
-            self.group[i], self.slot[i] = g, seen[g]
-            seen[g] += 1
-        n_slots = max([len(self.dsa_layers)] + [s + 1 for s in self.slot.values()])
         latent_page = BLOCK_TOKENS * LATENT_ROW
         if self.kda_layers and self.dsa_layers and state_page > latent_page:
             raise ValueError(f"a KDA state page ({state_page} B) does not fit a latent block ({latent_page} B)")

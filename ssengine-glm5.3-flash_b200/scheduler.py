@@ -365,14 +365,17 @@ class Scheduler:
     # --- messages ---------------------------------------------------------------------------------------------------
 
     @staticmethod
-    def plan(mb_id: int, chunks: list[ChunkSpec]) -> Plan:
+    def plan(mb_id: int, chunks: list[ChunkSpec], token_ids=None) -> Plan:
         """The stage message of a formed microbatch: each chunk's KV pages up to its last position, its state blocks,
-        and (when the request has them) its token ids, as the reference's controller sends them
-        (ssengine/runtime/controller.py:609-614)."""
+        and its token ids, as the reference's controller sends them (ssengine/runtime/controller.py:609-614). The ids
+        come from the request's `token_ids`, or from `token_ids(req, start, end)` when given."""
         out = []
         for c in chunks:
             r, end = c.req, c.start + c.num_tokens
-            ids = None if r.token_ids is None else [int(t) for t in r.token_ids[c.start:end]]
+            if token_ids is not None:
+                ids = [int(t) for t in token_ids(r, c.start, end)]
+            else:
+                ids = None if r.token_ids is None else [int(t) for t in r.token_ids[c.start:end]]
             out.append(Chunk(r.req_id, c.start, c.num_tokens, list(r.alloc.kv_pages[:kv_pages_for(end)]),
                              list(r.alloc.state_blocks), c.is_last, ids))
         return Plan(mb_id, out)

@@ -53,3 +53,17 @@ def test_microbatch_flops_count_the_projections_and_attention():
     assert moe < f_short < 4 * moe
     assert f_long > f_short                               # the indexer and the selected tokens grow with the context
     assert np.isfinite(f_long)
+
+
+def test_session_pool_is_sized_by_the_costliest_stage():
+    """The session run's pool: what the memory budget holds on the stage whose blocks cost the most, capped at the
+    reference's 7,143 usable blocks."""
+    import bench
+    from ssengine_b200.kvpages import block_bytes
+
+    dsa = lambda i: i % 4 == 3
+    stage0 = block_bytes(list(range(12)), dsa, bench.MODEL["kda_heads"])       # 3 DSA layers
+    assert bench.session_pool_blocks(bench.split_for(4), 100e9) == int(100e9 // stage0)
+    whole = block_bytes(list(range(45)), dsa, bench.MODEL["kda_heads"])        # 11 DSA layers
+    assert bench.session_pool_blocks(bench.split_for(1), 100e9) == int(100e9 // whole) < 2000
+    assert bench.session_pool_blocks(bench.split_for(8), 1e15) == 7143
