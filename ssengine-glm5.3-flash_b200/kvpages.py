@@ -24,6 +24,8 @@ Differences from the reference, by necessity or choice (stated where they live):
 
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import torch
 
 BLOCK_TOKENS = 8576
@@ -138,3 +140,46 @@ class StageKv:
         """(device pointer, bytes) of every tensor (the capacity tiers' view ranges)."""
         ts = self.pages + self.pool + self.tail
         return [(t.data_ptr(), t.numel() * t.element_size()) for t in ts]
+
+    def tier_ranges(self, stage: int) -> list["ViewRange"]:
+        """Every byte range a context owns on this stage, as one block's row of one cache view (the reference's
+        `kvpool.layout.from_stage_kv`, ssengine/kvpool/layout.py:32-59): KV ranges (kind "kv") -- each DSA layer's
+        latent block and its pool-key rows, one logical block = 8,576 tokens -- then state ranges (kind "state") --
+        each DSA layer's tail ring row (group 5), and each KDA layer's conv and recurrent state inside the latent
+        block it aliases (group = its KDA group, the index into the request's state_blocks)."""
+        out = []
+        for j, layer in enumerate(self.dsa_layers):
+            t = self.pages[j]
+            out.append(ViewRange(stage, f"layers.{layer}.latent", "kv", t.data_ptr(), t.stride(0), t.shape[1]))
+        for j, layer in enumerate(self.dsa_layers):
+            t = self.pool[j]
+            row = PAGES_PER_BLOCK * 32 * POOL_ROW * t.element_size()
+            out.append(ViewRange(stage, f"layers.{layer}.pool_keys", "kv", t.data_ptr(), row, row))
+        for j, layer in enumerate(self.dsa_layers):
+            t = self.tail[j]
+            row = t[0].numel() * t.element_size()
+            out.append(ViewRange(stage, f"layers.{layer}.tail", "state", t.data_ptr(), row, row, TAIL_STATE))
+        rec = self.kda_heads * 128 * 128 * 4
+        for g in range(KDA_GROUPS):
+            for layer in self.kda_layers:
+                if self.group[layer] != g:
+                    continue
+                t = self.pages[self.slot[layer]]
+                out.append(ViewRange(stage, f"layers.{layer}.conv", "state", t.data_ptr(), t.stride(0),
+                                     self.conv_bytes, g))
+                out.append(ViewRange(stage, f"layers.{layer}.recurrent", "state", t.data_ptr() + self.rec_off,
+                                     t.stride(0), rec, g))
+        return out
+
+
+@dataclass(frozen=True)
+class ViewRange:
+    """One cache view's row for a logical block on one stage (the reference's `kvpool.layout.ViewRange`, same
+    fields): block b's bytes are [base + b * stride, base + b * stride + nbytes)."""
+    stage: int
+    name: str
+    kind: str                 # "kv" or "state"
+    base: int                 # device address of logical block 0's row
+    stride: int               # bytes from one logical block's row to the next
+    nbytes: int               # bytes of one logical block's row
+    group: int = -1           # state: index into the request's state_blocks

@@ -285,6 +285,12 @@ class StageModel:
         torch.cuda.synchronize(self.device)
 
     # ---------------------------------------------------------------- the interface
+    def tier_ranges(self) -> list:
+        """This stage's cache views as `kvpages.ViewRange`s (the reference's `StageModel.tier_ranges`,
+        ssengine/model/stage.py:710): what a tier mover copies for a KV block or a request's state blocks. Empty for
+        the MoE-only stage kind, which holds no KV."""
+        return self.kv.tier_ranges(self.stage) if self.kda else []
+
     def prepare(self, plan) -> Batch:
         chunks = plan.chunks
         order = row_order([c.num_tokens for c in chunks])

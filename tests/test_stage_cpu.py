@@ -164,3 +164,43 @@ def test_indexer_work_groups_cover_every_row_with_visible_pools_once():
     # row sees one; its logits columns are outside its key range)
     assert covered.max() <= 1 and (covered[sees] == 1).all()
     assert (np.diff(g[:, 3]) <= 0).all()
+
+
+def test_tier_ranges_cover_the_stage_views_block_by_block():
+    """`StageKv.tier_ranges`: every range's rows stay inside their tensor; KV ranges of different views are disjoint;
+    each KDA layer's conv and recurrent ranges lie inside the latent block they alias, at `state_offsets`; every DSA
+    layer has its latent, pool-key and tail ranges; state groups are the layers' KDA groups (tail: 5)."""
+    from ssengine_b200.kvpages import PAGES_PER_BLOCK, StageKv
+
+    dsa = lambda i: i % 4 == 3
+    for layers in (list(range(12)), list(range(12, 23)), list(range(45))):
+        nb = 3
+        kv = StageKv(layers, dsa, nb, 4, "cpu")
+        rs = kv.tier_ranges(2)
+        spans = [(t.data_ptr(), t.data_ptr() + t.numel() * t.element_size()) for t in kv.pages + kv.pool + kv.tail]
+
+        def inside(a, b):
+            return any(lo <= a and b <= hi for lo, hi in spans)
+
+        for r in rs:
+            assert r.stage == 2 and r.kind in ("kv", "state") and r.nbytes <= r.stride
+            for b in range(nb):
+                assert inside(r.base + b * r.stride, r.base + b * r.stride + r.nbytes), r
+        kvr = sorted((r.base + b * r.stride, r.base + b * r.stride + r.nbytes) for r in rs if r.kind == "kv"
+                     for b in range(nb))
+        assert all(a[1] <= b[0] for a, b in zip(kvr, kvr[1:]))
+        n_dsa = len(kv.dsa_layers)
+        assert [r.kind for r in rs].count("kv") == 2 * n_dsa
+        assert sum(r.name.endswith(".tail") and r.group == 5 for r in rs) == n_dsa
+        for layer in kv.kda_layers:
+            conv = next(r for r in rs if r.name == f"layers.{layer}.conv")
+            rec = next(r for r in rs if r.name == f"layers.{layer}.recurrent")
+            page = kv.pages[kv.slot[layer]]
+            assert conv.group == rec.group == kv.group[layer]
+            for b in range(nb):
+                c, q = kv.state_offsets(layer, b)
+                assert conv.base + b * conv.stride == page.data_ptr() + c
+                assert rec.base + b * rec.stride == page.data_ptr() + q
+                assert rec.base + b * rec.stride + rec.nbytes <= page.data_ptr() + (b + 1) * page.shape[1]
+        pk = next(r for r in rs if r.name.endswith(".pool_keys"))
+        assert pk.nbytes == PAGES_PER_BLOCK * 32 * 128 * 2
