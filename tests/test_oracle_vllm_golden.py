@@ -187,3 +187,34 @@ def test_kda_conv_matches_vllm_causal_conv1d():
     # 0.031 absolute on outputs up to 4.1
     q, k, v, _ = kda.conv(i["x"], i["w"], i["state"], gen.KDA_SEQS, i["P"])
     assert np.abs(np.concatenate([q, k, v], axis=1) - f["out"]).max() <= 0.02 * np.abs(f["out"]).max()
+
+
+def test_mla_rope_matches_vllm_rotary_embedding():
+    """oracle.dsa.rope against vLLM's MLA rotary embedding (interleaved pairs, theta 10000, fp32 cos / sin cache).
+    vLLM forms each angle as fp32 position x fp32 inverse frequency, off the exact angle by up to ~2^-23 x position
+    radians; the oracle uses exact angles, so the bound grows with the position (measured: 1.9e-4 below position
+    2,048, 1.0e-2 near 131,072); the other pairing convention (NeoX halves) would be off by ~8."""
+    from oracle import dsa
+
+    f = np.load(GOLDEN / "rope_vllm.npz")
+    i = gen.rope_inputs()
+    q = dsa.rope(i["q"], i["pos"], gen.ROPE_THETA)
+    k = dsa.rope(i["k"][:, None, :], i["pos"], gen.ROPE_THETA)[:, 0]
+    for ours, ref, x in ((q, f["q"], i["q"]), (k, f["k"], i["k"][:, None, :])):
+        amax = np.abs(x).reshape(len(x), -1).max(axis=1)
+        bound = 2.0 * (i["pos"] * 2.0 ** -23 + 2.0 ** -20) * amax
+        err = np.abs(ours - ref).reshape(len(x), -1).max(axis=1)
+        assert (err <= bound).all(), float((err / bound).max())
+    short = i["pos"] < 2048
+    assert np.abs(q[short] - f["q"][short]).max() < 5e-4
+
+
+def test_dsa_latent_rmsnorm_matches_vllm():
+    """oracle.dsa.rmsnorm (the q_a / kv latent norms) against vLLM's `rms_norm`: within one bf16 step."""
+    from oracle import dsa
+    from oracle.mhc import bf16
+
+    f = np.load(GOLDEN / "norms_vllm.npz")
+    i = gen.norm_inputs()
+    ours = bf16(dsa.rmsnorm(i["x"], i["w"], i["eps"]))
+    assert (np.abs(ours - f["rms"]) <= BF16_STEP * np.abs(f["rms"])).all()
