@@ -85,6 +85,8 @@ def parse():
     ap.add_argument("--pool-gb", type=float, default=100.0,
                     help="sessions: device memory per stage for KV and state blocks (the pool size follows)")
     ap.add_argument("--force-after-ms", type=float, default=60_000.0, help="sessions: force-schedule bound")
+    ap.add_argument("--dram-gb", type=float, default=0.0,
+                    help="sessions: pinned host memory per stage for the DRAM tier under HBM (0: no tier)")
     return ap.parse_args()
 
 
@@ -493,6 +495,7 @@ def run_sessions(args, rank: int, world: int, local: int) -> None:
     from ssengine_b200.pagepool import KvManager
     from ssengine_b200.scheduler import Scheduler, SchedulerConfig
     from ssengine_b200.stage import StageConfig, StageModel
+    from ssengine_b200.tier import DramTier, TierArena
     from ssengine_b200.worker import StageWorker
 
     torch.cuda.set_device(local)
@@ -508,7 +511,9 @@ def run_sessions(args, rank: int, world: int, local: int) -> None:
     if world > 1:
         pipe = P2pPipe(rank, world, device, None, max_in_flight=gate, max_rows=args.tokens,
                        width=stage.hidden_width, init_group=False, wait_ns=60_000_000_000)
-    worker = StageWorker(stage, pipe, events=True)
+    dram_blocks = session_pool_blocks(split, args.dram_gb * 1e9, cap=1 << 30) if args.dram_gb > 0 else 0
+    arena = TierArena(stage.kv, rank, dram_blocks, device=device) if dram_blocks else None
+    worker = StageWorker(stage, pipe, events=True, tier=arena)
     step = cuda_step(worker, device)
     chan = None
     if world > 1:
@@ -522,6 +527,8 @@ def run_sessions(args, rank: int, world: int, local: int) -> None:
     summary = None
     if rank == 0:
         kv = KvManager(blocks, keep_sessions=True)
+        if dram_blocks:
+            kv.lower = DramTier(dram_blocks)
         sched = Scheduler(kv, SchedulerConfig(order="srpt", mb_tokens=args.tokens, force_after_ms=args.force_after_ms),
                           None, gate + 1, 1)
         load = SessionLoad(sessions=args.sessions, seed=SEED, vocab=MODEL["vocab"], think_s=args.think_s,
@@ -531,6 +538,8 @@ def run_sessions(args, rank: int, world: int, local: int) -> None:
         summary = ctl.run(step, rep, chan, duration_s=args.session_s, warm_s=args.session_warm_s)
         rep.close()
         summary["kv"] = {k: int(v) for k, v in kv.stats.items()}
+        if kv.lower is not None:
+            summary["dram_tier"] = {k: int(v) for k, v in kv.lower.stats.items()}
         busy = [m.get("busy0", 0) for m in ctl.microbatches]
         summary["stage0_busy_s"] = sum(busy) / 1e9
     else:
@@ -540,9 +549,11 @@ def run_sessions(args, rank: int, world: int, local: int) -> None:
     torch.cuda.synchronize()
     if pipe is not None:
         pipe.check()
+    if arena is not None:
+        arena.check()
     if int(stage.status.item()):
         raise lib.SsbError("stage device status", int(stage.status.item()))
-    mine = {"rank": rank, "launches": so.launches}
+    mine = {"rank": rank, "launches": so.launches, "tier_bytes": arena.bytes_moved if arena is not None else 0}
     allr = [mine]
     if world > 1:
         allr = [None] * world
@@ -562,7 +573,10 @@ def run_sessions(args, rank: int, world: int, local: int) -> None:
                        "parallelism": f"pp{world}", "layer_split": list(split),
                        "scheduler": f"srpt, {args.tokens}-token microbatches, force after {args.force_after_ms} ms, "
                                     f"in-flight gate {gate} on the GPU",
-                       "pool": f"{blocks} blocks per stage (HBM only: no DRAM / SSD tier), kept sessions LRU"},
+                       "pool": f"{blocks} blocks per stage, kept sessions LRU; "
+                               + (f"DRAM tier of {dram_blocks} blocks per stage ({args.dram_gb:.0f} GB pinned), "
+                                  f"exclusive, copies in stream order" if dram_blocks else "no DRAM tier")},
+            "dram_tier": summary.get("dram_tier"), "tier_bytes_per_rank": [r["tier_bytes"] for r in allr],
             "rounds": summary["rounds"], "unfinished": summary["unfinished"], "microbatches": summary["microbatches"],
             "kv": summary["kv"], "stage0_busy_s": summary["stage0_busy_s"],
             "gpu_launches": sum(r["launches"] for r in allr),

@@ -403,6 +403,13 @@ int ssb_flag_write(uint32_t* flag, uint32_t value, void* stream);
  * peer slot itself. */
 int ssb_p2p_copy(void* dst, const void* src, int64_t bytes, void* stream);
 
+/* ---- DRAM tier copies (the reference's tier mover, ssengine/kvpool/mover.py) -------------------------------------
+ * On `stream`: for r < n, copy runs[3r + 2] bytes from address runs[3r] to address runs[3r + 1] (runs: int64 [n, 3] in
+ * device memory; every address and size a multiple of 16 bytes). Either side may be pinned host memory (addressed
+ * through unified virtual addressing) or this device's memory: a context's KV pages and state rows between a stage's
+ * cache views and its DRAM tier, one launch per tier op. Misaligned runs are skipped and raise 1 in `status`. */
+int ssb_copy_runs(const int64_t* runs, int64_t n, int32_t* status, void* stream);
+
 /* MoE routing + permutation that allocates nothing: the same routing as ssb_moe_route and the same permutation as
  * ssb_moe_forward (expert-major, tokens ascending, shared expert last, experts at 128-aligned offsets), for callers
  * that cannot allocate device memory -- a stage whose KV pool already took the free HBM at start-up, code that must

@@ -13,6 +13,7 @@ modules are the host side: device memory, layouts, the random-init generator, an
 - `scheduler`, `pagepool`, `dispatch`  the control plane on stage 0's host: microbatch forming (FIFO / SRPT, budgets,
              force-schedule), the page pool with the exact prefix cache, and when to form (host only, no device code)
 - `controller`  serving a session load: stage 0's loop (arrivals -> plans -> reports -> TTFT), the other stages' loop
+- `tier`     the DRAM tier under HBM's kept contexts and the in-stream-order copies that move them
 """
 
 __all__ = ["lib", "layout", "weights", "moe"]

@@ -15,7 +15,7 @@ CSRC = PKG / "csrc"
 LIB = PKG / "libssengine_b200.so"
 OBJ = PKG.parent / "_build"
 SOURCES = ["gemm_nvfp4.cu", "moe_ops.cu", "capi.cu", "moe_noalloc.cu", "topk.cu", "stage.cu", "mhc.cu", "kda.cu",
-           "edge.cu", "indexer.cu", "mla.cu", "kpool.cu", "dsa.cu"]
+           "edge.cu", "indexer.cu", "mla.cu", "kpool.cu", "dsa.cu", "tier.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC"]
 

@@ -99,7 +99,7 @@ class SessionLoad:
 def for_later_stages(plan: Plan) -> Plan:
     """The plan without token ids (only stage 0 embeds them)."""
     return Plan(plan.mb_id, [Chunk(c.req_id, c.start, c.num_tokens, c.kv_pages, c.state_blocks, c.is_last, None)
-                             for c in plan.chunks])
+                             for c in plan.chunks], list(plan.tier_ops))
 
 
 class Reporter(threading.Thread):
@@ -258,6 +258,7 @@ class Controller:
                 raise reporter.error
             while (chunks := sched.next_microbatch(now)) is not None:
                 plan = Scheduler.plan(k, chunks, token_ids=load.ids)
+                plan.tier_ops = sched.kv.take_ops()              # copies recorded since the last plan, in order
                 self._plans[k] = [c.req for c in chunks if c.is_last]
                 self.microbatches.append({"mb": k, "formed_ns": now, "tokens": plan.num_tokens,
                                           "chunks": len(plan.chunks)})

@@ -84,10 +84,12 @@ class StageKv:
     is the index of the latent tensor its state aliases (extra state-only tensors when the stage has fewer DSA layers
     than a group has KDA layers here)."""
 
-    def __init__(self, layers, is_dsa, num_blocks: int, kda_heads: int, device):
+    def __init__(self, layers, is_dsa, num_blocks: int, kda_heads: int, device, pin: bool = False):
         dev = torch.device(device)
         self.num_blocks = num_blocks
         self.kda_heads = kda_heads
+        self.layers, self.is_dsa = list(layers), is_dsa
+        mem = dict(pin_memory=True) if pin else {}       # a host-memory copy of the views (the DRAM tier)
         self.conv_bytes, self.rec_off, state_page = kda_state_bytes(kda_heads)
         self.dsa_layers, self.group, self.slot, n_slots = _latent_slots(layers, is_dsa)
         self.kda_layers = [i for i in layers if not is_dsa(i)]
@@ -97,10 +99,10 @@ class StageKv:
         self.pages = []
         for j in range(n_slots):
             page = latent_page if j < len(self.dsa_layers) else state_page
-            self.pages.append(torch.zeros(num_blocks, page, dtype=torch.uint8, device=dev))
-        self.pool = [torch.zeros(num_blocks * PAGES_PER_BLOCK * 32, POOL_ROW, dtype=torch.bfloat16, device=dev)
+            self.pages.append(torch.zeros(num_blocks, page, dtype=torch.uint8, device=dev, **mem))
+        self.pool = [torch.zeros(num_blocks * PAGES_PER_BLOCK * 32, POOL_ROW, dtype=torch.bfloat16, device=dev, **mem)
                      for _ in self.dsa_layers]
-        self.tail = [torch.zeros(num_blocks, 2, 4, POOL_ROW, dtype=torch.bfloat16, device=dev)
+        self.tail = [torch.zeros(num_blocks, 2, 4, POOL_ROW, dtype=torch.bfloat16, device=dev, **mem)
                      for _ in self.dsa_layers]
 
     # ------------------------------------------------------------------ views

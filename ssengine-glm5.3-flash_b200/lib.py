@@ -23,7 +23,7 @@ EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_g
            "ssb_indexer_logits", "ssb_indexer_expand", "ssb_sparse_mla", "ssb_mla_cache_append", "ssb_mla_q_pack",
            "ssb_kpool_insert", "ssb_gated_rmsnorm", "ssb_gated_rmsnorm_nvfp4", "ssb_hc_expand", "ssb_hc_mean",
            "ssb_nvfp4_gemm_grouped", "ssb_rmsnorm_cols", "ssb_rope", "ssb_transpose_heads", "ssb_concat_cols",
-           "ssb_head_tiles", "ssb_moe_route_sigmoid")
+           "ssb_head_tiles", "ssb_moe_route_sigmoid", "ssb_copy_runs")
 
 EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
 ROUTE_SOFTMAX, ROUTE_SIGMOID_BIAS = 0, 1
@@ -140,6 +140,7 @@ _SIGS = {
     "ssb_flag_wait": ([_P, ctypes.c_uint32, _I64, _P, _P], ctypes.c_int),
     "ssb_flag_write": ([_P, ctypes.c_uint32, _P], ctypes.c_int),
     "ssb_p2p_copy": ([_P, _P, _I64, _P], ctypes.c_int),
+    "ssb_copy_runs": ([_P, _I64, _P, _P], ctypes.c_int),
     "ssb_indexer_logits": ([_P, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P], ctypes.c_int),
     "ssb_indexer_expand": ([_P, _I64, _I32, _P, _I64, _P, _I64, _P], ctypes.c_int),
     "ssb_sparse_mla": ([_P, _I64, _P, _P, _I64, _I32, _P, _I32, _P, _I64, _F, _F, _P, _P, _P], ctypes.c_int),

@@ -22,6 +22,8 @@ class Chunk:
 class Plan:
     mb_id: int                      # 0, 1, 2, ... in dispatch order
     chunks: list[Chunk] = field(default_factory=list)   # hidden rows concatenated in this order
+    tier_ops: list = field(default_factory=list)        # DRAM tier copies every stage applies, in order, before the
+                                                        # forward (`tier.TierOp`; not in the reference's message)
 
     @property
     def num_tokens(self) -> int:

@@ -21,7 +21,10 @@ The rules follow the reference's control plane so that the same arrivals give th
   hand out the pages and states.
 
 Not restated: the simulator-only token ledger and partial hits (kv.py `accounting="tokens"`, `partial_hits`), which
-exist to replay another system's targets, and the DRAM / SSD tier hooks (the pool's lower level, loading area, pins).
+exist to replay another system's targets, and the reference's tier hooks (write-back ahead of eviction, loading area,
+pins). A DRAM tier of this package's own design (`tier.DramTier`) can sit below as `lower`: it takes every kept
+context HBM evicts, and a round whose session's context it holds is admitted with a miss's footprint and a read of
+that context (`peek_hit` and `allocate` count it as a hit); without `lower` every rule above is the reference's.
 
 The pool is implemented with per-block free-page bitmasks, a heap of partly used blocks keyed (free pages, block) and
 a heap of whole blocks keyed by the time they became whole, both with lazy invalidation.
@@ -278,8 +281,9 @@ class KvManager:
         self._charge: dict[str, int] = {}
         self.evicted: dict[object, int] = {}           # key -> tokens of a kept context evicted and not replaced
         self._short = Counter()                        # content keys: lengths of kept contexts under the key size
+        self.lower = None                              # a DRAM tier (`tier.DramTier`) taking evicted contexts
         self.stats = dict(admitted=0, hits=0, hit_tokens=0, evicted_sessions=0, evicted_tokens=0, dropped_stale=0,
-                          peak_hard=0, states_short=0, repeats=0)
+                          peak_hard=0, states_short=0, repeats=0, tier_hits=0, tier_hit_tokens=0)
 
     @property
     def num_blocks(self) -> int:
@@ -310,11 +314,17 @@ class KvManager:
         return hit
 
     def peek_hit(self, req) -> int:
-        """The hit the request would get if admitted now."""
+        """The hit the request would get if admitted now (from HBM, else from the DRAM tier)."""
         if req.session is None or not self.keep_sessions:
             return 0
         k = self.kept.get(req.session)
-        return 0 if k is None else self._hit(k, req)
+        if k is None:
+            return self.lower.peek(req.session, req) if self.lower is not None else 0
+        return self._hit(k, req)
+
+    def take_ops(self) -> list:
+        """The DRAM tier's copies recorded since the last call, in order (they ride the next plan)."""
+        return self.lower.take_ops() if self.lower is not None else []
 
     def shared_prefix(self, req) -> int:
         """Tokens the prompt shares with its session's previous context when the request declares no prefix: the
@@ -324,7 +334,8 @@ class KvManager:
         k = self.kept.get(req.session)
         if k is not None:
             return self._hit(k, req) or min(common_prefix(k.content, req.token_ids) or 0, req.num_tokens - 1)
-        return min(self.evicted.get(req.session, 0), req.num_tokens - 1)
+        lower = self.lower.tokens(req.session) if self.lower is not None else 0
+        return min(lower or self.evicted.get(req.session, 0), req.num_tokens - 1)
 
     def find_session(self, token_ids) -> bytes:
         """Content keys: the key of the kept context this prompt may continue (its own key if none is kept)."""
@@ -390,6 +401,8 @@ class KvManager:
             key, k = self.kept.popitem(last=False)
             self._unkeep(k, evicted=True)
             self.evicted[key] = k.tokens
+            if self.lower is not None:
+                self.lower.store(key, k)               # its write-back is recorded before any reuse of the pages
             self.pool.give(k.alloc)
             self.stats["evicted_sessions"] += 1
             self.stats["evicted_tokens"] += k.tokens
@@ -420,6 +433,12 @@ class KvManager:
         elif req.session is not None and req.session in self.evicted:
             info["hit_kind"] = "evicted"
             info["evicted_context_tokens"] = self.evicted[req.session]
+        low = None                                     # the session's context in the DRAM tier, detached for a read
+        if k is None and self.lower is not None and req.session is not None:
+            low = self.lower.detach(req.session)
+            if low is not None and not resumable_tokens(low.tokens, low.content, req):
+                self.lower.release_detached(low)
+                low = None
         charge = self.footprint(req.num_tokens)
         self.hard += charge
         self.stats["peak_hard"] = max(self.stats["peak_hard"], self.hard)
@@ -433,6 +452,12 @@ class KvManager:
             self._make_room(n_kv, STATE_BLOCKS)
             pages = self.pool.take_pages(n_kv)         # KV pages before the state blocks
             alloc = Allocation(pages, self.pool.take_states(STATE_BLOCKS))
+            if low is not None:                        # resumes from the DRAM tier: its read fills the first pages
+                self.lower.read(low, alloc)
+                hit = low.tokens
+                info["hit_kind"], info["common_prefix_tokens"] = "tier", hit
+                self.stats["tier_hits"] += 1
+                self.stats["tier_hit_tokens"] += hit
         self.held[req.req_id] = alloc
         self._charge[req.req_id] = charge
         self.stats["admitted"] += 1
@@ -469,6 +494,8 @@ class KvManager:
         self.kept_charge += self.kept_cost(req.num_tokens)
         if self.content_keys and req.num_tokens < SESSION_KEY_TOKENS:
             self._short[req.num_tokens] += 1
+        if self.lower is not None:
+            self.lower.drop(key)                       # an older copy of this session's context is stale now
         self._make_room(0, 0)
         return key
 

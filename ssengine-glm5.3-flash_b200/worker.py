@@ -18,8 +18,9 @@ class StageWorker:
     """Runs microbatches through `stage`; `pipe` is the stage's `edge.P2pPipe` (None for a one-stage pipeline).
     With `events`, each forward is bracketed by CUDA events (busy time) appended to `self.spans`."""
 
-    def __init__(self, stage: StageModel, pipe=None, events: bool = False):
+    def __init__(self, stage: StageModel, pipe=None, events: bool = False, tier=None):
         self.stage, self.pipe = stage, pipe
+        self.tier = tier                # a `tier.TierArena`: a plan's DRAM tier copies run before its forward
         self.n = 0
         self.events = events
         self.spans: list[tuple] = []
@@ -29,6 +30,11 @@ class StageWorker:
         """One microbatch (a Plan, or a Batch prepared earlier). Returns the last stage's greedy tokens, else None."""
         st, pipe = self.stage, self.pipe
         batch = work if isinstance(work, Batch) else st.prepare(work)
+        ops = getattr(work, "tier_ops", None)
+        if ops:
+            if self.tier is None:
+                raise RuntimeError(f"plan {work.mb_id} carries DRAM tier copies but this stage has no tier")
+            self.tier.apply(ops, torch.cuda.current_stream())    # in stream order, before the forward
         self.n += 1
         hidden = None
         if pipe is not None:

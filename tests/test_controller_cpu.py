@@ -31,6 +31,7 @@ class FakeStage:
         self.num_blocks, self.per, self.base = num_blocks, us_per_token, base_us
         self.k = 0
         self.seen_tokens = 0
+        self.tier_ops = 0
 
     def step(self, plan):
         from ssengine_b200.stage import check_blocks
@@ -47,6 +48,7 @@ class FakeStage:
                 assert c.token_ids is None
         n = plan.num_tokens
         self.seen_tokens += n
+        self.tier_ops += len(plan.tier_ops)
         n_last = sum(c.is_last for c in plan.chunks)
 
         def done():
@@ -121,6 +123,26 @@ def test_one_stage_serves_the_session_load():
     assert 0 < s["prefix_hit_share"] < 1                # later rounds resume their session's kept context
     assert stage.k == s["microbatches"] and sched.in_flight == 0
     assert kv.hard == 0 and kv.stats["evicted_sessions"] > 0         # the pool is too small to keep them all
+    assert sum(r["tokens"] - r["cached"] for r in ctl.rounds) == stage.seen_tokens
+
+
+def test_one_stage_with_a_dram_tier_resumes_evicted_contexts():
+    import torch.distributed as dist
+
+    from ssengine_b200.tier import DramTier
+
+    store = dist.HashStore()
+    kv = KvManager(NUM_BLOCKS, keep_sessions=True)
+    kv.lower = DramTier(80)
+    sched = Scheduler(kv, CFG, None, GATE + 1, 1)
+    ctl = Controller(sched, small_load(), 1)
+    stage = FakeStage(0, 1, store, NUM_BLOCKS)
+    rep = Reporter(0, ctl.local.put)
+    s = ctl.run(stage.step, rep, None, duration_s=1.5, warm_s=0.4)
+    rep.close()
+    assert s["unfinished"] == 0 and kv.stats["tier_hits"] > 0 and stage.tier_ops > 0
+    assert kv.lower.stats["read"] == kv.stats["tier_hits"] and kv.lower.stats["stored"] >= kv.lower.stats["read"]
+    assert not kv.take_ops()                            # every recorded copy rode a plan
     assert sum(r["tokens"] - r["cached"] for r in ctl.rounds) == stage.seen_tokens
 
 

@@ -1,0 +1,151 @@
+"""The DRAM tier on CPU: the copy runs of a tier op move exactly a context's page slices and state rows between a
+stage's cache views and their host mirror; and under random session churn, applying the recorded ops in order before
+each forward always leaves a resumed context's pages and state where its round reads them."""
+
+import ctypes
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from ssengine_b200.kvpages import PAGES_PER_BLOCK, StageKv
+from ssengine_b200.pagepool import KvManager, kv_pages_for
+from ssengine_b200.scheduler import Request
+from ssengine_b200.tier import DramTier, TierArena, TierOp, op_runs
+
+
+def memmove_copier(runs, stream=None):
+    for s, d, n in runs.tolist():
+        ctypes.memmove(d, s, n)
+
+
+def test_runs_are_aligned_merged_and_cut():
+    kv = StageKv(list(range(12)), lambda i: i % 4 == 3, 4, 4, "cpu")
+    arena = TierArena(kv, 0, 3, copier=memmove_copier)
+    op = TierOp("write", [67, 68, 69, 200], [1, 2, 3, 1, 2, 3], [0 + 67, 1 + 67, 2 + 67, 134], [2, 1, 3, 2, 1, 3])
+    runs = op_runs(op, arena.hbm_ranges, arena.dram_ranges, piece=64 * 1024)
+    assert runs.dtype == np.int64 and (runs % 16 == 0).all() and (runs[:, 2] <= 64 * 1024).all()
+    # 3 latent + 3 pool-key views x (pages 67-69 contiguous on both sides, page 200 alone), 3 tails, 9 KDA x 2 states
+    lat = kv.tier_ranges(0)[0]
+    page = lat.nbytes // PAGES_PER_BLOCK
+    total = 3 * (4 * page) + 3 * 4 * (PAGES_PER_BLOCK * 32 * 256 // PAGES_PER_BLOCK)
+    total += sum(r.nbytes for r in arena.hbm_ranges if r.kind == "state")
+    assert int(runs[:, 2].sum()) == total
+    with pytest.raises(ValueError):
+        op_runs(TierOp("move", [], [], [], []), arena.hbm_ranges, arena.dram_ranges)
+
+
+@pytest.mark.parametrize("layers", [list(range(12)), list(range(12, 23)), list(range(39, 45))])
+def test_write_then_read_moves_the_context_bytes(layers):
+    g = torch.Generator().manual_seed(1)
+    # HBM blocks 1-9, DRAM blocks 1-9; as the page pool hands them out, a state block is never a KV page's block
+    hbm = StageKv(layers, lambda i: i % 4 == 3, 10, 4, "cpu")
+    for t in hbm.pages + hbm.pool + hbm.tail:
+        t.view(torch.uint8).copy_(torch.randint(0, 256, t.view(torch.uint8).shape, dtype=torch.uint8, generator=g))
+    arena = TierArena(hbm, 1, 9, copier=memmove_copier)
+    pages, old_states = [70, 71, 140, 141, 142], [3, 4, 5, 6, 7, 8]
+    dram_pages, dram_states = [70, 71, 72, 73, 74], [2, 3, 4, 5, 6, 7]
+    ref = {id(t): t.clone() for t in hbm.pages + hbm.pool + hbm.tail}
+    arena.apply([TierOp("write", pages, old_states, dram_pages, dram_states)])
+    for t in hbm.pages + hbm.pool + hbm.tail:                    # HBM reuses everything
+        t.zero_()
+    new_pages, new_states = [150, 151, 152, 153, 154], [9, 8, 7, 6, 5, 3]
+    arena.apply([TierOp("read", new_pages, new_states, dram_pages, dram_states)])
+    # every KV page slice and every state row came back at its new place
+    for j, layer in enumerate(hbm.dsa_layers):
+        lat_old, lat = ref[id(hbm.pages[j])], hbm.pages[j]
+        pb = lat.shape[1] // PAGES_PER_BLOCK
+        for po, pn in zip(pages, new_pages):
+            a = lat_old[po // PAGES_PER_BLOCK, (po % PAGES_PER_BLOCK) * pb:(po % PAGES_PER_BLOCK + 1) * pb]
+            b = lat[pn // PAGES_PER_BLOCK, (pn % PAGES_PER_BLOCK) * pb:(pn % PAGES_PER_BLOCK + 1) * pb]
+            assert torch.equal(a, b)
+            bits = lambda t: t.view(torch.int16)                 # random bytes as bf16 include NaNs
+            assert torch.equal(bits(ref[id(hbm.pool[j])][po * 32:(po + 1) * 32]), bits(hbm.pool[j][pn * 32:(pn + 1) * 32]))
+        assert torch.equal(ref[id(hbm.tail[j])][old_states[5]].view(torch.int16),
+                           hbm.tail[j][new_states[5]].view(torch.int16))
+    for layer in hbm.kda_layers:
+        gi = hbm.group[layer]
+        t_old, t = ref[id(hbm.pages[hbm.slot[layer]])], hbm.pages[hbm.slot[layer]]
+        c_o, r_o = hbm.state_offsets(layer, old_states[gi])
+        c_n, r_n = hbm.state_offsets(layer, new_states[gi])
+        flat_old, flat = t_old.reshape(-1), t.reshape(-1)
+        assert torch.equal(flat_old[c_o:c_o + hbm.conv_bytes], flat[c_n:c_n + hbm.conv_bytes])
+        rec = hbm.kda_heads * 128 * 128 * 4
+        assert torch.equal(flat_old[r_o:r_o + rec], flat[r_n:r_n + rec])
+    assert arena.bytes_moved > 0
+    with pytest.raises(ValueError):                              # block 10 is outside the 10 HBM rows
+        arena.apply([TierOp("read", [10 * 67], new_states, [70], dram_states)])
+    with pytest.raises(ValueError):                              # block 0 is the null block
+        arena.apply([TierOp("write", [70], [0, 2, 3, 4, 5, 6], [70], dram_states)])
+
+
+def _churn(seed: int, steps: int = 1500, hbm_blocks: int = 40, dram_blocks: int = 30):
+    """Random sessions over HBM + DRAM. Every page and state block carries a tag of what it holds; ops are applied in
+    the order recorded (before the next forward), a forward writes its request's pages and final state; at every
+    admission with a hit, the pages and state the round resumes from must hold its context."""
+    rng = random.Random(seed)
+    kv = KvManager(hbm_blocks, keep_sessions=True)
+    kv.lower = tier = DramTier(dram_blocks)
+    hbm, dram, hst, dst = {}, {}, {}, {}
+    ctx = {}                                              # session -> (epoch, tokens of its last prompt)
+    running = []
+    hits = {"hbm": 0, "tier": 0}
+
+    def apply_ops():
+        for op in kv.take_ops():
+            if op.kind == "write":
+                for p, q in zip(op.hbm_pages, op.dram_pages):
+                    dram[q] = hbm.get(p)
+                for p, q in zip(op.hbm_states, op.dram_states):
+                    dst[q] = hst.get(p)
+            else:
+                for p, q in zip(op.hbm_pages, op.dram_pages):
+                    hbm[p] = dram.get(q)
+                for p, q in zip(op.hbm_states, op.dram_states):
+                    hst[p] = dst.get(q)
+
+    for step in range(steps):
+        if running and rng.random() < 0.45:
+            r = running.pop(rng.randrange(len(running)))
+            kv.release(r)
+            ctx[r.session] = (r.epoch, r.num_tokens)
+            apply_ops()
+            continue
+        s = rng.randrange(24)
+        if any(r.session == s for r in running):
+            continue
+        epoch, prev = ctx.get(s, (0, 0))
+        if prev and rng.random() < 0.1:
+            epoch, prev = epoch + 1, 0                   # the session starts over
+        n = (prev + 1 if prev else 0) + rng.choice([rng.randrange(1, 400), rng.randrange(1, 2 * 8576)])
+        r = Request(f"r{step}", n, session=s, prefix_tokens=prev + 1 if prev else 0)
+        r.epoch = epoch
+        if not kv.fits(r):
+            continue
+        r.cached = kv.allocate(r)
+        apply_ops()
+        a = kv.held[r.req_id]
+        if r.cached:
+            hits["tier" if r.admit_info["hit_kind"] == "tier" else "hbm"] += 1
+            for i in range(kv_pages_for(r.cached)):
+                assert hbm.get(a.kv_pages[i]) == (s, epoch, i), (step, i, r.admit_info)
+            for gidx, b in enumerate(a.state_blocks):
+                assert hst.get(b) == (s, epoch, r.cached, gidx), (step, gidx)
+        for i in range(kv_pages_for(n)):                  # the forward writes the prompt's pages and final state
+            hbm[a.kv_pages[i]] = (s, epoch, i)
+        for gidx, b in enumerate(a.state_blocks):
+            hst[b] = (s, epoch, n, gidx)
+        running.append(r)
+    return kv, tier, hits
+
+
+def test_resumed_contexts_find_their_pages_and_states_after_in_order_copies():
+    tot = {"hbm": 0, "tier": 0}
+    for seed in range(4):
+        kv, tier, hits = _churn(seed)
+        for k in tot:
+            tot[k] += hits[k]
+        assert tier.stats["stored"] > 10 and tier.stats["read"] > 5
+        assert kv.stats["tier_hits"] == tier.stats["read"]
+    assert tot["tier"] > 20 and tot["hbm"] > 20
