@@ -333,6 +333,29 @@ int ssb_indexer_logits(const void* q, const void* w, int64_t ldw, int64_t T, con
   return ssb::launch_indexer_logits(q, k_cache, pool_rows, a, static_cast<cudaStream_t>(stream));
 }
 
+int ssb_indexer_logits_fp8(const uint8_t* q8, const float* q_scale, const void* w, int64_t ldw, int64_t T,
+                           const uint8_t* k_pages, int64_t pages, const int32_t* page_table, int64_t width,
+                           const int32_t* groups, int64_t G, float* logits, int64_t ldl, int32_t* status,
+                           void* stream) {
+  if (width <= 0 || width > (1 << 24) || G < 0 || G > (1 << 28) || pages > (1LL << 26)) return kErrArgs;
+  ssb::IdxArgs a;
+  a.w = w;
+  a.ldw = ldw;
+  a.T = T;
+  a.table = page_table;
+  a.width = static_cast<int32_t>(width);
+  a.groups = groups;
+  a.G = static_cast<int32_t>(G);
+  a.logits = logits;
+  a.ldl = ldl;
+  a.status = status;
+  return ssb::launch_indexer_logits_fp8(q8, q_scale, k_pages, pages, a, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_indexer_q_quant(const void* q, int64_t rows, uint8_t* q8, float* q_scale, void* stream) {
+  return ssb::launch_indexer_q_quant(q, rows, q8, q_scale, static_cast<cudaStream_t>(stream));
+}
+
 int ssb_indexer_expand(const int32_t* pool_ids, int64_t ldp, int32_t k, const int64_t* positions, int64_t rows,
                        int32_t* out, int64_t ldo, void* stream) {
   return ssb::launch_indexer_expand(pool_ids, ldp, k, positions, out, ldo, rows, static_cast<cudaStream_t>(stream));
@@ -385,6 +408,24 @@ int ssb_kpool_insert(const void* k, const void* gate, int64_t ld, const float* a
   a.table = page_table;
   a.width = static_cast<int32_t>(width);
   a.pool = static_cast<__nv_bfloat16*>(pool_cache);
+  a.tail = static_cast<__nv_bfloat16*>(tail_ring);
+  return ssb::launch_kpool_insert(a, max_rows, static_cast<cudaStream_t>(stream));
+}
+
+int ssb_kpool_insert_fp8(const void* k, const void* gate, int64_t ld, const float* ape, const int32_t* reqs, int64_t R,
+                         int32_t max_rows, const int32_t* page_table, int64_t width, uint8_t* pool_pages,
+                         void* tail_ring, void* stream) {
+  if (R < 0 || R > (1 << 20) || width <= 0 || width > (1 << 24) || pool_pages == nullptr) return kErrArgs;
+  ssb::KpoolArgs a;
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.gate = static_cast<const __nv_bfloat16*>(gate);
+  a.ld = ld;
+  a.ape = ape;
+  a.reqs = reqs;
+  a.R = static_cast<int32_t>(R);
+  a.table = page_table;
+  a.width = static_cast<int32_t>(width);
+  a.pool8 = pool_pages;
   a.tail = static_cast<__nv_bfloat16*>(tail_ring);
   return ssb::launch_kpool_insert(a, max_rows, static_cast<cudaStream_t>(stream));
 }

@@ -26,18 +26,27 @@ namespace {
 constexpr int kIdxEpiWarps = 8;             // two per TMEM lane quadrant, 4 of the 8 queries each
 constexpr int kIdxThreads = 64 + 32 * kIdxEpiWarps;
 constexpr int kStages = 4;
-constexpr int kAChunk = 128 * 128;          // one 64-dim k-chunk of a pool tile: 128 rows x 128 B
-constexpr int kABytes = 2 * kAChunk;        // 32 KB
+constexpr int kAChunk = 128 * 128;          // one 128-byte k-chunk of a pool tile: 128 rows x 128 B
 constexpr int kBChunk = 256 * 128;          // one k-chunk of the Q tile: 256 rows x 128 B
-constexpr int kBBytes = 2 * kBChunk;        // 64 KB
-constexpr int kOffB = 0;
-constexpr int kOffA = kBBytes;
-constexpr int kOffBar = kOffA + kStages * kABytes;
-// bars: full[S], empty[S], q_full, q_empty, acc_full[2], acc_empty[2], drain
-constexpr int kOffMisc = kOffBar + (2 * kStages + 7) * 8;
-constexpr int kOffW = (kOffMisc + 16 + 127) & ~127;   // fp32 head weights of a group's 8 queries, two buffers [2][8][32]
-static_assert(kOffW % 16 == 0, "float4 reads of the staged weights");
-constexpr int kIdxSmem = kOffW + 2 * 8 * 32 * 4 + 1024;
+constexpr int kFp8PageRows = 33;            // an FP8 pool page: 32 rows of 128 e4m3 codes, then 32 fp32 scales
+
+// Shared-memory plan of the bf16 form (128 dims = two 128-byte k-chunks of 64 values) and of the FP8 form (one chunk
+// of 128 codes): Q tile, a 4-stage pool-tile ring, barriers, the staged head weights.
+template <bool FP8>
+struct IdxCfg {
+  static constexpr int kChunks = FP8 ? 1 : 2;
+  static constexpr int kABytes = kChunks * kAChunk;     // 16 / 32 KB
+  static constexpr int kBBytes = kChunks * kBChunk;     // 32 / 64 KB
+  static constexpr int kOffB = 0;
+  static constexpr int kOffA = kBBytes;
+  static constexpr int kOffBar = kOffA + kStages * kABytes;
+  // bars: full[S], empty[S], q_full, q_empty, acc_full[2], acc_empty[2], drain
+  static constexpr int kOffMisc = kOffBar + (2 * kStages + 7) * 8;
+  static constexpr int kOffW = (kOffMisc + 16 + 127) & ~127;   // fp32 head weights of 8 queries, two buffers [2][8][32]
+  static constexpr int kSmem = kOffW + 2 * 8 * 32 * 4 + 1024;
+  static_assert(kOffA % 1024 == 0 && kABytes % 1024 == 0, "128-byte swizzle atoms of the tiles");
+  static_assert(kOffW % 16 == 0, "float4 reads of the staged weights");
+};
 
 SSB_DEVICE void drain(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer();
@@ -46,9 +55,13 @@ SSB_DEVICE void drain(uint32_t bar, uint32_t parity) {
   }
 }
 
+template <bool FP8>
 __global__ void __launch_bounds__(kIdxThreads, 1)
     indexer_logits_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                           const IdxArgs a) {
+  using C = IdxCfg<FP8>;
+  constexpr int kOffB = C::kOffB, kOffA = C::kOffA, kOffBar = C::kOffBar, kOffMisc = C::kOffMisc, kOffW = C::kOffW;
+  constexpr int kABytes = C::kABytes, kBBytes = C::kBBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -102,7 +115,7 @@ __global__ void __launch_bounds__(kIdxThreads, 1)
         if (!mbar_wait(bar_qempty, qphase ^ 1, abort_flag, a.status)) { ok = false; break; }
         mbar_arrive_expect_tx(bar_qfull, kBBytes);
         tma_load_2d(sbase + kOffB, &mq, 0, gr.y * 32, bar_qfull);
-        tma_load_2d(sbase + kOffB + kBChunk, &mq, 64, gr.y * 32, bar_qfull);
+        if (!FP8) tma_load_2d(sbase + kOffB + kBChunk, &mq, 64, gr.y * 32, bar_qfull);
         ++qissued;
         qphase ^= 1;
         const int32_t* pages = a.table + (int64_t)gr.x * a.width;
@@ -115,9 +128,10 @@ __global__ void __launch_bounds__(kIdxThreads, 1)
           for (int i = 0; i < 4; ++i) {
             const int j = 4 * m + i;
             const int page = j < a.width ? pages[j] : -1;
-            const int row = page >= 0 ? page * 32 : -32;           // a missing page reads as zeros
+            // a page's 32 pool rows (FP8: the first 32 of its 33 rows); a missing page reads as zeros
+            const int row = page >= 0 ? page * (FP8 ? kFp8PageRows : 32) : -32;
             tma_load_2d(sa + i * 4096, &mk, 0, row, fb);
-            tma_load_2d(sa + kAChunk + i * 4096, &mk, 64, row, fb);
+            if (!FP8) tma_load_2d(sa + kAChunk + i * 4096, &mk, 64, row, fb);
           }
           ++issued;
           if (++stage == kStages) { stage = 0; phase ^= 1; }
@@ -136,7 +150,7 @@ __global__ void __launch_bounds__(kIdxThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = idesc_bf16(128, 256);
+      constexpr uint32_t idesc = FP8 ? idesc_e4m3(128, 256) : idesc_bf16(128, 256);
       int stage = 0;
       uint32_t phase = 0, qphase = 0, iter = 0;
       bool ok = true, any = false;
@@ -152,13 +166,17 @@ __global__ void __launch_bounds__(kIdxThreads, 1)
           if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, a.status)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = sbase + kOffA + stage * kABytes;
+          // 32 bytes of K a step: 16 bf16 values (kind::f16) or 32 e4m3 codes (kind::f8f6f4)
 #pragma unroll
-          for (int kc = 0; kc < 2; ++kc) {
+          for (int kc = 0; kc < C::kChunks; ++kc) {
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
               const uint64_t ad = smem_desc(sa + kc * kAChunk + ks * 32, 0, 1024, 2);
               const uint64_t bd = smem_desc(sbase + kOffB + kc * kBChunk + ks * 32, 0, 1024, 2);
-              tc_mma_f16(tmem + buf * 256, ad, bd, idesc, (kc | ks) != 0 ? 1u : 0u);
+              if (FP8)
+                tc_mma_f8(tmem + buf * 256, ad, bd, idesc, (kc | ks) != 0 ? 1u : 0u);
+              else
+                tc_mma_f16(tmem + buf * 256, ad, bd, idesc, (kc | ks) != 0 ? 1u : 0u);
             }
           }
           any = true;
@@ -193,7 +211,9 @@ __global__ void __launch_bounds__(kIdxThreads, 1)
         const int j = et >> 5, hd = et & 31;
         if (ok && j < gr.z) {
           const uint16_t wb = static_cast<const uint16_t*>(a.w)[(int64_t)(gr.y + j) * a.ldw + hd];
-          wg[et] = __uint_as_float(static_cast<uint32_t>(wb) << 16);
+          float wv = __uint_as_float(static_cast<uint32_t>(wb) << 16);
+          if (FP8) wv *= a.q_scale[(int64_t)(gr.y + j) * 32 + hd];      // the query's scale folds into its weight
+          wg[et] = wv;
         }
       }
       if (named_bar_or(3, 32 * kIdxEpiWarps, !ok)) break;
@@ -203,6 +223,12 @@ __global__ void __launch_bounds__(kIdxThreads, 1)
         if (!mbar_wait(bar_accf + 8 * buf, (iter >> 1) & 1, abort_flag, a.status)) { ok = false; break; }
         tc_fence_after();
         const int64_t pool = (int64_t)m * 128 + quad * 32 + lane;
+        float kscale = 1.0f;                   // FP8: the pool's scale, row 32 of its page, entry lane
+        if (FP8) {
+          const int jp = 4 * m + quad;
+          const int page = jp < a.width ? a.table[(int64_t)gr.x * a.width + jp] : -1;
+          kscale = page >= 0 ? a.kscale[(int64_t)page * (kFp8PageRows * 32) + 32 * 32 + lane] : 0.0f;
+        }
         // two queries per TMEM wait; four partial sums over the heads (h % 4), added in a fixed order
         for (int j0 = 4 * half; j0 < min(gr.z, 4 * half + 4); j0 += 2) {
           const bool two = j0 + 1 < gr.z;
@@ -224,7 +250,7 @@ __global__ void __launch_bounds__(kIdxThreads, 1)
               acc[2] = __fmaf_rn(fmaxf(v[u][4 * i + 2], 0.0f), w4.z, acc[2]);
               acc[3] = __fmaf_rn(fmaxf(v[u][4 * i + 3], 0.0f), w4.w, acc[3]);
             }
-            if (pool < a.ldl) a.logits[q * a.ldl + pool] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+            if (pool < a.ldl) a.logits[q * a.ldl + pool] = ((acc[0] + acc[1]) + (acc[2] + acc[3])) * kscale;
           }
         }
         tc_fence_before();
@@ -281,14 +307,88 @@ int launch_indexer_logits(const void* q, const void* k_cache, int64_t pool_rows,
   if (rc != kOk) return rc;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(indexer_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kIdxSmem) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(indexer_logits_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             IdxCfg<false>::kSmem) != cudaSuccess)
       return kErrCuda;
     attr = true;
   }
   const int sms = device_sm_count();
   const int grid = a.G < sms ? a.G : sms;
-  indexer_logits_kernel<<<grid, kIdxThreads, kIdxSmem, stream>>>(mq, mk, a);
+  indexer_logits_kernel<false><<<grid, kIdxThreads, IdxCfg<false>::kSmem, stream>>>(mq, mk, a);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int launch_indexer_logits_fp8(const uint8_t* q8, const float* q_scale, const uint8_t* k_pages, int64_t pages,
+                              const IdxArgs& a_in, cudaStream_t stream) {
+  IdxArgs a = a_in;
+  if (q8 == nullptr || q_scale == nullptr || k_pages == nullptr || a.w == nullptr || a.table == nullptr ||
+      a.groups == nullptr || a.logits == nullptr || a.T <= 0 || pages <= 0 || a.width <= 0 || a.G < 0 ||
+      a.ldl <= 0 || (reinterpret_cast<uintptr_t>(a.w) & 15) || a.ldw < 32 || (a.ldw % 8) ||
+      (reinterpret_cast<uintptr_t>(k_pages) & 127) || (reinterpret_cast<uintptr_t>(q8) & 127))
+    return kErrArgs;
+  if (a.G == 0) return kOk;
+  a.q_scale = q_scale;
+  a.kscale = reinterpret_cast<const float*>(k_pages);
+  CUtensorMap mq, mk;
+  // e4m3 codes as bytes: Q [T * 32, 128] (one box of 256 rows), the pool pages [pages * 33, 128] (boxes of 32 rows)
+  int rc = make_map_2d_ex(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, q8, a.T * 32, 128, 128, 128, 256,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != kOk) return rc;
+  rc = make_map_2d_ex(&mk, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_pages, pages * kFp8PageRows, 128, 128, 128, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != kOk) return rc;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(indexer_logits_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             IdxCfg<true>::kSmem) != cudaSuccess)
+      return kErrCuda;
+    attr = true;
+  }
+  const int sms = device_sm_count();
+  const int grid = a.G < sms ? a.G : sms;
+  indexer_logits_kernel<true><<<grid, kIdxThreads, IdxCfg<true>::kSmem, stream>>>(mq, mk, a);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+namespace {
+
+// Indexer queries to e4m3 per (token, head) row of 128 (the FP8 indexer): one warp a row, 4 values a lane; scale =
+// 2^ceil(log2(max(amax, 1e-10) * fl(1 / 448))) (ue8m0, from the exponent bits), codes = e4m3(x / scale) (exact
+// quotients, rounded to nearest even by cvt.rn.satfinite).
+__global__ void idx_q_quant_kernel(const __nv_bfloat16* __restrict__ q, int64_t rows, uint8_t* __restrict__ q8,
+                                   float* __restrict__ qs) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint2 raw = *reinterpret_cast<const uint2*>(q + row * 128 + lane * 4);
+  float x[4];
+  x[0] = __uint_as_float(raw.x << 16);
+  x[1] = __uint_as_float(raw.x & 0xffff0000u);
+  x[2] = __uint_as_float(raw.y << 16);
+  x[3] = __uint_as_float(raw.y & 0xffff0000u);
+  float am = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+  const float s = fmaxf(am, 1e-10f) * (1.0f / 448.0f);
+  const uint32_t b = __float_as_uint(s);
+  const uint32_t e = ((b >> 23) & 0xffu) + ((b & 0x7fffffu) != 0u ? 1u : 0u);   // ceil(log2 s) + 127
+  const float scale = __uint_as_float(e << 23), inv = __uint_as_float((254u - e) << 23);
+  uint16_t lo, hi;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(x[1] * inv), "f"(x[0] * inv));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(x[3] * inv), "f"(x[2] * inv));
+  *reinterpret_cast<uint32_t*>(q8 + row * 128 + lane * 4) = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+  if (lane == 0) qs[row] = scale;
+}
+
+}  // namespace
+
+int launch_indexer_q_quant(const void* q, int64_t rows, uint8_t* q8, float* q_scale, cudaStream_t stream) {
+  if (q == nullptr || q8 == nullptr || q_scale == nullptr || rows < 0 || (reinterpret_cast<uintptr_t>(q) & 7) ||
+      (reinterpret_cast<uintptr_t>(q8) & 3))
+    return kErrArgs;
+  if (rows == 0) return kOk;
+  idx_q_quant_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(q), rows, q8,
+                                                                     q_scale);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

@@ -161,9 +161,16 @@ struct IdxArgs {
   float* logits = nullptr;             // [T, ldl]
   int64_t ldl = 0;
   int32_t* status = nullptr;
+  const float* q_scale = nullptr;      // FP8 form: fp32 [T, 32] query scales (folded into the head weights)
+  const float* kscale = nullptr;       // FP8 form: the pool pages read as fp32 (each page's scale row)
 };
 int launch_indexer_logits(const void* q, const void* k_cache, int64_t pool_rows, const IdxArgs& a,
                           cudaStream_t stream);
+// FP8 form: q8 e4m3 [T * 32, 128] with q_scale fp32 [T * 32]; the pool cache in pages of 33 rows of 128 bytes (32 rows
+// of e4m3 codes, then the 32 fp32 scales), `pages` of them.
+int launch_indexer_logits_fp8(const uint8_t* q8, const float* q_scale, const uint8_t* k_pages, int64_t pages,
+                              const IdxArgs& a, cudaStream_t stream);
+int launch_indexer_q_quant(const void* q, int64_t rows, uint8_t* q8, float* q_scale, cudaStream_t stream);
 int launch_indexer_expand(const int32_t* pool_ids, int64_t ldp, int32_t k, const int64_t* positions, int32_t* out,
                           int64_t ldo, int64_t rows, cudaStream_t stream);
 // bf16 map over [rows, width] elements (row pitch ld_bytes), box 64 x box_rows, 128-byte swizzle (csrc/gemm_nvfp4.cu).
@@ -205,6 +212,7 @@ struct KpoolArgs {
   int32_t width = 0;
   __nv_bfloat16* pool = nullptr;       // [pages * 32, 128]
   __nv_bfloat16* tail = nullptr;       // [blocks][2][4][128]
+  uint8_t* pool8 = nullptr;            // FP8 form instead of `pool`: pages of 33 rows x 128 bytes (32 code rows, scales)
 };
 int launch_kpool_insert(const KpoolArgs& a, int32_t max_rows, cudaStream_t stream);
 

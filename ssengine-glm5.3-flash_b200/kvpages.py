@@ -17,7 +17,8 @@ latent block's size).
 Differences from the reference, by necessity or choice (stated where they live):
 - latent rows are 576 bytes (e4m3 latent 512 + rope 64, BASELINE's DSA dims) at slot * 576 of the layer's latent
   tensor (the reference's fork stores 512 bytes a token);
-- the pool-key cache keeps bf16 rows of 128 (256 bytes) in pages of 32 pools (the reference: FP8 + scale, 132 bytes);
+- the pool-key cache keeps bf16 rows of 128 (256 bytes) in pages of 32 pools (the reference: FP8 + scale, 132 bytes;
+  `StageKv(pool_fp8=True)` lays the pages out that way, 33 rows of 128 bytes a page, for the FP8 indexer kernels);
 - the tail ring is its own [blocks, 2, 4, 128] bf16 tensor per DSA layer, indexed by `state_blocks[5]` (the
   reference aliases it into the indexer region).
 """
@@ -66,14 +67,19 @@ def _latent_slots(layers, is_dsa) -> tuple[list, dict, dict, int]:
     return dsa, group, slot, max([len(dsa)] + [s + 1 for s in slot.values()])
 
 
-def block_bytes(layers, is_dsa, kda_heads: int) -> int:
+POOL_PAGE_BYTES = 32 * POOL_ROW * 2                    # bf16 pool keys of one 128-token page
+POOL_PAGE_BYTES_FP8 = 33 * 128                          # the reference's 32 entries of 132 bytes (codes, then scales)
+
+
+def block_bytes(layers, is_dsa, kda_heads: int, pool_fp8: bool = False) -> int:
     """Device bytes one block id costs a stage holding `layers`: the latent (or state-only) block of every slot, plus
-    each DSA layer's pool-key rows and tail ring for that block."""
+    each DSA layer's pool-key pages and tail ring for that block."""
     dsa, _, _, n_slots = _latent_slots(layers, is_dsa)
     state_page = kda_state_bytes(kda_heads)[2]
     latent_page = BLOCK_TOKENS * LATENT_ROW
     pages = sum(latent_page if j < len(dsa) else state_page for j in range(n_slots))
-    return pages + len(dsa) * (PAGES_PER_BLOCK * 32 * POOL_ROW * 2 + 2 * 4 * POOL_ROW * 2)
+    pool = POOL_PAGE_BYTES_FP8 if pool_fp8 else POOL_PAGE_BYTES
+    return pages + len(dsa) * (PAGES_PER_BLOCK * pool + 2 * 4 * POOL_ROW * 2)
 
 
 class StageKv:
@@ -84,7 +90,8 @@ class StageKv:
     is the index of the latent tensor its state aliases (extra state-only tensors when the stage has fewer DSA layers
     than a group has KDA layers here)."""
 
-    def __init__(self, layers, is_dsa, num_blocks: int, kda_heads: int, device, pin: bool = False):
+    def __init__(self, layers, is_dsa, num_blocks: int, kda_heads: int, device, pin: bool = False,
+                 pool_fp8: bool = False):
         dev = torch.device(device)
         self.num_blocks = num_blocks
         self.kda_heads = kda_heads
@@ -100,8 +107,13 @@ class StageKv:
         for j in range(n_slots):
             page = latent_page if j < len(self.dsa_layers) else state_page
             self.pages.append(torch.zeros(num_blocks, page, dtype=torch.uint8, device=dev, **mem))
-        self.pool = [torch.zeros(num_blocks * PAGES_PER_BLOCK * 32, POOL_ROW, dtype=torch.bfloat16, device=dev, **mem)
-                     for _ in self.dsa_layers]
+        self.pool_fp8 = pool_fp8
+        if pool_fp8:       # the reference's indexer pages: 33 rows of 128 bytes a page (32 code rows, the scales)
+            self.pool = [torch.zeros(num_blocks * PAGES_PER_BLOCK * 33, 128, dtype=torch.uint8, device=dev, **mem)
+                         for _ in self.dsa_layers]
+        else:
+            self.pool = [torch.zeros(num_blocks * PAGES_PER_BLOCK * 32, POOL_ROW, dtype=torch.bfloat16, device=dev,
+                                     **mem) for _ in self.dsa_layers]
         self.tail = [torch.zeros(num_blocks, 2, 4, POOL_ROW, dtype=torch.bfloat16, device=dev, **mem)
                      for _ in self.dsa_layers]
 
@@ -155,7 +167,7 @@ class StageKv:
             out.append(ViewRange(stage, f"layers.{layer}.latent", "kv", t.data_ptr(), t.stride(0), t.shape[1]))
         for j, layer in enumerate(self.dsa_layers):
             t = self.pool[j]
-            row = PAGES_PER_BLOCK * 32 * POOL_ROW * t.element_size()
+            row = PAGES_PER_BLOCK * (POOL_PAGE_BYTES_FP8 if self.pool_fp8 else POOL_PAGE_BYTES)
             out.append(ViewRange(stage, f"layers.{layer}.pool_keys", "kv", t.data_ptr(), row, row))
         for j, layer in enumerate(self.dsa_layers):
             t = self.tail[j]

@@ -23,7 +23,8 @@ EXPORTS = ("ssb_version", "ssb_sf_atom_cols", "ssb_nvfp4_quantize", "ssb_nvfp4_g
            "ssb_indexer_logits", "ssb_indexer_expand", "ssb_sparse_mla", "ssb_mla_cache_append", "ssb_mla_q_pack",
            "ssb_kpool_insert", "ssb_gated_rmsnorm", "ssb_gated_rmsnorm_nvfp4", "ssb_hc_expand", "ssb_hc_mean",
            "ssb_nvfp4_gemm_grouped", "ssb_rmsnorm_cols", "ssb_rope", "ssb_transpose_heads", "ssb_concat_cols",
-           "ssb_head_tiles", "ssb_moe_route_sigmoid", "ssb_copy_runs")
+           "ssb_head_tiles", "ssb_moe_route_sigmoid", "ssb_copy_runs", "ssb_indexer_logits_fp8",
+           "ssb_indexer_q_quant", "ssb_kpool_insert_fp8")
 
 EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
 ROUTE_SOFTMAX, ROUTE_SIGMOID_BIAS = 0, 1
@@ -75,7 +76,8 @@ _LIB = None
 
 # Kernels each entry point launches (1 unless listed), for the count of this library's launches in a timed region
 KERNELS_PER_CALL = {"ssb_moe_forward": 10, "ssb_moe_forward_profiled": 10, "ssb_mhc_ws": 2,
-                    "ssb_kda_prefill": 2, "ssb_kda_prefill_ws": 2, "ssb_kpool_insert": 2, "ssb_stage_metadata": 2}
+                    "ssb_kda_prefill": 2, "ssb_kda_prefill_ws": 2, "ssb_kpool_insert": 2, "ssb_kpool_insert_fp8": 2,
+                    "ssb_stage_metadata": 2}
 
 
 class _Counting:
@@ -141,6 +143,10 @@ _SIGS = {
     "ssb_flag_write": ([_P, ctypes.c_uint32, _P], ctypes.c_int),
     "ssb_p2p_copy": ([_P, _P, _I64, _P], ctypes.c_int),
     "ssb_copy_runs": ([_P, _I64, _P, _P], ctypes.c_int),
+    "ssb_indexer_logits_fp8": ([_P, _P, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P],
+                               ctypes.c_int),
+    "ssb_indexer_q_quant": ([_P, _I64, _P, _P, _P], ctypes.c_int),
+    "ssb_kpool_insert_fp8": ([_P, _P, _I64, _P, _P, _I64, _I32, _P, _I64, _P, _P, _P], ctypes.c_int),
     "ssb_indexer_logits": ([_P, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P], ctypes.c_int),
     "ssb_indexer_expand": ([_P, _I64, _I32, _P, _I64, _P, _I64, _P], ctypes.c_int),
     "ssb_sparse_mla": ([_P, _I64, _P, _P, _I64, _I32, _P, _I32, _P, _I64, _F, _F, _P, _P, _P], ctypes.c_int),

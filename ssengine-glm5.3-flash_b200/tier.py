@@ -182,7 +182,7 @@ class TierArena:
         self.stage = stage
         self.hbm = stage_kv
         self.dram = StageKv(stage_kv.layers, stage_kv.is_dsa, num_blocks + 1, stage_kv.kda_heads, "cpu",
-                            pin=copier is None)
+                            pin=copier is None, pool_fp8=stage_kv.pool_fp8)
         self.hbm_ranges = stage_kv.tier_ranges(stage)
         self.dram_ranges = self.dram.tier_ranges(stage)
         self.device = device

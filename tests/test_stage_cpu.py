@@ -204,3 +204,38 @@ def test_tier_ranges_cover_the_stage_views_block_by_block():
                 assert rec.base + b * rec.stride + rec.nbytes <= page.data_ptr() + (b + 1) * page.shape[1]
         pk = next(r for r in rs if r.name.endswith(".pool_keys"))
         assert pk.nbytes == PAGES_PER_BLOCK * 32 * 128 * 2
+
+
+def test_fp8_pool_pages_have_the_reference_entry_layout():
+    """`StageKv(pool_fp8=True)`: each DSA layer's pool keys in pages of 33 rows of 128 bytes (the reference's 32
+    entries of 132 bytes: codes, then scales), the same bytes the oracle's page writer produces; block bytes and tier
+    ranges follow."""
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+    import numpy as np
+    import torch
+
+    from oracle import indexer as oidx
+    from ssengine_b200.kvpages import PAGES_PER_BLOCK, StageKv, block_bytes
+
+    dsa = lambda i: i % 4 == 3
+    layers = list(range(12))
+    kv = StageKv(layers, dsa, 3, 4, "cpu", pool_fp8=True)
+    assert kv.pool[0].shape == (3 * PAGES_PER_BLOCK * 33, 128) and kv.pool[0].dtype == torch.uint8
+    per_block = sum(t.numel() * t.element_size() for t in kv.pages + kv.pool + kv.tail) // 3
+    assert per_block == block_bytes(layers, dsa, 4, pool_fp8=True) < block_bytes(layers, dsa, 4)
+    pk = next(r for r in kv.tier_ranges(0) if r.name.endswith(".pool_keys"))
+    assert pk.nbytes == pk.stride == PAGES_PER_BLOCK * 132 * 32
+    rng = np.random.default_rng(0)
+    codes, scales = oidx.quant_pool_rows(rng.standard_normal((40, 128)).astype(np.float32))
+    pages = np.array([70, 71])                         # pool p of the request at page pages[p // 32], entry p % 32
+    rows = oidx.pool_rows(pages, 40)
+    ref = oidx.write_pool_pages(np.zeros((3 * PAGES_PER_BLOCK, 33 * 128), np.uint8), rows, codes, scales)
+    mine = kv.pool[0].numpy().reshape(-1, 33 * 128)
+    oidx.write_pool_pages(mine, rows, codes, scales)
+    np.testing.assert_array_equal(mine, ref)
+    got_c, got_s = oidx.read_pool_pages(mine, rows)
+    np.testing.assert_array_equal(got_c, codes)
+    np.testing.assert_array_equal(got_s, scales)

@@ -149,3 +149,20 @@ def test_resumed_contexts_find_their_pages_and_states_after_in_order_copies():
         assert tier.stats["stored"] > 10 and tier.stats["read"] > 5
         assert kv.stats["tier_hits"] == tier.stats["read"]
     assert tot["tier"] > 20 and tot["hbm"] > 20
+
+
+def test_fp8_pool_pages_move_with_the_context():
+    g = torch.Generator().manual_seed(2)
+    hbm = StageKv(list(range(12)), lambda i: i % 4 == 3, 10, 4, "cpu", pool_fp8=True)
+    for t in hbm.pages + hbm.pool + hbm.tail:
+        t.view(torch.uint8).copy_(torch.randint(0, 256, t.view(torch.uint8).shape, dtype=torch.uint8, generator=g))
+    arena = TierArena(hbm, 0, 9, copier=memmove_copier)
+    assert arena.dram.pool_fp8
+    ref = [t.clone() for t in hbm.pool]
+    arena.apply([TierOp("write", [70, 141], [3, 4, 5, 6, 7, 8], [75, 76], [2, 3, 4, 5, 6, 7])])
+    for t in hbm.pool:
+        t.zero_()
+    arena.apply([TierOp("read", [150, 80], [9, 8, 7, 6, 5, 4], [75, 76], [2, 3, 4, 5, 6, 7])])
+    for old, new in zip(ref, hbm.pool):
+        for po, pn in ((70, 150), (141, 80)):
+            assert torch.equal(old[po * 33:(po + 1) * 33], new[pn * 33:(pn + 1) * 33])
