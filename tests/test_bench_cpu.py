@@ -67,3 +67,63 @@ def test_session_pool_is_sized_by_the_costliest_stage():
     whole = block_bytes(list(range(45)), dsa, bench.MODEL["kda_heads"])        # 11 DSA layers
     assert bench.session_pool_blocks(bench.split_for(1), 100e9) == int(100e9 // whole) < 2000
     assert bench.session_pool_blocks(bench.split_for(8), 1e15) == 7143
+
+
+def test_session_workload_glue_runs_end_to_end_on_fakes(monkeypatch, capsys):
+    """`bench.run_sessions` at N = 1 with the device pieces replaced (no GPU here): the scheduler, page pool,
+    controller and reporter run for real, the stage's forward is a fake that takes a modeled time, and the JSON line
+    carries the TTFT fields."""
+    import json
+    import time
+    import types
+
+    import torch
+
+    import bench
+    from ssengine_b200 import controller, stage
+
+    class FakeStageModel:
+        def __init__(self, cfg, rank, device):
+            self.cfg, self.first, self.last = cfg, rank == 0, True
+            self.hidden_width = 4 * cfg.hidden
+            self.status = torch.zeros(1, dtype=torch.int32)
+            self.kv = None
+
+    def fake_step(worker, device):
+        def step(plan):
+            n = plan.num_tokens
+            done_last = [c for c in plan.chunks if c.is_last]
+
+            def done():
+                time.sleep(2e-4 + n * 1e-8)
+                return int(n * 1e4)
+
+            return done, (lambda: [7] * len(done_last))
+        return step
+
+    class FakeArena:                                          # the pinned host mirror needs a CUDA context
+        def __init__(self, stage_kv, rank, blocks, device=None):
+            self.blocks, self.bytes_moved = blocks, 0
+
+        def apply(self, ops, stream=None):
+            self.bytes_moved += len(ops)
+
+        def check(self):
+            pass
+
+    from ssengine_b200 import tier
+
+    monkeypatch.setattr(torch.cuda, "set_device", lambda *a: None)
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a: None)
+    monkeypatch.setattr(stage, "StageModel", FakeStageModel)
+    monkeypatch.setattr(controller, "cuda_step", fake_step)
+    monkeypatch.setattr(tier, "TierArena", FakeArena)
+    for dram in (0.0, 2.0):
+        args = types.SimpleNamespace(sessions=6, session_s=0.8, session_warm_s=0.2, think_s=0.02, start_ctx=2000,
+                                     pool_gb=1.0, force_after_ms=500.0, dram_gb=dram, tokens=8192, layers=45)
+        bench.run_sessions(args, 0, 1, 0)
+        line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+        assert line["metric"].startswith("TTFT") and line["unit"] == "s" and line["higher_is_better"] is False
+        assert line["rounds"] > 5 and line["unfinished"] == 0 and line["ttft_s"]["p50"] > 0
+        assert line["config"]["parallelism"] == "pp1" and line["kv"]["admitted"] >= line["rounds"]
+        assert (line["dram_tier"] is not None) == (dram > 0)
