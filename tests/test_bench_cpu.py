@@ -127,3 +127,89 @@ def test_session_workload_glue_runs_end_to_end_on_fakes(monkeypatch, capsys):
         assert line["rounds"] > 5 and line["unfinished"] == 0 and line["ttft_s"]["p50"] > 0
         assert line["config"]["parallelism"] == "pp1" and line["kv"]["admitted"] >= line["rounds"]
         assert (line["dram_tier"] is not None) == (dram > 0)
+
+
+def _sessions_rank(rank: int, port: int, out):
+    import io
+    import os
+    import sys
+    import time
+    import types
+    from contextlib import redirect_stdout
+
+    sys.path.insert(0, os.environ["SSB_ROOT"])
+    import __graft_entry__
+
+    __graft_entry__.import_package()
+    import torch
+
+    import bench
+    from ssengine_b200 import controller, edge, stage
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2")
+
+    class FakeStageModel:
+        def __init__(self, cfg, r, device):
+            self.cfg, self.first, self.last = cfg, r == 0, r == 1
+            self.hidden_width = 4 * cfg.hidden
+            self.status = torch.zeros(1, dtype=torch.int32)
+            self.kv = None
+
+    class FakePipe:
+        def __init__(self, *a, **k):
+            pass
+
+        def check(self):
+            pass
+
+        def close(self):
+            pass
+
+    def fake_step(worker, device):
+        def step(plan):
+            n_last = sum(c.is_last for c in plan.chunks)
+
+            def done():
+                time.sleep(2e-4)
+                return 100_000
+
+            return done, ((lambda: [3] * n_last) if worker.stage.last else None)
+        return step
+
+    torch.cuda.set_device = lambda *a: None
+    torch.cuda.synchronize = lambda *a: None
+    stage.StageModel = FakeStageModel
+    edge.P2pPipe = FakePipe
+    controller.cuda_step = fake_step
+    args = types.SimpleNamespace(sessions=6, session_s=0.8, session_warm_s=0.2, think_s=0.02, start_ctx=2000,
+                                 pool_gb=1.0, force_after_ms=500.0, dram_gb=0.0, tokens=8192, layers=45)
+    buf = io.StringIO()
+    with redirect_stdout(buf):
+        bench.run_sessions(args, rank, 2, rank)
+    out.put((rank, buf.getvalue()))
+
+
+def test_session_workload_glue_two_ranks():
+    import json
+    import multiprocessing as mp
+    import os
+    import socket
+    from pathlib import Path
+
+    os.environ["SSB_ROOT"] = str(Path(__file__).resolve().parent.parent)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_sessions_rank, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=180) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res[1] == ""                                      # only rank 0 prints
+    line = json.loads(res[0].strip().splitlines()[-1])
+    assert line["n_gpus"] == 2 and line["config"]["parallelism"] == "pp2"
+    assert line["rounds"] > 5 and line["unfinished"] == 0 and line["ttft_s"]["p50"] > 0
