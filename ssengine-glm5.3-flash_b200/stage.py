@@ -167,6 +167,20 @@ class _Pack:
         return dev[off:off + a.nbytes].view(dtype).view(a.shape)
 
 
+def kda_tables(chunks, order, qsl) -> np.ndarray:
+    """int32 [5, R, 4]: one sequence table per KDA state group g2..g6, a row per chunk = {first row, end row, the
+    chunk's state_blocks[g], has state (the chunk continues its request)}. `order`: the chunks in row order, `qsl`
+    their row starts (R + 1). Rows longest first: the scan runs one CTA per (sequence, head, value half) in table
+    order, so the longest sequences start first (an LPT order, in the place of the reference's head-split plan,
+    ssengine/native/kda_split_heads.cpp:17-91); each sequence's result does not depend on its place in the table."""
+    R = len(order)
+    q_lens = np.diff(np.asarray(qsl, np.int64))
+    lpt = sorted(range(R), key=lambda r: -int(q_lens[r]))
+    return np.array([[(int(qsl[r]), int(qsl[r + 1]), int(chunks[order[r]].state_blocks[g]),
+                       int(chunks[order[r]].start > 0)) for r in lpt] for g in range(5)],
+                    dtype=np.int32).reshape(5, -1, 4)
+
+
 class StageModel:
     def __init__(self, cfg: StageConfig, stage: int, device, *, num_blocks: int | None = None, warmup: bool = True,
                  cuda_graphs: bool | None = None, ipc_kv: bool = False, extra_blocks: int = 0):
@@ -324,16 +338,7 @@ class StageModel:
              "last": pk.add(last)}
         if self.kda:
             check_blocks(chunks, self.num_blocks)
-            # one sequence table per KDA state group g2..g6: the chunk's state_blocks[g] (has state = the chunk
-            # continues its request)
-            # Rows longest first: the scan runs one CTA per (sequence, head, value half) in table order, so the longest
-            # sequences start first (an LPT order, in the place of the reference's head-split plan); each sequence's
-            # result does not depend on its place in the table.
-            lpt = sorted(range(R), key=lambda r: -int(q_lens[r]))
-            ks = np.array([[(int(qsl[r]), int(qsl[r + 1]), int(chunks[order[r]].state_blocks[g]),
-                             int(chunks[order[r]].start > 0)) for r in lpt] for g in range(5)],
-                          dtype=np.int32).reshape(5, -1, 4)
-            h["kda"] = pk.add(ks)
+            h["kda"] = pk.add(kda_tables(chunks, order, qsl))
         if any(self.is_dsa):
             from .indexer import work_groups
 

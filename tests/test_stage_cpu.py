@@ -239,3 +239,35 @@ def test_fp8_pool_pages_have_the_reference_entry_layout():
     got_c, got_s = oidx.read_pool_pages(mine, rows)
     np.testing.assert_array_equal(got_c, codes)
     np.testing.assert_array_equal(got_s, scales)
+
+
+def test_kda_tables_cover_every_chunk_once_longest_first():
+    """The KDA sequence tables a microbatch's prepare builds: per state group, every chunk's rows exactly once (the
+    tables tile [0, T) with no overlap), longest first, each row with the chunk's state block of that group and its
+    has-state flag (the chunk continues its request)."""
+    import numpy as np
+
+    from ssengine_b200.messages import Chunk
+    from ssengine_b200.stage import kda_tables, row_order
+
+    rng = np.random.default_rng(4)
+    for trial in range(30):
+        R = int(rng.integers(1, 12))
+        lens = [int(x) for x in rng.choice([1, 3, 17, 64, 65, 256, 257, 3000, 8192], R)]
+        starts = [int(x) for x in rng.choice([0, 0, 5, 4096, 70000], R)]
+        chunks = [Chunk(f"r{i}", s, n, [], [10 * i + g + 1 for g in range(6)], True, None)
+                  for i, (s, n) in enumerate(zip(starts, lens))]
+        order = row_order(lens)
+        qsl = np.concatenate([[0], np.cumsum([lens[i] for i in order])])
+        t = kda_tables(chunks, order, qsl)
+        assert t.shape == (5, R, 4) and t.dtype == np.int32
+        for g in range(5):
+            spans = sorted((int(a), int(b)) for a, b in t[g, :, :2])
+            assert spans[0][0] == 0 and spans[-1][1] == qsl[-1]
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))            # a tiling: no gap, no overlap
+            sizes = t[g, :, 1] - t[g, :, 0]
+            assert (np.diff(sizes) <= 0).all()                                      # longest first
+            for a, b, blk, has in t[g]:
+                r = int(np.searchsorted(qsl, a))
+                c = chunks[order[r]]
+                assert b - a == c.num_tokens and blk == c.state_blocks[g] and has == int(c.start > 0)
