@@ -85,6 +85,9 @@ def parse():
     ap.add_argument("--pool-gb", type=float, default=100.0,
                     help="sessions: device memory per stage for KV and state blocks (the pool size follows)")
     ap.add_argument("--force-after-ms", type=float, default=60_000.0, help="sessions: force-schedule bound")
+    ap.add_argument("--forming", choices=["rule", "limits"], default="rule",
+                    help="sessions: form each microbatch when the dispatch rule's projection says so (the reference "
+                         "controller's way), or whenever the in-flight limits allow")
     ap.add_argument("--dram-gb", type=float, default=0.0,
                     help="sessions: pinned host memory per stage for the DRAM tier under HBM (0: no tier)")
     return ap.parse_args()
@@ -491,6 +494,7 @@ def run_sessions(args, rank: int, world: int, local: int) -> None:
 
     from ssengine_b200 import lib
     from ssengine_b200.controller import Controller, Reporter, SessionLoad, StoreChannel, cuda_step, serve_stage
+    from ssengine_b200.dispatch import DispatchRule
     from ssengine_b200.edge import P2pPipe
     from ssengine_b200.pagepool import KvManager
     from ssengine_b200.scheduler import Scheduler, SchedulerConfig
@@ -529,11 +533,12 @@ def run_sessions(args, rank: int, world: int, local: int) -> None:
         kv = KvManager(blocks, keep_sessions=True)
         if dram_blocks:
             kv.lower = DramTier(dram_blocks)
+        rule = DispatchRule(max_in_flight=gate, lead_ms=3.0, num_stages=world) if args.forming == "rule" else None
         sched = Scheduler(kv, SchedulerConfig(order="srpt", mb_tokens=args.tokens, force_after_ms=args.force_after_ms),
-                          None, gate + 1, 1)
+                          None, *(rule.sched_limits if rule is not None else (gate + 1, 1)))
         load = SessionLoad(sessions=args.sessions, seed=SEED, vocab=MODEL["vocab"], think_s=args.think_s,
                            start_ctx_max=args.start_ctx, stagger_s=min(5.0, args.session_warm_s))
-        ctl = Controller(sched, load, world)
+        ctl = Controller(sched, load, world, rule=rule)
         rep = Reporter(0, ctl.local.put, init=init)
         summary = ctl.run(step, rep, chan, duration_s=args.session_s, warm_s=args.session_warm_s)
         rep.close()
@@ -543,8 +548,7 @@ def run_sessions(args, rank: int, world: int, local: int) -> None:
         busy = [m.get("busy0", 0) for m in ctl.microbatches]
         summary["stage0_busy_s"] = sum(busy) / 1e9
     else:
-        sink = chan.put_report if rank == world - 1 else (lambda rep: None)
-        serve_stage(step, chan, Reporter(rank, sink, init=init))
+        serve_stage(step, chan, Reporter(rank, chan.put_report, init=init))
     so.on = False
     torch.cuda.synchronize()
     if pipe is not None:
@@ -572,13 +576,15 @@ def run_sessions(args, rank: int, world: int, local: int) -> None:
                                    f"{args.session_warm_s:.0f} s measured",
                        "parallelism": f"pp{world}", "layer_split": list(split),
                        "scheduler": f"srpt, {args.tokens}-token microbatches, force after {args.force_after_ms} ms, "
-                                    f"in-flight gate {gate} on the GPU",
+                                    f"in-flight gate {gate} on the GPU, formed "
+                                    + ("by the dispatch rule's projection" if args.forming == "rule"
+                                       else "whenever the in-flight limits allow"),
                        "pool": f"{blocks} blocks per stage, kept sessions LRU; "
                                + (f"DRAM tier of {dram_blocks} blocks per stage ({args.dram_gb:.0f} GB pinned), "
                                   f"exclusive, copies in stream order" if dram_blocks else "no DRAM tier")},
             "dram_tier": summary.get("dram_tier"), "tier_bytes_per_rank": [r["tier_bytes"] for r in allr],
             "rounds": summary["rounds"], "unfinished": summary["unfinished"], "microbatches": summary["microbatches"],
-            "kv": summary["kv"], "stage0_busy_s": summary["stage0_busy_s"],
+            "kv": summary["kv"], "stage0_busy_s": summary["stage0_busy_s"], "decisions": summary["decisions"],
             "gpu_launches": sum(r["launches"] for r in allr),
         }
         print(json.dumps(line), flush=True)

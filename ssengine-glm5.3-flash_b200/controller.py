@@ -9,8 +9,9 @@ the same roles run inside the stage processes of one `torch.distributed` job:
   session's next round arrives a think time later (closed loop);
 - every other stage runs `serve_stage`: take plan k from the store, run it, repeat until the stop plan;
 - a `Reporter` thread per stage waits for each microbatch's completion in order (a CUDA event, or whatever `done`
-  waits on) and emits {mb, stage, start_ns, end_ns, tokens}; the last stage's reports go back to stage 0 through the
-  store, stage 0's own stay local.
+  waits on) and emits {mb, stage, start_ns, end_ns, tokens}; the other stages' reports go back to stage 0 through
+  the store (the last stage's carry the tokens; all of them feed the dispatch rule when one forms the plans), stage
+  0's own stay local.
 Plans and reports are small host messages; the activations never leave the GPUs (the P2P stage edge, `edge.py`),
 and stage 0's GPU holds itself to the edge's in-flight limit whatever the host forms ahead.
 
@@ -150,13 +151,13 @@ def wait_key(store, key: str, give_up_s: float, poll_s: float = 2e-4) -> None:
 
 
 class StoreChannel:
-    """Plans from stage 0 to the other stages, and the last stage's reports back, over a c10d store (the job's
-    rendezvous store, or any `torch.distributed.Store`). Keys: plan/<k>, rep/<k>."""
+    """Plans from stage 0 to the other stages, and the other stages' reports back, over a c10d store (the job's
+    rendezvous store, or any `torch.distributed.Store`). Keys: plan/<k>, rep/<stage>/<k>."""
 
     def __init__(self, store, give_up_s: float = 900.0):
         self.store = store
         self.give_up_s = give_up_s
-        self.next_report = 0
+        self.next_report: dict[int, int] = {}
 
     def put_plan(self, k: int, plan: Plan | None):
         self.store.set(f"plan/{k}", pickle.dumps(plan))
@@ -170,24 +171,34 @@ class StoreChannel:
         self.store.delete_key(f"plan/{k}")
 
     def put_report(self, rep: dict):
-        self.store.set(f"rep/{rep['mb']}", pickle.dumps(rep))
+        self.store.set(f"rep/{rep['stage']}/{rep['mb']}", pickle.dumps(rep))
 
-    def poll_reports(self) -> list[dict]:
+    def poll_reports(self, stages) -> list[dict]:
+        """Every report that has arrived from `stages`, each stage's in microbatch order."""
         out = []
-        while self.store.check([f"rep/{self.next_report}"]):
-            key = f"rep/{self.next_report}"
-            out.append(pickle.loads(self.store.get(key)))
-            self.store.delete_key(key)
-            self.next_report += 1
+        for st in stages:
+            k = self.next_report.get(st, 0)
+            while self.store.check([f"rep/{st}/{k}"]):
+                key = f"rep/{st}/{k}"
+                out.append(pickle.loads(self.store.get(key)))
+                self.store.delete_key(key)
+                k += 1
+            self.next_report[st] = k
         return out
 
 
 class Controller:
-    """Stage 0's host loop (see the module docstring)."""
+    """Stage 0's host loop (see the module docstring). Without `rule` a microbatch is formed whenever the scheduler's
+    in-flight limits allow; with a `dispatch.DispatchRule` (built for the GPU's in-flight gate, the scheduler built
+    with `rule.sched_limits`), one is formed when the rule's projection of the pipeline says NOW, with the microbatches
+    projected to leave by its start not counted (`exiting`): the reference controller's forming
+    (ssengine/runtime/dispatch.py), so that rounds arriving until then can ride it."""
 
     def __init__(self, sched: Scheduler, load: SessionLoad, num_stages: int, clock=time.monotonic_ns,
-                 poll_s: float = 2e-4):
+                 poll_s: float = 2e-4, rule=None):
         self.sched, self.load, self.num_stages = sched, load, num_stages
+        self.rule = rule
+        self.decisions = {"now": 0, "wait": 0, "no": 0}
         self.last = num_stages - 1
         self.clock, self.poll_s = clock, poll_s
         self.local: queue.Queue = queue.Queue()          # stage 0's own reports
@@ -206,6 +217,8 @@ class Controller:
         k, st = rep["mb"], rep["stage"]
         mb = self.microbatches[k]
         mb[f"end{st}"], mb[f"busy{st}"] = rep["end_ns"], rep["end_ns"] - rep["start_ns"]
+        if self.rule is not None:
+            self.rule.stage_done(st, k, rep["start_ns"], rep["end_ns"])
         if st == 0 or st == self.last:
             self.sched.stage_done(st, self.last)
         if st != self.last:
@@ -248,7 +261,7 @@ class Controller:
             while not self.local.empty():
                 reps.append(self.local.get())
             if channel is not None and self.last > 0:
-                reps += channel.poll_reports()
+                reps += channel.poll_reports(range(1, self.num_stages))
             for rep in sorted(reps, key=lambda x: (x["mb"], x["stage"])):
                 self._on_report(rep)
                 if channel is not None and rep["stage"] == self.last and self.last > 0:
@@ -256,7 +269,17 @@ class Controller:
                 busy = True
             if reporter.error is not None:
                 raise reporter.error
-            while (chunks := sched.next_microbatch(now)) is not None:
+            while True:
+                if self.rule is not None:
+                    d, _ = self.rule.decide(now)
+                    self.decisions[d] += 1
+                    if d != "now":
+                        break
+                    chunks = sched.next_microbatch(now, self.rule.exiting)
+                else:
+                    chunks = sched.next_microbatch(now)
+                if chunks is None:
+                    break
                 plan = Scheduler.plan(k, chunks, token_ids=load.ids)
                 plan.tier_ops = sched.kv.take_ops()              # copies recorded since the last plan, in order
                 self._plans[k] = [c.req for c in chunks if c.is_last]
@@ -264,10 +287,13 @@ class Controller:
                                           "chunks": len(plan.chunks)})
                 if channel is not None and self.last > 0:
                     channel.put_plan(k, for_later_stages(plan))
+                if self.rule is not None:
+                    self.rule.dispatched(k, now, plan.num_tokens)
                 done, tokens = step(plan)
                 reporter.submit(k, done, tokens)
                 k += 1
                 busy = True
+                now = self.clock()
             if now >= end and sched.in_flight == 0 and not self._arrivals:
                 if not sched.has_work() or now >= end + int(drain_s * 1e9):
                     break
@@ -293,6 +319,8 @@ class Controller:
             "prefix_hit_share": cached / tok if tok else None,
             "microbatches": len(self.microbatches), "unfinished": len(self._reqs),
             "window_s": span, "all_rounds": len(self.rounds),
+            "forming": "dispatch rule" if self.rule is not None else "when the in-flight limits allow",
+            "decisions": dict(self.decisions) if self.rule is not None else None,
         }
 
 

@@ -120,7 +120,8 @@ def test_session_workload_glue_runs_end_to_end_on_fakes(monkeypatch, capsys):
     monkeypatch.setattr(tier, "TierArena", FakeArena)
     for dram in (0.0, 2.0):
         args = types.SimpleNamespace(sessions=6, session_s=0.8, session_warm_s=0.2, think_s=0.02, start_ctx=2000,
-                                     pool_gb=1.0, force_after_ms=500.0, dram_gb=dram, tokens=8192, layers=45)
+                                     pool_gb=1.0, force_after_ms=500.0, dram_gb=dram, tokens=8192, layers=45,
+                                     forming="rule" if dram else "limits")
         bench.run_sessions(args, 0, 1, 0)
         line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
         assert line["metric"].startswith("TTFT") and line["unit"] == "s" and line["higher_is_better"] is False
@@ -182,7 +183,8 @@ def _sessions_rank(rank: int, port: int, out):
     edge.P2pPipe = FakePipe
     controller.cuda_step = fake_step
     args = types.SimpleNamespace(sessions=6, session_s=0.8, session_warm_s=0.2, think_s=0.02, start_ctx=2000,
-                                 pool_gb=1.0, force_after_ms=500.0, dram_gb=0.0, tokens=8192, layers=45)
+                                 pool_gb=1.0, force_after_ms=500.0, dram_gb=0.0, tokens=8192, layers=45,
+                                 forming="rule")
     buf = io.StringIO()
     with redirect_stdout(buf):
         bench.run_sessions(args, rank, 2, rank)

@@ -146,7 +146,28 @@ def test_one_stage_with_a_dram_tier_resumes_evicted_contexts():
     assert sum(r["tokens"] - r["cached"] for r in ctl.rounds) == stage.seen_tokens
 
 
-def _rank(rank: int, port: int, out):
+def test_one_stage_with_the_dispatch_rule_forming_plans():
+    import torch.distributed as dist
+
+    from ssengine_b200.dispatch import DispatchRule
+
+    store = dist.HashStore()
+    rule = DispatchRule(max_in_flight=GATE, lead_ms=3.0, num_stages=1)
+    kv = KvManager(NUM_BLOCKS, keep_sessions=True)
+    sched = Scheduler(kv, CFG, None, *rule.sched_limits)
+    ctl = Controller(sched, small_load(), 1, rule=rule)
+    stage = FakeStage(0, 1, store, NUM_BLOCKS)
+    rep = Reporter(0, ctl.local.put)
+    s = ctl.run(stage.step, rep, None, duration_s=1.5, warm_s=0.4)
+    rep.close()
+    assert s["unfinished"] == 0 and s["rounds"] > 50 and sched.in_flight == 0
+    assert s["forming"] == "dispatch rule" and s["microbatches"] == stage.k
+    assert s["decisions"]["now"] >= s["microbatches"]               # a NOW with nothing waiting forms nothing
+    assert s["decisions"]["wait"] + s["decisions"]["no"] > 0
+    assert 0 < s["ttft_s"]["p50"] <= s["ttft_s"]["p90"] < 5.0
+
+
+def _rank(rank: int, port: int, out, use_rule: bool = False):
     import torch.distributed as dist
 
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
@@ -156,9 +177,12 @@ def _rank(rank: int, port: int, out):
         chan = StoreChannel(dist.PrefixStore("ctl/", store), give_up_s=60)
         stage = FakeStage(rank, 2, dist.PrefixStore("fake/", store), NUM_BLOCKS)
         if rank == 0:
+            from ssengine_b200.dispatch import DispatchRule
+
             kv = KvManager(NUM_BLOCKS, keep_sessions=True)
-            sched = Scheduler(kv, CFG, None, GATE + 1, 1)
-            ctl = Controller(sched, small_load(), 2)
+            rule = DispatchRule(max_in_flight=GATE, lead_ms=3.0, num_stages=2) if use_rule else None
+            sched = Scheduler(kv, CFG, None, *(rule.sched_limits if rule else (GATE + 1, 1)))
+            ctl = Controller(sched, small_load(), 2, rule=rule)
             rep = Reporter(0, ctl.local.put)
             s = ctl.run(stage.step, rep, chan, duration_s=1.5, warm_s=0.4)
             rep.close()
@@ -178,11 +202,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_two_stage_processes_serve_the_session_load():
+@pytest.mark.parametrize("use_rule", [False, True])
+def test_two_stage_processes_serve_the_session_load(use_rule):
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, port, out)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, port, out, use_rule)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -197,3 +222,5 @@ def test_two_stage_processes_serve_the_session_load():
     assert n0 == n1 == s["microbatches"] >= 5           # every plan reached both stages
     assert s["unfinished"] == 0 and s["in_flight"] == 0 and s["hard"] == 0 and s["rounds"] > 30
     assert 0 < s["ttft_s"]["p50"] <= s["ttft_s"]["p90"] < 5.0 and 0 < s["prefix_hit_share"] < 1
+    if use_rule:                                          # both stages' reports reached the rule
+        assert s["decisions"]["now"] >= s["microbatches"] and s["decisions"]["wait"] + s["decisions"]["no"] > 0
