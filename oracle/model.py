@@ -50,8 +50,9 @@ def dense_ffn(y, w, gs_x: float, gs_h: float) -> np.ndarray:
 def dsa_block(y, p, positions, reqs, kv_cache, pool_cache, tail, gs_in: float):
     """The DSA attention block on rows y [T, H] (bf16 values). p: a_proj, q_b, wq_idx, idx_proj, o_proj (codes, sf,
     gs), w_uk, w_uv (per-head bf16 weights [64, N, K]), q_norm, kv_norm, ape, q_lora, nope, v_dim, theta, eps, scale, q_scale,
-    k_scale. reqs: per request (first row, rows, start position, pages, tail block). kv_cache uint8 [slots, 576] e4m3,
-    pool_cache [rows, 128] (bf16 values), tail [blocks, 2, 4, 128] -- all updated in place. -> bf16-valued [T, H]."""
+    k_scale, and optionally indexer_fp8. reqs: per request (first row, rows, start position, pages, tail block). kv_cache
+    uint8 [slots, 576] e4m3, pool_cache [rows, 128] (bf16 values; with indexer_fp8 uint8 [pages * 33, 128], the
+    reference's 132-byte entries), tail [blocks, 2, 4, 128] -- all updated in place. -> bf16-valued [T, H]."""
     T = y.shape[0]
     QL, L, RP, NH = p["q_lora"], 512, 64, 64
     nope, v_dim = p["nope"], p["v_dim"]
@@ -73,13 +74,22 @@ def dsa_block(y, p, positions, reqs, kv_cache, pool_cache, tail, gs_in: float):
     idx = bf16(lin(y, p["idx_proj"]))
     k_idx, w, gate = idx[:, :128], idx[:, 128:160], idx[:, 160:288]
     out_lat = np.zeros((T, NH, L))
+    fp8 = bool(p.get("indexer_fp8"))          # pool_cache: uint8 [pages * 33, 128], the 132-byte entries
     for first, n, start, pages, tblk in reqs:
         rows = slice(first, first + n)
         pools, ring = okp.prefill_chunk(k_idx[rows], gate[rows], start, p["ape"], {}, tail[tblk].copy())
         tail[tblk] = bf16(ring)
-        for pid, v in pools.items():
-            pool_cache[oidx.pool_rows(pages, pid + 1)[pid]] = bf16(v)
-        lg = oidx.logits(q_idx[rows], w[rows], pool_cache, pages, positions[rows])
+        if fp8:
+            cache = pool_cache.reshape(-1, 33 * 128)
+            for pid, v in pools.items():
+                codes, sc = oidx.quant_pool_rows(np.asarray(v, np.float32)[None])
+                oidx.write_pool_pages(cache, oidx.pool_rows(pages, pid + 1)[pid:pid + 1], codes, sc)
+            qc, qs = oidx.quant_query_heads(q_idx[rows])
+            lg = oidx.logits_fp8(qc, qs, w[rows], cache, pages, positions[rows])
+        else:
+            for pid, v in pools.items():
+                pool_cache[oidx.pool_rows(pages, pid + 1)[pid]] = bf16(v)
+            lg = oidx.logits(q_idx[rows], w[rows], pool_cache, pages, positions[rows])
         width = max((len(r) for r in lg), default=0)
         dense = np.full((n, max(width, 1)), -np.inf, np.float32)
         for i, r in enumerate(lg):

@@ -418,12 +418,16 @@ class DsaAttention:
     POOLS_PER_PAGE = 32                # pools of 4 tokens in a 128-token KV page
 
     def __init__(self, seed: int, hidden: int, device, q_lora: int = 1536, nope: int = 192, v_dim: int = 256,
-                 theta: float = 10000.0, eps: float = 1e-6, init: str = "uniform", std: float = 0.02):
+                 theta: float = 10000.0, eps: float = 1e-6, init: str = "uniform", std: float = 0.02,
+                 indexer_fp8: bool = False):
         dev = torch.device(device)
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
         H = hidden
         self.H, self.q_lora, self.nope, self.v_dim, self.theta, self.eps = H, q_lora, nope, v_dim, theta, eps
+        # the FP8 indexer: e4m3 queries with per-(token, head) scales, pool keys in the reference's 132-byte entries
+        # (the pool cache is then uint8 [pages * 33, 128]); not yet run on a GPU, off by default
+        self.indexer_fp8 = indexer_fp8
         self.qh = nope + self.ROPE
         w = dict(init=init, std=std)
         self.a_proj = Nvfp4Linear.random(g, q_lora + self.LATENT + self.ROPE, H, dev, **w)
@@ -490,6 +494,9 @@ class DsaAttention:
             logits = torch.empty(T, ldl, dtype=torch.float32, device=dev)
         ids = torch.empty(T, self.TOPK, dtype=torch.int32, device=dev)
         tok = torch.empty(T, 4 * self.TOPK + 3 + 5, dtype=torch.int32, device=dev)
+        if self.indexer_fp8:
+            q8_idx = torch.empty(T, self.IDX_HEADS, self.IDX_DIM, dtype=torch.uint8, device=dev)
+            qs_idx = torch.empty(T, self.IDX_HEADS, dtype=torch.float32, device=dev)
         qa_q = self.q_b.quantize(qa, stream)
         # the indexer branch (projections, pool insert, logits, top-k, expansion) on a side stream, beside the query
         # branch; the layer's stream waits for it before the sparse MLA, so everything after stays ordered. Nothing
@@ -506,9 +513,17 @@ class DsaAttention:
         self.idx_proj.gemm(*y_q, T, idx, status, side)
         k_idx, gate = idx[:, :self.IDX_DIM], idx[:, self.IDX_DIM + self.IDX_HEADS:2 * self.IDX_DIM + self.IDX_HEADS]
         w = idx[:, self.IDX_DIM:self.IDX_DIM + self.IDX_HEADS]          # bf16 head weights, read in place
-        indexer.kpool_insert(k_idx, gate, self.ape, kpool_reqs, max_rows, page_table, pool_cache, tail_ring, side)
-        indexer.logits(q_idx.view(T, self.IDX_HEADS, self.IDX_DIM), w, pool_cache, page_table, groups, logits,
-                       status, side)
+        if self.indexer_fp8:
+            # the logits' common factor (softmax scale x heads^-1/2 = 2^-6) is left out: a power of two, it changes
+            # neither the top-k set nor its ties
+            indexer.q_quant(q_idx.view(T, self.IDX_HEADS, self.IDX_DIM), q8_idx, qs_idx, side)
+            indexer.kpool_insert_fp8(k_idx, gate, self.ape, kpool_reqs, max_rows, page_table, pool_cache, tail_ring,
+                                     side)
+            indexer.logits_fp8(q8_idx, qs_idx, w, pool_cache, page_table, groups, logits, status, side)
+        else:
+            indexer.kpool_insert(k_idx, gate, self.ape, kpool_reqs, max_rows, page_table, pool_cache, tail_ring, side)
+            indexer.logits(q_idx.view(T, self.IDX_HEADS, self.IDX_DIM), w, pool_cache, page_table, groups, logits,
+                           status, side)
         indexer.topk(logits, positions, self.TOPK, ids, side, ranges=ranges)
         indexer.expand(ids, positions, tok, side)
         join = torch.cuda.Event()
@@ -544,13 +559,14 @@ class DsaDecoderLayer:
 
     def __init__(self, seed: int, hidden: int, inter: int, experts: int, top_k: int, device, q_lora: int = 1536,
                  nope: int = 192, v_dim: int = 256, ffn: str = "moe", routing: dict | None = None,
-                 init: str = "uniform", std: float = 0.02):
+                 init: str = "uniform", std: float = 0.02, indexer_fp8: bool = False):
         dev = torch.device(device)
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
         self.H = hidden
         self.bound_a = MhcBoundary(g, hidden, dev)
-        self.attn = DsaAttention(seed + 1, hidden, dev, q_lora=q_lora, nope=nope, v_dim=v_dim, init=init, std=std)
+        self.attn = DsaAttention(seed + 1, hidden, dev, q_lora=q_lora, nope=nope, v_dim=v_dim, init=init, std=std,
+                                 indexer_fp8=indexer_fp8)
         self.bound_b = MhcBoundary(g, hidden, dev)
         self.ffn = _make_ffn(seed + 2, hidden, inter, experts, top_k, dev, ffn, routing, init, std)
         self.moe = self.ffn                  # the FFN sub-block (MoELayer or DenseFfn)

@@ -124,6 +124,8 @@ class StageConfig:
     init_std: float = 0.02
     max_context: int = 131_072         # the longest context a request reaches (sizes the indexer's logits buffer)
     reserve_reqs: int = 64             # requests per microbatch the KDA chunk workspace is reserved for
+    indexer_fp8: bool = False          # the FP8 indexer over the reference's 132-byte pool entries (not yet run on a
+                                       # GPU; the validated bf16 indexer by default)
 
 
 @dataclass
@@ -210,7 +212,8 @@ class StageModel:
 
             # KV and state pages in the reference's block layout: KDA group g2..g6 states alias the DSA layers'
             # latent blocks (kvpages.StageKv)
-            self.kv = StageKv(list(self.layer_range), self.layer_is_dsa, self.num_blocks, cfg.kda_heads, self.device)
+            self.kv = StageKv(list(self.layer_range), self.layer_is_dsa, self.num_blocks, cfg.kda_heads, self.device,
+                              pool_fp8=cfg.indexer_fp8)
             route = None if cfg.routing == "softmax" else dict(routing=cfg.routing, n_group=cfg.n_group,
                                                                topk_group=cfg.topk_group)
             self.layers, self.kda_states, self.kda_group = [], [], []
@@ -221,7 +224,8 @@ class StageModel:
                 inter = cfg.dense_inter if dense else F
                 if dsa:
                     self.layers.append(DsaDecoderLayer(seed, H, inter, E, cfg.top_k, self.device, q_lora=cfg.q_lora,
-                                                       nope=cfg.mla_nope, v_dim=cfg.mla_v_dim, **ffn))
+                                                       nope=cfg.mla_nope, v_dim=cfg.mla_v_dim,
+                                                       indexer_fp8=cfg.indexer_fp8, **ffn))
                     # latent cache e4m3 [slots, 576], pool-key cache [pages * 32, 128], tail ring [blocks, 2, 4, 128]
                     self.kda_states.append((self.kv.latent(i), self.kv.pool_keys(i), self.kv.tail_ring(i)))
                     self.kda_group.append(None)

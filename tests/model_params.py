@@ -33,7 +33,8 @@ def stage_params(stage) -> dict:
                                                                  "w_uk", "w_uv")}
             attn.update(q_norm=_n(blk.q_norm), kv_norm=_n(blk.kv_norm), ape=blk.ape.cpu().numpy(),
                         q_lora=blk.q_lora, nope=blk.nope, v_dim=blk.v_dim, theta=blk.theta, eps=blk.eps,
-                        scale=blk.scale, q_scale=blk.q_scale, k_scale=blk.k_scale)
+                        scale=blk.scale, q_scale=blk.q_scale, k_scale=blk.k_scale,
+                        indexer_fp8=getattr(blk, "indexer_fp8", False))
         else:
             attn = {name: _lin(getattr(blk, name)) for name in ("in_proj", "f_b", "g_b", "o_proj")}
             attn.update(conv_w=_n(blk.kda.conv_weight), a_log=_n(blk.kda.a_log), dt_bias=_n(blk.kda.dt_bias),
@@ -57,8 +58,9 @@ def stage_states(stage) -> list:
     """Host copies of each layer's states (KDA: conv, recurrent; DSA: latent cache bytes, pool keys, tail ring)."""
     out = []
     for st, dsa in zip(stage.kda_states, stage.is_dsa):
-        if dsa:
-            out.append([st[0].cpu().numpy().copy(), _n(st[1]).copy(), _n(st[2]).copy()])
+        if dsa:                                   # an FP8 pool cache (uint8 pages) is kept as its bytes
+            pools = st[1].cpu().numpy().copy() if st[1].dtype == torch.uint8 else _n(st[1]).copy()
+            out.append([st[0].cpu().numpy().copy(), pools, _n(st[2]).copy()])
         else:
             out.append([_n(st[0]).copy(), st[1].cpu().numpy().copy()])
     return out
