@@ -88,8 +88,8 @@ class SessionLoad:
                 self._epoch[i] += 1
                 prev, n = 0, add
         self._ctx[i] = n
-        r = Request(f"s{i}.{self._round[i]}", n, arrival_ns=arrival_ns, session=i, prefix_tokens=prev)
-        r.epoch = self._epoch[i]
+        r = Request(f"s{i}.{self._round[i]}", n, arrival_ns=arrival_ns, session=i, prefix_tokens=prev,
+                    epoch=self._epoch[i])
         self._round[i] += 1
         return r
 

@@ -389,7 +389,7 @@ class KvManager:
             return self._whole_blocks_for(states, back, req.session)
         return need <= self.capacity
 
-    def _unkeep(self, k: Kept, evicted: bool = False):
+    def _unkeep(self, k: Kept):
         self.kept_charge -= self.kept_cost(k.tokens)
         if self.content_keys and k.tokens < SESSION_KEY_TOKENS:
             self._short[k.tokens] -= 1
@@ -399,7 +399,7 @@ class KvManager:
         KV pages and `states` state blocks."""
         while self.kept and (self.hard + self.kept_charge > self.capacity or not self.pool.can_take(pages, states)):
             key, k = self.kept.popitem(last=False)
-            self._unkeep(k, evicted=True)
+            self._unkeep(k)
             self.evicted[key] = k.tokens
             if self.lower is not None:
                 self.lower.store(key, k)               # its write-back is recorded before any reuse of the pages

@@ -85,6 +85,8 @@ class Request:
     hit_memo: tuple | None = None
     admit_info: dict | None = None
     output_token: int | None = None
+    epoch: int = 0                     # which of its session's contexts the prompt continues (a session load's token
+                                       # stream restarts at its context cap)
 
     @property
     def remaining(self) -> int:

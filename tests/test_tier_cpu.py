@@ -119,8 +119,7 @@ def _churn(seed: int, steps: int = 1500, hbm_blocks: int = 40, dram_blocks: int 
         if prev and rng.random() < 0.1:
             epoch, prev = epoch + 1, 0                   # the session starts over
         n = (prev + 1 if prev else 0) + rng.choice([rng.randrange(1, 400), rng.randrange(1, 2 * 8576)])
-        r = Request(f"r{step}", n, session=s, prefix_tokens=prev + 1 if prev else 0)
-        r.epoch = epoch
+        r = Request(f"r{step}", n, session=s, prefix_tokens=prev + 1 if prev else 0, epoch=epoch)
         if not kv.fits(r):
             continue
         r.cached = kv.allocate(r)
