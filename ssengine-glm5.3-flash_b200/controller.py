@@ -217,8 +217,8 @@ class Controller:
         k, st = rep["mb"], rep["stage"]
         mb = self.microbatches[k]
         mb[f"end{st}"], mb[f"busy{st}"] = rep["end_ns"], rep["end_ns"] - rep["start_ns"]
-        if self.rule is not None:
-            self.rule.stage_done(st, k, rep["start_ns"], rep["end_ns"])
+        if self.rule is not None:            # stage 0's host stamps (delivered, prepare called, prepared, ready)
+            self.rule.stage_done(st, k, rep["start_ns"], rep["end_ns"], mb.get("host_ns") if st == 0 else None)
         if st == 0 or st == self.last:
             self.sched.stage_done(st, self.last)
         if st != self.last:
@@ -289,6 +289,11 @@ class Controller:
                     channel.put_plan(k, for_later_stages(plan))
                 if self.rule is not None:
                     self.rule.dispatched(k, now, plan.num_tokens)
+                # stage 0 runs in this process: the plan is delivered and prepared inside `step`, so every stamp is
+                # the call and the rule's launch term (GPU start - the later of the call, stage 0's previous end and
+                # the gate) measures forming -> first kernel on a free stage 0
+                t_call = self.clock()
+                self.microbatches[-1]["host_ns"] = (t_call, t_call, t_call, t_call)
                 done, tokens = step(plan)
                 reporter.submit(k, done, tokens)
                 k += 1
