@@ -18,12 +18,13 @@ import torch
 from oracle import indexer as oidx
 from oracle.mla import e4m3_decode
 
-pytestmark = [pytest.mark.gpu, pytest.mark.skip(reason="first run pending: the FP8 indexer kernels have not yet run "
-                                                        "on a B200")]
+pytestmark = pytest.mark.gpu
+pending = pytest.mark.skip(reason="first run pending: the FP8 indexer kernels have not yet run on a B200")
 
 REQS = [(0, 50), (37, 13), (300, 70), (1400, 21), (3, 1)]       # (position of the first query row, query rows)
 
 
+@pending
 def test_query_quantization_matches_the_oracle(cuda):
     from ssengine_b200 import indexer
 
@@ -39,6 +40,7 @@ def test_query_quantization_matches_the_oracle(cuda):
     np.testing.assert_array_equal(qs.cpu().numpy(), scales)
 
 
+@pending
 def test_fp8_logits_over_reference_pages(cuda):
     from ssengine_b200 import indexer
 
@@ -84,6 +86,7 @@ def test_fp8_logits_over_reference_pages(cuda):
                 assert np.abs(g - wr).max() <= 1e-4 * max(np.abs(wr).max(), 1e-6), (r, i)
 
 
+@pending
 def test_fp8_pool_insert_against_the_bf16_insert(cuda):
     from ssengine_b200 import indexer
 
@@ -118,6 +121,7 @@ def test_fp8_pool_insert_against_the_bf16_insert(cuda):
     assert (np.abs(vals - ref) <= (2.0 ** -3) * np.abs(ref) + scales[:, None] * 2.0 ** -9 + 1e-2 * np.abs(ref)).all()
 
 
+@pending
 def test_stage_with_the_fp8_indexer_matches_the_oracle(cuda):
     """BASELINE config 1's model with `indexer_fp8` on, over a 2,600-token prompt (650 pools: the 512-pool top-k
     drops some), against the oracle's composition with its FP8 indexer branch: every layer within 3e-2 on the device
