@@ -143,29 +143,38 @@ def op_runs(op: TierOp, hbm_ranges, dram_ranges, piece: int = PIECE_BYTES) -> np
         raise ValueError(f"tier op kind {op.kind!r}")
     if len(op.hbm_pages) != len(op.dram_pages) or len(op.hbm_states) != len(op.dram_states):
         raise ValueError("tier op: page or state counts differ between the two sides")
-    runs: list[list[int]] = []
-
-    def add(h: int, d: int, n: int):
-        s, t = (h, d) if write else (d, h)
-        if runs and runs[-1][0] + runs[-1][2] == s and runs[-1][1] + runs[-1][2] == t:
-            runs[-1][2] += n
-        else:
-            runs.append([s, t, n])
-
-    for hr, dr in zip(hbm_ranges, dram_ranges):
+    hp = np.asarray(op.hbm_pages, np.int64)
+    dp = np.asarray(op.dram_pages, np.int64)
+    src, dst, size = [], [], []
+    for hr, dr in zip(hbm_ranges, dram_ranges):       # every slice in view order, each view's pages in op order
         if hr.kind == "kv":
             pb = hr.nbytes // PAGES_PER_BLOCK
-            for hp, dp in zip(op.hbm_pages, op.dram_pages):
-                add(hr.base + (hp // PAGES_PER_BLOCK) * hr.stride + (hp % PAGES_PER_BLOCK) * pb,
-                    dr.base + (dp // PAGES_PER_BLOCK) * dr.stride + (dp % PAGES_PER_BLOCK) * pb, pb)
+            h = hr.base + (hp // PAGES_PER_BLOCK) * hr.stride + (hp % PAGES_PER_BLOCK) * pb
+            d = dr.base + (dp // PAGES_PER_BLOCK) * dr.stride + (dp % PAGES_PER_BLOCK) * pb
+            n = np.full(len(hp), pb, np.int64)
         elif 0 <= hr.group < len(op.hbm_states):
-            add(hr.base + op.hbm_states[hr.group] * hr.stride, dr.base + op.dram_states[hr.group] * dr.stride,
-                hr.nbytes)
-    out = []
-    for s, t, n in runs:
-        for o in range(0, n, piece):
-            out.append((s + o, t + o, min(piece, n - o)))
-    arr = np.asarray(out, dtype=np.int64).reshape(-1, 3)
+            h = np.array([hr.base + op.hbm_states[hr.group] * hr.stride], np.int64)
+            d = np.array([dr.base + op.dram_states[hr.group] * dr.stride], np.int64)
+            n = np.array([hr.nbytes], np.int64)
+        else:
+            continue
+        src.append(h if write else d)
+        dst.append(d if write else h)
+        size.append(n)
+    if not size:
+        return np.zeros((0, 3), np.int64)
+    s, t, n = np.concatenate(src), np.concatenate(dst), np.concatenate(size)
+    # merge slices that continue the previous one on both sides
+    brk = np.ones(len(n), bool)
+    brk[1:] = (s[1:] != s[:-1] + n[:-1]) | (t[1:] != t[:-1] + n[:-1])
+    head = np.flatnonzero(brk)
+    rs, rt = s[head], t[head]
+    rn = np.add.reduceat(n, head)
+    # cut runs into pieces of at most `piece` bytes
+    cnt = -(-rn // piece)
+    idx = np.repeat(np.arange(len(rn)), cnt)
+    off = (np.arange(int(cnt.sum())) - np.repeat(np.cumsum(cnt) - cnt, cnt)) * piece
+    arr = np.stack([rs[idx] + off, rt[idx] + off, np.minimum(piece, rn[idx] - off)], axis=1).astype(np.int64)
     if arr.size and ((arr & 15) != 0).any():
         raise ValueError("tier copy runs must be 16-byte aligned")
     return arr

@@ -165,3 +165,46 @@ def test_fp8_pool_pages_move_with_the_context():
     for old, new in zip(ref, hbm.pool):
         for po, pn in ((70, 150), (141, 80)):
             assert torch.equal(old[po * 33:(po + 1) * 33], new[pn * 33:(pn + 1) * 33])
+
+
+def _runs_reference(op, hbm_ranges, dram_ranges, piece):
+    """The copy runs restated slice by slice (the vectorized op_runs must give exactly these)."""
+    runs = []
+    write = op.kind == "write"
+    for hr, dr in zip(hbm_ranges, dram_ranges):
+        if hr.kind == "kv":
+            pb = hr.nbytes // PAGES_PER_BLOCK
+            sl = [(hr.base + (h // 67) * hr.stride + (h % 67) * pb, dr.base + (d // 67) * dr.stride + (d % 67) * pb,
+                   pb) for h, d in zip(op.hbm_pages, op.dram_pages)]
+        elif 0 <= hr.group < len(op.hbm_states):
+            sl = [(hr.base + op.hbm_states[hr.group] * hr.stride, dr.base + op.dram_states[hr.group] * dr.stride,
+                   hr.nbytes)]
+        else:
+            sl = []
+        for h, d, n in sl:
+            a, b = (h, d) if write else (d, h)
+            if runs and runs[-1][0] + runs[-1][2] == a and runs[-1][1] + runs[-1][2] == b:
+                runs[-1][2] += n
+            else:
+                runs.append([a, b, n])
+    return [(a + o, b + o, min(piece, n - o)) for a, b, n in runs for o in range(0, n, piece)]
+
+
+def test_vectorized_runs_equal_the_slice_by_slice_restatement():
+    rng = np.random.default_rng(9)
+    kv = StageKv(list(range(12)), lambda i: i % 4 == 3, 40, 4, "cpu")
+    arena = TierArena(kv, 0, 30, copier=memmove_copier)
+    for trial in range(20):
+        n = int(rng.integers(0, 300))
+        hb = rng.choice(np.arange(67, 39 * 67), n, replace=False)
+        if trial % 3 == 0:
+            hb = np.sort(hb)                                      # runs of consecutive pages merge
+        db = rng.choice(np.arange(67, 30 * 67), n, replace=False)
+        if trial % 2 == 0:
+            db = np.sort(db)
+        op = TierOp("write" if trial % 2 else "read", hb.tolist(), [1, 2, 3, 4, 5, 6], db.tolist(),
+                    [7, 8, 9, 10, 11, 12])
+        for piece in (64 * 1024, 256 * 1024):
+            got = op_runs(op, arena.hbm_ranges, arena.dram_ranges, piece)
+            want = np.asarray(_runs_reference(op, arena.hbm_ranges, arena.dram_ranges, piece), np.int64).reshape(-1, 3)
+            np.testing.assert_array_equal(got, want)
