@@ -61,6 +61,8 @@ class HostPredictor:
         self.rate: dict[int, float] = {}        # bucket -> mean ns
         self.dev: dict[int, float] = {}
 
+    bucket = staticmethod(size_bucket)
+
     def observe(self, tokens: int, ns: int):
         b, a = size_bucket(tokens), self.alpha
         if b in self.rate:
