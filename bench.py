@@ -24,6 +24,12 @@ the MoE gate_up GEMM's roofline and the model's algorithmic FLOP rate. `e2e`: th
 public path with each microbatch's plan metadata and token ids packed on the host and copied in (`prepare`) and the
 last stage's greedy tokens copied back to pinned host memory, inside the timed region.
 
+`--workload sessions` (not the default line): the same stages serving BASELINE config 5's closed-loop session load
+(`ssengine_b200.controller`): stage 0's host forms microbatches with the SRPT scheduler over the page pool with the
+exact prefix cache (optionally a DRAM tier under it, `--dram-gb`), by the dispatch rule's projection (`--forming`),
+and the line reports TTFT p50 / p90 / p99, rounds a second, computed and new tokens a second and the prefix-hit share
+over the rounds arriving after `--session-warm-s`.
+
 `--impl reference` times the reference's path on the host cores: the reference has no CPU implementation (its GPU path
 needs a vLLM fork and FlashInfer builds absent here), so it times this repository's CPU restatement (oracle/) of each
 layer kind on a bounded sample of a microbatch (rank 0 only), with weights built on the host without the CUDA library.
