@@ -205,9 +205,13 @@ class TierArena:
 
         if not hasattr(self, "_status"):
             self._status = torch.zeros(1, dtype=torch.int32, device=self.device)
-        dev = torch.from_numpy(runs).pin_memory().to(self.device, non_blocking=True)
-        lib.check("ssb_copy_runs", lib.load().ssb_copy_runs(dev.data_ptr(), runs.shape[0], self._status.data_ptr(),
-                                                            lib.stream_ptr(stream)))
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        # the runs' upload, the kernel and the runs buffer's life all on the kernel's stream: the caching allocators
+        # keep the pinned staging and the device buffer until that stream has passed them
+        with torch.cuda.stream(s):
+            dev = torch.from_numpy(runs).pin_memory().to(self.device, non_blocking=True)
+            lib.check("ssb_copy_runs", lib.load().ssb_copy_runs(dev.data_ptr(), runs.shape[0],
+                                                                self._status.data_ptr(), lib.stream_ptr(s)))
 
     def check(self):
         """Raise if a copy kernel rejected a run (reads the status word: synchronizes with the device)."""
