@@ -237,12 +237,15 @@ class Controller:
             self._arrive(rep["end_ns"] + self.load.think_ns(), req.session)
 
     def run(self, step, reporter: Reporter, channel: StoreChannel | None, *, duration_s: float, warm_s: float,
-            drain_s: float = 60.0) -> dict:
+            drain_s: float = 60.0, stall_s: float = 300.0) -> dict:
         """Serve the load for `duration_s` (arrivals stop then; rounds already arrived are served, up to `drain_s`
         more), then send the stop plan. `step(plan) -> (done, tokens)` runs stage 0's forward of one plan; `reporter`
-        is stage 0's `Reporter` whose sink is `self.local.put`; `channel` reaches the other stages (None at N = 1)."""
+        is stage 0's `Reporter` whose sink is `self.local.put`; `channel` reaches the other stages (None at N = 1).
+        Watchdog: with microbatches in flight and no report for `stall_s`, raise with the scheduler's state (a stage
+        that died or stopped reporting)."""
         sched, load = self.sched, self.load
         t0 = self.clock()
+        last_report = t0
         end, measure_from = t0 + int(duration_s * 1e9), t0 + int(warm_s * 1e9)
         self._stop_arrivals = end
         for t, i in load.first_arrivals(t0):
@@ -262,6 +265,13 @@ class Controller:
                 reps.append(self.local.get())
             if channel is not None and self.last > 0:
                 reps += channel.poll_reports(range(1, self.num_stages))
+            if reps:
+                last_report = now
+            elif sched.in_flight and now - last_report > int(stall_s * 1e9):
+                raise RuntimeError(f"no stage report for {stall_s:.0f} s with microbatches in flight: "
+                                   f"{sched.state()}, {len(self.microbatches)} formed")
+            elif not sched.in_flight:
+                last_report = now
             for rep in sorted(reps, key=lambda x: (x["mb"], x["stage"])):
                 self._on_report(rep)
                 if channel is not None and rep["stage"] == self.last and self.last > 0:

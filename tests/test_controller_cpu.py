@@ -224,3 +224,21 @@ def test_two_stage_processes_serve_the_session_load(use_rule):
     assert 0 < s["ttft_s"]["p50"] <= s["ttft_s"]["p90"] < 5.0 and 0 < s["prefix_hit_share"] < 1
     if use_rule:                                          # both stages' reports reached the rule
         assert s["decisions"]["now"] >= s["microbatches"] and s["decisions"]["wait"] + s["decisions"]["no"] > 0
+
+
+def test_a_stage_that_stops_reporting_trips_the_watchdog():
+    """A stage whose microbatches never complete: the controller raises after `stall_s` instead of waiting forever."""
+    import threading
+
+    never = threading.Event()
+    kv = KvManager(NUM_BLOCKS, keep_sessions=True)
+    sched = Scheduler(kv, CFG, None, GATE + 1, 1)
+    ctl = Controller(sched, small_load(), 1)
+    rep = Reporter(0, ctl.local.put)
+
+    def stuck_step(plan):
+        return (lambda: never.wait(5.0) and 0), None
+
+    with pytest.raises(RuntimeError, match="no stage report"):
+        ctl.run(stuck_step, rep, None, duration_s=0.5, warm_s=0.1, stall_s=0.5)
+    never.set()
