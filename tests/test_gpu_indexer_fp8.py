@@ -8,8 +8,7 @@ against the oracle's FP8 restatement (oracle/indexer.py, pinned to vLLM's own qu
   bf16 pool value over its scale, scales equal to the oracle's rule on the bf16 values except where a row's fp32 amax
   sits at a power-of-two boundary.
 
-The kernels were written after this build's last GPU run; these tests are skipped until that first run (remove the
-mark then)."""
+The three kernel tests passed on their first B200 run; the stage-level test stays skipped until its own first run."""
 
 import numpy as np
 import pytest
@@ -24,7 +23,6 @@ pending = pytest.mark.skip(reason="first run pending: the FP8 indexer kernels ha
 REQS = [(0, 50), (37, 13), (300, 70), (1400, 21), (3, 1)]       # (position of the first query row, query rows)
 
 
-@pending
 def test_query_quantization_matches_the_oracle(cuda):
     from ssengine_b200 import indexer
 
@@ -40,7 +38,6 @@ def test_query_quantization_matches_the_oracle(cuda):
     np.testing.assert_array_equal(qs.cpu().numpy(), scales)
 
 
-@pending
 def test_fp8_logits_over_reference_pages(cuda):
     from ssengine_b200 import indexer
 
@@ -86,7 +83,6 @@ def test_fp8_logits_over_reference_pages(cuda):
                 assert np.abs(g - wr).max() <= 1e-4 * max(np.abs(wr).max(), 1e-6), (r, i)
 
 
-@pending
 def test_fp8_pool_insert_against_the_bf16_insert(cuda):
     from ssengine_b200 import indexer
 
