@@ -214,14 +214,14 @@ int ssb_indexer_logits(const void* q, const void* w, int64_t ldw, int64_t T, con
  * reference's cache, a 128-token page of 32 pools = 33 rows of 128 bytes (32 rows of e4m3 codes, then the 32 fp32
  * scales), k_pages holding `pages` pages (128-byte aligned), pool p of request r in page page_table[r * width + p / 32]
  * at row p % 32. logit = sum_h w_h * q_scale_h * relu(q8_h . k8) * k_scale; the softmax scale and the head-count
- * factor belong to w. Other arguments as ssb_indexer_logits. Not yet run on a GPU. */
+ * factor belong to w. Other arguments as ssb_indexer_logits. */
 int ssb_indexer_logits_fp8(const uint8_t* q8, const float* q_scale, const void* w, int64_t ldw, int64_t T,
                            const uint8_t* k_pages, int64_t pages, const int32_t* page_table, int64_t width,
                            const int32_t* groups, int64_t G, float* logits, int64_t ldl, int32_t* status,
                            void* stream);
 /* Indexer queries (bf16 rows of 128, `rows` = tokens x heads, 8-byte aligned) -> e4m3 codes q8 [rows, 128] and fp32
  * scales [rows]: scale = 2^ceil(log2(max(amax, 1e-10) / 448)), the ue8m0 form of vLLM's per-token-group FP8
- * quantization with groups of 128. Not yet run on a GPU. */
+ * quantization with groups of 128. */
 int ssb_indexer_q_quant(const void* q, int64_t rows, uint8_t* q8, float* q_scale, void* stream);
 
 /* Indexer key pools of one prefill microbatch: every pool of 4 tokens that a request's chunk completes, pool[p, c] =
@@ -236,7 +236,7 @@ int ssb_kpool_insert(const void* k, const void* gate, int64_t ld, const float* a
                      void* stream);
 /* The FP8 form of ssb_kpool_insert: each completed pool row stored as e4m3 codes of x / s with s = 2^ceil(log2(
  * max(1e-4, amax) / 448)) in the request's 132-byte-entry page (33 rows of 128 bytes: row p % 32 the codes, row 32 the
- * fp32 scales) of pool_pages (4-byte aligned); the tail ring stays bf16. Not yet run on a GPU. */
+ * fp32 scales) of pool_pages (4-byte aligned); the tail ring stays bf16. */
 int ssb_kpool_insert_fp8(const void* k, const void* gate, int64_t ld, const float* ape, const int32_t* reqs, int64_t R,
                          int32_t max_rows, const int32_t* page_table, int64_t width, uint8_t* pool_pages,
                          void* tail_ring, void* stream);

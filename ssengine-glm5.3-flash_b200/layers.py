@@ -426,7 +426,8 @@ class DsaAttention:
         H = hidden
         self.H, self.q_lora, self.nope, self.v_dim, self.theta, self.eps = H, q_lora, nope, v_dim, theta, eps
         # the FP8 indexer: e4m3 queries with per-(token, head) scales, pool keys in the reference's 132-byte entries
-        # (the pool cache is then uint8 [pages * 33, 128]); not yet run on a GPU, off by default
+        # (the pool cache is then uint8 [pages * 33, 128]); off by default: its kernels are validated one by one, the
+        # whole stage on this form not yet
         self.indexer_fp8 = indexer_fp8
         self.qh = nope + self.ROPE
         w = dict(init=init, std=std)

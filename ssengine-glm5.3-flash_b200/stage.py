@@ -124,8 +124,8 @@ class StageConfig:
     init_std: float = 0.02
     max_context: int = 131_072         # the longest context a request reaches (sizes the indexer's logits buffer)
     reserve_reqs: int = 64             # requests per microbatch the KDA chunk workspace is reserved for
-    indexer_fp8: bool = False          # the FP8 indexer over the reference's 132-byte pool entries (not yet run on a
-                                       # GPU; the validated bf16 indexer by default)
+    indexer_fp8: bool = False          # the FP8 indexer over the reference's 132-byte pool entries (its kernels
+                                       # validated, the whole stage not yet; the bf16 indexer by default)
 
 
 @dataclass
