@@ -93,6 +93,7 @@ class StageKv:
     def __init__(self, layers, is_dsa, num_blocks: int, kda_heads: int, device, pin: bool = False,
                  pool_fp8: bool = False):
         dev = torch.device(device)
+        self.device = dev
         self.num_blocks = num_blocks
         self.kda_heads = kda_heads
         self.layers, self.is_dsa = list(layers), is_dsa

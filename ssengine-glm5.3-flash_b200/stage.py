@@ -142,6 +142,7 @@ class Batch:
     kda_seqs: torch.Tensor | None = None       # int32 [5, R, 4] per KDA state group g2..g6: {first row, end row,
                                                # state_blocks[g], has state}, device
     dsa: dict | None = None                    # DSA layers' metadata (positions, slots, qsl, page table, kpool, groups)
+    tier_ops: list = field(default_factory=list)   # the plan's DRAM tier copies, applied before its forward
 
 
 class _Pack:
@@ -379,7 +380,8 @@ class StageModel:
             dsa = dict(positions=positions[:T], slots=slots[:T], qsl=v["dsa_qsl"], page_table=v["dsa_pages"],
                        kpool_reqs=v["dsa_kreq"], max_rows=dsa_max_rows, groups=v["dsa_groups"][:dsa_ng])
         return Batch(T, order, positions[:rows_out], slots[:rows_out], table[: R * width].view(R, width),
-                     v.get("tok"), v["last"], bucket, keep=[host, dev], kda_seqs=v.get("kda"), dsa=dsa)
+                     v.get("tok"), v["last"], bucket, keep=[host, dev], kda_seqs=v.get("kda"), dsa=dsa,
+                     tier_ops=list(getattr(plan, "tier_ops", None) or []))
 
     def run(self, batch: Batch, hidden_in: torch.Tensor | None, edge_out=None) -> torch.Tensor | None:
         """edge_out: a device address, or a callable returning one when called right before the last kernel (the

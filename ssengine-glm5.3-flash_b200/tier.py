@@ -194,7 +194,7 @@ class TierArena:
                             pin=copier is None, pool_fp8=stage_kv.pool_fp8)
         self.hbm_ranges = stage_kv.tier_ranges(stage)
         self.dram_ranges = self.dram.tier_ranges(stage)
-        self.device = device
+        self.device = stage_kv.device if device is None else device     # where the copy kernel's status word lives
         self.copier = copier if copier is not None else self._cuda_copier
         self.bytes_moved = 0
 
@@ -204,6 +204,8 @@ class TierArena:
         from . import lib
 
         if not hasattr(self, "_status"):
+            if torch.device(self.device).type != "cuda":
+                raise ValueError(f"the copy kernel needs the stage's views on a CUDA device, not {self.device}")
             self._status = torch.zeros(1, dtype=torch.int32, device=self.device)
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         # the runs' upload, the kernel and the runs buffer's life all on the kernel's stream: the caching allocators

@@ -30,11 +30,10 @@ class StageWorker:
         """One microbatch (a Plan, or a Batch prepared earlier). Returns the last stage's greedy tokens, else None."""
         st, pipe = self.stage, self.pipe
         batch = work if isinstance(work, Batch) else st.prepare(work)
-        ops = getattr(work, "tier_ops", None)
-        if ops:
+        if batch.tier_ops:                             # carried from the plan by prepare, also for a batch made early
             if self.tier is None:
-                raise RuntimeError(f"plan {work.mb_id} carries DRAM tier copies but this stage has no tier")
-            self.tier.apply(ops, torch.cuda.current_stream())    # in stream order, before the forward
+                raise RuntimeError("a microbatch carries DRAM tier copies but this stage has no tier")
+            self.tier.apply(batch.tier_ops)            # on the current stream, in order, before the forward
         self.n += 1
         hidden = None
         if pipe is not None:

@@ -208,3 +208,42 @@ def test_vectorized_runs_equal_the_slice_by_slice_restatement():
             got = op_runs(op, arena.hbm_ranges, arena.dram_ranges, piece)
             want = np.asarray(_runs_reference(op, arena.hbm_ranges, arena.dram_ranges, piece), np.int64).reshape(-1, 3)
             np.testing.assert_array_equal(got, want)
+
+
+def test_a_batch_prepared_early_still_carries_its_tier_copies():
+    """The pipeline prepares batches ahead and steps them: the plan's copies ride the batch, not the plan object."""
+    from ssengine_b200.messages import Plan
+    from ssengine_b200.stage import Batch
+    from ssengine_b200.worker import StageWorker
+
+    op = TierOp("write", [70], [1, 2, 3, 4, 5, 6], [70], [1, 2, 3, 4, 5, 6], 10)
+
+    class Stage:
+        first = last = True
+
+        def prepare(self, plan):
+            return Batch(0, [], None, None, None, None, None, tier_ops=list(plan.tier_ops))
+
+        def run(self, batch, hidden):
+            return "tokens"
+
+    class Arena:
+        applied = []
+
+        def apply(self, ops, stream=None):
+            self.applied.append(list(ops))
+
+    plan = Plan(3, [], tier_ops=[op])
+    w = StageWorker(Stage(), tier=Arena())
+    assert w.step(Stage().prepare(plan)) == "tokens" and Arena.applied == [[op]]
+    assert w.step(plan) == "tokens" and Arena.applied == [[op], [op]]
+    with pytest.raises(RuntimeError):
+        StageWorker(Stage()).step(plan)                          # copies and no tier: refused
+
+
+def test_the_copy_kernel_path_refuses_host_views():
+    kv = StageKv(list(range(4)), lambda i: i % 4 == 3, 3, 4, "cpu")
+    arena = TierArena(kv, 0, 2, copier=memmove_copier)          # (pinned DRAM views need a driver)
+    arena.copier = arena._cuda_copier                            # the default: ssb_copy_runs, which needs device views
+    with pytest.raises(ValueError):
+        arena.apply([TierOp("write", [70], [1, 1, 1, 1, 1, 1], [70], [1, 1, 1, 1, 1, 1])])
