@@ -51,7 +51,7 @@ def grouped_linear(x_heads, codes, sf, gs_w, gs_in):
 def grouped_linear_bf16(x_heads, w):
     """x_heads [heads, T, K] bf16 values, w [heads, N, K] bf16 values -> [heads, T, N] float64 (the BF16 batched
     GEMM of the MLA absorb / v_up)."""
-    return np.einsum("htk,hnk->htn", np.asarray(x_heads, np.float64), np.asarray(w, np.float64))
+    return np.matmul(np.asarray(x_heads, np.float64), np.asarray(w, np.float64).transpose(0, 2, 1))
 
 
 __all__ = ["rmsnorm", "rope", "grouped_linear", "grouped_linear_bf16", "bf16"]

@@ -29,8 +29,14 @@ HC = 4
 
 
 def bf16(x) -> np.ndarray:
-    """Round fp32 to bf16 (nearest even) and back to fp32 (32-bit integer arithmetic; only NaN bit patterns wrap)."""
+    """Round fp32 to bf16 (nearest even) and back to fp32 (32-bit integer arithmetic; only NaN bit patterns wrap).
+    Large inputs go through in pieces of 2^20 values, so that the temporaries stay in cache."""
     x = np.ascontiguousarray(x, dtype=np.float32)
+    if x.size > 1 << 20:
+        flat, out = x.reshape(-1), np.empty(x.size, np.float32)
+        for i in range(0, x.size, 1 << 20):
+            out[i:i + (1 << 20)] = bf16(flat[i:i + (1 << 20)])
+        return out.reshape(x.shape)
     u = x.view(np.uint32)
     r = (u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)
     return r.view(np.float32)

@@ -23,14 +23,21 @@ import numpy as np
 
 DV = 512
 E4M3_MAX = 448.0
+CHUNK = 1 << 20        # values per piece of a large encode
 
 
 def e4m3_encode(x) -> np.ndarray:
     """fp32 values -> e4m3 bytes (round to nearest even, saturating to +-448, the sign of zero kept), by integer
     arithmetic on the fp32 bits: normals (|x| >= 2^-6) round their 23-bit mantissa to 3 bits, smaller values are
     multiples of 2^-9 (rint of |x| * 512; 8 of them is the smallest normal, code 0x08). Same bytes as
-    `e4m3_encode_reference` below (tested) at a fraction of its cost."""
+    `e4m3_encode_reference` below (tested) at a fraction of its cost. Large inputs go through in pieces of 2^20
+    values (each value's code depends on that value alone), so that the temporaries stay in cache."""
     x = np.ascontiguousarray(x, dtype=np.float32)
+    if x.size > CHUNK:
+        flat, out = x.reshape(-1), np.empty(x.size, np.uint8)
+        for i in range(0, x.size, CHUNK):
+            out[i:i + CHUNK] = e4m3_encode(flat[i:i + CHUNK])
+        return out.reshape(x.shape)
     u = x.view(np.uint32)
     sign = ((u >> np.uint32(31)).astype(np.uint8) << np.uint8(7))
     a = u & np.uint32(0x7FFFFFFF)
@@ -59,12 +66,20 @@ def e4m3_encode_reference(x) -> np.ndarray:
     return (sign | (E << 3).astype(np.uint8) | M.astype(np.uint8)).astype(np.uint8)
 
 
-def e4m3_decode(b) -> np.ndarray:
-    """e4m3 bytes -> float64 values (the NaN codes 0x7f / 0xff are not produced by the encoder)."""
-    b = np.asarray(b, np.uint8).astype(np.int64)
+def _e4m3_values(b) -> np.ndarray:
+    b = np.asarray(b, np.int64)
     s = np.where(b & 0x80, -1.0, 1.0)
     E, M = (b >> 3) & 15, b & 7
     return s * np.where(E == 0, M * 2.0 ** -9, (1.0 + M / 8.0) * 2.0 ** (E - 7))
+
+
+_E4M3_TABLE = _e4m3_values(np.arange(256))
+
+
+def e4m3_decode(b) -> np.ndarray:
+    """e4m3 bytes -> float64 values, by a table of the 256 codes (sign x 2^(E - 7) x (1 + M / 8); E = 0: M x 2^-9);
+    the NaN codes 0x7f / 0xff are not produced by the encoder."""
+    return _E4M3_TABLE[np.asarray(b, np.uint8)]
 
 
 def quantize(x, scale: float) -> np.ndarray:
@@ -83,13 +98,14 @@ LAZY = 3.0             # a block raising a row's (base-2) max by more than this 
 P_SCALE = 32.0         # P enters the P.V product as e4m3(32 p)
 
 
-def sparse_mla_fp8p(q, kv8, cols, pages, bmm1: float, bmm2: float) -> np.ndarray:
+def sparse_mla_fp8p(q, kv8, cols, pages, bmm1: float, bmm2: float, decoded=None) -> np.ndarray:
     """One query row with its softmax weights rounded to e4m3 where the FP8 attention rounds them (the activation
     quantization point of the P.V product, as the reference's FP8 sparse MLA kernel has one): the row's index
     columns in blocks of 128 (blocks without a selected token skipped); base-2 scores x = s * bmm1 * log2(e) (fp32);
     a running max m kept until a block raises it by more than 2^3 (then the accumulated output and sum are scaled by
     2^(m_old - m_new)); p = 2^(x - m) (fp32); the sum of p unrounded; the product with e4m3(32 p) / 32.
-    q [64, 576] float64 (the decoded e4m3 query), cols [m] (-1 = none) -> float64 [64, 512]."""
+    q [64, 576] float64 (the decoded e4m3 query), cols [m] (-1 = none) -> float64 [64, 512]. `decoded`: (sorted
+    slots, their decoded rows) covering every slot the row reads, to decode shared cache rows once per call."""
     H = q.shape[0]
     o = np.zeros((H, DV))
     l = np.zeros(H)
@@ -102,7 +118,8 @@ def sparse_mla_fp8p(q, kv8, cols, pages, bmm1: float, bmm2: float) -> np.ndarray
         c = c[pg[c // 128] >= 0] if c.size else c
         if c.size == 0:
             continue
-        k = e4m3_decode(kv8[slot_of(pg, c)])                               # [mb, 576]
+        slots = slot_of(pg, c)
+        k = e4m3_decode(kv8[slots]) if decoded is None else decoded[1][np.searchsorted(decoded[0], slots)]
         x = ((q @ k.T).astype(np.float32) * sc).astype(np.float32)         # [64, mb]
         mb = x.max(axis=1)
         fresh = m == -np.inf
@@ -125,8 +142,14 @@ def sparse_mla(q8, kv8, indices, pages, bmm1: float, bmm2: float, p_fp8: bool = 
     q = e4m3_decode(q8)
     out = np.zeros((q.shape[0], q.shape[1], DV))
     if p_fp8:
+        pg = np.asarray(pages, np.int64)
+        c = np.asarray(indices, np.int64).ravel()
+        c = c[(c >= 0) & (c // 128 < len(pg))]
+        c = c[pg[c // 128] >= 0] if c.size else c
+        used = np.unique(slot_of(pg, c))                                   # every cache row any query row reads
+        decoded = (used, e4m3_decode(kv8[used]))
         for i in range(q.shape[0]):
-            out[i] = sparse_mla_fp8p(q[i], kv8, indices[i], pages, bmm1, bmm2)
+            out[i] = sparse_mla_fp8p(q[i], kv8, indices[i], pages, bmm1, bmm2, decoded)
         return out
     for i in range(q.shape[0]):
         sel = np.asarray(indices[i])
