@@ -8,7 +8,8 @@ against the oracle's FP8 restatement (oracle/indexer.py, pinned to vLLM's own qu
   bf16 pool value over its scale, scales equal to the oracle's rule on the bf16 values except where a row's fp32 amax
   sits at a power-of-two boundary.
 
-The three kernel tests passed on their first B200 run; the stage-level test stays skipped until its own first run."""
+The three kernel tests passed on their first B200 run. The whole stage on these forms is checked in
+tests/test_zy_indexer_fp8_stage.py, collected after the other GPU tests."""
 
 import numpy as np
 import pytest
@@ -18,7 +19,6 @@ from oracle import indexer as oidx
 from oracle.mla import e4m3_decode
 
 pytestmark = pytest.mark.gpu
-pending = pytest.mark.skip(reason="first run pending: the whole stage on the FP8 indexer has not yet run on a B200 (its kernels have, above)")
 
 REQS = [(0, 50), (37, 13), (300, 70), (1400, 21), (3, 1)]       # (position of the first query row, query rows)
 
@@ -115,41 +115,3 @@ def test_fp8_pool_insert_against_the_bf16_insert(cuda):
     want_s = oidx.ue8m0(np.maximum(np.float32(1e-4), np.abs(ref).max(axis=1)) / np.float32(448))
     assert np.mean(scales == want_s) > 0.95
     assert (np.abs(vals - ref) <= (2.0 ** -3) * np.abs(ref) + scales[:, None] * 2.0 ** -9 + 1e-2 * np.abs(ref)).all()
-
-
-@pending
-def test_stage_with_the_fp8_indexer_matches_the_oracle(cuda):
-    """BASELINE config 1's model with `indexer_fp8` on, over a 2,600-token prompt (650 pools: the 512-pool top-k
-    drops some), against the oracle's composition with its FP8 indexer branch, teacher-forced: every layer within 3e-2
-    of the oracle's layer on the device layer's own inputs, the logits within 2e-2 of the oracle's head on the
-    device's own final residual (each oracle layer runs once: a chained oracle pass doubles the test's time)."""
-    from model_params import row_chunks, stage_params, stage_states
-    from oracle import mhc as omhc
-    from oracle import model as omodel
-    from ssengine_b200 import weights
-    from ssengine_b200.messages import Chunk, Plan
-    from ssengine_b200.stage import StageConfig, StageModel
-
-    rel = lambda a, b: float(np.linalg.norm(np.asarray(a, np.float64) - b) / max(np.linalg.norm(b), 1e-30))
-    cfg = StageConfig(layer_split=(4,), hidden=256, inter=128, experts=8, top_k=2, vocab=4096, mb_tokens=4096,
-                      num_blocks=8, seed=0, layer_kind="hybrid", kda_heads=2, q_lora=256, mla_nope=64, mla_v_dim=256,
-                      routing="sigmoid", weight_init="normal", init_std=0.02, indexer_fp8=True)
-    st = StageModel(cfg, 0, cuda)
-    caught = []
-    st.layer_hook = lambda layer, res, x_prev, post, comb: caught.append(
-        tuple(t.float().cpu().numpy() for t in (res, x_prev, post, comb)))
-    params, states = stage_params(st), stage_states(st)
-    prompt = np.random.default_rng(1).integers(0, cfg.vocab, 2600)
-    plan = Plan(0, [Chunk("p0", 0, 2600, list(range(67, 67 + 21)), [2, 3, 4, 5, 6, 7], True, prompt.tolist())])
-    st.forward(plan)
-    torch.cuda.synchronize()
-    assert int(st.status.item()) == 0
-    rows, _ = row_chunks(plan)
-    inp = (np.repeat(params["embed"][prompt][:, None, :], 4, axis=1), None, None, None)
-    for li, (L, stt) in enumerate(zip(params["layers"], states)):
-        res, _, _, _ = omodel.layer_forward(L, stt, rows, *inp, weights.GS_X, weights.GS_H)
-        assert rel(caught[li][0], res) < 3e-2, (li, rel(caught[li][0], res))
-        inp = caught[li]
-    res, x_prev, post, comb = caught[-1]
-    o_logits, _ = omodel.head(params, rows, omhc.post(x_prev, res, post, comb))
-    assert rel(st.last_logits.cpu().numpy(), o_logits) < 2e-2
