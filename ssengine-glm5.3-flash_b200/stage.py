@@ -2,7 +2,7 @@
 
 Mirrors ssengine/model/stage.py:216-762 of the reference and its contract in ssengine/runtime/README.md:72-100:
 - construction `StageModel(cfg, stage, device, *, num_blocks=None, warmup=True, cuda_graphs=None, ipc_kv=False,
-  extra_blocks=0)`; attributes `num_blocks` (counts the null block), `hidden_width`, `first`, `last`, `layer_range`;
+  extra_blocks=0)`, cfg a `StageConfig` or the reference's run config (`stage_settings`, stage.py:130-135); attributes `num_blocks` (counts the null block), `hidden_width`, `first`, `last`, `layer_range`;
 - `prepare(plan) -> Batch`: host work only (no wait on queued GPU work): row order with decode-class chunks
   (<= 256 tokens) first, stably (ssengine/model/metadata.py:43,214), query start offsets, each request's KV pages,
   stage-0 token ids and the last stage's rows, packed into ONE pinned buffer and copied in stream order; the
@@ -184,9 +184,46 @@ def kda_tables(chunks, order, qsl) -> np.ndarray:
                     dtype=np.int32).reshape(5, -1, 4)
 
 
+# The reference model's dimensions, as its op manifest states them (ssengine/kernels.py:109-121 dense FFN, :174-191
+# router and MoE: 288 experts, top 8, intermediate 2048, sigmoid + correction bias with routed scale 5/2, :277 split):
+# what a stage built from the reference's own run config gets, with random-init weights of that architecture
+REFERENCE_MODEL = dict(hidden=4096, inter=2048, experts=288, top_k=8, vocab=151_552, kda_heads=64, q_lora=1536,
+                       mla_nope=192, mla_v_dim=256, dense_layers=3, dense_inter=12288, routing="sigmoid",
+                       layer_kind="hybrid")
+
+
+def stage_settings(cfg) -> StageConfig:
+    """The `StageConfig` of a run config. A `StageConfig` is returned as it is. Anything else is read as the
+    reference's `RunConfig` (or a bench's namespace with its fields) the way the reference's `stage_settings` reads
+    it (ssengine/model/stage.py:130-135): `layer_split`, `checkpoint`, `scheduler.mb_tokens`, `pool_tokens`,
+    `cuda_graphs`, each read directly, so that a missing field raises here. The model is `REFERENCE_MODEL` with
+    random-init weights: a checkpoint path raises (this library loads no weights). The workspaces are sized for
+    max(mb_tokens, 8192) rows, as the reference sizes its stage; `pool_tokens` gives the KV blocks (rounded up to
+    whole 8,576-token blocks, plus the null block), else `StageConfig`'s default."""
+    if isinstance(cfg, StageConfig):
+        return cfg
+    split, ckpt = tuple(int(n) for n in cfg.layer_split), cfg.checkpoint
+    mb, pool, graphs = int(cfg.scheduler.mb_tokens), cfg.pool_tokens, bool(cfg.cuda_graphs)
+    if ckpt:
+        raise ValueError(f"checkpoint {ckpt!r}: this library builds random-init weights and loads none")
+    blocks = {} if pool is None else {"num_blocks": -(-int(pool) // BLOCK_TOKENS) + 1}
+    return StageConfig(layer_split=split, mb_tokens=max(mb, 8192), cuda_graphs=graphs, **blocks, **REFERENCE_MODEL)
+
+
+def bench_config(mb_tokens: int, checkpoint: str | None = None, cuda_graphs: bool = False, split=(12, 11, 11, 11)):
+    """A run-config stand-in with the fields `stage_settings` reads (the reference's `bench_config`,
+    ssengine/model/stage.py:138-144), for benches and tests."""
+    from types import SimpleNamespace
+
+    return SimpleNamespace(layer_split=list(split), checkpoint=checkpoint, pool_tokens=None,
+                           scheduler=SimpleNamespace(mb_tokens=mb_tokens), cuda_graphs=cuda_graphs)
+
+
 class StageModel:
-    def __init__(self, cfg: StageConfig, stage: int, device, *, num_blocks: int | None = None, warmup: bool = True,
+    def __init__(self, cfg, stage: int, device, *, num_blocks: int | None = None, warmup: bool = True,
                  cuda_graphs: bool | None = None, ipc_kv: bool = False, extra_blocks: int = 0):
+        """cfg: a `StageConfig`, or the reference's run config (read by `stage_settings`)."""
+        cfg = stage_settings(cfg)
         self.cfg, self.stage = cfg, stage
         self.device = torch.device(device)
         split = list(cfg.layer_split)

@@ -3,6 +3,8 @@
 
 import json
 
+import pytest
+
 from oracle import pages as opages
 from tests.conftest import GOLDEN
 
@@ -271,3 +273,27 @@ def test_kda_tables_cover_every_chunk_once_longest_first():
                 r = int(np.searchsorted(qsl, a))
                 c = chunks[order[r]]
                 assert b - a == c.num_tokens and blk == c.state_blocks[g] and has == int(c.start > 0)
+
+
+def test_the_reference_run_config_builds_a_stage_config():
+    """`StageModel(run_cfg, ...)` reads the reference's run config through `stage_settings` (its five fields, read
+    directly); a `StageConfig` passes through as it is."""
+    from types import SimpleNamespace
+
+    from ssengine_b200.stage import REFERENCE_MODEL, StageConfig, bench_config, stage_settings
+
+    own = StageConfig(layer_split=(4,), hidden=256)
+    assert stage_settings(own) is own
+    cfg = stage_settings(bench_config(4096))
+    assert cfg.layer_split == (12, 11, 11, 11) and cfg.mb_tokens == 8192 and not cfg.cuda_graphs
+    assert cfg.num_blocks == StageConfig().num_blocks
+    assert all(getattr(cfg, k) == v for k, v in REFERENCE_MODEL.items())
+    assert (cfg.experts, cfg.top_k, cfg.inter, cfg.routing) == (288, 8, 2048, "sigmoid")
+    run = bench_config(16384, cuda_graphs=True, split=(23, 22))
+    run.pool_tokens = 20_000                                     # 3 blocks of 8,576 tokens, plus the null block
+    cfg = stage_settings(run)
+    assert (cfg.layer_split, cfg.mb_tokens, cfg.cuda_graphs, cfg.num_blocks) == ((23, 22), 16384, True, 4)
+    with pytest.raises(ValueError):
+        stage_settings(bench_config(8192, checkpoint="/models/glm"))
+    with pytest.raises(AttributeError):                          # a field missing from the run config
+        stage_settings(SimpleNamespace(layer_split=[45], checkpoint=None, cuda_graphs=False, pool_tokens=None))
