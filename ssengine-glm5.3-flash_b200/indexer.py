@@ -26,17 +26,18 @@ FP8_PAGE_ROWS = 33                 # an FP8 pool page: 32 rows of 128 e4m3 codes
 
 def work_groups(q_starts, q_lens, starts) -> np.ndarray:
     """Per request (first query row, query rows, position of its first row): int32 [G, 4] groups of <= 8 rows
-    {request, first row, rows, pool tiles}, longest first (host side, like the reference's metadata)."""
-    g = []
-    for r, (qs, n, st) in enumerate(zip(q_starts, q_lens, starts)):
-        for q0 in range(int(qs), int(qs) + int(n), 8):
-            nq = min(8, int(qs) + int(n) - q0)
-            last_pos = int(st) + (q0 + nq - 1 - int(qs))
-            tiles = -(-((last_pos + 1) // POOL) // TILE)
-            if tiles > 0:
-                g.append((r, q0, nq, tiles))
-    g.sort(key=lambda e: -e[3])
-    return np.asarray(g, np.int32).reshape(-1, 4)
+    {request, first row, rows, pool tiles}, longest first (host side, like the reference's metadata); groups of equal
+    tiles keep request and row order. A request's groups start at its first row every 8 rows; a group's tiles cover
+    the pools visible to its last row ((position + 1) // 4 of them, 128 a tile); groups with no visible pool are
+    left out."""
+    qs, n, st = (np.asarray(a, np.int64).reshape(-1) for a in (q_starts, q_lens, starts))
+    cnt = -(-np.maximum(n, 0) // 8)                                   # groups per request
+    r = np.repeat(np.arange(len(n), dtype=np.int64), cnt)
+    q0 = qs[r] + 8 * (np.arange(int(cnt.sum()), dtype=np.int64) - np.repeat(np.cumsum(cnt) - cnt, cnt))
+    nq = np.minimum(8, qs[r] + n[r] - q0)
+    tiles = -(-((st[r] + (q0 + nq - 1 - qs[r]) + 1) // POOL) // TILE)
+    g = np.stack([r, q0, nq, tiles], axis=1)[tiles > 0]
+    return g[np.argsort(-g[:, 3], kind="stable")].astype(np.int32).reshape(-1, 4)
 
 
 def key_ranges(positions: torch.Tensor):

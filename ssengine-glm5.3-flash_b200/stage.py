@@ -65,13 +65,13 @@ def table_width(blocks: int, page_tokens: int = PAGE_TOKENS, block_tokens: int =
     return (1 << max(blocks - 1, 0).bit_length()) * per_block
 
 
-def check_blocks(chunks, num_blocks: int) -> None:
+def check_blocks(chunks, num_blocks: int, kv_pages=None) -> None:
     """The block contract the state pages rely on (ssengine/model/kv_tensors.py:1-14: a block holds a request's KV
     pages or one of its states, never both): every non-null state block of the plan belongs to one (request, group)
     only and is no request's KV block; blocks within the pool. Block 0 is the null block (a dummy request may use it
-    for every state). Raises ValueError."""
+    for every state). `kv_pages`: the chunks' KV page ids as int64 arrays, when the caller has them. Raises
+    ValueError."""
     seen = {}
-    kv_blocks = set()
     for c in chunks:
         if len(c.state_blocks) < 6:
             raise ValueError(f"chunk {c.req_id}: {len(c.state_blocks)} state blocks (6 needed)")
@@ -84,10 +84,14 @@ def check_blocks(chunks, num_blocks: int) -> None:
             if b in seen and seen[b] != (c.req_id, g):
                 raise ValueError(f"state block {b} held twice: {seen[b]} and {(c.req_id, g)}")
             seen[b] = (c.req_id, g)
-        kv_blocks.update(int(p) // (BLOCK_TOKENS // PAGE_TOKENS) for p in c.kv_pages)
-    both = kv_blocks.intersection(seen)
-    if both:
-        raise ValueError(f"blocks {sorted(both)[:8]} are both KV and state blocks")
+    if not seen:
+        return
+    if kv_pages is None:
+        kv_pages = [np.asarray(c.kv_pages, dtype=np.int64).reshape(-1) for c in chunks]
+    pages = np.concatenate(kv_pages)
+    both = np.intersect1d(pages // (BLOCK_TOKENS // PAGE_TOKENS), np.fromiter(seen, np.int64, len(seen)))
+    if both.size:
+        raise ValueError(f"blocks {both[:8].tolist()} are both KV and state blocks")
 
 
 @dataclass
@@ -358,12 +362,13 @@ class StageModel:
         T = int(qsl[-1])
         seq = starts + q_lens
         need = -(-seq // PAGE_TOKENS)
+        full = [np.asarray(c.kv_pages, dtype=np.int64).reshape(-1) for c in chunks]    # plan order, converted once
         page_lists = []
         for r, i in enumerate(order):
-            pg = chunks[i].kv_pages
+            pg = full[i]
             if len(pg) < need[r]:
                 raise ValueError(f"chunk {chunks[i].req_id}: {len(pg)} KV pages for {int(seq[r])} tokens")
-            page_lists.append(np.asarray(pg[: need[r]], dtype=np.int64))
+            page_lists.append(pg[: need[r]])
         page_ptr = np.zeros(R + 1, dtype=np.int64)
         np.cumsum([len(p) for p in page_lists], out=page_ptr[1:])
         pages = np.concatenate(page_lists) if page_lists else np.zeros(0, dtype=np.int64)
@@ -379,7 +384,7 @@ class StageModel:
              "page_ptr": pk.add(page_ptr.astype(np.int32)), "pages": pk.add(np.maximum(pages, 0).astype(np.int32)),
              "last": pk.add(last)}
         if self.kda:
-            check_blocks(chunks, self.num_blocks)
+            check_blocks(chunks, self.num_blocks, full)
             h["kda"] = pk.add(kda_tables(chunks, order, qsl))
         if any(self.is_dsa):
             from .indexer import work_groups
