@@ -181,11 +181,14 @@ def kda_tables(chunks, order, qsl) -> np.ndarray:
     order, so the longest sequences start first (an LPT order, in the place of the reference's head-split plan,
     ssengine/native/kda_split_heads.cpp:17-91); each sequence's result does not depend on its place in the table."""
     R = len(order)
-    q_lens = np.diff(np.asarray(qsl, np.int64))
-    lpt = sorted(range(R), key=lambda r: -int(q_lens[r]))
-    return np.array([[(int(qsl[r]), int(qsl[r + 1]), int(chunks[order[r]].state_blocks[g]),
-                       int(chunks[order[r]].start > 0)) for r in lpt] for g in range(5)],
-                    dtype=np.int32).reshape(5, -1, 4)
+    qsl = np.asarray(qsl, np.int64)
+    lpt = np.argsort(-np.diff(qsl), kind="stable")                     # ties keep row order
+    blocks = np.array([chunks[i].state_blocks[:5] for i in order], np.int64).reshape(R, 5)
+    cont = np.array([chunks[i].start > 0 for i in order], np.int64)
+    out = np.empty((5, R, 4), np.int32)
+    out[:, :, 0], out[:, :, 1] = qsl[lpt], qsl[lpt + 1]
+    out[:, :, 2], out[:, :, 3] = blocks[lpt].T, cont[lpt]
+    return out
 
 
 # The reference model's dimensions, as its op manifest states them (ssengine/kernels.py:109-121 dense FFN, :174-191
@@ -391,10 +394,10 @@ class StageModel:
 
             wp = max(1, max((len(p) for p in page_lists), default=1))
             ptab = np.full((max(R, 1), wp), -1, dtype=np.int32)
-            for r, p in enumerate(page_lists):
-                ptab[r, :len(p)] = p
-            kreq = np.array([(int(qsl[r]), int(q_lens[r]), int(starts[r]), int(chunks[i].state_blocks[5]))
-                             for r, i in enumerate(order)], dtype=np.int32).reshape(-1, 4)
+            n_pg = np.diff(page_ptr)
+            ptab[np.repeat(np.arange(R), n_pg), np.arange(pages.size) - np.repeat(page_ptr[:-1], n_pg)] = pages
+            tails = np.array([chunks[i].state_blocks[5] for i in order], np.int64)
+            kreq = np.stack([qsl[:-1], q_lens, starts, tails], axis=1).astype(np.int32).reshape(-1, 4)
             grp = work_groups(qsl[:-1], q_lens, starts)
             h["dsa_qsl"] = pk.add(qsl.astype(np.int32))
             h["dsa_pages"] = pk.add(ptab)
