@@ -150,9 +150,14 @@ def wait_key(store, key: str, give_up_s: float, poll_s: float = 2e-4) -> None:
         dt = min(2 * dt, 2e-3)
 
 
+class StageFailed(RuntimeError):
+    """Another stage's loop failed (its message came through the store)."""
+
+
 class StoreChannel:
     """Plans from stage 0 to the other stages, and the other stages' reports back, over a c10d store (the job's
-    rendezvous store, or any `torch.distributed.Store`). Keys: plan/<k>, rep/<stage>/<k>."""
+    rendezvous store, or any `torch.distributed.Store`). Keys: plan/<k>, rep/<stage>/<k>, and err/<stage> for a
+    stage whose loop failed."""
 
     def __init__(self, store, give_up_s: float = 900.0):
         self.store = store
@@ -163,9 +168,27 @@ class StoreChannel:
         self.store.set(f"plan/{k}", pickle.dumps(plan))
 
     def get_plan(self, k: int) -> Plan | None:
-        key = f"plan/{k}"
-        wait_key(self.store, key, self.give_up_s)
+        """Plan k, or None for the stop plan; raises `StageFailed` when stage 0 reports a failure first, and
+        TimeoutError after `give_up_s` without either."""
+        key, t0, dt = f"plan/{k}", time.monotonic(), 2e-4
+        while not self.store.check([key]):
+            if self.store.check(["err/0"]):
+                raise StageFailed(f"stage 0 failed: {self.store.get('err/0').decode()}")
+            if time.monotonic() - t0 > self.give_up_s:
+                raise TimeoutError(f"store key {key!r} not set within {self.give_up_s:.0f} s")
+            time.sleep(dt)
+            dt = min(2 * dt, 2e-3)
         return pickle.loads(self.store.get(key))
+
+    def put_error(self, stage: int, what: str):
+        self.store.set(f"err/{stage}", what.encode())
+
+    def error(self, stages) -> tuple[int, str] | None:
+        """(stage, message) of the first of `stages` that reported a failure, else None."""
+        for st in stages:
+            if self.store.check([f"err/{st}"]):
+                return st, self.store.get(f"err/{st}").decode()
+        return None
 
     def drop_plan(self, k: int):
         self.store.delete_key(f"plan/{k}")
@@ -242,10 +265,21 @@ class Controller:
         more), then send the stop plan. `step(plan) -> (done, tokens)` runs stage 0's forward of one plan; `reporter`
         is stage 0's `Reporter` whose sink is `self.local.put`; `channel` reaches the other stages (None at N = 1).
         Watchdog: with microbatches in flight and no report for `stall_s`, raise with the scheduler's state (a stage
-        that died or stopped reporting)."""
+        that died or stopped reporting). A stage whose loop failed reports it through the channel (checked every 50
+        ms): this raises `StageFailed`. On any failure here the other stages get the failure and a stop plan, so that
+        their loops end instead of waiting for plans."""
+        try:
+            return self._run(step, reporter, channel, duration_s, warm_s, drain_s, stall_s)
+        except BaseException as e:
+            if channel is not None and self.last > 0:
+                channel.put_error(0, f"{type(e).__name__}: {e}")
+                channel.put_plan(len(self.microbatches), None)
+            raise
+
+    def _run(self, step, reporter, channel, duration_s, warm_s, drain_s, stall_s) -> dict:
         sched, load = self.sched, self.load
         t0 = self.clock()
-        last_report = t0
+        last_report = last_check = t0
         end, measure_from = t0 + int(duration_s * 1e9), t0 + int(warm_s * 1e9)
         self._stop_arrivals = end
         for t, i in load.first_arrivals(t0):
@@ -265,6 +299,11 @@ class Controller:
                 reps.append(self.local.get())
             if channel is not None and self.last > 0:
                 reps += channel.poll_reports(range(1, self.num_stages))
+            if channel is not None and self.last > 0 and now - last_check > 50_000_000:
+                last_check = now
+                err = channel.error(range(1, self.num_stages))
+                if err is not None:
+                    raise StageFailed(f"stage {err[0]} failed: {err[1]}")
             if reps:
                 last_report = now
             elif sched.in_flight and now - last_report > int(stall_s * 1e9):
@@ -340,15 +379,26 @@ class Controller:
 
 
 def serve_stage(step, channel: StoreChannel, reporter: Reporter) -> int:
-    """A stage > 0: run plans 0, 1, ... from stage 0 until the stop plan. Returns the microbatches run."""
+    """A stage > 0: run plans 0, 1, ... from stage 0 until the stop plan. Returns the microbatches run. A failure
+    here is reported to stage 0 through the channel before it propagates; a failure of stage 0 (its message, then
+    the stop plan) raises `StageFailed` here."""
     k = 0
-    while (plan := channel.get_plan(k)) is not None:
-        if reporter.error is not None:
-            raise reporter.error
-        done, tokens = step(plan)
-        reporter.submit(k, done, tokens)
-        k += 1
-    reporter.close()
+    try:
+        while (plan := channel.get_plan(k)) is not None:
+            if reporter.error is not None:
+                raise reporter.error
+            done, tokens = step(plan)
+            reporter.submit(k, done, tokens)
+            k += 1
+        err = channel.error([0])
+        if err is not None:
+            raise StageFailed(f"stage 0 failed: {err[1]}")
+        reporter.close()
+    except StageFailed:
+        raise
+    except BaseException as e:
+        channel.put_error(reporter.stage, f"{type(e).__name__}: {e}")
+        raise
     return k
 
 

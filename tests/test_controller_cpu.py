@@ -242,3 +242,60 @@ def test_a_stage_that_stops_reporting_trips_the_watchdog():
     with pytest.raises(RuntimeError, match="no stage report"):
         ctl.run(stuck_step, rep, None, duration_s=0.5, warm_s=0.1, stall_s=0.5)
     never.set()
+
+
+def _failing_rank(rank: int, port: int, out, failing: int):
+    """A two-stage run in which stage `failing` raises at microbatch 3 (a host-side failure: the exception of a
+    stage's loop, no device involved); every rank reports how its own loop ended and after how long."""
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+                            timeout=timedelta(seconds=60))
+    try:
+        store = dist.distributed_c10d._get_default_store()
+        chan = StoreChannel(dist.PrefixStore("ctl/", store), give_up_s=60)
+        stage = FakeStage(rank, 2, dist.PrefixStore("fake/", store), NUM_BLOCKS)
+
+        def step(plan):
+            if rank == failing and plan.mb_id == 3:
+                raise ValueError("planted failure at microbatch 3")
+            return stage.step(plan)
+
+        t0 = time.monotonic()
+        try:
+            if rank == 0:
+                sched = Scheduler(KvManager(NUM_BLOCKS, keep_sessions=True), CFG, None, GATE + 1, 1)
+                ctl = Controller(sched, small_load(), 2)
+                ctl.run(step, Reporter(0, ctl.local.put), chan, duration_s=30.0, warm_s=0.4)
+            else:
+                serve_stage(step, chan, Reporter(1, chan.put_report))
+            out.put((rank, "finished", time.monotonic() - t0))
+        except Exception as e:                       # noqa: BLE001 -- the test reads which exception ended the loop
+            out.put((rank, f"{type(e).__name__}: {e}", time.monotonic() - t0))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("failing", [0, 1])
+def test_a_failing_stage_ends_every_stage_loop_promptly(failing):
+    """A stage whose loop raises tells the others through the store: a later stage's failure ends stage 0's
+    controller (`StageFailed`, within its 50 ms check, not after the stall watchdog's minutes), and stage 0's failure
+    ends the later stage's loop (the failure, then the stop plan) instead of leaving it waiting for plans."""
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_rank, args=(r, port, out, failing)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, how, secs = out.get(timeout=120)
+        res[r] = (how, secs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    other = 1 - failing
+    assert res[failing][0] == "ValueError: planted failure at microbatch 3", res
+    assert res[other][0].startswith(f"StageFailed: stage {failing} failed: ValueError: planted failure"), res
+    assert res[other][1] < 20.0, res                # the 30 s run ends at the failure, far below the watchdog
